@@ -1,0 +1,349 @@
+"""Benchmark: spiking OCR seq2seq forward (teacher forcing) on B200.
+
+Workload (the OCR seq2seq images/s configuration): per GPU a batch of 256
+synthetic text-line images [1, 64, 1024] (U(0, 0.2) background plus 5-40
+black rectangles of side 8-20 px, seeded), 16x16 patch embedding to D=384
+(256 tokens), 8 spiking encoder + 4 spiking decoder layers (H=8, MLP 1536),
+T=4, target sequences of 64 uniformly random byte tokens (vocab 256) with a
+causal decoder mask, random-init weights rounded to bf16.  A step is one
+forward pass over the batch.  Weak scaling: every rank runs its own batch,
+no collective on the data path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the CPU oracle (the PyTorch restatement of the
+reference modules, oracle/) on the host cores on a bounded sample of the same
+workload; under torchrun only rank 0 runs it.
+
+One JSON line on rank 0 (see DESIGN.md for the field definitions).
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "ocr_seq2seq_images_per_sec"
+UNIT = "images/s"
+ARCH = dict(patch_size=16, d_model=384, n_heads=8, ff_dim=1536, num_encoder_layers=8, num_decoder_layers=4,
+            tgt_vocab_size=256, n_steps=4, image_encoder="patch")
+IMG = (1, 64, 1024)
+SEQ = 64
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def synthetic_lines(B, seed, H=64, W=1024):
+    g = torch.Generator().manual_seed(seed)
+    img = torch.rand(B, 1, H, W, generator=g) * 0.2
+    for b in range(B):
+        n = int(torch.randint(5, 41, (1,), generator=g))
+        hs = torch.randint(8, 21, (n, 2), generator=g)
+        for i in range(n):
+            h, w = int(hs[i, 0]), int(hs[i, 1])
+            y = int(torch.randint(0, H - h + 1, (1,), generator=g))
+            x = int(torch.randint(0, W - w + 1, (1,), generator=g))
+            img[b, 0, y:y + h, x:x + w] = 0.0
+    return img
+
+
+def make_inputs(B, seed):
+    src = synthetic_lines(B, seed)
+    tgt = torch.randint(0, ARCH["tgt_vocab_size"], (B, SEQ), generator=torch.Generator().manual_seed(seed + 7))
+    mask = torch.tril(torch.ones(SEQ, SEQ)).expand(B, 1, SEQ, SEQ).contiguous()
+    return src, tgt, mask
+
+
+def round_weights_bf16(model):
+    with torch.no_grad():
+        for m in model.modules():
+            if isinstance(m, (torch.nn.Linear, torch.nn.Conv2d)):
+                m.weight.copy_(m.weight.to(torch.bfloat16).float())
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def cpu_oracle_rate(target_s=12.0, max_batch=64):
+    """Images/s of the CPU oracle forward on a bounded sample (all host threads)."""
+    from oracle import modules as om
+    torch.manual_seed(0)
+    m = om.Seq2Seq(**ARCH).eval()
+    round_weights_bf16(m)
+    B = 1
+    with torch.no_grad():
+        src, tgt, mask = make_inputs(B, 1234)
+        t0 = time.perf_counter()
+        m(src, tgt, look_ahead_mask=mask)
+        per_img = time.perf_counter() - t0
+        B = int(max(1, min(max_batch, target_s / max(per_img, 1e-3))))
+        src, tgt, mask = make_inputs(B, 4321)
+        t0 = time.perf_counter()
+        m(src, tgt, look_ahead_mask=mask)
+        dt = time.perf_counter() - t0
+    return B / dt, B, dt
+
+
+def run_reference(args, ws, rank):
+    """--impl reference: the CPU oracle timed on the host cores."""
+    if rank != 0:
+        return
+    from oracle import modules as om
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(0)
+    m = om.Seq2Seq(**ARCH).eval()
+    round_weights_bf16(m)
+    with torch.no_grad():
+        src, tgt, mask = make_inputs(1, 99)
+        t0 = time.perf_counter()
+        m(src, tgt, look_ahead_mask=mask)
+        per = time.perf_counter() - t0
+        # bounded sample per step: the whole run stays within a few minutes
+        budget = 150.0 / max(1, args.steps + args.warmup)
+        B = int(max(1, min(16, budget / max(per, 1e-3))))
+        src, tgt, mask = make_inputs(B, 100)
+        for _ in range(args.warmup):
+            m(src, tgt, look_ahead_mask=mask)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            m(src, tgt, look_ahead_mask=mask)
+        dt = time.perf_counter() - t0
+    rate = B * args.steps / dt
+    cores = torch.get_num_threads()
+    sample = "%d images [1,64,1024] per step, full 8+4-layer forward (PyTorch eager oracle, fp32)" % B
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "ocr_seq2seq_forward", "per_step_images": B, "seq_len": SEQ, "image": list(IMG),
+                   "T": 4, "d_model": 384, "layers": "8+4", "parallelism": "cpu"},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import spikingtransformer_b200 as pkg
+    from spikingtransformer_b200 import _lib, ops
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    _lib.load()
+
+    torch.manual_seed(0)
+    model = Seq2Seq(**ARCH)
+    round_weights_bf16(model)
+    model = model.to(dev).eval()
+
+    B = args.batch
+    # four input sets (4 x 67 MB of images > 126 MB L2), rotated between steps
+    sets = []
+    for i in range(4):
+        src, tgt, mask = make_inputs(B, 1000 * rank + i)
+        sets.append((src.to(dev), tgt.to(dev), mask.to(dev)))
+    torch.cuda.synchronize()
+
+    def step(i):
+        src, tgt, mask = sets[i % len(sets)]
+        logits, _ = model(src, tgt, look_ahead_mask=mask)
+        return logits
+
+    with torch.no_grad():
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+            e0.record()
+            for i in range(args.steps):
+                step(i)
+            e1.record()
+            torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if ws > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ops.device_error_check()
+
+        # ---- end to end through the public API: pinned host inputs in, logits out
+        e2e = None
+        if not args.no_e2e:
+            hsrc = [s[0].cpu().pin_memory() for s in sets]
+            htgt = [s[1].cpu().pin_memory() for s in sets]
+            hmask = [s[2].cpu().pin_memory() for s in sets]
+            out_host = torch.empty((4, B, SEQ, ARCH["tgt_vocab_size"]), dtype=torch.float32).pin_memory()
+            h2d = hsrc[0].numel() * 4 + htgt[0].numel() * 8 + hmask[0].numel() * 4
+            d2h = out_host.numel() * 4
+            for i in range(2):
+                lg, _ = model(hsrc[i].to(dev, non_blocking=True), htgt[i].to(dev, non_blocking=True),
+                              look_ahead_mask=hmask[i].to(dev, non_blocking=True))
+                out_host.copy_(lg, non_blocking=True)
+            torch.cuda.synchronize()
+            if ws > 1:
+                dist.barrier()
+            f0 = torch.cuda.Event(enable_timing=True)
+            f1 = torch.cuda.Event(enable_timing=True)
+            f0.record()
+            for i in range(args.steps):
+                j = i % 4
+                lg, _ = model(hsrc[j].to(dev, non_blocking=True), htgt[j].to(dev, non_blocking=True),
+                              look_ahead_mask=hmask[j].to(dev, non_blocking=True))
+                out_host.copy_(lg, non_blocking=True)
+            f1.record()
+            torch.cuda.synchronize()
+            ems = f0.elapsed_time(f1)
+            if ws > 1:
+                t = torch.tensor([ems], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ems = float(t.item())
+            e2e = {"value": ws * B * args.steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h, "ms_per_step": ems / args.steps}
+
+    kernels = rec.summary()
+    launches = sum(v["launches"] for v in kernels.values())
+    peaks, peak_src = measured_peaks()
+    # dominant kernel = largest total device time in the timed region
+    dom_tag, dom = max(kernels.items(), key=lambda kv: kv[1]["ms"])
+    per_launch_ms = dom["ms"] / dom["launches"]
+    if dom["flops"] > 0:
+        achieved = dom["flops"] / dom["launches"] / (per_launch_ms / 1000.0) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        roof = {"bound": "tensor", "unit": "TFLOP/s", "peak_kind": "bf16 dense, sustained (%s)" % peak_src}
+    else:
+        achieved = dom["bytes"] / dom["launches"] / (per_launch_ms / 1000.0) / 1e9
+        peak = peaks.get("hbm_gbs")
+        roof = {"bound": "hbm", "unit": "GB/s", "peak_kind": "HBM copy (%s)" % peak_src}
+    roof.update({"kernel": dom_tag, "achieved": achieved, "peak": peak, "frac": achieved / peak,
+                 "traffic": None, "ms_per_launch": per_launch_ms})
+
+    if rank == 0:
+        value = ws * B * args.steps / (ms / 1000.0)
+        cpu = None
+        if not args.no_cpu_baseline and ws == 1:
+            rate, nb, dt = cpu_oracle_rate()
+            cpu = {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                   "sample": "%d images [1,64,1024], one full 8+4-layer forward of the PyTorch eager oracle "
+                             "(fp32), %.1f s" % (nb, dt)}
+        breakdown = {k: {"launches": v["launches"], "ms_per_step": v["ms"] / args.steps,
+                         "share": v["ms"] / max(1e-9, sum(x["ms"] for x in kernels.values()))}
+                     for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "ocr_seq2seq_forward", "global_batch": ws * B, "per_gpu_batch": B,
+                       "seq_len": SEQ, "image": list(IMG), "T": 4, "d_model": 384, "heads": 8, "ff_dim": 1536,
+                       "layers": "8 enc + 4 dec", "vocab": 256, "parallelism": "dp%d (batch-sharded, no collective)" % ws,
+                       "l2": "inputs rotate over 4 sets of 67 MB images (> 126 MB L2); activations per step >> L2"},
+            "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+            "kernels": breakdown,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

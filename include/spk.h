@@ -1,0 +1,174 @@
+/*
+ * spk.h - C ABI of libspk.so, the B200 (sm_100a) kernels for the spiking
+ * hot path of flofiz/SpikingTransformer.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a device pointer unless stated otherwise; the library
+ *     allocates nothing.  Buffers are owned by the caller.
+ *   - Tensors are dense, row-major, in the reference's t-major fold: a tensor
+ *     "[T][R][F]" holds timestep t of row r, feature f at ((t*R)+r)*F+f.
+ *   - Neuron scalars (beta, v_th, v_reset, k, scale) are DEVICE pointers to
+ *     one fp32 value, as in the reference kernels (Lif.py:121-123,145-147), so
+ *     learnable values need no host synchronisation.
+ *   - `stream` is a cudaStream_t; work is enqueued there, nothing synchronises.
+ *   - Return value: 0 on success, otherwise an SPK_ERR_* code; the message of
+ *     the last failure on the calling thread is spk_last_error().
+ *
+ * Reference interfaces replaced (file:line in flofiz/SpikingTransformer):
+ *   spk_lif_fwd            lif_forward_kernel launch in LIFLayer.forward,
+ *                          Triton_Layers/Lif.py:17-43 (kernel Lif.py:118-165)
+ *   spk_lif_bwd            lif_backward_kernel launch + grad_beta sum in
+ *                          LIFLayer.backward, Lif.py:46-102 (kernel Lif.py:181-282)
+ *   spk_linear_ln_lif_fwd  nn.Linear -> nn.LayerNorm -> LIF triples:
+ *                          SSA.py:218-228 (q/k/v), SSA.py:247-249 (out_proj),
+ *                          SpikingMLP.py:31-36 (expand, compress), plus the
+ *                          residual adds Encoder.py:19,22 / Decoder.py:18-25
+ *   spk_linear_fwd         Seq2Seq.py:117 output_layer (nn.Linear)
+ *   spk_ssa_fwd            attention core of SSAMultiHeadAttention.forward,
+ *                          SSA.py:230-245 (xnor_attention :145-165, log-PE
+ *                          :177-201, mask, scale, @V, lifs) and of
+ *                          SSAMultiHeadAttention_.forward SSA.py:77-87
+ *   spk_embed_pe_lif_fwd   TokenEmbedding + PositionalEncoding + lifPE,
+ *                          Seq2Seq.py:11-36, :109-114
+ *   spk_patch_im2col       patch gather of the 16x16 patch-embedding image
+ *                          encoder (no reference counterpart; the OCR
+ *                          benchmark's ImageEncoder)
+ */
+#ifndef SPK_H_
+#define SPK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SPK_OK 0
+#define SPK_ERR_INVALID 1     /* bad argument (null pointer, bad enum)       */
+#define SPK_ERR_SHAPE 2       /* unsupported or inconsistent sizes            */
+#define SPK_ERR_ALIGN 3       /* pointer alignment requirement not met        */
+#define SPK_ERR_LAUNCH 4      /* kernel launch failed                          */
+#define SPK_ERR_TIMEOUT 5     /* a device-side wait gave up (bounded spin)    */
+#define SPK_ERR_UNSUPPORTED 6 /* device is not sm_100 / feature unavailable   */
+#define SPK_ERR_CUDA 7        /* other CUDA runtime error                      */
+
+/* element type codes */
+#define SPK_F32 0
+#define SPK_F16 1
+#define SPK_BF16 2
+#define SPK_U8 3
+
+/* LIF surrogate gradients */
+#define SPK_SURROGATE_SUPERSPIKE 0 /* 1/(1+k|v-th|)^2, Lif.py:280-282        */
+#define SPK_SURROGATE_ARCTAN 1     /* (a/2)/(1+(pi/2*a*(v-th))^2)            */
+
+int spk_version(void);
+const char* spk_status_string(int status);
+const char* spk_last_error(void);
+/* Reads (synchronising `stream`) and clears the device-side error flags set
+ * by bounded waits in the tensor-core kernels; SPK_ERR_TIMEOUT if any was set. */
+int spk_device_error_check(void* stream);
+
+/*
+ * LIF forward scan over T steps (Lif.py:118-165):
+ *   v_0 = 0;  v = beta*v + in_gain*x[t];  s[t] = (v > v_th);  v = s[t] ? v_reset : v
+ *   v_final = v after the last step.
+ * x: [T][N] of x_dtype (F32/F16/BF16), spikes: [T][N] of spike_dtype
+ * (F32/BF16/U8, values 0 or 1), v_final: [N] fp32 (may be NULL).
+ * in_gain == 1 reproduces the reference exactly (two roundings per step).
+ */
+int spk_lif_fwd(const void* x, int x_dtype, void* spikes, int spike_dtype, float* v_final,
+                const float* beta, const float* v_th, const float* v_reset, float in_gain,
+                int64_t T, int64_t N, void* stream);
+
+/*
+ * LIF backward (Lif.py:221-276) with the membrane history held in registers.
+ * g_spikes: [T][N] fp32; g_vfinal: [N] fp32 or NULL; x: [T][N] x_dtype;
+ * spikes: [T][N] spike_dtype (from spk_lif_fwd).  grad_x: [T][N] x_dtype.
+ * grad_beta: one fp32 (device), the sum over all neurons (Lif.py:95);
+ * may be NULL.  `surrogate_k` is k (SuperSpike) or alpha (arctan).
+ * workspace: fp32 scratch of spk_lif_bwd_workspace_bytes(T, N) bytes
+ * (per-block partial sums of grad_beta, reduced in a fixed order).
+ * T <= 64.
+ */
+int64_t spk_lif_bwd_workspace_bytes(int64_t T, int64_t N);
+int spk_lif_bwd(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype,
+                const void* spikes, int spike_dtype, const float* beta, const float* v_th,
+                const float* v_reset, float in_gain, int surrogate, float surrogate_k,
+                void* grad_x, float* grad_beta, void* workspace, int64_t workspace_bytes,
+                int64_t T, int64_t N, void* stream);
+
+/*
+ * Fused Linear -> LayerNorm -> LIF (tcgen05, bf16 operands, fp32 accumulate).
+ *   pre = A W^T + bias;  y = LN(pre) * ln_gamma + ln_beta  (over the N features,
+ *   eps = ln_eps);  LIF over T on y;  spikes (0/1) written as bf16 or fp32.
+ * t_broadcast == 0: A is [T][R][K] (t-major fold), spikes [T][R][N].
+ * t_broadcast != 0: A is [R][K]; the LIF sees the same y at every step (input
+ *                   repeated over T); spikes [T][R][N].
+ * W: [N][K] bf16 (nn.Linear layout).  bias/ln_gamma/ln_beta: [N] fp32 or NULL
+ * (0 / 1 / 0).  residual: [T][R][N] bf16 or NULL; if given, spikes are added
+ * into it in place (the residual stream of Encoder/Decoder layers).  spikes
+ * may be NULL when residual is given.  ln_out: [T][R][N] fp32 (or [R][N] for
+ * t_broadcast) copy of y, or NULL.  Requires K % 8 == 0, N % 32 == 0,
+ * N <= 4096 (rows wider than 384 are split over a CTA cluster), T <= 128.
+ */
+int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const float* ln_gamma,
+                          const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
+                          const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t K, int64_t N,
+                          int t_broadcast, void* spikes, int spike_dtype, void* residual, float* ln_out,
+                          void* stream);
+
+/* out[M][N] (fp32) = A[M][K] W[N][K]^T + bias (bias may be NULL); bf16 A, W. */
+int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, int64_t M, int64_t K, int64_t N,
+                   void* stream);
+
+/*
+ * Spiking attention core + output LIF.
+ * q: [T][B][Nq][H*dh], k, v: [T][B][Nk][H*dh], bf16 spikes (0/1).
+ * variant 1 (XNOR, SSA.py:145-165,235-242):
+ *   S[i,j] = dh - (|q_i| + |k_j| - 2 q_i.k_j) + R(|i-j|),
+ *   R(d) = max(0, ceil(log2((max(Nq,Nk)-1)/(d+1))))
+ * variant 0 (plain, SSA.py:81-84): S = q_i.k_j.
+ * S is multiplied by the mask, O = S V (exact integer), a = scale * O, then a
+ * LIF over T (lif_* parameters) gives out [T][B][Nq][H*dh] (bf16 or fp32).
+ * mask_mode 0: none; 1: causal (key index <= query index); 2: dense uint8,
+ * nonzero = keep, element (t,b,h,i,j) at t*mask_stride_t + b*mask_stride_b +
+ * h*mask_stride_h + i*mask_stride_q + j (strides in elements, 0 broadcasts).
+ * scale: device fp32 scalar (the learnable SSA.scale, or 0.125 for plain).
+ * attn_out: [T][B][H][Nq][dh] fp32 copy of a (the LIF input), or NULL.
+ * Requires dh % 8 == 0, 8 <= dh <= 64, Nq, Nk <= 8192.
+ */
+int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int mask_mode, const uint8_t* mask,
+                int64_t mask_stride_t, int64_t mask_stride_b, int64_t mask_stride_h, int64_t mask_stride_q,
+                const float* scale, const float* lif_beta, const float* lif_vth, const float* lif_vreset,
+                float in_gain, int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, void* out,
+                int out_dtype, float* attn_out, void* stream);
+
+/*
+ * tokens: [B][N] int64; emb: [V][D] fp32; pe: [>=N][D] fp32 (row n for
+ * position n).  x = emb[tok]*emb_scale + pe[n] (fp32, two roundings); LIF over
+ * T with input x at every step; out [T][B][N][D] bf16 or fp32.
+ * bad_token: device int set to 1 if a token is outside [0, V) (that token
+ * then reads row 0); the caller zeroes it beforehand.
+ */
+int spk_embed_pe_lif_fwd(const int64_t* tokens, const float* emb, float emb_scale, const float* pe,
+                         const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain,
+                         int64_t T, int64_t B, int64_t N, int64_t D, int64_t V, void* out, int out_dtype,
+                         int* bad_token, void* stream);
+
+/*
+ * img: [B][C][H][W] fp32 -> out: [B*(H/p)*(W/p)][2*C*p*p] bf16; row
+ * (b, ph, pw) in row-major patch order, columns [0, K) the bf16 rounding of
+ * pixel (c, i, j) at k = (c*p + i)*p + j, columns [K, 2K) the bf16 rounding
+ * of the remainder.  Against W' = [W | W] this reproduces Conv2d(C, D, p,
+ * stride p) in fp32 to ~2^-17 relative.
+ */
+int spk_patch_im2col(const float* img, int64_t B, int64_t C, int64_t H, int64_t W, int64_t patch, void* out,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPK_H_ */

@@ -1,0 +1,60 @@
+"""Decoder stack: drop-in for ``Triton_Layers/Decoder.py``.
+
+``DecoderLayer``: masked self-SSA, cross-SSA against the encoder output
+(no mask), MLP, each added to the residual stream (``Decoder.py:4-26``).
+``Decoder``: ``num_layers`` of them (``:28-43``).
+"""
+
+import torch
+import torch.nn as nn
+
+from ._fused import fast_path_ok
+from .Encoder import bf16_exact
+from .SSA import SSAMultiHeadAttention
+from .SpikingMLP import SpikingMLP
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, d_model, n_heads, ff_dim, dropout=0.1, alpha=0.125, n_steps=10):
+        super().__init__()
+        self.self_attns = SSAMultiHeadAttention(d_model=d_model, n_heads=n_heads, dropout=dropout, alpha=alpha,
+                                                n_steps=n_steps)
+        self.cross_attns = SSAMultiHeadAttention(d_model=d_model, n_heads=n_heads, dropout=dropout, alpha=alpha,
+                                                 n_steps=n_steps)
+        self.mlp = SpikingMLP(d_model=d_model, ff_dim=ff_dim, n_steps=n_steps)
+
+    def _fast(self, x, enc, mask=None):
+        """In place on the bf16 residual stream ``x``; ``enc`` bf16 encoder output."""
+        self.self_attns._fast(x, None, mask)
+        self.cross_attns._fast(x, enc, None)
+        self.mlp._fast(x)
+        return x
+
+    def forward(self, x, enc_output, mask=None):
+        if fast_path_ok(x, enc_output, mask, module=self) and bf16_exact(x) and bf16_exact(enc_output):
+            enc = enc_output.to(torch.bfloat16).contiguous()
+            return self._fast(x.to(torch.bfloat16).contiguous(), enc, mask).to(x.dtype)
+        x = x + self.self_attns(x, x, x, attention_mask=mask)
+        x = x + self.cross_attns(x, enc_output, enc_output)
+        return x + self.mlp(x)
+
+
+class Decoder(nn.Module):
+    def __init__(self, num_layers, d_model, n_heads, ff_dim, dropout=0.1, alpha=0.125, n_steps=10):
+        super().__init__()
+        self.layers = nn.ModuleList([
+            DecoderLayer(d_model=d_model, n_heads=n_heads, ff_dim=ff_dim, dropout=dropout, alpha=alpha,
+                         n_steps=n_steps) for _ in range(num_layers)])
+
+    def _fast(self, x, enc, mask=None):
+        for layer in self.layers:
+            layer._fast(x, enc, mask)
+        return x
+
+    def forward(self, x, enc_output, mask=None):
+        if fast_path_ok(x, enc_output, mask, module=self) and bf16_exact(x) and bf16_exact(enc_output):
+            enc = enc_output.to(torch.bfloat16).contiguous()
+            return self._fast(x.to(torch.bfloat16).contiguous(), enc, mask).to(x.dtype)
+        for layer in self.layers:
+            x = layer(x, enc_output, mask=mask)
+        return x

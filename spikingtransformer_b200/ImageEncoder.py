@@ -1,0 +1,142 @@
+"""Image encoders: drop-in for ``Triton_Layers/ImageEncoder.py`` plus the
+16x16 patch embedding of the OCR benchmark.
+
+``CNNBackbone`` and its blocks (``ImageEncoder.py:8-102``) keep the reference
+structure and names; their convolutions and batch norms are library (cuDNN)
+ops and every LIF is this package's kernel.  ``PatchEmbed`` (no reference
+counterpart) is Conv2d(C, D, p, stride p) -> tokens in row-major patch order
+-> LayerNorm(D) -> LIF, computed as one fused tensor-core GEMM over gathered
+patches: pixels are split into two bf16 terms against [W | W], which keeps
+the projection at fp32 accuracy (~2^-17 relative).
+"""
+
+import torch
+from torch import nn
+
+from . import ops
+from ._fused import bf16_weight, fast_path_ok, lif_params
+from .Lif import LIF
+
+
+class FusedInvertedBottleneck(nn.Module):
+    """``ImageEncoder.py:8-28``: conv3x3 64->512, BN, LIF, conv1x1 512->64, BN, LIF, + identity."""
+
+    def __init__(self, n_steps=1, threshold=0.5):
+        super().__init__()
+        self.conv1 = nn.Conv2d(64, 512, kernel_size=3, stride=1, padding=1)
+        self.bn1 = nn.BatchNorm2d(512)
+        self.lif_1 = LIF(n_steps=n_steps, beta=0.5)
+        self.conv2 = nn.Conv2d(512, 64, kernel_size=1, stride=1, padding=0)
+        self.bn2 = nn.BatchNorm2d(64)
+        self.lif_2 = LIF(n_steps=n_steps, beta=0.5)
+
+    def forward(self, x):
+        out = self.lif_1(self.bn1(self.conv1(x)))[0]
+        out = self.lif_2(self.bn2(self.conv2(out)))[0]
+        return out + x
+
+
+class ReduceConvBlock(nn.Module):
+    """``ImageEncoder.py:31-44``: fold (channel, height) into channels, 1x1 conv, BN, LIF."""
+
+    def __init__(self, in_channels=1, out_channels=512, n_steps=1, threshold=0.5):
+        super().__init__()
+        self.conv = nn.Conv2d(64 * 8, out_channels, kernel_size=1)
+        self.bn = nn.BatchNorm2d(out_channels)
+        self.lif = LIF(n_steps=n_steps, beta=0.5)
+
+    def forward(self, x):
+        b, c, h, w = x.shape
+        x = x.reshape(b, c * h, w).unsqueeze(-2)
+        out = self.bn(self.conv(x)).squeeze(-2)
+        return self.lif(out)[0]
+
+
+class RPE2D(nn.Module):
+    """``ImageEncoder.py:47-61``: conv1d k3 + BN + LIF."""
+
+    def __init__(self, d_model, stride=1, n_steps=1, threshold=0.5):
+        super().__init__()
+        self.conv = nn.Conv1d(d_model, d_model, kernel_size=3, stride=stride, padding=1)
+        self.lif = LIF(n_steps=n_steps, beta=0.5)
+        self.bn = nn.BatchNorm1d(d_model)
+
+    def get_mem(self):
+        return {"mem": getattr(self.lif, "mem", None)}
+
+    def forward(self, x):
+        return self.lif(self.bn(self.conv(x)))[0]
+
+
+class CNNBackbone(nn.Module):
+    """``ImageEncoder.py:64-102``; ``forward(x[T*B,1,32,W]) -> (tokens [T*B, W/4, D], record)``."""
+
+    def __init__(self, d_model=512, nb_layers=11, patch_size=4, n_steps=1, threshold=0.5):
+        super().__init__()
+        self.nb_layers = nb_layers
+        self.d_model = d_model
+        self.layers = nn.ModuleList([FusedInvertedBottleneck(n_steps=n_steps, threshold=threshold)
+                                     for _ in range(nb_layers)])
+        self.space_to_depth = nn.PixelUnshuffle(patch_size)
+        self.conv1 = nn.Conv2d(16, 128, kernel_size=3, stride=1, padding=1)
+        self.bn1 = nn.BatchNorm2d(128)
+        self.lif_1 = LIF(n_steps=n_steps, beta=0.5)
+        self.conv2 = nn.Conv2d(128, 64, kernel_size=1, stride=1, padding=0)
+        self.bn2 = nn.BatchNorm2d(64)
+        self.lif_2 = LIF(n_steps=n_steps, beta=0.5)
+        self.reduce = ReduceConvBlock(64, d_model, n_steps=n_steps, threshold=threshold)
+        self.rpe = RPE2D(d_model, n_steps=n_steps, threshold=threshold)
+
+    def forward(self, x):
+        record = {}
+        x = self.space_to_depth(x)
+        x = self.lif_1(self.bn1(self.conv1(x)))[0]
+        record["conv1"] = x
+        x = self.lif_2(self.bn2(self.conv2(x)))[0]
+        record["conv2"] = x
+        record["FusedInvertedBottleneck"] = []
+        for layer in self.layers:
+            x = layer(x)
+            record["FusedInvertedBottleneck"].append(x)
+        x = self.reduce(x)
+        rpe_value = self.rpe(x)
+        x = (x + rpe_value).transpose(-1, -2)
+        record["RPE2D"] = rpe_value
+        record["output"] = x
+        return x, record
+
+
+class PatchEmbed(nn.Module):
+    """Patch image encoder: ``forward(x[T*B, C, H, W]) -> (spikes [T*B, (H/p)(W/p), D], record)``."""
+
+    def __init__(self, d_model=384, patch_size=16, n_steps=1, in_chans=1):
+        super().__init__()
+        self.patch_size = patch_size
+        self.d_model = d_model
+        self.proj = nn.Conv2d(in_chans, d_model, kernel_size=patch_size, stride=patch_size)
+        self.norm = nn.LayerNorm(d_model)
+        self.lif = LIF(n_steps=n_steps)
+
+    def _fused(self, images, t_broadcast):
+        """images [rows, C, H, W] fp32 -> bf16 spikes [T*B, n_patches, D]."""
+        T = self.lif.n_steps
+        a = ops.patch_im2col(images, self.patch_size)
+        p = lif_params(self.lif)
+        s, _ = ops.linear_ln_lif(a, bf16_weight(self.proj, duplicate=True), self.proj.bias, self.norm.weight,
+                                 self.norm.bias, self.norm.eps, p[0:1], p[1:2], p[2:3], T,
+                                 in_gain=self.lif.in_gain, t_broadcast=t_broadcast)
+        n_patch = a.shape[0] // images.shape[0]
+        TB = T * images.shape[0] if t_broadcast else images.shape[0]
+        return s.view(TB, n_patch, self.d_model)
+
+    def encode_images(self, src):
+        """The T-fold of ``src [B, C, H, W]`` repeated over T, computed once per image."""
+        return self._fused(src, t_broadcast=True)
+
+    def forward(self, x):
+        if fast_path_ok(x, module=self):
+            s = self._fused(x, t_broadcast=False).float()
+            return s, {"output": s}
+        y = self.proj(x).flatten(2).transpose(1, 2)
+        s = self.lif(self.norm(y))[0]
+        return s, {"output": s}

@@ -1,0 +1,200 @@
+"""Spiking self-attention: drop-in for ``Triton_Layers/SSA.py``.
+
+``SSAMultiHeadAttention`` (XNOR scores + log-distance bias + learnable scale,
+``SSA.py:103-258``) and ``SSAMultiHeadAttention_`` (plain ``Q K^T``, fixed
+0.125 scale after ``@ V``, ``SSA.py:10-100``) keep the reference constructor
+arguments, submodule names (q_proj, k_proj, v_proj, lnq..lno, lifq..lifo,
+out_proj, scale) and ``forward(query, key=None, value=None,
+attention_mask=None) -> [B', N, D]`` fp32 spikes.
+
+Inference (no autograd graph needed): three fused Linear->LN->LIF kernels
+produce Q, K, V spikes, ``spk_ssa_fwd`` computes the attention core and the
+``lifs`` LIF, and a fourth fused kernel applies out_proj->lno->lifo.
+Training: the reference composition (torch Linear / LayerNorm / einsum) over
+the LIF kernels of this package, so autograd sees the same graph as the
+reference.
+"""
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from ._fused import fast_path_ok, lif_params, lin_ln_lif
+from .Lif import LIF
+
+
+class _SSACore(nn.Module):
+    variant = 1
+
+    def __init__(self, d_model, n_heads, n_steps, bias):
+        super().__init__()
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.d_head = d_model // n_heads
+        self.q_proj = nn.Linear(d_model, d_model, bias=bias)
+        self.k_proj = nn.Linear(d_model, d_model, bias=bias)
+        self.v_proj = nn.Linear(d_model, d_model, bias=bias)
+        self.lnq = nn.LayerNorm(d_model)
+        self.lnk = nn.LayerNorm(d_model)
+        self.lnv = nn.LayerNorm(d_model)
+        self.lno = nn.LayerNorm(d_model)
+        self.lifq = LIF(n_steps=n_steps)
+        self.lifk = LIF(n_steps=n_steps)
+        self.lifv = LIF(n_steps=n_steps)
+        self.lifs = LIF(n_steps=n_steps, v_th=0.5)
+        self.lifo = LIF(n_steps=n_steps)
+        self.out_proj = nn.Linear(d_model, d_model, bias=bias)
+
+    # ---------------------------------------------------------------- fused path
+
+    def _scale_tensor(self, device):
+        raise NotImplementedError
+
+    def _attend(self, q, k, v, T, mask, out_dtype=torch.bfloat16):
+        """q [T*B, Nq, D], k/v [T*B, Nk, D] bf16 spikes -> lifs spikes."""
+        TB = q.shape[0]
+        p = lif_params(self.lifs)
+        causal = False
+        if isinstance(mask, str) and mask == "causal":
+            causal, mask = True, None
+        out, _ = ops.ssa(q, k, v, T, TB // T, self.n_heads, self.variant, self._scale_tensor(q.device),
+                         p[0:1], p[1:2], p[2:3], in_gain=self.lifs.in_gain, mask=mask, causal=causal,
+                         out_dtype=out_dtype)
+        return out
+
+    def _fast(self, x, kv=None, mask=None):
+        """Residual step on bf16 spike counts: ``x += SSA(x, kv, kv)`` in place.
+
+        ``x``: [T*B, Nq, D] bf16; ``kv``: [T*B, Nk, D] bf16 or None (self);
+        ``mask``: None, "causal", or a mask accepted by ``ops.ssa``.
+        """
+        T = self.lifq.n_steps
+        TB, Nq, D = x.shape
+        src = x if kv is None else kv
+        Nk = src.shape[1]
+        q = lin_ln_lif(x, self.q_proj, self.lnq, self.lifq, T)[0].view(TB, Nq, D)
+        k = lin_ln_lif(src, self.k_proj, self.lnk, self.lifk, T)[0].view(TB, Nk, D)
+        v = lin_ln_lif(src, self.v_proj, self.lnv, self.lifv, T)[0].view(TB, Nk, D)
+        a = self._attend(q, k, v, T, mask)
+        lin_ln_lif(a, self.out_proj, self.lno, self.lifo, T, residual=x.view(-1, D), want_spikes=False)
+        return x
+
+    def _fast_public(self, query, key, value, attention_mask):
+        T = self.lifq.n_steps
+        TB, N, D = query.shape
+        Nk = key.shape[1]
+        q = lin_ln_lif(query, self.q_proj, self.lnq, self.lifq, T)[0].view(TB, N, D)
+        k = lin_ln_lif(key, self.k_proj, self.lnk, self.lifk, T)[0].view(TB, Nk, D)
+        v = lin_ln_lif(value, self.v_proj, self.lnv, self.lifv, T)[0].view(TB, Nk, D)
+        a = self._attend(q, k, v, T, attention_mask)
+        out = lin_ln_lif(a, self.out_proj, self.lno, self.lifo, T, spike_dtype=torch.float32)[0]
+        return out.view(TB, N, D)
+
+    # ---------------------------------------------------------------- autograd path
+
+    def _heads(self, t, n):
+        return t.view(t.shape[0], n, self.n_heads, self.d_head).transpose(1, 2)
+
+    def _scores(self, q, k):
+        raise NotImplementedError
+
+    def _reference_forward(self, query, key, value, attention_mask):
+        TB, N, D = query.shape
+        Nk = key.shape[1]
+        q = self._heads(self.lifq(self.lnq(self.q_proj(query)))[0], N)
+        k = self._heads(self.lifk(self.lnk(self.k_proj(key)))[0], Nk)
+        v = self._heads(self.lifv(self.lnv(self.v_proj(value)))[0], Nk)
+        a = self._combine(q, k, v, attention_mask)
+        s = self.lifs(a)[0].transpose(1, 2).contiguous().view(TB, N, D)
+        return self.lifo(self.lno(self.out_proj(s)))[0]
+
+    def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
+                attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        key = query if key is None else key
+        value = query if value is None else value
+        if fast_path_ok(query, key, value, attention_mask, module=self):
+            return self._fast_public(query, key, value, attention_mask)
+        return self._reference_forward(query, key, value, attention_mask)
+
+    def extra_repr(self) -> str:
+        return f"d_model={self.d_model}, n_heads={self.n_heads}, d_head={self.d_head}"
+
+
+class SSAMultiHeadAttention(_SSACore):
+    """XNOR spiking attention (``SSA.py:103-258``).
+
+    ``S = Dh - (sum q + sum k - 2 q.k) + R``, ``R[i,j] = max(0,
+    ceil(log2((max(Nq,Nk)-1)/(|i-j|+1))))``, ``S *= mask``,
+    ``out = LIF_{v_th=.5}((S * scale) @ V)``; ``alpha``, ``causal``,
+    ``learnable_alpha`` and ``dropout`` are accepted and unused, as in the
+    reference.
+    """
+
+    variant = 1
+
+    def __init__(self, d_model: int, n_heads: int, alpha: Optional[float] = None, causal: bool = False,
+                 learnable_alpha: bool = False, dropout: float = 0.0, n_steps: int = 1, bias: bool = True):
+        super().__init__(d_model, n_heads, n_steps, bias)
+        self.scale = nn.Parameter(torch.sqrt(torch.tensor(1.0 / (d_model // n_heads))), requires_grad=True)
+
+    def _scale_tensor(self, device):
+        return self.scale.detach()
+
+    @staticmethod
+    def xnor_attention_scores(q, k):
+        dh = q.shape[-1]
+        qk = torch.einsum("bhld,bhmd->bhlm", q, k)
+        return dh - (q.sum(-1, keepdim=True) + k.sum(-1, keepdim=True).transpose(2, 3) - 2 * qk)
+
+    def xnor_attention(self, Q, K):
+        """``Dh - Hamming(Q, K)`` as in ``SSA.py:145-165``."""
+        return self.xnor_attention_scores(Q, K)
+
+    def get_log_pe_bias(self, seq_len, device):
+        """Self-attention log-distance bias (``SSA.py:167-175``)."""
+        return self.get_log_pe_bias_cross(seq_len, seq_len, device)
+
+    def get_log_pe_bias_cross(self, seq_len_q, seq_len_k, device):
+        """``max(0, ceil(log2((max(Lq,Lk)-1)/(|i-j|+1))))``, ``SSA.py:177-201``."""
+        iq = torch.arange(seq_len_q, device=device).unsqueeze(1)
+        jk = torch.arange(seq_len_k, device=device).unsqueeze(0)
+        dist = (iq - jk).abs().float()
+        L = max(seq_len_q, seq_len_k)
+        return torch.ceil(torch.log2((L - 1) / (dist + 1))).clamp(min=0)
+
+    def _combine(self, q, k, v, mask):
+        a = self.xnor_attention(q, k)
+        a = a + self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device).unsqueeze(0).unsqueeze(0)
+        if mask is not None:
+            a = a * mask
+        return (a * self.scale) @ v
+
+
+class SSAMultiHeadAttention_(_SSACore):
+    """Plain spiking attention (``SSA.py:10-100``):
+    ``out = LIF_{v_th=.5}(((Q K^T) * mask) @ V * 0.125)``."""
+
+    variant = 0
+
+    def __init__(self, d_model: int, n_heads: int, alpha: Optional[float] = None, causal: bool = False,
+                 learnable_alpha: bool = False, dropout: float = 0.0, n_steps: int = 1, bias: bool = True):
+        super().__init__(d_model, n_heads, n_steps, bias)
+
+    def _scale_tensor(self, device):
+        c = getattr(self, "_spk_scale", None)
+        if c is None or c.device != device:
+            c = torch.full((1,), 0.125, dtype=torch.float32, device=device)
+            object.__setattr__(self, "_spk_scale", c)
+        return c
+
+    def _combine(self, q, k, v, mask):
+        a = q @ k.transpose(-2, -1)
+        if mask is not None:
+            a = a * mask
+        return (a @ v) * 0.125
+
+
+_ = math  # kept for parity with the reference module namespace

@@ -1,0 +1,86 @@
+"""Plumbing shared by the module classes: cached bf16 weight copies, packed
+device-side LIF parameters and the Linear -> LayerNorm -> LIF call.
+
+Derived state only (never saved in the state dict): caches are keyed on the
+source tensor's storage pointer and version counter, so an optimizer step or
+``load_state_dict`` invalidates them without a host synchronisation.
+"""
+
+import torch
+
+from . import ops
+
+
+def _key(*ts):
+    return tuple((t.data_ptr(), t._version, t.device, t.dtype) for t in ts)
+
+
+def bf16_weight(lin, duplicate=False):
+    """bf16 copy of ``lin.weight`` ([N, K]); with ``duplicate`` the columns are
+    repeated, [W | W] ([N, 2K]), for split-precision inputs."""
+    w = lin.weight
+    attr = "_spk_w2" if duplicate else "_spk_w"
+    k = _key(w)
+    cached = getattr(lin, attr, None)
+    if cached is not None and cached[0] == k:
+        return cached[1]
+    with torch.no_grad():
+        wb = w.detach().reshape(w.shape[0], -1).to(torch.bfloat16)
+        if duplicate:
+            wb = torch.cat([wb, wb], dim=1)
+        wb = wb.contiguous()
+    object.__setattr__(lin, attr, (k, wb))
+    return wb
+
+
+def lif_params(lif):
+    """fp32 device tensor [beta, v_th, v_reset] of a LIF module (cached)."""
+    beta_src = lif.beta_raw if lif.learn_beta else lif.beta
+    k = _key(beta_src, lif.v_th, lif.v_reset)
+    cached = getattr(lif, "_spk_params", None)
+    if cached is not None and cached[0] == k:
+        return cached[1]
+    with torch.no_grad():
+        b = torch.sigmoid(beta_src.detach()) if lif.learn_beta else beta_src.detach()
+        p = torch.stack([b.float().reshape(()), lif.v_th.detach().float().reshape(()),
+                         lif.v_reset.detach().float().reshape(())]).contiguous()
+    object.__setattr__(lif, "_spk_params", (k, p))
+    return p
+
+
+def split_bf16(x):
+    """fp32 ``[..., K]`` -> bf16 ``[..., 2K]`` = [hi | lo] with hi + lo ~ x."""
+    x = x.float()
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    return torch.cat([hi, lo], dim=-1)
+
+
+def lin_ln_lif(x, lin, ln, lif, T, t_broadcast=False, residual=None, spike_dtype=torch.bfloat16,
+               want_spikes=True, want_ln_out=False):
+    """``lif(ln(lin(x)))`` through the fused kernel.
+
+    ``x``: bf16 (used as is: exact for spike counts) or fp32 (split into two
+    bf16 terms against [W | W]).  Returns ``(spikes [rows, N], ln_out)``.
+    """
+    if x.dtype == torch.bfloat16:
+        A, W = x, bf16_weight(lin)
+    else:
+        A, W = split_bf16(x), bf16_weight(lin, duplicate=True)
+    K = A.shape[-1]
+    p = lif_params(lif)
+    return ops.linear_ln_lif(A.reshape(-1, K), W, lin.bias, ln.weight, ln.bias, ln.eps, p[0:1], p[1:2], p[2:3], T,
+                             in_gain=lif.in_gain, t_broadcast=t_broadcast, spike_dtype=spike_dtype,
+                             residual=residual, want_spikes=want_spikes, want_ln_out=want_ln_out)
+
+
+def fast_path_ok(*tensors, module=None):
+    """Inference fast path: CUDA tensors and no autograd graph to build."""
+    if not all(t is None or t.is_cuda for t in tensors):
+        return False
+    if torch.is_grad_enabled():
+        if any(t is not None and t.requires_grad for t in tensors):
+            return False
+        if module is not None and any(p.requires_grad for p in module.parameters()):
+            return False
+    return True

@@ -1,0 +1,407 @@
+// LIF temporal scan, forward and backward (HBM-bound elementwise recurrences).
+//
+// Reference: Triton_Layers/Lif.py:118-165 (forward), :181-282 (backward).
+// Layout: x, spikes, grads are [T][N] (N = batch * features, t-major), the
+// reference's [T, B, F] after .contiguous().
+//
+// One thread owns VEC consecutive neurons and walks all T steps with the
+// membrane in registers; loads and stores are 16-byte vectors where the
+// pointers allow.  The backward keeps the pre-reset membrane of all T steps in
+// registers (T <= 64), so unlike the reference there is no v_mem_history
+// round trip through HBM.  Arithmetic uses explicitly rounded fp32 operations
+// (__fmul_rn / __fadd_rn / __fdiv_rn, never contracted into FMA) in the
+// reference's order, so results are bit-identical to the reference evaluated
+// in fp32 one operation at a time.
+#include "common.cuh"
+
+namespace spk {
+namespace lifk {
+
+template <typename T, int VEC>
+struct alignas(sizeof(T) * VEC >= 16 ? 16 : sizeof(T) * VEC) Pack {
+  T v[VEC];
+};
+
+template <int DT, int VEC>
+__device__ __forceinline__ void load_vec(const void* base, int64_t idx, float* out) {
+  using T = typename Elem<DT>::T;
+  const T* p = reinterpret_cast<const T*>(base) + idx;
+  if constexpr (VEC == 1) {
+    out[0] = Elem<DT>::load(p);
+  } else if constexpr (sizeof(T) * VEC <= 16) {
+    Pack<T, VEC> pk = *reinterpret_cast<const Pack<T, VEC>*>(p);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) out[i] = Elem<DT>::load(&pk.v[i]);
+  } else {
+    constexpr int H = VEC / 2;
+    load_vec<DT, H>(base, idx, out);
+    load_vec<DT, H>(base, idx + H, out + H);
+  }
+}
+
+template <int DT, int VEC>
+__device__ __forceinline__ void store_vec(void* base, int64_t idx, const float* in) {
+  using T = typename Elem<DT>::T;
+  T* p = reinterpret_cast<T*>(base) + idx;
+  if constexpr (VEC == 1) {
+    *p = Elem<DT>::make(in[0]);
+  } else if constexpr (sizeof(T) * VEC <= 16) {
+    Pack<T, VEC> pk;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) pk.v[i] = Elem<DT>::make(in[i]);
+    *reinterpret_cast<Pack<T, VEC>*>(p) = pk;
+  } else {
+    constexpr int H = VEC / 2;
+    store_vec<DT, H>(base, idx, in);
+    store_vec<DT, H>(base, idx + H, in + H);
+  }
+}
+
+template <int XDT, int SDT, int VEC>
+__global__ void __launch_bounds__(256) lif_fwd_kernel(const void* __restrict__ x, void* __restrict__ spikes,
+                                                      float* __restrict__ v_final, const float* pbeta,
+                                                      const float* pvth, const float* pvr, float gain, int T,
+                                                      int64_t N) {
+  const float beta = __ldg(pbeta), vth = __ldg(pvth), vr = __ldg(pvr);
+  const bool use_gain = gain != 1.0f;
+  const int64_t groups = N / VEC;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    float v[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = 0.0f;
+    const int64_t col = g * VEC;
+    for (int t = 0; t < T; ++t) {
+      float xv[VEC], sv[VEC];
+      load_vec<XDT, VEC>(x, (int64_t)t * N + col, xv);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        float cur = use_gain ? __fmul_rn(xv[i], gain) : xv[i];
+        float u = __fadd_rn(__fmul_rn(v[i], beta), cur);
+        bool s = u > vth;
+        sv[i] = s ? 1.0f : 0.0f;
+        v[i] = s ? vr : u;
+      }
+      store_vec<SDT, VEC>(spikes, (int64_t)t * N + col, sv);
+    }
+    if (v_final) store_vec<SPK_F32, VEC>(v_final, col, v);
+  }
+}
+
+__device__ __forceinline__ float surrogate(int kind, float u, float k, float c_arctan) {
+  if (kind == SPK_SURROGATE_SUPERSPIKE) {
+    float a = __fadd_rn(1.0f, __fmul_rn(k, fabsf(u)));
+    return __fdiv_rn(__fdiv_rn(1.0f, a), a);
+  }
+  float z = __fmul_rn(c_arctan, u);
+  return __fdiv_rn(__fmul_rn(k, 0.5f), __fadd_rn(1.0f, __fmul_rn(z, z)));
+}
+
+constexpr int kBwdThreads = 256;
+constexpr int kBwdMaxBlocks = 4096;
+
+template <int XDT, int SDT, int TMAX, int VEC>
+__global__ void __launch_bounds__(kBwdThreads) lif_bwd_kernel(
+    const float* __restrict__ gs, const float* __restrict__ gvf, const void* __restrict__ x,
+    const void* __restrict__ spikes, const float* pbeta, const float* pvth, const float* pvr, float gain,
+    int surr, float k, float c_arctan, void* __restrict__ gx, float* __restrict__ partials, int T, int64_t N) {
+  const float beta = __ldg(pbeta), vth = __ldg(pvth), vr = __ldg(pvr);
+  const bool use_gain = gain != 1.0f;
+  const int64_t groups = N / VEC;
+  float thread_acc = 0.0f;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = g * VEC;
+    float vh[TMAX][VEC];
+    uint32_t sbits[TMAX];
+    float v[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = 0.0f;
+    // pass 1: recompute the pre-reset membrane (Lif.py:222-233)
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) {
+      if (t < T) {
+        float xv[VEC], sv[VEC];
+        load_vec<XDT, VEC>(x, (int64_t)t * N + col, xv);
+        load_vec<SDT, VEC>(spikes, (int64_t)t * N + col, sv);
+        uint32_t bits = 0;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          float cur = use_gain ? __fmul_rn(xv[i], gain) : xv[i];
+          float u = __fadd_rn(__fmul_rn(v[i], beta), cur);
+          vh[t][i] = u;
+          bool s = sv[i] > 0.0f;
+          bits |= (s ? 1u : 0u) << i;
+          v[i] = s ? vr : u;
+        }
+        sbits[t] = bits;
+      }
+    }
+    // pass 2: reverse sweep (Lif.py:236-273)
+    float gstate[VEC], acc[VEC];
+    if (gvf) {
+      load_vec<SPK_F32, VEC>(gvf, col, gstate);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) gstate[i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = 0.0f;
+#pragma unroll
+    for (int t = TMAX - 1; t >= 0; --t) {
+      if (t < T) {
+        float gsv[VEC], out[VEC];
+        load_vec<SPK_F32, VEC>(gs, (int64_t)t * N + col, gsv);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const bool s = (sbits[t] >> i) & 1u;
+          const float sg = surrogate(surr, __fadd_rn(vh[t][i], -vth), k, c_arctan);
+          const float from_state = s ? 0.0f : gstate[i];
+          const float gv = __fadd_rn(__fmul_rn(gsv[i], sg), from_state);
+          out[i] = use_gain ? __fmul_rn(gv, gain) : gv;
+          float vprev = 0.0f;
+          if (t > 0) vprev = ((sbits[t - 1] >> i) & 1u) ? vr : vh[t - 1][i];
+          acc[i] = __fadd_rn(acc[i], __fmul_rn(gv, vprev));
+          gstate[i] = __fmul_rn(gv, beta);
+        }
+        store_vec<XDT, VEC>(gx, (int64_t)t * N + col, out);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) thread_acc += acc[i];
+  }
+  // deterministic block reduction of the grad_beta partial
+  __shared__ float red[kBwdThreads / 32];
+  float s = thread_acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float r = threadIdx.x < kBwdThreads / 32 ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (threadIdx.x == 0 && partials) partials[blockIdx.x] = r;
+  }
+}
+
+__global__ void __launch_bounds__(1024) sum_partials_kernel(const float* __restrict__ partials, int n,
+                                                            float* __restrict__ out) {
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += partials[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float r = threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (threadIdx.x == 0) *out = r;
+  }
+}
+
+int grid_for(int64_t groups, int threads) {
+  int64_t need = (groups + threads - 1) / threads;
+  int64_t cap = (int64_t)num_sms() * (2048 / threads) * 4;
+  if (need > cap) need = cap;
+  if (need < 1) need = 1;
+  return (int)need;
+}
+
+template <int XDT, int SDT, int VEC>
+void launch_fwd(const void* x, void* s, float* vf, const float* b, const float* th, const float* vr, float gain,
+                int T, int64_t N, cudaStream_t st) {
+  int grid = grid_for(N / VEC, 256);
+  lif_fwd_kernel<XDT, SDT, VEC><<<grid, 256, 0, st>>>(x, s, vf, b, th, vr, gain, T, N);
+}
+
+template <int XDT, int SDT>
+void dispatch_fwd_vec(bool vec, const void* x, void* s, float* vf, const float* b, const float* th,
+                      const float* vr, float gain, int T, int64_t N, cudaStream_t st) {
+  if (vec)
+    launch_fwd<XDT, SDT, 8>(x, s, vf, b, th, vr, gain, T, N, st);
+  else
+    launch_fwd<XDT, SDT, 1>(x, s, vf, b, th, vr, gain, T, N, st);
+}
+
+template <int XDT>
+int dispatch_fwd_s(int sdt, bool vec, const void* x, void* s, float* vf, const float* b, const float* th,
+                   const float* vr, float gain, int T, int64_t N, cudaStream_t st) {
+  switch (sdt) {
+    case SPK_F32: dispatch_fwd_vec<XDT, SPK_F32>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
+    case SPK_BF16: dispatch_fwd_vec<XDT, SPK_BF16>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
+    case SPK_U8: dispatch_fwd_vec<XDT, SPK_U8>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
+    default: return fail(SPK_ERR_INVALID, "spike dtype %d not supported", sdt);
+  }
+}
+
+template <int XDT, int SDT, int TMAX, int VEC>
+void launch_bwd(int grid, const float* gs, const float* gvf, const void* x, const void* s, const float* b,
+                const float* th, const float* vr, float gain, int surr, float k, float c, void* gx, float* part,
+                int T, int64_t N, cudaStream_t st) {
+  lif_bwd_kernel<XDT, SDT, TMAX, VEC><<<grid, kBwdThreads, 0, st>>>(gs, gvf, x, s, b, th, vr, gain, surr, k, c,
+                                                                    gx, part, T, N);
+}
+
+template <int XDT, int SDT>
+int dispatch_bwd_t(int T, bool vec, int grid, const float* gs, const float* gvf, const void* x, const void* s,
+                   const float* b, const float* th, const float* vr, float gain, int surr, float k, float c,
+                   void* gx, float* part, int64_t N, cudaStream_t st) {
+  if (T <= 8) {
+    if (vec) launch_bwd<XDT, SDT, 8, 4>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+    else launch_bwd<XDT, SDT, 8, 1>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+  } else if (T <= 16) {
+    if (vec) launch_bwd<XDT, SDT, 16, 4>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+    else launch_bwd<XDT, SDT, 16, 1>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+  } else {
+    launch_bwd<XDT, SDT, 64, 1>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+  }
+  return SPK_OK;
+}
+
+template <int XDT>
+int dispatch_bwd_s(int sdt, int T, bool vec, int grid, const float* gs, const float* gvf, const void* x,
+                   const void* s, const float* b, const float* th, const float* vr, float gain, int surr, float k,
+                   float c, void* gx, float* part, int64_t N, cudaStream_t st) {
+  switch (sdt) {
+    case SPK_F32:
+      return dispatch_bwd_t<XDT, SPK_F32>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
+    case SPK_BF16:
+      return dispatch_bwd_t<XDT, SPK_BF16>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
+    case SPK_U8:
+      return dispatch_bwd_t<XDT, SPK_U8>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
+    default: return fail(SPK_ERR_INVALID, "spike dtype %d not supported", sdt);
+  }
+}
+
+}  // namespace lifk
+
+using namespace lifk;
+
+// Shared implementation of the backward entry points: `partials` holds at
+// least bwd_grid(T, N) floats.
+int lif_bwd_impl(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype, const void* spikes,
+                 int spike_dtype, const float* beta, const float* v_th, const float* v_reset, float in_gain,
+                 int surrogate_kind, float surrogate_k, void* grad_x, float* grad_beta, float* partials,
+                 int64_t T, int64_t N, cudaStream_t st);
+
+int lif_bwd_grid(int64_t T, int64_t N) {
+  const bool vec = true;
+  int64_t groups = vec && T <= 16 ? N / 4 : N;
+  int g = grid_for(groups, kBwdThreads);
+  return g > kBwdMaxBlocks ? kBwdMaxBlocks : g;
+}
+
+int lif_bwd_impl(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype, const void* spikes,
+                 int spike_dtype, const float* beta, const float* v_th, const float* v_reset, float in_gain,
+                 int surrogate_kind, float surrogate_k, void* grad_x, float* grad_beta, float* partials,
+                 int64_t T, int64_t N, cudaStream_t st) {
+  // the vector path needs N % 4 == 0 and 16-byte aligned rows for fp32 tensors
+  bool vec = T <= 16 && (N % 4 == 0) && aligned(g_spikes, 16) && (!g_vfinal || aligned(g_vfinal, 16)) &&
+             aligned(x, 4 * dtype_size(x_dtype)) && aligned(spikes, 4 * dtype_size(spike_dtype)) &&
+             aligned(grad_x, 4 * dtype_size(x_dtype));
+  int64_t groups = vec ? N / 4 : N;
+  int grid = grid_for(groups, kBwdThreads);
+  if (grid > kBwdMaxBlocks) grid = kBwdMaxBlocks;
+  const float c = (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k);
+  int rc;
+  switch (x_dtype) {
+    case SPK_F32:
+      rc = dispatch_bwd_s<SPK_F32>(spike_dtype, (int)T, vec, grid, g_spikes, g_vfinal, x, spikes, beta, v_th,
+                                   v_reset, in_gain, surrogate_kind, surrogate_k, c, grad_x, partials, N, st);
+      break;
+    case SPK_F16:
+      rc = dispatch_bwd_s<SPK_F16>(spike_dtype, (int)T, vec, grid, g_spikes, g_vfinal, x, spikes, beta, v_th,
+                                   v_reset, in_gain, surrogate_kind, surrogate_k, c, grad_x, partials, N, st);
+      break;
+    case SPK_BF16:
+      rc = dispatch_bwd_s<SPK_BF16>(spike_dtype, (int)T, vec, grid, g_spikes, g_vfinal, x, spikes, beta, v_th,
+                                    v_reset, in_gain, surrogate_kind, surrogate_k, c, grad_x, partials, N, st);
+      break;
+    default: return fail(SPK_ERR_INVALID, "x dtype %d not supported", x_dtype);
+  }
+  if (rc != SPK_OK) return rc;
+  if ((rc = check_launch("lif_bwd_kernel")) != SPK_OK) return rc;
+  if (grad_beta) {
+    sum_partials_kernel<<<1, 1024, 0, st>>>(partials, grid, grad_beta);
+    if ((rc = check_launch("sum_partials_kernel")) != SPK_OK) return rc;
+  }
+  return SPK_OK;
+}
+
+static int check_lif_args(const void* x, int x_dtype, const void* spikes, int spike_dtype, const float* beta,
+                          const float* v_th, const float* v_reset, int64_t T, int64_t N) {
+  // an empty tensor may carry a null data pointer
+  SPK_REQUIRE((x && spikes) || N == 0, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(beta && v_th && v_reset, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(x_dtype == SPK_F32 || x_dtype == SPK_F16 || x_dtype == SPK_BF16, SPK_ERR_INVALID,
+              "x dtype %d not supported", x_dtype);
+  SPK_REQUIRE(spike_dtype == SPK_F32 || spike_dtype == SPK_BF16 || spike_dtype == SPK_U8, SPK_ERR_INVALID,
+              "spike dtype %d not supported", spike_dtype);
+  SPK_REQUIRE(T >= 1 && T <= 64, SPK_ERR_SHAPE, "T=%lld outside [1, 64]", (long long)T);
+  SPK_REQUIRE(N >= 0, SPK_ERR_SHAPE, "N=%lld negative", (long long)N);
+  SPK_REQUIRE(aligned(x, dtype_size(x_dtype)) && aligned(spikes, dtype_size(spike_dtype)), SPK_ERR_ALIGN,
+              "x / spikes not aligned to their element size");
+  return SPK_OK;
+}
+
+}  // namespace spk
+
+extern "C" {
+
+int spk_lif_fwd(const void* x, int x_dtype, void* spikes, int spike_dtype, float* v_final, const float* beta,
+                const float* v_th, const float* v_reset, float in_gain, int64_t T, int64_t N, void* stream) {
+  using namespace spk;
+  int rc = check_lif_args(x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, T, N);
+  if (rc != SPK_OK) return rc;
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  if (N == 0) return SPK_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = (N % 8 == 0) && aligned(x, 8 * dtype_size(x_dtype)) &&
+                   aligned(spikes, 8 * dtype_size(spike_dtype)) && (!v_final || aligned(v_final, 32));
+  switch (x_dtype) {
+    case SPK_F32: rc = dispatch_fwd_s<SPK_F32>(spike_dtype, vec, x, spikes, v_final, beta, v_th, v_reset, in_gain, (int)T, N, st); break;
+    case SPK_F16: rc = dispatch_fwd_s<SPK_F16>(spike_dtype, vec, x, spikes, v_final, beta, v_th, v_reset, in_gain, (int)T, N, st); break;
+    default: rc = dispatch_fwd_s<SPK_BF16>(spike_dtype, vec, x, spikes, v_final, beta, v_th, v_reset, in_gain, (int)T, N, st); break;
+  }
+  if (rc != SPK_OK) return rc;
+  return check_launch("lif_fwd_kernel");
+}
+
+int64_t spk_lif_bwd_workspace_bytes(int64_t T, int64_t N) {
+  (void)T;
+  (void)N;
+  return (int64_t)spk::kBwdMaxBlocks * (int64_t)sizeof(float);
+}
+
+int spk_lif_bwd(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype, const void* spikes,
+                int spike_dtype, const float* beta, const float* v_th, const float* v_reset, float in_gain,
+                int surrogate, float surrogate_k, void* grad_x, float* grad_beta, void* workspace,
+                int64_t workspace_bytes, int64_t T, int64_t N, void* stream) {
+  using namespace spk;
+  int rc = check_lif_args(x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, T, N);
+  if (rc != SPK_OK) return rc;
+  SPK_REQUIRE((g_spikes && grad_x) || N == 0, SPK_ERR_INVALID, "null gradient pointer");
+  SPK_REQUIRE(surrogate == SPK_SURROGATE_SUPERSPIKE || surrogate == SPK_SURROGATE_ARCTAN, SPK_ERR_INVALID,
+              "unknown surrogate %d", surrogate);
+  SPK_REQUIRE(aligned(g_spikes, 4) && aligned(grad_x, dtype_size(x_dtype)), SPK_ERR_ALIGN,
+              "gradient pointers misaligned");
+  if (grad_beta) {
+    SPK_REQUIRE(workspace && workspace_bytes >= spk_lif_bwd_workspace_bytes(T, N), SPK_ERR_INVALID,
+                "workspace of %lld bytes is smaller than spk_lif_bwd_workspace_bytes() = %lld",
+                (long long)workspace_bytes, (long long)spk_lif_bwd_workspace_bytes(T, N));
+    SPK_REQUIRE(aligned(workspace, 4), SPK_ERR_ALIGN, "workspace misaligned");
+  }
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    if (grad_beta) cudaMemsetAsync(grad_beta, 0, sizeof(float), st);
+    return SPK_OK;
+  }
+  return lif_bwd_impl(g_spikes, g_vfinal, x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, in_gain,
+                      surrogate, surrogate_k, grad_x, grad_beta, reinterpret_cast<float*>(workspace), T, N, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+"""Tensor-level wrappers over the C ABI (no autograd; see Lif.py for that).
+
+Every function requires CUDA tensors and raises on CPU input: there is no
+CPU implementation in this package.
+"""
+
+import torch
+
+from . import _lib
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("spikingtransformer_b200 ops need CUDA tensors (got %s)" % t.device)
+
+
+def _scalar_f32(v, device):
+    """A one-element fp32 device tensor holding ``v`` (tensor or number)."""
+    if isinstance(v, torch.Tensor):
+        if v.device != device:
+            v = v.to(device)
+        if v.dtype != torch.float32:
+            v = v.float()
+        return v.reshape(1).contiguous()
+    return torch.full((1,), float(v), dtype=torch.float32, device=device)
+
+
+def lif_fwd(x, beta, v_th, v_reset, in_gain=1.0, spike_dtype=torch.float32, want_v_final=True):
+    """LIF scan over dim 0 of ``x`` ([T, ...]); returns ``(spikes, v_final)``.
+
+    ``x`` may be fp32/fp16/bf16; spikes are ``spike_dtype`` (fp32, bf16 or
+    uint8); ``v_final`` is fp32 shaped like ``x[0]`` (or None).
+    """
+    _cuda(x)
+    x = x.contiguous()
+    T = x.shape[0]
+    N = x[0].numel()
+    dev = x.device
+    s = torch.empty(x.shape, dtype=spike_dtype, device=dev)
+    vf = torch.empty(x.shape[1:], dtype=torch.float32, device=dev) if want_v_final else None
+    b, th, vr = (_scalar_f32(v, dev) for v in (beta, v_th, v_reset))
+    nbytes = T * N * (x.element_size() + s.element_size()) + (4 * N if vf is not None else 0)
+    _lib.call("spk_lif_fwd", _lib.ptr(x), _lib.dtype_code(x), _lib.ptr(s), _lib.dtype_code(s), _lib.ptr(vf),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, N, _lib.stream_ptr(dev),
+              tag="lif_fwd", work=dict(bytes=nbytes))
+    return s, vf
+
+
+def lif_bwd(g_spikes, g_vfinal, x, spikes, beta, v_th, v_reset, in_gain=1.0, surrogate="superspike", k=4.0,
+            need_beta_grad=True):
+    """Backward of ``lif_fwd``; returns ``(grad_x in x.dtype, grad_beta fp32 [1] or None)``."""
+    _cuda(g_spikes, g_vfinal, x, spikes)
+    x = x.contiguous()
+    spikes = spikes.contiguous()
+    g_spikes = g_spikes.contiguous().to(torch.float32)
+    if g_vfinal is not None:
+        g_vfinal = g_vfinal.contiguous().to(torch.float32)
+    T = x.shape[0]
+    N = x[0].numel()
+    dev = x.device
+    gx = torch.empty_like(x)
+    b, th, vr = (_scalar_f32(v, dev) for v in (beta, v_th, v_reset))
+    gb = ws = None
+    wsb = 0
+    if need_beta_grad:
+        gb = torch.empty(1, dtype=torch.float32, device=dev)
+        wsb = int(_lib.load().spk_lif_bwd_workspace_bytes(T, N))
+        ws = torch.empty(wsb // 4, dtype=torch.float32, device=dev)
+    _lib.call("spk_lif_bwd", _lib.ptr(g_spikes), _lib.ptr(g_vfinal), _lib.ptr(x), _lib.dtype_code(x),
+              _lib.ptr(spikes), _lib.dtype_code(spikes), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain),
+              _lib.SURROGATE[surrogate], float(k), _lib.ptr(gx), _lib.ptr(gb), _lib.ptr(ws), wsb, T, N,
+              _lib.stream_ptr(dev), tag="lif_bwd",
+              work=dict(bytes=T * N * (4 + 2 * x.element_size() + spikes.element_size()), launches=2))
+    return gx, gb
+
+
+def linear_ln_lif(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
+                  t_broadcast=False, spike_dtype=torch.bfloat16, residual=None, want_spikes=True,
+                  want_ln_out=False):
+    """Fused ``LIF(LayerNorm(A @ W.T + bias))`` over the t-major fold.
+
+    ``A``: bf16 ``[T*R, K]`` (or ``[R, K]`` with ``t_broadcast``); ``W``: bf16
+    ``[N, K]``.  Returns ``(spikes [T*R, N] or None, ln_out fp32 or None)``.
+    With ``residual`` (bf16 ``[T*R, N]``) the spikes are also added into it.
+    """
+    _cuda(A, W, residual)
+    if A.dtype != torch.bfloat16 or W.dtype != torch.bfloat16:
+        raise TypeError("linear_ln_lif expects bf16 A and W")
+    A = A.contiguous()
+    W = W.contiguous()
+    K = A.shape[-1]
+    N = W.shape[0]
+    rows = A.numel() // K
+    R = rows if t_broadcast else rows // T
+    if not t_broadcast and rows % T:
+        raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
+    dev = A.device
+    out_rows = T * R
+    spikes = torch.empty((out_rows, N), dtype=spike_dtype, device=dev) if want_spikes else None
+    ln_out = torch.empty(((R if t_broadcast else out_rows), N), dtype=torch.float32, device=dev) \
+        if want_ln_out else None
+    if residual is not None and (residual.dtype != torch.bfloat16 or not residual.is_contiguous()):
+        raise TypeError("residual must be a contiguous bf16 tensor")
+    f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    bias, ln_gamma, ln_beta = f(bias), f(ln_gamma), f(ln_beta)
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_linear_ln_lif_fwd", _lib.ptr(A), _lib.ptr(W), _lib.ptr(bias), _lib.ptr(ln_gamma),
+              _lib.ptr(ln_beta), float(ln_eps), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, K, N,
+              1 if t_broadcast else 0, _lib.ptr(spikes), _lib.DTYPE_CODE[spike_dtype], _lib.ptr(residual),
+              _lib.ptr(ln_out), _lib.stream_ptr(dev), tag="linear_ln_lif K=%d N=%d" % (K, N),
+              work=dict(flops=2.0 * rows * K * N))
+    return spikes, ln_out
+
+
+def linear(A, W, bias=None):
+    """``A @ W.T + bias`` in fp32 from bf16 ``A [M, K]`` and ``W [N, K]``."""
+    _cuda(A, W)
+    A = A.contiguous()
+    W = W.contiguous()
+    M, K = A.numel() // A.shape[-1], A.shape[-1]
+    N = W.shape[0]
+    out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    bias = None if bias is None else bias.float().contiguous()
+    _lib.call("spk_linear_fwd", _lib.ptr(A), _lib.ptr(W), _lib.ptr(bias), _lib.ptr(out), M, K, N,
+              _lib.stream_ptr(A.device), tag="linear K=%d N=%d" % (K, N), work=dict(flops=2.0 * M * K * N))
+    return out
+
+
+def ssa(q, k, v, T, B, H, variant, scale, lif_beta, lif_vth, lif_vr, in_gain=1.0, mask=None, causal=False,
+        out_dtype=torch.bfloat16, want_attn=False):
+    """Spiking attention core + output LIF on head-merged bf16 spikes.
+
+    ``q``: ``[T*B, Nq, H*dh]``, ``k``/``v``: ``[T*B, Nk, H*dh]``.  ``mask``:
+    None, or a tensor broadcastable to ``[T, B, H, Nq, Nk]`` (nonzero = keep);
+    ``causal=True`` uses the built-in key <= query mask instead.
+    Returns ``(spikes [T*B, Nq, H*dh], attn fp32 [T*B, H, Nq, dh] or None)``.
+    """
+    _cuda(q, k, v, mask)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    Nq, D = q.shape[-2], q.shape[-1]
+    Nk = k.shape[-2]
+    dh = D // H
+    dev = q.device
+    out = torch.empty(q.shape, dtype=out_dtype, device=dev)
+    attn = torch.empty((T * B, H, Nq, dh), dtype=torch.float32, device=dev) if want_attn else None
+    mask_mode, mptr, strides = 0, None, (0, 0, 0, 0)
+    m8 = None
+    if causal:
+        mask_mode = 1
+    elif mask is not None:
+        m8 = mask_to_u8(mask, T, B, H, Nq, Nk)
+        mask_mode, mptr = 2, m8.data_ptr()
+        strides = tuple(m8.stride(i) for i in range(4))
+    sc, b, th, vr = (_scalar_f32(x, dev) for x in (scale, lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_ssa_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), int(variant), mask_mode, mptr, *strides,
+              _lib.ptr(sc), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, B, H, Nq, Nk, dh,
+              _lib.ptr(out), _lib.DTYPE_CODE[out_dtype], _lib.ptr(attn), _lib.stream_ptr(dev),
+              tag="ssa Nq=%d Nk=%d" % (Nq, Nk), work=dict(flops=4.0 * T * B * H * Nq * Nk * dh))
+    return out, attn
+
+
+def mask_to_u8(mask, T, B, H, Nq, Nk):
+    """uint8 view of an attention mask, expanded (stride 0) to [T, B, H, Nq, Nk].
+
+    Accepts the reference's T-folded masks ``[T*B, 1|H, Nq, Nk]`` and any mask
+    broadcastable to ``[B, H, Nq, Nk]``.
+    """
+    if mask.dtype == torch.uint8 and mask.dim() == 5 and tuple(mask.shape) == (T, B, H, Nq, Nk):
+        return mask  # already converted
+    m = (mask != 0).to(torch.uint8)
+    if m.dim() == 4 and m.shape[0] == T * B and T * B != B:
+        m = m.reshape(T, B, *m.shape[1:])
+    else:
+        while m.dim() < 4:
+            m = m.unsqueeze(0)
+        m = m.unsqueeze(0)
+    m = m.expand(T, B, H, Nq, Nk)
+    if m.stride(-1) != 1:
+        m = m.contiguous()
+    return m
+
+
+def embed_pe_lif(tokens, emb, emb_scale, pe, lif_beta, lif_vth, lif_vr, T, in_gain=1.0, out_dtype=torch.bfloat16):
+    """``LIF(T-fold(emb[tokens]*emb_scale + pe[:N]))`` -> spikes ``[T*B, N, D]``."""
+    _cuda(tokens, emb, pe)
+    tokens = tokens.to(torch.int64).contiguous()
+    B, N = tokens.shape
+    V, D = emb.shape
+    emb = emb.float().contiguous()
+    pe = pe.reshape(-1, D).float().contiguous()
+    dev = tokens.device
+    out = torch.empty((T * B, N, D), dtype=out_dtype, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    b, th, vr = (_scalar_f32(x, dev) for x in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_embed_pe_lif_fwd", _lib.ptr(tokens), _lib.ptr(emb), float(emb_scale), _lib.ptr(pe), _lib.ptr(b),
+              _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, B, N, D, V, _lib.ptr(out), _lib.DTYPE_CODE[out_dtype],
+              _lib.ptr(bad), _lib.stream_ptr(dev), tag="embed_pe_lif",
+              work=dict(bytes=B * N * (8 + 8 * D) + T * B * N * D * out.element_size()))
+    return out, bad
+
+
+def patch_im2col(img, patch):
+    """``[B, C, H, W]`` fp32 -> bf16 ``[B*(H/p)*(W/p), 2*C*p*p]`` (hi | lo split)."""
+    _cuda(img)
+    img = img.float().contiguous()
+    B, C, H, W = img.shape
+    K = C * patch * patch
+    out = torch.empty((B * (H // patch) * (W // patch), 2 * K), dtype=torch.bfloat16, device=img.device)
+    _lib.call("spk_patch_im2col", _lib.ptr(img), B, C, H, W, patch, _lib.ptr(out), _lib.stream_ptr(img.device),
+              tag="patch_im2col", work=dict(bytes=img.numel() * 4 + out.numel() * 2))
+    return out
+
+
+def device_error_check(device=None):
+    """Synchronise and raise if a kernel's bounded wait gave up."""
+    _lib.call("spk_device_error_check", _lib.stream_ptr(device))

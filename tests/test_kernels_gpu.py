@@ -1,0 +1,291 @@
+"""Kernel-level parity: libspk.so (through the C ABI) against the CPU oracle
+and the golden fixtures made from the reference.
+
+Rules (tests/parity.py): spikes bit-exact outside the 1e-4 near-threshold
+band; membrane / LayerNorm outputs within 1e-3 relative; SSA spike-count
+products bit-exact.
+"""
+
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from oracle import modules as om
+from parity import assert_spikes_match, assert_close_rel, membrane_history
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from spikingtransformer_b200 import ops as o
+    return o
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+# ------------------------------------------------------------------ LIF
+
+
+@pytest.mark.parametrize("spike_dtype", [torch.float32, torch.bfloat16, torch.uint8])
+def test_lif_fwd_cfg1_bit_exact(ops, spike_dtype):
+    # LIF forward at the CPU benchmark shape [T=4, B=8, N=128, D=256], tau=2
+    g = gen(0)
+    x = torch.randn(4, 8, 128, 256, generator=g) + 0.5
+    x3 = x.reshape(4, 8, -1)
+    s_ref, vf_ref = oracle.lif_forward(x3, 0.5, 1.0, 0.0, in_gain=0.5)
+    s, vf = ops.lif_fwd(x3.to(DEV), 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype=spike_dtype)
+    assert torch.equal(s.float().cpu(), s_ref)
+    assert torch.equal(vf.cpu(), vf_ref)
+
+
+def test_lif_golden(ops, golden_dir):
+    for c in torch.load(os.path.join(golden_dir, "lif.pt"), weights_only=False):
+        x = c["x_in"].to(DEV)
+        s, vf = ops.lif_fwd(x, c["beta"], c["v_th"], c["v_reset"])
+        assert torch.equal(s.cpu(), c["spikes"]), c["dtype"]
+        assert torch.equal(vf.cpu(), c["v_final"]), c["dtype"]
+        gx, gb = ops.lif_bwd(c["g_spikes"].to(DEV), None, x, s, c["beta"], c["v_th"], c["v_reset"])
+        assert torch.equal(gx.cpu(), c["grad_x"].to(gx.dtype))
+        assert torch.allclose(gb.cpu().reshape(()), c["grad_beta"], rtol=1e-5, atol=1e-5)
+        gx, gb = ops.lif_bwd(c["g_spikes"].to(DEV), c["g_vfinal"].to(DEV), x, s, c["beta"], c["v_th"], c["v_reset"])
+        assert torch.equal(gx.cpu(), c["grad_x_vf"].to(gx.dtype))
+        assert torch.allclose(gb.cpu().reshape(()), c["grad_beta_vf"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("T,N", [(1, 5), (3, 1023), (8, 4096), (13, 77), (20, 640), (64, 33)])
+@pytest.mark.parametrize("surrogate", ["superspike", "arctan"])
+def test_lif_shapes_and_surrogates(ops, T, N, surrogate):
+    g = gen(T * 1000 + N)
+    x = torch.randn(T, N, generator=g) + 0.3
+    gs = torch.randn(T, N, generator=g)
+    gvf = torch.randn(N, generator=g)
+    s_ref, vf_ref = oracle.lif_forward(x, 0.8, 0.9, -0.1)
+    s, vf = ops.lif_fwd(x.to(DEV), 0.8, 0.9, -0.1)
+    assert torch.equal(s.cpu(), s_ref)
+    assert torch.equal(vf.cpu(), vf_ref)
+    gx_ref, gb_ref = oracle.lif_backward(gs, gvf, x, s_ref, 0.8, 0.9, -0.1, k=2.0, surrogate=surrogate)
+    gx, gb = ops.lif_bwd(gs.to(DEV), gvf.to(DEV), x.to(DEV), s, 0.8, 0.9, -0.1, surrogate=surrogate, k=2.0)
+    if surrogate == "superspike":
+        assert torch.equal(gx.cpu(), gx_ref)
+    else:
+        assert torch.allclose(gx.cpu(), gx_ref, rtol=1e-6, atol=1e-7)
+    assert torch.allclose(gb.cpu().reshape(()), gb_ref, rtol=1e-4, atol=1e-5)
+
+
+def test_lif_empty(ops):
+    x = torch.empty(4, 0, device=DEV)
+    s, vf = ops.lif_fwd(x, 0.9, 1.0, 0.0)
+    assert s.shape == (4, 0)
+
+
+def test_lif_rejects_cpu(ops):
+    with pytest.raises(RuntimeError):
+        ops.lif_fwd(torch.zeros(2, 3), 0.9, 1.0, 0.0)
+
+
+def test_lif_rejects_long_T(ops):
+    with pytest.raises(RuntimeError):
+        ops.lif_fwd(torch.zeros(65, 8, device=DEV), 0.9, 1.0, 0.0)
+
+
+# ------------------------------------------------------------------ Linear -> LN -> LIF
+
+
+def ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, lif_beta, vth, vr, gain=1.0, t_broadcast=False, eps=1e-5):
+    pre = A.float() @ W.float().t() + bias
+    y = F.layer_norm(pre, (W.shape[0],), gamma, beta_ln, eps)
+    if t_broadcast:
+        y3 = y.unsqueeze(0).expand(T, *y.shape).reshape(T, -1)
+    else:
+        y3 = y.reshape(T, -1)
+    s, _ = oracle.lif_forward(y3, lif_beta, vth, vr, in_gain=gain)
+    vh = membrane_history(y3, lif_beta, vth, vr, gain)
+    return s.reshape(-1, W.shape[0]), y, vh
+
+
+def make_lin(seed, R, K, N, T, t_broadcast=False, counts=1, p=0.15):
+    g = gen(seed)
+    rows = R if t_broadcast else T * R
+    A = torch.zeros(rows, K)
+    for _ in range(counts):
+        A += (torch.rand(rows, K, generator=g) < p).float()
+    bound = 1.0 / K ** 0.5
+    W = ((torch.rand(N, K, generator=g) * 2 - 1) * bound).to(torch.bfloat16)
+    bias = (torch.rand(N, generator=g) * 2 - 1) * 0.01
+    gamma = 1.0 + 0.1 * torch.randn(N, generator=g)
+    beta_ln = 0.1 * torch.randn(N, generator=g)
+    return A.to(torch.bfloat16), W, bias, gamma, beta_ln
+
+
+@pytest.mark.parametrize("T,R,K,N", [
+    (4, 256, 384, 384),     # QKV / out_proj shape
+    (4, 96, 384, 1536),     # MLP expand (cluster of 4 CTAs)
+    (4, 64, 1536, 384),     # MLP compress
+    (2, 24, 32, 32),        # small model
+    (3, 50, 64, 128),       # T not dividing 128, partial tiles
+    (1, 300, 128, 64),
+    (10, 37, 96, 512),
+])
+def test_linear_ln_lif(ops, T, R, K, N):
+    A, W, bias, gamma, beta_ln = make_lin(T * 7 + R + K + N, R, K, N, T, counts=2)
+    s_ref, y_ref, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.9, 1.0, 0.0)
+    s, y = ops.linear_ln_lif(A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.9, 1.0,
+                             0.0, T, want_ln_out=True, spike_dtype=torch.float32)
+    assert_close_rel(y, y_ref, what="layernorm out")
+    assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+
+
+def test_linear_ln_lif_cfg2_tau(ops):
+    # fused Linear->LN->LIF at the cfg-2 feature sizes (tau=2 neuron), fewer rows
+    T, R, K, N = 4, 2048, 384, 1536
+    A, W, bias, _, _ = make_lin(2, R, K, N, T)
+    gamma, beta_ln = torch.ones(N), torch.zeros(N)
+    s_ref, y_ref, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.5, 1.0, 0.0, gain=0.5)
+    s, y = ops.linear_ln_lif(A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.5, 1.0,
+                             0.0, T, in_gain=0.5, want_ln_out=True)
+    assert_close_rel(y, y_ref, what="layernorm out")
+    assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+
+
+def test_linear_ln_lif_residual_and_tbcast(ops):
+    T, R, K, N = 4, 200, 256, 384
+    A, W, bias, gamma, beta_ln = make_lin(5, R, K, N, T, t_broadcast=True)
+    s_ref, y_ref, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.9, 1.0, 0.0, t_broadcast=True)
+    resid = torch.randint(0, 5, (T * R, N)).to(torch.bfloat16)
+    r_dev = resid.to(DEV)
+    s, y = ops.linear_ln_lif(A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.9, 1.0,
+                             0.0, T, t_broadcast=True, residual=r_dev, want_ln_out=True)
+    assert_close_rel(y, y_ref, what="layernorm out")
+    assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+    assert torch.equal(r_dev.float().cpu(), resid.float() + s.float().cpu())
+
+
+def test_linear_plain(ops):
+    for M, K, N in [(300, 384, 256), (77, 64, 40), (1000, 128, 600)]:
+        g = gen(M + N)
+        A = torch.randint(0, 4, (M, K), generator=g).to(torch.bfloat16)
+        W = torch.randn(N, K, generator=g).to(torch.bfloat16)
+        b = torch.randn(N, generator=g)
+        out = ops.linear(A.to(DEV), W.to(DEV), b.to(DEV))
+        ref = A.float() @ W.float().t() + b
+        assert torch.allclose(out.cpu(), ref, rtol=1e-5, atol=1e-4)
+
+
+def test_patch_embed_split(ops):
+    g = gen(3)
+    img = torch.rand(3, 1, 32, 64, generator=g)
+    Wc = (torch.randn(64, 1, 16, 16, generator=g) * 0.05).to(torch.bfloat16).float()
+    a = ops.patch_im2col(img.to(DEV), 16)
+    W2 = torch.cat([Wc.reshape(64, -1), Wc.reshape(64, -1)], 1).to(torch.bfloat16)
+    out = ops.linear(a, W2.to(DEV))
+    ref = F.conv2d(img, Wc, stride=16).flatten(2).transpose(1, 2).reshape(-1, 64)
+    assert torch.allclose(out.cpu(), ref, rtol=2e-5, atol=2e-5)
+
+
+# ------------------------------------------------------------------ SSA
+
+
+def ref_ssa(q, k, v, T, H, variant, scale, mask, vth=0.5, beta=0.9, gain=1.0):
+    """q,k,v [T*B, N, D] float spikes -> (spikes, attn, exact integer O)."""
+    TB, Nq, D = q.shape
+    Nk = k.shape[1]
+    dh = D // H
+    qh = q.view(TB, Nq, H, dh).transpose(1, 2)
+    kh = k.view(TB, Nk, H, dh).transpose(1, 2)
+    vh = v.view(TB, Nk, H, dh).transpose(1, 2)
+    if variant == 1:
+        m = om.SSAMultiHeadAttention(D, H, n_steps=T)
+        with torch.no_grad():
+            m.scale.fill_(scale)
+            attn = m.attention(qh, kh, vh, mask)
+        s_int = om.SSAMultiHeadAttention.xnor_scores(qh.double(), kh.double()) + \
+            om.log_pe_bias(Nq, Nk).double()
+    else:
+        attn = om.SSAMultiHeadAttention_.attention(None, qh, kh, vh, mask)
+        s_int = qh.double() @ kh.double().transpose(-2, -1)
+    if mask is not None:
+        s_int = s_int * mask.double()
+    o_int = s_int @ vh.double()
+    x3 = attn.reshape(T, -1)
+    s, _ = oracle.lif_forward(x3, beta, vth, 0.0, in_gain=gain)
+    vhist = membrane_history(x3, beta, vth, 0.0, gain)
+    spikes = s.reshape(TB, H, Nq, dh).transpose(1, 2).reshape(TB, Nq, D)
+    return spikes, attn, o_int, vhist
+
+
+def spikes_qkv(seed, TB, Nq, Nk, D, p=0.15):
+    g = gen(seed)
+    q = (torch.rand(TB, Nq, D, generator=g) < p).float()
+    k = (torch.rand(TB, Nk, D, generator=g) < p).float()
+    v = (torch.rand(TB, Nk, D, generator=g) < p).float()
+    return q, k, v
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("T,B,H,Nq,Nk,dh,maskkind", [
+    (2, 2, 4, 12, 12, 8, None),
+    (2, 3, 2, 40, 40, 48, "causal"),
+    (4, 2, 8, 256, 256, 48, None),     # encoder shape (two key blocks)
+    (4, 2, 8, 64, 64, 48, "causal"),   # decoder self-attention
+    (4, 2, 8, 64, 256, 48, None),      # decoder cross-attention
+    (2, 2, 2, 130, 70, 64, "dense"),
+    (1, 1, 1, 200, 300, 16, "dense"),
+])
+def test_ssa(ops, variant, T, B, H, Nq, Nk, dh, maskkind):
+    D = H * dh
+    q, k, v = spikes_qkv(Nq * 31 + Nk + dh + variant, T * B, Nq, Nk, D, p=0.2 if variant == 0 else 0.15)
+    scale = 0.125 if variant == 0 else (1.0 / dh) ** 0.5
+    mask = None
+    if maskkind == "causal":
+        mask = torch.tril(torch.ones(Nq, Nk)).expand(T * B, 1, Nq, Nk)
+    elif maskkind == "dense":
+        mask = (torch.rand(T * B, 1, Nq, Nk, generator=gen(9)) < 0.7).float()
+    s_ref, attn_ref, o_int, vhist = ref_ssa(q, k, v, T, H, variant, scale, mask)
+    s, attn = ops.ssa(q.to(DEV).bfloat16(), k.to(DEV).bfloat16(), v.to(DEV).bfloat16(), T, B, H, variant, scale,
+                      0.9, 0.5, 0.0, mask=None if maskkind == "causal" else (mask.to(DEV) if mask is not None else None),
+                      causal=maskkind == "causal", out_dtype=torch.float32, want_attn=True)
+    # spike-count products: a = fl(scale * O) with O the exact integer product
+    expect = (o_int.float() * torch.tensor(scale, dtype=torch.float32))
+    assert torch.equal(attn.cpu(), expect), "attention products differ from the exact integer product"
+    assert_close_rel(attn, attn_ref, tol=1e-5, what="attention vs reference rounding")
+    s_ours = s.cpu().reshape(T * B, Nq, H, dh).transpose(1, 2).reshape(T, -1)
+    s_want = s_ref.reshape(T * B, Nq, H, dh).transpose(1, 2).reshape(T, -1)
+    if variant == 0:
+        # plain: a = 0.125 * integer is computed exactly on both sides, so the
+        # spike trains must agree bit for bit (values sit exactly on v_th often)
+        assert torch.equal(s_ours, s_want)
+    else:
+        assert_spikes_match(s_ours, s_want, vhist.reshape(T, -1), 0.5, what="ssa spikes")
+
+
+# ------------------------------------------------------------------ embedding
+
+
+def test_embed_pe_lif(ops):
+    g = gen(4)
+    V, D, B, N, T = 50, 32, 3, 7, 4
+    pe_mod = om.PositionalEncoding(D, 0.0, maxlen=64)
+    emb = torch.randn(V, D, generator=g).to(torch.bfloat16).float()
+    tok = torch.randint(0, V, (B, N), generator=g)
+    x = emb[tok] * (D ** 0.5) + pe_mod.pos_embedding[:, :N]
+    x3 = x.unsqueeze(0).expand(T, B, N, D).reshape(T, -1)
+    s_ref, _ = oracle.lif_forward(x3, 0.9, 1.0, 0.0)
+    s, bad = ops.embed_pe_lif(tok.to(DEV), emb.to(DEV), D ** 0.5, pe_mod.pos_embedding.to(DEV), 0.9, 1.0, 0.0, T,
+                              out_dtype=torch.float32)
+    assert int(bad.item()) == 0
+    assert torch.equal(s.cpu().reshape(T, -1), s_ref)
+    _, bad = ops.embed_pe_lif((tok + V).to(DEV), emb.to(DEV), D ** 0.5, pe_mod.pos_embedding.to(DEV), 0.9, 1.0, 0.0,
+                              T)
+    assert int(bad.item()) == 1
+
+
+def test_no_device_timeouts(ops):
+    ops.device_error_check()

@@ -1,0 +1,61 @@
+"""Host-side checks of the C ABI that need no GPU: the library loads, exports
+every entry point include/spk.h declares, and rejects bad arguments before
+touching the device."""
+
+import ctypes
+
+import pytest
+
+from spikingtransformer_b200 import _lib
+
+
+def test_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _lib.header_symbols()
+    assert len(declared) >= 10
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    # every declared symbol has a ctypes signature in the binding
+    assert set(declared) <= set(_lib.SIGNATURES), set(declared) - set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.spk_version() >= 1
+    assert lib.spk_status_string(0) == b"ok"
+    assert lib.spk_status_string(5) == b"device wait timed out"
+
+
+def test_null_arguments_rejected_without_device():
+    lib = _lib.load()
+    rc = lib.spk_lif_fwd(None, 0, None, 0, None, None, None, None, 1.0, 4, 16, None)
+    assert rc == 1
+    assert b"null" in lib.spk_last_error()
+    rc = lib.spk_ssa_fwd(None, None, None, 1, 0, None, 0, 0, 0, 0, None, None, None, None, 1.0,
+                         1, 1, 1, 1, 1, 48, None, 2, None, None)
+    assert rc == 1
+
+
+def test_shape_limits_rejected_without_device():
+    lib = _lib.load()
+    buf = ctypes.c_void_p(16)  # never dereferenced: shape checks come first
+    rc = lib.spk_lif_fwd(buf, 0, buf, 0, None, buf, buf, buf, 1.0, 65, 16, None)
+    assert rc == 2
+    rc = lib.spk_ssa_fwd(buf, buf, buf, 1, 0, None, 0, 0, 0, 0, buf, buf, buf, buf, 1.0,
+                         1, 1, 1, 8, 8, 100, buf, 2, None, None)
+    assert rc == 2
+    rc = lib.spk_linear_ln_lif_fwd(buf, buf, None, None, None, 1e-5, buf, buf, buf, 1.0, 4, 8, 12, 64, 0, buf,
+                                   2, None, None, None)
+    assert rc == 2  # K % 8 != 0
+
+
+def test_workspace_query():
+    lib = _lib.load()
+    assert lib.spk_lif_bwd_workspace_bytes(4, 1000) >= 4
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from spikingtransformer_b200 import ops
+    with pytest.raises(RuntimeError):
+        ops.lif_fwd(torch.zeros(2, 4), 0.9, 1.0, 0.0)

@@ -1,0 +1,212 @@
+"""Module-level parity of the Triton_Layers-compatible surface on the GPU:
+against the golden fixtures (made by running the reference) and the CPU
+oracle, including the full OCR benchmark architecture at a small batch."""
+
+import math
+import os
+
+import pytest
+import torch
+
+from oracle import modules as om
+from parity import assert_spikes_match, assert_close_rel, membrane_history, spike_mismatch_rate
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    import spikingtransformer_b200 as p
+    p.install_as_triton_layers()
+    return p
+
+
+def load(golden_dir, name):
+    return torch.load(os.path.join(golden_dir, name), weights_only=False)
+
+
+def test_lif_module_golden(pkg, golden_dir):
+    from spikingtransformer_b200.Lif import LIF
+    for c in load(golden_dir, "lif_module.pt"):
+        m = LIF(beta=0.8, v_th=0.9, n_steps=3, learn_beta=c["learn_beta"]).to(DEV)
+        m.load_state_dict(c["state"])
+        with torch.no_grad():
+            s, vf = m(c["x"].to(DEV))
+        assert torch.equal(s.cpu(), c["spikes"])
+        assert torch.equal(vf.cpu(), c["v_final"])
+
+
+def test_lif_layer_autograd_golden(pkg, golden_dir):
+    from spikingtransformer_b200.Lif import LIFLayer
+    for c in load(golden_dir, "lif.pt"):
+        x = c["x_in"].to(DEV).requires_grad_(True)
+        b = torch.tensor(c["beta"], device=DEV, requires_grad=True)
+        s, vf = LIFLayer.apply(x, b, torch.tensor(c["v_th"], device=DEV), torch.tensor(c["v_reset"], device=DEV), 4.0)
+        (s * c["g_spikes"].to(DEV)).sum().backward()
+        assert torch.equal(x.grad.cpu(), c["grad_x"].to(x.dtype))
+        assert torch.allclose(b.grad.cpu(), c["grad_beta"], rtol=1e-5, atol=1e-5)
+
+
+def test_triton_layers_alias(pkg):
+    import Triton_Layers.Seq2Seq as S
+    import spikingtransformer_b200.Seq2Seq as T
+    assert S is T
+
+
+def _ssa_cls(c):
+    from spikingtransformer_b200.SSA import SSAMultiHeadAttention, SSAMultiHeadAttention_
+    return SSAMultiHeadAttention if c["variant"] == "xnor" else SSAMultiHeadAttention_
+
+
+@pytest.mark.parametrize("path", ["fused", "autograd"])
+def test_ssa_golden(pkg, golden_dir, path):
+    for c in load(golden_dir, "ssa.pt"):
+        m = _ssa_cls(c)(d_model=c["D"], n_heads=c["H"], n_steps=c["T"]).to(DEV)
+        m.load_state_dict(c["state"])
+        q, k = c["query"].to(DEV), c["key"].to(DEV)
+        mask = None if c["mask"] is None else c["mask"].to(DEV)
+        if path == "fused":
+            with torch.no_grad():
+                y = m(q, k, k, attention_mask=mask)
+        else:
+            y = m(q, k, k, attention_mask=mask)
+        T = c["T"]
+        vh = membrane_history(c["ln_o"].reshape(T, -1), 0.9, 1.0, 0.0)
+        assert_spikes_match(y.reshape(T, -1), c["out"].reshape(T, -1), vh, 1.0,
+                            what=f"ssa {c['variant']} {c['case']} {path}")
+
+
+def test_mlp_golden(pkg, golden_dir):
+    from spikingtransformer_b200.SpikingMLP import SpikingMLP
+    c = load(golden_dir, "mlp.pt")
+    m = SpikingMLP(c["D"], c["F"], n_steps=c["T"]).to(DEV)
+    m.load_state_dict(c["state"])
+    with torch.no_grad():
+        y = m(c["x"].to(DEV))
+    T = c["T"]
+    beta = torch.sigmoid(c["state"]["lifcompress.beta_raw"])
+    vh = membrane_history(c["ln_compress"].reshape(T, -1), beta, 1.0, 0.0)
+    assert_spikes_match(y.reshape(T, -1), c["out"].reshape(T, -1), vh, 1.0, what="mlp")
+
+
+def test_encoder_decoder_golden(pkg, golden_dir):
+    from spikingtransformer_b200.Encoder import Encoder
+    from spikingtransformer_b200.Decoder import Decoder
+    c = load(golden_dir, "stacks.pt")
+    enc = Encoder(2, c["D"], c["H"], c["F"], n_steps=c["T"]).to(DEV)
+    enc.load_state_dict(c["enc_state"])
+    dec = Decoder(1, c["D"], c["H"], c["F"], n_steps=c["T"]).to(DEV)
+    dec.load_state_dict(c["dec_state"])
+    with torch.no_grad():
+        y = enc(c["x"].to(DEV))
+        z = dec(c["tgt"].to(DEV), c["enc_out"].to(DEV), mask=c["mask"].to(DEV))
+    assert spike_mismatch_rate(y, c["enc_out"]) < 0.01
+    assert spike_mismatch_rate(z, c["dec_out"]) < 0.01
+
+
+def test_seq2seq_cnn_golden(pkg, golden_dir):
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    c = load(golden_dir, "seq2seq_cnn.pt")
+    m = Seq2Seq(patch_size=4, d_model=32, n_heads=4, ff_dim=64, num_encoder_layers=1, num_decoder_layers=1,
+                tgt_vocab_size=40, nb_sps_blocks=1, n_steps=c["T"]).to(DEV)
+    m.load_state_dict(c["state"])
+    m.eval()
+    with torch.no_grad():
+        logits, aux = m(c["src"].to(DEV), c["tgt"].to(DEV), look_ahead_mask=c["mask"].to(DEV))
+        enc, _ = m.encode(c["src"].to(DEV))
+    assert aux is None
+    assert logits.shape == c["logits"].shape
+    assert spike_mismatch_rate(enc, c["enc"]) < 0.01
+    close = torch.isclose(logits.cpu(), c["logits"], rtol=1e-4, atol=1e-4).float().mean().item()
+    assert close > 0.95, close
+
+
+def _bench_models(seed=0, enc_layers=8, dec_layers=4, T=4):
+    """The OCR benchmark architecture (D=384, H=8, F=1536, patch 16, vocab 256),
+    bf16-rounded random weights, ours on the GPU and the oracle on the CPU."""
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    torch.manual_seed(seed)
+    ours = Seq2Seq(patch_size=16, d_model=384, n_heads=8, ff_dim=1536, num_encoder_layers=enc_layers,
+                   num_decoder_layers=dec_layers, tgt_vocab_size=256, n_steps=T, image_encoder="patch")
+    with torch.no_grad():
+        for mod in ours.modules():
+            if isinstance(mod, (torch.nn.Linear, torch.nn.Conv2d)):
+                mod.weight.copy_(mod.weight.to(torch.bfloat16).float())
+    ref = om.Seq2Seq(patch_size=16, d_model=384, n_heads=8, ff_dim=1536, num_encoder_layers=enc_layers,
+                     num_decoder_layers=dec_layers, tgt_vocab_size=256, n_steps=T, image_encoder="patch")
+    ref.load_state_dict(ours.state_dict())
+    return ours.to(DEV).eval(), ref.eval()
+
+
+def synthetic_lines(B, seed, H=64, W=1024):
+    """Text-line stand-ins: U(0, 0.2) background plus 5-40 black rectangles of
+    side 8-20 px per image, from a seed."""
+    g = torch.Generator().manual_seed(seed)
+    img = torch.rand(B, 1, H, W, generator=g) * 0.2
+    for b in range(B):
+        n = int(torch.randint(5, 41, (1,), generator=g))
+        for _ in range(n):
+            h, w = (int(v) for v in torch.randint(8, 21, (2,), generator=g))
+            y = int(torch.randint(0, H - h + 1, (1,), generator=g))
+            x = int(torch.randint(0, W - w + 1, (1,), generator=g))
+            img[b, 0, y:y + h, x:x + w] = 0.0
+    return img
+
+
+def test_seq2seq_ocr_benchmark_architecture(pkg):
+    ours, ref = _bench_models()
+    B, N = 2, 64
+    src = synthetic_lines(B, 1)
+    tgt = torch.randint(0, 256, (B, N), generator=torch.Generator().manual_seed(2))
+    mask = torch.tril(torch.ones(N, N)).expand(B, 1, N, N)
+    with torch.no_grad():
+        enc_ref, _ = ref.encode(src)
+        logits_ref, _ = ref(src, tgt, look_ahead_mask=mask)
+        enc, _ = ours.encode(src.to(DEV))
+        logits, _ = ours(src.to(DEV), tgt.to(DEV), look_ahead_mask=mask.to(DEV))
+    # the first layer's patch-embedding spikes must match outside the near-threshold band
+    pe_ours, _ = ours.image_encoder(src.to(DEV).unsqueeze(0).expand(4, *src.shape).reshape(4 * B, *src.shape[1:]))
+    with torch.no_grad():
+        y = ref.image_encoder.norm(ref.image_encoder.proj(
+            src.unsqueeze(0).expand(4, *src.shape).reshape(4 * B, *src.shape[1:])).flatten(2).transpose(1, 2))
+        pe_ref = ref.image_encoder.lif(y)[0]
+    vh = membrane_history(y.reshape(4, -1), 0.9, 1.0, 0.0)
+    assert_spikes_match(pe_ours.reshape(4, -1), pe_ref.reshape(4, -1), vh, 1.0, what="patch embedding")
+    rate_enc = spike_mismatch_rate(enc, enc_ref)
+    assert rate_enc < 0.02, rate_enc
+    close = torch.isclose(logits.cpu(), logits_ref, rtol=1e-3, atol=1e-3).float().mean().item()
+    assert close > 0.9, close
+
+
+def test_seq2seq_training_path_runs(pkg):
+    """Autograd path (reference composition over the LIF kernels) with the
+    arctan surrogate: finite loss and gradients on every parameter."""
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    ours.train()
+    ours.set_surrogate("arctan", 2.0)
+    B, N = 2, 16
+    src = synthetic_lines(B, 3).to(DEV)
+    tgt = torch.randint(0, 256, (B, N + 1), device=DEV)
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(B, 1, N, N)
+    logits, _ = ours(src, tgt[:, :-1], look_ahead_mask=mask)
+    loss = sum(torch.nn.functional.cross_entropy(logits[t].reshape(-1, 256), tgt[:, 1:].reshape(-1))
+               for t in range(logits.shape[0])) / logits.shape[0]
+    loss.backward()
+    assert math.isfinite(loss.item())
+    missing = [n for n, p in ours.named_parameters() if p.grad is None]
+    assert not [n for n in missing if "image_encoder" not in n], missing
+
+
+def test_greedy_decode(pkg):
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    src = synthetic_lines(1, 4)[0]
+    ys, rec, out = ours.greedy_decode(src, max_len=5, start_symbol=1, eos_idx=2, pad_idx=0, device=DEV)
+    assert ys.shape[0] == 1 and 2 <= ys.shape[1] <= 5
+    assert rec is None
+    assert out.shape[0] == 4
+
+
+def test_no_device_timeouts(pkg):
+    from spikingtransformer_b200 import ops
+    ops.device_error_check()
