@@ -166,8 +166,9 @@ def test_seq2seq_ocr_benchmark_architecture(pkg):
         enc, _ = ours.encode(src.to(DEV))
         logits, _ = ours(src.to(DEV), tgt.to(DEV), look_ahead_mask=mask.to(DEV))
     # the first layer's patch-embedding spikes must match outside the near-threshold band
-    pe_ours, _ = ours.image_encoder(src.to(DEV).unsqueeze(0).expand(4, *src.shape).reshape(4 * B, *src.shape[1:]))
     with torch.no_grad():
+        pe_ours, _ = ours.image_encoder(src.to(DEV).unsqueeze(0).expand(4, *src.shape).reshape(4 * B,
+                                                                                              *src.shape[1:]))
         y = ref.image_encoder.norm(ref.image_encoder.proj(
             src.unsqueeze(0).expand(4, *src.shape).reshape(4 * B, *src.shape[1:])).flatten(2).transpose(1, 2))
         pe_ref = ref.image_encoder.lif(y)[0]
