@@ -32,6 +32,8 @@
 // staged in shared memory, then each thread runs the recurrence over t for
 // two columns of one token and writes bf16 (or fp32) spikes, optionally
 // adding them into the residual stream in place.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace spk {
@@ -142,8 +144,10 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ln_lif_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
+  // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
+  // it by plain arithmetic so the compiler keeps them in the shared address space
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
   Smem sm;
   smem_layout(p, base, &sm);
 
@@ -516,6 +520,7 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
 
+  const int cfg_cs = p.cs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(clusters * p.cs), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -528,9 +533,34 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cfg_cs > 1) {
+    // persistent grid: never more clusters than can be co-resident (a cluster
+    // left over for a second wave would run all its tiles after the others)
+    int max_clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&max_clusters, (const void*)kern, &cfg) == cudaSuccess && max_clusters > 0 &&
+        max_clusters < clusters) {
+      clusters = max_clusters;
+      cfg.gridDim = dim3((unsigned)(clusters * cfg_cs), 1, 1);
+    }
+  }
   e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, p);
   if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "gemm_ln_lif_kernel launch: %s", cudaGetErrorString(e));
   return SPK_OK;
+}
+
+// t-coupled kernel with interleaved rows (gemm_il.cu)
+int launch_gemm_il(const void* A, const void* W, const float* bias, const float* gamma, const float* beta_ln,
+                   float eps, const float* lif_beta, const float* lif_vth, const float* lif_vr, float gain, int T,
+                   int64_t R, int K, int N, void* spk_bf16, float* spk_f32, void* residual, float* ln_out,
+                   cudaStream_t st);
+
+static bool force_generic() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SPK_GEMM_GENERIC");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 static int pick_split(int N, int* cs, int* n_cta) {
@@ -615,6 +645,13 @@ int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const
     mode = MODE_TCOUPLED;
     p.tpt = (int)(128 / T);
     p.num_m_tiles = (int)((R + p.tpt - 1) / p.tpt);
+    if (!force_generic()) {
+      rc = launch_gemm_il(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain, (int)T, R,
+                          (int)K, (int)N, p.spk_bf16, p.spk_f32, residual, ln_out,
+                          reinterpret_cast<cudaStream_t>(stream));
+      if (rc == SPK_OK) return check_launch("gemm_il_kernel");
+      if (rc != SPK_ERR_UNSUPPORTED) return rc;
+    }
   }
   rc = launch_gemm(mode, A, W, p, rows_2d, reinterpret_cast<cudaStream_t>(stream));
   if (rc != SPK_OK) return rc;

@@ -1,0 +1,642 @@
+// Fused Linear -> LayerNorm -> LIF, t-coupled rows, T a power of two <= 16.
+//
+// Same contract as the t-coupled mode of gemm.cu (SSA.py:218-249,
+// SpikingMLP.py:31-36, residual adds Encoder.py:19,22 / Decoder.py:18-25),
+// organised for epilogue throughput and MMA / epilogue overlap:
+//
+//  * Tile rows are interleaved token-major: row = tok*T + t.  A permuted 3-D
+//    TMA map (dims {K, T, R}, strides {R*K*2, K*2} bytes) writes the 128-row
+//    box in that order, so the T timesteps of a token sit in adjacent TMEM
+//    lanes of one warp.
+//  * Column slices of at most 256 (N = 384 -> 2 x 192, N = 1536 -> 6 x 256,
+//    split over a CTA cluster) so two accumulators fit in TMEM: the MMA of
+//    tile i+1 runs while the epilogue drains tile i.
+//  * Ten warps: warp 0 TMA producer, warp 1 TMEM owner + single-thread
+//    tcgen05.mma issuer, warps 2-9 epilogue; each TMEM lane quadrant is read
+//    by two epilogue warps, each owning half of the slice's columns.
+//  * LayerNorm statistics in one TMEM pass (sums shifted by the first
+//    32-column chunk's mean), merged across column halves and cluster CTAs
+//    with the parallel-variance formula.
+//  * The LIF transposition (lane (tok, t) -> lane (tok, column block)) goes
+//    through a warp-private XOR-swizzled shared buffer; the recurrence runs in
+//    packed fp32x2 arithmetic (round-to-nearest mul, then add, as the
+//    reference) and spikes are written as bf16 bit patterns straight from the
+//    threshold compare.
+//  * TMEM loads are 32 columns wide and double-buffered.
+//  * Compile-time variants: FAST (bf16 spikes and/or residual add only) with
+//    the residual add and the input gain specialised; a general variant
+//    handles fp32 spikes and the LayerNorm debug output.
+#include "common.cuh"
+
+namespace spk {
+namespace gil {
+
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kBK = 64;
+constexpr int kAStage = 128 * 128;
+constexpr int kMaxSmem = 232448;
+
+struct Params {
+  int T, tpt;
+  int64_t R;
+  int K, N, n_cta, cs, num_m_tiles, stages, wbox;
+  uint32_t tmem_cols;
+  const float *bias, *gamma, *beta_ln;
+  float eps;
+  const float *lif_beta, *lif_vth, *lif_vr;
+  float gain;
+  __nv_bfloat16* spk_bf16;
+  float* spk_f32;
+  __nv_bfloat16* residual;
+  float* ln_out;
+};
+
+struct Smem {
+  uint8_t *a, *w;
+  float* xs;       // 8 warps x 32 rows x 16 floats (swizzled)
+  float *bias, *gamma, *beta;
+  float2* stat;    // 2 parities x 2 halves x 128 rows (mean, M2)
+  float2* xbuf;    // 2 parities x cs x 128 rows (mean, M2)
+  uint64_t *full, *empty, *acc_full, *acc_empty, *xbar, *drain;
+  uint32_t* tmem_base;
+  int* abort_flag;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Smem* s) {
+  size_t off = 0;
+  auto take = [&](size_t bytes, size_t al) {
+    off = align_up(off, al);
+    size_t o = off;
+    off += bytes;
+    return o;
+  };
+  size_t oa = take((size_t)p.stages * kAStage, 1024);
+  size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
+  size_t oxs = take(kEpiWarps * 32 * 16 * 4, 16);
+  size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
+  size_t ost = take(2 * 2 * 128 * 8, 16);
+  size_t oxb = take((size_t)2 * p.cs * 128 * 8, 16);
+  size_t ofu = take(p.stages * 8, 8), oem = take(p.stages * 8, 8);
+  size_t oaf = take(16, 8), oae = take(16, 8), oxbar = take(16, 8), odr = take(8, 8);
+  size_t otm = take(4, 4), oab = take(4, 4);
+  if (s) {
+    s->a = base + oa;
+    s->w = base + ow;
+    s->xs = reinterpret_cast<float*>(base + oxs);
+    s->bias = reinterpret_cast<float*>(base + ob);
+    s->gamma = reinterpret_cast<float*>(base + og);
+    s->beta = reinterpret_cast<float*>(base + obe);
+    s->stat = reinterpret_cast<float2*>(base + ost);
+    s->xbuf = reinterpret_cast<float2*>(base + oxb);
+    s->full = reinterpret_cast<uint64_t*>(base + ofu);
+    s->empty = reinterpret_cast<uint64_t*>(base + oem);
+    s->acc_full = reinterpret_cast<uint64_t*>(base + oaf);
+    s->acc_empty = reinterpret_cast<uint64_t*>(base + oae);
+    s->xbar = reinterpret_cast<uint64_t*>(base + oxbar);
+    s->drain = reinterpret_cast<uint64_t*>(base + odr);
+    s->tmem_base = reinterpret_cast<uint32_t*>(base + otm);
+    s->abort_flag = reinterpret_cast<int*>(base + oab);
+  }
+  return off;
+}
+
+// merge (mean_b, M2_b) over nb samples into (mean, M2) over na samples
+__device__ __forceinline__ void chan_merge(float& mean, float& m2, float na, float mb, float m2b, float nb) {
+  const float tot = na + nb;
+  const float d = mb - mean;
+  mean = fmaf(d, nb / tot, mean);
+  m2 = m2 + m2b + d * d * (na * nb / tot);
+}
+
+template <int T, bool FAST, bool RES, bool GAIN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_il_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const Params p) {
+  constexpr int CPL = 16 / T;  // columns per lane after the transposition
+  constexpr int TPQ = 32 / T;  // tokens per TMEM lane quadrant
+  // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
+  // it by plain arithmetic so the compiler keeps them in the shared address space
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
+  Smem sm;
+  smem_layout(p, base, &sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cs = p.cs;
+  const uint32_t rank = cs > 1 ? cluster_ctarank() : 0u;
+  const int cid = cs > 1 ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int ncl = cs > 1 ? (int)cluster_count_x() : (int)gridDim.x;
+  const int nk = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.acc_full[i], 1);
+      mbar_init(&sm.acc_empty[i], kEpiWarps);
+      mbar_init(&sm.xbar[i], 1);  // one local arrive (with the expected bytes) per use
+    }
+    mbar_init(sm.drain, 1);
+    *sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(sm.tmem_base, p.tmem_cols);
+    tmem_relinquish();
+  }
+  {
+    const int n0 = (int)rank * p.n_cta;
+    for (int c = threadIdx.x; c < p.n_cta; c += kThreads) {
+      sm.bias[c] = p.bias ? p.bias[n0 + c] : 0.0f;
+      sm.gamma[c] = p.gamma ? p.gamma[n0 + c] : 1.0f;
+      sm.beta[c] = p.beta_ln ? p.beta_ln[n0 + c] : 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (cs > 1) cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmW);
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t bytes = (uint32_t)(p.tpt * T * 128) + (uint32_t)p.n_cta * 128;
+      const int n0 = (int)rank * p.n_cta;
+      bool ok = true;
+      uint32_t outstanding = 0, issued_phase = 0;  // bit i: stage i loaded / its phase
+      for (int tile = cid; tile < p.num_m_tiles && ok; tile += ncl) {
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&sm.empty[stage], phase ^ 1u, 111)) { ok = false; break; }
+          outstanding &= ~(1u << stage);
+          if (*((volatile int*)sm.abort_flag)) { ok = false; break; }
+          mbar_expect_tx(&sm.full[stage], bytes);
+          tma_load_3d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, tile * p.tpt);
+          uint8_t* w_dst = sm.w + (size_t)stage * p.n_cta * 128;
+          for (int r = 0; r < p.n_cta; r += p.wbox)
+            tma_load_2d(w_dst + (size_t)r * 128, &tmW, &sm.full[stage], kc * kBK, n0 + r);
+          outstanding |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        atomicExch(sm.abort_flag, 1);
+        for (int i = 0; i < p.stages; ++i)
+          if ((outstanding >> i) & 1u) mbar_wait(&sm.full[i], (issued_phase >> i) & 1u, 112);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int iter = 0;
+    for (int tile = cid; tile < p.num_m_tiles && ok; tile += ncl, ++iter) {
+      const int buf = iter & 1;
+      if (!mbar_wait(&sm.acc_empty[buf], ((uint32_t)(iter >> 1) & 1u) ^ 1u, 121)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t dcol = tmem + (uint32_t)(buf * p.n_cta);
+      for (int kc = 0; kc < nk; ++kc) {
+        if (!mbar_wait(&sm.full[stage], phase, 122)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(sm.a + (size_t)stage * kAStage);
+          const uint32_t w_addr = smem_u32(sm.w + (size_t)stage * p.n_cta * 128);
+          const uint32_t idesc = idesc_bf16_f32(128, p.n_cta, 0, 0);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16(dcol, umma_desc(a_addr + kk * 32, 16, 1024, 2), umma_desc(w_addr + kk * 32, 16, 1024, 2),
+                      idesc, (kc | kk) ? 1u : 0u);
+          umma_commit(&sm.empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&sm.acc_full[buf]);
+      __syncwarp();
+    }
+    if (!ok) {
+      atomicExch(sm.abort_flag, 1);
+      if (lane == 0) umma_commit(sm.drain);
+      __syncwarp();
+      mbar_wait(sm.drain, 0, 123);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp - 2;        // 0..7
+    const int q = warp & 3;         // TMEM lane quadrant
+    const int h = ew >> 2;          // column half
+    const int row = q * 32 + lane;  // tile row = tok * T + t
+    const int half = p.n_cta >> 1;
+    const int cb = h * half;        // first column of this warp within the slice
+    const int nch = half / 32;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int tok_l = lane / T;     // token within the quadrant
+    const int jblk = lane % T;      // timestep (before the transposition) / column block (after)
+    const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+    const float2 beta2 = make_float2(beta, beta);
+    const float2 gain2 = make_float2(p.gain, p.gain);
+    const int n0 = (int)rank * p.n_cta;
+    const int64_t tstride = p.R * (int64_t)p.N;
+    // warp-private transposition buffer: row r, logical 16-byte chunk c at r*16 + (c ^ ((r>>1)&3))*4
+    float* xs = sm.xs + ew * 32 * 16;
+    float* xs_wr = xs + lane * 16;
+    const int wkey = (lane >> 1) & 3;
+    int iter = 0;
+    for (int tile = cid; tile < p.num_m_tiles; tile += ncl, ++iter) {
+      const int buf = iter & 1;
+      if (!mbar_wait(&sm.acc_full[buf], (uint32_t)(iter >> 1) & 1u, 131)) { atomicExch(sm.abort_flag, 1); break; }
+      tc_fence_after();
+      const uint32_t trow = tmem + lane_off + (uint32_t)(buf * p.n_cta + cb);
+      // ---- statistics over this warp's columns
+      float mean, m2;
+      {
+        float K = 0.0f;
+        float2 s1 = make_float2(0.0f, 0.0f), s2 = make_float2(0.0f, 0.0f);
+        float2 s1b = s1, s2b = s2;
+        auto stats_chunk = [&](const uint32_t (&r)[32], int c) {
+          const float* bcol = sm.bias + cb + c * 32;
+          if (c == 0) {
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(bcol + i);
+              a0 += __uint_as_float(r[i]) + b4.x;
+              a1 += __uint_as_float(r[i + 1]) + b4.y;
+              a2 += __uint_as_float(r[i + 2]) + b4.z;
+              a3 += __uint_as_float(r[i + 3]) + b4.w;
+            }
+            K = ((a0 + a1) + (a2 + a3)) * (1.0f / 32.0f);
+            float q0 = 0.0f, q1 = 0.0f, q2 = 0.0f, q3 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(bcol + i);
+              const float d0 = (__uint_as_float(r[i]) + b4.x) - K, d1 = (__uint_as_float(r[i + 1]) + b4.y) - K;
+              const float d2 = (__uint_as_float(r[i + 2]) + b4.z) - K, d3 = (__uint_as_float(r[i + 3]) + b4.w) - K;
+              q0 = fmaf(d0, d0, q0);
+              q1 = fmaf(d1, d1, q1);
+              q2 = fmaf(d2, d2, q2);
+              q3 = fmaf(d3, d3, q3);
+            }
+            s2.x = (q0 + q1) + (q2 + q3);
+          } else {
+            const float2 nK = make_float2(-K, -K);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(bcol + i);
+              const float2 d0 = add2(add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                          make_float2(b4.x, b4.y)), nK);
+              const float2 d1 = add2(add2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])),
+                                          make_float2(b4.z, b4.w)), nK);
+              s1 = add2(s1, d0);
+              s1b = add2(s1b, d1);
+              s2 = fma2(d0, d0, s2);
+              s2b = fma2(d1, d1, s2b);
+            }
+          }
+        };
+        uint32_t ra[32], rb[32];
+        tmem_ld32_raw(trow, ra);
+        for (int c = 0; c < nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence32(ra);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
+            stats_chunk(ra, c);
+          } else {
+            tmem_wait_ld_fence32(rb);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+            stats_chunk(rb, c);
+          }
+        }
+        const float S1 = (s1.x + s1.y) + (s1b.x + s1b.y);
+        const float S2 = (s2.x + s2.y) + (s2b.x + s2b.y);
+        const float inv_n = 1.0f / (float)half;
+        mean = K + S1 * inv_n;
+        m2 = fmaxf(S2 - S1 * S1 * inv_n, 0.0f);
+      }
+      // ---- merge the two column halves of the slice
+      {
+        float2* st = sm.stat + (iter & 1) * 256;
+        st[h * 128 + row] = make_float2(mean, m2);
+        named_bar_sync(1, 32 * kEpiWarps);
+        const float2 o = st[(h ^ 1) * 128 + row];
+        const float2 a = h == 0 ? make_float2(mean, m2) : o;
+        const float2 b = h == 0 ? o : make_float2(mean, m2);
+        mean = a.x;
+        m2 = a.y;
+        chan_merge(mean, m2, (float)half, b.x, b.y, (float)half);
+      }
+      // ---- merge across the CTAs of the cluster (the row's columns are split over them)
+      if (cs > 1) {
+        const int par = iter & 1;
+        float2* xb = sm.xbuf + (size_t)par * cs * 128;
+        if (h == 0) {
+          // every row's (mean, M2) into every CTA's slot [rank][row]; the bytes complete the
+          // destination's barrier
+          const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + row);
+          const uint32_t bar = smem_u32(&sm.xbar[par]);
+          for (int r = 0; r < cs; ++r)
+            st_async_f32x2(mapa_shared(slot, (uint32_t)r), mean, m2, mapa_shared(bar, (uint32_t)r));
+        }
+        if (threadIdx.x == 64) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
+        if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 132)) {
+          atomicExch(sm.abort_flag, 1);
+          break;
+        }
+        float2 a = xb[row];
+        mean = a.x;
+        m2 = a.y;
+        for (int r = 1; r < cs; ++r) {
+          const float2 b = xb[(size_t)r * 128 + row];
+          chan_merge(mean, m2, (float)(p.n_cta * r), b.x, b.y, (float)p.n_cta);
+        }
+      }
+      const float rstd = 1.0f / sqrtf(m2 / (float)p.N + p.eps);
+      const float2 rstd2 = make_float2(rstd, rstd);
+      const float2 nmean2 = make_float2(-mean, -mean);
+
+      // ---- normalise, transpose, LIF, store
+      const int64_t gtok = (int64_t)tile * p.tpt + q * TPQ + tok_l;
+      const bool tok_ok = gtok < p.R;
+      const int64_t lane_out = gtok * p.N + n0 + cb + jblk * CPL;  // element offset at t = 0
+      auto norm_sub = [&](const uint32_t* r, int c16) {
+        const int col = cb + c16 * 16;  // column within the slice
+        float* ln_dst = nullptr;
+        if (!FAST && p.ln_out && tok_ok)
+          ln_dst = p.ln_out + (int64_t)(lane % T) * tstride + gtok * p.N + n0 + col;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(sm.bias + col + i);
+          const float4 g4 = *reinterpret_cast<const float4*>(sm.gamma + col + i);
+          const float4 e4 = *reinterpret_cast<const float4*>(sm.beta + col + i);
+          float2 x0 = make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          float2 x1 = make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          x0 = add2(add2(x0, make_float2(b4.x, b4.y)), nmean2);
+          x1 = add2(add2(x1, make_float2(b4.z, b4.w)), nmean2);
+          x0 = fma2(mul2(x0, rstd2), make_float2(g4.x, g4.y), make_float2(e4.x, e4.y));
+          x1 = fma2(mul2(x1, rstd2), make_float2(g4.z, g4.w), make_float2(e4.z, e4.w));
+          const float4 y4 = make_float4(x0.x, x0.y, x1.x, x1.y);
+          *reinterpret_cast<float4*>(xs_wr + (((i >> 2) ^ wkey) << 2)) = y4;
+          if (!FAST && ln_dst) *reinterpret_cast<float4*>(ln_dst + i) = y4;
+        }
+        __syncwarp();
+        float yt[T][CPL];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int rr = tok_l * T + t;
+          const int rkey = (rr >> 1) & 3;
+#pragma unroll
+          for (int u = 0; u < CPL; u += (CPL >= 4 ? 4 : CPL)) {
+            const int lc = jblk * CPL + u;  // logical column within the 16
+            const float* src = xs + rr * 16 + ((((lc >> 2) ^ rkey) << 2) | (lc & 3));
+            if constexpr (CPL >= 4) {
+              const float4 v4 = *reinterpret_cast<const float4*>(src);
+              yt[t][u] = v4.x;
+              yt[t][u + 1] = v4.y;
+              yt[t][u + 2] = v4.z;
+              yt[t][u + 3] = v4.w;
+            } else if constexpr (CPL == 2) {
+              const float2 v2 = *reinterpret_cast<const float2*>(src);
+              yt[t][u] = v2.x;
+              yt[t][u + 1] = v2.y;
+            } else {
+              yt[t][u] = *src;
+            }
+          }
+        }
+        __syncwarp();
+        if (!tok_ok) return;
+        const int64_t off0 = lane_out + c16 * 16;
+        constexpr int NP = CPL >= 2 ? CPL / 2 : 1;  // spike words (bf16 pairs) per step
+        float2 mem2[NP];
+#pragma unroll
+        for (int u = 0; u < NP; ++u) mem2[u] = make_float2(0.0f, 0.0f);
+        __nv_bfloat16* sp_ptr = p.spk_bf16 ? p.spk_bf16 + off0 : nullptr;
+        // (the general variant is instantiated with RES = true: the pointer is checked at run time)
+        __nv_bfloat16* res_ptr = (RES && p.residual) ? p.residual + off0 : nullptr;
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          uint32_t bits[NP];
+          float sp[CPL];
+#pragma unroll
+          for (int u = 0; u < NP; ++u) {
+            float2 y2 = CPL >= 2 ? make_float2(yt[t][2 * u], yt[t][(2 * u + 1) % CPL]) : make_float2(yt[t][0], 0.0f);
+            if (GAIN) y2 = mul2(y2, gain2);
+            const float2 uu = add2(mul2(mem2[u], beta2), y2);
+            const bool f0 = uu.x > vth, f1 = uu.y > vth;
+            mem2[u] = make_float2(f0 ? vr : uu.x, f1 ? vr : uu.y);
+            bits[u] = (f0 ? 0x3F80u : 0u) | ((CPL >= 2 && f1) ? 0x3F800000u : 0u);
+            if (!FAST) {
+              sp[(2 * u) % CPL] = f0 ? 1.0f : 0.0f;
+              if (CPL >= 2) sp[(2 * u + 1) % CPL] = f1 ? 1.0f : 0.0f;
+            }
+          }
+          if (sp_ptr) {
+            if constexpr (CPL == 16) {
+              *reinterpret_cast<uint4*>(sp_ptr) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+              *reinterpret_cast<uint4*>(sp_ptr + 8) = make_uint4(bits[4], bits[5], bits[6], bits[7]);
+            } else if constexpr (CPL == 8) {
+              *reinterpret_cast<uint4*>(sp_ptr) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+            } else if constexpr (CPL == 4) {
+              *reinterpret_cast<uint2*>(sp_ptr) = make_uint2(bits[0], bits[1]);
+            } else if constexpr (CPL == 2) {
+              *reinterpret_cast<uint32_t*>(sp_ptr) = bits[0];
+            } else {
+              *reinterpret_cast<uint16_t*>(sp_ptr) = (uint16_t)(bits[0] & 0xFFFFu);
+            }
+            sp_ptr += tstride;
+          }
+          if (!FAST && p.spk_f32) {
+            float* fp = p.spk_f32 + off0 + (int64_t)t * tstride;
+#pragma unroll
+            for (int u = 0; u < CPL; ++u) fp[u] = sp[u];
+          }
+          if (RES && res_ptr) {
+            // spikes are exactly 0/1 and the stream holds small integers: the bf16 add is exact
+#pragma unroll
+            for (int u = 0; u < NP; ++u) {
+              if (CPL >= 2) {
+                __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(res_ptr) + u;
+                __nv_bfloat162 sb;
+                *reinterpret_cast<uint32_t*>(&sb) = bits[u];
+                *r2 = __hadd2(*r2, sb);
+              } else {
+                __nv_bfloat16 sb;
+                *reinterpret_cast<uint16_t*>(&sb) = (uint16_t)(bits[0] & 0xFFFFu);
+                *res_ptr = __hadd(*res_ptr, sb);
+              }
+            }
+            res_ptr += tstride;
+          }
+        }
+      };
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32_raw(trow, ra);
+        for (int c = 0; c < nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence32(ra);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
+          } else {
+            tmem_wait_ld_fence32(rb);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+          }
+          if (c + 1 == nch) {
+            // last TMEM read of this buffer: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+          }
+          if ((c & 1) == 0) {
+            norm_sub(ra, 2 * c);
+            norm_sub(ra + 16, 2 * c + 1);
+          } else {
+            norm_sub(rb, 2 * c);
+            norm_sub(rb + 16, 2 * c + 1);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (cs > 1) cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, p.tmem_cols);
+  }
+}
+
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const Params);
+
+template <int T>
+KernelFn pick_kernel(bool fast, bool res, bool gain) {
+  if (!fast) return gemm_il_kernel<T, false, true, true>;
+  if (res) return gain ? gemm_il_kernel<T, true, true, true> : gemm_il_kernel<T, true, true, false>;
+  return gain ? gemm_il_kernel<T, true, false, true> : gemm_il_kernel<T, true, false, false>;
+}
+
+}  // namespace gil
+
+// Column slice for the interleaved kernel: <= 256 columns (two TMEM
+// accumulators), a multiple of 64, at most 8 CTAs per cluster.
+bool gemm_il_split(int N, int* cs, int* n_cta) {
+  for (int w : {256, 192, 128, 64}) {
+    if (N % w == 0 && N / w <= 8) {
+      *cs = N / w;
+      *n_cta = w;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Host launcher used by spk_linear_ln_lif_fwd for t-coupled rows with T in
+// {1, 2, 4, 8, 16}; returns SPK_ERR_UNSUPPORTED for shapes it does not cover.
+int launch_gemm_il(const void* A, const void* W, const float* bias, const float* gamma, const float* beta_ln,
+                   float eps, const float* lif_beta, const float* lif_vth, const float* lif_vr, float gain, int T,
+                   int64_t R, int K, int N, void* spk_bf16, float* spk_f32, void* residual, float* ln_out,
+                   cudaStream_t st) {
+  using namespace gil;
+  if (!(T == 1 || T == 2 || T == 4 || T == 8 || T == 16)) return SPK_ERR_UNSUPPORTED;
+  int cs = 1, n_cta = 0;
+  if (!gemm_il_split(N, &cs, &n_cta)) return SPK_ERR_UNSUPPORTED;
+  Params p = {};
+  p.T = T;
+  p.tpt = 128 / T;
+  p.R = R;
+  p.K = K;
+  p.N = N;
+  p.n_cta = n_cta;
+  p.cs = cs;
+  p.num_m_tiles = (int)((R + p.tpt - 1) / p.tpt);
+  p.wbox = n_cta;
+  p.tmem_cols = 2 * n_cta <= 256 ? 256 : 512;
+  p.bias = bias;
+  p.gamma = gamma;
+  p.beta_ln = beta_ln;
+  p.eps = eps;
+  p.lif_beta = lif_beta;
+  p.lif_vth = lif_vth;
+  p.lif_vr = lif_vr;
+  p.gain = gain;
+  p.spk_bf16 = reinterpret_cast<__nv_bfloat16*>(spk_bf16);
+  p.spk_f32 = spk_f32;
+  p.residual = reinterpret_cast<__nv_bfloat16*>(residual);
+  p.ln_out = ln_out;
+
+  CUtensorMap tmA, tmW;
+  int rc;
+  {
+    // dims {K, T, R}: the box {64, T, tpt} lands as rows tok*T + t
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)T, (uint64_t)R};
+    uint64_t strides[2] = {(uint64_t)R * K * 2, (uint64_t)K * 2};
+    uint32_t box[3] = {kBK, (uint32_t)T, (uint32_t)p.tpt};
+    if ((rc = make_tmap_bf16(&tmA, A, 3, dims, strides, box, true)) != SPK_OK) return rc;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    uint64_t strides[1] = {(uint64_t)K * 2};
+    uint32_t box[2] = {kBK, (uint32_t)p.wbox};
+    if ((rc = make_tmap_bf16(&tmW, W, 2, dims, strides, box, true)) != SPK_OK) return rc;
+  }
+  size_t smem = 0;
+  for (p.stages = 4; p.stages >= 2; --p.stages) {
+    smem = smem_layout(p, nullptr, nullptr);
+    if (smem <= (size_t)kMaxSmem) break;
+  }
+  if (smem > (size_t)kMaxSmem) return fail(SPK_ERR_SHAPE, "tile of %d columns does not fit in shared memory", n_cta);
+  const bool fast = spk_f32 == nullptr && ln_out == nullptr;
+  const bool res = residual != nullptr;
+  const bool gn = gain != 1.0f;
+  KernelFn kern;
+  switch (T) {
+    case 1: kern = pick_kernel<1>(fast, res, gn); break;
+    case 2: kern = pick_kernel<2>(fast, res, gn); break;
+    case 4: kern = pick_kernel<4>(fast, res, gn); break;
+    case 8: kern = pick_kernel<8>(fast, res, gn); break;
+    default: kern = pick_kernel<16>(fast, res, gn); break;
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  int clusters = num_sms() / cs;
+  if (clusters > p.num_m_tiles) clusters = p.num_m_tiles;
+  if (clusters < 1) clusters = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(clusters * cs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cs > 1) {
+    // persistent grid: never more clusters than can be co-resident
+    int max_clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&max_clusters, (const void*)kern, &cfg) == cudaSuccess && max_clusters > 0 &&
+        max_clusters < clusters) {
+      clusters = max_clusters;
+      cfg.gridDim = dim3((unsigned)(clusters * cs), 1, 1);
+    }
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, p);
+  if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "gemm_il_kernel launch: %s", cudaGetErrorString(e));
+  return SPK_OK;
+}
+
+}  // namespace spk

@@ -21,6 +21,8 @@
 // The spike-count product O is exact.  The reference rounds S*scale per
 // element before the @V (SSA.py:242); here the scale is applied once to the
 // exact integer sum, a difference of a few ulp in the LIF input.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace spk {
@@ -136,8 +138,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 __global__ void __launch_bounds__(kThreads, 1)
     ssa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
+  // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
+  // it by plain arithmetic so the compiler keeps them in the shared address space
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
   Smem sm;
   smem_layout(p.lmax, base, &sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -439,6 +443,21 @@ SPK_DEFINE_ERROR_READER(ssa_read_device_error)
 
 using namespace ssak;
 
+// score-free kernel for unmasked attention (ssa_lin.cu)
+int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, int T, int B, int H,
+                   int Nq, int Nk, int dh, int variant, const float* scale, const float* lif_beta,
+                   const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
+                   float* attn_out, cudaStream_t st);
+
+static bool force_dense() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SPK_SSA_DENSE");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 static int make_qkv_map(CUtensorMap* m, const void* ptr, int dh, int H, int N, int TB) {
   uint64_t dims[4] = {(uint64_t)dh, (uint64_t)H, (uint64_t)N, (uint64_t)TB};
   uint64_t strides[3] = {(uint64_t)dh * 2, (uint64_t)H * dh * 2, (uint64_t)N * H * dh * 2};
@@ -475,6 +494,14 @@ int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int ma
   if ((rc = make_qkv_map(&tq, q, (int)dh, (int)H, (int)Nq, (int)(T * B))) != SPK_OK) return rc;
   if ((rc = make_qkv_map(&tk, k, (int)dh, (int)H, (int)Nk, (int)(T * B))) != SPK_OK) return rc;
   if ((rc = make_qkv_map(&tv, v, (int)dh, (int)H, (int)Nk, (int)(T * B))) != SPK_OK) return rc;
+  if (mask_mode == 0 && !force_dense()) {
+    rc = launch_ssa_lin(tq, tk, tv, (int)T, (int)B, (int)H, (int)Nq, (int)Nk, (int)dh, variant, scale, lif_beta,
+                        lif_vth, lif_vreset, in_gain, out_dtype == SPK_BF16 ? out : nullptr,
+                        out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out,
+                        reinterpret_cast<cudaStream_t>(stream));
+    if (rc == SPK_OK) return check_launch("ssa_lin_kernel");
+    if (rc != SPK_ERR_UNSUPPORTED) return rc;
+  }
   Params p = {};
   p.T = (int)T;
   p.B = (int)B;

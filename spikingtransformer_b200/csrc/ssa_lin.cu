@@ -1,0 +1,458 @@
+// Spiking attention without a score matrix (unmasked case), on tcgen05.
+//
+// Same result as the dense kernel in ssa.cu (SSA.py:145-165, :177-201,
+// :234-244; plain form SSA.py:81-84) whenever no mask is applied: the
+// encoder self-attention and the decoder cross-attention (Encoder.py:18,
+// Decoder.py:21).  With S'[i,j] = 2 q_i.k_j + c_i - s_j + R(|i-j|),
+// c_i = dh - |q_i|, s_j = |k_j|, the attention product is regrouped exactly:
+//
+//   O_i = sum_j S'[i,j] v_j = 2 q_i (K^T V) + c_i (1^T V) - (s^T V) + (R V)_i
+//
+// Every term is an integer computed exactly (bf16 operands <= 512, fp32
+// accumulation < 2^24), so O equals the dense product bit for bit; the
+// output stage (a = scale*O, LIF over t) is the dense kernel's.  Cost per
+// (t, query block) is O(Nk*dh*(dh+Nq)) tensor work and O(Nq*dh) epilogue work
+// instead of O(Nq*Nk) score elements.
+//
+// Per CTA: a persistent walk over (query block, batch, head) items with the
+// query block outermost.  The log-distance matrix R of the query block
+// (128 x Nk, bf16, values <= 13) stays resident in TMEM as the A operand of
+// the R V product.  Per timestep:
+//   MMA1  D1[128 x dh] = A1 V,  A1 = [K^T ; AUX^T] (MN-major, two 64-row
+//         atoms: K tile and an auxiliary tile whose columns 0/1 hold 1 and
+//         s_j), so D1 rows 0..dh-1 = K^T V, row 64 = 1^T V, row 65 = s^T V
+//   epi   rows 0..63 of D1 -> bf16 (x2 for XNOR) B operand in shared memory
+//   MMA2  D2 = Q (2 K^T V) [+ R V]
+//   epi   O = D2 + c_i (1^T V) - s^T V; a = scale O; LIF over t; spikes
+// Requirements: Nk <= 256, dh <= 64 (dh % 8 == 0).
+#include "common.cuh"
+
+namespace spk {
+namespace ssal {
+
+constexpr int kThreads = 192;
+constexpr int kEpi = 128;
+constexpr int kQTile = 128 * 128;   // 128 rows x 128 B
+constexpr int kKVTile = 256 * 128;  // 256 rows x 128 B
+
+struct Params {
+  int T, B, H, Nq, Nk, dh, dpad, mode;
+  const float* scale;
+  const float *lif_beta, *lif_vth, *lif_vr;
+  float gain;
+  __nv_bfloat16* out_bf16;
+  float* out_f32;
+  float* attn_out;
+  int q_blocks, lmax, items;
+};
+
+struct Smem {
+  uint8_t *q, *k, *v, *aux, *mb;
+  float *cs, *kv;
+  uint64_t *q_full, *q_empty, *kv_full, *kv_empty;
+  uint64_t *aux_ready, *m_full, *mb_ready, *o_full, *o_empty, *r_ready, *drain;
+  uint32_t* tmem_base;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
+  size_t off = 0;
+  auto take = [&](size_t bytes, size_t al) {
+    off = align_up(off, al);
+    size_t o = off;
+    off += bytes;
+    return o;
+  };
+  size_t oq = take(2 * kQTile, 1024), ok = take(2 * kKVTile, 1024), ov = take(2 * kKVTile, 1024);
+  size_t oaux = take(kKVTile, 1024);  // after both K slots: positive LBO from K to AUX
+  size_t omb = take(64 * 128, 1024);
+  size_t ocs = take(64 * 4, 16), okv = take(64 * 4, 16);
+  size_t ob = take(20 * 8, 8), otm = take(4, 4);
+  if (s) {
+    s->q = base + oq;
+    s->k = base + ok;
+    s->v = base + ov;
+    s->aux = base + oaux;
+    s->mb = base + omb;
+    s->cs = reinterpret_cast<float*>(base + ocs);
+    s->kv = reinterpret_cast<float*>(base + okv);
+    uint64_t* b = reinterpret_cast<uint64_t*>(base + ob);
+    s->q_full = b;
+    s->q_empty = b + 2;
+    s->kv_full = b + 4;
+    s->kv_empty = b + 6;
+    s->aux_ready = b + 8;
+    s->m_full = b + 9;
+    s->mb_ready = b + 10;
+    s->o_full = b + 11;
+    s->o_empty = b + 12;
+    s->r_ready = b + 13;
+    s->drain = b + 14;
+    s->tmem_base = reinterpret_cast<uint32_t*>(base + otm);
+  }
+  return off + 1024;
+}
+
+__device__ __forceinline__ float row_sum_sw128(const uint8_t* tile, int r, int n) {
+  float s = 0.0f;
+  const int chunks = (n + 7) >> 3;
+  for (int c = 0; c < chunks; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      s += f.x + f.y;
+    }
+  }
+  return s;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int h, int row, int tb) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(0), "r"(h), "r"(row), "r"(tb)
+      : "memory");
+}
+
+// smallest k >= 0 with (d+1) * 2^k >= L-1: max(0, ceil(log2((L-1)/(d+1))))
+__device__ __forceinline__ int log_bias(int d, int L1) {
+  int k = 0;
+  long long x = d + 1;
+  while (x < L1) {
+    x <<= 1;
+    ++k;
+  }
+  return k;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    ssa_lin_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const Params p) {
+  // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
+  // it by plain arithmetic so the compiler keeps them in the shared address space
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
+  Smem sm;
+  smem_layout(base, &sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool xnor = p.mode == 1;
+  const int ksteps = (p.Nk + 15) >> 4;
+  const int dsteps = (p.dh + 15) >> 4;
+  const int BH = p.B * p.H;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], 1 + 4);
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1 + 4);
+    }
+    mbar_init(sm.aux_ready, 4);
+    mbar_init(sm.m_full, 1);
+    mbar_init(sm.mb_ready, 1);
+    mbar_init(sm.o_full, 1);
+    mbar_init(sm.o_empty, 4);
+    mbar_init(sm.r_ready, 4);
+    mbar_init(sm.drain, 1);
+    fence_mbar_init();
+  }
+  // auxiliary tile: column 0 = 1 (keys < Nk), column 1 = key sums (per step), rest 0
+  for (int i = threadIdx.x; i < kKVTile / 16; i += kThreads) {
+    const int r = i >> 3, c = i & 7;
+    uint4 w = make_uint4(0, 0, 0, 0);
+    if ((c ^ (r & 7)) == 0 && r < p.Nk) w.x = 0x3F80u;  // logical chunk 0, element 0 = 1.0
+    *reinterpret_cast<uint4*>(sm.aux + i * 16) = w;
+  }
+  if (warp == 1) {
+    tmem_alloc(sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sm.tmem_base;
+  const uint32_t tm_r = tmem, tm_d1 = tmem + 128, tm_d2 = tmem + 192;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int g = 0;
+      bool ok = true;
+      int q_ph[2] = {-1, -1}, kv_ph[2] = {-1, -1};
+      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int qb = item / BH, bh = item % BH;
+        const int b = bh / p.H, h = bh % p.H;
+        for (int t = 0; t < p.T; ++t, ++g) {
+          const int s = g & 1;
+          const uint32_t ph = (uint32_t)((g >> 1) & 1);
+          if (!mbar_wait(&sm.q_empty[s], ph ^ 1u, 71)) { ok = false; break; }
+          mbar_expect_tx(&sm.q_full[s], kQTile);
+          q_ph[s] = (int)ph;
+          load_4d(sm.q + s * kQTile, &tmQ, &sm.q_full[s], h, qb * 128, t * p.B + b);
+          if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, 72)) { ok = false; break; }
+          mbar_expect_tx(&sm.kv_full[s], 4 * kQTile);
+          kv_ph[s] = (int)ph;
+          for (int half = 0; half < 2; ++half) {
+            load_4d(sm.k + s * kKVTile + half * kQTile, &tmK, &sm.kv_full[s], h, half * 128, t * p.B + b);
+            load_4d(sm.v + s * kKVTile + half * kQTile, &tmV, &sm.kv_full[s], h, half * 128, t * p.B + b);
+          }
+        }
+      }
+      if (!ok) {
+        for (int i = 0; i < 2; ++i) {
+          if (q_ph[i] >= 0) mbar_wait(&sm.q_full[i], (uint32_t)q_ph[i], 73);
+          if (kv_ph[i] >= 0) mbar_wait(&sm.kv_full[i], (uint32_t)kv_ph[i], 73);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    int g = 0, r_uses = 0, prev_qb = -1;
+    bool ok = true;
+    const uint32_t id1 = idesc_bf16_f32(128, p.dpad, 1, 1);  // A1, V: MN-major
+    const uint32_t id2 = idesc_bf16_f32(128, p.dpad, 0, 1);  // Q: K-major, Mb / V: MN-major
+    for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+      const int qb = item / BH;
+      if (xnor && qb != prev_qb) {
+        if (!mbar_wait(sm.r_ready, (uint32_t)(r_uses & 1), 81)) { ok = false; break; }
+        ++r_uses;
+        prev_qb = qb;
+      }
+      for (int t = 0; t < p.T; ++t, ++g) {
+        const int s = g & 1;
+        const uint32_t ph = (uint32_t)((g >> 1) & 1);
+        if (!mbar_wait(&sm.kv_full[s], ph, 82)) { ok = false; break; }
+        if (!mbar_wait(sm.aux_ready, (uint32_t)(g & 1), 83)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ka = smem_u32(sm.k + s * kKVTile), va = smem_u32(sm.v + s * kKVTile);
+          const uint32_t lbo = smem_u32(sm.aux) - ka;
+          for (int kk = 0; kk < ksteps; ++kk)
+            umma_bf16(tm_d1, umma_desc(ka + kk * 2048, lbo, 1024, 2), umma_desc(va + kk * 2048, kKVTile, 1024, 2),
+                      id1, kk > 0 ? 1u : 0u);
+          umma_commit(sm.m_full);
+        }
+        __syncwarp();
+        if (!mbar_wait(sm.mb_ready, (uint32_t)(g & 1), 84)) { ok = false; break; }
+        if (!mbar_wait(&sm.q_full[s], ph, 85)) { ok = false; break; }
+        if (!mbar_wait(sm.o_empty, (uint32_t)((g & 1) ^ 1), 86)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qa = smem_u32(sm.q + s * kQTile), mba = smem_u32(sm.mb);
+          const uint32_t va = smem_u32(sm.v + s * kKVTile);
+          for (int kk = 0; kk < dsteps; ++kk)
+            umma_bf16(tm_d2, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(mba + kk * 2048, 8192, 1024, 2), id2,
+                      kk > 0 ? 1u : 0u);
+          if (xnor)
+            for (int kk = 0; kk < ksteps; ++kk)
+              umma_bf16_ts(tm_d2, tm_r + kk * 8, umma_desc(va + kk * 2048, kKVTile, 1024, 2), id2, 1u);
+          umma_commit(sm.o_full);
+          umma_commit(&sm.q_empty[s]);
+          umma_commit(&sm.kv_empty[s]);
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      if (lane == 0) umma_commit(sm.drain);
+      __syncwarp();
+      mbar_wait(sm.drain, 0, 87);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (lane = query row / D1 row)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const float scale = __ldg(p.scale);
+    const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+    const int D = p.H * p.dh;
+    const int L1 = p.lmax - 1;
+    int g = 0, prev_qb = -1;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+      const int qb = item / BH, bh = item % BH;
+      const int b = bh / p.H, h = bh % p.H;
+      const int qi = qb * 128 + row;
+      if (xnor && qb != prev_qb) {
+        // R rows of this query block -> TMEM (bf16 pairs, keys 2c and 2c+1 in column c)
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t rr[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int j0 = 2 * (c0 + i), j1 = j0 + 1;
+            const float r0 = j0 < p.Nk ? (float)log_bias(qi > j0 ? qi - j0 : j0 - qi, L1) : 0.0f;
+            const float r1 = j1 < p.Nk ? (float)log_bias(qi > j1 ? qi - j1 : j1 - qi, L1) : 0.0f;
+            rr[i] = pack_bf16x2(r0, r1);
+          }
+          tmem_st32(tm_r + lane_off + c0, rr);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.r_ready);
+        prev_qb = qb;
+      }
+      float mem[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mem[i] = 0.0f;
+      for (int t = 0; t < p.T; ++t, ++g) {
+        const int s = g & 1;
+        const uint32_t ph = (uint32_t)((g >> 1) & 1);
+        // ---- key sums into the auxiliary tile (column 1, bf16), release K for reading
+        if (!mbar_wait(&sm.kv_full[s], ph, 91)) { ok = false; break; }
+        if (xnor) {
+          const uint8_t* kt = sm.k + s * kKVTile;
+#pragma unroll
+          for (int rr2 = 0; rr2 < 2; ++rr2) {
+            const int j = row + rr2 * 128;
+            const float ks = row_sum_sw128(kt, j, p.dh);
+            __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
+            *slot = __float2bfloat16_rn(ks);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(sm.aux_ready);
+          mbar_arrive(&sm.kv_empty[s]);
+        }
+        // ---- query sums (c_i = dh - |q_i|)
+        if (!mbar_wait(&sm.q_full[s], ph, 92)) { ok = false; break; }
+        const float c_row = xnor ? (float)p.dh - row_sum_sw128(sm.q + s * kQTile, row, p.dh) : 0.0f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.q_empty[s]);
+        // ---- K^T V -> bf16 operand; 1^T V and s^T V -> shared floats
+        if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) { ok = false; break; }
+        tc_fence_after();
+        if (q < 3) {
+          float d1[64];
+          for (int c0 = 0; c0 < p.dpad; c0 += 16) tmem_ld16(tm_d1 + lane_off + c0, d1 + c0);
+          if (q < 2) {
+            const float f = xnor ? 2.0f : 1.0f;
+            for (int c = 0; c < p.dpad / 8; ++c) {
+              uint4 w;
+              w.x = pack_bf16x2(f * d1[8 * c + 0], f * d1[8 * c + 1]);
+              w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
+              w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
+              w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
+              *reinterpret_cast<uint4*>(sm.mb + row * 128 + ((c ^ (row & 7)) << 4)) = w;
+            }
+          } else if (lane < 2) {
+            float* dst = lane == 0 ? sm.cs : sm.kv;
+            for (int c = 0; c < p.dpad; ++c) dst[c] = d1[c];
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        named_bar_sync(1, kEpi);
+        if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
+        // ---- output: O = D2 + c_i (1^T V) - s^T V, a = scale O, LIF over t
+        if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
+        tc_fence_after();
+        float o[64];
+        for (int c0 = 0; c0 < p.dpad; c0 += 16) tmem_ld16(tm_d2 + lane_off + c0, o + c0);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.o_empty);
+        if (qi < p.Nq) {
+          const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
+          float* aout =
+              p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
+#pragma unroll
+          for (int d0 = 0; d0 < 64; d0 += 8) {
+            if (d0 < p.dh) {
+              float sp[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float ov = o[d0 + i];
+                if (xnor) ov = (ov + c_row * sm.cs[d0 + i]) - sm.kv[d0 + i];
+                const float a = __fmul_rn(ov, scale);
+                if (aout) aout[d0 + i] = a;
+                const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
+                const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
+                const bool fire = u > vth;
+                sp[i] = fire ? 1.0f : 0.0f;
+                mem[d0 + i] = fire ? vr : u;
+              }
+              if (p.out_bf16) {
+                uint4 w;
+                w.x = pack_bf16x2(sp[0], sp[1]);
+                w.y = pack_bf16x2(sp[2], sp[3]);
+                w.z = pack_bf16x2(sp[4], sp[5]);
+                w.w = pack_bf16x2(sp[6], sp[7]);
+                *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
+              }
+              if (p.out_f32) {
+                *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
+                *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
+              }
+            }
+          }
+        }
+      }
+    }
+    (void)ok;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace ssal
+
+// Host launcher used by spk_ssa_fwd for unmasked attention; returns
+// SPK_ERR_UNSUPPORTED when the sizes are outside this kernel's range.
+int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, int T, int B, int H,
+                   int Nq, int Nk, int dh, int variant, const float* scale, const float* lif_beta,
+                   const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
+                   float* attn_out, cudaStream_t st) {
+  using namespace ssal;
+  if (Nk > 256 || dh > 64 || dh % 8 != 0) return SPK_ERR_UNSUPPORTED;
+  Params p = {};
+  p.T = T;
+  p.B = B;
+  p.H = H;
+  p.Nq = Nq;
+  p.Nk = Nk;
+  p.dh = dh;
+  p.dpad = (dh + 15) / 16 * 16;
+  p.mode = variant;
+  p.scale = scale;
+  p.lif_beta = lif_beta;
+  p.lif_vth = lif_vth;
+  p.lif_vr = lif_vr;
+  p.gain = gain;
+  p.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  p.out_f32 = out_f32;
+  p.attn_out = attn_out;
+  p.q_blocks = (Nq + 127) / 128;
+  p.lmax = Nq > Nk ? Nq : Nk;
+  const long long items = (long long)p.q_blocks * B * H;
+  if (items >= (1ll << 31)) return fail(SPK_ERR_SHAPE, "too many attention work items");
+  p.items = (int)items;
+  size_t smem = smem_layout(nullptr, nullptr);
+  cudaError_t e = cudaFuncSetAttribute(ssa_lin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  int grid = num_sms();
+  if (grid > p.items) grid = p.items;
+  ssa_lin_kernel<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  return SPK_OK;
+}
+
+}  // namespace spk

@@ -1,0 +1,121 @@
+"""Kernel micro-benchmarks at the benchmark shapes (CUDA events, device time).
+
+    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa] [--iters N]
+
+  lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 spikes (the MLP
+        expansion LIF of a 64-image batch); bound: HBM bytes.
+  gemm  fused Linear(384->1536) -> LayerNorm -> LIF on A [4*32*256, 384]
+        Bernoulli(0.15) spikes (bf16), tau=2 neuron; bound: bf16 tensor FLOPs.
+  ssa   spiking attention on Q, K, V [T=4, B=32, H=8, N=256, d=48]
+        Bernoulli(0.15), plain (QK^T)V*0.125 and XNOR variants, plus the
+        causal N=64 case; FLOPs counted dense (QK^T and PV).
+Inputs are regenerated per configuration; each timed iteration rotates over
+input copies whose total exceeds the 126 MB L2.  Prints one JSON line.
+"""
+
+import argparse
+import json
+import os
+
+import torch
+
+from . import ops
+
+
+def _peaks():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    try:
+        with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _time(fn, iters, warmup=3):
+    """Device time per call: the calls are captured once into a CUDA graph and
+    replayed, so host launch overhead does not enter the measurement."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_lif(iters):
+    T, N = 4, 64 * 256 * 1536
+    copies = 2
+    xs = [torch.randn(T, N, device="cuda") + 0.5 for _ in range(copies)]
+    ms = _time(lambda i: ops.lif_fwd(xs[i % copies], 0.9, 1.0, 0.0, spike_dtype=torch.bfloat16), iters)
+    nbytes = T * N * (4 + 2) + 4 * N
+    return {"kernel": "lif_fwd", "shape": [T, N], "ms": ms, "GB/s": nbytes / ms / 1e6, "bytes": nbytes}
+
+
+def bench_gemm(iters, N=1536, K=384, T=4, R=32 * 256):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    copies = 3
+    As = [(torch.rand(T * R, K, device="cuda", generator=g) < 0.15).to(torch.bfloat16) for _ in range(copies)]
+    bound = 1.0 / K ** 0.5
+    W = ((torch.rand(N, K, device="cuda", generator=g) * 2 - 1) * bound).to(torch.bfloat16)
+    b = (torch.rand(N, device="cuda", generator=g) * 2 - 1) * 0.01
+    gamma, beta = torch.ones(N, device="cuda"), torch.zeros(N, device="cuda")
+    ms = _time(lambda i: ops.linear_ln_lif(As[i % copies], W, b, gamma, beta, 1e-5, 0.5, 1.0, 0.0, T,
+                                           in_gain=0.5), iters)
+    flops = 2.0 * T * R * K * N
+    return {"kernel": "linear_ln_lif", "shape": [T * R, K, N], "ms": ms, "TFLOP/s": flops / ms / 1e9,
+            "flops": flops}
+
+
+def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    copies = 2
+    mk = lambda: (torch.rand(T * B, N, H * d, device="cuda", generator=g) < 0.15).to(torch.bfloat16)  # noqa: E731
+    qkv = [(mk(), mk(), mk()) for _ in range(copies)]
+    scale = 0.125 if variant == 0 else (1.0 / d) ** 0.5
+
+    def run(i):
+        q, k, v = qkv[i % copies]
+        ops.ssa(q, k, v, T, B, H, variant, scale, 0.5, 0.5, 0.0, in_gain=0.5, causal=causal)
+    ms = _time(run, iters)
+    flops = 4.0 * T * B * H * N * N * d
+    return {"kernel": "ssa", "variant": "plain" if variant == 0 else "xnor", "causal": causal,
+            "shape": [T, B, H, N, d], "ms": ms, "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
+    a = ap.parse_args()
+    peaks, src = _peaks()
+    out = {"peaks": {"hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained"),
+                     "source": src}, "results": []}
+    if a.only in (None, "lif"):
+        r = bench_lif(a.iters)
+        r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
+        out["results"].append(r)
+    if a.only in (None, "gemm"):
+        for n, k in ((1536, 384), (384, 384), (384, 1536)):
+            r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)
+            r["frac_tensor"] = r["TFLOP/s"] / peaks["bf16_tflops_sustained"]
+            out["results"].append(r)
+    if a.only in (None, "ssa"):
+        for variant in (0, 1):
+            out["results"].append(bench_ssa(a.iters, variant))
+        out["results"].append(bench_ssa(a.iters, 0, N=64, causal=True))
+    ops.device_error_check()
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()
