@@ -36,7 +36,7 @@ constexpr int kQTile = 128 * 128;   // 128 rows x 128 B
 constexpr int kKVTile = 256 * 128;  // 256 rows x 128 B
 
 struct Params {
-  int T, B, H, Nq, Nk, dh, dpad, mode;
+  int T, B, H, Nq, Nk, dh;
   const float* scale;
   const float *lif_beta, *lif_vth, *lif_vr;
   float gain;
@@ -47,8 +47,8 @@ struct Params {
 };
 
 struct Smem {
-  uint8_t *q, *k, *v, *aux, *mb;
-  float *cs, *kv;
+  uint8_t *q, *k, *v, *aux, *mb, *rl;
+  float *cs, *kv;  // 2 parities x 64
   uint64_t *q_full, *q_empty, *kv_full, *kv_empty;
   uint64_t *aux_ready, *m_full, *mb_ready, *o_full, *o_empty, *r_ready, *drain;
   uint32_t* tmem_base;
@@ -56,7 +56,7 @@ struct Smem {
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
+__host__ __device__ inline size_t smem_layout(int lmax, uint8_t* base, Smem* s) {
   size_t off = 0;
   auto take = [&](size_t bytes, size_t al) {
     off = align_up(off, al);
@@ -67,7 +67,8 @@ __host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
   size_t oq = take(2 * kQTile, 1024), ok = take(2 * kKVTile, 1024), ov = take(2 * kKVTile, 1024);
   size_t oaux = take(kKVTile, 1024);  // after both K slots: positive LBO from K to AUX
   size_t omb = take(64 * 128, 1024);
-  size_t ocs = take(64 * 4, 16), okv = take(64 * 4, 16);
+  size_t ocs = take(2 * 64 * 4, 16), okv = take(2 * 64 * 4, 16);
+  size_t orl = take((size_t)lmax, 16);
   size_t ob = take(20 * 8, 8), otm = take(4, 4);
   if (s) {
     s->q = base + oq;
@@ -75,6 +76,7 @@ __host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
     s->v = base + ov;
     s->aux = base + oaux;
     s->mb = base + omb;
+    s->rl = base + orl;
     s->cs = reinterpret_cast<float*>(base + ocs);
     s->kv = reinterpret_cast<float*>(base + okv);
     uint64_t* b = reinterpret_cast<uint64_t*>(base + ob);
@@ -91,7 +93,7 @@ __host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
     s->drain = b + 14;
     s->tmem_base = reinterpret_cast<uint32_t*>(base + otm);
   }
-  return off + 1024;
+  return off;
 }
 
 __device__ __forceinline__ float row_sum_sw128(const uint8_t* tile, int r, int n) {
@@ -122,17 +124,9 @@ __device__ __forceinline__ void load_4d(void* dst, const CUtensorMap* map, uint6
       : "memory");
 }
 
-// smallest k >= 0 with (d+1) * 2^k >= L-1: max(0, ceil(log2((L-1)/(d+1))))
-__device__ __forceinline__ int log_bias(int d, int L1) {
-  int k = 0;
-  long long x = d + 1;
-  while (x < L1) {
-    x <<= 1;
-    ++k;
-  }
-  return k;
-}
-
+// DP: head width rounded up to 16 (the N of both MMAs); XNOR selects the
+// S' = 2QK^T + c - s + R form, otherwise the plain Q K^T.
+template <int DP, bool XNOR>
 __global__ void __launch_bounds__(kThreads, 1)
     ssa_lin_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -141,12 +135,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = smem_raw;
   Smem sm;
-  smem_layout(base, &sm);
+  smem_layout(p.lmax, base, &sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool xnor = p.mode == 1;
   const int ksteps = (p.Nk + 15) >> 4;
-  const int dsteps = (p.dh + 15) >> 4;
+  constexpr int dsteps = DP / 16;
   const int BH = p.B * p.H;
+  // per-CTA sequence of work units g = (item, t): item = blockIdx.x + k * gridDim.x
+  const int n_items = p.items > (int)blockIdx.x ? (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  const int n_units = n_items * p.T;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -171,6 +167,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((c ^ (r & 7)) == 0 && r < p.Nk) w.x = 0x3F80u;  // logical chunk 0, element 0 = 1.0
     *reinterpret_cast<uint4*>(sm.aux + i * 16) = w;
   }
+  // log-distance table R[d] = smallest k >= 0 with (d+1) * 2^k >= L-1
+  for (int d = threadIdx.x; d < p.lmax; d += kThreads) {
+    const long long L1 = (long long)p.lmax - 1;
+    int k = 0;
+    long long x = d + 1;
+    while (x < L1) {
+      x <<= 1;
+      ++k;
+    }
+    sm.rl[d] = (uint8_t)k;
+  }
   if (warp == 1) {
     tmem_alloc(sm.tmem_base, 256);
     tmem_relinquish();
@@ -188,27 +195,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      int g = 0;
       bool ok = true;
       int q_ph[2] = {-1, -1}, kv_ph[2] = {-1, -1};
-      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+      for (int g = 0; g < n_units && ok; ++g) {
+        const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
         const int qb = item / BH, bh = item % BH;
         const int b = bh / p.H, h = bh % p.H;
-        for (int t = 0; t < p.T; ++t, ++g) {
-          const int s = g & 1;
-          const uint32_t ph = (uint32_t)((g >> 1) & 1);
-          if (!mbar_wait(&sm.q_empty[s], ph ^ 1u, 71)) { ok = false; break; }
-          mbar_expect_tx(&sm.q_full[s], kQTile);
-          q_ph[s] = (int)ph;
-          load_4d(sm.q + s * kQTile, &tmQ, &sm.q_full[s], h, qb * 128, t * p.B + b);
-          if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, 72)) { ok = false; break; }
-          mbar_expect_tx(&sm.kv_full[s], 4 * kQTile);
-          kv_ph[s] = (int)ph;
-          for (int half = 0; half < 2; ++half) {
-            load_4d(sm.k + s * kKVTile + half * kQTile, &tmK, &sm.kv_full[s], h, half * 128, t * p.B + b);
-            load_4d(sm.v + s * kKVTile + half * kQTile, &tmV, &sm.kv_full[s], h, half * 128, t * p.B + b);
-          }
+        const int s = g & 1;
+        const uint32_t ph = (uint32_t)((g >> 1) & 1);
+        if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, 72)) { ok = false; break; }
+        mbar_expect_tx(&sm.kv_full[s], 4 * kQTile);
+        kv_ph[s] = (int)ph;
+        for (int half = 0; half < 2; ++half) {
+          load_4d(sm.k + s * kKVTile + half * kQTile, &tmK, &sm.kv_full[s], h, half * 128, t * p.B + b);
+          load_4d(sm.v + s * kKVTile + half * kQTile, &tmV, &sm.kv_full[s], h, half * 128, t * p.B + b);
         }
+        if (!mbar_wait(&sm.q_empty[s], ph ^ 1u, 71)) { ok = false; break; }
+        mbar_expect_tx(&sm.q_full[s], kQTile);
+        q_ph[s] = (int)ph;
+        load_4d(sm.q + s * kQTile, &tmQ, &sm.q_full[s], h, qb * 128, t * p.B + b);
       }
       if (!ok) {
         for (int i = 0; i < 2; ++i) {
@@ -219,51 +224,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
-    int g = 0, r_uses = 0, prev_qb = -1;
     bool ok = true;
-    const uint32_t id1 = idesc_bf16_f32(128, p.dpad, 1, 1);  // A1, V: MN-major
-    const uint32_t id2 = idesc_bf16_f32(128, p.dpad, 0, 1);  // Q: K-major, Mb / V: MN-major
-    for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+    int r_uses = 0, prev_qb = -1;
+    const uint32_t id1 = idesc_bf16_f32(128, DP, 1, 1);  // A1, V: MN-major
+    const uint32_t id2 = idesc_bf16_f32(128, DP, 0, 1);  // Q: K-major, Mb / V: MN-major
+    for (int g = 0; g < n_units && ok; ++g) {
+      const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x;
       const int qb = item / BH;
-      if (xnor && qb != prev_qb) {
+      const int s = g & 1;
+      const uint32_t ph = (uint32_t)((g >> 1) & 1);
+      // MMA1: [K^T ; AUX^T] V
+      if (!mbar_wait(&sm.kv_full[s], ph, 82)) { ok = false; break; }
+      if (!mbar_wait(sm.aux_ready, (uint32_t)(g & 1), 83)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t ka = smem_u32(sm.k + s * kKVTile), va = smem_u32(sm.v + s * kKVTile);
+        const uint32_t lbo = smem_u32(sm.aux) - ka;
+        for (int kk = 0; kk < ksteps; ++kk)
+          umma_bf16(tm_d1, umma_desc(ka + kk * 2048, lbo, 1024, 2), umma_desc(va + kk * 2048, kKVTile, 1024, 2),
+                    id1, kk > 0 ? 1u : 0u);
+        umma_commit(sm.m_full);
+      }
+      __syncwarp();
+      // MMA2: Q (2 K^T V) [+ R V]
+      if (XNOR && qb != prev_qb) {
         if (!mbar_wait(sm.r_ready, (uint32_t)(r_uses & 1), 81)) { ok = false; break; }
         ++r_uses;
         prev_qb = qb;
       }
-      for (int t = 0; t < p.T; ++t, ++g) {
-        const int s = g & 1;
-        const uint32_t ph = (uint32_t)((g >> 1) & 1);
-        if (!mbar_wait(&sm.kv_full[s], ph, 82)) { ok = false; break; }
-        if (!mbar_wait(sm.aux_ready, (uint32_t)(g & 1), 83)) { ok = false; break; }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ka = smem_u32(sm.k + s * kKVTile), va = smem_u32(sm.v + s * kKVTile);
-          const uint32_t lbo = smem_u32(sm.aux) - ka;
+      if (!mbar_wait(sm.mb_ready, (uint32_t)(g & 1), 84)) { ok = false; break; }
+      if (!mbar_wait(&sm.q_full[s], ph, 85)) { ok = false; break; }
+      if (!mbar_wait(sm.o_empty, (uint32_t)((g & 1) ^ 1), 86)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t qa = smem_u32(sm.q + s * kQTile), mba = smem_u32(sm.mb);
+        const uint32_t va = smem_u32(sm.v + s * kKVTile);
+#pragma unroll
+        for (int kk = 0; kk < dsteps; ++kk)
+          umma_bf16(tm_d2, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(mba + kk * 2048, 8192, 1024, 2), id2,
+                    kk > 0 ? 1u : 0u);
+        if (XNOR)
           for (int kk = 0; kk < ksteps; ++kk)
-            umma_bf16(tm_d1, umma_desc(ka + kk * 2048, lbo, 1024, 2), umma_desc(va + kk * 2048, kKVTile, 1024, 2),
-                      id1, kk > 0 ? 1u : 0u);
-          umma_commit(sm.m_full);
-        }
-        __syncwarp();
-        if (!mbar_wait(sm.mb_ready, (uint32_t)(g & 1), 84)) { ok = false; break; }
-        if (!mbar_wait(&sm.q_full[s], ph, 85)) { ok = false; break; }
-        if (!mbar_wait(sm.o_empty, (uint32_t)((g & 1) ^ 1), 86)) { ok = false; break; }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t qa = smem_u32(sm.q + s * kQTile), mba = smem_u32(sm.mb);
-          const uint32_t va = smem_u32(sm.v + s * kKVTile);
-          for (int kk = 0; kk < dsteps; ++kk)
-            umma_bf16(tm_d2, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(mba + kk * 2048, 8192, 1024, 2), id2,
-                      kk > 0 ? 1u : 0u);
-          if (xnor)
-            for (int kk = 0; kk < ksteps; ++kk)
-              umma_bf16_ts(tm_d2, tm_r + kk * 8, umma_desc(va + kk * 2048, kKVTile, 1024, 2), id2, 1u);
-          umma_commit(sm.o_full);
-          umma_commit(&sm.q_empty[s]);
-          umma_commit(&sm.kv_empty[s]);
-        }
-        __syncwarp();
+            umma_bf16_ts(tm_d2, tm_r + kk * 8, umma_desc(va + kk * 2048, kKVTile, 1024, 2), id2, 1u);
+        umma_commit(sm.o_full);
+        umma_commit(&sm.q_empty[s]);
+        umma_commit(&sm.kv_empty[s]);
       }
+      __syncwarp();
     }
     if (!ok) {
       if (lane == 0) umma_commit(sm.drain);
@@ -278,128 +285,161 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale = __ldg(p.scale);
     const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
     const int D = p.H * p.dh;
-    const int L1 = p.lmax - 1;
-    int g = 0, prev_qb = -1;
     bool ok = true;
-    for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
-      const int qb = item / BH, bh = item % BH;
-      const int b = bh / p.H, h = bh % p.H;
-      const int qi = qb * 128 + row;
-      if (xnor && qb != prev_qb) {
-        // R rows of this query block -> TMEM (bf16 pairs, keys 2c and 2c+1 in column c)
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t rr[32];
+    int prev_qb = -1;
+    float mem[DP];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int j0 = 2 * (c0 + i), j1 = j0 + 1;
-            const float r0 = j0 < p.Nk ? (float)log_bias(qi > j0 ? qi - j0 : j0 - qi, L1) : 0.0f;
-            const float r1 = j1 < p.Nk ? (float)log_bias(qi > j1 ? qi - j1 : j1 - qi, L1) : 0.0f;
-            rr[i] = pack_bf16x2(r0, r1);
-          }
-          tmem_st32(tm_r + lane_off + c0, rr);
+    for (int i = 0; i < DP; ++i) mem[i] = 0.0f;
+
+    // key sums of unit g into the auxiliary tile, query sum of unit g; releases K and Q for reading
+    auto prepare = [&](int g, float& c_row) -> bool {
+      const int s = g & 1;
+      const uint32_t ph = (uint32_t)((g >> 1) & 1);
+      if (!mbar_wait(&sm.kv_full[s], ph, 91)) return false;
+      if (XNOR) {
+        const uint8_t* kt = sm.k + s * kKVTile;
+#pragma unroll
+        for (int rr2 = 0; rr2 < 2; ++rr2) {
+          const int j = row + rr2 * 128;
+          const float ks = row_sum_sw128(kt, j, p.dh);
+          __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
+          *slot = __float2bfloat16_rn(ks);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sm.r_ready);
-        prev_qb = qb;
       }
-      float mem[64];
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sm.aux_ready);
+        mbar_arrive(&sm.kv_empty[s]);
+      }
+      if (!mbar_wait(&sm.q_full[s], ph, 92)) return false;
+      c_row = XNOR ? (float)p.dh - row_sum_sw128(sm.q + s * kQTile, row, p.dh) : 0.0f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.q_empty[s]);
+      return true;
+    };
+    // R rows of query block qb -> TMEM (bf16 pairs: keys 2c and 2c+1 in column c)
+    auto build_r = [&](int qb) {
+      const int qi = qb * 128 + row;
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t rr[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mem[i] = 0.0f;
-      for (int t = 0; t < p.T; ++t, ++g) {
-        const int s = g & 1;
-        const uint32_t ph = (uint32_t)((g >> 1) & 1);
-        // ---- key sums into the auxiliary tile (column 1, bf16), release K for reading
-        if (!mbar_wait(&sm.kv_full[s], ph, 91)) { ok = false; break; }
-        if (xnor) {
-          const uint8_t* kt = sm.k + s * kKVTile;
+        for (int i = 0; i < 32; ++i) {
+          const int j0 = 2 * (c0 + i), j1 = j0 + 1;
+          const float r0 = j0 < p.Nk ? (float)sm.rl[qi > j0 ? qi - j0 : j0 - qi] : 0.0f;
+          const float r1 = j1 < p.Nk ? (float)sm.rl[qi > j1 ? qi - j1 : j1 - qi] : 0.0f;
+          rr[i] = pack_bf16x2(r0, r1);
+        }
+        tmem_st32(tm_r + lane_off + c0, rr);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.r_ready);
+    };
+
+    float c_cur = 0.0f;
+    if (n_units > 0) {
+      const int qb0 = (int)blockIdx.x / BH;
+      if (XNOR) {
+        build_r(qb0);
+        prev_qb = qb0;
+      }
+      ok = prepare(0, c_cur);
+    }
+    for (int g = 0; g < n_units && ok; ++g) {
+      const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
+      const int bh = item % BH, b = bh / p.H, h = bh % p.H;
+      const int qi = (item / BH) * 128 + row;
+      const int par = g & 1;
+      if (t == 0) {
 #pragma unroll
-          for (int rr2 = 0; rr2 < 2; ++rr2) {
-            const int j = row + rr2 * 128;
-            const float ks = row_sum_sw128(kt, j, p.dh);
-            __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
-            *slot = __float2bfloat16_rn(ks);
+        for (int i = 0; i < DP; ++i) mem[i] = 0.0f;
+      }
+      // ---- A: K^T V -> bf16 operand (x2 for XNOR); 1^T V, s^T V -> shared floats
+      if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) { ok = false; break; }
+      tc_fence_after();
+      if (q < 3) {
+        float d1[DP];
+#pragma unroll
+        for (int c0 = 0; c0 < DP; c0 += 16) tmem_ld16(tm_d1 + lane_off + c0, d1 + c0);
+        if (q < 2) {
+          const float f = XNOR ? 2.0f : 1.0f;
+#pragma unroll
+          for (int c = 0; c < DP / 8; ++c) {
+            uint4 w;
+            w.x = pack_bf16x2(f * d1[8 * c + 0], f * d1[8 * c + 1]);
+            w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
+            w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
+            w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
+            *reinterpret_cast<uint4*>(sm.mb + row * 128 + ((c ^ (row & 7)) << 4)) = w;
           }
+        } else if (XNOR && lane < 2) {
+          float* dst = (lane == 0 ? sm.cs : sm.kv) + par * 64;
+#pragma unroll
+          for (int c = 0; c < DP; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(d1[c], d1[c + 1], d1[c + 2], d1[c + 3]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(sm.aux_ready);
-          mbar_arrive(&sm.kv_empty[s]);
-        }
-        // ---- query sums (c_i = dh - |q_i|)
-        if (!mbar_wait(&sm.q_full[s], ph, 92)) { ok = false; break; }
-        const float c_row = xnor ? (float)p.dh - row_sum_sw128(sm.q + s * kQTile, row, p.dh) : 0.0f;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.q_empty[s]);
-        // ---- K^T V -> bf16 operand; 1^T V and s^T V -> shared floats
-        if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) { ok = false; break; }
-        tc_fence_after();
-        if (q < 3) {
-          float d1[64];
-          for (int c0 = 0; c0 < p.dpad; c0 += 16) tmem_ld16(tm_d1 + lane_off + c0, d1 + c0);
-          if (q < 2) {
-            const float f = xnor ? 2.0f : 1.0f;
-            for (int c = 0; c < p.dpad / 8; ++c) {
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1, kEpi);
+      if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
+      // ---- B: prepare the next unit so its MMA1 overlaps this unit's MMA2 and output
+      float c_next = 0.0f;
+      if (g + 1 < n_units && !prepare(g + 1, c_next)) { ok = false; break; }
+      // ---- C: O = D2 + c_i (1^T V) - s^T V, a = scale O, LIF over t, spikes
+      if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
+      tc_fence_after();
+      float o[DP];
+#pragma unroll
+      for (int c0 = 0; c0 < DP; c0 += 16) tmem_ld16(tm_d2 + lane_off + c0, o + c0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.o_empty);
+      if (qi < p.Nq) {
+        const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
+        float* aout = p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
+        const float* csp = sm.cs + par * 64;
+        const float* kvp = sm.kv + par * 64;
+#pragma unroll
+        for (int d0 = 0; d0 < DP; d0 += 8) {
+          if (d0 < p.dh) {
+            float sp[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float ov = o[d0 + i];
+              if (XNOR) ov = (ov + c_cur * csp[d0 + i]) - kvp[d0 + i];
+              const float a = __fmul_rn(ov, scale);
+              if (aout) aout[d0 + i] = a;
+              const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
+              const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
+              const bool fire = u > vth;
+              sp[i] = fire ? 1.0f : 0.0f;
+              mem[d0 + i] = fire ? vr : u;
+            }
+            if (p.out_bf16) {
               uint4 w;
-              w.x = pack_bf16x2(f * d1[8 * c + 0], f * d1[8 * c + 1]);
-              w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
-              w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
-              w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
-              *reinterpret_cast<uint4*>(sm.mb + row * 128 + ((c ^ (row & 7)) << 4)) = w;
+              w.x = pack_bf16x2(sp[0], sp[1]);
+              w.y = pack_bf16x2(sp[2], sp[3]);
+              w.z = pack_bf16x2(sp[4], sp[5]);
+              w.w = pack_bf16x2(sp[6], sp[7]);
+              *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
             }
-          } else if (lane < 2) {
-            float* dst = lane == 0 ? sm.cs : sm.kv;
-            for (int c = 0; c < p.dpad; ++c) dst[c] = d1[c];
+            if (p.out_f32) {
+              *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
+              *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
+            }
           }
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        named_bar_sync(1, kEpi);
-        if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
-        // ---- output: O = D2 + c_i (1^T V) - s^T V, a = scale O, LIF over t
-        if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
-        tc_fence_after();
-        float o[64];
-        for (int c0 = 0; c0 < p.dpad; c0 += 16) tmem_ld16(tm_d2 + lane_off + c0, o + c0);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sm.o_empty);
-        if (qi < p.Nq) {
-          const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
-          float* aout =
-              p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
-#pragma unroll
-          for (int d0 = 0; d0 < 64; d0 += 8) {
-            if (d0 < p.dh) {
-              float sp[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float ov = o[d0 + i];
-                if (xnor) ov = (ov + c_row * sm.cs[d0 + i]) - sm.kv[d0 + i];
-                const float a = __fmul_rn(ov, scale);
-                if (aout) aout[d0 + i] = a;
-                const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
-                const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
-                const bool fire = u > vth;
-                sp[i] = fire ? 1.0f : 0.0f;
-                mem[d0 + i] = fire ? vr : u;
-              }
-              if (p.out_bf16) {
-                uint4 w;
-                w.x = pack_bf16x2(sp[0], sp[1]);
-                w.y = pack_bf16x2(sp[2], sp[3]);
-                w.z = pack_bf16x2(sp[4], sp[5]);
-                w.w = pack_bf16x2(sp[6], sp[7]);
-                *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
-              }
-              if (p.out_f32) {
-                *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
-                *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
-              }
-            }
-          }
+      }
+      c_cur = c_next;
+      // ---- new query block for the next unit: rebuild R (MMA2 of this unit has completed)
+      if (XNOR && g + 1 < n_units) {
+        const int nitem = (int)blockIdx.x + ((g + 1) / p.T) * (int)gridDim.x;
+        const int nqb = nitem / BH;
+        if (nqb != prev_qb) {
+          build_r(nqb);
+          prev_qb = nqb;
         }
       }
     }
@@ -431,8 +471,6 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   p.Nq = Nq;
   p.Nk = Nk;
   p.dh = dh;
-  p.dpad = (dh + 15) / 16 * 16;
-  p.mode = variant;
   p.scale = scale;
   p.lif_beta = lif_beta;
   p.lif_vth = lif_vth;
@@ -446,12 +484,21 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   const long long items = (long long)p.q_blocks * B * H;
   if (items >= (1ll << 31)) return fail(SPK_ERR_SHAPE, "too many attention work items");
   p.items = (int)items;
-  size_t smem = smem_layout(nullptr, nullptr);
-  cudaError_t e = cudaFuncSetAttribute(ssa_lin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int dp = (dh + 15) / 16 * 16;
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
+  const bool x = variant == 1;
+  switch (dp) {
+    case 16: kern = x ? ssa_lin_kernel<16, true> : ssa_lin_kernel<16, false>; break;
+    case 32: kern = x ? ssa_lin_kernel<32, true> : ssa_lin_kernel<32, false>; break;
+    case 48: kern = x ? ssa_lin_kernel<48, true> : ssa_lin_kernel<48, false>; break;
+    default: kern = x ? ssa_lin_kernel<64, true> : ssa_lin_kernel<64, false>; break;
+  }
+  size_t smem = smem_layout(p.lmax, nullptr, nullptr);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
   if (grid > p.items) grid = p.items;
-  ssa_lin_kernel<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
   return SPK_OK;
 }
 
