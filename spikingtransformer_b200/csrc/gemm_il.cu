@@ -18,7 +18,7 @@
 //    32-column chunk's mean), merged across column halves and cluster CTAs
 //    with the parallel-variance formula.
 //  * The LIF transposition (lane (tok, t) -> lane (tok, column block)) goes
-//    through a warp-private XOR-swizzled shared buffer; the recurrence runs in
+//    through a warp-private, bank-conflict-free padded shared buffer; the recurrence runs in
 //    packed fp32x2 arithmetic (round-to-nearest mul, then add, as the
 //    reference) and spikes are written as bf16 bit patterns straight from the
 //    threshold compare.
@@ -36,6 +36,9 @@ constexpr int kEpiWarps = 8;
 constexpr int kBK = 64;
 constexpr int kAStage = 128 * 128;
 constexpr int kMaxSmem = 232448;
+// transposition buffer row stride (floats): 16 data + 4 pad, so that both the
+// row writes and the transposed reads of a quarter-warp hit 8 distinct bank groups
+constexpr int kXS = 20;
 
 struct Params {
   int T, tpt;
@@ -54,7 +57,7 @@ struct Params {
 
 struct Smem {
   uint8_t *a, *w;
-  float* xs;       // 8 warps x 32 rows x 16 floats (swizzled)
+  float* xs;       // 8 warps x 32 rows x kXS floats (padded rows)
   float *bias, *gamma, *beta;
   float2* stat;    // 2 parities x 2 halves x 128 rows (mean, M2)
   float2* xbuf;    // 2 parities x cs x 128 rows (mean, M2)
@@ -75,7 +78,7 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   };
   size_t oa = take((size_t)p.stages * kAStage, 1024);
   size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
-  size_t oxs = take(kEpiWarps * 32 * 16 * 4, 16);
+  size_t oxs = take(kEpiWarps * 32 * kXS * 4, 16);
   size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
   size_t ost = take(2 * 2 * 128 * 8, 16);
   size_t oxb = take((size_t)2 * p.cs * 128 * 8, 16);
@@ -248,10 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 gain2 = make_float2(p.gain, p.gain);
     const int n0 = (int)rank * p.n_cta;
     const int64_t tstride = p.R * (int64_t)p.N;
-    // warp-private transposition buffer: row r, logical 16-byte chunk c at r*16 + (c ^ ((r>>1)&3))*4
-    float* xs = sm.xs + ew * 32 * 16;
-    float* xs_wr = xs + lane * 16;
-    const int wkey = (lane >> 1) & 3;
+    // warp-private transposition buffer: row r (tile row within the quadrant), column c at r*kXS + c
+    float* xs = sm.xs + ew * 32 * kXS;
+    float* xs_wr = xs + lane * kXS;
     int iter = 0;
     for (int tile = cid; tile < p.num_m_tiles; tile += ncl, ++iter) {
       const int buf = iter & 1;
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           x0 = fma2(mul2(x0, rstd2), make_float2(g4.x, g4.y), make_float2(e4.x, e4.y));
           x1 = fma2(mul2(x1, rstd2), make_float2(g4.z, g4.w), make_float2(e4.z, e4.w));
           const float4 y4 = make_float4(x0.x, x0.y, x1.x, x1.y);
-          *reinterpret_cast<float4*>(xs_wr + (((i >> 2) ^ wkey) << 2)) = y4;
+          *reinterpret_cast<float4*>(xs_wr + i) = y4;
           if (!FAST && ln_dst) *reinterpret_cast<float4*>(ln_dst + i) = y4;
         }
         __syncwarp();
@@ -394,11 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < T; ++t) {
           const int rr = tok_l * T + t;
-          const int rkey = (rr >> 1) & 3;
 #pragma unroll
           for (int u = 0; u < CPL; u += (CPL >= 4 ? 4 : CPL)) {
-            const int lc = jblk * CPL + u;  // logical column within the 16
-            const float* src = xs + rr * 16 + ((((lc >> 2) ^ rkey) << 2) | (lc & 3));
+            const float* src = xs + rr * kXS + jblk * CPL + u;
             if constexpr (CPL >= 4) {
               const float4 v4 = *reinterpret_cast<const float4*>(src);
               yt[t][u] = v4.x;
