@@ -15,7 +15,10 @@ no collective on the data path.
 reference modules, oracle/) on the host cores on a bounded sample of the same
 workload; under torchrun only rank 0 runs it.
 
-One JSON line on rank 0 (see DESIGN.md for the field definitions).
+One JSON line on rank 0: the metric, the device-timed value, the end-to-end
+value through host buffers (e2e), the roofline of the dominant kernel, the CPU
+baseline, the SM clocks sampled during the timed region and the number of
+library kernel launches.
 """
 
 import argparse

@@ -14,7 +14,7 @@ reference writes it (``v*beta`` rounded, then ``+ x`` rounded), which is how
 the reference kernel evaluates when run by the Triton interpreter; the fixtures
 in ``tests/golden`` pin this bit-for-bit.
 
-Extension beyond the reference (documented in DESIGN.md): ``in_gain`` scales
+Extension beyond the reference: ``in_gain`` scales
 the input current before integration, ``v = beta*v + in_gain*x``.  With
 ``in_gain == 1`` the computation is exactly the reference one.  The
 ``tau``-parameterised neuron ``v <- v + (x - v)/tau`` maps to
