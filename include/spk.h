@@ -100,6 +100,29 @@ int spk_lif_bwd(const float* g_spikes, const float* g_vfinal, const void* x, int
                 int64_t T, int64_t N, void* stream);
 
 /*
+ * spk_lif_bwd without a workspace argument; it allocates nothing.
+ * No counterpart in the reference (its LIFLayer.backward allocates through
+ * torch); this entry point exists for callers that cannot allocate device
+ * memory: code running while a custom allocator owns the whole device heap,
+ * plugin hosts with a memory budget fixed up front, or plain C / FFI callers
+ * with no device allocator of their own.
+ * Arguments and results are those of spk_lif_bwd, bit-identical to it.  The
+ * grad_beta partial sums go to a file-scope 16 KiB device array (4096 floats,
+ * the most any call's grid needs, so no N is too large; a call that would
+ * need more is rejected with SPK_ERR_SHAPE; T > 64 is rejected as in
+ * spk_lif_bwd).  The first call on a device, with that device current, looks
+ * up the array's address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls on a device share the array: calls whose
+ * kernels overlap on the GPU (unordered streams) race and must be serialised
+ * by the caller.  No cudaMalloc, cudaFree or allocating library routine is
+ * called.
+ */
+int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype,
+                        const void* spikes, int spike_dtype, const float* beta, const float* v_th,
+                        const float* v_reset, float in_gain, int surrogate, float surrogate_k,
+                        void* grad_x, float* grad_beta, int64_t T, int64_t N, void* stream);
+
+/*
  * Fused Linear -> LayerNorm -> LIF (tcgen05, bf16 operands, fp32 accumulate).
  *   pre = A W^T + bias;  y = LN(pre) * ln_gamma + ln_beta  (over the N features,
  *   eps = ln_eps);  LIF over T on y;  spikes (0/1) written as bf16 or fp32.

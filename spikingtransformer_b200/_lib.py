@@ -34,6 +34,7 @@ SIGNATURES = {
     "spk_lif_fwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _f, _i64, _i64, _p], _i),
     "spk_lif_bwd_workspace_bytes": ([_i64, _i64], _i64),
     "spk_lif_bwd": ([_p, _p, _p, _i, _p, _i, _p, _p, _p, _f, _i, _f, _p, _p, _p, _i64, _i64, _i64, _p], _i),
+    "spk_lif_bwd_noalloc": ([_p, _p, _p, _i, _p, _i, _p, _p, _p, _f, _i, _f, _p, _p, _i64, _i64, _p], _i),
     "spk_linear_ln_lif_fwd": ([_p, _p, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _p, _i, _p,
                                _p, _p], _i),
     "spk_linear_fwd": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),

@@ -12,6 +12,8 @@
 // (__fmul_rn / __fadd_rn / __fdiv_rn, never contracted into FMA) in the
 // reference's order, so results are bit-identical to the reference evaluated
 // in fp32 one operation at a time.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace spk {
@@ -347,6 +349,59 @@ static int check_lif_args(const void* x, int x_dtype, const void* spikes, int sp
   return SPK_OK;
 }
 
+// ---- allocation-free backward (spk_lif_bwd_noalloc) ----------------------
+// Some callers cannot allocate device memory: code that runs while a custom
+// caching allocator owns the whole device heap, plugin hosts whose memory
+// budget is fixed up front, or callers without a device allocator of their
+// own (plain C, FFI).  For them the grad_beta partial sums live in this
+// file-scope array instead of a caller-provided workspace.  It holds
+// kNoAllocScratchFloats = 4096 floats (16 KiB), the largest grid the backward
+// kernel ever launches (kBwdMaxBlocks), so no N is too large for it; a call
+// whose grid would need more partial sums is rejected with SPK_ERR_SHAPE.
+// Every call on a device shares the array and it keeps the last call's
+// contents.  Nothing in it has to start at zero: each block writes its own
+// partial before the reduction kernel, stream-ordered after it, reads
+// partials [0, grid).  Calls whose kernels overlap on the GPU (different
+// streams, no ordering between them) race on the array.
+constexpr int kNoAllocScratchFloats = 4096;
+static_assert(kNoAllocScratchFloats >= kBwdMaxBlocks, "scratch must cover the largest backward grid");
+static __device__ __align__(256) float g_lif_bwd_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+
+// Device address of g_lif_bwd_scratch on the current device.  The first call
+// on a device resolves it with cudaGetSymbolAddress (with that device
+// current, which loads the module there if it is not loaded yet); later calls
+// reuse the cached address.
+static int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[kNoAllocMaxDevices] = {};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  SPK_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, SPK_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev,
+              kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_lif_bwd_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(SPK_ERR_CUDA, "cudaGetSymbolAddress(LIF backward scratch) on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return SPK_OK;
+}
+
+// Upper bound on the grid lif_bwd_impl launches for (T, N): the scalar path
+// (one neuron per thread) gives the larger grid, and both are capped at
+// kBwdMaxBlocks.
+static int64_t noalloc_partials_needed(int64_t N) {
+  int64_t g = grid_for(N, kBwdThreads);
+  return g > kBwdMaxBlocks ? kBwdMaxBlocks : g;
+}
+
 }  // namespace spk
 
 extern "C" {
@@ -402,6 +457,37 @@ int spk_lif_bwd(const float* g_spikes, const float* g_vfinal, const void* x, int
   }
   return lif_bwd_impl(g_spikes, g_vfinal, x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, in_gain,
                       surrogate, surrogate_k, grad_x, grad_beta, reinterpret_cast<float*>(workspace), T, N, st);
+}
+
+int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype,
+                        const void* spikes, int spike_dtype, const float* beta, const float* v_th,
+                        const float* v_reset, float in_gain, int surrogate, float surrogate_k, void* grad_x,
+                        float* grad_beta, int64_t T, int64_t N, void* stream) {
+  using namespace spk;
+  int rc = check_lif_args(x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, T, N);
+  if (rc != SPK_OK) return rc;
+  SPK_REQUIRE((g_spikes && grad_x) || N == 0, SPK_ERR_INVALID, "null gradient pointer");
+  SPK_REQUIRE(surrogate == SPK_SURROGATE_SUPERSPIKE || surrogate == SPK_SURROGATE_ARCTAN, SPK_ERR_INVALID,
+              "unknown surrogate %d", surrogate);
+  SPK_REQUIRE(aligned(g_spikes, 4) && aligned(grad_x, dtype_size(x_dtype)), SPK_ERR_ALIGN,
+              "gradient pointers misaligned");
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  const int64_t need = noalloc_partials_needed(N);
+  SPK_REQUIRE(need <= kNoAllocScratchFloats, SPK_ERR_SHAPE,
+              "N=%lld needs %lld grad_beta partial sums; the static scratch holds %d", (long long)N,
+              (long long)need, kNoAllocScratchFloats);
+  float* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch)) != SPK_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    if (grad_beta) {
+      cudaError_t e = cudaMemsetAsync(grad_beta, 0, sizeof(float), st);
+      if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    return SPK_OK;
+  }
+  return lif_bwd_impl(g_spikes, g_vfinal, x, x_dtype, spikes, spike_dtype, beta, v_th, v_reset, in_gain,
+                      surrogate, surrogate_k, grad_x, grad_beta, scratch, T, N, st);
 }
 
 }  // extern "C"
