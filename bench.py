@@ -92,6 +92,22 @@ def dist_env():
     return ws, rank, local
 
 
+def shard_seed(rank, i):
+    """Seed of input set i on a rank: every rank draws its own images."""
+    return 1000 * rank + i
+
+
+def max_over_ranks(x, device):
+    """The largest value of x over all ranks (one all-reduce of a scalar);
+    x itself when no process group is running."""
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
 
@@ -235,7 +251,7 @@ def main():
     # four input sets (4 x 67 MB of images > 126 MB L2), rotated between steps
     sets = []
     for i in range(4):
-        src, tgt, mask = make_inputs(B, 1000 * rank + i)
+        src, tgt, mask = make_inputs(B, shard_seed(rank, i))
         sets.append((src.to(dev), tgt.to(dev), mask.to(dev)))
     torch.cuda.synchronize()
 
@@ -262,11 +278,7 @@ def main():
         if ws > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if ws > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = max_over_ranks(e0.elapsed_time(e1), dev)
         ops.device_error_check()
 
         # ---- end to end through the public API: pinned host inputs in, logits out
@@ -295,11 +307,7 @@ def main():
                 out_host.copy_(lg, non_blocking=True)
             f1.record()
             torch.cuda.synchronize()
-            ems = f0.elapsed_time(f1)
-            if ws > 1:
-                t = torch.tensor([ems], device=dev)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                ems = float(t.item())
+            ems = max_over_ranks(f0.elapsed_time(f1), dev)
             e2e = {"value": ws * B * args.steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h, "ms_per_step": ems / args.steps}
 
