@@ -106,9 +106,13 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
 
 // Per-file device error readers (defined in the kernel files that spin-wait).
 int gemm_read_device_error(cudaStream_t);
+int gemm_il_read_device_error(cudaStream_t);
 int ssa_read_device_error(cudaStream_t);
+int ssa_lin_read_device_error(cudaStream_t);
+int ssa_short_read_device_error(cudaStream_t);
 typedef int (*ErrorReader)(cudaStream_t);
-static ErrorReader g_error_readers[] = {gemm_read_device_error, ssa_read_device_error, nullptr};
+static ErrorReader g_error_readers[] = {gemm_read_device_error, gemm_il_read_device_error, ssa_read_device_error,
+                                        ssa_lin_read_device_error, ssa_short_read_device_error, nullptr};
 
 }  // namespace spk
 

@@ -529,6 +529,8 @@ KernelFn pick_kernel(bool fast, bool res, bool gain) {
 
 }  // namespace gil
 
+SPK_DEFINE_ERROR_READER(gemm_il_read_device_error)
+
 // Column slice for the interleaved kernel: <= 256 columns (two TMEM
 // accumulators), a multiple of 64, at most 8 CTAs per cluster.
 bool gemm_il_split(int N, int* cs, int* n_cta) {

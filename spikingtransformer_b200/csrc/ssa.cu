@@ -449,6 +449,13 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
                    const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
                    float* attn_out, cudaStream_t st);
 
+// two (batch, head) pairs per tile for Nq, Nk <= 64 (ssa_short.cu)
+int launch_ssa_short(const void* q, const void* k, const void* v, int T, int B, int H, int Nq, int Nk, int dh,
+                     int variant, int mask_mode, const uint8_t* mask, int64_t m_st, int64_t m_sb, int64_t m_sh,
+                     int64_t m_sq, const float* scale, const float* lif_beta, const float* lif_vth,
+                     const float* lif_vr, float gain, void* out_bf16, float* out_f32, float* attn_out,
+                     cudaStream_t st);
+
 static bool force_dense() {
   static int v = -1;
   if (v < 0) {
@@ -500,6 +507,14 @@ int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int ma
                         out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out,
                         reinterpret_cast<cudaStream_t>(stream));
     if (rc == SPK_OK) return check_launch("ssa_lin_kernel");
+    if (rc != SPK_ERR_UNSUPPORTED) return rc;
+  }
+  if (Nq <= 64 && Nk <= 64 && !force_dense()) {
+    rc = launch_ssa_short(q, k, v, (int)T, (int)B, (int)H, (int)Nq, (int)Nk, (int)dh, variant, mask_mode, mask,
+                          mask_stride_t, mask_stride_b, mask_stride_h, mask_stride_q, scale, lif_beta, lif_vth,
+                          lif_vreset, in_gain, out_dtype == SPK_BF16 ? out : nullptr,
+                          out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out,
+                          reinterpret_cast<cudaStream_t>(stream));
     if (rc != SPK_ERR_UNSUPPORTED) return rc;
   }
   Params p = {};

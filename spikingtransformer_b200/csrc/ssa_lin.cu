@@ -456,6 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace ssal
 
+SPK_DEFINE_ERROR_READER(ssa_lin_read_device_error)
+
 // Host launcher used by spk_ssa_fwd for unmasked attention; returns
 // SPK_ERR_UNSUPPORTED when the sizes are outside this kernel's range.
 int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, int T, int B, int H,

@@ -238,6 +238,11 @@ def spikes_qkv(seed, TB, Nq, Nk, D, p=0.15):
     (4, 2, 8, 64, 256, 48, None),      # decoder cross-attention
     (2, 2, 2, 130, 70, 64, "dense"),
     (1, 1, 1, 200, 300, 16, "dense"),
+    # short sequences (two (batch, head) pairs per tile): odd pair count,
+    # Nq != Nk, keys < 32, head width 8 / 16 / 32
+    (3, 5, 3, 33, 50, 32, "dense"),
+    (2, 3, 3, 64, 20, 16, "dense"),
+    (2, 2, 4, 12, 12, 8, "causal"),
 ])
 def test_ssa(ops, variant, T, B, H, Nq, Nk, dh, maskkind):
     D = H * dh
