@@ -23,9 +23,12 @@
 //    reference) and spikes are written as bf16 bit patterns straight from the
 //    threshold compare.
 //  * TMEM loads are 32 columns wide and double-buffered.
-//  * Compile-time variants: FAST (bf16 spikes and/or residual add only) with
-//    the residual add and the input gain specialised; a general variant
-//    handles fp32 spikes and the LayerNorm debug output.
+//  * Compile-time variants: FAST (bf16 spikes and/or residual add only, the
+//    residual add specialised) and a general variant for fp32 spikes and the
+//    LayerNorm debug output.  The fast variant pre-loads each accumulator with
+//    the bias (tcgen05.st by the epilogue before handing it back), folds the
+//    LIF input gain into gamma/beta, and runs the LIF branch-free as
+//    u = beta (1 - s) u + y + s beta v_reset with s from set.gt.
 #include "common.cuh"
 
 namespace spk {
@@ -106,6 +109,20 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   return off;
 }
 
+// 1.0f if a > b else 0.0f
+__device__ __forceinline__ float set_gt(float a, float b) {
+  float r;
+  asm("set.gt.f32.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// bf16 pair {hi16(lo), hi16(hi)}: the bf16 patterns of two floats that are 0 or 1
+__device__ __forceinline__ uint32_t bf16x2_of_01(float lo, float hi) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(__float_as_uint(lo)), "r"(__float_as_uint(hi)));
+  return r;
+}
+
 // merge (mean_b, M2_b) over nb samples into (mean, M2) over na samples
 __device__ __forceinline__ void chan_merge(float& mean, float& m2, float na, float mb, float m2b, float nb) {
   const float tot = na + nb;
@@ -114,7 +131,7 @@ __device__ __forceinline__ void chan_merge(float& mean, float& m2, float na, flo
   m2 = m2 + m2b + d * d * (na * nb / tot);
 }
 
-template <int T, bool FAST, bool RES, bool GAIN>
+template <int T, bool FAST, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_il_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const Params p) {
@@ -152,11 +169,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   {
+    // the fast variant folds the LIF input gain into the affine LayerNorm parameters
     const int n0 = (int)rank * p.n_cta;
+    const float g = FAST ? p.gain : 1.0f;
     for (int c = threadIdx.x; c < p.n_cta; c += kThreads) {
       sm.bias[c] = p.bias ? p.bias[n0 + c] : 0.0f;
-      sm.gamma[c] = p.gamma ? p.gamma[n0 + c] : 1.0f;
-      sm.beta[c] = p.beta_ln ? p.beta_ln[n0 + c] : 0.0f;
+      sm.gamma[c] = (p.gamma ? p.gamma[n0 + c] : 1.0f) * g;
+      sm.beta[c] = (p.beta_ln ? p.beta_ln[n0 + c] : 0.0f) * g;
     }
   }
   tc_fence_before();
@@ -205,7 +224,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int iter = 0;
     for (int tile = cid; tile < p.num_m_tiles && ok; tile += ncl, ++iter) {
       const int buf = iter & 1;
-      if (!mbar_wait(&sm.acc_empty[buf], ((uint32_t)(iter >> 1) & 1u) ^ 1u, 121)) { ok = false; break; }
+      // fast variant: the epilogue hands each accumulator over pre-loaded with the bias
+      // (one arrival per use, the first before the first tile)
+      if (!mbar_wait(&sm.acc_empty[buf], ((uint32_t)(iter >> 1) & 1u) ^ (FAST ? 0u : 1u), 121)) { ok = false; break; }
       tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t)(buf * p.n_cta);
       for (int kc = 0; kc < nk; ++kc) {
@@ -218,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             umma_bf16(dcol, umma_desc(a_addr + kk * 32, 16, 1024, 2), umma_desc(w_addr + kk * 32, 16, 1024, 2),
-                      idesc, (kc | kk) ? 1u : 0u);
+                      idesc, (FAST || (kc | kk)) ? 1u : 0u);
           umma_commit(&sm.empty[stage]);
         }
         __syncwarp();
@@ -254,6 +275,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warp-private transposition buffer: row r (tile row within the quadrant), column c at r*kXS + c
     float* xs = sm.xs + ew * 32 * kXS;
     float* xs_wr = xs + lane * kXS;
+    // fast variant: LIF integration as u = beta (1 - s) u + y (+ s beta v_reset), s the previous spike
+    const float2 nbeta2 = make_float2(-beta, -beta);
+    const float bvr = __fmul_rn(beta, vr);
+    const float2 bvr2 = make_float2(bvr, bvr);
+    // fast variant: this thread's lane and columns of an accumulator := bias, so the MMAs add it
+    auto write_bias = [&](uint32_t tcol) {
+      for (int c = 0; c < 2 * nch; ++c) {
+        uint32_t r[16];
+        const float* bsrc = sm.bias + cb + c * 16;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(bsrc + i);
+          r[i] = __float_as_uint(b4.x);
+          r[i + 1] = __float_as_uint(b4.y);
+          r[i + 2] = __float_as_uint(b4.z);
+          r[i + 3] = __float_as_uint(b4.w);
+        }
+        tmem_st16(tcol + c * 16, r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+    };
+    if constexpr (FAST) {
+      for (int b = 0; b < 2; ++b) {
+        write_bias(tmem + lane_off + (uint32_t)(b * p.n_cta + cb));
+        if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      }
+    }
     int iter = 0;
     for (int tile = cid; tile < p.num_m_tiles; tile += ncl, ++iter) {
       const int buf = iter & 1;
@@ -262,7 +312,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t trow = tmem + lane_off + (uint32_t)(buf * p.n_cta + cb);
       // ---- statistics over this warp's columns
       float mean, m2;
-      {
+      if constexpr (FAST) {
+        // one pass of sums shifted by the row's first value (the bias is already in the accumulator)
+        float2 s1a = make_float2(0.0f, 0.0f), s2a = s1a, s1b = s1a, s2b = s1a, nK2 = s1a;
+        float K = 0.0f;
+        auto stats_chunk = [&](const uint32_t (&r)[32]) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float2 d0 = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nK2);
+            const float2 d1 = add2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])), nK2);
+            s1a = add2(s1a, d0);
+            s1b = add2(s1b, d1);
+            s2a = fma2(d0, d0, s2a);
+            s2b = fma2(d1, d1, s2b);
+          }
+        };
+        uint32_t ra[32], rb[32];
+        tmem_ld32_raw(trow, ra);
+        for (int c = 0; c < nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence32(ra);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
+            if (c == 0) {
+              K = __uint_as_float(ra[0]);
+              nK2 = make_float2(-K, -K);
+            }
+            stats_chunk(ra);
+          } else {
+            tmem_wait_ld_fence32(rb);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+            stats_chunk(rb);
+          }
+        }
+        const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
+        const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
+        const float inv_n = 1.0f / (float)half;
+        mean = K + S1 * inv_n;
+        m2 = fmaxf(S2 - S1 * S1 * inv_n, 0.0f);
+      } else {
         float K = 0.0f;
         float2 s1 = make_float2(0.0f, 0.0f), s2 = make_float2(0.0f, 0.0f);
         float2 s1b = s1, s2b = s2;
@@ -366,11 +453,135 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float rstd = 1.0f / sqrtf(m2 / (float)p.N + p.eps);
       const float2 rstd2 = make_float2(rstd, rstd);
       const float2 nmean2 = make_float2(-mean, -mean);
+      const float nmr = -mean * rstd;
+      const float2 nmr2 = make_float2(nmr, nmr);
 
       // ---- normalise, transpose, LIF, store
       const int64_t gtok = (int64_t)tile * p.tpt + q * TPQ + tok_l;
       const bool tok_ok = gtok < p.R;
       const int64_t lane_out = gtok * p.N + n0 + cb + jblk * CPL;  // element offset at t = 0
+      auto norm_sub_fast = [&](const uint32_t* r, int c16) {
+        const int col = cb + c16 * 16;  // column within the slice
+        const int64_t off0 = lane_out + c16 * 16;
+        constexpr int NP = CPL >= 2 ? CPL / 2 : 1;  // bf16 pairs per step
+        // residual words of all T steps first: their latency hides behind the arithmetic below
+        uint32_t rs[T][NP];
+        if (RES && tok_ok) {
+#pragma unroll
+          for (int t = 0; t < T; ++t) {
+            const __nv_bfloat16* src = p.residual + off0 + (int64_t)t * tstride;
+            if constexpr (CPL == 16) {
+              const uint4 a = *reinterpret_cast<const uint4*>(src), b = *reinterpret_cast<const uint4*>(src + 8);
+              rs[t][0] = a.x; rs[t][1] = a.y; rs[t][2] = a.z; rs[t][3] = a.w;
+              rs[t][4] = b.x; rs[t][5] = b.y; rs[t][6] = b.z; rs[t][7] = b.w;
+            } else if constexpr (CPL == 8) {
+              const uint4 a = *reinterpret_cast<const uint4*>(src);
+              rs[t][0] = a.x; rs[t][1] = a.y; rs[t][2] = a.z; rs[t][3] = a.w;
+            } else if constexpr (CPL == 4) {
+              const uint2 a = *reinterpret_cast<const uint2*>(src);
+              rs[t][0] = a.x; rs[t][1] = a.y;
+            } else if constexpr (CPL == 2) {
+              rs[t][0] = *reinterpret_cast<const uint32_t*>(src);
+            } else {
+              rs[t][0] = *reinterpret_cast<const uint16_t*>(src);
+            }
+          }
+        }
+        // y' = (x - mean) rstd (gain gamma) + gain beta; x already holds the bias
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 g4 = *reinterpret_cast<const float4*>(sm.gamma + col + i);
+          const float4 e4 = *reinterpret_cast<const float4*>(sm.beta + col + i);
+          float2 x0 = make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          float2 x1 = make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          x0 = fma2(fma2(x0, rstd2, nmr2), make_float2(g4.x, g4.y), make_float2(e4.x, e4.y));
+          x1 = fma2(fma2(x1, rstd2, nmr2), make_float2(g4.z, g4.w), make_float2(e4.z, e4.w));
+          *reinterpret_cast<float4*>(xs_wr + i) = make_float4(x0.x, x0.y, x1.x, x1.y);
+        }
+        __syncwarp();
+        float yt[T][CPL];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int rr = tok_l * T + t;
+#pragma unroll
+          for (int u = 0; u < CPL; u += (CPL >= 4 ? 4 : CPL)) {
+            const float* src = xs + rr * kXS + jblk * CPL + u;
+            if constexpr (CPL >= 4) {
+              const float4 v4 = *reinterpret_cast<const float4*>(src);
+              yt[t][u] = v4.x;
+              yt[t][u + 1] = v4.y;
+              yt[t][u + 2] = v4.z;
+              yt[t][u + 3] = v4.w;
+            } else if constexpr (CPL == 2) {
+              const float2 v2 = *reinterpret_cast<const float2*>(src);
+              yt[t][u] = v2.x;
+              yt[t][u + 1] = v2.y;
+            } else {
+              yt[t][u] = *src;
+            }
+          }
+        }
+        __syncwarp();
+        if (!tok_ok) return;
+        __nv_bfloat16* sp_ptr = p.spk_bf16 ? p.spk_bf16 + off0 : nullptr;
+        float2 u2[NP], s2[NP];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          uint32_t bits[NP];
+#pragma unroll
+          for (int u = 0; u < NP; ++u) {
+            float2 y2 = CPL >= 2 ? make_float2(yt[t][2 * u], yt[t][(2 * u + 1) % CPL]) : make_float2(yt[t][0], 0.0f);
+            if (t == 0) {
+              u2[u] = y2;  // membrane starts at 0
+            } else {
+              y2 = fma2(s2[u], bvr2, y2);  // exact no-op when v_reset = 0
+              u2[u] = fma2(fma2(s2[u], nbeta2, beta2), u2[u], y2);
+            }
+            s2[u] = make_float2(set_gt(u2[u].x, vth), set_gt(u2[u].y, vth));
+            bits[u] = bf16x2_of_01(s2[u].x, s2[u].y);
+          }
+          if (sp_ptr) {
+            if constexpr (CPL == 16) {
+              *reinterpret_cast<uint4*>(sp_ptr) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+              *reinterpret_cast<uint4*>(sp_ptr + 8) = make_uint4(bits[4], bits[5], bits[6], bits[7]);
+            } else if constexpr (CPL == 8) {
+              *reinterpret_cast<uint4*>(sp_ptr) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+            } else if constexpr (CPL == 4) {
+              *reinterpret_cast<uint2*>(sp_ptr) = make_uint2(bits[0], bits[1]);
+            } else if constexpr (CPL == 2) {
+              *reinterpret_cast<uint32_t*>(sp_ptr) = bits[0];
+            } else {
+              *reinterpret_cast<uint16_t*>(sp_ptr) = (uint16_t)(bits[0] & 0xFFFFu);
+            }
+            sp_ptr += tstride;
+          }
+          if constexpr (RES) {
+            // spikes are exactly 0/1 and the stream holds small integers: the bf16 add is exact
+            __nv_bfloat16* dst = p.residual + off0 + (int64_t)t * tstride;
+            uint32_t o[NP];
+#pragma unroll
+            for (int u = 0; u < NP; ++u) {
+              __nv_bfloat162 a, b;
+              *reinterpret_cast<uint32_t*>(&a) = rs[t][u];
+              *reinterpret_cast<uint32_t*>(&b) = bits[u];
+              const __nv_bfloat162 c = __hadd2(a, b);
+              o[u] = *reinterpret_cast<const uint32_t*>(&c);
+            }
+            if constexpr (CPL == 16) {
+              *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(dst + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+            } else if constexpr (CPL == 8) {
+              *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else if constexpr (CPL == 4) {
+              *reinterpret_cast<uint2*>(dst) = make_uint2(o[0], o[1]);
+            } else if constexpr (CPL == 2) {
+              *reinterpret_cast<uint32_t*>(dst) = o[0];
+            } else {
+              *reinterpret_cast<uint16_t*>(dst) = (uint16_t)(o[0] & 0xFFFFu);
+            }
+          }
+        }
+      };
       auto norm_sub = [&](const uint32_t* r, int c16) {
         const int col = cb + c16 * 16;  // column within the slice
         float* ln_dst = nullptr;
@@ -431,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < NP; ++u) {
             float2 y2 = CPL >= 2 ? make_float2(yt[t][2 * u], yt[t][(2 * u + 1) % CPL]) : make_float2(yt[t][0], 0.0f);
-            if (GAIN) y2 = mul2(y2, gain2);
+            y2 = mul2(y2, gain2);
             const float2 uu = add2(mul2(mem2[u], beta2), y2);
             const bool f0 = uu.x > vth, f1 = uu.y > vth;
             mem2[u] = make_float2(f0 ? vr : uu.x, f1 ? vr : uu.y);
@@ -480,7 +691,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      {
+      if constexpr (FAST) {
+        // 16-column TMEM loads, double-buffered
+        uint32_t ra[16], rb[16];
+        tmem_ld16_raw(trow, ra);
+        for (int c = 0; c < 2 * nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence(ra);
+            if (c + 1 < 2 * nch) tmem_ld16_raw(trow + (c + 1) * 16, rb);
+            norm_sub_fast(ra, c);
+          } else {
+            tmem_wait_ld_fence(rb);
+            if (c + 1 < 2 * nch) tmem_ld16_raw(trow + (c + 1) * 16, ra);
+            norm_sub_fast(rb, c);
+          }
+        }
+      } else {
         uint32_t ra[32], rb[32];
         tmem_ld32_raw(trow, ra);
         for (int c = 0; c < nch; ++c) {
@@ -506,6 +732,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if constexpr (FAST) {
+        // hand the buffer back to the MMA warp pre-loaded with the bias for its next tile
+        write_bias(trow);
+        if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+      }
     }
   }
 
@@ -521,10 +752,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const Params);
 
 template <int T>
-KernelFn pick_kernel(bool fast, bool res, bool gain) {
-  if (!fast) return gemm_il_kernel<T, false, true, true>;
-  if (res) return gain ? gemm_il_kernel<T, true, true, true> : gemm_il_kernel<T, true, true, false>;
-  return gain ? gemm_il_kernel<T, true, false, true> : gemm_il_kernel<T, true, false, false>;
+KernelFn pick_kernel(bool fast, bool res) {
+  if (!fast) return gemm_il_kernel<T, false, true>;
+  return res ? gemm_il_kernel<T, true, true> : gemm_il_kernel<T, true, false>;
 }
 
 }  // namespace gil
@@ -601,14 +831,13 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   if (smem > (size_t)kMaxSmem) return fail(SPK_ERR_SHAPE, "tile of %d columns does not fit in shared memory", n_cta);
   const bool fast = spk_f32 == nullptr && ln_out == nullptr;
   const bool res = residual != nullptr;
-  const bool gn = gain != 1.0f;
   KernelFn kern;
   switch (T) {
-    case 1: kern = pick_kernel<1>(fast, res, gn); break;
-    case 2: kern = pick_kernel<2>(fast, res, gn); break;
-    case 4: kern = pick_kernel<4>(fast, res, gn); break;
-    case 8: kern = pick_kernel<8>(fast, res, gn); break;
-    default: kern = pick_kernel<16>(fast, res, gn); break;
+    case 1: kern = pick_kernel<1>(fast, res); break;
+    case 2: kern = pick_kernel<2>(fast, res); break;
+    case 4: kern = pick_kernel<4>(fast, res); break;
+    case 8: kern = pick_kernel<8>(fast, res); break;
+    default: kern = pick_kernel<16>(fast, res); break;
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));

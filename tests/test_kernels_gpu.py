@@ -143,6 +143,30 @@ def test_linear_ln_lif(ops, T, R, K, N):
     assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
 
 
+@pytest.mark.parametrize("T,R,K,N,gain,vr,res", [
+    (4, 256, 384, 384, 1.0, 0.0, False),
+    (4, 256, 384, 384, 0.5, 0.0, True),     # out_proj with the residual add
+    (4, 96, 384, 1536, 0.5, 0.0, False),    # MLP expand (cluster split)
+    (4, 64, 1536, 384, 1.0, -0.25, True),   # MLP compress, non-zero reset
+    (2, 100, 128, 256, 0.7, 0.125, True),
+    (8, 40, 64, 128, 1.0, 0.0, False),
+    (1, 300, 128, 64, 1.0, 0.0, True),
+    (16, 20, 64, 64, 1.0, 0.0, True),
+])
+def test_linear_ln_lif_fast(ops, T, R, K, N, gain, vr, res):
+    # bf16 spikes without the LayerNorm output: the kernel variant the model runs
+    A, W, bias, gamma, beta_ln = make_lin(T * 13 + R + K + N, R, K, N, T, counts=2)
+    s_ref, _, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.9, 1.0, vr, gain=gain)
+    resid = torch.randint(0, 5, (T * R, N), generator=gen(R)).to(torch.bfloat16) if res else None
+    r_dev = resid.to(DEV) if res else None
+    s, y = ops.linear_ln_lif(A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.9, 1.0,
+                             vr, T, in_gain=gain, residual=r_dev, spike_dtype=torch.bfloat16)
+    assert y is None and s.dtype == torch.bfloat16
+    assert_spikes_match(s.float().cpu().reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+    if res:
+        assert torch.equal(r_dev.float().cpu(), resid.float() + s.float().cpu())
+
+
 def test_linear_ln_lif_cfg2_tau(ops):
     # fused Linear->LN->LIF at the cfg-2 feature sizes (tau=2 neuron), fewer rows
     T, R, K, N = 4, 2048, 384, 1536
