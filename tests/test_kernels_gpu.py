@@ -148,6 +148,7 @@ def test_linear_ln_lif(ops, T, R, K, N):
     (4, 256, 384, 384, 0.5, 0.0, True),     # out_proj with the residual add
     (4, 96, 384, 1536, 0.5, 0.0, False),    # MLP expand (cluster split)
     (4, 64, 1536, 384, 1.0, -0.25, True),   # MLP compress, non-zero reset
+    (4, 50, 128, 128, 0.5, 0.0, True),      # token count not a multiple of 8
     (2, 100, 128, 256, 0.7, 0.125, True),
     (8, 40, 64, 128, 1.0, 0.0, False),
     (1, 300, 128, 64, 1.0, 0.0, True),
