@@ -11,39 +11,47 @@
 // Every term is an integer computed exactly (bf16 operands <= 512, fp32
 // accumulation < 2^24), so O equals the dense product bit for bit; the
 // output stage (a = scale*O, LIF over t) is the dense kernel's.  Cost per
-// (t, query block) is O(Nk*dh*(dh+Nq)) tensor work and O(Nq*dh) epilogue work
+// (t, batch, head) is O(Nk*dh*(dh+Nq)) tensor work and O(Nq*dh) epilogue work
 // instead of O(Nq*Nk) score elements.
 //
-// Per CTA: a persistent walk over (query block, batch, head) items with the
-// query block outermost.  The log-distance matrix R of the query block
-// (128 x Nk, bf16, values <= 13) stays resident in TMEM as the A operand of
-// the R V product.  Per timestep:
+// Per CTA: a persistent walk over (batch, head) items, each over its T steps;
+// one unit (item, t) covers all Nq <= 256 queries (one or two 128-row blocks),
+// so K and V are read once per (t, batch, head).  The log-distance matrix R
+// of both query blocks (128 x Nk each, bf16, values <= 13) is built once and
+// stays resident in TMEM as the A operand of the R V products.  Per unit:
 //   MMA1  D1[128 x dh] = A1 V,  A1 = [K^T ; AUX^T] (MN-major, two 64-row
 //         atoms: K tile and an auxiliary tile whose columns 0/1 hold 1 and
 //         s_j), so D1 rows 0..dh-1 = K^T V, row 64 = 1^T V, row 65 = s^T V
-//   epi   rows 0..63 of D1 -> bf16 (x2 for XNOR) B operand in shared memory
-//   MMA2  D2 = Q (2 K^T V) [+ R V]
-//   epi   O = D2 + c_i (1^T V) - s^T V; a = scale O; LIF over t; spikes
-// Requirements: Nk <= 256, dh <= 64 (dh % 8 == 0).
+//   epi   rows 0..63 of D1 -> bf16 (x2 for XNOR) B operand Mb in shared memory;
+//         Mb has one extra column of ones
+//   MMA2  per query block: D2 = Q [2 K^T V | 1] [+ R V]; the extra column
+//         gives |q_i|, so the epilogue never reads Q
+//   epi   O = D2 + (dh - |q_i|) (1^T V) - s^T V; a = scale O; LIF over t
+// Warps: 0 TMA, 1 TMEM owner + MMA issuer, 2-9 epilogue (two groups of four;
+// with two query blocks each group owns one, with one they split the head
+// dimension).  Requirements: Nq <= 256, Nk <= 256, dh <= 64 (dh % 8 == 0).
 #include "common.cuh"
 
 namespace spk {
 namespace ssal {
 
-constexpr int kThreads = 192;
-constexpr int kEpi = 128;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kEpi = 32 * kEpiWarps;
 constexpr int kQTile = 128 * 128;   // 128 rows x 128 B
 constexpr int kKVTile = 256 * 128;  // 256 rows x 128 B
 
 struct Params {
   int T, B, H, Nq, Nk, dh;
+  int QB;      // query blocks of 128 (1 or 2)
+  int dsplit;  // head-dimension split between the two epilogue groups when QB = 1
   const float* scale;
   const float *lif_beta, *lif_vth, *lif_vr;
   float gain;
   __nv_bfloat16* out_bf16;
   float* out_f32;
   float* attn_out;
-  int q_blocks, lmax, items;
+  int lmax, items;
 };
 
 struct Smem {
@@ -66,7 +74,7 @@ __host__ __device__ inline size_t smem_layout(int lmax, uint8_t* base, Smem* s) 
   };
   size_t oq = take(2 * kQTile, 1024), ok = take(2 * kKVTile, 1024), ov = take(2 * kKVTile, 1024);
   size_t oaux = take(kKVTile, 1024);  // after both K slots: positive LBO from K to AUX
-  size_t omb = take(64 * 128, 1024);
+  size_t omb = take(2 * 64 * 128, 1024);  // two 64-column atoms: [2 K^T V | ones]
   size_t ocs = take(2 * 64 * 4, 16), okv = take(2 * 64 * 4, 16);
   size_t orl = take((size_t)lmax, 16);
   size_t ob = take(20 * 8, 8), otm = take(4, 4);
@@ -81,16 +89,16 @@ __host__ __device__ inline size_t smem_layout(int lmax, uint8_t* base, Smem* s) 
     s->kv = reinterpret_cast<float*>(base + okv);
     uint64_t* b = reinterpret_cast<uint64_t*>(base + ob);
     s->q_full = b;
-    s->q_empty = b + 2;
-    s->kv_full = b + 4;
-    s->kv_empty = b + 6;
-    s->aux_ready = b + 8;
-    s->m_full = b + 9;
-    s->mb_ready = b + 10;
-    s->o_full = b + 11;
-    s->o_empty = b + 12;
-    s->r_ready = b + 13;
-    s->drain = b + 14;
+    s->q_empty = b + 1;
+    s->kv_full = b + 2;
+    s->kv_empty = b + 4;
+    s->aux_ready = b + 6;
+    s->m_full = b + 7;
+    s->mb_ready = b + 8;
+    s->o_full = b + 9;
+    s->o_empty = b + 10;
+    s->r_ready = b + 11;
+    s->drain = b + 12;
     s->tmem_base = reinterpret_cast<uint32_t*>(base + otm);
   }
   return off;
@@ -124,14 +132,14 @@ __device__ __forceinline__ void load_4d(void* dst, const CUtensorMap* map, uint6
       : "memory");
 }
 
-// DP: head width rounded up to 16 (the N of both MMAs); XNOR selects the
-// S' = 2QK^T + c - s + R form, otherwise the plain Q K^T.
+// DP: head width rounded up to 16; XNOR selects the S' = 2QK^T + c - s + R
+// form, otherwise the plain Q K^T.  NO = DP + 16: the columns of D2 (the
+// product with Mb and its ones column).
 template <int DP, bool XNOR>
 __global__ void __launch_bounds__(kThreads, 1)
     ssa_lin_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const Params p) {
-  // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
-  // it by plain arithmetic so the compiler keeps them in the shared address space
+  constexpr int NO = DP + 16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = smem_raw;
   Smem sm;
@@ -139,24 +147,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ksteps = (p.Nk + 15) >> 4;
   constexpr int dsteps = DP / 16;
-  const int BH = p.B * p.H;
+  const int QB = p.QB;
   // per-CTA sequence of work units g = (item, t): item = blockIdx.x + k * gridDim.x
   const int n_items = p.items > (int)blockIdx.x ? (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
   const int n_units = n_items * p.T;
 
   if (threadIdx.x == 0) {
+    mbar_init(sm.q_full, 1);
+    mbar_init(sm.q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.q_full[i], 1);
-      mbar_init(&sm.q_empty[i], 1 + 4);
       mbar_init(&sm.kv_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1 + 4);
+      mbar_init(&sm.kv_empty[i], 1 + kEpiWarps);
     }
-    mbar_init(sm.aux_ready, 4);
+    mbar_init(sm.aux_ready, kEpiWarps);
     mbar_init(sm.m_full, 1);
     mbar_init(sm.mb_ready, 1);
     mbar_init(sm.o_full, 1);
-    mbar_init(sm.o_empty, 4);
-    mbar_init(sm.r_ready, 4);
+    mbar_init(sm.o_empty, kEpiWarps);
+    mbar_init(sm.r_ready, kEpiWarps);
     mbar_init(sm.drain, 1);
     fence_mbar_init();
   }
@@ -166,6 +174,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint4 w = make_uint4(0, 0, 0, 0);
     if ((c ^ (r & 7)) == 0 && r < p.Nk) w.x = 0x3F80u;  // logical chunk 0, element 0 = 1.0
     *reinterpret_cast<uint4*>(sm.aux + i * 16) = w;
+  }
+  // Mb: zero, then the ones column (column DP: atom DP/64, chunk (DP%64)/8, element 0)
+  for (int i = threadIdx.x; i < (2 * 64 * 128) / 16; i += kThreads) {
+    const int atom = i >> 9, r = (i >> 3) & 63, c = i & 7;
+    uint4 w = make_uint4(0, 0, 0, 0);
+    if (atom == DP / 64 && (c ^ (r & 7)) == (DP % 64) / 8) w.x = 0x3F80u;
+    *reinterpret_cast<uint4*>(sm.mb + i * 16) = w;
   }
   // log-distance table R[d] = smallest k >= 0 with (d+1) * 2^k >= L-1
   for (int d = threadIdx.x; d < p.lmax; d += kThreads) {
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.rl[d] = (uint8_t)k;
   }
   if (warp == 1) {
-    tmem_alloc(sm.tmem_base, 256);
+    tmem_alloc(sm.tmem_base, 512);
     tmem_relinquish();
   }
   fence_proxy_async_smem();
@@ -187,7 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
-  const uint32_t tm_r = tmem, tm_d1 = tmem + 128, tm_d2 = tmem + 192;
+  // R: [0, 256) (128 columns per query block), D1: [256, 320), D2: [320, 320 + 2 NO)
+  const uint32_t tm_r = tmem, tm_d1 = tmem + 256, tm_d2 = tmem + 320;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
@@ -196,11 +212,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       bool ok = true;
-      int q_ph[2] = {-1, -1}, kv_ph[2] = {-1, -1};
+      int q_ph = -1, kv_ph[2] = {-1, -1};
       for (int g = 0; g < n_units && ok; ++g) {
         const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
-        const int qb = item / BH, bh = item % BH;
-        const int b = bh / p.H, h = bh % p.H;
+        const int b = item / p.H, h = item % p.H;
         const int s = g & 1;
         const uint32_t ph = (uint32_t)((g >> 1) & 1);
         if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, 72)) { ok = false; break; }
@@ -210,27 +225,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           load_4d(sm.k + s * kKVTile + half * kQTile, &tmK, &sm.kv_full[s], h, half * 128, t * p.B + b);
           load_4d(sm.v + s * kKVTile + half * kQTile, &tmV, &sm.kv_full[s], h, half * 128, t * p.B + b);
         }
-        if (!mbar_wait(&sm.q_empty[s], ph ^ 1u, 71)) { ok = false; break; }
-        mbar_expect_tx(&sm.q_full[s], kQTile);
-        q_ph[s] = (int)ph;
-        load_4d(sm.q + s * kQTile, &tmQ, &sm.q_full[s], h, qb * 128, t * p.B + b);
+        if (!mbar_wait(sm.q_empty, (uint32_t)((g & 1) ^ 1), 71)) { ok = false; break; }
+        mbar_expect_tx(sm.q_full, (uint32_t)(QB * kQTile));
+        q_ph = g & 1;
+        for (int qb = 0; qb < QB; ++qb)
+          load_4d(sm.q + qb * kQTile, &tmQ, sm.q_full, h, qb * 128, t * p.B + b);
       }
       if (!ok) {
-        for (int i = 0; i < 2; ++i) {
-          if (q_ph[i] >= 0) mbar_wait(&sm.q_full[i], (uint32_t)q_ph[i], 73);
+        if (q_ph >= 0) mbar_wait(sm.q_full, (uint32_t)q_ph, 73);
+        for (int i = 0; i < 2; ++i)
           if (kv_ph[i] >= 0) mbar_wait(&sm.kv_full[i], (uint32_t)kv_ph[i], 73);
-        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     bool ok = true;
-    int r_uses = 0, prev_qb = -1;
-    const uint32_t id1 = idesc_bf16_f32(128, DP, 1, 1);  // A1, V: MN-major
-    const uint32_t id2 = idesc_bf16_f32(128, DP, 0, 1);  // Q: K-major, Mb / V: MN-major
+    const uint32_t id1 = idesc_bf16_f32(128, DP, 1, 1);   // A1, V: MN-major
+    const uint32_t idq = idesc_bf16_f32(128, NO, 0, 1);   // Q: K-major, Mb: MN-major
+    const uint32_t idr = idesc_bf16_f32(128, DP, 0, 1);   // R (TMEM), V: MN-major
+    if (XNOR && n_units > 0 && !mbar_wait(sm.r_ready, 0u, 81)) ok = false;
     for (int g = 0; g < n_units && ok; ++g) {
-      const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x;
-      const int qb = item / BH;
       const int s = g & 1;
       const uint32_t ph = (uint32_t)((g >> 1) & 1);
       // MMA1: [K^T ; AUX^T] V
@@ -246,28 +260,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(sm.m_full);
       }
       __syncwarp();
-      // MMA2: Q (2 K^T V) [+ R V]
-      if (XNOR && qb != prev_qb) {
-        if (!mbar_wait(sm.r_ready, (uint32_t)(r_uses & 1), 81)) { ok = false; break; }
-        ++r_uses;
-        prev_qb = qb;
-      }
+      // MMA2 per query block: Q [2 K^T V | 1] [+ R V]
       if (!mbar_wait(sm.mb_ready, (uint32_t)(g & 1), 84)) { ok = false; break; }
-      if (!mbar_wait(&sm.q_full[s], ph, 85)) { ok = false; break; }
+      if (!mbar_wait(sm.q_full, (uint32_t)(g & 1), 85)) { ok = false; break; }
       if (!mbar_wait(sm.o_empty, (uint32_t)((g & 1) ^ 1), 86)) { ok = false; break; }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t qa = smem_u32(sm.q + s * kQTile), mba = smem_u32(sm.mb);
-        const uint32_t va = smem_u32(sm.v + s * kKVTile);
+        const uint32_t mba = smem_u32(sm.mb), va = smem_u32(sm.v + s * kKVTile);
+        for (int qb = 0; qb < QB; ++qb) {
+          const uint32_t qa = smem_u32(sm.q + qb * kQTile);
 #pragma unroll
-        for (int kk = 0; kk < dsteps; ++kk)
-          umma_bf16(tm_d2, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(mba + kk * 2048, 8192, 1024, 2), id2,
-                    kk > 0 ? 1u : 0u);
-        if (XNOR)
-          for (int kk = 0; kk < ksteps; ++kk)
-            umma_bf16_ts(tm_d2, tm_r + kk * 8, umma_desc(va + kk * 2048, kKVTile, 1024, 2), id2, 1u);
+          for (int kk = 0; kk < dsteps; ++kk)
+            umma_bf16(tm_d2 + qb * NO, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(mba + kk * 2048, 8192, 1024, 2),
+                      idq, kk > 0 ? 1u : 0u);
+          if (XNOR)
+            for (int kk = 0; kk < ksteps; ++kk)
+              umma_bf16_ts(tm_d2 + qb * NO, tm_r + qb * 128 + kk * 8, umma_desc(va + kk * 2048, kKVTile, 1024, 2),
+                           idr, 1u);
+        }
         umma_commit(sm.o_full);
-        umma_commit(&sm.q_empty[s]);
+        umma_commit(sm.q_empty);
         umma_commit(&sm.kv_empty[s]);
       }
       __syncwarp();
@@ -278,33 +290,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(sm.drain, 0, 87);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (lane = query row / D1 row)
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;           // TMEM lane quadrant
+    const int grp = ew >> 2;             // epilogue group
+    const int lrow = quad * 32 + lane;   // TMEM lane = row within a 128-row block
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int qb = QB == 2 ? grp : 0;    // query block of this thread's row
+    const int dc0 = QB == 2 ? 0 : (grp ? p.dsplit : 0);           // first head column
+    const int dcols = QB == 2 ? p.dh : (grp ? p.dh - p.dsplit : p.dsplit);
+    const int qi = qb * 128 + lrow;
     const float scale = __ldg(p.scale);
     const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
     const int D = p.H * p.dh;
     bool ok = true;
-    int prev_qb = -1;
     float mem[DP];
 #pragma unroll
     for (int i = 0; i < DP; ++i) mem[i] = 0.0f;
 
-    // key sums of unit g into the auxiliary tile, query sum of unit g; releases K and Q for reading
-    auto prepare = [&](int g, float& c_row) -> bool {
+    // R rows of both query blocks -> TMEM once (bf16 pairs: keys 2c and 2c+1 in column c)
+    if (XNOR) {
+      const int rb = QB == 2 ? grp : 0;                       // block built by this group
+      const int cbeg = QB == 2 ? 0 : grp * 64, cend = QB == 2 ? 128 : cbeg + 64;
+      const int ri = rb * 128 + lrow;
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
+        uint32_t rr[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j0 = 2 * (c0 + i), j1 = j0 + 1;
+          // rows past Nq are never stored; the guard keeps their distances inside the table
+          const int e0 = ri > j0 ? ri - j0 : j0 - ri, e1 = ri > j1 ? ri - j1 : j1 - ri;
+          const float r0 = (j0 < p.Nk && e0 < p.lmax) ? (float)sm.rl[e0] : 0.0f;
+          const float r1 = (j1 < p.Nk && e1 < p.lmax) ? (float)sm.rl[e1] : 0.0f;
+          rr[i] = pack_bf16x2(r0, r1);
+        }
+        tmem_st32(tm_r + rb * 128 + lane_off + c0, rr);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.r_ready);
+    }
+
+    // key sums of unit g into the auxiliary tile; releases the K slot for reading
+    auto key_sums = [&](int g) -> bool {
       const int s = g & 1;
       const uint32_t ph = (uint32_t)((g >> 1) & 1);
       if (!mbar_wait(&sm.kv_full[s], ph, 91)) return false;
       if (XNOR) {
-        const uint8_t* kt = sm.k + s * kKVTile;
-#pragma unroll
-        for (int rr2 = 0; rr2 < 2; ++rr2) {
-          const int j = row + rr2 * 128;
-          const float ks = row_sum_sw128(kt, j, p.dh);
-          __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
-          *slot = __float2bfloat16_rn(ks);
-        }
+        const int j = grp * 128 + lrow;
+        const float ks = row_sum_sw128(sm.k + s * kKVTile, j, p.dh);
+        __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
+        *slot = __float2bfloat16_rn(ks);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -312,45 +349,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(sm.aux_ready);
         mbar_arrive(&sm.kv_empty[s]);
       }
-      if (!mbar_wait(&sm.q_full[s], ph, 92)) return false;
-      c_row = XNOR ? (float)p.dh - row_sum_sw128(sm.q + s * kQTile, row, p.dh) : 0.0f;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.q_empty[s]);
       return true;
     };
-    // R rows of query block qb -> TMEM (bf16 pairs: keys 2c and 2c+1 in column c)
-    auto build_r = [&](int qb) {
-      const int qi = qb * 128 + row;
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t rr[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j0 = 2 * (c0 + i), j1 = j0 + 1;
-          const float r0 = j0 < p.Nk ? (float)sm.rl[qi > j0 ? qi - j0 : j0 - qi] : 0.0f;
-          const float r1 = j1 < p.Nk ? (float)sm.rl[qi > j1 ? qi - j1 : j1 - qi] : 0.0f;
-          rr[i] = pack_bf16x2(r0, r1);
-        }
-        tmem_st32(tm_r + lane_off + c0, rr);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.r_ready);
-    };
 
-    float c_cur = 0.0f;
-    if (n_units > 0) {
-      const int qb0 = (int)blockIdx.x / BH;
-      if (XNOR) {
-        build_r(qb0);
-        prev_qb = qb0;
-      }
-      ok = prepare(0, c_cur);
-    }
+    if (n_units > 0) ok = key_sums(0);
     for (int g = 0; g < n_units && ok; ++g) {
       const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
-      const int bh = item % BH, b = bh / p.H, h = bh % p.H;
-      const int qi = (item / BH) * 128 + row;
+      const int b = item / p.H, h = item % p.H;
       const int par = g & 1;
       if (t == 0) {
 #pragma unroll
@@ -359,11 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- A: K^T V -> bf16 operand (x2 for XNOR); 1^T V, s^T V -> shared floats
       if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) { ok = false; break; }
       tc_fence_after();
-      if (q < 3) {
+      if (grp == 0 && quad < 3) {
         float d1[DP];
 #pragma unroll
         for (int c0 = 0; c0 < DP; c0 += 16) tmem_ld16(tm_d1 + lane_off + c0, d1 + c0);
-        if (q < 2) {
+        if (quad < 2) {
           const float f = XNOR ? 2.0f : 1.0f;
 #pragma unroll
           for (int c = 0; c < DP / 8; ++c) {
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
             w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
             w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
-            *reinterpret_cast<uint4*>(sm.mb + row * 128 + ((c ^ (row & 7)) << 4)) = w;
+            *reinterpret_cast<uint4*>(sm.mb + lrow * 128 + ((c ^ (lrow & 7)) << 4)) = w;
           }
         } else if (XNOR && lane < 2) {
           float* dst = (lane == 0 ? sm.cs : sm.kv) + par * 64;
@@ -384,64 +389,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       named_bar_sync(1, kEpi);
       if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
-      // ---- B: prepare the next unit so its MMA1 overlaps this unit's MMA2 and output
-      float c_next = 0.0f;
-      if (g + 1 < n_units && !prepare(g + 1, c_next)) { ok = false; break; }
-      // ---- C: O = D2 + c_i (1^T V) - s^T V, a = scale O, LIF over t, spikes
+      // ---- B: key sums of the next unit, so its MMA1 overlaps this unit's MMA2 and output
+      if (g + 1 < n_units && !key_sums(g + 1)) { ok = false; break; }
+      // ---- C: O = D2 + (dh - |q_i|) (1^T V) - s^T V, a = scale O, LIF over t, spikes
       if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
       tc_fence_after();
-      float o[DP];
+      const uint32_t ta = tm_d2 + qb * NO + lane_off;
+      float c_row = 0.0f;
+      if (XNOR) {
+        float e[16];
+        tmem_ld16(ta + DP, e);  // the ones column: |q_i|
+        c_row = (float)p.dh - e[0];
+      }
+      const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
+      float* aout = p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
+      const float* csp = sm.cs + par * 64;
+      const float* kvp = sm.kv + par * 64;
 #pragma unroll
-      for (int c0 = 0; c0 < DP; c0 += 16) tmem_ld16(tm_d2 + lane_off + c0, o + c0);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.o_empty);
-      if (qi < p.Nq) {
-        const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
-        float* aout = p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
-        const float* csp = sm.cs + par * 64;
-        const float* kvp = sm.kv + par * 64;
+      for (int c0 = 0; c0 < DP; c0 += 16) {
+        if (c0 + 16 <= dc0 || c0 >= dc0 + dcols) continue;
+        float o[16];
+        tmem_ld16(ta + c0, o);
+        if (qi >= p.Nq) continue;
 #pragma unroll
-        for (int d0 = 0; d0 < DP; d0 += 8) {
-          if (d0 < p.dh) {
-            float sp[8];
+        for (int d8 = 0; d8 < 16; d8 += 8) {
+          const int d0 = c0 + d8;
+          if (d0 < dc0 || d0 >= dc0 + dcols) continue;
+          float sp[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float ov = o[d0 + i];
-              if (XNOR) ov = (ov + c_cur * csp[d0 + i]) - kvp[d0 + i];
-              const float a = __fmul_rn(ov, scale);
-              if (aout) aout[d0 + i] = a;
-              const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
-              const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
-              const bool fire = u > vth;
-              sp[i] = fire ? 1.0f : 0.0f;
-              mem[d0 + i] = fire ? vr : u;
-            }
-            if (p.out_bf16) {
-              uint4 w;
-              w.x = pack_bf16x2(sp[0], sp[1]);
-              w.y = pack_bf16x2(sp[2], sp[3]);
-              w.z = pack_bf16x2(sp[4], sp[5]);
-              w.w = pack_bf16x2(sp[6], sp[7]);
-              *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
-            }
-            if (p.out_f32) {
-              *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
-              *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
-            }
+          for (int i = 0; i < 8; ++i) {
+            float ov = o[d8 + i];
+            if (XNOR) ov = (ov + c_row * csp[d0 + i]) - kvp[d0 + i];
+            const float a = __fmul_rn(ov, scale);
+            if (aout) aout[d0 + i] = a;
+            const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
+            const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
+            const bool fire = u > vth;
+            sp[i] = fire ? 1.0f : 0.0f;
+            mem[d0 + i] = fire ? vr : u;
+          }
+          if (p.out_bf16) {
+            uint4 w;
+            w.x = pack_bf16x2(sp[0], sp[1]);
+            w.y = pack_bf16x2(sp[2], sp[3]);
+            w.z = pack_bf16x2(sp[4], sp[5]);
+            w.w = pack_bf16x2(sp[6], sp[7]);
+            *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
+          }
+          if (p.out_f32) {
+            *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
+            *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
           }
         }
       }
-      c_cur = c_next;
-      // ---- new query block for the next unit: rebuild R (MMA2 of this unit has completed)
-      if (XNOR && g + 1 < n_units) {
-        const int nitem = (int)blockIdx.x + ((g + 1) / p.T) * (int)gridDim.x;
-        const int nqb = nitem / BH;
-        if (nqb != prev_qb) {
-          build_r(nqb);
-          prev_qb = nqb;
-        }
-      }
+      // all of D2 is in registers (each load waited): hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sm.o_empty);
     }
     (void)ok;
   }
@@ -450,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -465,7 +469,7 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
                    const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
                    float* attn_out, cudaStream_t st) {
   using namespace ssal;
-  if (Nk > 256 || dh > 64 || dh % 8 != 0) return SPK_ERR_UNSUPPORTED;
+  if (Nq > 256 || Nk > 256 || dh > 64 || dh % 8 != 0) return SPK_ERR_UNSUPPORTED;
   Params p = {};
   p.T = T;
   p.B = B;
@@ -481,9 +485,10 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   p.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
   p.out_f32 = out_f32;
   p.attn_out = attn_out;
-  p.q_blocks = (Nq + 127) / 128;
+  p.QB = (Nq + 127) / 128;
+  p.dsplit = ((dh / 8 + 1) / 2) * 8;
   p.lmax = Nq > Nk ? Nq : Nk;
-  const long long items = (long long)p.q_blocks * B * H;
+  const long long items = (long long)B * H;
   if (items >= (1ll << 31)) return fail(SPK_ERR_SHAPE, "too many attention work items");
   p.items = (int)items;
   const int dp = (dh + 15) / 16 * 16;

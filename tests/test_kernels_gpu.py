@@ -261,6 +261,8 @@ def spikes_qkv(seed, TB, Nq, Nk, D, p=0.15):
     (4, 2, 8, 256, 256, 48, None),     # encoder shape (two key blocks)
     (4, 2, 8, 64, 64, 48, "causal"),   # decoder self-attention
     (4, 2, 8, 64, 256, 48, None),      # decoder cross-attention
+    (2, 3, 2, 200, 130, 64, None),     # two query blocks, the second partial; head width 64
+    (1, 2, 3, 300, 40, 16, None),      # more than two query blocks (dense kernel)
     (2, 2, 2, 130, 70, 64, "dense"),
     (1, 1, 1, 200, 300, 16, "dense"),
     # short sequences (two (batch, head) pairs per tile): odd pair count,
