@@ -51,7 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--workload", default="forward", choices=["forward", "train"],
+                    help="forward: the OCR seq2seq forward (default); train: one DDP training step per step")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (forward 256, train 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -225,12 +227,101 @@ def run_reference(args, ws, rank):
     }), flush=True)
 
 
+def run_train(args, ws, rank, local):
+    """--workload train: forward + backward + AdamW step of the same model, one
+    process per GPU, gradients all-reduced by DDP over NCCL (bf16 autocast as
+    the reference trains under fp16 autocast, train_spikeformer.py:545-555;
+    loss = mean over T of the cross-entropy of each step's logits,
+    train_spikeformer.py:309-323; arctan surrogate, alpha = 2)."""
+    import datetime
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from spikingtransformer_b200 import _lib
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _lib.load()
+    torch.manual_seed(0)  # same initial weights on every rank
+    model = Seq2Seq(**ARCH)
+    round_weights_bf16(model)
+    model.set_surrogate("arctan", 2.0)
+    model = model.to(dev).train()
+    net = model
+    if ws > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
+                                                        gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    B = args.batch or 64
+    sets = []
+    for i in range(2):
+        src, _, _ = make_inputs(B, shard_seed(rank, i))
+        labels = torch.randint(0, ARCH["tgt_vocab_size"], (B, SEQ + 1),
+                               generator=torch.Generator().manual_seed(shard_seed(rank, i) + 11))
+        sets.append((src.to(dev), labels.to(dev)))
+    mask = torch.tril(torch.ones(SEQ, SEQ, device=dev)).expand(B, 1, SEQ, SEQ)
+
+    def step(i):
+        src, labels = sets[i % len(sets)]
+        tgt_in, tgt_out = labels[:, :-1], labels[:, 1:]
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, _ = net(src, tgt_in, look_ahead_mask=mask)
+            loss = sum(F.cross_entropy(logits[t].reshape(-1, logits.shape[-1]).float(), tgt_out.reshape(-1))
+                       for t in range(logits.shape[0])) / logits.shape[0]
+        loss.backward()
+        opt.step()
+        return loss
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+        e0.record()
+        for i in range(args.steps):
+            loss = step(i)
+        e1.record()
+        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1), dev)
+    last = float(loss.item())
+    kernels = rec.summary()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "ocr_seq2seq_train_images_per_sec", "value": ws * B * args.steps / (ms / 1000.0),
+            "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "ocr_seq2seq_train_step", "global_batch": ws * B, "per_gpu_batch": B,
+                       "seq_len": SEQ, "image": list(IMG), "T": 4, "layers": "8 enc + 4 dec",
+                       "optimizer": "AdamW lr 1e-4", "surrogate": "arctan alpha 2",
+                       "parallelism": "ddp%d (NCCL all-reduce of gradients)" % ws},
+            "loss": last, "clocks": clk.summary(),
+            "gpu_launches": sum(v["launches"] for v in kernels.values()),
+            "kernels": {k: {"launches": v["launches"], "ms_per_step": v["ms"] / args.steps}
+                        for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])},
+        }), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)
         return
+    if args.workload == "train":
+        run_train(args, ws, rank, local)
+        return
+    if args.batch is None:
+        args.batch = 256
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:

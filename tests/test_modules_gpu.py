@@ -199,6 +199,35 @@ def test_seq2seq_training_path_runs(pkg):
     assert not [n for n in missing if "image_encoder" not in n], missing
 
 
+def test_seq2seq_train_steps_bf16_autocast(pkg):
+    """Three optimizer steps as the training workload runs them (bf16
+    autocast, mean over T of the per-step cross-entropy, AdamW): finite losses
+    and every trained weight updated."""
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    ours.train()
+    ours.set_surrogate("arctan", 2.0)
+    opt = torch.optim.AdamW(ours.parameters(), lr=1e-3)
+    B, N = 2, 16
+    src = synthetic_lines(B, 5).to(DEV)
+    tgt = torch.randint(0, 256, (B, N + 1), device=DEV, generator=torch.Generator(device=DEV).manual_seed(5))
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(B, 1, N, N)
+    before = {n: p.detach().clone() for n, p in ours.named_parameters()}
+    losses = []
+    for _ in range(3):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, _ = ours(src, tgt[:, :-1], look_ahead_mask=mask)
+            loss = sum(torch.nn.functional.cross_entropy(logits[t].reshape(-1, 256).float(), tgt[:, 1:].reshape(-1))
+                       for t in range(logits.shape[0])) / logits.shape[0]
+        loss.backward()
+        assert all(torch.isfinite(p.grad).all() for p in ours.parameters() if p.grad is not None)
+        opt.step()
+        losses.append(loss.item())
+    assert all(math.isfinite(x) for x in losses)
+    changed = [n for n, p in ours.named_parameters() if not torch.equal(p.detach(), before[n])]
+    assert any("out_proj" in n for n in changed) and any("output_layer" in n for n in changed)
+
+
 def test_greedy_decode(pkg):
     ours, _ = _bench_models(enc_layers=1, dec_layers=1)
     src = synthetic_lines(1, 4)[0]
