@@ -487,15 +487,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        // y' = (x - mean) rstd (gain gamma) + gain beta; x already holds the bias
+        // (x - mean) rstd before the transposition (per-row statistics; x already holds the
+        // bias), gain gamma and gain beta after it (per-column parameters, so each lane loads
+        // only its own CPL columns once for all T steps)
+        (void)col;
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const float4 g4 = *reinterpret_cast<const float4*>(sm.gamma + col + i);
-          const float4 e4 = *reinterpret_cast<const float4*>(sm.beta + col + i);
           float2 x0 = make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
           float2 x1 = make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-          x0 = fma2(fma2(x0, rstd2, nmr2), make_float2(g4.x, g4.y), make_float2(e4.x, e4.y));
-          x1 = fma2(fma2(x1, rstd2, nmr2), make_float2(g4.z, g4.w), make_float2(e4.z, e4.w));
+          x0 = fma2(x0, rstd2, nmr2);
+          x1 = fma2(x1, rstd2, nmr2);
           *reinterpret_cast<float4*>(xs_wr + i) = make_float4(x0.x, x0.y, x1.x, x1.y);
         }
         __syncwarp();
@@ -523,6 +524,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (!tok_ok) return;
+        float2 gg[NP], ee[NP];
+        {
+          const int lc = col + jblk * CPL;  // this lane's first column after the transposition
+          float gv[CPL], ev[CPL];
+#pragma unroll
+          for (int u = 0; u < CPL; u += (CPL >= 4 ? 4 : CPL)) {
+            if constexpr (CPL >= 4) {
+              const float4 g4 = *reinterpret_cast<const float4*>(sm.gamma + lc + u);
+              const float4 e4 = *reinterpret_cast<const float4*>(sm.beta + lc + u);
+              gv[u] = g4.x; gv[u + 1] = g4.y; gv[u + 2] = g4.z; gv[u + 3] = g4.w;
+              ev[u] = e4.x; ev[u + 1] = e4.y; ev[u + 2] = e4.z; ev[u + 3] = e4.w;
+            } else if constexpr (CPL == 2) {
+              const float2 g2 = *reinterpret_cast<const float2*>(sm.gamma + lc + u);
+              const float2 e2 = *reinterpret_cast<const float2*>(sm.beta + lc + u);
+              gv[u] = g2.x; gv[u + 1] = g2.y;
+              ev[u] = e2.x; ev[u + 1] = e2.y;
+            } else {
+              gv[u] = sm.gamma[lc + u];
+              ev[u] = sm.beta[lc + u];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < NP; ++u) {
+            gg[u] = CPL >= 2 ? make_float2(gv[2 * u], gv[(2 * u + 1) % CPL]) : make_float2(gv[0], 0.0f);
+            ee[u] = CPL >= 2 ? make_float2(ev[2 * u], ev[(2 * u + 1) % CPL]) : make_float2(ev[0], 0.0f);
+          }
+        }
         __nv_bfloat16* sp_ptr = p.spk_bf16 ? p.spk_bf16 + off0 : nullptr;
         float2 u2[NP], s2[NP];
 #pragma unroll
@@ -531,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int u = 0; u < NP; ++u) {
             float2 y2 = CPL >= 2 ? make_float2(yt[t][2 * u], yt[t][(2 * u + 1) % CPL]) : make_float2(yt[t][0], 0.0f);
+            y2 = fma2(y2, gg[u], ee[u]);
             if (t == 0) {
               u2[u] = y2;  // membrane starts at 0
             } else {
