@@ -25,9 +25,9 @@
 //  * TMEM loads are 32 columns wide and double-buffered.
 //  * Compile-time variants: FAST (bf16 spikes and/or residual add only, the
 //    residual add specialised) and a general variant for fp32 spikes and the
-//    LayerNorm debug output.  The fast variant pre-loads each accumulator with
-//    the bias (tcgen05.st by the epilogue before handing it back), folds the
-//    LIF input gain into gamma/beta, and runs the LIF branch-free as
+//    LayerNorm debug output.  The fast variant starts each tile's accumulator
+//    with a K = 16 MMA of a ones tile and the bias split into two bf16 terms,
+//    folds the LIF input gain into gamma/beta, and runs the LIF branch-free as
 //    u = beta (1 - s) u + y + s beta v_reset with s from set.gt.
 #include "common.cuh"
 
@@ -60,6 +60,7 @@ struct Params {
 
 struct Smem {
   uint8_t *a, *w;
+  uint8_t *ones, *bsplit;  // fast variant: bias MMA operands (no-swizzle K-major, K = 16)
   float* xs;       // 8 warps x 32 rows x kXS floats (padded rows)
   float *bias, *gamma, *beta;
   float2* stat;    // 2 parities x 2 halves x 128 rows (mean, M2)
@@ -81,6 +82,7 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   };
   size_t oa = take((size_t)p.stages * kAStage, 1024);
   size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
+  size_t oon = take(128 * 32, 128), obs = take((size_t)p.n_cta * 32, 128);
   size_t oxs = take(kEpiWarps * 32 * kXS * 4, 16);
   size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
   size_t ost = take(2 * 2 * 128 * 8, 16);
@@ -91,6 +93,8 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   if (s) {
     s->a = base + oa;
     s->w = base + ow;
+    s->ones = base + oon;
+    s->bsplit = base + obs;
     s->xs = reinterpret_cast<float*>(base + oxs);
     s->bias = reinterpret_cast<float*>(base + ob);
     s->gamma = reinterpret_cast<float*>(base + og);
@@ -168,6 +172,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(sm.tmem_base, p.tmem_cols);
     tmem_relinquish();
   }
+  if (FAST) {
+    // bias as one K = 16 MMA per tile: ones[128 x 16] (columns 0 and 1 = 1) times
+    // bsplit[n_cta x 16] (columns 0 and 1 = the bias split into two bf16 terms), both in the
+    // no-swizzle K-major layout: 8 x 8 core matrices of 128 bytes, (row, k) at
+    // (row / 8) * 256 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2
+    const int n0 = (int)rank * p.n_cta;
+    for (int i = threadIdx.x; i < 128 * 2; i += kThreads) {
+      const int r = i >> 1, k8 = i & 1;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (k8 == 0) w.x = 0x3F803F80u;  // 1.0, 1.0
+      *reinterpret_cast<uint4*>(sm.ones + (r >> 3) * 256 + k8 * 128 + (r & 7) * 16) = w;
+    }
+    for (int i = threadIdx.x; i < p.n_cta * 2; i += kThreads) {
+      const int r = i >> 1, k8 = i & 1;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (k8 == 0 && p.bias) {
+        const float b = p.bias[n0 + r];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(b);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(b - __bfloat162float(hi));
+        w.x = (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
+      }
+      *reinterpret_cast<uint4*>(sm.bsplit + (r >> 3) * 256 + k8 * 128 + (r & 7) * 16) = w;
+    }
+    fence_proxy_async_smem();
+  }
   {
     // the fast variant folds the LIF input gain into the affine LayerNorm parameters
     const int n0 = (int)rank * p.n_cta;
@@ -224,11 +253,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int iter = 0;
     for (int tile = cid; tile < p.num_m_tiles && ok; tile += ncl, ++iter) {
       const int buf = iter & 1;
-      // fast variant: the epilogue hands each accumulator over pre-loaded with the bias
-      // (one arrival per use, the first before the first tile)
-      if (!mbar_wait(&sm.acc_empty[buf], ((uint32_t)(iter >> 1) & 1u) ^ (FAST ? 0u : 1u), 121)) { ok = false; break; }
+      if (!mbar_wait(&sm.acc_empty[buf], ((uint32_t)(iter >> 1) & 1u) ^ 1u, 121)) { ok = false; break; }
       tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t)(buf * p.n_cta);
+      if (FAST && lane == 0)  // accumulator := bias (hi + lo), the K loop accumulates onto it
+        umma_bf16(dcol, umma_desc(smem_u32(sm.ones), 128, 256, 0), umma_desc(smem_u32(sm.bsplit), 128, 256, 0),
+                  idesc_bf16_f32(128, p.n_cta, 0, 0), 0u);
       for (int kc = 0; kc < nk; ++kc) {
         if (!mbar_wait(&sm.full[stage], phase, 122)) { ok = false; break; }
         tc_fence_after();
@@ -279,31 +309,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 nbeta2 = make_float2(-beta, -beta);
     const float bvr = __fmul_rn(beta, vr);
     const float2 bvr2 = make_float2(bvr, bvr);
-    // fast variant: this thread's lane and columns of an accumulator := bias, so the MMAs add it
-    auto write_bias = [&](uint32_t tcol) {
-      for (int c = 0; c < 2 * nch; ++c) {
-        uint32_t r[16];
-        const float* bsrc = sm.bias + cb + c * 16;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 b4 = *reinterpret_cast<const float4*>(bsrc + i);
-          r[i] = __float_as_uint(b4.x);
-          r[i + 1] = __float_as_uint(b4.y);
-          r[i + 2] = __float_as_uint(b4.z);
-          r[i + 3] = __float_as_uint(b4.w);
-        }
-        tmem_st16(tcol + c * 16, r);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-    };
-    if constexpr (FAST) {
-      for (int b = 0; b < 2; ++b) {
-        write_bias(tmem + lane_off + (uint32_t)(b * p.n_cta + cb));
-        if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
-      }
-    }
     int iter = 0;
     for (int tile = cid; tile < p.num_m_tiles; tile += ncl, ++iter) {
       const int buf = iter & 1;
@@ -728,12 +733,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if ((c & 1) == 0) {
             tmem_wait_ld_fence(ra);
             if (c + 1 < 2 * nch) tmem_ld16_raw(trow + (c + 1) * 16, rb);
-            norm_sub_fast(ra, c);
           } else {
             tmem_wait_ld_fence(rb);
             if (c + 1 < 2 * nch) tmem_ld16_raw(trow + (c + 1) * 16, ra);
-            norm_sub_fast(rb, c);
           }
+          if (c + 1 == 2 * nch) {
+            // last TMEM read of this buffer: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+          }
+          if ((c & 1) == 0)
+            norm_sub_fast(ra, c);
+          else
+            norm_sub_fast(rb, c);
         }
       } else {
         uint32_t ra[32], rb[32];
@@ -761,11 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if constexpr (FAST) {
-        // hand the buffer back to the MMA warp pre-loaded with the bias for its next tile
-        write_bias(trow);
-        if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
-      }
+
     }
   }
 
