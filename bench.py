@@ -159,6 +159,18 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture of
+# the same launch shape; profiles/dram_traffic_b256_shapes.md) of the kernels that can be
+# the dominant one of the 256-image forward
+NCU_TRAFFIC = {
+    "linear_ln_lif K=384 N=384 rows=262144": 354.0e6,
+    "linear_ln_lif K=384 N=384 rows=262144 +residual": 553.6e6,
+    "linear_ln_lif K=384 N=1536 rows=262144": 950.7e6,
+    "linear_ln_lif K=1536 N=384 rows=262144 +residual": 1185.5e6,
+    "ssa Nq=256 Nk=256": 779.1e6,
+}
+
+
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -417,7 +429,9 @@ def main():
         peak = peaks.get("hbm_gbs")
         roof = {"bound": "hbm", "unit": "GB/s", "peak_kind": "HBM copy (%s)" % peak_src}
     roof.update({"kernel": dom_tag, "achieved": achieved, "peak": peak, "frac": achieved / peak,
-                 "traffic": None, "ms_per_launch": per_launch_ms})
+                 "traffic": NCU_TRAFFIC.get(dom_tag) if B == 256 else None,
+                 "traffic_unit": "bytes per launch (ncu dram read + write)",
+                 "algorithmic_bytes": dom["bytes"] / dom["launches"], "ms_per_launch": per_launch_ms})
 
     if rank == 0:
         value = ws * B * args.steps / (ms / 1000.0)

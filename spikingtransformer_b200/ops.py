@@ -108,8 +108,11 @@ def linear_ln_lif(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_
     _lib.call("spk_linear_ln_lif_fwd", _lib.ptr(A), _lib.ptr(W), _lib.ptr(bias), _lib.ptr(ln_gamma),
               _lib.ptr(ln_beta), float(ln_eps), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, K, N,
               1 if t_broadcast else 0, _lib.ptr(spikes), _lib.DTYPE_CODE[spike_dtype], _lib.ptr(residual),
-              _lib.ptr(ln_out), _lib.stream_ptr(dev), tag="linear_ln_lif K=%d N=%d" % (K, N),
-              work=dict(flops=2.0 * rows * K * N))
+              _lib.ptr(ln_out), _lib.stream_ptr(dev),
+              tag="linear_ln_lif K=%d N=%d rows=%d%s" % (K, N, rows, " +residual" if residual is not None else ""),
+              work=dict(flops=2.0 * rows * K * N,
+                        bytes=(rows * K + N * K) * 2 + out_rows * N * (spikes.element_size() if want_spikes else 0)
+                        + (4 * out_rows * N if residual is not None else 0)))
     return spikes, ln_out
 
 
