@@ -391,54 +391,81 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
       // ---- B: key sums of the next unit, so its MMA1 overlaps this unit's MMA2 and output
       if (g + 1 < n_units && !key_sums(g + 1)) { ok = false; break; }
-      // ---- C: O = D2 + (dh - |q_i|) (1^T V) - s^T V, a = scale O, LIF over t, spikes
+      // ---- C: O = D2 + (dh - |q_i|) (1^T V) - s^T V, a = scale O, LIF over t, spikes.
+      // Packed fp32x2 arithmetic; every product and sum rounds as the scalar reference
+      // (the integer terms are exact in any order).  TMEM columns are read 16 at a time,
+      // the next chunk in flight while the current one is processed.
       if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
       tc_fence_after();
       const uint32_t ta = tm_d2 + qb * NO + lane_off;
-      float c_row = 0.0f;
-      if (XNOR) {
-        float e[16];
-        tmem_ld16(ta + DP, e);  // the ones column: |q_i|
-        c_row = (float)p.dh - e[0];
-      }
       const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
       float* aout = p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
       const float* csp = sm.cs + par * 64;
       const float* kvp = sm.kv + par * 64;
+      const bool row_ok = qi < p.Nq;
+      constexpr int NCH = DP / 16;
+      // chunk c (16 columns) is read into rbuf[c & 1]: issued one chunk ahead, or on the spot
+      // for the first chunk of this thread's columns
+      uint32_t rbuf[2][16];
+      uint32_t rq[16];
+      auto in_range = [&](int c) { return !(c * 16 + 16 <= dc0 || c * 16 >= dc0 + dcols); };
+      if (XNOR) {
+        tmem_ld16_raw(ta + DP, rq);  // the ones column: |q_i|
+        tmem_wait_ld_fence(rq);
+      }
+      const float c_row = XNOR ? (float)p.dh - __uint_as_float(rq[0]) : 0.0f;
+      const float2 c2 = make_float2(c_row, c_row), scale2 = make_float2(scale, scale);
+      const float2 gain2 = make_float2(p.gain, p.gain), beta2 = make_float2(beta, beta);
 #pragma unroll
-      for (int c0 = 0; c0 < DP; c0 += 16) {
-        if (c0 + 16 <= dc0 || c0 >= dc0 + dcols) continue;
-        float o[16];
-        tmem_ld16(ta + c0, o);
-        if (qi >= p.Nq) continue;
+      for (int c = 0; c < NCH; ++c) {
+        const int c0 = c * 16;
+        if (!in_range(c)) continue;
+        // (head width 64: no read-ahead, the registers go to the LIF state)
+        constexpr bool AHEAD = DP <= 48;
+        const int cur = AHEAD ? (c & 1) : 0;
+        if (!AHEAD || c == 0 || !in_range(c - 1)) tmem_ld16_raw(ta + c0, rbuf[cur]);
+        tmem_wait_ld_fence(rbuf[cur]);
+        if (AHEAD && c + 1 < NCH && in_range(c + 1)) tmem_ld16_raw(ta + c0 + 16, rbuf[cur ^ 1]);
+        if (row_ok) {
 #pragma unroll
-        for (int d8 = 0; d8 < 16; d8 += 8) {
-          const int d0 = c0 + d8;
-          if (d0 < dc0 || d0 >= dc0 + dcols) continue;
-          float sp[8];
+          for (int d8 = 0; d8 < 16; d8 += 8) {
+            const int d0 = c0 + d8;
+            if (d0 < dc0 || d0 >= dc0 + dcols) continue;
+            uint32_t bits[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float ov = o[d8 + i];
-            if (XNOR) ov = (ov + c_row * csp[d0 + i]) - kvp[d0 + i];
-            const float a = __fmul_rn(ov, scale);
-            if (aout) aout[d0 + i] = a;
-            const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
-            const float u = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
-            const bool fire = u > vth;
-            sp[i] = fire ? 1.0f : 0.0f;
-            mem[d0 + i] = fire ? vr : u;
-          }
-          if (p.out_bf16) {
-            uint4 w;
-            w.x = pack_bf16x2(sp[0], sp[1]);
-            w.y = pack_bf16x2(sp[2], sp[3]);
-            w.z = pack_bf16x2(sp[4], sp[5]);
-            w.w = pack_bf16x2(sp[6], sp[7]);
-            *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
-          }
-          if (p.out_f32) {
-            *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
-            *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
+            for (int i = 0; i < 8; i += 4) {
+              const float4 cs4 = *reinterpret_cast<const float4*>(csp + d0 + i);
+              const float4 kv4 = *reinterpret_cast<const float4*>(kvp + d0 + i);
+#pragma unroll
+              for (int j = 0; j < 4; j += 2) {
+                const uint32_t* r = rbuf[cur] + d8 + i + j;
+                float2 ov = make_float2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+                if (XNOR) {
+                  const float2 cs2 = j == 0 ? make_float2(cs4.x, cs4.y) : make_float2(cs4.z, cs4.w);
+                  const float2 kv2 = j == 0 ? make_float2(kv4.x, kv4.y) : make_float2(kv4.z, kv4.w);
+                  ov = add2(fma2(c2, cs2, ov), make_float2(-kv2.x, -kv2.y));
+                }
+                const float2 a = mul2(ov, scale2);
+                const int dd = d0 + i + j;
+                if (aout) *reinterpret_cast<float2*>(aout + dd) = a;
+                const float2 cu = mul2(a, gain2);  // exact when the gain is 1
+                const float2 u = add2(mul2(make_float2(mem[dd], mem[dd + 1]), beta2), cu);
+                const bool f0 = u.x > vth, f1 = u.y > vth;
+                mem[dd] = f0 ? vr : u.x;
+                mem[dd + 1] = f1 ? vr : u.y;
+                bits[(i + j) >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
+              }
+            }
+            if (p.out_bf16) *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+            if (p.out_f32) {
+              float4 lo, hi;
+              lo.x = (bits[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bits[0] >> 16) ? 1.0f : 0.0f;
+              lo.z = (bits[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bits[1] >> 16) ? 1.0f : 0.0f;
+              hi.x = (bits[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bits[2] >> 16) ? 1.0f : 0.0f;
+              hi.z = (bits[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bits[3] >> 16) ? 1.0f : 0.0f;
+              *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = lo;
+              *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = hi;
+            }
           }
         }
       }
