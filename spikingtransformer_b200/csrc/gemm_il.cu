@@ -47,6 +47,7 @@ struct Params {
   int T, tpt;
   int64_t R;
   int K, N, n_cta, cs, num_m_tiles, stages, wbox;
+  int res_prefetch;  // the residual rows may be bulk-prefetched (16-byte aligned blocks)
   uint32_t tmem_cols;
   const float *bias, *gamma, *beta_ln;
   float eps;
@@ -225,6 +226,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       uint32_t outstanding = 0, issued_phase = 0;  // bit i: stage i loaded / its phase
       for (int tile = cid; tile < p.num_m_tiles && ok; tile += ncl) {
+        if (RES && p.res_prefetch && rank == 0) {
+          // the epilogue reads this tile's residual rows about one tile from now: pull them
+          // into L2 (one contiguous block of tokens x N per step)
+          const int64_t tok0 = (int64_t)tile * p.tpt;
+          const int64_t ntok = (p.R - tok0) < p.tpt ? (p.R - tok0) : p.tpt;
+          const uint32_t bytes_t = (uint32_t)(ntok * p.N * 2);
+          for (int t = 0; t < T; ++t) {
+            const __nv_bfloat16* src = p.residual + ((int64_t)t * p.R + tok0) * p.N;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes_t) : "memory");
+          }
+        }
         for (int kc = 0; kc < nk; ++kc) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1u, 111)) { ok = false; break; }
           outstanding &= ~(1u << stage);
@@ -845,6 +857,7 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   p.spk_f32 = spk_f32;
   p.residual = reinterpret_cast<__nv_bfloat16*>(residual);
   p.ln_out = ln_out;
+  p.res_prefetch = residual != nullptr && aligned(residual, 16) && N % 8 == 0;
 
   CUtensorMap tmA, tmW;
   int rc;
