@@ -14,7 +14,7 @@ import torch
 from torch import nn
 
 from . import ops
-from ._fused import bf16_weight, fast_path_ok, lif_params
+from ._fused import bf16_weight, fast_path_ok, lif_params, ln_lif
 from .Lif import LIF
 
 
@@ -138,5 +138,5 @@ class PatchEmbed(nn.Module):
             s = self._fused(x, t_broadcast=False).float()
             return s, {"output": s}
         y = self.proj(x).flatten(2).transpose(1, 2)
-        s = self.lif(self.norm(y))[0]
+        s = ln_lif(y, self.norm, self.lif)
         return s, {"output": s}

@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from ._fused import fast_path_ok, lif_params, lin_ln_lif
+from ._fused import fast_path_ok, lif_params, lin_ln_lif, ln_lif
 from .Lif import LIF
 
 
@@ -104,12 +104,12 @@ class _SSACore(nn.Module):
     def _reference_forward(self, query, key, value, attention_mask):
         TB, N, D = query.shape
         Nk = key.shape[1]
-        q = self._heads(self.lifq(self.lnq(self.q_proj(query)))[0], N)
-        k = self._heads(self.lifk(self.lnk(self.k_proj(key)))[0], Nk)
-        v = self._heads(self.lifv(self.lnv(self.v_proj(value)))[0], Nk)
+        q = self._heads(ln_lif(self.q_proj(query), self.lnq, self.lifq), N)
+        k = self._heads(ln_lif(self.k_proj(key), self.lnk, self.lifk), Nk)
+        v = self._heads(ln_lif(self.v_proj(value), self.lnv, self.lifv), Nk)
         a = self._combine(q, k, v, attention_mask)
         s = self.lifs(a)[0].transpose(1, 2).contiguous().view(TB, N, D)
-        return self.lifo(self.lno(self.out_proj(s)))[0]
+        return ln_lif(self.out_proj(s), self.lno, self.lifo)
 
     def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:

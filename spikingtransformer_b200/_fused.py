@@ -84,3 +84,42 @@ def fast_path_ok(*tensors, module=None):
         if module is not None and any(p.requires_grad for p in module.parameters()):
             return False
     return True
+
+
+class LNLIFFunction(torch.autograd.Function):
+    """``lif(ln(pre))`` for training in two kernels (``ops.ln_lif_fwd`` / ``ops.ln_lif_bwd``):
+    the LayerNorm, the LIF scan and both backwards fused over the T steps of
+    each token; the Linear before it stays a library GEMM.  Gradients: pre,
+    the LayerNorm weight and bias, and the LIF beta."""
+
+    @staticmethod
+    def forward(ctx, pre, ln_weight, ln_bias, lif_beta, v_th, v_reset, eps, k, surrogate, in_gain, T):
+        spikes, stats = ops.ln_lif_fwd(pre, ln_weight, ln_bias, eps, lif_beta, v_th, v_reset, T, in_gain)
+        ctx.save_for_backward(pre, stats, ln_weight, ln_bias, lif_beta, v_th, v_reset)
+        ctx.k, ctx.surrogate, ctx.in_gain, ctx.T = float(k), surrogate, float(in_gain), int(T)
+        return spikes
+
+    @staticmethod
+    def backward(ctx, g_spikes):
+        pre, stats, w, b, lb, vth, vr = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        g_pre, gw, gb, glb = ops.ln_lif_bwd(g_spikes, pre, stats, w, b, lb, vth, vr, ctx.T, ctx.in_gain,
+                                            ctx.surrogate, ctx.k, need_gamma=need[1], need_beta=need[2],
+                                            need_lif_beta=need[3])
+        gw = gw.to(w.dtype) if gw is not None else None
+        gb = gb.to(b.dtype) if gb is not None else None
+        glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
+        return g_pre, gw, gb, glb, None, None, None, None, None, None, None
+
+
+def ln_lif(x, ln, lif):
+    """``lif(ln(x))[0]`` on the autograd path: the fused training kernels when the
+    shapes allow (CUDA, affine LayerNorm over the last dimension), the module
+    composition otherwise (``Lif.py:288-441`` over torch's LayerNorm)."""
+    T = lif.n_steps
+    D = x.shape[-1]
+    if (x.is_cuda and isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine
+            and tuple(ln.normalized_shape) == (D,) and x.shape[0] % T == 0 and ops.ln_lif_ok(T, D)):
+        return LNLIFFunction.apply(x, ln.weight, ln.bias, lif.effective_beta(), lif.v_th, lif.v_reset, ln.eps,
+                                   lif._k_host, lif.surrogate, lif.in_gain, T)
+    return lif(ln(x))[0]

@@ -116,6 +116,65 @@ def linear_ln_lif(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_
     return spikes, ln_out
 
 
+def ln_lif_ok(T, D):
+    """Shapes the fused LayerNorm -> LIF training kernels take."""
+    return 1 <= T <= 4 and D % 32 == 0 and 32 <= D <= 2048 and (D <= 512 or D % 128 == 0)
+
+
+def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
+               spike_dtype=torch.float32):
+    """``LIF(LayerNorm(pre))`` over the t-major fold; ``pre`` ``[T*R, ..., D]``.
+    Returns ``(spikes like pre in spike_dtype, stats fp32 [T*R', 2] (mean, rstd))``."""
+    _cuda(pre)
+    pre = pre.contiguous()
+    D = pre.shape[-1]
+    rows = pre.numel() // D
+    if rows % T:
+        raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
+    R = rows // T
+    dev = pre.device
+    spikes = torch.empty(pre.shape, dtype=spike_dtype, device=dev)
+    stats = torch.empty((rows, 2), dtype=torch.float32, device=dev)
+    g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
+    bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_ln_lif_fwd", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(g), _lib.ptr(bt), float(ln_eps),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, _lib.ptr(spikes),
+              _lib.DTYPE_CODE[spike_dtype], _lib.ptr(stats), _lib.stream_ptr(dev), tag="ln_lif_fwd D=%d" % D,
+              work=dict(bytes=rows * D * (pre.element_size() + spikes.element_size()) + rows * 8))
+    return spikes, stats
+
+
+def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
+               surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True):
+    """Backward of ``ln_lif_fwd``: ``(g_pre like pre, g_gamma [D] or None, g_beta [D] or None,
+    g_lif_beta [1] or None)``."""
+    _cuda(g_spikes, pre, stats)
+    pre = pre.contiguous()
+    g_spikes = g_spikes.contiguous()
+    if g_spikes.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        g_spikes = g_spikes.float()
+    D = pre.shape[-1]
+    rows = pre.numel() // D
+    R = rows // T
+    dev = pre.device
+    g_pre = torch.empty_like(pre)
+    gg = torch.empty(D, dtype=torch.float32, device=dev) if need_gamma else None
+    gb = torch.empty(D, dtype=torch.float32, device=dev) if need_beta else None
+    glb = torch.empty(1, dtype=torch.float32, device=dev) if need_lif_beta else None
+    wsb = int(_lib.load().spk_ln_lif_bwd_workspace_bytes(T, R, D))
+    ws = torch.empty(wsb // 4, dtype=torch.float32, device=dev)
+    g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
+    bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_ln_lif_bwd", _lib.ptr(g_spikes), _lib.dtype_code(g_spikes), _lib.ptr(pre), _lib.dtype_code(pre),
+              _lib.ptr(stats), _lib.ptr(g), _lib.ptr(bt), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain),
+              _lib.SURROGATE[surrogate], float(k), T, R, D, _lib.ptr(g_pre), _lib.ptr(gg), _lib.ptr(gb),
+              _lib.ptr(glb), _lib.ptr(ws), wsb, _lib.stream_ptr(dev), tag="ln_lif_bwd D=%d" % D,
+              work=dict(bytes=rows * D * (g_spikes.element_size() + 2 * pre.element_size()) + rows * 8))
+    return g_pre, gg, gb, glb
+
+
 def linear(A, W, bias=None):
     """``A @ W.T + bias`` in fp32 from bf16 ``A [M, K]`` and ``W [N, K]``."""
     _cuda(A, W)

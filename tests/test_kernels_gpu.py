@@ -321,3 +321,61 @@ def test_embed_pe_lif(ops):
 
 def test_no_device_timeouts(ops):
     ops.device_error_check()
+
+
+# ------------------------------------------------------------------ LayerNorm -> LIF (training)
+
+
+@pytest.mark.parametrize("T,R,D,pre_dtype,surrogate,gain", [
+    (4, 64, 384, torch.float32, "superspike", 1.0),
+    (4, 48, 384, torch.bfloat16, "arctan", 0.5),
+    (4, 8, 1536, torch.bfloat16, "arctan", 1.0),    # four warps per token
+    (2, 50, 64, torch.float32, "superspike", 0.7),
+    (3, 17, 96, torch.float32, "arctan", 1.0),
+    (1, 5, 512, torch.float32, "superspike", 1.0),
+])
+def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
+    g = gen(T * 100 + R + D)
+    pre = (torch.randn(T * R, D, generator=g) * 1.5 + 0.3).to(pre_dtype)
+    gamma = (1.0 + 0.2 * torch.randn(D, generator=g))
+    beta_ln = 0.3 * torch.randn(D, generator=g)
+    lif_beta = torch.tensor(0.8)
+    k = 2.0 if surrogate == "arctan" else 4.0
+    gs = torch.randn(T * R, D, generator=g)
+    # reference: torch LayerNorm (fp32) composed with the oracle's autograd LIF
+    x = pre.float().clone().requires_grad_(True)
+    w = gamma.clone().requires_grad_(True)
+    b = beta_ln.clone().requires_grad_(True)
+    lb = lif_beta.clone().requires_grad_(True)
+    y = F.layer_norm(x, (D,), w, b, 1e-5)
+    s_ref, _ = oracle.lif.LIFFunction.apply(y.view(T, R, D), lb, torch.tensor(1.0), torch.tensor(0.0), k, surrogate,
+                                            gain)
+    (s_ref * gs.view(T, R, D)).sum().backward()
+    # ours
+    s, stats = ops.ln_lif_fwd(pre.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, lif_beta, 1.0, 0.0, T,
+                              in_gain=gain)
+    g_pre, g_w, g_b, g_lb = ops.ln_lif_bwd(gs.to(DEV), pre.to(DEV), stats, gamma.to(DEV), beta_ln.to(DEV),
+                                           lif_beta, 1.0, 0.0, T, gain, surrogate, k)
+    vh = membrane_history(y.detach().view(T, -1), lif_beta, 1.0, 0.0, gain)
+    assert_spikes_match(s.cpu().view(T, -1), s_ref.detach().view(T, -1), vh, 1.0, what="ln_lif spikes")
+    mean = x.detach().mean(-1)
+    assert torch.allclose(stats[:, 0].cpu(), mean, rtol=1e-4, atol=1e-5)
+    # gradients on the rows whose spike train matches (a flipped near-threshold spike changes the
+    # backward of its token)
+    same = (s.cpu().view(T, R, D) == s_ref.detach().view(T, R, D)).all(dim=0).all(dim=-1)  # [R]
+    assert same.float().mean() > 0.9
+    rows = same.repeat(T)
+    tol = 2e-2 if pre_dtype == torch.bfloat16 else 2e-3
+    gp, gp_ref = g_pre.float().cpu()[rows], x.grad[rows]
+    assert_close_rel(gp, gp_ref, tol=tol, what="g_pre")
+    if bool(same.all()):
+        assert_close_rel(g_w.cpu(), w.grad, tol=tol, what="g_gamma")
+        assert_close_rel(g_b.cpu(), b.grad, tol=tol, what="g_beta")
+        assert abs(g_lb.item() - lb.grad.item()) <= tol * max(1.0, abs(lb.grad.item()))
+
+
+def test_ln_lif_train_rejects_unsupported(ops):
+    with pytest.raises(RuntimeError):
+        ops.ln_lif_fwd(torch.zeros(5 * 4, 96, device=DEV), None, None, 1e-5, 0.5, 1.0, 0.0, 5)  # T > 4
+    with pytest.raises(RuntimeError):
+        ops.ln_lif_fwd(torch.zeros(4 * 4, 100, device=DEV), None, None, 1e-5, 0.5, 1.0, 0.0, 4)  # D % 32
