@@ -343,6 +343,7 @@ def main():
     import spikingtransformer_b200 as pkg
     from spikingtransformer_b200 import _lib, ops
     from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    from spikingtransformer_b200.streaming import stream_forward
     _lib.load()
 
     torch.manual_seed(0)
@@ -390,24 +391,25 @@ def main():
             hsrc = [s[0].cpu().pin_memory() for s in sets]
             htgt = [s[1].cpu().pin_memory() for s in sets]
             hmask = [s[2].cpu().pin_memory() for s in sets]
-            out_host = torch.empty((4, B, SEQ, ARCH["tgt_vocab_size"]), dtype=torch.float32).pin_memory()
+            # logits [T, B, seq, vocab] fp32, two pinned buffers used in turn
+            out_host = [torch.empty((4, B, SEQ, ARCH["tgt_vocab_size"]), dtype=torch.float32).pin_memory()
+                        for _ in range(2)]
             h2d = hsrc[0].numel() * 4 + htgt[0].numel() * 8 + hmask[0].numel() * 4
-            d2h = out_host.numel() * 4
-            for i in range(2):
-                lg, _ = model(hsrc[i].to(dev, non_blocking=True), htgt[i].to(dev, non_blocking=True),
-                              look_ahead_mask=hmask[i].to(dev, non_blocking=True))
-                out_host.copy_(lg, non_blocking=True)
+            d2h = out_host[0].numel() * 4
+
+            def fwd(src, tgt, mask):
+                return model(src, tgt, look_ahead_mask=mask)[0]
+
+            order = [j % 4 for j in range(args.steps)]
+            stream_forward(fwd, [(hsrc[j], htgt[j], hmask[j]) for j in range(2)], [out_host[j] for j in range(2)])
             torch.cuda.synchronize()
             if ws > 1:
                 dist.barrier()
             f0 = torch.cuda.Event(enable_timing=True)
             f1 = torch.cuda.Event(enable_timing=True)
             f0.record()
-            for i in range(args.steps):
-                j = i % 4
-                lg, _ = model(hsrc[j].to(dev, non_blocking=True), htgt[j].to(dev, non_blocking=True),
-                              look_ahead_mask=hmask[j].to(dev, non_blocking=True))
-                out_host.copy_(lg, non_blocking=True)
+            # every step copies its own images, tokens and mask in and its logits out
+            stream_forward(fwd, [(hsrc[j], htgt[j], hmask[j]) for j in order], [out_host[j % 2] for j in order])
             f1.record()
             torch.cuda.synchronize()
             ems = max_over_ranks(f0.elapsed_time(f1), dev)

@@ -59,3 +59,16 @@ def test_ops_refuse_cpu_tensors():
     from spikingtransformer_b200 import ops
     with pytest.raises(RuntimeError):
         ops.lif_fwd(torch.zeros(2, 4), 0.9, 1.0, 0.0)
+
+
+def test_stream_forward_checks_host_buffers():
+    import torch
+    from spikingtransformer_b200.streaming import stream_forward
+    x = torch.zeros(2, 3)
+    with pytest.raises(ValueError, match="entries"):
+        stream_forward(lambda t: t, [(x,), (x,)], [torch.zeros(2, 3)])
+    with pytest.raises(ValueError, match="shape or dtype"):
+        stream_forward(lambda t: t, [(x,), (torch.zeros(3, 2),)], [x, x])
+    with pytest.raises(ValueError, match="tensors"):
+        stream_forward(lambda t: t, [(x,), (x, x)], [x, x])
+    stream_forward(lambda t: t, [], [])  # nothing to do

@@ -237,6 +237,32 @@ def test_greedy_decode(pkg):
     assert out.shape[0] == 4
 
 
+def test_stream_forward_matches_direct_forward(pkg):
+    """Host batches streamed with overlapped copies give the logits of a
+    direct forward of each batch, bit for bit, including a host buffer reused
+    by several batches."""
+    from spikingtransformer_b200.streaming import stream_forward
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    B, N = 2, 16
+    batches = []
+    for i in range(5):
+        src = synthetic_lines(B, 20 + i)
+        tgt = torch.randint(0, 256, (B, N), generator=torch.Generator().manual_seed(30 + i))
+        mask = torch.tril(torch.ones(N, N)).expand(B, 1, N, N).contiguous()
+        batches.append((src.pin_memory(), tgt.pin_memory(), mask.pin_memory()))
+    with torch.no_grad():
+        want = [ours(s.to(DEV), t.to(DEV), look_ahead_mask=m.to(DEV))[0].cpu() for s, t, m in batches]
+        outs = [torch.empty_like(want[0]).pin_memory() for _ in range(5)]
+        stream_forward(lambda s, t, m: ours(s, t, look_ahead_mask=m)[0], batches, outs)
+        torch.cuda.current_stream().synchronize()
+        for i in range(5):
+            assert torch.equal(outs[i], want[i]), i
+        shared = torch.empty_like(want[0]).pin_memory()
+        stream_forward(lambda s, t, m: ours(s, t, look_ahead_mask=m)[0], batches, [shared] * 5)
+        torch.cuda.current_stream().synchronize()
+        assert torch.equal(shared, want[4])
+
+
 def test_no_device_timeouts(pkg):
     from spikingtransformer_b200 import ops
     ops.device_error_check()
