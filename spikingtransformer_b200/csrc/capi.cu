@@ -81,6 +81,19 @@ static EncodeTiledFn encode_fn() {
 
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  return make_tmap_bf16_sw(map, base, rank, dims, strides_bytes, box, swizzle128 ? 128 : 0);
+}
+
+int make_tmap_bf16_sw(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
+  CUtensorMapSwizzle sw;
+  switch (swizzle_bytes) {
+    case 0: sw = CU_TENSOR_MAP_SWIZZLE_NONE; break;
+    case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
+    case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
+    case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
+    default: return fail(SPK_ERR_INVALID, "unsupported TMA swizzle %d", swizzle_bytes);
+  }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(SPK_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   if (!aligned(base, 16)) return fail(SPK_ERR_ALIGN, "TMA base address must be 16-byte aligned");
@@ -98,7 +111,7 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
   }
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SPK_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return SPK_OK;

@@ -285,6 +285,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 // are innermost first; strides in bytes for dims 1..rank-1.
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
+// The same with the swizzle span in bytes (0, 32, 64 or 128).
+int make_tmap_bf16_sw(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
 
 }  // namespace spk
 
@@ -481,6 +484,72 @@ __device__ __forceinline__ void st_async_f32x2(uint32_t cluster_addr, float a, f
                    cluster_addr),
                "f"(a), "f"(b), "r"(cluster_mbar)
                : "memory");
+}
+
+}  // namespace spk
+
+namespace spk {
+
+// ---------------------------------------------------------------- PTX: transposed TMEM reads, matrix
+// shared-memory moves, TMA stores
+
+// 16 lanes x 256 bits, four column repeats: thread i receives, for repeat j,
+// r[4j], r[4j+1] = lane (base + i/4), columns 8j + 2(i%4) and +1, and
+// r[4j+2], r[4j+3] = lane (base + i/4 + 8), the same columns.  Raw issue:
+// valid after a tcgen05.wait::ld that names the registers.
+__device__ __forceinline__ void tmem_ld16x256_x4_raw(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Four 8x8 b16 matrices from registers into shared memory: lane i gives the
+// address of row i%8 of matrix i/8; register k of thread i holds row i/4,
+// columns 2(i%4) and +1 of matrix k.
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
+// The inverse of stmatrix_x4 (same addresses, same register layout).
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* desc, uint64_t* bar, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// shared -> global tile store, tracked by the issuing thread's bulk groups
+__device__ __forceinline__ void tma_store_3d(const void* desc, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(desc),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// at most N of this thread's bulk groups still reading their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// at most N of this thread's bulk groups not yet complete
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 }  // namespace spk

@@ -42,12 +42,15 @@ constexpr int kMaxSmem = 232448;
 // transposition buffer row stride (floats): 16 data + 4 pad, so that both the
 // row writes and the transposed reads of a quarter-warp hit 8 distinct bank groups
 constexpr int kXS = 20;
+// transposed-read epilogue: one staged output box per warp and buffer, [4 t][8 tokens][32 columns] bf16
+constexpr int kStgBox = 4 * 8 * 32 * 2;
 
 struct Params {
   int T, tpt;
   int64_t R;
   int K, N, n_cta, cs, num_m_tiles, stages, wbox;
   int res_prefetch;  // the residual rows may be bulk-prefetched (16-byte aligned blocks)
+  int tv;            // transposed-read epilogue (T = 4, rows ordered t-major within groups of 8 tokens)
   uint32_t tmem_cols;
   const float *bias, *gamma, *beta_ln;
   float eps;
@@ -63,9 +66,12 @@ struct Smem {
   uint8_t *a, *w;
   uint8_t *ones, *bsplit;  // fast variant: bias MMA operands (no-swizzle K-major, K = 16)
   float* xs;       // 8 warps x 32 rows x kXS floats (padded rows)
+  uint8_t* stg;    // transposed-read epilogue: 8 warps x 2 output boxes (aliases xs)
+  uint64_t* rbar;  // transposed-read epilogue: 8 warps x 2 residual-box barriers
   float *bias, *gamma, *beta;
   float2* stat;    // 2 parities x 2 halves x 128 rows (mean, M2)
   float2* xbuf;    // 2 parities x cs x 128 rows (mean, M2)
+  float2* mw;      // merge weights: [0] the two column halves, [r] cluster CTA r merged onto 0..r-1
   uint64_t *full, *empty, *acc_full, *acc_empty, *xbar, *drain;
   uint32_t* tmem_base;
   int* abort_flag;
@@ -84,12 +90,14 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   size_t oa = take((size_t)p.stages * kAStage, 1024);
   size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
   size_t oon = take(128 * 32, 128), obs = take((size_t)p.n_cta * 32, 128);
-  size_t oxs = take(kEpiWarps * 32 * kXS * 4, 16);
+  size_t oxs = p.tv ? take((size_t)kEpiWarps * 2 * kStgBox, 1024) : take(kEpiWarps * 32 * kXS * 4, 16);
   size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
   size_t ost = take(2 * 2 * 128 * 8, 16);
   size_t oxb = take((size_t)2 * p.cs * 128 * 8, 16);
+  size_t omw = take(16 * 8, 8);
   size_t ofu = take(p.stages * 8, 8), oem = take(p.stages * 8, 8);
   size_t oaf = take(16, 8), oae = take(16, 8), oxbar = take(16, 8), odr = take(8, 8);
+  size_t orb = take(kEpiWarps * 2 * 8, 8);
   size_t otm = take(4, 4), oab = take(4, 4);
   if (s) {
     s->a = base + oa;
@@ -97,11 +105,14 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
     s->ones = base + oon;
     s->bsplit = base + obs;
     s->xs = reinterpret_cast<float*>(base + oxs);
+    s->stg = base + oxs;
+    s->rbar = reinterpret_cast<uint64_t*>(base + orb);
     s->bias = reinterpret_cast<float*>(base + ob);
     s->gamma = reinterpret_cast<float*>(base + og);
     s->beta = reinterpret_cast<float*>(base + obe);
     s->stat = reinterpret_cast<float2*>(base + ost);
     s->xbuf = reinterpret_cast<float2*>(base + oxb);
+    s->mw = reinterpret_cast<float2*>(base + omw);
     s->full = reinterpret_cast<uint64_t*>(base + ofu);
     s->empty = reinterpret_cast<uint64_t*>(base + oem);
     s->acc_full = reinterpret_cast<uint64_t*>(base + oaf);
@@ -128,18 +139,24 @@ __device__ __forceinline__ uint32_t bf16x2_of_01(float lo, float hi) {
   return r;
 }
 
-// merge (mean_b, M2_b) over nb samples into (mean, M2) over na samples
-__device__ __forceinline__ void chan_merge(float& mean, float& m2, float na, float mb, float m2b, float nb) {
-  const float tot = na + nb;
+// merge (mean_b, M2_b) over nb samples into (mean, M2) over na samples (parallel-variance
+// formula); w = (nb / (na + nb), na * nb / (na + nb)) depends only on the counts, so it is
+// computed once per kernel (merge_weights) rather than per row
+__device__ __forceinline__ void chan_merge(float& mean, float& m2, float mb, float m2b, float2 w) {
   const float d = mb - mean;
-  mean = fmaf(d, nb / tot, mean);
-  m2 = m2 + m2b + d * d * (na * nb / tot);
+  mean = fmaf(d, w.x, mean);
+  m2 = m2 + m2b + d * d * w.y;
 }
 
-template <int T, bool FAST, bool RES>
+__device__ __forceinline__ float2 merge_weights(float na, float nb) {
+  const float tot = na + nb;
+  return make_float2(nb / tot, na * nb / tot);
+}
+
+template <int T, bool FAST, bool RES, bool TV>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_il_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tmO, const Params p) {
   constexpr int CPL = 16 / T;  // columns per lane after the transposition
   constexpr int TPQ = 32 / T;  // tokens per TMEM lane quadrant
   // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
@@ -162,10 +179,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], kEpiWarps);
+      mbar_init(&sm.acc_empty[i], TV ? kEpiWarps / 2 : kEpiWarps);
       mbar_init(&sm.xbar[i], 1);  // one local arrive (with the expected bytes) per use
     }
     mbar_init(sm.drain, 1);
+    if (TV)
+      for (int i = 0; i < kEpiWarps * 2; ++i) mbar_init(&sm.rbar[i], 1);
     *sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -202,6 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the fast variant folds the LIF input gain into the affine LayerNorm parameters
     const int n0 = (int)rank * p.n_cta;
     const float g = FAST ? p.gain : 1.0f;
+    if (threadIdx.x < 16) {
+      const int r = threadIdx.x;
+      sm.mw[r] = r == 0 ? merge_weights((float)(p.n_cta >> 1), (float)(p.n_cta >> 1))
+                        : merge_weights((float)(p.n_cta * r), (float)p.n_cta);
+    }
     for (int c = threadIdx.x; c < p.n_cta; c += kThreads) {
       sm.bias[c] = p.bias ? p.bias[n0 + c] : 0.0f;
       sm.gamma[c] = (p.gamma ? p.gamma[n0 + c] : 1.0f) * g;
@@ -242,7 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           outstanding &= ~(1u << stage);
           if (*((volatile int*)sm.abort_flag)) { ok = false; break; }
           mbar_expect_tx(&sm.full[stage], bytes);
-          tma_load_3d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, tile * p.tpt);
+          if (TV)  // dims {K, 8 tokens, T, R / 8}: rows g*32 + t*8 + k
+            tma_load_4d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, 0, tile * 4);
+          else
+            tma_load_3d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, tile * p.tpt);
           uint8_t* w_dst = sm.w + (size_t)stage * p.n_cta * 128;
           for (int r = 0; r < p.n_cta; r += p.wbox)
             tma_load_2d(w_dst + (size_t)r * 128, &tmW, &sm.full[stage], kc * kBK, n0 + r);
@@ -297,6 +324,267 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       mbar_wait(sm.drain, 0, 123);
     }
+  } else if constexpr (TV) {
+    // ---------------------------------------------------------------- epilogue, transposed TMEM reads
+    // Tile rows are ordered q*32 + t*8 + k (k = token within the quadrant's group of 8), so two
+    // 16x256b loads at lanes q*32 and q*32 + 16 hand thread i all four steps of token i/4 for the
+    // column pairs 8j + 2(i%4): the LIF runs in registers with no transposition.  The spikes of a
+    // 32-column chunk are staged with stmatrix as a [t][token][32] box in the 64-byte swizzle and
+    // written by one TMA store per warp; with a residual, the box is first loaded by TMA, added to
+    // with ldmatrix / stmatrix, and stored back.
+    static_assert(T == 4 && FAST, "transposed-read epilogue: T = 4, bf16 spikes or residual");
+    const int ew = warp - 2;
+    const int q = warp & 3;         // TMEM lane quadrant
+    const int grp = ew >> 2;        // tile parity: group g drains accumulator g of every other tile
+    const int tok_l = lane >> 2;    // token within the group of 8
+    const int cp = lane & 3;        // column pair within each 8-column group
+    const int nch = p.n_cta / 32;
+    const uint32_t lane_lo = (uint32_t)(q * 32) << 16, lane_hi = (uint32_t)(q * 32 + 16) << 16;
+    const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+    const float2 beta2 = make_float2(beta, beta), nbeta2 = make_float2(-beta, -beta);
+    const float bvr = __fmul_rn(beta, vr);
+    const float2 bvr2 = make_float2(bvr, bvr);
+    const int n0 = (int)rank * p.n_cta;
+    const float inv_cta = 1.0f / (float)p.n_cta;
+    const float inv_n_all = 1.0f / (float)p.N;
+    // this warp's two staging boxes; lane i addresses row i%8 of matrix i/8 (8-column group) in
+    // the 64-byte swizzle (16-byte unit u of row r at u ^ ((r >> 1) & 3))
+    uint8_t* stg = sm.stg + (size_t)ew * 2 * kStgBox;
+    const int r8 = lane & 7, m8 = lane >> 3;
+    const uint32_t mat_off = (uint32_t)(r8 * 64 + ((m8 ^ ((r8 >> 1) & 3)) << 4));
+    uint64_t* rbar = sm.rbar + ew * 2;
+    uint32_t sc = 0;      // boxes staged so far by this warp (buffer sc & 1)
+    uint32_t rpar = 0;    // bit b: parity of the next residual-box completion on buffer b
+    uint32_t rout = 0;    // bit b: a residual box is in flight to buffer b (warp-uniform)
+    bool rfail = false;   // a residual box did not land in time: stop waiting for them
+    if (lane == 0) tma_prefetch_desc(&tmO);
+    // the two groups take alternate tiles of this CTA's sequence (iteration parity = group), so
+    // one group's waits overlap the other's arithmetic; each warp covers all n_cta columns
+    int iter = grp;
+    for (int tile = cid + grp * ncl; tile < p.num_m_tiles; tile += 2 * ncl, iter += 2) {
+      const int buf = grp;
+      const int y0 = tile * 32 + q * 8;  // first token of this warp's rows
+      if (RES && lane == 0) {
+        // the tile's first residual box: its latency hides behind the statistics
+        const int b = (int)(sc & 1u);
+        bulk_wait_read<0>();
+        mbar_expect_tx(&rbar[b], (uint32_t)kStgBox);
+        tma_load_3d(stg + b * kStgBox, &tmO, &rbar[b], n0, y0, 0);
+      }
+      if (RES) rout |= 1u << (sc & 1u);
+      if (!mbar_wait(&sm.acc_full[buf], (uint32_t)(iter >> 1) & 1u, 131)) { atomicExch(sm.abort_flag, 1); break; }
+      tc_fence_after();
+      const uint32_t tcol = tmem + (uint32_t)(buf * p.n_cta);
+      // ---- statistics of the four rows (t = 0..3) of this thread's token over the warp's columns,
+      // sums shifted by each row's first value (the accumulator already holds the bias)
+      float mean[4], m2[4];
+      {
+        float2 s1[4], s2[4], nK2[4];
+        float K[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) s1[t] = s2[t] = nK2[t] = make_float2(0.0f, 0.0f);
+        auto stats_chunk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16]) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const uint32_t* src = (t < 2 ? lo : hi) + 4 * j + 2 * (t & 1);
+              const float2 d = add2(make_float2(__uint_as_float(src[0]), __uint_as_float(src[1])), nK2[t]);
+              s1[t] = add2(s1[t], d);
+              s2[t] = fma2(d, d, s2[t]);
+            }
+          }
+        };
+        uint32_t a0[16], a1[16], b0[16], b1[16];
+        tmem_ld16x256_x4_raw(tcol + lane_lo, a0);
+        tmem_ld16x256_x4_raw(tcol + lane_hi, a1);
+        for (int c = 0; c < nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence2(a0, a1);
+            if (c + 1 < nch) {
+              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, b0);
+              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, b1);
+            }
+            if (c == 0) {
+              // each row's shift: its first column, held by the token's cp = 0 lane
+              const int src = lane & ~3;
+              K[0] = __shfl_sync(0xffffffffu, __uint_as_float(a0[0]), src);
+              K[1] = __shfl_sync(0xffffffffu, __uint_as_float(a0[2]), src);
+              K[2] = __shfl_sync(0xffffffffu, __uint_as_float(a1[0]), src);
+              K[3] = __shfl_sync(0xffffffffu, __uint_as_float(a1[2]), src);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) nK2[t] = make_float2(-K[t], -K[t]);
+            }
+            stats_chunk(a0, a1);
+          } else {
+            tmem_wait_ld_fence2(b0, b1);
+            if (c + 1 < nch) {
+              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, a0);
+              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, a1);
+            }
+            stats_chunk(b0, b1);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float S1 = s1[t].x + s1[t].y, S2 = s2[t].x + s2[t].y;
+          // the token's four lanes hold disjoint columns
+          S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
+          S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
+          S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
+          S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
+          mean[t] = K[t] + S1 * inv_cta;
+          m2[t] = fmaxf(S2 - S1 * S1 * inv_cta, 0.0f);
+        }
+      }
+      // ---- merge across the CTAs of the cluster (the row's columns are split over them)
+      if (cs > 1) {
+        const int par = grp;
+        float2* xb = sm.xbuf + (size_t)par * cs * 128;
+        {
+          const float2 mine = cp == 0 ? make_float2(mean[0], m2[0])
+                              : cp == 1 ? make_float2(mean[1], m2[1])
+                              : cp == 2 ? make_float2(mean[2], m2[2]) : make_float2(mean[3], m2[3]);
+          const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + q * 32 + cp * 8 + tok_l);
+          const uint32_t bar = smem_u32(&sm.xbar[par]);
+          for (int r = 0; r < cs; ++r)
+            st_async_f32x2(mapa_shared(slot, (uint32_t)r), mine.x, mine.y, mapa_shared(bar, (uint32_t)r));
+        }
+        if (ew == grp * 4 && lane == 0) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
+        if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 132)) {
+          atomicExch(sm.abort_flag, 1);
+          break;
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int row = q * 32 + t * 8 + tok_l;
+          float2 a = xb[row];
+          mean[t] = a.x;
+          m2[t] = a.y;
+          for (int r = 1; r < cs; ++r) {
+            const float2 b = xb[(size_t)r * 128 + row];
+            chan_merge(mean[t], m2[t], b.x, b.y, sm.mw[r]);
+          }
+        }
+      }
+      float2 r2[4], nmr2[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float rstd = rsqrtf(fmaf(m2[t], inv_n_all, p.eps));
+        const float nmr = -mean[t] * rstd;
+        r2[t] = make_float2(rstd, rstd);
+        nmr2[t] = make_float2(nmr, nmr);
+      }
+      // ---- normalise, LIF over t in registers, stage and store one box per 32 columns
+      auto lif_chunk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16], int c) {
+        const int b = (int)(sc & 1u);
+        uint8_t* box = stg + b * kStgBox;
+        const uint32_t box_lane = smem_u32(box) + mat_off;
+        uint32_t bits[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = c * 32 + 8 * j + 2 * cp;
+          const float2 g2 = *reinterpret_cast<const float2*>(sm.gamma + col);
+          const float2 e2 = *reinterpret_cast<const float2*>(sm.beta + col);
+          float2 u = make_float2(0.0f, 0.0f), sp = u;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t* src = (t < 2 ? lo : hi) + 4 * j + 2 * (t & 1);
+            float2 y = make_float2(__uint_as_float(src[0]), __uint_as_float(src[1]));
+            y = fma2(fma2(y, r2[t], nmr2[t]), g2, e2);
+            if (t == 0) {
+              u = y;  // membrane starts at 0
+            } else {
+              y = fma2(sp, bvr2, y);  // exact no-op when v_reset = 0
+              u = fma2(fma2(sp, nbeta2, beta2), u, y);
+            }
+            sp = make_float2(set_gt(u.x, vth), set_gt(u.y, vth));
+            bits[t][j] = bf16x2_of_01(sp.x, sp.y);
+          }
+        }
+        if constexpr (RES) {
+          if (!rfail && !mbar_wait(&rbar[b], (rpar >> b) & 1u, 133)) {
+            atomicExch(sm.abort_flag, 1);
+            rfail = true;
+          }
+          rpar ^= 1u << b;
+          rout &= ~(1u << b);
+          if (c + 1 < nch) {
+            // the next chunk's residual box into the other buffer, once its last store has read it
+            if (lane == 0) {
+              bulk_wait_read<0>();
+              mbar_expect_tx(&rbar[b ^ 1], (uint32_t)kStgBox);
+              tma_load_3d(stg + (b ^ 1) * kStgBox, &tmO, &rbar[b ^ 1], n0 + (c + 1) * 32, y0, 0);
+            }
+            rout |= 1u << (b ^ 1);
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint32_t rv[4];
+            ldmatrix_x4(box_lane + t * 512, rv[0], rv[1], rv[2], rv[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              // spikes are exactly 0/1 and the stream holds small integers: the bf16 add is exact
+              __nv_bfloat162 x, y;
+              *reinterpret_cast<uint32_t*>(&x) = rv[j];
+              *reinterpret_cast<uint32_t*>(&y) = bits[t][j];
+              const __nv_bfloat162 z = __hadd2(x, y);
+              rv[j] = *reinterpret_cast<const uint32_t*>(&z);
+            }
+            stmatrix_x4(box_lane + t * 512, rv[0], rv[1], rv[2], rv[3]);
+          }
+        } else {
+          if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+          __syncwarp();
+#pragma unroll
+          for (int t = 0; t < 4; ++t) stmatrix_x4(box_lane + t * 512, bits[t][0], bits[t][1], bits[t][2], bits[t][3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (y0 < p.R) tma_store_3d(&tmO, box, n0 + c * 32, y0, 0);
+          bulk_commit();
+        }
+        ++sc;
+      };
+      {
+        uint32_t a0[16], a1[16], b0[16], b1[16];
+        tmem_ld16x256_x4_raw(tcol + lane_lo, a0);
+        tmem_ld16x256_x4_raw(tcol + lane_hi, a1);
+        for (int c = 0; c < nch; ++c) {
+          if ((c & 1) == 0) {
+            tmem_wait_ld_fence2(a0, a1);
+            if (c + 1 < nch) {
+              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, b0);
+              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, b1);
+            }
+          } else {
+            tmem_wait_ld_fence2(b0, b1);
+            if (c + 1 < nch) {
+              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, a0);
+              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, a1);
+            }
+          }
+          if (c + 1 == nch) {
+            // last TMEM read of this buffer: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+          }
+          if ((c & 1) == 0)
+            lif_chunk(a0, a1, c);
+          else
+            lif_chunk(b0, b1, c);
+        }
+      }
+    }
+    // every staged box has been written out (and, with a residual, every load has landed)
+    if (lane == 0) bulk_wait<0>();
+    if (RES && !rfail) {
+      // after an abort a residual box may still be in flight: wait (bounded) for it to land
+      for (int b = 0; b < 2; ++b)
+        if ((rout >> b) & 1u) mbar_wait(&rbar[b], (rpar >> b) & 1u, 134);
+    }
   } else {
     // ---------------------------------------------------------------- epilogue
     const int ew = warp - 2;        // 0..7
@@ -304,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int h = ew >> 2;          // column half
     const int row = q * 32 + lane;  // tile row = tok * T + t
     const int half = p.n_cta >> 1;
+    const float inv_half_o = 1.0f / (float)half;
     const int cb = h * half;        // first column of this warp within the slice
     const int nch = half / 32;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
@@ -314,6 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float2 gain2 = make_float2(p.gain, p.gain);
     const int n0 = (int)rank * p.n_cta;
     const int64_t tstride = p.R * (int64_t)p.N;
+    const float inv_n_all = 1.0f / (float)p.N;
+    const float2 w_half = sm.mw[0];
     // warp-private transposition buffer: row r (tile row within the quadrant), column c at r*kXS + c
     float* xs = sm.xs + ew * 32 * kXS;
     float* xs_wr = xs + lane * kXS;
@@ -363,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
         const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
-        const float inv_n = 1.0f / (float)half;
+        const float inv_n = inv_half_o;
         mean = K + S1 * inv_n;
         m2 = fmaxf(S2 - S1 * S1 * inv_n, 0.0f);
       } else {
@@ -426,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float S1 = (s1.x + s1.y) + (s1b.x + s1b.y);
         const float S2 = (s2.x + s2.y) + (s2b.x + s2b.y);
-        const float inv_n = 1.0f / (float)half;
+        const float inv_n = inv_half_o;
         mean = K + S1 * inv_n;
         m2 = fmaxf(S2 - S1 * S1 * inv_n, 0.0f);
       }
@@ -440,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float2 b = h == 0 ? o : make_float2(mean, m2);
         mean = a.x;
         m2 = a.y;
-        chan_merge(mean, m2, (float)half, b.x, b.y, (float)half);
+        chan_merge(mean, m2, b.x, b.y, w_half);
       }
       // ---- merge across the CTAs of the cluster (the row's columns are split over them)
       if (cs > 1) {
@@ -464,10 +755,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         m2 = a.y;
         for (int r = 1; r < cs; ++r) {
           const float2 b = xb[(size_t)r * 128 + row];
-          chan_merge(mean, m2, (float)(p.n_cta * r), b.x, b.y, (float)p.n_cta);
+          chan_merge(mean, m2, b.x, b.y, sm.mw[r]);
         }
       }
-      const float rstd = 1.0f / sqrtf(m2 / (float)p.N + p.eps);
+      const float rstd = rsqrtf(fmaf(m2, inv_n_all, p.eps));
       const float2 rstd2 = make_float2(rstd, rstd);
       const float2 nmean2 = make_float2(-mean, -mean);
       const float nmr = -mean * rstd;
@@ -799,12 +1090,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const Params);
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
 
 template <int T>
-KernelFn pick_kernel(bool fast, bool res) {
-  if (!fast) return gemm_il_kernel<T, false, true>;
-  return res ? gemm_il_kernel<T, true, true> : gemm_il_kernel<T, true, false>;
+KernelFn pick_kernel(bool fast, bool res, bool tv) {
+  if (!fast) return gemm_il_kernel<T, false, true, false>;
+  if constexpr (T == 4) {
+    if (tv) return res ? gemm_il_kernel<4, true, true, true> : gemm_il_kernel<4, true, false, true>;
+  }
+  return res ? gemm_il_kernel<T, true, true, false> : gemm_il_kernel<T, true, false, false>;
 }
 
 }  // namespace gil
@@ -858,15 +1152,32 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   p.residual = reinterpret_cast<__nv_bfloat16*>(residual);
   p.ln_out = ln_out;
   p.res_prefetch = residual != nullptr && aligned(residual, 16) && N % 8 == 0;
+  const bool fast = spk_f32 == nullptr && ln_out == nullptr;
+  const bool res = residual != nullptr;
+  // the transposed-read epilogue writes one bf16 output (spikes, or the residual stream) by TMA
+  void* out = res ? residual : spk_bf16;
+  p.tv = T == 4 && fast && R % 8 == 0 && N % 8 == 0 && out != nullptr && !(res && spk_bf16) && aligned(out, 16);
 
-  CUtensorMap tmA, tmW;
+  CUtensorMap tmA, tmW, tmO;
   int rc;
-  {
+  if (p.tv) {
+    // dims {K, 8, T, R / 8}: the box {64, 8, 4, 4} lands as rows g*32 + t*8 + k, token 8g + k
+    uint64_t dims[4] = {(uint64_t)K, 8, (uint64_t)T, (uint64_t)(R / 8)};
+    uint64_t strides[3] = {(uint64_t)K * 2, (uint64_t)R * K * 2, (uint64_t)K * 16};
+    uint32_t box[4] = {kBK, 8, (uint32_t)T, 4};
+    if ((rc = make_tmap_bf16(&tmA, A, 4, dims, strides, box, true)) != SPK_OK) return rc;
+    // output [T][R][N]: box {32 columns, 8 tokens, 4 t} in the 64-byte swizzle
+    uint64_t odims[3] = {(uint64_t)N, (uint64_t)R, (uint64_t)T};
+    uint64_t ostrides[2] = {(uint64_t)N * 2, (uint64_t)R * N * 2};
+    uint32_t obox[3] = {32, 8, 4};
+    if ((rc = make_tmap_bf16_sw(&tmO, out, 3, odims, ostrides, obox, 64)) != SPK_OK) return rc;
+  } else {
     // dims {K, T, R}: the box {64, T, tpt} lands as rows tok*T + t
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)T, (uint64_t)R};
     uint64_t strides[2] = {(uint64_t)R * K * 2, (uint64_t)K * 2};
     uint32_t box[3] = {kBK, (uint32_t)T, (uint32_t)p.tpt};
     if ((rc = make_tmap_bf16(&tmA, A, 3, dims, strides, box, true)) != SPK_OK) return rc;
+    tmO = tmA;  // unused
   }
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
@@ -880,15 +1191,13 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
     if (smem <= (size_t)kMaxSmem) break;
   }
   if (smem > (size_t)kMaxSmem) return fail(SPK_ERR_SHAPE, "tile of %d columns does not fit in shared memory", n_cta);
-  const bool fast = spk_f32 == nullptr && ln_out == nullptr;
-  const bool res = residual != nullptr;
   KernelFn kern;
   switch (T) {
-    case 1: kern = pick_kernel<1>(fast, res); break;
-    case 2: kern = pick_kernel<2>(fast, res); break;
-    case 4: kern = pick_kernel<4>(fast, res); break;
-    case 8: kern = pick_kernel<8>(fast, res); break;
-    default: kern = pick_kernel<16>(fast, res); break;
+    case 1: kern = pick_kernel<1>(fast, res, false); break;
+    case 2: kern = pick_kernel<2>(fast, res, false); break;
+    case 4: kern = pick_kernel<4>(fast, res, p.tv != 0); break;
+    case 8: kern = pick_kernel<8>(fast, res, false); break;
+    default: kern = pick_kernel<16>(fast, res, false); break;
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -916,7 +1225,7 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
       cfg.gridDim = dim3((unsigned)(clusters * cs), 1, 1);
     }
   }
-  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, p);
+  e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmO, p);
   if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "gemm_il_kernel launch: %s", cudaGetErrorString(e));
   return SPK_OK;
 }

@@ -168,6 +168,37 @@ def test_linear_ln_lif_fast(ops, T, R, K, N, gain, vr, res):
         assert torch.equal(r_dev.float().cpu(), resid.float() + s.float().cpu())
 
 
+@pytest.mark.parametrize("R,K,N,gain,vr,res", [
+    (256, 384, 384, 1.0, 0.0, False),
+    (256, 384, 384, 0.5, 0.0, True),     # out_proj: residual only, as the model calls it
+    (96, 384, 1536, 0.5, 0.0, False),    # MLP expand, 6-CTA cluster
+    (64, 1536, 384, 1.0, -0.25, True),   # MLP compress into the residual, non-zero reset
+    (200, 256, 128, 0.5, 0.0, True),     # last tile holds one group of 8 tokens
+    (104, 128, 64, 1.0, 0.0, False),     # one 32-column chunk per warp
+    (72, 192, 512, 0.8, 0.1, True),      # 2-CTA cluster of 256 columns, K not a multiple of 64
+    (40, 384, 256, 1.0, 0.0, False),
+])
+def test_linear_ln_lif_t4_transposed_epilogue(ops, R, K, N, gain, vr, res):
+    """T = 4 with a token count divisible by 8 and one bf16 output (the spikes,
+    or the residual stream without the spikes): the epilogue that reads TMEM
+    transposed and writes through TMA stores."""
+    T = 4
+    A, W, bias, gamma, beta_ln = make_lin(T * 17 + R + K + N, R, K, N, T, counts=2)
+    s_ref, _, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.9, 1.0, vr, gain=gain)
+    args = (A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.9, 1.0, vr, T)
+    if res:
+        resid = torch.randint(0, 5, (T * R, N), generator=gen(R + 1)).to(torch.bfloat16)
+        r_dev = resid.to(DEV)
+        s, y = ops.linear_ln_lif(*args, in_gain=gain, residual=r_dev, want_spikes=False)
+        assert s is None and y is None
+        s = r_dev.float().cpu() - resid.float()
+        assert set(s.unique().tolist()) <= {0.0, 1.0}
+    else:
+        s, y = ops.linear_ln_lif(*args, in_gain=gain, spike_dtype=torch.bfloat16)
+        s = s.float().cpu()
+    assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+
+
 def test_linear_ln_lif_cfg2_tau(ops):
     # fused Linear->LN->LIF at the cfg-2 feature sizes (tau=2 neuron), fewer rows
     T, R, K, N = 4, 2048, 384, 1536
