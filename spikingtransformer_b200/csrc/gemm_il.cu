@@ -375,103 +375,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&sm.acc_full[buf], (uint32_t)(iter >> 1) & 1u, 131)) { atomicExch(sm.abort_flag, 1); break; }
       tc_fence_after();
       const uint32_t tcol = tmem + (uint32_t)(buf * p.n_cta);
-      // ---- statistics of the four rows (t = 0..3) of this thread's token over the warp's columns,
-      // sums shifted by each row's first value (the accumulator already holds the bias)
-      float mean[4], m2[4];
+      // ---- statistics: lane l owns tile row q*32 + l (= step l / 8 of token l % 8) over the CTA's
+      // columns (32x32b loads), sums shifted by the row's first value (the accumulator already
+      // holds the bias)
+      float mean, m2;
       {
-        float2 s1[4], s2[4], nK2[4];
-        float K[4];
+        float2 s1a = make_float2(0.0f, 0.0f), s2a = s1a, s1b = s1a, s2b = s1a, nK2 = s1a;
+        auto stats_chunk = [&](const uint32_t (&r)[32]) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) s1[t] = s2[t] = nK2[t] = make_float2(0.0f, 0.0f);
-        auto stats_chunk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16]) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const uint32_t* src = (t < 2 ? lo : hi) + 4 * j + 2 * (t & 1);
-              const float2 d = add2(make_float2(__uint_as_float(src[0]), __uint_as_float(src[1])), nK2[t]);
-              s1[t] = add2(s1[t], d);
-              s2[t] = fma2(d, d, s2[t]);
-            }
+          for (int i = 0; i < 32; i += 4) {
+            const float2 d0 = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nK2);
+            const float2 d1 = add2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])), nK2);
+            s1a = add2(s1a, d0);
+            s1b = add2(s1b, d1);
+            s2a = fma2(d0, d0, s2a);
+            s2b = fma2(d1, d1, s2b);
           }
         };
-        uint32_t a0[16], a1[16], b0[16], b1[16];
-        tmem_ld16x256_x4_raw(tcol + lane_lo, a0);
-        tmem_ld16x256_x4_raw(tcol + lane_hi, a1);
+        const uint32_t trow = tcol + lane_lo;
+        float K = 0.0f;
+        uint32_t ra[32], rb[32];
+        tmem_ld32_raw(trow, ra);
         for (int c = 0; c < nch; ++c) {
           if ((c & 1) == 0) {
-            tmem_wait_ld_fence2(a0, a1);
-            if (c + 1 < nch) {
-              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, b0);
-              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, b1);
-            }
+            tmem_wait_ld_fence32(ra);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
             if (c == 0) {
-              // each row's shift: its first column, held by the token's cp = 0 lane
-              const int src = lane & ~3;
-              K[0] = __shfl_sync(0xffffffffu, __uint_as_float(a0[0]), src);
-              K[1] = __shfl_sync(0xffffffffu, __uint_as_float(a0[2]), src);
-              K[2] = __shfl_sync(0xffffffffu, __uint_as_float(a1[0]), src);
-              K[3] = __shfl_sync(0xffffffffu, __uint_as_float(a1[2]), src);
-#pragma unroll
-              for (int t = 0; t < 4; ++t) nK2[t] = make_float2(-K[t], -K[t]);
+              K = __uint_as_float(ra[0]);
+              nK2 = make_float2(-K, -K);
             }
-            stats_chunk(a0, a1);
+            stats_chunk(ra);
           } else {
-            tmem_wait_ld_fence2(b0, b1);
-            if (c + 1 < nch) {
-              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, a0);
-              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, a1);
-            }
-            stats_chunk(b0, b1);
+            tmem_wait_ld_fence32(rb);
+            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+            stats_chunk(rb);
           }
         }
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float S1 = s1[t].x + s1[t].y, S2 = s2[t].x + s2[t].y;
-          // the token's four lanes hold disjoint columns
-          S1 += __shfl_xor_sync(0xffffffffu, S1, 1);
-          S2 += __shfl_xor_sync(0xffffffffu, S2, 1);
-          S1 += __shfl_xor_sync(0xffffffffu, S1, 2);
-          S2 += __shfl_xor_sync(0xffffffffu, S2, 2);
-          mean[t] = K[t] + S1 * inv_cta;
-          m2[t] = fmaxf(S2 - S1 * S1 * inv_cta, 0.0f);
-        }
+        const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
+        const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
+        mean = K + S1 * inv_cta;
+        m2 = fmaxf(S2 - S1 * S1 * inv_cta, 0.0f);
       }
       // ---- merge across the CTAs of the cluster (the row's columns are split over them)
       if (cs > 1) {
         const int par = grp;
         float2* xb = sm.xbuf + (size_t)par * cs * 128;
-        {
-          const float2 mine = cp == 0 ? make_float2(mean[0], m2[0])
-                              : cp == 1 ? make_float2(mean[1], m2[1])
-                              : cp == 2 ? make_float2(mean[2], m2[2]) : make_float2(mean[3], m2[3]);
-          const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + q * 32 + cp * 8 + tok_l);
-          const uint32_t bar = smem_u32(&sm.xbar[par]);
-          for (int r = 0; r < cs; ++r)
-            st_async_f32x2(mapa_shared(slot, (uint32_t)r), mine.x, mine.y, mapa_shared(bar, (uint32_t)r));
-        }
+        const int row = q * 32 + lane;
+        const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + row);
+        const uint32_t bar = smem_u32(&sm.xbar[par]);
+        for (int r = 0; r < cs; ++r)
+          st_async_f32x2(mapa_shared(slot, (uint32_t)r), mean, m2, mapa_shared(bar, (uint32_t)r));
         if (ew == grp * 4 && lane == 0) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
         if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 132)) {
           atomicExch(sm.abort_flag, 1);
           break;
         }
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int row = q * 32 + t * 8 + tok_l;
-          float2 a = xb[row];
-          mean[t] = a.x;
-          m2[t] = a.y;
-          for (int r = 1; r < cs; ++r) {
-            const float2 b = xb[(size_t)r * 128 + row];
-            chan_merge(mean[t], m2[t], b.x, b.y, sm.mw[r]);
-          }
+        float2 a = xb[row];
+        mean = a.x;
+        m2 = a.y;
+        for (int r = 1; r < cs; ++r) {
+          const float2 b = xb[(size_t)r * 128 + row];
+          chan_merge(mean, m2, b.x, b.y, sm.mw[r]);
         }
       }
+      // this lane's row, then the four rows of this thread's token (lanes t*8 + token)
+      const float rstd_l = rsqrtf(fmaf(m2, inv_n_all, p.eps));
+      const float nmr_l = -mean * rstd_l;
       float2 r2[4], nmr2[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        const float rstd = rsqrtf(fmaf(m2[t], inv_n_all, p.eps));
-        const float nmr = -mean[t] * rstd;
+        const float rstd = __shfl_sync(0xffffffffu, rstd_l, t * 8 + tok_l);
+        const float nmr = __shfl_sync(0xffffffffu, nmr_l, t * 8 + tok_l);
         r2[t] = make_float2(rstd, rstd);
         nmr2[t] = make_float2(nmr, nmr);
       }
