@@ -376,6 +376,22 @@ __device__ __forceinline__ void tmem_wait_ld_fence(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// one column of the calling thread's lane, raw issue (valid after a wait that names it)
+__device__ __forceinline__ void tmem_ld1_raw(uint32_t taddr, uint32_t& r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+}
+
+// After a bare tcgen05.wait::ld: makes the registers of one more 16-column load
+// read-write at this point, so that no use of them moves above the wait.
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
 // two buffers in flight: waits for both, fences both
 __device__ __forceinline__ void tmem_wait_ld_fence2(uint32_t (&a)[16], uint32_t (&b)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"

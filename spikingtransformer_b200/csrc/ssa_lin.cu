@@ -352,7 +352,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 
+    // A: K^T V of unit g -> bf16 operand (x2 for XNOR); 1^T V, s^T V -> shared floats (parity g & 1)
+    auto build_mb = [&](int g) -> bool {
+      const int par = g & 1;
+      if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) return false;
+      tc_fence_after();
+      if (grp == 0 && quad < 3) {
+        const float f = XNOR ? 2.0f : 1.0f;
+#pragma unroll
+        for (int c0 = 0; c0 < DP; c0 += 16) {
+          float d1[16];
+          tmem_ld16(tm_d1 + lane_off + c0, d1);
+          if (quad < 2) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint4 w;
+              w.x = pack_bf16x2(f * d1[8 * c + 0], f * d1[8 * c + 1]);
+              w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
+              w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
+              w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
+              const int ch = c0 / 8 + c;
+              *reinterpret_cast<uint4*>(sm.mb + lrow * 128 + ((ch ^ (lrow & 7)) << 4)) = w;
+            }
+          } else if (XNOR && lane < 2) {
+            float* dst = (lane == 0 ? sm.cs : sm.kv) + par * 64 + c0;
+#pragma unroll
+            for (int c = 0; c < 16; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(d1[c], d1[c + 1], d1[c + 2], d1[c + 3]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1, kEpi);
+      if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
+      return true;
+    };
+
+    // Unit order with EARLY (head width <= 48): the operand of unit g+1 is built as soon as unit
+    // g's product has been read out of TMEM, so the product of unit g+1 runs on the tensor cores
+    // while unit g's output is computed; key sums run two units ahead.  Wider heads keep the
+    // product in TMEM while the output is computed (the registers hold the LIF state).
+    constexpr bool EARLY = DP <= 48;
+    constexpr int NCH = DP / 16;
+    auto in_range = [&](int c) { return !(c * 16 + 16 <= dc0 || c * 16 >= dc0 + dcols); };
     if (n_units > 0) ok = key_sums(0);
+    if (EARLY) {
+      if (ok && n_units > 0) ok = build_mb(0);
+      if (ok && n_units > 1) ok = key_sums(1);
+    }
     for (int g = 0; g < n_units && ok; ++g) {
       const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
       const int b = item / p.H, h = item % p.H;
@@ -361,40 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < DP; ++i) mem[i] = 0.0f;
       }
-      // ---- A: K^T V -> bf16 operand (x2 for XNOR); 1^T V, s^T V -> shared floats
-      if (!mbar_wait(sm.m_full, (uint32_t)(g & 1), 93)) { ok = false; break; }
-      tc_fence_after();
-      if (grp == 0 && quad < 3) {
-        float d1[DP];
-#pragma unroll
-        for (int c0 = 0; c0 < DP; c0 += 16) tmem_ld16(tm_d1 + lane_off + c0, d1 + c0);
-        if (quad < 2) {
-          const float f = XNOR ? 2.0f : 1.0f;
-#pragma unroll
-          for (int c = 0; c < DP / 8; ++c) {
-            uint4 w;
-            w.x = pack_bf16x2(f * d1[8 * c + 0], f * d1[8 * c + 1]);
-            w.y = pack_bf16x2(f * d1[8 * c + 2], f * d1[8 * c + 3]);
-            w.z = pack_bf16x2(f * d1[8 * c + 4], f * d1[8 * c + 5]);
-            w.w = pack_bf16x2(f * d1[8 * c + 6], f * d1[8 * c + 7]);
-            *reinterpret_cast<uint4*>(sm.mb + lrow * 128 + ((c ^ (lrow & 7)) << 4)) = w;
-          }
-        } else if (XNOR && lane < 2) {
-          float* dst = (lane == 0 ? sm.cs : sm.kv) + par * 64;
-#pragma unroll
-          for (int c = 0; c < DP; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(d1[c], d1[c + 1], d1[c + 2], d1[c + 3]);
-        }
+      if (!EARLY) {
+        if (!build_mb(g)) { ok = false; break; }
+        if (g + 1 < n_units && !key_sums(g + 1)) { ok = false; break; }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      named_bar_sync(1, kEpi);
-      if (threadIdx.x == 64) mbar_arrive(sm.mb_ready);
-      // ---- B: key sums of the next unit, so its MMA1 overlaps this unit's MMA2 and output
-      if (g + 1 < n_units && !key_sums(g + 1)) { ok = false; break; }
-      // ---- C: O = D2 + (dh - |q_i|) (1^T V) - s^T V, a = scale O, LIF over t, spikes.
-      // Packed fp32x2 arithmetic; every product and sum rounds as the scalar reference
-      // (the integer terms are exact in any order).  TMEM columns are read 16 at a time,
-      // the next chunk in flight while the current one is processed.
       if (!mbar_wait(sm.o_full, (uint32_t)(g & 1), 94)) { ok = false; break; }
       tc_fence_after();
       const uint32_t ta = tm_d2 + qb * NO + lane_off;
@@ -403,76 +420,94 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* csp = sm.cs + par * 64;
       const float* kvp = sm.kv + par * 64;
       const bool row_ok = qi < p.Nq;
-      constexpr int NCH = DP / 16;
-      // chunk c (16 columns) is read into rbuf[c & 1]: issued one chunk ahead, or on the spot
-      // for the first chunk of this thread's columns
-      uint32_t rbuf[2][16];
-      uint32_t rq[16];
-      auto in_range = [&](int c) { return !(c * 16 + 16 <= dc0 || c * 16 >= dc0 + dcols); };
+      uint32_t rq = 0;
       if (XNOR) {
-        tmem_ld16_raw(ta + DP, rq);  // the ones column: |q_i|
-        tmem_wait_ld_fence(rq);
+        tmem_ld1_raw(ta + DP, rq);  // the ones column: |q_i|
+        tmem_wait_ld();
+        asm volatile("" : "+r"(rq) : : "memory");
       }
-      const float c_row = XNOR ? (float)p.dh - __uint_as_float(rq[0]) : 0.0f;
+      const float c_row = XNOR ? (float)p.dh - __uint_as_float(rq) : 0.0f;
       const float2 c2 = make_float2(c_row, c_row), scale2 = make_float2(scale, scale);
       const float2 gain2 = make_float2(p.gain, p.gain), beta2 = make_float2(beta, beta);
-#pragma unroll
-      for (int c = 0; c < NCH; ++c) {
+      // O = D2 + (dh - |q_i|) (1^T V) - s^T V, a = scale O, LIF over t, spikes, for the 16 columns
+      // of chunk c.  Packed fp32x2 arithmetic; every product and sum rounds as the scalar
+      // reference (the integer terms are exact in any order).
+      auto out_chunk = [&](int c, const uint32_t (&rc)[16]) {
         const int c0 = c * 16;
-        if (!in_range(c)) continue;
-        // (head width 64: no read-ahead, the registers go to the LIF state)
-        constexpr bool AHEAD = DP <= 48;
-        const int cur = AHEAD ? (c & 1) : 0;
-        if (!AHEAD || c == 0 || !in_range(c - 1)) tmem_ld16_raw(ta + c0, rbuf[cur]);
-        tmem_wait_ld_fence(rbuf[cur]);
-        if (AHEAD && c + 1 < NCH && in_range(c + 1)) tmem_ld16_raw(ta + c0 + 16, rbuf[cur ^ 1]);
-        if (row_ok) {
 #pragma unroll
-          for (int d8 = 0; d8 < 16; d8 += 8) {
-            const int d0 = c0 + d8;
-            if (d0 < dc0 || d0 >= dc0 + dcols) continue;
-            uint32_t bits[4];
+        for (int d8 = 0; d8 < 16; d8 += 8) {
+          const int d0 = c0 + d8;
+          if (d0 < dc0 || d0 >= dc0 + dcols) continue;
+          uint32_t bits[4];
 #pragma unroll
-            for (int i = 0; i < 8; i += 4) {
-              const float4 cs4 = *reinterpret_cast<const float4*>(csp + d0 + i);
-              const float4 kv4 = *reinterpret_cast<const float4*>(kvp + d0 + i);
+          for (int i = 0; i < 8; i += 4) {
+            const float4 cs4 = *reinterpret_cast<const float4*>(csp + d0 + i);
+            const float4 kv4 = *reinterpret_cast<const float4*>(kvp + d0 + i);
 #pragma unroll
-              for (int j = 0; j < 4; j += 2) {
-                const uint32_t* r = rbuf[cur] + d8 + i + j;
-                float2 ov = make_float2(__uint_as_float(r[0]), __uint_as_float(r[1]));
-                if (XNOR) {
-                  const float2 cs2 = j == 0 ? make_float2(cs4.x, cs4.y) : make_float2(cs4.z, cs4.w);
-                  const float2 kv2 = j == 0 ? make_float2(kv4.x, kv4.y) : make_float2(kv4.z, kv4.w);
-                  ov = add2(fma2(c2, cs2, ov), make_float2(-kv2.x, -kv2.y));
-                }
-                const float2 a = mul2(ov, scale2);
-                const int dd = d0 + i + j;
-                if (aout) *reinterpret_cast<float2*>(aout + dd) = a;
-                const float2 cu = mul2(a, gain2);  // exact when the gain is 1
-                const float2 u = add2(mul2(make_float2(mem[dd], mem[dd + 1]), beta2), cu);
-                const bool f0 = u.x > vth, f1 = u.y > vth;
-                mem[dd] = f0 ? vr : u.x;
-                mem[dd + 1] = f1 ? vr : u.y;
-                bits[(i + j) >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
+            for (int j = 0; j < 4; j += 2) {
+              const uint32_t* r = rc + d8 + i + j;
+              float2 ov = make_float2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+              if (XNOR) {
+                const float2 cs2 = j == 0 ? make_float2(cs4.x, cs4.y) : make_float2(cs4.z, cs4.w);
+                const float2 kv2 = j == 0 ? make_float2(kv4.x, kv4.y) : make_float2(kv4.z, kv4.w);
+                ov = add2(fma2(c2, cs2, ov), make_float2(-kv2.x, -kv2.y));
               }
-            }
-            if (p.out_bf16) *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
-            if (p.out_f32) {
-              float4 lo, hi;
-              lo.x = (bits[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bits[0] >> 16) ? 1.0f : 0.0f;
-              lo.z = (bits[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bits[1] >> 16) ? 1.0f : 0.0f;
-              hi.x = (bits[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bits[2] >> 16) ? 1.0f : 0.0f;
-              hi.z = (bits[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bits[3] >> 16) ? 1.0f : 0.0f;
-              *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = lo;
-              *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = hi;
+              const float2 a = mul2(ov, scale2);
+              const int dd = d0 + i + j;
+              if (aout) *reinterpret_cast<float2*>(aout + dd) = a;
+              const float2 cu = mul2(a, gain2);  // exact when the gain is 1
+              const float2 u = add2(mul2(make_float2(mem[dd], mem[dd + 1]), beta2), cu);
+              const bool f0 = u.x > vth, f1 = u.y > vth;
+              mem[dd] = f0 ? vr : u.x;
+              mem[dd + 1] = f1 ? vr : u.y;
+              bits[(i + j) >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
             }
           }
+          if (p.out_bf16) *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+          if (p.out_f32) {
+            float4 lo, hi;
+            lo.x = (bits[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bits[0] >> 16) ? 1.0f : 0.0f;
+            lo.z = (bits[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bits[1] >> 16) ? 1.0f : 0.0f;
+            hi.x = (bits[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bits[2] >> 16) ? 1.0f : 0.0f;
+            hi.z = (bits[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bits[3] >> 16) ? 1.0f : 0.0f;
+            *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = lo;
+            *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = hi;
+          }
         }
+      };
+      if constexpr (EARLY) {
+        // all of D2 into registers, the accumulator back to the MMA warp, the next operand
+        uint32_t dreg[NCH][16];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+          if (in_range(c)) tmem_ld16_raw(ta + c * 16, dreg[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) reg_fence16(dreg[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.o_empty);
+        if (g + 1 < n_units && !build_mb(g + 1)) { ok = false; break; }
+        if (row_ok) {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c)
+            if (in_range(c)) out_chunk(c, dreg[c]);
+        }
+        if (g + 2 < n_units && !key_sums(g + 2)) { ok = false; break; }
+      } else {
+        // chunk by chunk (16 columns), then the accumulator back to the MMA warp
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          if (!in_range(c)) continue;
+          uint32_t rbuf[16];
+          tmem_ld16_raw(ta + c * 16, rbuf);
+          tmem_wait_ld_fence(rbuf);
+          if (row_ok) out_chunk(c, rbuf);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sm.o_empty);
       }
-      // all of D2 is in registers (each load waited): hand it back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sm.o_empty);
     }
     (void)ok;
   }
