@@ -551,8 +551,8 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
 // t-coupled kernel with interleaved rows (gemm_il.cu)
 int launch_gemm_il(const void* A, const void* W, const float* bias, const float* gamma, const float* beta_ln,
                    float eps, const float* lif_beta, const float* lif_vth, const float* lif_vr, float gain, int T,
-                   int64_t R, int K, int N, void* spk_bf16, float* spk_f32, void* residual, float* ln_out,
-                   cudaStream_t st);
+                   int64_t R, int K, int N, int t_broadcast, void* spk_bf16, float* spk_f32, void* residual,
+                   float* ln_out, cudaStream_t st);
 
 static bool force_generic() {
   static int v = -1;
@@ -641,13 +641,20 @@ int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const
     mode = MODE_TBCAST;
     p.tpt = 128;
     p.num_m_tiles = (int)((R + 127) / 128);
+    if (!force_generic()) {
+      rc = launch_gemm_il(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain, (int)T, R,
+                          (int)K, (int)N, 1, p.spk_bf16, p.spk_f32, residual, ln_out,
+                          reinterpret_cast<cudaStream_t>(stream));
+      if (rc == SPK_OK) return check_launch("gemm_il_kernel");
+      if (rc != SPK_ERR_UNSUPPORTED) return rc;
+    }
   } else {
     mode = MODE_TCOUPLED;
     p.tpt = (int)(128 / T);
     p.num_m_tiles = (int)((R + p.tpt - 1) / p.tpt);
     if (!force_generic()) {
       rc = launch_gemm_il(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain, (int)T, R,
-                          (int)K, (int)N, p.spk_bf16, p.spk_f32, residual, ln_out,
+                          (int)K, (int)N, 0, p.spk_bf16, p.spk_f32, residual, ln_out,
                           reinterpret_cast<cudaStream_t>(stream));
       if (rc == SPK_OK) return check_launch("gemm_il_kernel");
       if (rc != SPK_ERR_UNSUPPORTED) return rc;

@@ -50,7 +50,7 @@ struct Params {
   int64_t R;
   int K, N, n_cta, cs, num_m_tiles, stages, wbox;
   int res_prefetch;  // the residual rows may be bulk-prefetched (16-byte aligned blocks)
-  int tv;            // transposed-read epilogue (T = 4, rows ordered t-major within groups of 8 tokens)
+  int epi;           // epilogue variant (kEpiTranspose, kEpiTV, kEpiTB)
   uint32_t tmem_cols;
   const float *bias, *gamma, *beta_ln;
   float eps;
@@ -90,7 +90,9 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   size_t oa = take((size_t)p.stages * kAStage, 1024);
   size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
   size_t oon = take(128 * 32, 128), obs = take((size_t)p.n_cta * 32, 128);
-  size_t oxs = p.tv ? take((size_t)kEpiWarps * 2 * kStgBox, 1024) : take(kEpiWarps * 32 * kXS * 4, 16);
+  size_t oxs = p.epi == 1   ? take((size_t)kEpiWarps * 2 * kStgBox, 1024)
+               : p.epi == 0 ? take(kEpiWarps * 32 * kXS * 4, 16)
+                            : take((size_t)kEpiWarps * p.T * 2048, 1024);
   size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
   size_t ost = take(2 * 2 * 128 * 8, 16);
   size_t oxb = take((size_t)2 * p.cs * 128 * 8, 16);
@@ -153,7 +155,51 @@ __device__ __forceinline__ float2 merge_weights(float na, float nb) {
   return make_float2(nb / tot, na * nb / tot);
 }
 
-template <int T, bool FAST, bool RES, bool TV>
+// (mean, M2) of the calling thread's TMEM lane over nch 32-column chunks starting at trow
+// (32x32b loads, double-buffered); sums shifted by the row's first value
+__device__ __forceinline__ void lane_row_stats(uint32_t trow, int nch, float inv_cols, float& mean, float& m2) {
+  float2 s1a = make_float2(0.0f, 0.0f), s2a = s1a, s1b = s1a, s2b = s1a, nK2 = s1a;
+  auto stats_chunk = [&](const uint32_t (&r)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float2 d0 = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nK2);
+      const float2 d1 = add2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])), nK2);
+      s1a = add2(s1a, d0);
+      s1b = add2(s1b, d1);
+      s2a = fma2(d0, d0, s2a);
+      s2b = fma2(d1, d1, s2b);
+    }
+  };
+  float K = 0.0f;
+  uint32_t ra[32], rb[32];
+  tmem_ld32_raw(trow, ra);
+  for (int c = 0; c < nch; ++c) {
+    if ((c & 1) == 0) {
+      tmem_wait_ld_fence32(ra);
+      if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
+      if (c == 0) {
+        K = __uint_as_float(ra[0]);
+        nK2 = make_float2(-K, -K);
+      }
+      stats_chunk(ra);
+    } else {
+      tmem_wait_ld_fence32(rb);
+      if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+      stats_chunk(rb);
+    }
+  }
+  const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
+  const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
+  mean = K + S1 * inv_cols;
+  m2 = fmaxf(S2 - S1 * S1 * inv_cols, 0.0f);
+}
+
+// epilogue variants
+constexpr int kEpiTranspose = 0;  // rows tok*T + t, lanes transposed through shared memory
+constexpr int kEpiTV = 1;         // T = 4, rows t-major within groups of 8 tokens, transposed TMEM reads
+constexpr int kEpiTB = 2;         // t-broadcast: rows are tokens, one pre-activation for every step
+
+template <int T, bool FAST, bool RES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_il_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmO, const Params p) {
@@ -179,11 +225,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], TV ? kEpiWarps / 2 : kEpiWarps);
+      mbar_init(&sm.acc_empty[i], EPI != kEpiTranspose ? kEpiWarps / 2 : kEpiWarps);
       mbar_init(&sm.xbar[i], 1);  // one local arrive (with the expected bytes) per use
     }
     mbar_init(sm.drain, 1);
-    if (TV)
+    if (EPI == kEpiTV)
       for (int i = 0; i < kEpiWarps * 2; ++i) mbar_init(&sm.rbar[i], 1);
     *sm.abort_flag = 0;
     fence_mbar_init();
@@ -266,8 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           outstanding &= ~(1u << stage);
           if (*((volatile int*)sm.abort_flag)) { ok = false; break; }
           mbar_expect_tx(&sm.full[stage], bytes);
-          if (TV)  // dims {K, 8 tokens, T, R / 8}: rows g*32 + t*8 + k
+          if (EPI == kEpiTV)  // dims {K, 8 tokens, T, R / 8}: rows g*32 + t*8 + k
             tma_load_4d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, 0, tile * 4);
+          else if (EPI == kEpiTB)  // dims {K, R}: rows = tokens
+            tma_load_2d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, tile * 128);
           else
             tma_load_3d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, tile * p.tpt);
           uint8_t* w_dst = sm.w + (size_t)stage * p.n_cta * 128;
@@ -324,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       mbar_wait(sm.drain, 0, 123);
     }
-  } else if constexpr (TV) {
+  } else if constexpr (EPI == kEpiTV) {
     // ---------------------------------------------------------------- epilogue, transposed TMEM reads
     // Tile rows are ordered q*32 + t*8 + k (k = token within the quadrant's group of 8), so two
     // 16x256b loads at lanes q*32 and q*32 + 16 hand thread i all four steps of token i/4 for the
@@ -333,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // written by one TMA store per warp; with a residual, the box is first loaded by TMA, added to
     // with ldmatrix / stmatrix, and stored back.
     static_assert(T == 4 && FAST, "transposed-read epilogue: T = 4, bf16 spikes or residual");
+    static_assert(EPI == kEpiTV, "");
     const int ew = warp - 2;
     const int q = warp & 3;         // TMEM lane quadrant
     const int grp = ew >> 2;        // tile parity: group g drains accumulator g of every other tile
@@ -379,43 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // columns (32x32b loads), sums shifted by the row's first value (the accumulator already
       // holds the bias)
       float mean, m2;
-      {
-        float2 s1a = make_float2(0.0f, 0.0f), s2a = s1a, s1b = s1a, s2b = s1a, nK2 = s1a;
-        auto stats_chunk = [&](const uint32_t (&r)[32]) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float2 d0 = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nK2);
-            const float2 d1 = add2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])), nK2);
-            s1a = add2(s1a, d0);
-            s1b = add2(s1b, d1);
-            s2a = fma2(d0, d0, s2a);
-            s2b = fma2(d1, d1, s2b);
-          }
-        };
-        const uint32_t trow = tcol + lane_lo;
-        float K = 0.0f;
-        uint32_t ra[32], rb[32];
-        tmem_ld32_raw(trow, ra);
-        for (int c = 0; c < nch; ++c) {
-          if ((c & 1) == 0) {
-            tmem_wait_ld_fence32(ra);
-            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
-            if (c == 0) {
-              K = __uint_as_float(ra[0]);
-              nK2 = make_float2(-K, -K);
-            }
-            stats_chunk(ra);
-          } else {
-            tmem_wait_ld_fence32(rb);
-            if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
-            stats_chunk(rb);
-          }
-        }
-        const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
-        const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
-        mean = K + S1 * inv_cta;
-        m2 = fmaxf(S2 - S1 * S1 * inv_cta, 0.0f);
-      }
+      lane_row_stats(tcol + lane_lo, nch, inv_cta, mean, m2);
       // ---- merge across the CTAs of the cluster (the row's columns are split over them)
       if (cs > 1) {
         const int par = grp;
@@ -559,6 +572,125 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int b = 0; b < 2; ++b)
         if ((rout >> b) & 1u) mbar_wait(&rbar[b], (rpar >> b) & 1u, 134);
     }
+  } else if constexpr (EPI == kEpiTB) {
+    // ---------------------------------------------------------------- epilogue, t-broadcast
+    // Tile rows are 128 tokens; the same LayerNorm output y drives the LIF at every step
+    // (u_t = beta (1 - s) u + y + s beta v_reset), so each lane keeps its token's membrane for a
+    // column pair in registers over T.  A 32-column chunk's spikes of all T steps are staged as a
+    // warp-private [t][32 tokens][32 columns] box (64-byte swizzle) and written by one TMA store.
+    // Two groups of four warps drain alternate tiles (accumulator g), as in the T = 4 epilogue.
+    static_assert(FAST && !RES, "t-broadcast epilogue: bf16 spikes only");
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int grp = ew >> 2;
+    const int nch = p.n_cta / 32;
+    const uint32_t lane_lo = (uint32_t)(q * 32) << 16;
+    const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+    const float2 beta2 = make_float2(beta, beta), nbeta2 = make_float2(-beta, -beta);
+    const float bvr = __fmul_rn(beta, vr);
+    const float2 bvr2 = make_float2(bvr, bvr);
+    const int n0 = (int)rank * p.n_cta;
+    const float inv_cta = 1.0f / (float)p.n_cta;
+    const float inv_n_all = 1.0f / (float)p.N;
+    const int nT = p.T;
+    uint8_t* const box = sm.stg + (size_t)ew * nT * 2048;
+    if (lane == 0) tma_prefetch_desc(&tmO);
+    int iter = grp;
+    for (int tile = cid + grp * ncl; tile < p.num_m_tiles; tile += 2 * ncl, iter += 2) {
+      const int buf = grp;
+      if (!mbar_wait(&sm.acc_full[buf], (uint32_t)(iter >> 1) & 1u, 141)) { atomicExch(sm.abort_flag, 1); break; }
+      tc_fence_after();
+      const uint32_t trow = tmem + (uint32_t)(buf * p.n_cta) + lane_lo;
+      float mean, m2;
+      lane_row_stats(trow, nch, inv_cta, mean, m2);
+      if (cs > 1) {
+        const int par = grp;
+        float2* xb = sm.xbuf + (size_t)par * cs * 128;
+        const int row = q * 32 + lane;
+        const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + row);
+        const uint32_t bar = smem_u32(&sm.xbar[par]);
+        for (int r = 0; r < cs; ++r)
+          st_async_f32x2(mapa_shared(slot, (uint32_t)r), mean, m2, mapa_shared(bar, (uint32_t)r));
+        if (ew == grp * 4 && lane == 0) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
+        if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 142)) {
+          atomicExch(sm.abort_flag, 1);
+          break;
+        }
+        float2 a = xb[row];
+        mean = a.x;
+        m2 = a.y;
+        for (int r = 1; r < cs; ++r) {
+          const float2 b = xb[(size_t)r * 128 + row];
+          chan_merge(mean, m2, b.x, b.y, sm.mw[r]);
+        }
+      }
+      const float rstd = rsqrtf(fmaf(m2, inv_n_all, p.eps));
+      const float2 r2 = make_float2(rstd, rstd);
+      const float2 nmr2 = make_float2(-mean * rstd, -mean * rstd);
+      const int y0 = tile * 128 + q * 32;  // first token of this warp's rows
+      // 8 columns (4 pairs; octet o of the chunk) of this lane's row: normalise, then LIF over
+      // every step, each step's 16 bytes into row t*32 + lane of the box
+      auto lif_oct = [&](const uint32_t* x, int col, int o) {
+        float2 y[4], u[4], sp[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 g2 = *reinterpret_cast<const float2*>(sm.gamma + col + 2 * i);
+          const float2 e2 = *reinterpret_cast<const float2*>(sm.beta + col + 2 * i);
+          y[i] = fma2(fma2(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), r2, nmr2), g2, e2);
+          u[i] = make_float2(0.0f, 0.0f);
+          sp[i] = u[i];
+        }
+#pragma unroll 1
+        for (int t = 0; t < nT; ++t) {
+          uint32_t bits[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // u = beta (1 - s) u + y + s beta v_reset; at t = 0 u and s are 0, so u = y
+            const float2 yy = fma2(sp[i], bvr2, y[i]);
+            u[i] = fma2(fma2(sp[i], nbeta2, beta2), u[i], yy);
+            sp[i] = make_float2(set_gt(u[i].x, vth), set_gt(u[i].y, vth));
+            bits[i] = bf16x2_of_01(sp[i].x, sp[i].y);
+          }
+          const int row = t * 32 + lane;
+          *reinterpret_cast<uint4*>(box + row * 64 + ((o ^ ((row >> 1) & 3)) << 4)) =
+              make_uint4(bits[0], bits[1], bits[2], bits[3]);
+        }
+      };
+      uint32_t ra[32], rb[32];
+      tmem_ld32_raw(trow, ra);
+      for (int c = 0; c < nch; ++c) {
+        if ((c & 1) == 0) {
+          tmem_wait_ld_fence32(ra);
+          if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, rb);
+        } else {
+          tmem_wait_ld_fence32(rb);
+          if (c + 1 < nch) tmem_ld32_raw(trow + (c + 1) * 32, ra);
+        }
+        if (c + 1 == nch) {
+          // last TMEM read of this buffer: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+        }
+        // the previous chunk's store must have read the box
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        if ((c & 1) == 0) {
+#pragma unroll
+          for (int o = 0; o < 4; ++o) lif_oct(ra + 8 * o, c * 32 + 8 * o, o);
+        } else {
+#pragma unroll
+          for (int o = 0; o < 4; ++o) lif_oct(rb + 8 * o, c * 32 + 8 * o, o);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (y0 < p.R) tma_store_3d(&tmO, box, n0 + c * 32, y0, 0);
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
   } else {
     // ---------------------------------------------------------------- epilogue
     const int ew = warp - 2;        // 0..7
@@ -1068,11 +1200,11 @@ using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMa
 
 template <int T>
 KernelFn pick_kernel(bool fast, bool res, bool tv) {
-  if (!fast) return gemm_il_kernel<T, false, true, false>;
+  if (!fast) return gemm_il_kernel<T, false, true, kEpiTranspose>;
   if constexpr (T == 4) {
-    if (tv) return res ? gemm_il_kernel<4, true, true, true> : gemm_il_kernel<4, true, false, true>;
+    if (tv) return res ? gemm_il_kernel<4, true, true, kEpiTV> : gemm_il_kernel<4, true, false, kEpiTV>;
   }
-  return res ? gemm_il_kernel<T, true, true, false> : gemm_il_kernel<T, true, false, false>;
+  return res ? gemm_il_kernel<T, true, true, kEpiTranspose> : gemm_il_kernel<T, true, false, kEpiTranspose>;
 }
 
 }  // namespace gil
@@ -1093,18 +1225,24 @@ bool gemm_il_split(int N, int* cs, int* n_cta) {
 }
 
 // Host launcher used by spk_linear_ln_lif_fwd for t-coupled rows with T in
-// {1, 2, 4, 8, 16}; returns SPK_ERR_UNSUPPORTED for shapes it does not cover.
+// {1, 2, 4, 8, 16}, and for t-broadcast rows (bf16 spikes, any T); returns
+// SPK_ERR_UNSUPPORTED for shapes it does not cover.
 int launch_gemm_il(const void* A, const void* W, const float* bias, const float* gamma, const float* beta_ln,
                    float eps, const float* lif_beta, const float* lif_vth, const float* lif_vr, float gain, int T,
-                   int64_t R, int K, int N, void* spk_bf16, float* spk_f32, void* residual, float* ln_out,
-                   cudaStream_t st) {
+                   int64_t R, int K, int N, int t_broadcast, void* spk_bf16, float* spk_f32, void* residual,
+                   float* ln_out, cudaStream_t st) {
   using namespace gil;
-  if (!(T == 1 || T == 2 || T == 4 || T == 8 || T == 16)) return SPK_ERR_UNSUPPORTED;
+  if (t_broadcast) {
+    if (T > 4 || spk_f32 || ln_out || residual || !spk_bf16 || N % 8 != 0 || !aligned(spk_bf16, 16))
+      return SPK_ERR_UNSUPPORTED;
+  } else if (!(T == 1 || T == 2 || T == 4 || T == 8 || T == 16)) {
+    return SPK_ERR_UNSUPPORTED;
+  }
   int cs = 1, n_cta = 0;
   if (!gemm_il_split(N, &cs, &n_cta)) return SPK_ERR_UNSUPPORTED;
   Params p = {};
   p.T = T;
-  p.tpt = 128 / T;
+  p.tpt = t_broadcast ? 128 : 128 / T;
   p.R = R;
   p.K = K;
   p.N = N;
@@ -1130,11 +1268,24 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   const bool res = residual != nullptr;
   // the transposed-read epilogue writes one bf16 output (spikes, or the residual stream) by TMA
   void* out = res ? residual : spk_bf16;
-  p.tv = T == 4 && fast && R % 8 == 0 && N % 8 == 0 && out != nullptr && !(res && spk_bf16) && aligned(out, 16);
+  const bool tv = !t_broadcast && T == 4 && fast && R % 8 == 0 && N % 8 == 0 && out != nullptr &&
+                  !(res && spk_bf16) && aligned(out, 16);
+  p.epi = t_broadcast ? kEpiTB : tv ? kEpiTV : kEpiTranspose;
 
   CUtensorMap tmA, tmW, tmO;
   int rc;
-  if (p.tv) {
+  if (t_broadcast) {
+    // dims {K, R}: the box {64, 128} is 128 tokens
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)R};
+    uint64_t strides[1] = {(uint64_t)K * 2};
+    uint32_t box[2] = {kBK, 128};
+    if ((rc = make_tmap_bf16(&tmA, A, 2, dims, strides, box, true)) != SPK_OK) return rc;
+    // spikes [T][R][N]: box {32 columns, 32 tokens, T} in the 64-byte swizzle
+    uint64_t odims[3] = {(uint64_t)N, (uint64_t)R, (uint64_t)T};
+    uint64_t ostrides[2] = {(uint64_t)N * 2, (uint64_t)R * N * 2};
+    uint32_t obox[3] = {32, 32, (uint32_t)T};
+    if ((rc = make_tmap_bf16_sw(&tmO, spk_bf16, 3, odims, ostrides, obox, 64)) != SPK_OK) return rc;
+  } else if (tv) {
     // dims {K, 8, T, R / 8}: the box {64, 8, 4, 4} lands as rows g*32 + t*8 + k, token 8g + k
     uint64_t dims[4] = {(uint64_t)K, 8, (uint64_t)T, (uint64_t)(R / 8)};
     uint64_t strides[3] = {(uint64_t)K * 2, (uint64_t)R * K * 2, (uint64_t)K * 16};
@@ -1166,12 +1317,16 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   }
   if (smem > (size_t)kMaxSmem) return fail(SPK_ERR_SHAPE, "tile of %d columns does not fit in shared memory", n_cta);
   KernelFn kern;
-  switch (T) {
-    case 1: kern = pick_kernel<1>(fast, res, false); break;
-    case 2: kern = pick_kernel<2>(fast, res, false); break;
-    case 4: kern = pick_kernel<4>(fast, res, p.tv != 0); break;
-    case 8: kern = pick_kernel<8>(fast, res, false); break;
-    default: kern = pick_kernel<16>(fast, res, false); break;
+  if (t_broadcast) {
+    kern = gemm_il_kernel<1, true, false, kEpiTB>;  // T is read from the parameters
+  } else {
+    switch (T) {
+      case 1: kern = pick_kernel<1>(fast, res, false); break;
+      case 2: kern = pick_kernel<2>(fast, res, false); break;
+      case 4: kern = pick_kernel<4>(fast, res, tv); break;
+      case 8: kern = pick_kernel<8>(fast, res, false); break;
+      default: kern = pick_kernel<16>(fast, res, false); break;
+    }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));

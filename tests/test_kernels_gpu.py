@@ -199,6 +199,24 @@ def test_linear_ln_lif_t4_transposed_epilogue(ops, R, K, N, gain, vr, res):
     assert_spikes_match(s.reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
 
 
+@pytest.mark.parametrize("T,R,K,N,gain,vr", [
+    (4, 300, 512, 384, 1.0, 0.0),    # patch embedding (split-bf16 pixels, K = 2 x 256)
+    (4, 200, 256, 1536, 0.5, 0.0),   # 6-CTA cluster, last tile partial
+    (3, 129, 128, 128, 0.7, 0.1),    # T not a power of two, non-zero reset
+    (1, 64, 64, 64, 1.0, 0.0),
+    (8, 150, 192, 512, 0.5, -0.25),
+])
+def test_linear_ln_lif_t_broadcast_bf16(ops, T, R, K, N, gain, vr):
+    """t-broadcast rows with bf16 spikes: one pre-activation per token drives
+    the LIF at every step (the patch-embedding path)."""
+    A, W, bias, gamma, beta_ln = make_lin(T * 3 + R + K + N, R, K, N, T, t_broadcast=True)
+    s_ref, _, vh = ref_linear_ln_lif(A, W, bias, gamma, beta_ln, T, 0.9, 1.0, vr, gain=gain, t_broadcast=True)
+    s, y = ops.linear_ln_lif(A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.9, 1.0, vr,
+                             T, in_gain=gain, t_broadcast=True, spike_dtype=torch.bfloat16)
+    assert y is None and s.shape == (T * R, N)
+    assert_spikes_match(s.float().cpu().reshape(T, -1), s_ref.reshape(T, -1), vh, 1.0, what="spikes")
+
+
 def test_linear_ln_lif_cfg2_tau(ops):
     # fused Linear->LN->LIF at the cfg-2 feature sizes (tau=2 neuron), fewer rows
     T, R, K, N = 4, 2048, 384, 1536
