@@ -432,3 +432,26 @@ class Seq2Seq(nn.Module):
         y = self.decoder(y, enc_output, mask=look_ahead_mask)
         out = self.output_layer(y)
         return out.view(T, out.shape[0] // T, out.shape[1], out.shape[2]), None
+
+    # Seq2Seq.py:121-134: keep = 1, pad = 0; the look-ahead mask combined with the key padding
+    def create_decoder_mask(self, tgt, pad_idx, device):
+        look_ahead = torch.tril(torch.ones((tgt.shape[1], tgt.shape[1]), device=device))
+        pad = torch.where(tgt == pad_idx, 0.0, 1.0).unsqueeze(1).unsqueeze(1).to(device)
+        return torch.minimum(pad, look_ahead)
+
+    @torch.no_grad()
+    def greedy_decode(self, src, max_len, start_symbol, eos_idx, pad_idx, device="cpu"):
+        """Seq2Seq.py:136-162: decode the whole prefix every step, append the
+        argmax of the T-averaged logits of the last position, stop at eos."""
+        if src.dim() == 3:
+            src = src.unsqueeze(0)
+        memory, _ = self.encode(src.to(device))
+        ys = torch.full((1, 1), fill_value=start_symbol, dtype=torch.long, device=device)
+        out = None
+        for _ in range(max_len - 1):
+            out, _ = self.decode(ys, memory, self.create_decoder_mask(ys, pad_idx, device))
+            nxt = int(torch.argmax(out.mean(dim=0)[:, -1, :], dim=-1))
+            ys = torch.cat([ys, torch.tensor([[nxt]], dtype=torch.long, device=device)], dim=1)
+            if nxt == eos_idx:
+                break
+        return ys, None, out

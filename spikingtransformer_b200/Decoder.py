@@ -23,10 +23,11 @@ class DecoderLayer(nn.Module):
                                                  n_steps=n_steps)
         self.mlp = SpikingMLP(d_model=d_model, ff_dim=ff_dim, n_steps=n_steps)
 
-    def _fast(self, x, enc, mask=None):
-        """In place on the bf16 residual stream ``x``; ``enc`` bf16 encoder output."""
+    def _fast(self, x, enc, mask=None, cross_kv=None):
+        """In place on the bf16 residual stream ``x``; ``enc`` bf16 encoder output;
+        ``cross_kv``: the cross-attention's (K, V) spikes of ``enc``, if cached."""
         self.self_attns._fast(x, None, mask)
-        self.cross_attns._fast(x, enc, None)
+        self.cross_attns._fast(x, enc, None, kv_spikes=cross_kv)
         self.mlp._fast(x)
         return x
 
@@ -46,9 +47,13 @@ class Decoder(nn.Module):
             DecoderLayer(d_model=d_model, n_heads=n_heads, ff_dim=ff_dim, dropout=dropout, alpha=alpha,
                          n_steps=n_steps) for _ in range(num_layers)])
 
-    def _fast(self, x, enc, mask=None):
-        for layer in self.layers:
-            layer._fast(x, enc, mask)
+    def cross_key_values(self, enc):
+        """Per layer, the cross-attention (K, V) spikes of the bf16 encoder output."""
+        return [layer.cross_attns.key_value_spikes(enc) for layer in self.layers]
+
+    def _fast(self, x, enc, mask=None, cross_kv=None):
+        for i, layer in enumerate(self.layers):
+            layer._fast(x, enc, mask, None if cross_kv is None else cross_kv[i])
         return x
 
     def forward(self, x, enc_output, mask=None):

@@ -65,19 +65,28 @@ class _SSACore(nn.Module):
                          out_dtype=out_dtype)
         return out
 
-    def _fast(self, x, kv=None, mask=None):
+    def key_value_spikes(self, src):
+        """K and V spikes (bf16 [T*B, Nk, D]) of a bf16 key/value source; a
+        cross-attention over a fixed source (the encoder output during
+        decoding) can compute them once and pass them to ``_fast``."""
+        T = self.lifq.n_steps
+        TB, Nk, D = src.shape
+        k = lin_ln_lif(src, self.k_proj, self.lnk, self.lifk, T)[0].view(TB, Nk, D)
+        v = lin_ln_lif(src, self.v_proj, self.lnv, self.lifv, T)[0].view(TB, Nk, D)
+        return k, v
+
+    def _fast(self, x, kv=None, mask=None, kv_spikes=None):
         """Residual step on bf16 spike counts: ``x += SSA(x, kv, kv)`` in place.
 
         ``x``: [T*B, Nq, D] bf16; ``kv``: [T*B, Nk, D] bf16 or None (self);
-        ``mask``: None, "causal", or a mask accepted by ``ops.ssa``.
+        ``mask``: None, "causal", or a mask accepted by ``ops.ssa``;
+        ``kv_spikes``: (K, V) from ``key_value_spikes(kv)``, used instead of
+        projecting ``kv`` again.
         """
         T = self.lifq.n_steps
         TB, Nq, D = x.shape
-        src = x if kv is None else kv
-        Nk = src.shape[1]
         q = lin_ln_lif(x, self.q_proj, self.lnq, self.lifq, T)[0].view(TB, Nq, D)
-        k = lin_ln_lif(src, self.k_proj, self.lnk, self.lifk, T)[0].view(TB, Nk, D)
-        v = lin_ln_lif(src, self.v_proj, self.lnv, self.lifv, T)[0].view(TB, Nk, D)
+        k, v = self.key_value_spikes(x if kv is None else kv) if kv_spikes is None else kv_spikes
         a = self._attend(q, k, v, T, mask)
         lin_ln_lif(a, self.out_proj, self.lno, self.lifo, T, residual=x.view(-1, D), want_spikes=False)
         return x

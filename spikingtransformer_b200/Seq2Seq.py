@@ -108,7 +108,7 @@ class Seq2Seq(nn.Module):
             x = self.image_encoder(src_t)[0].to(torch.bfloat16).contiguous()
         return self.encoder._fast(x)
 
-    def _decode_fast(self, tgt, enc, look_ahead_mask):
+    def _decode_fast(self, tgt, enc, look_ahead_mask, cross_kv=None):
         T = self.n_steps
         emb = self.tgt_tok_emb
         p = lif_params(self.lifPE)
@@ -120,7 +120,7 @@ class Seq2Seq(nn.Module):
             B, N = tgt.shape
             H = self.decoder.layers[0].self_attns.n_heads if len(self.decoder.layers) else 1
             mask = ops.mask_to_u8(look_ahead_mask, T, B, H, N, N)
-        self.decoder._fast(y, enc, mask)
+        self.decoder._fast(y, enc, mask, cross_kv)
         D = y.shape[-1]
         logits = ops.linear(y.view(-1, D), bf16_weight(self.output_layer), self.output_layer.bias)
         return logits.view(T, -1, tgt.shape[1], logits.shape[-1])
@@ -176,19 +176,78 @@ class Seq2Seq(nn.Module):
     def greedy_decode(self, src: Tensor, max_len: int, start_symbol: int, eos_idx: int, pad_idx: int,
                       device: str = "cuda"):
         """Greedy decoding as ``Seq2Seq.py:136-162``: re-decodes the prefix each
-        step, picks argmax of the T-averaged logits of the last position."""
+        step, picks argmax of the T-averaged logits of the last position.
+
+        The whole prefix is decoded every step because the self-attention's
+        log-distance bias is normalised by the current length, so earlier
+        positions change as the sequence grows.  On the fused path the
+        cross-attention K/V spikes of the fixed encoder output are computed
+        once and reused by every step (the same values each step would
+        compute)."""
         if src.dim() == 3:
             src = src.unsqueeze(0)
         src = src.to(device)
-        memory, attention_rec = self.encode(src)
+        fast = self._fast_ok(src)
+        if fast:
+            enc = self._encode_fast(src)
+            cross_kv = self.decoder.cross_key_values(enc)
+            attention_rec = None
+        else:
+            memory, attention_rec = self.encode(src)
         ys = torch.full((1, 1), fill_value=start_symbol, dtype=torch.long, device=device)
         out = None
         for _ in range(max_len - 1):
             tgt_mask = self.create_decoder_mask(ys, pad_idx, device)
-            out, _ = self.decode(ys, memory, tgt_mask)
+            if fast:
+                out = self._decode_fast(ys, enc, tgt_mask, cross_kv)
+            else:
+                out, _ = self.decode(ys, memory, tgt_mask)
             prob = out.mean(dim=0)
             next_token_id = torch.argmax(prob[:, -1, :], dim=-1).item()
             ys = torch.cat([ys, torch.tensor([[next_token_id]], device=device, dtype=torch.long)], dim=1)
             if next_token_id == eos_idx:
                 break
         return ys, attention_rec, out
+
+    @torch.no_grad()
+    def greedy_decode_batch(self, src: Tensor, max_len: int, start_symbol: int, eos_idx: int, pad_idx: int,
+                            device: str = "cuda"):
+        """Greedy decoding of a batch of images ``src`` [B, C, H, W] in one
+        pass per step.
+
+        Every operation is per image and all sequences share the current
+        length, so row b of the result is exactly what ``greedy_decode``
+        returns for image b alone.  Decoding continues until every row has
+        produced ``eos_idx`` (or ``max_len`` tokens); positions after a row's
+        eos are set to ``pad_idx``.  Returns ``(ys [B, L], lengths [B])``,
+        ``lengths`` counting the start symbol and the eos.
+        """
+        if src.dim() == 3:
+            src = src.unsqueeze(0)
+        src = src.to(device)
+        B = src.shape[0]
+        fast = self._fast_ok(src)
+        if fast:
+            enc = self._encode_fast(src)
+            cross_kv = self.decoder.cross_key_values(enc)
+        else:
+            memory, _ = self.encode(src)
+        ys = torch.full((B, 1), fill_value=start_symbol, dtype=torch.long, device=device)
+        done = torch.zeros(B, dtype=torch.bool, device=device)
+        lengths = torch.full((B,), max_len, dtype=torch.long, device=device)
+        for n in range(1, max_len):
+            tgt_mask = self.create_decoder_mask(ys, pad_idx, device)
+            if fast:
+                out = self._decode_fast(ys, enc, tgt_mask, cross_kv)
+            else:
+                out, _ = self.decode(ys, memory, tgt_mask)
+            nxt = torch.argmax(out.mean(dim=0)[:, -1, :], dim=-1)
+            hit = (nxt == eos_idx) & ~done
+            lengths = torch.where(hit, torch.full_like(lengths, n + 1), lengths)
+            ys = torch.cat([ys, nxt.unsqueeze(1)], dim=1)
+            done = done | hit
+            if bool(done.all()):
+                break
+        pos = torch.arange(ys.shape[1], device=device).unsqueeze(0)
+        ys = torch.where(pos < lengths.clamp(max=ys.shape[1]).unsqueeze(1), ys, torch.full_like(ys, pad_idx))
+        return ys, lengths.clamp(max=ys.shape[1])

@@ -237,6 +237,54 @@ def test_greedy_decode(pkg):
     assert out.shape[0] == 4
 
 
+def test_cached_cross_kv_decode_is_exact(pkg):
+    """The decoder with the cross-attention K/V spikes computed once gives the
+    logits of the decoder that projects the encoder output every call."""
+    ours, _ = _bench_models(enc_layers=1, dec_layers=2)
+    with torch.no_grad():
+        src = synthetic_lines(2, 11).to(DEV)
+        enc = ours._encode_fast(src)
+        cross_kv = ours.decoder.cross_key_values(enc)
+        tgt = torch.randint(0, 256, (2, 9), device=DEV, generator=torch.Generator(device=DEV).manual_seed(3))
+        mask = ours.create_decoder_mask(tgt, 0, DEV)
+        a = ours._decode_fast(tgt, enc, mask)
+        b = ours._decode_fast(tgt, enc, mask, cross_kv)
+    assert torch.equal(a, b)
+
+
+def test_greedy_decode_batch_matches_single_image(pkg):
+    """Row b of the batched greedy decode is what greedy_decode returns for
+    image b alone, with an eos that stops one row early."""
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    B, L = 3, 7
+    src = synthetic_lines(B, 12)
+    singles = [ours.greedy_decode(src[b], max_len=L, start_symbol=1, eos_idx=-1, pad_idx=0, device=DEV)[0]
+               for b in range(B)]
+    eos = int(singles[0][0, 2])  # the token image 0 emits second: it stops there
+    singles = [ours.greedy_decode(src[b], max_len=L, start_symbol=1, eos_idx=eos, pad_idx=0, device=DEV)[0]
+               for b in range(B)]
+    ys, lengths = ours.greedy_decode_batch(src, max_len=L, start_symbol=1, eos_idx=eos, pad_idx=0, device=DEV)
+    assert ys.shape[0] == B
+    for b in range(B):
+        n = singles[b].shape[1]
+        assert int(lengths[b]) == n
+        assert torch.equal(ys[b, :n], singles[b][0])
+        assert bool((ys[b, n:] == 0).all())
+    assert int(lengths[0]) == 3
+
+
+def test_greedy_decode_matches_oracle(pkg):
+    """Token sequence of the fused greedy decode against the CPU oracle's on a
+    small model."""
+    ours, ref = _bench_models(enc_layers=1, dec_layers=1)
+    src = synthetic_lines(1, 13)[0]
+    ys, _, out = ours.greedy_decode(src, max_len=5, start_symbol=1, eos_idx=-1, pad_idx=0, device=DEV)
+    ys_ref, _, out_ref = ref.greedy_decode(src, max_len=5, start_symbol=1, eos_idx=-1, pad_idx=0, device="cpu")
+    assert torch.equal(ys.cpu(), ys_ref)
+    close = torch.isclose(out.cpu(), out_ref, rtol=1e-3, atol=1e-3).float().mean().item()
+    assert close > 0.9, close
+
+
 def test_stream_forward_matches_direct_forward(pkg):
     """Host batches streamed with overlapped copies give the logits of a
     direct forward of each batch, bit for bit, including a host buffer reused
