@@ -51,9 +51,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="forward", choices=["forward", "train"],
-                    help="forward: the OCR seq2seq forward (default); train: one DDP training step per step")
-    ap.add_argument("--batch", type=int, default=None, help="images per GPU (forward 256, train 64)")
+    ap.add_argument("--workload", default="forward", choices=["forward", "train", "decode"],
+                    help="forward: the OCR seq2seq forward (default); train: one DDP training step per step; "
+                         "decode: batched greedy decoding of 64 tokens per image")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (forward 256, train 64, decode 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -323,6 +324,78 @@ def run_train(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+def run_decode(args, ws, rank, local):
+    """--workload decode: greedy decoding (``Seq2Seq.py:136-162``) of a batch of
+    images per GPU, 64 tokens each (no eos, so every image runs all steps),
+    through ``greedy_decode_batch``; beside it the per-image ``greedy_decode``
+    loop of the reference's API on a few images of the same batch."""
+    import datetime
+    import torch.distributed as dist
+    from spikingtransformer_b200 import _lib
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _lib.load()
+    torch.manual_seed(0)
+    model = Seq2Seq(**ARCH)
+    round_weights_bf16(model)
+    model = model.to(dev).eval()
+    B = args.batch or 64
+    max_len = SEQ + 1
+    src, _, _ = make_inputs(B, shard_seed(rank, 0))
+    src = src.to(dev)
+
+    def batch_decode():
+        return model.greedy_decode_batch(src, max_len=max_len, start_symbol=1, eos_idx=-1, pad_idx=0, device=dev)
+
+    for _ in range(max(1, args.warmup)):
+        ys, _ = batch_decode()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps // 4)
+    with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+        e0.record()
+        for _ in range(steps):
+            ys, _ = batch_decode()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dev) / steps
+    kernels = rec.summary()
+    # the reference API: one image at a time
+    n_single = 2
+    model.greedy_decode(src[0], max_len=max_len, start_symbol=1, eos_idx=-1, pad_idx=0, device=dev)
+    torch.cuda.synchronize()
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for b in range(n_single):
+        y1, _, _ = model.greedy_decode(src[b], max_len=max_len, start_symbol=1, eos_idx=-1, pad_idx=0, device=dev)
+    s1.record()
+    torch.cuda.synchronize()
+    single_ms = s0.elapsed_time(s1) / n_single
+    assert torch.equal(y1[0], ys[n_single - 1]), "batched and single-image decodes differ"
+    if rank == 0:
+        print(json.dumps({
+            "metric": "ocr_greedy_decode_images_per_sec", "value": ws * B / (ms / 1000.0), "unit": UNIT,
+            "n_gpus": ws, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "ocr_greedy_decode", "per_gpu_batch": B, "tokens_per_image": max_len - 1,
+                       "image": list(IMG), "T": 4, "layers": "8 enc + 4 dec",
+                       "parallelism": "dp%d (batch-sharded, no collective)" % ws},
+            "single_image_decode": {"ms_per_image": single_ms, "images_per_sec": 1000.0 / single_ms,
+                                    "api": "greedy_decode, one image per call"},
+            "clocks": clk.summary(), "gpu_launches": sum(v["launches"] for v in kernels.values()) // steps,
+        }), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
@@ -331,6 +404,9 @@ def main():
         return
     if args.workload == "train":
         run_train(args, ws, rank, local)
+        return
+    if args.workload == "decode":
+        run_decode(args, ws, rank, local)
         return
     if args.batch is None:
         args.batch = 256
