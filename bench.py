@@ -164,11 +164,14 @@ class ClockSampler:
 # the same launch shape; profiles/dram_traffic_b256_shapes.md) of the kernels that can be
 # the dominant one of the 256-image forward
 NCU_TRAFFIC = {
-    "linear_ln_lif K=384 N=384 rows=262144": 354.0e6,
-    "linear_ln_lif K=384 N=384 rows=262144 +residual": 553.6e6,
-    "linear_ln_lif K=384 N=1536 rows=262144": 950.7e6,
-    "linear_ln_lif K=1536 N=384 rows=262144 +residual": 1185.5e6,
-    "ssa Nq=256 Nk=256": 779.1e6,
+    "linear_ln_lif K=384 N=384 rows=262144": 355.2e6,
+    "linear_ln_lif K=384 N=384 rows=262144 +residual": 558.5e6,
+    "linear_ln_lif K=384 N=1536 rows=262144": 950.6e6,
+    "linear_ln_lif K=1536 N=384 rows=262144 +residual": 1212.4e6,
+    "linear_ln_lif K=512 N=384 rows=65536": 211.3e6,
+    "ssa Nq=256 Nk=256": 774.4e6,
+    "ssa Nq=64 Nk=256": 493.4e6,
+    "ssa Nq=64 Nk=64": 173.4e6,
 }
 
 

@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks at the benchmark shapes (CUDA events, device time).
 
-    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa] [--iters N]
+    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|shapes] [--iters N]
 
   lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 spikes (the MLP
         expansion LIF of a 64-image batch); bound: HBM bytes.
@@ -91,12 +91,61 @@ def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48):
             "shape": [T, B, H, N, d], "ms": ms, "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops}
 
 
+def bench_shapes_once():
+    """Each fused launch shape of the 256-image forward, twice, untimed (a
+    short program for per-launch DRAM captures with ncu).  Order: q/k/v,
+    out_proj + residual, expand, compress + residual (encoder rows 4 x 256 x
+    256), patch embedding (t-broadcast), encoder self-attention, decoder
+    cross-attention, decoder causal self-attention."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    T, R, D = 4, 256 * 256, 384
+    spk = lambda *shape: (torch.rand(*shape, device="cuda", generator=g) < 0.15).to(torch.bfloat16)  # noqa: E731
+    w = lambda n, k: ((torch.rand(n, k, device="cuda", generator=g) * 2 - 1) / k ** 0.5).to(torch.bfloat16)  # noqa
+    ones = lambda n: torch.ones(n, device="cuda")  # noqa: E731
+    zeros = lambda n: torch.zeros(n, device="cuda")  # noqa: E731
+    A384, A1536 = spk(T * R, D), spk(T * R, 4 * D)
+    W = {(384, 384): w(384, 384), (1536, 384): w(1536, 384), (384, 1536): w(384, 1536), (384, 512): w(384, 512)}
+    res = torch.zeros(T * R, D, dtype=torch.bfloat16, device="cuda")
+    patches = (torch.rand(R, 512, device="cuda", generator=g) * 0.2).to(torch.bfloat16)
+    lif = (0.5, 1.0, 0.0)
+    for _ in range(2):
+        ops.linear_ln_lif(A384, W[(384, 384)], zeros(384), ones(384), zeros(384), 1e-5, *lif, T, in_gain=0.5)
+    for _ in range(2):
+        ops.linear_ln_lif(A384, W[(384, 384)], zeros(384), ones(384), zeros(384), 1e-5, *lif, T, in_gain=0.5,
+                          residual=res, want_spikes=False)
+    for _ in range(2):
+        ops.linear_ln_lif(A384, W[(1536, 384)], zeros(1536), ones(1536), zeros(1536), 1e-5, *lif, T, in_gain=0.5)
+    for _ in range(2):
+        ops.linear_ln_lif(A1536, W[(384, 1536)], zeros(384), ones(384), zeros(384), 1e-5, *lif, T, in_gain=0.5,
+                          residual=res, want_spikes=False)
+    for _ in range(2):
+        ops.linear_ln_lif(patches, W[(384, 512)], zeros(384), ones(384), zeros(384), 1e-5, *lif, T,
+                          t_broadcast=True)
+    del A1536
+    B, H = 256, 8
+    q, k, v = spk(T * B, 256, D), spk(T * B, 256, D), spk(T * B, 256, D)
+    for _ in range(2):
+        ops.ssa(q, k, v, T, B, H, 1, 0.125, 0.5, 0.5, 0.0, in_gain=0.5)
+    qd = spk(T * B, 64, D)
+    for _ in range(2):
+        ops.ssa(qd, k, v, T, B, H, 1, 0.125, 0.5, 0.5, 0.0, in_gain=0.5)
+    kd, vd = spk(T * B, 64, D), spk(T * B, 64, D)
+    for _ in range(2):
+        ops.ssa(qd, kd, vd, T, B, H, 1, 0.125, 0.5, 0.5, 0.0, in_gain=0.5, causal=True)
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa"])
+    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "shapes"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
     a = ap.parse_args()
+    if a.only == "shapes":
+        bench_shapes_once()
+        ops.device_error_check()
+        print(json.dumps({"shapes": "done"}))
+        return
     peaks, src = _peaks()
     out = {"peaks": {"hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained"),
                      "source": src}, "results": []}
