@@ -175,11 +175,23 @@ class SSAMultiHeadAttention(_SSACore):
         return torch.ceil(torch.log2((L - 1) / (dist + 1))).clamp(min=0)
 
     def _combine(self, q, k, v, mask):
-        a = self.xnor_attention(q, k)
-        a = a + self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device).unsqueeze(0).unsqueeze(0)
         if mask is not None:
-            a = a * mask
-        return (a * self.scale) @ v
+            a = self.xnor_attention(q, k)
+            a = a + self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device).unsqueeze(0).unsqueeze(0)
+            return (a * mask * self.scale) @ v
+        # Without a mask the score matrix regroups exactly (spikes are 0/1):
+        #   S V = 2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V,  s_j = |k_j|,
+        # so neither S nor its gradient is formed.  fp32 matmuls keep every
+        # integer term exact (sums below 2^24), whatever the autocast state.
+        dh = q.shape[-1]
+        with torch.autocast(q.device.type, enabled=False):
+            qf, kf, vf = q.float(), k.float(), v.float()
+            R = self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device)
+            m = 2.0 * (qf @ (kf.transpose(-2, -1) @ vf))
+            m = m + (dh - qf.sum(-1, keepdim=True)) * vf.sum(-2, keepdim=True)
+            m = m - kf.sum(-1).unsqueeze(-2) @ vf
+            m = m + R @ vf
+            return m * self.scale
 
 
 class SSAMultiHeadAttention_(_SSACore):
