@@ -33,6 +33,14 @@
  *   spk_patch_im2col       patch gather of the 16x16 patch-embedding image
  *                          encoder (no reference counterpart; the OCR
  *                          benchmark's ImageEncoder)
+ *   spk_synth_text_lines   on-device synthetic text-line batch (stands in for
+ *                          the rendered lines of wiki_text_images3.py:173-236
+ *                          and the DataLoader of train_spikeformer.py)
+ *   spk_ce_over_t          the training loss and token accuracy,
+ *                          train_spikeformer.py:309-323 (step_loss with
+ *                          CrossEntropyLoss(ignore_index, label_smoothing),
+ *                          :269) and :84-93 (compute_token_accuracy of the
+ *                          T-averaged logits, :556-559)
  */
 #ifndef SPK_H_
 #define SPK_H_
@@ -223,6 +231,31 @@ int spk_embed_pe_lif_fwd(const int64_t* tokens, const float* emb, float emb_scal
  */
 int spk_patch_im2col(const float* img, int64_t B, int64_t C, int64_t H, int64_t W, int64_t patch, void* out,
                      void* stream);
+
+/*
+ * img: [B][1][H][W] fp32 <- U(0, 0.2) background with 5-40 black (0.0)
+ * rectangles of side 8-20 px per image; tokens (optional, else NULL):
+ * [B][L] int64 uniform in [0, V).  Every value is a function of (seed,
+ * image, draw) through a counter-based hash (SplitMix64), so batches are
+ * reproducible on any GPU and on the CPU.  H, W >= 20.
+ */
+int spk_synth_text_lines(float* img, int64_t B, int64_t H, int64_t W, uint64_t seed, int64_t* tokens, int64_t L,
+                         int64_t V, void* stream);
+
+/*
+ * logits: [T][rows][V] (dtype SPK_F32 or SPK_BF16); targets: [rows] int64.
+ * out[0] = mean over t of CrossEntropyLoss(ignore_index, label_smoothing) of
+ * step t (mean over non-ignored rows), out[1] = token accuracy of the argmax
+ * of the T-averaged logits over non-ignored rows, out[2] = 1 / max(1, number
+ * of non-ignored rows).  grad (optional, else NULL; logits' dtype and shape)
+ * <- dloss/dlogits divided by out[2]'s reciprocal, i.e. the caller multiplies
+ * grad by out[2].  workspace: spk_ce_over_t_workspace_bytes(rows) bytes.
+ * bad_target: device int set to 1 if a non-ignored target is outside [0, V).
+ */
+int64_t spk_ce_over_t_workspace_bytes(int64_t rows);
+int spk_ce_over_t(const void* logits, int dtype, const int64_t* targets, int64_t T, int64_t rows, int64_t V,
+                  int64_t ignore_index, float label_smoothing, float* out, void* grad, void* workspace,
+                  int64_t workspace_bytes, int* bad_target, void* stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,9 @@ SIGNATURES = {
                      _i64, _i64, _p, _i, _p, _p], _i),
     "spk_embed_pe_lif_fwd": ([_p, _p, _f, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),
     "spk_patch_im2col": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _p], _i),
+    "spk_synth_text_lines": ([_p, _i64, _i64, _i64, ctypes.c_uint64, _p, _i64, _i64, _p], _i),
+    "spk_ce_over_t_workspace_bytes": ([_i64], _i64),
+    "spk_ce_over_t": ([_p, _i, _p, _i64, _i64, _i64, _i64, _f, _p, _p, _p, _i64, _p, _p], _i),
 }
 
 _lib = None

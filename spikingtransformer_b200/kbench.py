@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks at the benchmark shapes (CUDA events, device time).
 
-    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|shapes] [--iters N]
+    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|data|shapes] [--iters N]
 
   lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 spikes (the MLP
         expansion LIF of a 64-image batch); bound: HBM bytes.
@@ -91,6 +91,29 @@ def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48):
             "shape": [T, B, H, N, d], "ms": ms, "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops}
 
 
+def bench_data(iters):
+    """The on-device batch generator (256 images [1, 64, 1024] + 64 targets
+    each) and the fused loss at the training shape (T=4, 64 images x 64
+    positions, vocab 256; forward and gradient); bound: HBM bytes."""
+    out = []
+    ms = _time(lambda i: ops.synth_text_lines(256, 1000 + i, H=64, W=1024, L=64, V=256), iters)
+    nbytes = 256 * 64 * 1024 * 4 + 256 * 64 * 8
+    out.append({"kernel": "synth_text_lines", "shape": [256, 1, 64, 1024], "ms": ms, "GB/s": nbytes / ms / 1e6,
+                "images/s": 256 / ms * 1e3, "bytes": nbytes})
+    g = torch.Generator(device="cuda").manual_seed(5)
+    logits = [torch.randn(4, 64, 64, 256, device="cuda", generator=g).requires_grad_(True) for _ in range(2)]
+    tgt = torch.randint(0, 256, (64, 64), device="cuda", generator=g)
+
+    def run(i):
+        loss, _, _ = ops.ce_over_t(logits[i % 2], tgt, ignore_index=0, label_smoothing=0.1)
+        loss.backward()
+    ms = _time(run, iters)
+    nbytes = 2 * logits[0].numel() * 4 * 2  # logits read, gradient written, gradient accumulated
+    out.append({"kernel": "ce_over_t (+backward)", "shape": [4, 64, 64, 256], "ms": ms, "GB/s": nbytes / ms / 1e6,
+                "bytes": nbytes})
+    return out
+
+
 def bench_shapes_once():
     """Each fused launch shape of the 256-image forward, twice, untimed (a
     short program for per-launch DRAM captures with ncu).  Order: q/k/v,
@@ -137,7 +160,7 @@ def bench_shapes_once():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "shapes"])
+    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "data", "shapes"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
     a = ap.parse_args()
@@ -162,6 +185,10 @@ def main():
         for variant in (0, 1):
             out["results"].append(bench_ssa(a.iters, variant))
         out["results"].append(bench_ssa(a.iters, 0, N=64, causal=True))
+    if a.only in (None, "data"):
+        for r in bench_data(a.iters):
+            r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
+            out["results"].append(r)
     ops.device_error_check()
     print(json.dumps(out))
 

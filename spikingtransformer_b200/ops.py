@@ -274,6 +274,66 @@ def patch_im2col(img, patch):
     return out
 
 
+def synth_text_lines(B, seed, H=64, W=1024, L=None, V=256, device="cuda"):
+    """On-device synthetic text-line batch: images ``[B, 1, H, W]`` fp32
+    (U(0, 0.2) background, 5-40 black rectangles of side 8-20 px each) and,
+    with ``L``, byte targets ``[B, L]`` int64 in ``[0, V)``; a function of
+    ``seed`` only (counter-based hash), reproducible on the CPU."""
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise RuntimeError("synth_text_lines runs on a CUDA device")
+    img = torch.empty((B, 1, H, W), dtype=torch.float32, device=dev)
+    tok = torch.empty((B, L), dtype=torch.int64, device=dev) if L else None
+    _lib.call("spk_synth_text_lines", _lib.ptr(img), B, H, W, int(seed) & 0xFFFFFFFFFFFFFFFF, _lib.ptr(tok),
+              int(L or 0), V, _lib.stream_ptr(dev), tag="synth_text_lines",
+              work=dict(bytes=img.numel() * 4 + (tok.numel() * 8 if tok is not None else 0)))
+    return img, tok
+
+
+class _CEOverT(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, targets, ignore_index, label_smoothing, bad):
+        T, V = logits.shape[0], logits.shape[-1]
+        rows = logits[0].numel() // V
+        dev = logits.device
+        out = torch.empty(3, dtype=torch.float32, device=dev)
+        grad = torch.empty_like(logits) if ctx.needs_input_grad[0] else None
+        ws = torch.empty(int(_lib.load().spk_ce_over_t_workspace_bytes(rows)), dtype=torch.uint8, device=dev)
+        _lib.call("spk_ce_over_t", _lib.ptr(logits), _lib.DTYPE_CODE[logits.dtype], _lib.ptr(targets), T, rows, V,
+                  int(ignore_index), float(label_smoothing), _lib.ptr(out), _lib.ptr(grad), _lib.ptr(ws), ws.numel(),
+                  _lib.ptr(bad), _lib.stream_ptr(dev), tag="ce_over_t",
+                  work=dict(bytes=logits.numel() * logits.element_size() * (2 if grad is not None else 1)))
+        ctx.save_for_backward(grad, out)
+        loss, acc = out[0], out[1]
+        ctx.mark_non_differentiable(acc)
+        return loss, acc
+
+    @staticmethod
+    def backward(ctx, g_loss, g_acc):
+        grad, out = ctx.saved_tensors
+        return grad * (g_loss * out[2]).to(grad.dtype), None, None, None, None
+
+
+def ce_over_t(logits, targets, ignore_index=-100, label_smoothing=0.0):
+    """Training loss and metric of the OCR seq2seq in one pass: the mean over
+    the T steps of ``CrossEntropyLoss(ignore_index, label_smoothing)`` of each
+    step's logits, and the token accuracy of the argmax of the T-averaged
+    logits over non-ignored targets.  ``logits``: ``[T, ..., V]`` fp32 or
+    bf16; ``targets``: ``[...]`` int64.  Returns ``(loss, accuracy, bad)``;
+    ``loss`` is differentiable, ``bad`` a device flag set by out-of-range
+    targets."""
+    _cuda(logits, targets)
+    if logits.dtype not in (torch.float32, torch.bfloat16):
+        logits = logits.float()
+    logits = logits.contiguous()
+    targets = targets.to(torch.int64).contiguous()
+    if targets.numel() * logits.shape[-1] * logits.shape[0] != logits.numel():
+        raise RuntimeError("targets %s do not match logits %s" % (tuple(targets.shape), tuple(logits.shape)))
+    bad = torch.zeros(1, dtype=torch.int32, device=logits.device)
+    loss, acc = _CEOverT.apply(logits, targets, ignore_index, label_smoothing, bad)
+    return loss, acc, bad
+
+
 def device_error_check(device=None):
     """Synchronise and raise if a kernel's bounded wait gave up."""
     _lib.call("spk_device_error_check", _lib.stream_ptr(device))
