@@ -569,3 +569,27 @@ __device__ __forceinline__ void bulk_wait() {
 }
 
 }  // namespace spk
+
+namespace spk {
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may be scheduled before the previous
+// kernel in the stream has finished.  pdl_wait() blocks until that grid has completed and its
+// memory is visible; every CTA calls it before reading anything an earlier kernel wrote, so the
+// completion of a grid implies the completion of all earlier ones.  Without the launch
+// attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// lets the next kernel in the stream be scheduled once every CTA of this grid has issued it
+// (or exited); its CTAs then take SMs as this grid's CTAs leave them
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// adds programmatic stream serialisation to a launch configuration's attribute list
+inline void add_pdl_attr(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attrs) {
+  cudaLaunchAttribute& a = attrs[cfg.numAttrs++];
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+}
+
+}  // namespace spk

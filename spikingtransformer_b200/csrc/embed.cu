@@ -22,7 +22,9 @@ __global__ void __launch_bounds__(256) embed_pe_lif_kernel(const int64_t* __rest
                                                            const float* pvth, const float* pvr, float gain, int T,
                                                            int64_t B, int64_t N, int D, int64_t V,
                                                            void* __restrict__ out, int* __restrict__ bad_token) {
+  pdl_trigger();
   const float beta = __ldg(pbeta), vth = __ldg(pvth), vr = __ldg(pvr);
+  pdl_wait();
   const int64_t total = B * N * D;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int d = (int)(i % D);
@@ -52,6 +54,8 @@ __global__ void __launch_bounds__(256) embed_pe_lif_kernel(const int64_t* __rest
 // one thread per (row, c, i, j) element of the patch matrix
 __global__ void __launch_bounds__(256) patch_im2col_kernel(const float* __restrict__ img, int64_t B, int C, int H,
                                                            int W, int p, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int nh = H / p, nw = W / p;
   const int K = C * p * p;
   const int64_t total = B * nh * nw * (int64_t)K;
@@ -98,16 +102,21 @@ int spk_embed_pe_lif_fwd(const int64_t* tokens, const float* emb, float emb_scal
   if (rc != SPK_OK) return rc;
   if (B * N == 0) return SPK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int grid = grid_1d(B * N * D);
-  if (out_dtype == SPK_BF16)
-    embk::embed_pe_lif_kernel<SPK_BF16><<<grid, 256, 0, st>>>(tokens, emb, emb_scale, pe, lif_beta, lif_vth,
-                                                             lif_vreset, in_gain, (int)T, B, N, (int)D, V, out,
-                                                             bad_token);
-  else
-    embk::embed_pe_lif_kernel<SPK_F32><<<grid, 256, 0, st>>>(tokens, emb, emb_scale, pe, lif_beta, lif_vth,
-                                                            lif_vreset, in_gain, (int)T, B, N, (int)D, V, out,
-                                                            bad_token);
-  return check_launch("embed_pe_lif_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid_1d(B * N * D), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  add_pdl_attr(cfg, attr);
+  const int iT = (int)T, iD = (int)D;
+  const cudaError_t e =
+      out_dtype == SPK_BF16
+          ? cudaLaunchKernelEx(&cfg, embk::embed_pe_lif_kernel<SPK_BF16>, tokens, emb, emb_scale, pe, lif_beta,
+                               lif_vth, lif_vreset, in_gain, iT, B, N, iD, V, out, bad_token)
+          : cudaLaunchKernelEx(&cfg, embk::embed_pe_lif_kernel<SPK_F32>, tokens, emb, emb_scale, pe, lif_beta,
+                               lif_vth, lif_vreset, in_gain, iT, B, N, iD, V, out, bad_token);
+  if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "embed_pe_lif_kernel launch: %s", cudaGetErrorString(e));
+  return SPK_OK;
 }
 
 int spk_patch_im2col(const float* img, int64_t B, int64_t C, int64_t H, int64_t W, int64_t patch, void* out,
@@ -120,9 +129,16 @@ int spk_patch_im2col(const float* img, int64_t B, int64_t C, int64_t H, int64_t 
   if (rc != SPK_OK) return rc;
   if (B == 0) return SPK_OK;
   const int64_t n = B * (H / patch) * (W / patch) * C * patch * patch;
-  embk::patch_im2col_kernel<<<grid_1d(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      img, B, (int)C, (int)H, (int)W, (int)patch, reinterpret_cast<__nv_bfloat16*>(out));
-  return check_launch("patch_im2col_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid_1d(n), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  add_pdl_attr(cfg, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, embk::patch_im2col_kernel, img, B, (int)C, (int)H, (int)W,
+                                           (int)patch, reinterpret_cast<__nv_bfloat16*>(out));
+  if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "patch_im2col_kernel launch: %s", cudaGetErrorString(e));
+  return SPK_OK;
 }
 
 }  // extern "C"

@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* base = smem_raw;
   Smem sm;
   smem_layout(p, base, &sm);
+  pdl_trigger();
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -195,6 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (cs > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
+  // the setup above reads only weights and constants; activations come after this
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -526,7 +529,7 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)p.cs;
   attr[0].val.clusterDim.y = 1;
@@ -543,6 +546,7 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
       cfg.gridDim = dim3((unsigned)(clusters * cfg_cs), 1, 1);
     }
   }
+  add_pdl_attr(cfg, attr);  // after the occupancy query, which describes the cluster shape alone
   e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, p);
   if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "gemm_ln_lif_kernel launch: %s", cudaGetErrorString(e));
   return SPK_OK;

@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmO, const Params p) {
   constexpr int CPL = 16 / T;  // columns per lane after the transposition
   constexpr int TPQ = 32 / T;  // tokens per TMEM lane quadrant
+  pdl_trigger();
   // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
   // it by plain arithmetic so the compiler keeps them in the shared address space
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -283,6 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (cs > 1) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
+  // the setup above reads only weights; activations (A, the residual) come after this
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -1338,7 +1341,7 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cs;
   attr[0].val.clusterDim.y = 1;
@@ -1354,6 +1357,7 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
       cfg.gridDim = dim3((unsigned)(clusters * cs), 1, 1);
     }
   }
+  add_pdl_attr(cfg, attr);  // after the occupancy query, which describes the cluster shape alone
   e = cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmO, p);
   if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "gemm_il_kernel launch: %s", cudaGetErrorString(e));
   return SPK_OK;

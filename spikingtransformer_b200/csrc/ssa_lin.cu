@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem sm;
   smem_layout(p.lmax, base, &sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   const int ksteps = (p.Nk + 15) >> 4;
   constexpr int dsteps = DP / 16;
   const int QB = p.QB;
@@ -202,6 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
+  // the setup above reads only weights and constants; activations come after this
+  pdl_wait();
   // R: [0, 256) (128 columns per query block), D1: [256, 320), D2: [320, 320 + 2 NO)
   const uint32_t tm_r = tmem, tm_d1 = tmem + 256, tm_d2 = tmem + 320;
 
@@ -567,7 +570,15 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
   if (grid > p.items) grid = p.items;
-  kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  add_pdl_attr(cfg, attr);
+  e = cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p);
+  if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "ssa_lin_kernel launch: %s", cudaGetErrorString(e));
   return SPK_OK;
 }
 

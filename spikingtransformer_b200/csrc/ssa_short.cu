@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem sm;
   smem_layout(smem_raw, &sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   const int BH = p.B * p.H;
   const int my_items = (p.items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int G = my_items * p.T;  // units of this CTA
@@ -192,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
+  // the setup above reads only weights and constants; activations come after this
+  pdl_wait();
   const uint32_t tm_s = tmem, tm_o = tmem + 256;
 
   if (warp == 0) {
@@ -490,8 +493,16 @@ int launch_ssa_short(const void* q, const void* k, const void* v, int T, int B, 
   if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
   if (grid > p.items) grid = p.items;
-  ssa_short_kernel<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
-  return check_launch("ssa_short_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  add_pdl_attr(cfg, attr);
+  e = cudaLaunchKernelEx(&cfg, ssa_short_kernel, tq, tk, tv, p);
+  if (e != cudaSuccess) return fail(SPK_ERR_LAUNCH, "ssa_short_kernel launch: %s", cudaGetErrorString(e));
+  return SPK_OK;
 }
 
 }  // namespace spk
