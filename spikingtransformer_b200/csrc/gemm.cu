@@ -71,6 +71,7 @@ struct Params {
   __nv_bfloat16* residual;  // [T][R][N] (+= spikes)
   float* ln_out;            // TCOUPLED: [T][R][N]; TBCAST: [R][N]
   float* out_f32;           // PLAIN: [R][N]
+  int vec_out;              // PLAIN: N % 4 == 0 and out, bias 16-byte aligned
 };
 
 struct Smem {
@@ -304,7 +305,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
           tmem_ld32(trow + c0, v);
           tmem_wait_ld();
-          if (grow < p.R) {
+          if (p.vec_out) {
+            // transpose through the warp's 32 staged rows so that every store
+            // instruction writes four 128-byte row segments
+            float* ys = sm.ys + row * kYsStride;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(ys + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            __syncwarp();
+            const int cb = n0 + c0 + 4 * (lane & 7);
+            float4 b4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (p.bias && cb < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + cb));
+            const float* ysw = sm.ys + q * 32 * kYsStride + 4 * (lane & 7);
+            const int64_t rbase = (int64_t)mt * 128 + q * 32;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int r = 4 * k + (lane >> 3);
+              const float4 y = *reinterpret_cast<const float4*>(ysw + r * kYsStride);
+              if (rbase + r < p.R && cb < p.N)
+                *reinterpret_cast<float4*>(p.out_f32 + (rbase + r) * p.N + cb) =
+                    make_float4(y.x + b4.x, y.y + b4.y, y.z + b4.z, y.w + b4.w);
+            }
+            __syncwarp();
+          } else if (grow < p.R) {
             float* dst = p.out_f32 + grow * p.N + n0 + c0;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -693,6 +716,7 @@ int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, 
   p.tmem_cols = tmem_cols_for(p.n_cta);
   p.bias = bias;
   p.out_f32 = out;
+  p.vec_out = (N % 4 == 0 && aligned(out, 16) && (!bias || aligned(bias, 16))) ? 1 : 0;
   p.tpt = 128;
   rc = launch_gemm(MODE_PLAIN, A, W, p, M, reinterpret_cast<cudaStream_t>(stream));
   if (rc != SPK_OK) return rc;
