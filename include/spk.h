@@ -134,35 +134,39 @@ int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void
  * LayerNorm -> LIF for training, forward (replaces nn.LayerNorm followed by
  * the LIF module in the autograd path: SSA.py:218-228, :247-249,
  * SpikingMLP.py:31-36, LIFLayer.forward Lif.py:10-43).
- *   y = LN(pre) * ln_gamma + ln_beta over the D features of each of the T*R
- *   rows; LIF over t: v = lif_beta v + in_gain y, s = v > lif_vth, reset.
+ *   y = LN(pre + pre_bias) * ln_gamma + ln_beta over the D features of each
+ *   of the T*R rows; LIF over t: v = lif_beta v + in_gain y, s = v > lif_vth,
+ *   reset.  pre_bias ([D] fp32 or NULL) is the preceding Linear's bias, so
+ *   that Linear can run without one.
  * pre: [T][R][D] (f32/f16/bf16); spikes: [T][R][D] in spike_dtype;
  * stats: [T*R] (mean, rstd) float pairs for the backward.  ln_gamma /
  * ln_beta may be NULL (1 / 0).  T <= 4; D a multiple of 32 up to 512, or of
  * 128 up to 2048.
  */
-int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* ln_gamma, const float* ln_beta,
-                   float ln_eps, const float* lif_beta, const float* lif_vth, const float* lif_vreset,
-                   float in_gain, int64_t T, int64_t R, int64_t D, void* spikes, int spike_dtype,
-                   float* stats, void* stream);
+int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
+                   const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
+                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, void* spikes,
+                   int spike_dtype, float* stats, void* stream);
 
 /*
  * Backward of spk_ln_lif_fwd (LIFLayer.backward Lif.py:46-102 composed with
  * the LayerNorm backward): recomputes x^ and the membrane from pre and stats,
  * BPTT with the surrogate, then
  *   g_pre = rstd (g - mean(g) - x^ mean(g x^)),  g = ln_gamma dL/dy,
- *   g_gamma = sum dL/dy x^, g_beta_ln = sum dL/dy, g_lif_beta = sum g_v v_prev
+ *   g_gamma = sum dL/dy x^, g_beta_ln = sum dL/dy, g_bias = sum g_pre,
+ *   g_lif_beta = sum g_v v_prev
  * (sums over all rows, reduced in a fixed order).  g_spikes: f32/f16/bf16;
- * g_pre has pre's dtype; g_gamma / g_beta_ln / g_lif_beta may be NULL.
+ * g_pre has pre's dtype; pre_bias is the forward's; g_gamma / g_beta_ln /
+ * g_bias / g_lif_beta may be NULL.
  * workspace: spk_ln_lif_bwd_workspace_bytes(T, R, D) bytes.
  */
 int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D);
 int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype,
-                   const float* stats, const float* ln_gamma, const float* ln_beta,
-                   const float* lif_beta, const float* lif_vth, const float* lif_vreset,
-                   float in_gain, int surrogate, float surrogate_k, int64_t T, int64_t R, int64_t D,
-                   void* g_pre, float* g_gamma, float* g_beta_ln, float* g_lif_beta, void* workspace,
-                   int64_t workspace_bytes, void* stream);
+                   const float* pre_bias, const float* stats, const float* ln_gamma,
+                   const float* ln_beta, const float* lif_beta, const float* lif_vth,
+                   const float* lif_vreset, float in_gain, int surrogate, float surrogate_k, int64_t T,
+                   int64_t R, int64_t D, void* g_pre, float* g_gamma, float* g_beta_ln, float* g_bias,
+                   float* g_lif_beta, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Fused Linear -> LayerNorm -> LIF (tcgen05, bf16 operands, fp32 accumulate).

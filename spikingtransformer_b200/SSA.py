@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from ._fused import fast_path_ok, lif_params, lin_ln_lif, ln_lif
+from ._fused import fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train
 from .Lif import LIF
 
 
@@ -113,12 +113,14 @@ class _SSACore(nn.Module):
     def _reference_forward(self, query, key, value, attention_mask):
         TB, N, D = query.shape
         Nk = key.shape[1]
-        q = self._heads(ln_lif(self.q_proj(query), self.lnq, self.lifq), N)
-        k = self._heads(ln_lif(self.k_proj(key), self.lnk, self.lifk), Nk)
-        v = self._heads(ln_lif(self.v_proj(value), self.lnv, self.lifv), Nk)
+        # Q, K, V spikes feed only the attention products, so under autocast
+        # they are written in its dtype (0/1 exact)
+        q = self._heads(lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True), N)
+        k = self._heads(lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True), Nk)
+        v = self._heads(lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True), Nk)
         a = self._combine(q, k, v, attention_mask)
         s = self.lifs(a)[0].transpose(1, 2).contiguous().view(TB, N, D)
-        return ln_lif(self.out_proj(s), self.lno, self.lifo)
+        return lin_ln_lif_train(s, self.out_proj, self.lno, self.lifo)
 
     def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -181,17 +183,116 @@ class SSAMultiHeadAttention(_SSACore):
             return (a * mask * self.scale) @ v
         # Without a mask the score matrix regroups exactly (spikes are 0/1):
         #   S V = 2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V,  s_j = |k_j|,
-        # so neither S nor its gradient is formed.  fp32 matmuls keep every
-        # integer term exact (sums below 2^24), whatever the autocast state.
+        # so neither S nor its gradient is formed.
         dh = q.shape[-1]
+        R = self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device)
+        if q.is_cuda and k.shape[2] <= 256 and dh <= 256:
+            return XnorScoreFree.apply(q, k, v, R, self.scale)
+        # fp32 matmuls keep every integer term exact (sums below 2^24), whatever
+        # the autocast state
         with torch.autocast(q.device.type, enabled=False):
             qf, kf, vf = q.float(), k.float(), v.float()
-            R = self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device)
             m = 2.0 * (qf @ (kf.transpose(-2, -1) @ vf))
             m = m + (dh - qf.sum(-1, keepdim=True)) * vf.sum(-2, keepdim=True)
             m = m - kf.sum(-1).unsqueeze(-2) @ vf
             m = m + R @ vf
             return m * self.scale
+
+
+def _split_bf16(x):
+    """fp32 -> (hi, lo) bf16 with hi + lo equal to x to about 2^-16 relative."""
+    hi = x.to(torch.bfloat16)
+    return hi, (x - hi.float()).to(torch.bfloat16)
+
+
+def _flat_bf16(t):
+    """[TB, H, N, d] of any strides -> contiguous bf16 [TB*H, N, d] in one pass."""
+    out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
+    out.copy_(t)
+    return out.view(-1, t.shape[-2], t.shape[-1])
+
+
+def _bmm32(a, b):
+    """bf16 x bf16 -> fp32 batched product on the tensor cores."""
+    return torch.bmm(a, b, out_dtype=torch.float32)
+
+
+def _mm_shared(Rb, x, transpose=False):
+    """``R @ x[b]`` (or ``R^T @ x[b]``) for every batch b of ``x`` [B, N, d] as one
+    [Nq, Nk] x [Nk, B*d] product; bf16 in, fp32 out, [B, N', d]."""
+    B, N, d = x.shape
+    A = Rb.t() if transpose else Rb
+    xp = x.permute(1, 0, 2).reshape(N, B * d)
+    y = torch.mm(A, xp, out_dtype=torch.float32)
+    return y.view(A.shape[0], B, d).permute(1, 0, 2)
+
+
+class XnorScoreFree(torch.autograd.Function):
+    """Score-free XNOR attention core on the tensor cores, for training.
+
+    ``m = scale * [2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V]`` with
+    ``s_j = |k_j|``, which equals ``(S * scale) @ V`` for the reference's
+    ``S = dh - (|q_i| + |k_j| - 2 q_i.k_j) + R`` (``SSA.py:145-165``,
+    ``:177-201``, ``:235-240``) when Q, K, V are 0/1.
+
+    Forward: every operand is an integer that bf16 holds exactly (spikes, the
+    counts ``K^T V <= Nk <= 256``, ``|k_j| <= dh``, ``R <= 8``) and every
+    product accumulates in fp32, so ``m / scale`` is exact and equals the fp32
+    formulation bit for bit.  Backward: the real-valued gradient operands are
+    split into two bf16 terms (hi + lo, about 2^-16 relative), each product
+    runs on the tensor cores with fp32 accumulation, and the halves are added.
+
+    Inputs: q [TB, H, Nq, dh], k and v [TB, H, Nk, dh] (0/1 in any float
+    dtype, any strides), R [Nq, Nk] fp32, scale a 0-d parameter.  Output: fp32
+    [TB, H, Nq, dh].
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, R, scale):
+        with torch.autocast("cuda", enabled=False):
+            dh = q.shape[-1]
+            qb, kb, vb = (_flat_bf16(t) for t in (q, k, v))
+            Rb = R.to(torch.bfloat16)
+            kv = _bmm32(kb.transpose(1, 2), vb)                           # [B, dh, dh]
+            cv = vb.sum(1, keepdim=True, dtype=torch.float32)              # 1^T V  [B, 1, dh]
+            sk = kb.sum(2, keepdim=True, dtype=torch.float32)              # |k_j|  [B, Nk, 1]
+            qs = qb.sum(2, keepdim=True, dtype=torch.float32)              # |q_i|  [B, Nq, 1]
+            m = 2.0 * _bmm32(qb, kv.to(torch.bfloat16))
+            m = m + (dh - qs) * cv
+            m = m - _bmm32(sk.transpose(1, 2).to(torch.bfloat16), vb)
+            m = m + _mm_shared(Rb, vb)
+            out = (m * scale.float()).view(q.shape)
+        ctx.save_for_backward(qb, kb, vb, kv, cv, sk, qs, Rb, m, scale)
+        ctx.meta = ((q.dtype, q.shape), (k.dtype, k.shape), (v.dtype, v.shape))
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        qb, kb, vb, kv, cv, sk, qs, Rb, m, scale = ctx.saved_tensors
+        dh = qb.shape[-1]
+        with torch.autocast("cuda", enabled=False):
+            g = g.float().reshape(m.shape)
+            gscale = (g * m).sum().reshape(scale.shape).to(scale.dtype)
+            gs = g * scale.float()                                         # dL/dm
+            gh, gl = _split_bf16(gs)
+            gcol = gs.sum(1, keepdim=True)                                 # 1^T G  [B, 1, dh]
+            # dQ = 2 G (K^T V)^T - (G . 1^T V) 1^T
+            kvt = kv.to(torch.bfloat16).transpose(1, 2)
+            dq = 2.0 * (_bmm32(gh, kvt) + _bmm32(gl, kvt))
+            dq = dq - (gs * cv).sum(-1, keepdim=True)
+            # d(K^T V) = 2 Q^T G
+            qt = qb.transpose(1, 2)
+            dkv = 2.0 * (_bmm32(qt, gh) + _bmm32(qt, gl))                   # [B, dh, dh]
+            dkh, dkl = _split_bf16(dkv)
+            # dK = V d(K^T V)^T - (V . 1^T G) 1^T
+            dk = _bmm32(vb, dkh.transpose(1, 2)) + _bmm32(vb, dkl.transpose(1, 2))
+            dk = dk - (vb.float() * gcol).sum(-1, keepdim=True)
+            # dV = K d(K^T V) + 1 ((dh - |q|)^T G) - s (1^T G) + R^T G
+            dv = _bmm32(kb, dkh) + _bmm32(kb, dkl)
+            dv = dv + ((dh - qs) * gs).sum(1, keepdim=True) - sk * gcol
+            dv = dv + _mm_shared(Rb, gh, transpose=True) + _mm_shared(Rb, gl, transpose=True)
+        (tq, sq), (tk, sk_), (tv, sv) = ctx.meta
+        return dq.to(tq).view(sq), dk.to(tk).view(sk_), dv.to(tv).view(sv), None, gscale
 
 
 class SSAMultiHeadAttention_(_SSACore):

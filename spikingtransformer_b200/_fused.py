@@ -87,39 +87,68 @@ def fast_path_ok(*tensors, module=None):
 
 
 class LNLIFFunction(torch.autograd.Function):
-    """``lif(ln(pre))`` for training in two kernels (``ops.ln_lif_fwd`` / ``ops.ln_lif_bwd``):
-    the LayerNorm, the LIF scan and both backwards fused over the T steps of
-    each token; the Linear before it stays a library GEMM.  Gradients: pre,
-    the LayerNorm weight and bias, and the LIF beta."""
+    """``lif(ln(pre + bias))`` for training in two kernels (``ops.ln_lif_fwd`` /
+    ``ops.ln_lif_bwd``): the LayerNorm, the LIF scan and both backwards fused
+    over the T steps of each token.  ``bias`` is the preceding Linear's (or
+    None): its GEMM runs without one and the bias gradient comes out of the
+    backward kernel.  Gradients: pre, the Linear bias, the LayerNorm weight and
+    bias, and the LIF beta.  Spikes are written in ``spike_dtype`` (0/1 are
+    exact in every float type)."""
 
     @staticmethod
-    def forward(ctx, pre, ln_weight, ln_bias, lif_beta, v_th, v_reset, eps, k, surrogate, in_gain, T):
-        spikes, stats = ops.ln_lif_fwd(pre, ln_weight, ln_bias, eps, lif_beta, v_th, v_reset, T, in_gain)
-        ctx.save_for_backward(pre, stats, ln_weight, ln_bias, lif_beta, v_th, v_reset)
+    def forward(ctx, pre, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset, eps, k, surrogate, in_gain, T,
+                spike_dtype):
+        spikes, stats = ops.ln_lif_fwd(pre, ln_weight, ln_bias, eps, lif_beta, v_th, v_reset, T, in_gain,
+                                       spike_dtype=spike_dtype, bias=bias)
+        ctx.save_for_backward(pre, stats, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset)
         ctx.k, ctx.surrogate, ctx.in_gain, ctx.T = float(k), surrogate, float(in_gain), int(T)
         return spikes
 
     @staticmethod
     def backward(ctx, g_spikes):
-        pre, stats, w, b, lb, vth, vr = ctx.saved_tensors
+        pre, stats, pb, w, b, lb, vth, vr = ctx.saved_tensors
         need = ctx.needs_input_grad
-        g_pre, gw, gb, glb = ops.ln_lif_bwd(g_spikes, pre, stats, w, b, lb, vth, vr, ctx.T, ctx.in_gain,
-                                            ctx.surrogate, ctx.k, need_gamma=need[1], need_beta=need[2],
-                                            need_lif_beta=need[3])
+        g_pre, gw, gb, glb, gpb = ops.ln_lif_bwd(g_spikes, pre, stats, w, b, lb, vth, vr, ctx.T, ctx.in_gain,
+                                                 ctx.surrogate, ctx.k, need_gamma=need[2], need_beta=need[3],
+                                                 need_lif_beta=need[4], bias=pb,
+                                                 need_bias=pb is not None and need[1])
+        gpb = gpb.to(pb.dtype) if gpb is not None else None
         gw = gw.to(w.dtype) if gw is not None else None
         gb = gb.to(b.dtype) if gb is not None else None
         glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
-        return g_pre, gw, gb, glb, None, None, None, None, None, None, None
+        return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, None
+
+
+def _ln_lif_fusable(x, D, ln, lif):
+    return (x.is_cuda and isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine
+            and tuple(ln.normalized_shape) == (D,) and x.shape[0] % lif.n_steps == 0
+            and ops.ln_lif_ok(lif.n_steps, D))
+
+
+def _lif_args(ln, lif):
+    return (ln.weight, ln.bias, lif.effective_beta(), lif.v_th, lif.v_reset, ln.eps, lif._k_host, lif.surrogate,
+            lif.in_gain, lif.n_steps)
 
 
 def ln_lif(x, ln, lif):
     """``lif(ln(x))[0]`` on the autograd path: the fused training kernels when the
     shapes allow (CUDA, affine LayerNorm over the last dimension), the module
     composition otherwise (``Lif.py:288-441`` over torch's LayerNorm)."""
-    T = lif.n_steps
-    D = x.shape[-1]
-    if (x.is_cuda and isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine
-            and tuple(ln.normalized_shape) == (D,) and x.shape[0] % T == 0 and ops.ln_lif_ok(T, D)):
-        return LNLIFFunction.apply(x, ln.weight, ln.bias, lif.effective_beta(), lif.v_th, lif.v_reset, ln.eps,
-                                   lif._k_host, lif.surrogate, lif.in_gain, T)
+    if _ln_lif_fusable(x, x.shape[-1], ln, lif):
+        return LNLIFFunction.apply(x, None, *_lif_args(ln, lif), torch.float32)
     return lif(ln(x))[0]
+
+
+def lin_ln_lif_train(x, lin, ln, lif, narrow=False):
+    """``lif(ln(lin(x)))[0]`` on the autograd path.  With the fused kernels the
+    GEMM (``F.linear``, under whatever autocast is active) runs without the bias,
+    which the LayerNorm->LIF kernels add and differentiate.  ``narrow``: under
+    autocast, write the spikes in the autocast dtype; meant for spikes whose
+    consumer is a GEMM that casts to that dtype anyway."""
+    if _ln_lif_fusable(x, lin.out_features, ln, lif):
+        pre = torch.nn.functional.linear(x, lin.weight)
+        dt = torch.float32
+        if narrow and torch.is_autocast_enabled(x.device.type):
+            dt = torch.get_autocast_dtype(x.device.type)
+        return LNLIFFunction.apply(pre, lin.bias, *_lif_args(ln, lif), dt)
+    return ln_lif(lin(x), ln, lif)

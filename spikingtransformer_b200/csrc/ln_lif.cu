@@ -8,20 +8,29 @@
 // [T][R][D] (t-major fold, R tokens, D features); LayerNorm runs over D for
 // each of the T*R rows; the LIF couples the T rows of a token.
 //
-// Forward, per token: the T rows are loaded once into registers (D/(32 NW)
-// columns per thread, NW warps per token), mean and variance by two passes
-// (warp shuffles, plus shared memory when NW > 1), y = (x - mean) rstd gamma
-// + beta, then the LIF over t with v = beta v + gain y (separately rounded
-// multiply and add, as the reference), s = v > v_th, v = s ? v_reset : v.
-// Spikes are written and (mean, rstd) of every row is saved.
+// The Linear's bias may be handed to these kernels instead of the GEMM: the
+// forward adds it to pre before the LayerNorm, and the backward returns its
+// gradient (the column sums of g_pre), so the library GEMM runs without a
+// bias and no separate bias-gradient reduction is needed.
+//
+// Forward, per token: mean and variance by two passes, y = (x - mean) rstd
+// gamma + beta, then the LIF over t with v = beta v + gain y (separately
+// rounded multiply and add, as the reference), s = v > v_th,
+// v = s ? v_reset : v.  Spikes are written and (mean, rstd) of every row is
+// saved.  When D is a multiple of 128 one block handles one token (D/128
+// warps, four consecutive columns per lane, the T rows kept as packed raw
+// vectors and processed in t order); otherwise one warp handles one token
+// with single interleaved columns.
 //
 // Backward, per token: x^ and the membrane are recomputed from the saved
 // statistics; BPTT over t with the surrogate (SuperSpike or arctan) gives
 // dL/dy; then the LayerNorm input gradient
 //   dx = rstd (g - mean(g) - x^ mean(g x^)),  g = gamma dL/dy
-// and per-column partial sums of dL/dgamma = sum dL/dy x^ and
-// dL/dbeta = sum dL/dy, plus the LIF beta gradient sum g_v v_prev, are kept
-// per block and reduced in a fixed order by a second kernel.
+// and per-column partial sums of dL/dgamma = sum dL/dy x^, dL/dbeta = sum
+// dL/dy and dL/dbias = sum dx, plus the LIF beta gradient sum g_v v_prev, are
+// kept per block and reduced in a fixed order by a second kernel.
+#include <initializer_list>
+
 #include "common.cuh"
 
 namespace spk {
@@ -34,6 +43,7 @@ constexpr int kMaxT = 4;
 struct FwdParams {
   const void* pre;
   int pre_dtype;
+  const float* bias;  // [D] added to pre, or null
   const float* gamma;
   const float* beta_ln;
   float eps;
@@ -52,6 +62,7 @@ struct BwdParams {
   int gs_dtype;
   const void* pre;
   int pre_dtype;
+  const float* bias;  // [D] added to pre, or null
   const float2* stats;
   const float* gamma;
   const float* beta_ln;
@@ -60,7 +71,7 @@ struct BwdParams {
   int surrogate;
   float k, c_arctan;
   void* g_pre;  // same dtype as pre
-  float* part;  // [grid][2 D + 1]: dgamma partials, dbeta partials, LIF beta partial
+  float* part;  // [grid][3 D + 1]: dgamma, dbeta, dbias partials, LIF beta partial
   int T;
   int64_t R;
   int D, cpt;
@@ -160,6 +171,41 @@ __device__ __forceinline__ void token_sums(float (&vals)[kMaxT], int T, float* r
   }
 }
 
+// four consecutive elements kept packed until their row is processed
+template <int EB>
+struct RawVec;
+template <>
+struct RawVec<2> {
+  uint2 w;
+};
+template <>
+struct RawVec<4> {
+  float4 w;
+};
+
+template <int EB>
+__device__ __forceinline__ void raw_load(RawVec<EB>& r, const void* p, int64_t i) {
+  if constexpr (EB == 2)
+    r.w = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p) + i);
+  else
+    r.w = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+}
+
+template <int EB>
+__device__ __forceinline__ void raw_unpack(const RawVec<EB>& r, int dt, float* o) {
+  if constexpr (EB == 4) {
+    o[0] = r.w.x; o[1] = r.w.y; o[2] = r.w.z; o[3] = r.w.w;
+  } else if (dt == SPK_F16) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.w.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.w.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  } else {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.w.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.w.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+}
+
 // Surrogate derivative for the training kernels (gradients are compared within a
 // tolerance, so the fast-division intrinsic is used; the LIF backward entry point in
 // lif.cu keeps IEEE division for bit-exact parity with the reference).
@@ -183,12 +229,13 @@ __global__ void __launch_bounds__(kThreads) ln_lif_fwd_kernel(const FwdParams p)
   const int slot = NW == 1 ? warp : 0;
   const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
   const int T = p.T, D = p.D, cpt = p.cpt;
-  float g[CM], bl[CM];
+  float g[CM], bl[CM], pb[CM];
 #pragma unroll
   for (int i = 0; i < CM; ++i) {
     const int c = col_of<NW, V>(i, wt, lane);
     g[i] = (i < cpt && p.gamma) ? __ldg(p.gamma + c) : 1.0f;
     bl[i] = (i < cpt && p.beta_ln) ? __ldg(p.beta_ln + c) : 0.0f;
+    pb[i] = (i < cpt && p.bias) ? __ldg(p.bias + c) : 0.0f;
   }
   for (int64_t tok = (int64_t)blockIdx.x * slots + slot; tok < p.R; tok += (int64_t)gridDim.x * slots) {
     float x[kMaxT][CM];
@@ -211,6 +258,8 @@ __global__ void __launch_bounds__(kThreads) ln_lif_fwd_kernel(const FwdParams p)
             for (int v = 0; v < V; ++v) x[t][i + v] = 0.0f;
           }
         }
+#pragma unroll
+        for (int i = 0; i < CM; ++i) x[t][i] += pb[i];
 #pragma unroll
         for (int i = 0; i < CM; ++i) s1[t] += x[t][i];
       }
@@ -273,7 +322,7 @@ __global__ void __launch_bounds__(kThreads) ln_lif_fwd_kernel(const FwdParams p)
 template <int NW, int V, int CM>
 __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p) {
   __shared__ float red[4 * kMaxT];
-  __shared__ float blk[4][kMaxCpt * 32 * 2 + 1];
+  __shared__ float blk[4][kMaxCpt * 32 * 3 + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wt = NW == 1 ? 0 : warp;
   const int slots = kThreads / 32 / NW;
@@ -281,14 +330,16 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
   const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
   const int T = p.T, D = p.D, cpt = p.cpt;
   const float invD = 1.0f / (float)D;
-  float g[CM], bl[CM], acc_g[CM], acc_b[CM];
+  float g[CM], bl[CM], pb[CM], acc_g[CM], acc_b[CM], acc_d[CM];
 #pragma unroll
   for (int i = 0; i < CM; ++i) {
     const int c = col_of<NW, V>(i, wt, lane);
     g[i] = (i < cpt && p.gamma) ? __ldg(p.gamma + c) : 1.0f;
     bl[i] = (i < cpt && p.beta_ln) ? __ldg(p.beta_ln + c) : 0.0f;
+    pb[i] = (i < cpt && p.bias) ? __ldg(p.bias + c) : 0.0f;
     acc_g[i] = 0.0f;
     acc_b[i] = 0.0f;
+    acc_d[i] = 0.0f;
   }
   float acc_lb = 0.0f;
   for (int64_t tok = (int64_t)blockIdx.x * slots + slot; tok < p.R; tok += (int64_t)gridDim.x * slots) {
@@ -313,7 +364,7 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
               gy[t][i] = load_elem(p.g_spikes, p.gs_dtype, e);
             }
 #pragma unroll
-            for (int v = 0; v < V; ++v) xh[t][i + v] = (xh[t][i + v] - st.x) * st.y;
+            for (int v = 0; v < V; ++v) xh[t][i + v] = ((xh[t][i + v] + pb[i + v]) - st.x) * st.y;
           } else {
 #pragma unroll
             for (int v = 0; v < V; ++v) {
@@ -380,7 +431,10 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
       const float ma = a[t] * invD, mb = b[t] * invD;
       const int64_t rb = ((int64_t)t * p.R + tok) * D;
 #pragma unroll
-      for (int i = 0; i < CM; ++i) gy[t][i] = rstd[t] * (gy[t][i] * g[i] - ma - xh[t][i] * mb);
+      for (int i = 0; i < CM; ++i) {
+        gy[t][i] = rstd[t] * (gy[t][i] * g[i] - ma - xh[t][i] * mb);
+        if (i < cpt) acc_d[i] += gy[t][i];
+      }
 #pragma unroll
       for (int i = 0; i < CM; i += V) {
         if (i >= cpt) continue;
@@ -393,29 +447,30 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
   }
   // per-block partials: the warps of a block own the same columns when NW = 1, so they are
   // combined in warp order first; NW = 4 warps own disjoint columns
-  const int W = 2 * D + 1;
+  const int W = 3 * D + 1;
   float* out = p.part + (int64_t)blockIdx.x * W;
   if constexpr (NW == 1) {
     // (for NW = 1 the D <= 512 columns index blk directly)
+    constexpr int S = kMaxCpt * 32;
 #pragma unroll
     for (int i = 0; i < CM; ++i) {
       if (i < cpt) {
         const int c = col_of<NW, V>(i, 0, lane);
         blk[warp][c] = acc_g[i];
-        blk[warp][kMaxCpt * 32 + c] = acc_b[i];
+        blk[warp][S + c] = acc_b[i];
+        blk[warp][2 * S + c] = acc_d[i];
       }
     }
     const float lbw = warp_sum(acc_lb);
-    if (lane == 0) blk[warp][kMaxCpt * 32 * 2] = lbw;
+    if (lane == 0) blk[warp][3 * S] = lbw;
     __syncthreads();
     if (warp == 0) {
       for (int c = lane; c < D; c += 32) {
-        out[c] = ((blk[0][c] + blk[1][c]) + blk[2][c]) + blk[3][c];
-        out[D + c] = ((blk[0][kMaxCpt * 32 + c] + blk[1][kMaxCpt * 32 + c]) + blk[2][kMaxCpt * 32 + c]) +
-                     blk[3][kMaxCpt * 32 + c];
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          out[k * D + c] = ((blk[0][k * S + c] + blk[1][k * S + c]) + blk[2][k * S + c]) + blk[3][k * S + c];
       }
-      if (lane == 0)
-        out[2 * D] = ((blk[0][kMaxCpt * 64] + blk[1][kMaxCpt * 64]) + blk[2][kMaxCpt * 64]) + blk[3][kMaxCpt * 64];
+      if (lane == 0) out[3 * D] = ((blk[0][3 * S] + blk[1][3 * S]) + blk[2][3 * S]) + blk[3][3 * S];
     }
   } else {
 #pragma unroll
@@ -424,20 +479,207 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
         const int c = col_of<NW, V>(i, wt, lane);
         out[c] = acc_g[i];
         out[D + c] = acc_b[i];
+        out[2 * D + c] = acc_d[i];
       }
     }
     const float lbw = warp_sum(acc_lb);
     if (lane == 0) red[warp] = lbw;
     __syncthreads();
-    if (threadIdx.x == 0) out[2 * D] = ((red[0] + red[1]) + red[2]) + red[3];
+    if (threadIdx.x == 0) out[3 * D] = ((red[0] + red[1]) + red[2]) + red[3];
   }
 }
 
-// column c of the [rows][W] partials (dgamma, dbeta, LIF beta): 8 row groups
-// (rows r = g mod 8, in order) per column, combined in group order
+// ---------------------------------------------------------------------------
+// One token per block (D % 128 == 0): NW = D / 128 warps, four consecutive
+// columns per lane, so one 8- or 16-byte vector per row and lane.  The
+// working set is a few dozen registers, and many blocks are resident per SM
+// to keep enough loads in flight.  Row sums over the block go through
+// double-buffered shared slots: one barrier per sum (a slot is rewritten only
+// two sums later, after a barrier that every reader has passed).
+
+constexpr int kTokMaxWarps = 16;  // D <= 2048
+
+struct BlockSum {
+  float2* red;  // [2][kTokMaxWarps]
+  int buf;
+  __device__ __forceinline__ float2 sum2(float2 v, int nw) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+      v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+    }
+    float2* r = red + buf * kTokMaxWarps;
+    if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float2 s = make_float2(0.0f, 0.0f);
+    for (int w = 0; w < nw; ++w) {
+      s.x += r[w].x;
+      s.y += r[w].y;
+    }
+    buf ^= 1;
+    return s;
+  }
+  __device__ __forceinline__ float sum(float v, int nw) { return sum2(make_float2(v, 0.0f), nw).x; }
+};
+
+template <int EB>
+__global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const FwdParams p) {
+  __shared__ float2 red[2 * kTokMaxWarps];
+  BlockSum bs{red, 0};
+  const int nw = blockDim.x >> 5;
+  const int c = threadIdx.x * 4;  // this lane's four columns
+  const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+  const int T = p.T, D = p.D;
+  const float4 g4 = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
+  const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
+  for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
+    RawVec<EB> raw[kMaxT];
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t)
+      if (t < T) raw_load<EB>(raw[t], p.pre, ((int64_t)t * p.R + tok) * D + c);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      float x[4];
+      raw_unpack<EB>(raw[t], p.pre_dtype, x);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] += pp[e];
+      const float mean = bs.sum((x[0] + x[1]) + (x[2] + x[3]), nw) / (float)D;
+      float s2 = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float d = x[e] - mean;
+        s2 = fmaf(d, d, s2);
+      }
+      const float rstd = 1.0f / sqrtf(bs.sum(s2, nw) / (float)D + p.eps);
+      const int64_t row = (int64_t)t * p.R + tok;
+      if (threadIdx.x == 0) p.stats[row] = make_float2(mean, rstd);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float y = fmaf((x[e] - mean) * rstd, gg[e], bb[e]);
+        const float cur = p.gain != 1.0f ? __fmul_rn(y, p.gain) : y;
+        const float u = __fadd_rn(__fmul_rn(v[e], lb), cur);
+        const bool sp = u > vth;
+        x[e] = sp ? 1.0f : 0.0f;
+        v[e] = sp ? vr : u;
+      }
+      store4(p.spikes, p.spike_dtype, row * D + c, x);
+    }
+  }
+}
+
+// Backward, one token per block: the membrane is recomputed in t order from
+// the saved statistics, then the steps are walked backwards; BPTT of step t
+// gives dL/dy of row t, whose LayerNorm backward (one pair of block sums)
+// runs at once.
+template <int EBP, int EBG>
+__global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const BwdParams p) {
+  __shared__ float2 red[2 * kTokMaxWarps];
+  BlockSum bs{red, 0};
+  const int nw = blockDim.x >> 5;
+  const int c = threadIdx.x * 4;
+  const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+  const int T = p.T, D = p.D;
+  const float invD = 1.0f / (float)D;
+  const float4 g4 = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
+  const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
+  float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f}, acc_d[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc_lb = 0.0f;
+  for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
+    RawVec<EBP> rp[kMaxT];
+    RawVec<EBG> rg[kMaxT];
+    float2 st[kMaxT];
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      st[t] = make_float2(0.0f, 1.0f);
+      if (t >= T) continue;
+      const int64_t row = (int64_t)t * p.R + tok;
+      st[t] = p.stats[row];
+      raw_load<EBP>(rp[t], p.pre, row * D + c);
+      raw_load<EBG>(rg[t], p.g_spikes, row * D + c);
+    }
+    // membrane before reset at every step
+    float u[kMaxT][4];
+    {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t) {
+        if (t >= T) continue;
+        float x[4];
+        raw_unpack<EBP>(rp[t], p.pre_dtype, x);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float xh = ((x[e] + pp[e]) - st[t].x) * st[t].y;
+          const float y = fmaf(xh, gg[e], bb[e]);
+          const float cur = p.gain != 1.0f ? __fmul_rn(y, p.gain) : y;
+          const float uu = __fadd_rn(__fmul_rn(v[e], lb), cur);
+          u[t][e] = uu;
+          v[e] = uu > vth ? vr : uu;
+        }
+      }
+    }
+    float gstate[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int t = kMaxT - 1; t >= 0; --t) {
+      if (t >= T) continue;
+      float gy[4], x[4], xh[4];
+      raw_unpack<EBG>(rg[t], p.gs_dtype, gy);
+      raw_unpack<EBP>(rp[t], p.pre_dtype, x);
+      float a = 0.0f, b = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // BPTT step t: dL/ds -> dL/dy
+        const float sg = surrogate_grad(p.surrogate, u[t][e] - vth, p.k, p.c_arctan);
+        const bool sp = u[t][e] > vth;
+        const float gv = gy[e] * sg + (sp ? 0.0f : gstate[e]);
+        const float vprev = t > 0 ? (u[t - 1][e] > vth ? vr : u[t - 1][e]) : 0.0f;
+        acc_lb = fmaf(gv, vprev, acc_lb);
+        gstate[e] = gv * lb;
+        gy[e] = p.gain != 1.0f ? gv * p.gain : gv;
+        // LayerNorm backward terms of row t
+        xh[e] = ((x[e] + pp[e]) - st[t].x) * st[t].y;
+        const float gx = gy[e] * gg[e];
+        a += gx;
+        b = fmaf(gx, xh[e], b);
+        acc_g[e] = fmaf(gy[e], xh[e], acc_g[e]);
+        acc_b[e] += gy[e];
+      }
+      const float2 ab = bs.sum2(make_float2(a, b), nw);
+      const float ma = ab.x * invD, mb = ab.y * invD;
+      float dx[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dx[e] = st[t].y * (gy[e] * gg[e] - ma - xh[e] * mb);
+        acc_d[e] += dx[e];
+      }
+      store4(p.g_pre, p.pre_dtype, ((int64_t)t * p.R + tok) * D + c, dx);
+    }
+  }
+  // per-block partials: each thread owns its four columns; the LIF beta term
+  // is summed over the block.  Rows are 3 D + 1 floats long, so a row start is
+  // only 4-byte aligned: scalar stores.
+  float* out = p.part + (int64_t)blockIdx.x * (3 * D + 1);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    out[c + e] = acc_g[e];
+    out[D + c + e] = acc_b[e];
+    out[2 * D + c + e] = acc_d[e];
+  }
+  const float lbs = bs.sum(acc_lb, nw);
+  if (threadIdx.x == 0) out[3 * D] = lbs;
+}
+
+// column c of the [rows][W] partials (dgamma, dbeta, dbias, LIF beta): 8 row
+// groups (rows r = g mod 8, in order) per column, combined in group order
 __global__ void __launch_bounds__(256) sum_columns_kernel(const float* __restrict__ part, int rows, int W,
                                                           float* __restrict__ dgamma, float* __restrict__ dbeta,
-                                                          float* __restrict__ dlif_beta, int D) {
+                                                          float* __restrict__ dbias, float* __restrict__ dlif_beta,
+                                                          int D) {
   __shared__ float acc[8][33];
   const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + cl;
@@ -454,6 +696,8 @@ __global__ void __launch_bounds__(256) sum_columns_kernel(const float* __restric
     if (dgamma) dgamma[c] = s;
   } else if (c < 2 * D) {
     if (dbeta) dbeta[c - D] = s;
+  } else if (c < 3 * D) {
+    if (dbias) dbias[c - 2 * D] = s;
   } else if (dlif_beta) {
     *dlif_beta = s;
   }
@@ -469,6 +713,28 @@ inline int grid_blocks(int64_t R, int nw, int blocks_per_sm = 2) {
   const int64_t cap = (int64_t)num_sms() * blocks_per_sm;
   if (need > cap) need = cap;
   return need < 1 ? 1 : (int)need;
+}
+
+// one-token-per-block kernels: D % 128 == 0; persistent grid of up to 64 warps
+// (at most 16 blocks) per SM
+inline bool use_tok(int D) { return D % 128 == 0 && D <= 128 * kTokMaxWarps; }
+// the one-token-per-block kernels move four elements per vector access and
+// read gamma / beta / bias as float4: every pointer 16-byte aligned
+inline bool tok_aligned(std::initializer_list<const void*> ptrs) {
+  for (const void* q : ptrs)
+    if (q && (reinterpret_cast<uintptr_t>(q) & 15) != 0) return false;
+  return true;
+}
+inline int tok_grid(int64_t R, int D) {
+  const int nw = D / 128;
+  int bps = 64 / nw;
+  if (bps > 16) bps = 16;
+  const int64_t cap = (int64_t)num_sms() * bps;
+  const int64_t g = R < cap ? R : cap;
+  return g < 1 ? 1 : (int)g;
+}
+inline int bwd_grid(int64_t R, int D, bool aligned16) {
+  return R == 0 ? 1 : (use_tok(D) && aligned16) ? tok_grid(R, D) : grid_blocks(R, pick_nw(D));
 }
 
 }  // namespace lnlif
@@ -490,16 +756,15 @@ extern "C" {
 
 int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D) {
   (void)T;
-  const int nw = spk::lnlif::pick_nw((int)D);
-  const int64_t slots = 4 / nw;
-  int64_t need = (R + slots - 1) / slots;
-  const int64_t cap = 296ll * 2;  // upper bound of the grid on any sm_100 part with up to 296 SMs
-  if (need > cap) need = cap;
-  if (need < 1) need = 1;
-  return need * (2 * D + 1) * (int64_t)sizeof(float);
+  if (D < 32 || D > 4 * 32 * spk::lnlif::kMaxCpt || R < 0) return 0;
+  // the larger of the backward's two possible grids on the current device (one
+  // partial row per block)
+  const int g1 = spk::lnlif::bwd_grid(R, (int)D, true), g2 = spk::lnlif::bwd_grid(R, (int)D, false);
+  return (int64_t)(g1 > g2 ? g1 : g2) * (3 * D + 1) * (int64_t)sizeof(float);
 }
 
-int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* ln_gamma, const float* ln_beta, float ln_eps,
+int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
+                   const float* ln_beta, float ln_eps,
                    const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain, int64_t T,
                    int64_t R, int64_t D, void* spikes, int spike_dtype, float* stats, void* stream) {
   using namespace spk;
@@ -512,30 +777,33 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* ln_gamma, const 
   SPK_REQUIRE(spike_dtype >= SPK_F32 && spike_dtype <= SPK_U8, SPK_ERR_INVALID, "spike dtype %d", spike_dtype);
   if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
   if (R == 0) return SPK_OK;
-  FwdParams p = {pre, pre_dtype, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain, spikes,
-                 spike_dtype, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0};
-  const int nw = pick_nw((int)D);
-  p.cpt = (int)D / (32 * nw);
-  const int grid = grid_blocks(R, nw, 8);
+  FwdParams p = {pre, pre_dtype, pre_bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain,
+                 spikes, spike_dtype, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // exact-size register arrays for 12 columns per thread (D = 384, 1536), else up to 16
-  if (p.cpt == 12)
-    nw == 1 ? ln_lif_fwd_kernel<1, 4, 12><<<grid, kThreads, 0, st>>>(p)
-            : ln_lif_fwd_kernel<4, 4, 12><<<grid, kThreads, 0, st>>>(p);
-  else if (p.cpt % 4 == 0)
-    nw == 1 ? ln_lif_fwd_kernel<1, 4, kMaxCpt><<<grid, kThreads, 0, st>>>(p)
-            : ln_lif_fwd_kernel<4, 4, kMaxCpt><<<grid, kThreads, 0, st>>>(p);
-  else
-    nw == 1 ? ln_lif_fwd_kernel<1, 1, kMaxCpt><<<grid, kThreads, 0, st>>>(p)
-            : ln_lif_fwd_kernel<4, 1, kMaxCpt><<<grid, kThreads, 0, st>>>(p);
+  const bool aligned16 = tok_aligned({pre, spikes, ln_gamma, ln_beta, pre_bias});
+  SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
+              "D=%lld > %d needs pre, spikes, ln_gamma, ln_beta and pre_bias 16-byte aligned", (long long)D,
+              32 * kMaxCpt);
+  if (use_tok((int)D) && aligned16) {
+    const int grid = tok_grid(R, (int)D), threads = (int)D / 4;
+    if (pre_dtype == SPK_F32)
+      ln_lif_fwd_tok_kernel<4><<<grid, threads, 0, st>>>(p);
+    else
+      ln_lif_fwd_tok_kernel<2><<<grid, threads, 0, st>>>(p);
+  } else {
+    // D not a multiple of 128 (so D <= 512): one warp per token, single columns
+    const int nw = pick_nw((int)D);
+    p.cpt = (int)D / (32 * nw);
+    ln_lif_fwd_kernel<1, 1, kMaxCpt><<<grid_blocks(R, nw, 8), kThreads, 0, st>>>(p);
+  }
   return check_launch("ln_lif_fwd_kernel");
 }
 
-int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype, const float* stats,
-                   const float* ln_gamma, const float* ln_beta, const float* lif_beta, const float* lif_vth,
-                   const float* lif_vreset, float in_gain, int surrogate, float surrogate_k, int64_t T, int64_t R,
-                   int64_t D, void* g_pre, float* g_gamma, float* g_beta_ln, float* g_lif_beta, void* workspace,
-                   int64_t workspace_bytes, void* stream) {
+int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype, const float* pre_bias,
+                   const float* stats, const float* ln_gamma, const float* ln_beta, const float* lif_beta,
+                   const float* lif_vth, const float* lif_vreset, float in_gain, int surrogate, float surrogate_k,
+                   int64_t T, int64_t R, int64_t D, void* g_pre, float* g_gamma, float* g_beta_ln, float* g_bias,
+                   float* g_lif_beta, void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace spk;
   int rc = check_ln_lif((int)T, R, (int)D);
   if (rc != SPK_OK) return rc;
@@ -553,32 +821,39 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
               (long long)workspace_bytes, (long long)need);
   if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int nw = pick_nw((int)D);
-  const int grid = R == 0 ? 1 : grid_blocks(R, nw);
-  SPK_REQUIRE((int64_t)grid * (2 * D + 1) * 4 <= workspace_bytes, SPK_ERR_INVALID, "workspace too small for %d blocks",
+  const bool aligned16 = tok_aligned({g_spikes, pre, g_pre, ln_gamma, ln_beta, pre_bias});
+  SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
+              "D=%lld > %d needs g_spikes, pre, g_pre, ln_gamma, ln_beta and pre_bias 16-byte aligned",
+              (long long)D, 32 * kMaxCpt);
+  const int grid = bwd_grid(R, (int)D, aligned16);
+  SPK_REQUIRE((int64_t)grid * (3 * D + 1) * 4 <= workspace_bytes, SPK_ERR_INVALID, "workspace too small for %d blocks",
               grid);
   float* part = reinterpret_cast<float*>(workspace);
   if (R == 0) {
-    cudaError_t e = cudaMemsetAsync(part, 0, (size_t)(2 * D + 1) * 4, st);
+    cudaError_t e = cudaMemsetAsync(part, 0, (size_t)(3 * D + 1) * 4, st);
     if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   } else {
-    BwdParams p = {g_spikes, gs_dtype, pre, pre_dtype, reinterpret_cast<const float2*>(stats), ln_gamma, ln_beta,
-                   lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
+    BwdParams p = {g_spikes, gs_dtype, pre, pre_dtype, pre_bias, reinterpret_cast<const float2*>(stats), ln_gamma,
+                   ln_beta, lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
                    (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k), g_pre, part, (int)T, R, (int)D, 0};
-    p.cpt = (int)D / (32 * nw);
-    if (p.cpt == 12)
-      nw == 1 ? ln_lif_bwd_kernel<1, 4, 12><<<grid, kThreads, 0, st>>>(p)
-              : ln_lif_bwd_kernel<4, 4, 12><<<grid, kThreads, 0, st>>>(p);
-    else if (p.cpt % 4 == 0)
-      nw == 1 ? ln_lif_bwd_kernel<1, 4, kMaxCpt><<<grid, kThreads, 0, st>>>(p)
-              : ln_lif_bwd_kernel<4, 4, kMaxCpt><<<grid, kThreads, 0, st>>>(p);
-    else
-      nw == 1 ? ln_lif_bwd_kernel<1, 1, kMaxCpt><<<grid, kThreads, 0, st>>>(p)
-              : ln_lif_bwd_kernel<4, 1, kMaxCpt><<<grid, kThreads, 0, st>>>(p);
+    if (use_tok((int)D) && aligned16) {
+      const int threads = (int)D / 4;
+      const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;
+      if (p32)
+        g32 ? ln_lif_bwd_tok_kernel<4, 4><<<grid, threads, 0, st>>>(p)
+            : ln_lif_bwd_tok_kernel<4, 2><<<grid, threads, 0, st>>>(p);
+      else
+        g32 ? ln_lif_bwd_tok_kernel<2, 4><<<grid, threads, 0, st>>>(p)
+            : ln_lif_bwd_tok_kernel<2, 2><<<grid, threads, 0, st>>>(p);
+    } else {
+      // D not a multiple of 128 (so D <= 512): one warp per token, single columns
+      p.cpt = (int)D / 32;
+      ln_lif_bwd_kernel<1, 1, kMaxCpt><<<grid, kThreads, 0, st>>>(p);
+    }
     if ((rc = check_launch("ln_lif_bwd_kernel")) != SPK_OK) return rc;
   }
-  const int W = 2 * (int)D + 1;
-  sum_columns_kernel<<<(W + 31) / 32, 256, 0, st>>>(part, grid, W, g_gamma, g_beta_ln, g_lif_beta, (int)D);
+  const int W = 3 * (int)D + 1;
+  sum_columns_kernel<<<(W + 31) / 32, 256, 0, st>>>(part, grid, W, g_gamma, g_beta_ln, g_bias, g_lif_beta, (int)D);
   return check_launch("sum_columns_kernel");
 }
 

@@ -122,8 +122,9 @@ def ln_lif_ok(T, D):
 
 
 def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
-               spike_dtype=torch.float32):
-    """``LIF(LayerNorm(pre))`` over the t-major fold; ``pre`` ``[T*R, ..., D]``.
+               spike_dtype=torch.float32, bias=None):
+    """``LIF(LayerNorm(pre + bias))`` over the t-major fold; ``pre`` ``[T*R, ..., D]``,
+    ``bias`` ``[D]`` or None (the preceding Linear's bias, taken out of its GEMM).
     Returns ``(spikes like pre in spike_dtype, stats fp32 [T*R', 2] (mean, rstd))``."""
     _cuda(pre)
     pre = pre.contiguous()
@@ -137,8 +138,10 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
     stats = torch.empty((rows, 2), dtype=torch.float32, device=dev)
     g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
     bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
+    pb = None if bias is None else bias.detach().float().contiguous()
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
-    _lib.call("spk_ln_lif_fwd", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(g), _lib.ptr(bt), float(ln_eps),
+    _lib.call("spk_ln_lif_fwd", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(pb), _lib.ptr(g), _lib.ptr(bt),
+              float(ln_eps),
               _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, _lib.ptr(spikes),
               _lib.DTYPE_CODE[spike_dtype], _lib.ptr(stats), _lib.stream_ptr(dev), tag="ln_lif_fwd D=%d" % D,
               work=dict(bytes=rows * D * (pre.element_size() + spikes.element_size()) + rows * 8))
@@ -146,9 +149,10 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
 
 
 def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
-               surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True):
+               surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True, bias=None,
+               need_bias=False):
     """Backward of ``ln_lif_fwd``: ``(g_pre like pre, g_gamma [D] or None, g_beta [D] or None,
-    g_lif_beta [1] or None)``."""
+    g_lif_beta [1] or None, g_bias [D] or None)``; ``bias`` is the forward's."""
     _cuda(g_spikes, pre, stats)
     pre = pre.contiguous()
     g_spikes = g_spikes.contiguous()
@@ -162,17 +166,20 @@ def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_v
     gg = torch.empty(D, dtype=torch.float32, device=dev) if need_gamma else None
     gb = torch.empty(D, dtype=torch.float32, device=dev) if need_beta else None
     glb = torch.empty(1, dtype=torch.float32, device=dev) if need_lif_beta else None
+    gpb = torch.empty(D, dtype=torch.float32, device=dev) if need_bias else None
+    pb = None if bias is None else bias.detach().float().contiguous()
     wsb = int(_lib.load().spk_ln_lif_bwd_workspace_bytes(T, R, D))
     ws = torch.empty(wsb // 4, dtype=torch.float32, device=dev)
     g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
     bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
     _lib.call("spk_ln_lif_bwd", _lib.ptr(g_spikes), _lib.dtype_code(g_spikes), _lib.ptr(pre), _lib.dtype_code(pre),
-              _lib.ptr(stats), _lib.ptr(g), _lib.ptr(bt), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain),
-              _lib.SURROGATE[surrogate], float(k), T, R, D, _lib.ptr(g_pre), _lib.ptr(gg), _lib.ptr(gb),
-              _lib.ptr(glb), _lib.ptr(ws), wsb, _lib.stream_ptr(dev), tag="ln_lif_bwd D=%d" % D,
+              _lib.ptr(pb), _lib.ptr(stats), _lib.ptr(g), _lib.ptr(bt), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr),
+              float(in_gain), _lib.SURROGATE[surrogate], float(k), T, R, D, _lib.ptr(g_pre), _lib.ptr(gg),
+              _lib.ptr(gb), _lib.ptr(gpb), _lib.ptr(glb), _lib.ptr(ws), wsb, _lib.stream_ptr(dev),
+              tag="ln_lif_bwd D=%d" % D,
               work=dict(bytes=rows * D * (g_spikes.element_size() + 2 * pre.element_size()) + rows * 8))
-    return g_pre, gg, gb, glb
+    return g_pre, gg, gb, glb, gpb
 
 
 def linear(A, W, bias=None):

@@ -383,6 +383,8 @@ def test_no_device_timeouts(ops):
     (2, 50, 64, torch.float32, "superspike", 0.7),
     (3, 17, 96, torch.float32, "arctan", 1.0),
     (1, 5, 512, torch.float32, "superspike", 1.0),
+    (2, 9, 1536, torch.float32, "superspike", 1.0),
+    (4, 30, 256, torch.float16, "arctan", 1.0),
 ])
 def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
     g = gen(T * 100 + R + D)
@@ -392,23 +394,28 @@ def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
     lif_beta = torch.tensor(0.8)
     k = 2.0 if surrogate == "arctan" else 4.0
     gs = torch.randn(T * R, D, generator=g)
+    # the Linear's bias handed to the kernels on every other case
+    bias = 0.2 * torch.randn(D, generator=g) if R % 2 == 0 else None
     # reference: torch LayerNorm (fp32) composed with the oracle's autograd LIF
     x = pre.float().clone().requires_grad_(True)
     w = gamma.clone().requires_grad_(True)
     b = beta_ln.clone().requires_grad_(True)
     lb = lif_beta.clone().requires_grad_(True)
-    y = F.layer_norm(x, (D,), w, b, 1e-5)
+    pb = None if bias is None else bias.clone().requires_grad_(True)
+    y = F.layer_norm(x if pb is None else x + pb, (D,), w, b, 1e-5)
     s_ref, _ = oracle.lif.LIFFunction.apply(y.view(T, R, D), lb, torch.tensor(1.0), torch.tensor(0.0), k, surrogate,
                                             gain)
     (s_ref * gs.view(T, R, D)).sum().backward()
     # ours
+    bias_dev = None if bias is None else bias.to(DEV)
     s, stats = ops.ln_lif_fwd(pre.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, lif_beta, 1.0, 0.0, T,
-                              in_gain=gain)
-    g_pre, g_w, g_b, g_lb = ops.ln_lif_bwd(gs.to(DEV), pre.to(DEV), stats, gamma.to(DEV), beta_ln.to(DEV),
-                                           lif_beta, 1.0, 0.0, T, gain, surrogate, k)
+                              in_gain=gain, bias=bias_dev)
+    g_pre, g_w, g_b, g_lb, g_pb = ops.ln_lif_bwd(gs.to(DEV), pre.to(DEV), stats, gamma.to(DEV), beta_ln.to(DEV),
+                                                 lif_beta, 1.0, 0.0, T, gain, surrogate, k, bias=bias_dev,
+                                                 need_bias=bias is not None)
     vh = membrane_history(y.detach().view(T, -1), lif_beta, 1.0, 0.0, gain)
     assert_spikes_match(s.cpu().view(T, -1), s_ref.detach().view(T, -1), vh, 1.0, what="ln_lif spikes")
-    mean = x.detach().mean(-1)
+    mean = (x.detach() if bias is None else x.detach() + bias).mean(-1)
     assert torch.allclose(stats[:, 0].cpu(), mean, rtol=1e-4, atol=1e-5)
     # gradients on the rows whose spike train matches (a flipped near-threshold spike changes the
     # backward of its token)
@@ -422,6 +429,27 @@ def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
         assert_close_rel(g_w.cpu(), w.grad, tol=tol, what="g_gamma")
         assert_close_rel(g_b.cpu(), b.grad, tol=tol, what="g_beta")
         assert abs(g_lb.item() - lb.grad.item()) <= tol * max(1.0, abs(lb.grad.item()))
+        if bias is not None:
+            assert_close_rel(g_pb.cpu(), pb.grad, tol=tol, what="g_bias")
+
+
+def test_ln_lif_train_unaligned_inputs(ops):
+    """The vectorised one-token-per-block kernels need 16-byte aligned rows:
+    an input offset by one element takes the scalar kernels (D <= 512) with the
+    same results, or is rejected (D > 512)."""
+    g = gen(11)
+    T, R, D = 4, 6, 384
+    flat = torch.randn(T * R * D + 1, generator=g).to(DEV)
+    pre_off = flat[1:].view(T * R, D)            # 4-byte offset
+    pre_al = pre_off.clone()
+    bias = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    s1, st1 = ops.ln_lif_fwd(pre_off, None, None, 1e-5, 0.8, 1.0, 0.0, T, bias=bias)
+    s2, st2 = ops.ln_lif_fwd(pre_al, None, None, 1e-5, 0.8, 1.0, 0.0, T, bias=bias)
+    assert torch.equal(s1, s2)
+    assert torch.allclose(st1, st2, rtol=1e-6, atol=1e-6)
+    wide = torch.randn(T * 2 * 1536 + 1, generator=g).to(DEV)[1:].view(T * 2, 1536)
+    with pytest.raises(RuntimeError):
+        ops.ln_lif_fwd(wide, None, None, 1e-5, 0.8, 1.0, 0.0, T)
 
 
 def test_ln_lif_train_rejects_unsupported(ops):

@@ -77,6 +77,41 @@ def test_ssa_golden(pkg, golden_dir, path):
                             what=f"ssa {c['variant']} {c['case']} {path}")
 
 
+@pytest.mark.parametrize("Nq,Nk,dtype", [(40, 70, torch.float32), (64, 256, torch.bfloat16), (33, 5, torch.float32)])
+def test_xnor_score_free_training_core(pkg, Nq, Nk, dtype):
+    """The tensor-core autograd core of the unmasked XNOR attention against the
+    dense reference formula (``SSA.py:145-165``, ``:235-240``) in float64:
+    forward bit for bit, gradients of Q, K, V and the scale within 1e-4 of
+    the largest gradient (split-bf16 products)."""
+    from spikingtransformer_b200.SSA import SSAMultiHeadAttention, XnorScoreFree
+    TB, H, dh = 6, 3, 48
+    m = SSAMultiHeadAttention(d_model=H * dh, n_heads=H).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(Nq + Nk)
+    leaves = [(torch.rand(TB, n, H, dh, generator=g, device=DEV) < 0.3).to(dtype).requires_grad_()
+              for n in (Nq, Nk, Nk)]
+    q, k, v = (t.transpose(1, 2) for t in leaves)
+    R = m.get_log_pe_bias_cross(Nq, Nk, DEV)
+    out = XnorScoreFree.apply(q, k, v, R, m.scale)
+    w = torch.randn(out.shape, generator=g, device=DEV)
+    (out * w).sum().backward()
+
+    ref_leaves = [t.detach().double().requires_grad_() for t in leaves]
+    rq, rk, rv = (t.transpose(1, 2) for t in ref_leaves)
+    rs = m.scale.detach().double().requires_grad_()
+    S = dh - (rq.sum(-1, keepdim=True) + rk.sum(-1, keepdim=True).transpose(2, 3) - 2 * rq @ rk.transpose(2, 3))
+    ref = ((S + R.double()) * rs) @ rv
+    (ref * w.double()).sum().backward()
+    assert out.dtype == torch.float32 and torch.equal(out, ref.float())
+    for name, a, b in (("q", leaves[0].grad, ref_leaves[0].grad), ("k", leaves[1].grad, ref_leaves[1].grad),
+                       ("v", leaves[2].grad, ref_leaves[2].grad)):
+        assert a.dtype == dtype
+        err = (a.double() - b).abs().max().item()
+        tol = 1e-4 if dtype == torch.float32 else 1e-2  # bf16 gradients carry 8 bits
+        assert err <= tol * b.abs().max().item(), (name, err, b.abs().max().item())
+    gs_bound = (w.double().abs() * ref.detach().abs()).sum().item() / abs(rs.item())
+    assert abs(m.scale.grad.item() - rs.grad.item()) <= 1e-5 * gs_bound
+
+
 def test_mlp_golden(pkg, golden_dir):
     from spikingtransformer_b200.SpikingMLP import SpikingMLP
     c = load(golden_dir, "mlp.pt")
