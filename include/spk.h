@@ -139,14 +139,18 @@ int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void
  *   reset.  pre_bias ([D] fp32 or NULL) is the preceding Linear's bias, so
  *   that Linear can run without one.
  * pre: [T][R][D] (f32/f16/bf16); spikes: [T][R][D] in spike_dtype;
+ * With head_dim > 0 the spikes are written head-major instead,
+ * [T*B][D/head_dim][seq_len][head_dim] with R = B * seq_len (the layout of
+ * SSA.py's per-head Q, K, V, :221-233), for D % 128 == 0 only.
  * stats: [T*R] (mean, rstd) float pairs for the backward.  ln_gamma /
  * ln_beta may be NULL (1 / 0).  T <= 4; D a multiple of 32 up to 512, or of
  * 128 up to 2048.
  */
 int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
                    const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
-                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, void* spikes,
-                   int spike_dtype, float* stats, void* stream);
+                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D,
+                   int64_t head_dim, int64_t seq_len, void* spikes, int spike_dtype, float* stats,
+                   void* stream);
 
 /*
  * Backward of spk_ln_lif_fwd (LIFLayer.backward Lif.py:46-102 composed with
@@ -157,7 +161,8 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
  *   g_lif_beta = sum g_v v_prev
  * (sums over all rows, reduced in a fixed order).  g_spikes: f32/f16/bf16;
  * g_pre has pre's dtype; pre_bias is the forward's; g_gamma / g_beta_ln /
- * g_bias / g_lif_beta may be NULL.
+ * g_bias / g_lif_beta may be NULL.  head_dim / seq_len: the forward's;
+ * g_spikes is then read head-major.
  * workspace: spk_ln_lif_bwd_workspace_bytes(T, R, D) bytes.
  */
 int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D);
@@ -165,8 +170,9 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
                    const float* pre_bias, const float* stats, const float* ln_gamma,
                    const float* ln_beta, const float* lif_beta, const float* lif_vth,
                    const float* lif_vreset, float in_gain, int surrogate, float surrogate_k, int64_t T,
-                   int64_t R, int64_t D, void* g_pre, float* g_gamma, float* g_beta_ln, float* g_bias,
-                   float* g_lif_beta, void* workspace, int64_t workspace_bytes, void* stream);
+                   int64_t R, int64_t D, int64_t head_dim, int64_t seq_len, void* g_pre, float* g_gamma,
+                   float* g_beta_ln, float* g_bias, float* g_lif_beta, void* workspace,
+                   int64_t workspace_bytes, void* stream);
 
 /*
  * Fused Linear -> LayerNorm -> LIF (tcgen05, bf16 operands, fp32 accumulate).
@@ -260,6 +266,50 @@ int64_t spk_ce_over_t_workspace_bytes(int64_t rows);
 int spk_ce_over_t(const void* logits, int dtype, const int64_t* targets, int64_t T, int64_t rows, int64_t V,
                   int64_t ignore_index, float label_smoothing, float* out, void* grad, void* workspace,
                   int64_t workspace_bytes, int* bad_target, void* stream);
+
+/*
+ * Memory-bound passes of the training-path XNOR attention core, the autograd
+ * regrouping of SSAMultiHeadAttention's unmasked attention (SSA.py:145-165,
+ * :177-201, :235-240; the reference differentiates the dense score matrix
+ * instead).  With B = TB*H heads and M = 2 K^T V - 1 (1^T V)^T,
+ * w = (dh - |k|)^T V, the forward is m = Q M + R V + 1 w^T; the products run
+ * as library GEMMs with fp32 accumulation.  dh % 4 == 0, fp32 buffers
+ * 16-byte aligned.
+ *
+ * combine: out[tb][n][h][:] = (qm[b][n][:] + rv[n][b][:] + w[b][:]) * scale[0]
+ *   with b = tb*H + h; qm [B][Nq][dh], rv [Nq][B][dh], w [B][dh] fp32; out
+ *   token-major [TB][Nq][H][dh] fp32.
+ */
+int spk_xnor_train_combine(const float* qm, const float* rv, const float* w, const float* scale, float* out,
+                           int64_t TB, int64_t H, int64_t Nq, int64_t dh, void* stream);
+
+/*
+ * Row chunks of spk_xnor_train_grad_prep's partial sums (16 rows each).
+ */
+int64_t spk_xnor_train_prep_chunks(int64_t Nq);
+
+/*
+ * grad_prep: from the token-major gradient g [TB][Nq][H][dh] fp32 and the
+ * forward's out, gs = g * scale[0] split into bf16 hi = bf16(gs) and
+ * lo = bf16(gs - hi):
+ *   g_heads [B][Nq][2 dh] bf16 (hi | lo along the last dimension),
+ *   g_rows  [Nq][2][B][dh] bf16 (hi block, lo block),
+ *   gcol_part [C][B][dh] fp32 (sums of gs over each chunk of 16 rows),
+ *   gscale_part [C][B*dh/4] fp32 (partial sums of g * out),
+ * C = spk_xnor_train_prep_chunks(Nq).
+ */
+int spk_xnor_train_grad_prep(const float* g, const float* out, const float* scale, void* g_heads, void* g_rows,
+                             float* gcol_part, float* gscale_part, int64_t TB, int64_t H, int64_t Nq, int64_t dh,
+                             void* stream);
+
+/*
+ * grad_finish: dv[b][j][:] = ke[b][j][:] + rg[j][b][:] + u[b][:] and
+ * dk = dk32, both written in out_dtype (SPK_F32 / SPK_F16 / SPK_BF16),
+ * head-major [B][Nk][dh]; ke, dk32 [B][Nk][dh], rg [Nk][B][dh], u [B][dh]
+ * fp32.
+ */
+int spk_xnor_train_grad_finish(const float* ke, const float* rg, const float* u, const float* dk32, void* dk,
+                               void* dv, int out_dtype, int64_t TB, int64_t H, int64_t Nk, int64_t dh, void* stream);
 
 #ifdef __cplusplus
 }

@@ -104,9 +104,6 @@ class _SSACore(nn.Module):
 
     # ---------------------------------------------------------------- autograd path
 
-    def _heads(self, t, n):
-        return t.view(t.shape[0], n, self.n_heads, self.d_head).transpose(1, 2)
-
     def _scores(self, q, k):
         raise NotImplementedError
 
@@ -114,12 +111,15 @@ class _SSACore(nn.Module):
         TB, N, D = query.shape
         Nk = key.shape[1]
         # Q, K, V spikes feed only the attention products, so under autocast
-        # they are written in its dtype (0/1 exact)
-        q = self._heads(lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True), N)
-        k = self._heads(lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True), Nk)
-        v = self._heads(lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True), Nk)
+        # they are written in its dtype (0/1 exact), per head [TB, H, N, dh]
+        hd = self.d_head
+        q = lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True, heads=(hd, N))
+        k = lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True, heads=(hd, Nk))
+        v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk))
+        # token-major [TB, N, D]; the lifs LIF is per neuron, so it commutes with
+        # the reference's transpose back from heads (SSA.py:242-247)
         a = self._combine(q, k, v, attention_mask)
-        s = self.lifs(a)[0].transpose(1, 2).contiguous().view(TB, N, D)
+        s = self.lifs(a)[0]
         return lin_ln_lif_train(s, self.out_proj, self.lno, self.lifo)
 
     def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
@@ -177,10 +177,12 @@ class SSAMultiHeadAttention(_SSACore):
         return torch.ceil(torch.log2((L - 1) / (dist + 1))).clamp(min=0)
 
     def _combine(self, q, k, v, mask):
+        """Attention core before the lifs LIF: q [TB, H, Nq, dh], k / v [TB, H,
+        Nk, dh] -> token-major [TB, Nq, H*dh]."""
         if mask is not None:
             a = self.xnor_attention(q, k)
             a = a + self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device).unsqueeze(0).unsqueeze(0)
-            return (a * mask * self.scale) @ v
+            return _token_major((a * mask * self.scale) @ v)
         # Without a mask the score matrix regroups exactly (spikes are 0/1):
         #   S V = 2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V,  s_j = |k_j|,
         # so neither S nor its gradient is formed.
@@ -196,7 +198,13 @@ class SSAMultiHeadAttention(_SSACore):
             m = m + (dh - qf.sum(-1, keepdim=True)) * vf.sum(-2, keepdim=True)
             m = m - kf.sum(-1).unsqueeze(-2) @ vf
             m = m + R @ vf
-            return m * self.scale
+            return _token_major(m * self.scale)
+
+
+def _token_major(a):
+    """[TB, H, N, dh] -> [TB, N, H*dh]."""
+    TB, H, N, dh = a.shape
+    return a.transpose(1, 2).reshape(TB, N, H * dh)
 
 
 def _split_bf16(x):
@@ -206,25 +214,18 @@ def _split_bf16(x):
 
 
 def _flat_bf16(t):
-    """[TB, H, N, d] of any strides -> contiguous bf16 [TB*H, N, d] in one pass."""
-    out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
-    out.copy_(t)
-    return out.view(-1, t.shape[-2], t.shape[-1])
+    """[TB, H, N, d] of any strides -> contiguous bf16 [TB*H, N, d] (no copy when
+    it already is, else one pass)."""
+    if t.dtype != torch.bfloat16 or not t.is_contiguous():
+        out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
+        out.copy_(t)
+        t = out
+    return t.view(-1, t.shape[-2], t.shape[-1])
 
 
 def _bmm32(a, b):
     """bf16 x bf16 -> fp32 batched product on the tensor cores."""
     return torch.bmm(a, b, out_dtype=torch.float32)
-
-
-def _mm_shared(Rb, x, transpose=False):
-    """``R @ x[b]`` (or ``R^T @ x[b]``) for every batch b of ``x`` [B, N, d] as one
-    [Nq, Nk] x [Nk, B*d] product; bf16 in, fp32 out, [B, N', d]."""
-    B, N, d = x.shape
-    A = Rb.t() if transpose else Rb
-    xp = x.permute(1, 0, 2).reshape(N, B * d)
-    y = torch.mm(A, xp, out_dtype=torch.float32)
-    return y.view(A.shape[0], B, d).permute(1, 0, 2)
 
 
 class XnorScoreFree(torch.autograd.Function):
@@ -233,66 +234,74 @@ class XnorScoreFree(torch.autograd.Function):
     ``m = scale * [2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V]`` with
     ``s_j = |k_j|``, which equals ``(S * scale) @ V`` for the reference's
     ``S = dh - (|q_i| + |k_j| - 2 q_i.k_j) + R`` (``SSA.py:145-165``,
-    ``:177-201``, ``:235-240``) when Q, K, V are 0/1.
+    ``:177-201``, ``:235-240``) when Q, K, V are 0/1.  Grouped as
+    ``m / scale = Q M + R V + 1 w^T`` with the small ``M = 2 K^T V - 1 (1^T V)^T``
+    and ``w = (dh - s)^T V``.
 
-    Forward: every operand is an integer that bf16 holds exactly (spikes, the
-    counts ``K^T V <= Nk <= 256``, ``|k_j| <= dh``, ``R <= 8``) and every
-    product accumulates in fp32, so ``m / scale`` is exact and equals the fp32
-    formulation bit for bit.  Backward: the real-valued gradient operands are
-    split into two bf16 terms (hi + lo, about 2^-16 relative), each product
-    runs on the tensor cores with fp32 accumulation, and the halves are added.
+    Forward: every operand is an integer that bf16 holds exactly (spikes,
+    ``|M| <= Nk <= 256``, ``dh - s_j <= dh``, ``R <= 8``) and every product
+    accumulates in fp32, so ``m / scale`` is exact and the output equals the
+    fp32 formulation bit for bit.  Backward: the real-valued gradient operands
+    are split into two bf16 terms (hi + lo, about 2^-16 relative); with
+    ``E = 2 dM - 1 gcol^T`` (``gcol`` the column sums of the scaled gradient)
+    the rank-one terms fold into the products: ``dQ = G M^T``,
+    ``dK = V E^T``, ``dV = K E + R^T G + 1 u^T``.  Everything between the
+    library GEMMs runs in three memory-bound kernels (``xnor_train.cu``).
 
     Inputs: q [TB, H, Nq, dh], k and v [TB, H, Nk, dh] (0/1 in any float
     dtype, any strides), R [Nq, Nk] fp32, scale a 0-d parameter.  Output: fp32
-    [TB, H, Nq, dh].
+    token-major [TB, Nq, H*dh] (the layout the output projection reads).
     """
 
     @staticmethod
     def forward(ctx, q, k, v, R, scale):
         with torch.autocast("cuda", enabled=False):
-            dh = q.shape[-1]
+            TB, H, Nq, dh = q.shape
+            Nk = k.shape[2]
             qb, kb, vb = (_flat_bf16(t) for t in (q, k, v))
+            B = qb.shape[0]
             Rb = R.to(torch.bfloat16)
             kv = _bmm32(kb.transpose(1, 2), vb)                           # [B, dh, dh]
             cv = vb.sum(1, keepdim=True, dtype=torch.float32)              # 1^T V  [B, 1, dh]
             sk = kb.sum(2, keepdim=True, dtype=torch.float32)              # |k_j|  [B, Nk, 1]
-            qs = qb.sum(2, keepdim=True, dtype=torch.float32)              # |q_i|  [B, Nq, 1]
-            m = 2.0 * _bmm32(qb, kv.to(torch.bfloat16))
-            m = m + (dh - qs) * cv
-            m = m - _bmm32(sk.transpose(1, 2).to(torch.bfloat16), vb)
-            m = m + _mm_shared(Rb, vb)
-            out = (m * scale.float()).view(q.shape)
-        ctx.save_for_backward(qb, kb, vb, kv, cv, sk, qs, Rb, m, scale)
+            Mb = (2.0 * kv - cv).to(torch.bfloat16)                        # exact: |M| <= Nk
+            w = _bmm32((dh - sk).transpose(1, 2).to(torch.bfloat16), vb)   # [B, 1, dh]
+            qm = _bmm32(qb, Mb)                                            # [B, Nq, dh]
+            rv = torch.mm(Rb, vb.permute(1, 0, 2).reshape(Nk, B * dh), out_dtype=torch.float32)
+            out = ops.xnor_train_combine(qm, rv, w, scale, TB, H)
+        ctx.save_for_backward(qb, kb, vb, Mb, Rb, out, scale)
         ctx.meta = ((q.dtype, q.shape), (k.dtype, k.shape), (v.dtype, v.shape))
         return out
 
     @staticmethod
     def backward(ctx, g):
-        qb, kb, vb, kv, cv, sk, qs, Rb, m, scale = ctx.saved_tensors
-        dh = qb.shape[-1]
-        with torch.autocast("cuda", enabled=False):
-            g = g.float().reshape(m.shape)
-            gscale = (g * m).sum().reshape(scale.shape).to(scale.dtype)
-            gs = g * scale.float()                                         # dL/dm
-            gh, gl = _split_bf16(gs)
-            gcol = gs.sum(1, keepdim=True)                                 # 1^T G  [B, 1, dh]
-            # dQ = 2 G (K^T V)^T - (G . 1^T V) 1^T
-            kvt = kv.to(torch.bfloat16).transpose(1, 2)
-            dq = 2.0 * (_bmm32(gh, kvt) + _bmm32(gl, kvt))
-            dq = dq - (gs * cv).sum(-1, keepdim=True)
-            # d(K^T V) = 2 Q^T G
-            qt = qb.transpose(1, 2)
-            dkv = 2.0 * (_bmm32(qt, gh) + _bmm32(qt, gl))                   # [B, dh, dh]
-            dkh, dkl = _split_bf16(dkv)
-            # dK = V d(K^T V)^T - (V . 1^T G) 1^T
-            dk = _bmm32(vb, dkh.transpose(1, 2)) + _bmm32(vb, dkl.transpose(1, 2))
-            dk = dk - (vb.float() * gcol).sum(-1, keepdim=True)
-            # dV = K d(K^T V) + 1 ((dh - |q|)^T G) - s (1^T G) + R^T G
-            dv = _bmm32(kb, dkh) + _bmm32(kb, dkl)
-            dv = dv + ((dh - qs) * gs).sum(1, keepdim=True) - sk * gcol
-            dv = dv + _mm_shared(Rb, gh, transpose=True) + _mm_shared(Rb, gl, transpose=True)
+        qb, kb, vb, Mb, Rb, out, scale = ctx.saved_tensors
         (tq, sq), (tk, sk_), (tv, sv) = ctx.meta
-        return dq.to(tq).view(sq), dk.to(tk).view(sk_), dv.to(tv).view(sv), None, gscale
+        TB, H, Nq, dh = sq
+        B, Nk = kb.shape[0], kb.shape[1]
+        with torch.autocast("cuda", enabled=False):
+            g_heads, g_rows, gcol, gdot = ops.xnor_train_grad_prep(g, out, scale, H, dh)
+            gscale = (gdot / scale.float()).reshape(scale.shape).to(scale.dtype)   # sum(g * m)
+            # dQ = G M^T with G = hi | lo against [M^T; M^T]
+            mt = Mb.transpose(1, 2)
+            mt2 = torch.cat([mt, mt], dim=1)                               # [B, 2dh, dh]
+            # one fp32-accumulated product, rounded once to q's dtype
+            dq = torch.bmm(g_heads, mt2) if tq == torch.bfloat16 else _bmm32(g_heads, mt2).to(tq)
+            # dM = Q^T G, E = 2 dM - 1 gcol^T, u = -1^T dM + dh gcol
+            dm2 = _bmm32(qb.transpose(1, 2), g_heads)                      # [B, dh, 2dh]
+            dm = dm2[..., :dh] + dm2[..., dh:]
+            e = 2.0 * dm - gcol.unsqueeze(1)
+            u = dh * gcol - dm.sum(1)
+            eh, el = _split_bf16(e)
+            bf = torch.ops.aten.baddbmm.dtype
+            dk32 = bf(_bmm32(vb, eh.transpose(1, 2)), vb, el.transpose(1, 2), torch.float32)   # V E^T
+            ke = bf(_bmm32(kb, eh), kb, el, torch.float32)                                       # K E
+            rt = Rb.t()
+            rg = torch.ops.aten.addmm.dtype(
+                torch.mm(rt, g_rows[:, 0].reshape(Nq, B * dh), out_dtype=torch.float32), rt,
+                g_rows[:, 1].reshape(Nq, B * dh), torch.float32)                                 # R^T G
+            dk, dv = ops.xnor_train_grad_finish(ke, rg, u, dk32, TB, H, tk)
+        return dq.view(sq), dk.view(sk_), dv.to(tv).view(sv), None, gscale
 
 
 class SSAMultiHeadAttention_(_SSACore):
@@ -316,7 +325,7 @@ class SSAMultiHeadAttention_(_SSACore):
         a = q @ k.transpose(-2, -1)
         if mask is not None:
             a = a * mask
-        return (a @ v) * 0.125
+        return _token_major((a @ v) * 0.125)
 
 
 _ = math  # kept for parity with the reference module namespace

@@ -93,15 +93,15 @@ class LNLIFFunction(torch.autograd.Function):
     None): its GEMM runs without one and the bias gradient comes out of the
     backward kernel.  Gradients: pre, the Linear bias, the LayerNorm weight and
     bias, and the LIF beta.  Spikes are written in ``spike_dtype`` (0/1 are
-    exact in every float type)."""
+    exact in every float type), head-major when ``heads = (head_dim, seq_len)``."""
 
     @staticmethod
     def forward(ctx, pre, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset, eps, k, surrogate, in_gain, T,
-                spike_dtype):
+                spike_dtype, heads=None):
         spikes, stats = ops.ln_lif_fwd(pre, ln_weight, ln_bias, eps, lif_beta, v_th, v_reset, T, in_gain,
-                                       spike_dtype=spike_dtype, bias=bias)
+                                       spike_dtype=spike_dtype, bias=bias, heads=heads)
         ctx.save_for_backward(pre, stats, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset)
-        ctx.k, ctx.surrogate, ctx.in_gain, ctx.T = float(k), surrogate, float(in_gain), int(T)
+        ctx.k, ctx.surrogate, ctx.in_gain, ctx.T, ctx.heads = float(k), surrogate, float(in_gain), int(T), heads
         return spikes
 
     @staticmethod
@@ -111,12 +111,12 @@ class LNLIFFunction(torch.autograd.Function):
         g_pre, gw, gb, glb, gpb = ops.ln_lif_bwd(g_spikes, pre, stats, w, b, lb, vth, vr, ctx.T, ctx.in_gain,
                                                  ctx.surrogate, ctx.k, need_gamma=need[2], need_beta=need[3],
                                                  need_lif_beta=need[4], bias=pb,
-                                                 need_bias=pb is not None and need[1])
+                                                 need_bias=pb is not None and need[1], heads=ctx.heads)
         gpb = gpb.to(pb.dtype) if gpb is not None else None
         gw = gw.to(w.dtype) if gw is not None else None
         gb = gb.to(b.dtype) if gb is not None else None
         glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
-        return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, None
+        return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, None, None
 
 
 def _ln_lif_fusable(x, D, ln, lif):
@@ -139,16 +139,25 @@ def ln_lif(x, ln, lif):
     return lif(ln(x))[0]
 
 
-def lin_ln_lif_train(x, lin, ln, lif, narrow=False):
+def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None):
     """``lif(ln(lin(x)))[0]`` on the autograd path.  With the fused kernels the
     GEMM (``F.linear``, under whatever autocast is active) runs without the bias,
     which the LayerNorm->LIF kernels add and differentiate.  ``narrow``: under
     autocast, write the spikes in the autocast dtype; meant for spikes whose
-    consumer is a GEMM that casts to that dtype anyway."""
-    if _ln_lif_fusable(x, lin.out_features, ln, lif):
+    consumer is a GEMM that casts to that dtype anyway.  ``heads = (head_dim,
+    n)`` for ``x`` ``[TB, n, D]``: return the spikes as ``[TB, D/head_dim, n,
+    head_dim]``, written in that layout by the kernel where it can."""
+    D = lin.out_features
+    if _ln_lif_fusable(x, D, ln, lif):
         pre = torch.nn.functional.linear(x, lin.weight)
         dt = torch.float32
         if narrow and torch.is_autocast_enabled(x.device.type):
             dt = torch.get_autocast_dtype(x.device.type)
-        return LNLIFFunction.apply(pre, lin.bias, *_lif_args(ln, lif), dt)
-    return ln_lif(lin(x), ln, lif)
+        direct = heads is not None and D % 128 == 0 and heads[0] % 4 == 0 and D % heads[0] == 0
+        out = LNLIFFunction.apply(pre, lin.bias, *_lif_args(ln, lif), dt, heads if direct else None)
+        if heads is None or direct:
+            return out
+    else:
+        out = ln_lif(lin(x), ln, lif)
+    hd, n = heads
+    return out.view(-1, n, D // hd, hd).transpose(1, 2)

@@ -38,10 +38,10 @@ SIGNATURES = {
     "spk_linear_ln_lif_fwd": ([_p, _p, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _p, _i, _p,
                                _p, _p], _i),
     "spk_linear_fwd": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),
-    "spk_ln_lif_fwd": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _p, _i, _p, _p], _i),
+    "spk_ln_lif_fwd": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),
     "spk_ln_lif_bwd_workspace_bytes": ([_i64, _i64, _i64], _i64),
-    "spk_ln_lif_bwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _f, _i, _f, _i64, _i64, _i64, _p, _p, _p, _p, _p,
-                        _p, _i64, _p], _i),
+    "spk_ln_lif_bwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _f, _i, _f, _i64, _i64, _i64, _i64, _i64, _p,
+                        _p, _p, _p, _p, _p, _i64, _p], _i),
     "spk_ssa_fwd": ([_p, _p, _p, _i, _i, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64,
                      _i64, _i64, _p, _i, _p, _p], _i),
     "spk_embed_pe_lif_fwd": ([_p, _p, _f, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),
@@ -49,6 +49,10 @@ SIGNATURES = {
     "spk_synth_text_lines": ([_p, _i64, _i64, _i64, ctypes.c_uint64, _p, _i64, _i64, _p], _i),
     "spk_ce_over_t_workspace_bytes": ([_i64], _i64),
     "spk_ce_over_t": ([_p, _i, _p, _i64, _i64, _i64, _i64, _f, _p, _p, _p, _i64, _p, _p], _i),
+    "spk_xnor_train_combine": ([_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
+    "spk_xnor_train_prep_chunks": ([_i64], _i64),
+    "spk_xnor_train_grad_prep": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
+    "spk_xnor_train_grad_finish": ([_p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p], _i),
 }
 
 _lib = None

@@ -55,6 +55,7 @@ struct FwdParams {
   int T;
   int64_t R;
   int D, cpt;
+  int hd, seq;  // head-major spikes [T*B][D/hd][seq][hd] when hd > 0 (R = B * seq)
 };
 
 struct BwdParams {
@@ -75,6 +76,7 @@ struct BwdParams {
   int T;
   int64_t R;
   int D, cpt;
+  int hd, seq;  // head-major spikes [T*B][D/hd][seq][hd] when hd > 0 (R = B * seq)
 };
 
 __device__ __forceinline__ float load_elem(const void* p, int dt, int64_t i) {
@@ -489,6 +491,34 @@ __global__ void __launch_bounds__(kThreads) ln_lif_bwd_kernel(const BwdParams p)
   }
 }
 
+// Offsets of a lane's four columns c in the spikes / their gradient: row-major
+// [T*R][D], or head-major [T*B][D/hd][seq][hd] for attention (token r = b*seq
+// + n, column c = h*hd + d), the layout the attention products read.
+// Row (t, r) starts at t * t_stride + tok_off(r); the lane adds col_off.
+struct SpikeLayout {
+  int64_t t_stride;  // elements between step t and t + 1 of one token
+  int64_t col_off;   // the lane's column offset within a token row
+  int hd, seq;
+  int64_t head_block;  // seq * hd
+  __device__ __forceinline__ SpikeLayout(int64_t R, int D, int c, int hd_, int seq_) : hd(hd_), seq(seq_) {
+    t_stride = R * D;  // both layouts: [T][R*D] with B = R / seq
+    if (hd <= 0) {
+      col_off = c;
+      head_block = 0;
+    } else {
+      const int h = c / hd;
+      head_block = (int64_t)seq * hd;
+      col_off = h * head_block + (c - h * hd);
+    }
+  }
+  __device__ __forceinline__ int64_t tok_off(int64_t tok, int D) const {
+    if (hd <= 0) return tok * D;
+    const int ti = (int)tok;  // R < 2^31 in this layout
+    const int b = ti / seq, n = ti - b * seq;  // one 32-bit division per token
+    return (int64_t)b * D * seq + (int64_t)n * hd;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // One token per block (D % 128 == 0): NW = D / 128 warps, four consecutive
 // columns per lane, so one 8- or 16-byte vector per row and lane.  The
@@ -534,7 +564,9 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
   const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
+  const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
   for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
+    const int64_t so = lay.tok_off(tok, D) + lay.col_off;
     RawVec<EB> raw[kMaxT];
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t)
@@ -566,7 +598,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
         x[e] = sp ? 1.0f : 0.0f;
         v[e] = sp ? vr : u;
       }
-      store4(p.spikes, p.spike_dtype, row * D + c, x);
+      store4(p.spikes, p.spike_dtype, so + t * lay.t_stride, x);
     }
   }
 }
@@ -590,7 +622,9 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const
   const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
   float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f}, acc_d[4] = {0.f, 0.f, 0.f, 0.f};
   float acc_lb = 0.0f;
+  const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
   for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
+    const int64_t so = lay.tok_off(tok, D) + lay.col_off;
     RawVec<EBP> rp[kMaxT];
     RawVec<EBG> rg[kMaxT];
     float2 st[kMaxT];
@@ -601,7 +635,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const
       const int64_t row = (int64_t)t * p.R + tok;
       st[t] = p.stats[row];
       raw_load<EBP>(rp[t], p.pre, row * D + c);
-      raw_load<EBG>(rg[t], p.g_spikes, row * D + c);
+      raw_load<EBG>(rg[t], p.g_spikes, so + t * lay.t_stride);
     }
     // membrane before reset at every step
     float u[kMaxT][4];
@@ -741,6 +775,18 @@ inline int bwd_grid(int64_t R, int D, bool aligned16) {
 
 using namespace lnlif;
 
+// head-major spike layout (head_dim > 0): only the one-token-per-block kernels
+static int check_heads(int64_t head_dim, int64_t seq_len, int64_t R, int D, bool tok_ok) {
+  if (head_dim <= 0) return SPK_OK;
+  SPK_REQUIRE(tok_ok, SPK_ERR_SHAPE,
+              "head-major spikes need D %% 128 == 0 (D=%d) and 16-byte aligned pointers", D);
+  SPK_REQUIRE(head_dim % 4 == 0 && D % head_dim == 0 && seq_len >= 1 && R % seq_len == 0 && R < (1ll << 31),
+              SPK_ERR_SHAPE,
+              "head-major spikes: head_dim=%lld must be a multiple of 4 dividing D=%d, and seq_len=%lld must "
+              "divide R=%lld", (long long)head_dim, D, (long long)seq_len, (long long)R);
+  return SPK_OK;
+}
+
 static int check_ln_lif(int T, int64_t R, int D) {
   SPK_REQUIRE(T >= 1 && T <= kMaxT, SPK_ERR_SHAPE, "T=%d outside [1, %d]", T, kMaxT);
   SPK_REQUIRE(R >= 0, SPK_ERR_SHAPE, "R negative");
@@ -764,9 +810,9 @@ int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D) {
 }
 
 int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
-                   const float* ln_beta, float ln_eps,
-                   const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain, int64_t T,
-                   int64_t R, int64_t D, void* spikes, int spike_dtype, float* stats, void* stream) {
+                   const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
+                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, int64_t head_dim,
+                   int64_t seq_len, void* spikes, int spike_dtype, float* stats, void* stream) {
   using namespace spk;
   int rc = check_ln_lif((int)T, R, (int)D);
   if (rc != SPK_OK) return rc;
@@ -778,12 +824,14 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
   if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
   if (R == 0) return SPK_OK;
   FwdParams p = {pre, pre_dtype, pre_bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain,
-                 spikes, spike_dtype, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0};
+                 spikes, spike_dtype, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0,
+                 (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1)};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool aligned16 = tok_aligned({pre, spikes, ln_gamma, ln_beta, pre_bias});
   SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
               "D=%lld > %d needs pre, spikes, ln_gamma, ln_beta and pre_bias 16-byte aligned", (long long)D,
               32 * kMaxCpt);
+  if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
   if (use_tok((int)D) && aligned16) {
     const int grid = tok_grid(R, (int)D), threads = (int)D / 4;
     if (pre_dtype == SPK_F32)
@@ -802,8 +850,9 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
 int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype, const float* pre_bias,
                    const float* stats, const float* ln_gamma, const float* ln_beta, const float* lif_beta,
                    const float* lif_vth, const float* lif_vreset, float in_gain, int surrogate, float surrogate_k,
-                   int64_t T, int64_t R, int64_t D, void* g_pre, float* g_gamma, float* g_beta_ln, float* g_bias,
-                   float* g_lif_beta, void* workspace, int64_t workspace_bytes, void* stream) {
+                   int64_t T, int64_t R, int64_t D, int64_t head_dim, int64_t seq_len, void* g_pre, float* g_gamma,
+                   float* g_beta_ln, float* g_bias, float* g_lif_beta, void* workspace, int64_t workspace_bytes,
+                   void* stream) {
   using namespace spk;
   int rc = check_ln_lif((int)T, R, (int)D);
   if (rc != SPK_OK) return rc;
@@ -825,6 +874,7 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
   SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
               "D=%lld > %d needs g_spikes, pre, g_pre, ln_gamma, ln_beta and pre_bias 16-byte aligned",
               (long long)D, 32 * kMaxCpt);
+  if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
   const int grid = bwd_grid(R, (int)D, aligned16);
   SPK_REQUIRE((int64_t)grid * (3 * D + 1) * 4 <= workspace_bytes, SPK_ERR_INVALID, "workspace too small for %d blocks",
               grid);
@@ -835,7 +885,8 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
   } else {
     BwdParams p = {g_spikes, gs_dtype, pre, pre_dtype, pre_bias, reinterpret_cast<const float2*>(stats), ln_gamma,
                    ln_beta, lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
-                   (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k), g_pre, part, (int)T, R, (int)D, 0};
+                   (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k), g_pre, part, (int)T, R, (int)D, 0,
+                   (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1)};
     if (use_tok((int)D) && aligned16) {
       const int threads = (int)D / 4;
       const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;

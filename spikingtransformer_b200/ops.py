@@ -122,9 +122,11 @@ def ln_lif_ok(T, D):
 
 
 def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
-               spike_dtype=torch.float32, bias=None):
+               spike_dtype=torch.float32, bias=None, heads=None):
     """``LIF(LayerNorm(pre + bias))`` over the t-major fold; ``pre`` ``[T*R, ..., D]``,
     ``bias`` ``[D]`` or None (the preceding Linear's bias, taken out of its GEMM).
+    ``heads=(head_dim, seq_len)``: spikes written head-major, ``[T*R/seq_len,
+    D/head_dim, seq_len, head_dim]`` (the per-head layout the attention reads).
     Returns ``(spikes like pre in spike_dtype, stats fp32 [T*R', 2] (mean, rstd))``."""
     _cuda(pre)
     pre = pre.contiguous()
@@ -134,7 +136,9 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
         raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
     R = rows // T
     dev = pre.device
-    spikes = torch.empty(pre.shape, dtype=spike_dtype, device=dev)
+    hd, sl = heads if heads is not None else (0, 1)
+    shape = pre.shape if heads is None else (rows // sl, D // hd, sl, hd)
+    spikes = torch.empty(shape, dtype=spike_dtype, device=dev)
     stats = torch.empty((rows, 2), dtype=torch.float32, device=dev)
     g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
     bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
@@ -142,7 +146,7 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
     _lib.call("spk_ln_lif_fwd", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(pb), _lib.ptr(g), _lib.ptr(bt),
               float(ln_eps),
-              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, _lib.ptr(spikes),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, hd, sl, _lib.ptr(spikes),
               _lib.DTYPE_CODE[spike_dtype], _lib.ptr(stats), _lib.stream_ptr(dev), tag="ln_lif_fwd D=%d" % D,
               work=dict(bytes=rows * D * (pre.element_size() + spikes.element_size()) + rows * 8))
     return spikes, stats
@@ -150,9 +154,10 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
 
 def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
                surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True, bias=None,
-               need_bias=False):
+               need_bias=False, heads=None):
     """Backward of ``ln_lif_fwd``: ``(g_pre like pre, g_gamma [D] or None, g_beta [D] or None,
-    g_lif_beta [1] or None, g_bias [D] or None)``; ``bias`` is the forward's."""
+    g_lif_beta [1] or None, g_bias [D] or None)``; ``bias`` and ``heads`` are the
+    forward's (with ``heads``, ``g_spikes`` is head-major like the spikes)."""
     _cuda(g_spikes, pre, stats)
     pre = pre.contiguous()
     g_spikes = g_spikes.contiguous()
@@ -168,6 +173,7 @@ def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_v
     glb = torch.empty(1, dtype=torch.float32, device=dev) if need_lif_beta else None
     gpb = torch.empty(D, dtype=torch.float32, device=dev) if need_bias else None
     pb = None if bias is None else bias.detach().float().contiguous()
+    hd, sl = heads if heads is not None else (0, 1)
     wsb = int(_lib.load().spk_ln_lif_bwd_workspace_bytes(T, R, D))
     ws = torch.empty(wsb // 4, dtype=torch.float32, device=dev)
     g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
@@ -175,7 +181,7 @@ def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_v
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
     _lib.call("spk_ln_lif_bwd", _lib.ptr(g_spikes), _lib.dtype_code(g_spikes), _lib.ptr(pre), _lib.dtype_code(pre),
               _lib.ptr(pb), _lib.ptr(stats), _lib.ptr(g), _lib.ptr(bt), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr),
-              float(in_gain), _lib.SURROGATE[surrogate], float(k), T, R, D, _lib.ptr(g_pre), _lib.ptr(gg),
+              float(in_gain), _lib.SURROGATE[surrogate], float(k), T, R, D, hd, sl, _lib.ptr(g_pre), _lib.ptr(gg),
               _lib.ptr(gb), _lib.ptr(gpb), _lib.ptr(glb), _lib.ptr(ws), wsb, _lib.stream_ptr(dev),
               tag="ln_lif_bwd D=%d" % D,
               work=dict(bytes=rows * D * (g_spikes.element_size() + 2 * pre.element_size()) + rows * 8))
@@ -344,3 +350,56 @@ def ce_over_t(logits, targets, ignore_index=-100, label_smoothing=0.0):
 def device_error_check(device=None):
     """Synchronise and raise if a kernel's bounded wait gave up."""
     _lib.call("spk_device_error_check", _lib.stream_ptr(device))
+
+
+# ------------------------------------------------- training-path XNOR attention core
+
+
+def xnor_train_combine(qm, rv, w, scale, TB, H):
+    """``(qm + rv + w) * scale`` -> token-major ``[TB, Nq, H*dh]`` fp32; ``qm``
+    ``[B, Nq, dh]``, ``rv`` ``[Nq, B*dh]``, ``w`` ``[B, 1, dh]`` fp32, ``B = TB*H``."""
+    _cuda(qm, rv, w)
+    B, Nq, dh = qm.shape
+    qm, rv, w = qm.contiguous(), rv.contiguous(), w.contiguous()
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, qm.device)
+    out = torch.empty((TB, Nq, H * dh), dtype=torch.float32, device=qm.device)
+    _lib.call("spk_xnor_train_combine", _lib.ptr(qm), _lib.ptr(rv), _lib.ptr(w), _lib.ptr(sc), _lib.ptr(out), TB, H,
+              Nq, dh, _lib.stream_ptr(qm.device), tag="xnor_train_combine",
+              work=dict(bytes=3 * out.numel() * 4))
+    return out
+
+
+def xnor_train_grad_prep(g, out, scale, H, dh):
+    """From the token-major gradient ``g`` and forward output ``out``
+    (``[TB, Nq, H*dh]`` fp32): ``(g_heads [B, Nq, 2dh] bf16, g_rows [Nq, 2, B, dh]
+    bf16, gcol [B, dh] fp32, sum(g * out))`` with ``gs = g * scale`` split hi | lo."""
+    _cuda(g, out)
+    g = g.float().contiguous()
+    out = out.contiguous()
+    TB, Nq, D = g.shape
+    B = TB * H
+    dev = g.device
+    C = int(_lib.load().spk_xnor_train_prep_chunks(Nq))
+    g_heads = torch.empty((B, Nq, 2 * dh), dtype=torch.bfloat16, device=dev)
+    g_rows = torch.empty((Nq, 2, B, dh), dtype=torch.bfloat16, device=dev)
+    gcol_part = torch.empty((C, B, dh), dtype=torch.float32, device=dev)
+    gsc_part = torch.empty((C, B * dh // 4), dtype=torch.float32, device=dev)
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, dev)
+    _lib.call("spk_xnor_train_grad_prep", _lib.ptr(g), _lib.ptr(out), _lib.ptr(sc), _lib.ptr(g_heads),
+              _lib.ptr(g_rows), _lib.ptr(gcol_part), _lib.ptr(gsc_part), TB, H, Nq, dh, _lib.stream_ptr(dev),
+              tag="xnor_train_grad_prep", work=dict(bytes=g.numel() * 16))
+    return g_heads, g_rows, gcol_part.sum(0), gsc_part.sum()
+
+
+def xnor_train_grad_finish(ke, rg, u, dk32, TB, H, out_dtype):
+    """``(dk, dv)`` head-major ``[B, Nk, dh]`` in ``out_dtype``: ``dv = ke + rg^P + u``,
+    ``dk = dk32``; ``rg`` ``[Nk, B*dh]``, ``u`` ``[B, dh]``."""
+    _cuda(ke, rg, u, dk32)
+    B, Nk, dh = ke.shape
+    ke, rg, u, dk32 = ke.contiguous(), rg.contiguous(), u.contiguous(), dk32.contiguous()
+    dk = torch.empty((B, Nk, dh), dtype=out_dtype, device=ke.device)
+    dv = torch.empty((B, Nk, dh), dtype=out_dtype, device=ke.device)
+    _lib.call("spk_xnor_train_grad_finish", _lib.ptr(ke), _lib.ptr(rg), _lib.ptr(u), _lib.ptr(dk32), _lib.ptr(dk),
+              _lib.ptr(dv), _lib.DTYPE_CODE[out_dtype], TB, H, Nk, dh, _lib.stream_ptr(ke.device),
+              tag="xnor_train_grad_finish", work=dict(bytes=ke.numel() * 20))
+    return dk, dv

@@ -433,6 +433,33 @@ def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
             assert_close_rel(g_pb.cpu(), pb.grad, tol=tol, what="g_bias")
 
 
+@pytest.mark.parametrize("pre_dtype,gs_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
+def test_ln_lif_train_head_major_spikes(ops, pre_dtype, gs_dtype):
+    """Spikes written per head, [T*B, H, N, dh] (the layout the attention reads),
+    and their gradient read in that layout, equal the row-major results
+    transposed."""
+    g = gen(21)
+    T, B, N, H, dh = 4, 3, 20, 8, 48
+    D = H * dh
+    pre = (torch.randn(T * B * N, D, generator=g) * 1.3 + 0.2).to(pre_dtype).to(DEV)
+    bias = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    gamma = (1.0 + 0.2 * torch.randn(D, generator=g)).to(DEV)
+    s_rm, st_rm = ops.ln_lif_fwd(pre, gamma, None, 1e-5, 0.8, 1.0, 0.0, T, bias=bias, spike_dtype=torch.bfloat16)
+    s_hm, st_hm = ops.ln_lif_fwd(pre, gamma, None, 1e-5, 0.8, 1.0, 0.0, T, bias=bias, spike_dtype=torch.bfloat16,
+                                 heads=(dh, N))
+    assert s_hm.shape == (T * B, H, N, dh) and s_hm.is_contiguous()
+    assert torch.equal(s_hm, s_rm.view(T * B, N, H, dh).transpose(1, 2))
+    assert torch.equal(st_hm, st_rm)
+    gs_hm = torch.randn(T * B, H, N, dh, generator=g).to(gs_dtype).to(DEV)
+    gs_rm = gs_hm.transpose(1, 2).reshape(T * B * N, D).contiguous()
+    a = ops.ln_lif_bwd(gs_rm, pre, st_rm, gamma, None, 0.8, 1.0, 0.0, T, 1.0, "arctan", 2.0, need_beta=False,
+                       bias=bias, need_bias=True)
+    b = ops.ln_lif_bwd(gs_hm, pre, st_hm, gamma, None, 0.8, 1.0, 0.0, T, 1.0, "arctan", 2.0, need_beta=False,
+                       bias=bias, need_bias=True, heads=(dh, N))
+    for x, y in zip(a, b):
+        assert (x is None and y is None) or torch.equal(x, y)
+
+
 def test_ln_lif_train_unaligned_inputs(ops):
     """The vectorised one-token-per-block kernels need 16-byte aligned rows:
     an input offset by one element takes the scalar kernels (D <= 512) with the

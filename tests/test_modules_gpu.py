@@ -99,7 +99,7 @@ def test_xnor_score_free_training_core(pkg, Nq, Nk, dtype):
     rq, rk, rv = (t.transpose(1, 2) for t in ref_leaves)
     rs = m.scale.detach().double().requires_grad_()
     S = dh - (rq.sum(-1, keepdim=True) + rk.sum(-1, keepdim=True).transpose(2, 3) - 2 * rq @ rk.transpose(2, 3))
-    ref = ((S + R.double()) * rs) @ rv
+    ref = (((S + R.double()) * rs) @ rv).transpose(1, 2).reshape(TB, Nq, H * dh)  # token-major, as ours
     (ref * w.double()).sum().backward()
     assert out.dtype == torch.float32 and torch.equal(out, ref.float())
     for name, a, b in (("q", leaves[0].grad, ref_leaves[0].grad), ("k", leaves[1].grad, ref_leaves[1].grad),
