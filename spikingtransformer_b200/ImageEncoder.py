@@ -133,10 +133,39 @@ class PatchEmbed(nn.Module):
         """The T-fold of ``src [B, C, H, W]`` repeated over T, computed once per image."""
         return self._fused(src, t_broadcast=True)
 
+    def _project(self, x):
+        """The 16x16 / stride-16 convolution without its bias as one GEMM:
+        ``[N, C, H, W]`` -> ``[N, (H/p)(W/p), D]`` in the order of
+        ``proj(x).flatten(2).transpose(1, 2)`` (H and W multiples of p)."""
+        p = self.patch_size
+        N, C, H, W = x.shape
+        a = x.reshape(N, C, H // p, p, W // p, p).permute(0, 2, 4, 1, 3, 5).reshape(N * (H // p) * (W // p), -1)
+        y = torch.nn.functional.linear(a, self.proj.weight.reshape(self.d_model, -1))
+        return y.view(N, (H // p) * (W // p), self.d_model)
+
+    def _tiles(self, x):
+        p = self.patch_size
+        return x.is_cuda and x.shape[-2] % p == 0 and x.shape[-1] % p == 0
+
     def forward(self, x):
         if fast_path_ok(x, module=self):
             s = self._fused(x, t_broadcast=False).float()
             return s, {"output": s}
-        y = self.proj(x).flatten(2).transpose(1, 2)
-        s = ln_lif(y, self.norm, self.lif)
+        if self._tiles(x):
+            # conv bias handed to the LayerNorm->LIF kernels
+            s = ln_lif(self._project(x), self.norm, self.lif, bias=self.proj.bias)
+        else:
+            s = ln_lif(self.proj(x).flatten(2).transpose(1, 2), self.norm, self.lif)
+        return s, {"output": s}
+
+    def forward_repeated(self, src, T):
+        """``forward`` of ``src [B, C, H, W]`` repeated T times along dim 0 (the
+        encoder input of ``Seq2Seq.py:98-104``), with the projection computed once
+        per image; its gradient sums over the T copies as the repeat's does."""
+        if not self._tiles(src):
+            B = src.shape[0]
+            return self(src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:]))
+        y = self._project(src)
+        y = y.unsqueeze(0).expand(T, *y.shape).reshape(T * y.shape[0], *y.shape[1:])
+        s = ln_lif(y, self.norm, self.lif, bias=self.proj.bias)
         return s, {"output": s}

@@ -140,8 +140,11 @@ class Seq2Seq(nn.Module):
             return self._encode_fast(src).float(), None
         B = src.shape[0]
         T = self.n_steps
-        src = src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:])
-        enc_output, _ = self.image_encoder(src)
+        if isinstance(self.image_encoder, PatchEmbed):
+            enc_output, _ = self.image_encoder.forward_repeated(src, T)
+        else:
+            src = src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:])
+            enc_output, _ = self.image_encoder(src)
         return self.encoder(enc_output), None
 
     def decode(self, tgt: Tensor, enc_output: Tensor, look_ahead_mask: Tensor = None,

@@ -130,13 +130,13 @@ def _lif_args(ln, lif):
             lif.in_gain, lif.n_steps)
 
 
-def ln_lif(x, ln, lif):
-    """``lif(ln(x))[0]`` on the autograd path: the fused training kernels when the
-    shapes allow (CUDA, affine LayerNorm over the last dimension), the module
-    composition otherwise (``Lif.py:288-441`` over torch's LayerNorm)."""
+def ln_lif(x, ln, lif, bias=None):
+    """``lif(ln(x + bias))[0]`` on the autograd path: the fused training kernels
+    when the shapes allow (CUDA, affine LayerNorm over the last dimension), the
+    module composition otherwise (``Lif.py:288-441`` over torch's LayerNorm)."""
     if _ln_lif_fusable(x, x.shape[-1], ln, lif):
-        return LNLIFFunction.apply(x, None, *_lif_args(ln, lif), torch.float32)
-    return lif(ln(x))[0]
+        return LNLIFFunction.apply(x, bias, *_lif_args(ln, lif), torch.float32)
+    return lif(ln(x if bias is None else x + bias))[0]
 
 
 def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None):

@@ -528,6 +528,7 @@ struct SpikeLayout {
 // two sums later, after a barrier that every reader has passed).
 
 constexpr int kTokMaxWarps = 16;  // D <= 2048
+constexpr int kTokPfWarps = 12;   // the prefetching backward: D <= 1536 (fits 170 registers)
 
 struct BlockSum {
   float2* red;  // [2][kTokMaxWarps]
@@ -565,12 +566,24 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
   const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
   const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
+  // the next token's rows are loaded while this one is processed
+  RawVec<EB> nxt[kMaxT];
+  if ((int64_t)blockIdx.x < p.R) {
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t)
+      if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + blockIdx.x) * D + c);
+  }
   for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
     const int64_t so = lay.tok_off(tok, D) + lay.col_off;
     RawVec<EB> raw[kMaxT];
 #pragma unroll
-    for (int t = 0; t < kMaxT; ++t)
-      if (t < T) raw_load<EB>(raw[t], p.pre, ((int64_t)t * p.R + tok) * D + c);
+    for (int t = 0; t < kMaxT; ++t) raw[t] = nxt[t];
+    const int64_t tn = tok + gridDim.x;
+    if (tn < p.R) {
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t)
+        if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + tn) * D + c);
+    }
     float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t) {
@@ -607,8 +620,8 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
 // the saved statistics, then the steps are walked backwards; BPTT of step t
 // gives dL/dy of row t, whose LayerNorm backward (one pair of block sums)
 // runs at once.
-template <int EBP, int EBG>
-__global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const BwdParams p) {
+template <int EBP, int EBG, bool PF>
+__global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const BwdParams p) {
   __shared__ float2 red[2 * kTokMaxWarps];
   BlockSum bs{red, 0};
   const int nw = blockDim.x >> 5;
@@ -623,19 +636,37 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const
   float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f}, acc_d[4] = {0.f, 0.f, 0.f, 0.f};
   float acc_lb = 0.0f;
   const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
-  for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
-    const int64_t so = lay.tok_off(tok, D) + lay.col_off;
-    RawVec<EBP> rp[kMaxT];
-    RawVec<EBG> rg[kMaxT];
-    float2 st[kMaxT];
+  RawVec<EBP> np_[kMaxT];
+  RawVec<EBG> ng_[kMaxT];
+  float2 ns_[kMaxT];
+  auto load_tok = [&](int64_t tk, RawVec<EBP>* rp, RawVec<EBG>* rg, float2* st) {
+    const int64_t so = lay.tok_off(tk, D) + lay.col_off;
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t) {
       st[t] = make_float2(0.0f, 1.0f);
       if (t >= T) continue;
-      const int64_t row = (int64_t)t * p.R + tok;
+      const int64_t row = (int64_t)t * p.R + tk;
       st[t] = p.stats[row];
       raw_load<EBP>(rp[t], p.pre, row * D + c);
       raw_load<EBG>(rg[t], p.g_spikes, so + t * lay.t_stride);
+    }
+  };
+  if (PF && (int64_t)blockIdx.x < p.R) load_tok(blockIdx.x, np_, ng_, ns_);
+  for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
+    RawVec<EBP> rp[kMaxT];
+    RawVec<EBG> rg[kMaxT];
+    float2 st[kMaxT];
+    if constexpr (PF) {
+      // this token's rows were loaded during the previous one; start the next
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t) {
+        rp[t] = np_[t];
+        rg[t] = ng_[t];
+        st[t] = ns_[t];
+      }
+      if (tok + gridDim.x < p.R) load_tok(tok + gridDim.x, np_, ng_, ns_);
+    } else {
+      load_tok(tok, rp, rg, st);
     }
     // membrane before reset at every step
     float u[kMaxT][4];
@@ -708,24 +739,25 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const
   if (threadIdx.x == 0) out[3 * D] = lbs;
 }
 
-// column c of the [rows][W] partials (dgamma, dbeta, dbias, LIF beta): 8 row
-// groups (rows r = g mod 8, in order) per column, combined in group order
-__global__ void __launch_bounds__(256) sum_columns_kernel(const float* __restrict__ part, int rows, int W,
+// column c of the [rows][W] partials (dgamma, dbeta, dbias, LIF beta): 32 row
+// groups (rows r = g mod 32, in order) per column, combined in group order
+constexpr int kSumGroups = 32;
+__global__ void __launch_bounds__(32 * kSumGroups) sum_columns_kernel(const float* __restrict__ part, int rows, int W,
                                                           float* __restrict__ dgamma, float* __restrict__ dbeta,
                                                           float* __restrict__ dbias, float* __restrict__ dlif_beta,
                                                           int D) {
-  __shared__ float acc[8][33];
+  __shared__ float acc[kSumGroups][33];
   const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + cl;
   float s = 0.0f;
   if (c < W)
-    for (int r = grp; r < rows; r += 8) s += part[(int64_t)r * W + c];
+    for (int r = grp; r < rows; r += kSumGroups) s += part[(int64_t)r * W + c];
   acc[grp][cl] = s;
   __syncthreads();
   if (grp != 0 || c >= W) return;
   s = acc[0][cl];
 #pragma unroll
-  for (int g = 1; g < 8; ++g) s += acc[g][cl];
+  for (int g = 1; g < kSumGroups; ++g) s += acc[g][cl];
   if (c < D) {
     if (dgamma) dgamma[c] = s;
   } else if (c < 2 * D) {
@@ -890,12 +922,21 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
     if (use_tok((int)D) && aligned16) {
       const int threads = (int)D / 4;
       const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;
-      if (p32)
-        g32 ? ln_lif_bwd_tok_kernel<4, 4><<<grid, threads, 0, st>>>(p)
-            : ln_lif_bwd_tok_kernel<4, 2><<<grid, threads, 0, st>>>(p);
-      else
-        g32 ? ln_lif_bwd_tok_kernel<2, 4><<<grid, threads, 0, st>>>(p)
-            : ln_lif_bwd_tok_kernel<2, 2><<<grid, threads, 0, st>>>(p);
+      if (D <= 128 * kTokPfWarps) {
+        if (p32)
+          g32 ? ln_lif_bwd_tok_kernel<4, 4, true><<<grid, threads, 0, st>>>(p)
+              : ln_lif_bwd_tok_kernel<4, 2, true><<<grid, threads, 0, st>>>(p);
+        else
+          g32 ? ln_lif_bwd_tok_kernel<2, 4, true><<<grid, threads, 0, st>>>(p)
+              : ln_lif_bwd_tok_kernel<2, 2, true><<<grid, threads, 0, st>>>(p);
+      } else {
+        if (p32)
+          g32 ? ln_lif_bwd_tok_kernel<4, 4, false><<<grid, threads, 0, st>>>(p)
+              : ln_lif_bwd_tok_kernel<4, 2, false><<<grid, threads, 0, st>>>(p);
+        else
+          g32 ? ln_lif_bwd_tok_kernel<2, 4, false><<<grid, threads, 0, st>>>(p)
+              : ln_lif_bwd_tok_kernel<2, 2, false><<<grid, threads, 0, st>>>(p);
+      }
     } else {
       // D not a multiple of 128 (so D <= 512): one warp per token, single columns
       p.cpt = (int)D / 32;
@@ -904,7 +945,8 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
     if ((rc = check_launch("ln_lif_bwd_kernel")) != SPK_OK) return rc;
   }
   const int W = 3 * (int)D + 1;
-  sum_columns_kernel<<<(W + 31) / 32, 256, 0, st>>>(part, grid, W, g_gamma, g_beta_ln, g_bias, g_lif_beta, (int)D);
+  sum_columns_kernel<<<(W + 31) / 32, 32 * kSumGroups, 0, st>>>(part, grid, W, g_gamma, g_beta_ln, g_bias,
+                                                                  g_lif_beta, (int)D);
   return check_launch("sum_columns_kernel");
 }
 
