@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from ._fused import fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train
+from ._fused import bf16_input, fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train
 from .Lif import LIF
 
 
@@ -113,9 +113,13 @@ class _SSACore(nn.Module):
         # Q, K, V spikes feed only the attention products, so under autocast
         # they are written in its dtype (0/1 exact), per head [TB, H, N, dh]
         hd = self.d_head
-        q = lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True, heads=(hd, N))
-        k = lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True, heads=(hd, Nk))
-        v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk))
+        # one bf16 copy of each distinct input for all the GEMMs that read it
+        qb = bf16_input(query)
+        kb = qb if key is query else bf16_input(key)
+        vb = kb if value is key else (qb if value is query else bf16_input(value))
+        q = lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True, heads=(hd, N), xb=qb)
+        k = lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True, heads=(hd, Nk), xb=kb)
+        v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk), xb=vb)
         # token-major [TB, N, D]; the lifs LIF is per neuron, so it commutes with
         # the reference's transpose back from heads (SSA.py:242-247)
         a = self._combine(q, k, v, attention_mask)

@@ -139,17 +139,67 @@ def ln_lif(x, ln, lif, bias=None):
     return lif(ln(x if bias is None else x + bias))[0]
 
 
-def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None):
+class LinearBF16(torch.autograd.Function):
+    """``x W^T`` (no bias) for the bf16-autocast training path: bf16 operands,
+    fp32 accumulation, bf16 output.  ``xb`` / ``wb`` are bf16 copies of x and W
+    made once and shared by every GEMM that reads them (Q, K and V read the same
+    x).  The backward GEMMs write the input and weight gradients directly in
+    x's and W's dtypes (fp32 output from fp32 accumulation), so no cast kernel
+    runs in either direction and fp32 gradients are summed in fp32."""
+
+    @staticmethod
+    def forward(ctx, x, w, xb, wb):
+        with torch.autocast(x.device.type, enabled=False):
+            y = torch.nn.functional.linear(xb, wb)
+        ctx.save_for_backward(xb, wb)
+        ctx.dtypes = (x.dtype, w.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        xb, wb = ctx.saved_tensors
+        tx, tw = ctx.dtypes
+        g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16)
+        dx = dw = None
+        with torch.autocast(gy.device.type, enabled=False):
+            if ctx.needs_input_grad[0]:
+                dx = torch.mm(g2, wb) if tx == torch.bfloat16 else torch.mm(g2, wb, out_dtype=torch.float32).to(tx)
+                dx = dx.view(*gy.shape[:-1], wb.shape[1])
+            if ctx.needs_input_grad[1]:
+                dw = torch.mm(g2.t(), xb.reshape(-1, xb.shape[-1]), out_dtype=torch.float32).to(tw)
+        return dx, dw, None, None
+
+
+def bf16_input(x):
+    """The bf16 copy of an activation that ``lin_ln_lif_train`` GEMMs read under
+    bf16 autocast (None otherwise); made once and passed to every consumer."""
+    if x.is_cuda and torch.is_autocast_enabled(x.device.type) and \
+            torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
+        return x.detach().to(torch.bfloat16) if x.dtype != torch.bfloat16 else x.detach()
+    return None
+
+
+def _linear_nobias(x, lin, xb):
+    if xb is None:
+        xb = bf16_input(x)
+    if xb is None or lin.weight.dtype not in (torch.float32, torch.bfloat16):
+        return torch.nn.functional.linear(x, lin.weight)
+    return LinearBF16.apply(x, lin.weight, xb, bf16_weight(lin))
+
+
+def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None, xb=None):
     """``lif(ln(lin(x)))[0]`` on the autograd path.  With the fused kernels the
-    GEMM (``F.linear``, under whatever autocast is active) runs without the bias,
-    which the LayerNorm->LIF kernels add and differentiate.  ``narrow``: under
-    autocast, write the spikes in the autocast dtype; meant for spikes whose
-    consumer is a GEMM that casts to that dtype anyway.  ``heads = (head_dim,
-    n)`` for ``x`` ``[TB, n, D]``: return the spikes as ``[TB, D/head_dim, n,
-    head_dim]``, written in that layout by the kernel where it can."""
+    GEMM runs without the bias, which the LayerNorm->LIF kernels add and
+    differentiate; under bf16 autocast it is ``LinearBF16`` on ``xb`` (the
+    shared bf16 copy of x from ``bf16_input``, made here if not given).
+    ``narrow``: under autocast, write the spikes in the autocast dtype; meant
+    for spikes whose consumer is a GEMM that reads that dtype.  ``heads =
+    (head_dim, n)`` for ``x`` ``[TB, n, D]``: return the spikes as ``[TB,
+    D/head_dim, n, head_dim]``, written in that layout by the kernel where it
+    can."""
     D = lin.out_features
     if _ln_lif_fusable(x, D, ln, lif):
-        pre = torch.nn.functional.linear(x, lin.weight)
+        pre = _linear_nobias(x, lin, xb)
         dt = torch.float32
         if narrow and torch.is_autocast_enabled(x.device.type):
             dt = torch.get_autocast_dtype(x.device.type)

@@ -112,6 +112,31 @@ def test_xnor_score_free_training_core(pkg, Nq, Nk, dtype):
     assert abs(m.scale.grad.item() - rs.grad.item()) <= 1e-5 * gs_bound
 
 
+def test_linear_bf16_training_gemm(pkg):
+    """The training path's bias-free bf16 GEMM against torch's autocast Linear:
+    the same bf16 output, and fp32 input / weight gradients at least as close
+    to the fp64 reference as autocast's (which round them to bf16 first)."""
+    from spikingtransformer_b200._fused import LinearBF16, bf16_input
+    g = torch.Generator(device=DEV).manual_seed(3)
+    lin = torch.nn.Linear(96, 160, bias=False).to(DEV)
+    x = torch.randn(4, 50, 96, generator=g, device=DEV, requires_grad=True)
+    gy = torch.randn(4, 50, 160, generator=g, device=DEV).to(torch.bfloat16)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        xb = bf16_input(x)
+        y = LinearBF16.apply(x, lin.weight, xb, lin.weight.detach().to(torch.bfloat16))
+        y_ref = torch.nn.functional.linear(x, lin.weight)
+    assert y.dtype == torch.bfloat16 and torch.equal(y, y_ref)
+    y.backward(gy)
+    dx, dw = x.grad.clone(), lin.weight.grad.clone()
+    assert dx.dtype == torch.float32 and dw.dtype == torch.float32
+    x64, w64 = x.detach().double(), lin.weight.detach().double()
+    xr, wr = x64.to(torch.bfloat16).double(), w64.to(torch.bfloat16).double()
+    dx64 = gy.double() @ wr
+    dw64 = gy.double().reshape(-1, 160).t() @ xr.reshape(-1, 96)
+    assert (dx.double() - dx64).abs().max() <= 1e-5 * dx64.abs().max()
+    assert (dw.double() - dw64).abs().max() <= 1e-5 * dw64.abs().max()
+
+
 def test_mlp_golden(pkg, golden_dir):
     from spikingtransformer_b200.SpikingMLP import SpikingMLP
     c = load(golden_dir, "mlp.pt")
