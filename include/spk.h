@@ -311,6 +311,31 @@ int spk_xnor_train_grad_prep(const float* g, const float* out, const float* scal
 int spk_xnor_train_grad_finish(const float* ke, const float* rg, const float* u, const float* dk32, void* dk,
                                void* dv, int out_dtype, int64_t TB, int64_t H, int64_t Nk, int64_t dh, void* stream);
 
+/*
+ * combine followed by the attention's output LIF (SSA.py:242, the LIF
+ * module of Lif.py:288-441 over the T-major fold, T <= 4, TB % T == 0):
+ * a_out <- the combined pre-activation (as spk_xnor_train_combine's out),
+ * spikes <- LIF(a_out) in spike_dtype (SPK_F32 / SPK_F16 / SPK_BF16), both
+ * token-major [TB][Nq][H][dh].  The LIF arithmetic is spk_lif_fwd's.
+ */
+int spk_xnor_train_combine_lif(const float* qm, const float* rv, const float* w, const float* scale,
+                               const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain,
+                               float* a_out, void* spikes, int spike_dtype, int64_t T, int64_t TB, int64_t H,
+                               int64_t Nq, int64_t dh, void* stream);
+
+/*
+ * grad_prep after the output LIF's backward: g_spikes (dL/dspikes,
+ * token-major, gs_dtype) and the pre-activation a give dL/da by BPTT with
+ * the surrogate (spk_lif_bwd's arithmetic), then the outputs of
+ * spk_xnor_train_grad_prep, except that gscale_part (and gbeta_part, the
+ * partial sums of the LIF beta gradient, or NULL) are [C][TB/T*H*dh/4].
+ */
+int spk_xnor_train_grad_prep_lif(const void* g_spikes, int gs_dtype, const float* a, const float* scale,
+                                 const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain,
+                                 int surrogate, float surrogate_k, void* g_heads, void* g_rows, float* gcol_part,
+                                 float* gscale_part, float* gbeta_part, int64_t T, int64_t TB, int64_t H, int64_t Nq,
+                                 int64_t dh, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -122,9 +122,12 @@ class _SSACore(nn.Module):
         v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk), xb=vb)
         # token-major [TB, N, D]; the lifs LIF is per neuron, so it commutes with
         # the reference's transpose back from heads (SSA.py:242-247)
-        a = self._combine(q, k, v, attention_mask)
-        s = self.lifs(a)[0]
+        s = self._combine_lif(q, k, v, attention_mask)
         return lin_ln_lif_train(s, self.out_proj, self.lno, self.lifo)
+
+    def _combine_lif(self, q, k, v, mask):
+        """lifs(attention core) -> token-major spikes [TB, N, H*dh]."""
+        return self.lifs(self._combine(q, k, v, mask))[0]
 
     def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -180,6 +183,21 @@ class SSAMultiHeadAttention(_SSACore):
         L = max(seq_len_q, seq_len_k)
         return torch.ceil(torch.log2((L - 1) / (dist + 1))).clamp(min=0)
 
+    def _combine_lif(self, q, k, v, mask):
+        lifs = self.lifs
+        TB, H, Nq, dh = q.shape
+        if (mask is None and q.is_cuda and k.shape[2] <= 256 and dh <= 256 and dh % 4 == 0
+                and 1 <= lifs.n_steps <= 4 and TB % lifs.n_steps == 0):
+            # the core and the lifs LIF in the same kernels; spikes feed only
+            # the output projection, so under autocast they take its dtype
+            dt = torch.float32
+            if torch.is_autocast_enabled(q.device.type):
+                dt = torch.get_autocast_dtype(q.device.type)
+            R = self.get_log_pe_bias_cross(Nq, k.shape[2], q.device)
+            return XnorLIF.apply(q, k, v, R, self.scale, lifs.effective_beta(), lifs.v_th, lifs.v_reset,
+                                 lifs.in_gain, lifs.surrogate, lifs._k_host, lifs.n_steps, dt)
+        return super()._combine_lif(q, k, v, mask)
+
     def _combine(self, q, k, v, mask):
         """Attention core before the lifs LIF: q [TB, H, Nq, dh], k / v [TB, H,
         Nk, dh] -> token-major [TB, Nq, H*dh]."""
@@ -227,9 +245,70 @@ def _flat_bf16(t):
     return t.view(-1, t.shape[-2], t.shape[-1])
 
 
+_ONES = {}
+
+
+def _ones_bf16(r, c, device):
+    key = (r, c, device)
+    t = _ONES.get(key)
+    if t is None:
+        t = _ONES[key] = torch.ones((r, c), dtype=torch.bfloat16, device=device)
+    return t
+
+
 def _bmm32(a, b):
     """bf16 x bf16 -> fp32 batched product on the tensor cores."""
     return torch.bmm(a, b, out_dtype=torch.float32)
+
+
+def _xnor_products(q, k, v, R):
+    """Forward products of the regrouped core: ``(qb, kb, vb, Mb, Rb, qm, rv, w)``
+    with ``m / scale = qm + rv^P + w`` (see ``XnorScoreFree``)."""
+    TB, H, Nq, dh = q.shape
+    Nk = k.shape[2]
+    qb, kb, vb = (_flat_bf16(t) for t in (q, k, v))
+    B = qb.shape[0]
+    Rb = R.to(torch.bfloat16)
+    kv = _bmm32(kb.transpose(1, 2), vb)                           # [B, dh, dh]
+    # |k_j| as a product with a ones vector; then [1; dh - |k|]^T V gives
+    # 1^T V and w in one product (all exact)
+    sk = torch.mm(kb.view(-1, dh), _ones_bf16(dh, 1, kb.device), out_dtype=torch.float32).view(B, 1, Nk)
+    lw = torch.cat([torch.ones_like(sk), dh - sk], dim=1).to(torch.bfloat16)   # [B, 2, Nk]
+    cw = _bmm32(lw, vb)                                            # [B, 2, dh]
+    cv, w = cw[:, :1], cw[:, 1:]
+    Mb = (2.0 * kv - cv).to(torch.bfloat16)                        # exact: |M| <= Nk
+    qm = _bmm32(qb, Mb)                                            # [B, Nq, dh]
+    rv = torch.mm(Rb, vb.permute(1, 0, 2).reshape(Nk, B * dh), out_dtype=torch.float32)
+    return qb, kb, vb, Mb, Rb, qm, rv, w
+
+
+def _xnor_backward(qb, kb, vb, Mb, Rb, g_heads, g_rows, gcol, meta):
+    """dQ, dK, dV of the regrouped core from the prepared gradient."""
+    (tq, sq), (tk, sk_), (tv, sv) = meta
+    TB, H, Nq, dh = sq
+    B = kb.shape[0]
+    # dQ = G M^T with G = hi | lo against [M^T; M^T]: one fp32-accumulated
+    # product, rounded once to q's dtype
+    mt = Mb.transpose(1, 2)
+    mt2 = torch.cat([mt, mt], dim=1)                               # [B, 2dh, dh]
+    dq = torch.bmm(g_heads, mt2) if tq == torch.bfloat16 else _bmm32(g_heads, mt2).to(tq)
+    # dM = Q^T G, E = 2 dM - 1 gcol^T, u = -1^T dM + dh gcol
+    dm2 = _bmm32(qb.transpose(1, 2), g_heads)                      # [B, dh, 2dh]
+    dm = dm2[..., :dh] + dm2[..., dh:]
+    e = 2.0 * dm - gcol.unsqueeze(1)
+    u = dh * gcol - dm.sum(1)
+    eh, el = _split_bf16(e)
+    # second split term accumulated in place into the first product's output
+    bf = torch.ops.aten.baddbmm.dtype_out
+    dk32 = _bmm32(vb, eh.transpose(1, 2))
+    bf(dk32, vb, el.transpose(1, 2), torch.float32, out=dk32)      # V E^T
+    ke = _bmm32(kb, eh)
+    bf(ke, kb, el, torch.float32, out=ke)                          # K E
+    rt = Rb.t()
+    rg = torch.mm(rt, g_rows[:, 0].reshape(Nq, B * dh), out_dtype=torch.float32)
+    torch.ops.aten.addmm.dtype_out(rg, rt, g_rows[:, 1].reshape(Nq, B * dh), torch.float32, out=rg)  # R^T G
+    dk, dv = ops.xnor_train_grad_finish(ke, rg, u, dk32, TB, H, tk)
+    return dq.view(sq), dk.view(sk_), dv.to(tv).view(sv)
 
 
 class XnorScoreFree(torch.autograd.Function):
@@ -260,18 +339,8 @@ class XnorScoreFree(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, R, scale):
         with torch.autocast("cuda", enabled=False):
-            TB, H, Nq, dh = q.shape
-            Nk = k.shape[2]
-            qb, kb, vb = (_flat_bf16(t) for t in (q, k, v))
-            B = qb.shape[0]
-            Rb = R.to(torch.bfloat16)
-            kv = _bmm32(kb.transpose(1, 2), vb)                           # [B, dh, dh]
-            cv = vb.sum(1, keepdim=True, dtype=torch.float32)              # 1^T V  [B, 1, dh]
-            sk = kb.sum(2, keepdim=True, dtype=torch.float32)              # |k_j|  [B, Nk, 1]
-            Mb = (2.0 * kv - cv).to(torch.bfloat16)                        # exact: |M| <= Nk
-            w = _bmm32((dh - sk).transpose(1, 2).to(torch.bfloat16), vb)   # [B, 1, dh]
-            qm = _bmm32(qb, Mb)                                            # [B, Nq, dh]
-            rv = torch.mm(Rb, vb.permute(1, 0, 2).reshape(Nk, B * dh), out_dtype=torch.float32)
+            TB, H = q.shape[:2]
+            qb, kb, vb, Mb, Rb, qm, rv, w = _xnor_products(q, k, v, R)
             out = ops.xnor_train_combine(qm, rv, w, scale, TB, H)
         ctx.save_for_backward(qb, kb, vb, Mb, Rb, out, scale)
         ctx.meta = ((q.dtype, q.shape), (k.dtype, k.shape), (v.dtype, v.shape))
@@ -280,32 +349,47 @@ class XnorScoreFree(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         qb, kb, vb, Mb, Rb, out, scale = ctx.saved_tensors
-        (tq, sq), (tk, sk_), (tv, sv) = ctx.meta
-        TB, H, Nq, dh = sq
-        B, Nk = kb.shape[0], kb.shape[1]
+        TB, H, Nq, dh = ctx.meta[0][1]
         with torch.autocast("cuda", enabled=False):
             g_heads, g_rows, gcol, gdot = ops.xnor_train_grad_prep(g, out, scale, H, dh)
             gscale = (gdot / scale.float()).reshape(scale.shape).to(scale.dtype)   # sum(g * m)
-            # dQ = G M^T with G = hi | lo against [M^T; M^T]
-            mt = Mb.transpose(1, 2)
-            mt2 = torch.cat([mt, mt], dim=1)                               # [B, 2dh, dh]
-            # one fp32-accumulated product, rounded once to q's dtype
-            dq = torch.bmm(g_heads, mt2) if tq == torch.bfloat16 else _bmm32(g_heads, mt2).to(tq)
-            # dM = Q^T G, E = 2 dM - 1 gcol^T, u = -1^T dM + dh gcol
-            dm2 = _bmm32(qb.transpose(1, 2), g_heads)                      # [B, dh, 2dh]
-            dm = dm2[..., :dh] + dm2[..., dh:]
-            e = 2.0 * dm - gcol.unsqueeze(1)
-            u = dh * gcol - dm.sum(1)
-            eh, el = _split_bf16(e)
-            bf = torch.ops.aten.baddbmm.dtype
-            dk32 = bf(_bmm32(vb, eh.transpose(1, 2)), vb, el.transpose(1, 2), torch.float32)   # V E^T
-            ke = bf(_bmm32(kb, eh), kb, el, torch.float32)                                       # K E
-            rt = Rb.t()
-            rg = torch.ops.aten.addmm.dtype(
-                torch.mm(rt, g_rows[:, 0].reshape(Nq, B * dh), out_dtype=torch.float32), rt,
-                g_rows[:, 1].reshape(Nq, B * dh), torch.float32)                                 # R^T G
-            dk, dv = ops.xnor_train_grad_finish(ke, rg, u, dk32, TB, H, tk)
-        return dq.view(sq), dk.view(sk_), dv.to(tv).view(sv), None, gscale
+            dq, dk, dv = _xnor_backward(qb, kb, vb, Mb, Rb, g_heads, g_rows, gcol, ctx.meta)
+        return dq, dk, dv, None, gscale
+
+
+class XnorLIF(torch.autograd.Function):
+    """``XnorScoreFree`` followed by the attention's output LIF (``lifs``,
+    ``SSA.py:242``), both passes fused into the core's kernels: spikes come out
+    token-major in ``spike_dtype`` (they feed only the output projection), and
+    the backward runs the LIF's BPTT inside the gradient preparation.  Equal
+    to ``lifs(XnorScoreFree(...))`` (the LIF kernels' arithmetic).  Gradients:
+    Q, K, V, scale and the LIF beta."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, R, scale, lif_beta, v_th, v_reset, in_gain, surrogate, k_sg, T, spike_dtype):
+        with torch.autocast("cuda", enabled=False):
+            TB, H = q.shape[:2]
+            qb, kb, vb, Mb, Rb, qm, rv, w = _xnor_products(q, k, v, R)
+            a, spikes = ops.xnor_train_combine_lif(qm, rv, w, scale, TB, H, T, lif_beta, v_th, v_reset, in_gain,
+                                                   spike_dtype)
+        ctx.save_for_backward(qb, kb, vb, Mb, Rb, a, scale, lif_beta, v_th, v_reset)
+        ctx.meta = ((q.dtype, q.shape), (k.dtype, k.shape), (v.dtype, v.shape))
+        ctx.lif = (float(in_gain), surrogate, float(k_sg), int(T))
+        return spikes
+
+    @staticmethod
+    def backward(ctx, g):
+        qb, kb, vb, Mb, Rb, a, scale, lb, vth, vr = ctx.saved_tensors
+        TB, H, Nq, dh = ctx.meta[0][1]
+        gain, surrogate, k_sg, T = ctx.lif
+        need_lb = ctx.needs_input_grad[5]
+        with torch.autocast("cuda", enabled=False):
+            g_heads, g_rows, gcol, gdot, glb = ops.xnor_train_grad_prep_lif(
+                g, a, scale, H, dh, T, lb, vth, vr, gain, surrogate, k_sg, need_lif_beta=need_lb)
+            gscale = (gdot / scale.float()).reshape(scale.shape).to(scale.dtype)
+            dq, dk, dv = _xnor_backward(qb, kb, vb, Mb, Rb, g_heads, g_rows, gcol, ctx.meta)
+        glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
+        return dq, dk, dv, None, gscale, glb, None, None, None, None, None, None, None
 
 
 class SSAMultiHeadAttention_(_SSACore):

@@ -15,6 +15,15 @@
 //                 product); per-chunk column sums of gs and per-thread partial
 //                 sums of g * out (for the scale gradient).
 //   grad_finish:  dv = KE + RG (n-major) + u, and dk cast to the spike dtype.
+//
+// The *_lif variants also run the attention's output LIF (lifs, SSA.py:242;
+// v_th 0.5): combine_lif scans the T steps of each neuron in registers and
+// writes its spikes (for the output projection) besides the pre-activation;
+// grad_prep_lif recomputes the membrane from the pre-activation and runs the
+// BPTT (the LIF backward of Lif.py:46-102) before the split.  Both keep the
+// LIF kernels' operation order (separately rounded multiply and add, IEEE
+// division in the surrogate), so they equal the unfused composition bit for
+// bit.
 #include <type_traits>
 
 #include "common.cuh"
@@ -150,6 +159,175 @@ __global__ void __launch_bounds__(256) grad_finish_kernel(const float* __restric
   }
 }
 
+
+// ---------------------------------------------------------------- with the output LIF
+
+constexpr int kLifMaxT = 4;
+
+struct LifArgs {
+  const float *beta, *vth, *vr;
+  float gain;
+  int surrogate;
+  float k, c_arctan;
+};
+
+__device__ __forceinline__ float lif_surrogate(int kind, float u, float k, float c_arctan) {
+  if (kind == SPK_SURROGATE_SUPERSPIKE) {
+    const float a = __fadd_rn(1.0f, __fmul_rn(k, fabsf(u)));
+    return __fdiv_rn(1.0f, __fmul_rn(a, a));
+  }
+  const float z = __fmul_rn(c_arctan, u);
+  return __fdiv_rn(__fmul_rn(k, 0.5f), __fadd_rn(1.0f, __fmul_rn(z, z)));
+}
+
+__device__ __forceinline__ void unpack4(const float* p, float* o) {
+  const float4 v = ld4(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+__device__ __forceinline__ void unpack4(const __nv_bfloat16* p, float* o) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+  o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+}
+__device__ __forceinline__ void unpack4(const __half* p, float* o) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+  o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+}
+
+// one thread per (b', n, h, d4) neuron quad, all T steps: tb = t * Bp + b'
+template <typename OT>
+__global__ void __launch_bounds__(256) combine_lif_kernel(const float* __restrict__ qm, const float* __restrict__ rv,
+                                                          const float* __restrict__ w, const float* __restrict__ scale,
+                                                          LifArgs L, float* __restrict__ a_out, OT* __restrict__ spikes,
+                                                          int T, int64_t Bp, int H, int Nq, int dh) {
+  const int dq4 = dh / 4;
+  const int64_t B = (int64_t)T * Bp * H;
+  const int64_t total = Bp * Nq * H * dq4;
+  const float s = __ldg(scale), beta = __ldg(L.beta), vth = __ldg(L.vth), vr = __ldg(L.vr);
+  const bool use_gain = L.gain != 1.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int d4 = (int)(i % dq4);
+    int64_t r = i / dq4;
+    const int h = (int)(r % H);
+    r /= H;
+    const int n = (int)(r % Nq);
+    const int64_t bp = r / Nq;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = 0; t < T; ++t) {
+      const int64_t tb = (int64_t)t * Bp + bp, b = tb * H + h;
+      const float4 x = ld4(qm + (b * Nq + n) * dh + 4 * d4);
+      const float4 c = ld4(rv + ((int64_t)n * B + b) * dh + 4 * d4);
+      const float4 e = ld4(w + b * dh + 4 * d4);
+      const float a[4] = {((x.x + c.x) + e.x) * s, ((x.y + c.y) + e.y) * s, ((x.z + c.z) + e.z) * s,
+                          ((x.w + c.w) + e.w) * s};
+      const int64_t tm = ((tb * Nq + n) * H + h) * dh + 4 * d4;
+      *reinterpret_cast<float4*>(a_out + tm) = make_float4(a[0], a[1], a[2], a[3]);
+      float sp[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float cur = use_gain ? __fmul_rn(a[q], L.gain) : a[q];
+        const float u = __fadd_rn(__fmul_rn(v[q], beta), cur);
+        const bool f = u > vth;
+        sp[q] = f ? 1.0f : 0.0f;
+        v[q] = f ? vr : u;
+      }
+      store4o<OT>(spikes + tm, make_float4(sp[0], sp[1], sp[2], sp[3]));
+    }
+  }
+}
+
+// grid: x over (b', h, d4), y over chunks of kChunk rows of n
+template <typename GT>
+__global__ void __launch_bounds__(256) grad_prep_lif_kernel(
+    const GT* __restrict__ gsp, const float* __restrict__ a_in, const float* __restrict__ scale, LifArgs L,
+    uint16_t* __restrict__ g_heads, uint16_t* __restrict__ g_rows, float* __restrict__ gcol_part,
+    float* __restrict__ gsc_part, float* __restrict__ gbeta_part, int T, int64_t Bp, int H, int Nq, int dh) {
+  const int dq4 = dh / 4;
+  const int64_t B = (int64_t)T * Bp * H, X = Bp * H * dq4;
+  const int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (x >= X) return;
+  const int d4 = (int)(x % dq4);
+  const int64_t bh = x / dq4;  // = b' * H + h
+  const int64_t bp = bh / H;
+  const int h = (int)(bh - bp * H);
+  const float s = __ldg(scale), beta = __ldg(L.beta), vth = __ldg(L.vth), vr = __ldg(L.vr);
+  const bool use_gain = L.gain != 1.0f;
+  const int n0 = blockIdx.y * kChunk;
+  const int n1 = n0 + kChunk < Nq ? n0 + kChunk : Nq;
+  float col[kLifMaxT][4];
+#pragma unroll
+  for (int t = 0; t < kLifMaxT; ++t)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) col[t][q] = 0.0f;
+  float dot = 0.0f, bacc = 0.0f;
+  for (int n = n0; n < n1; ++n) {
+    float av[kLifMaxT][4], gv[kLifMaxT][4], u[kLifMaxT][4];
+    bool sb[kLifMaxT][4];
+#pragma unroll
+    for (int t = 0; t < kLifMaxT; ++t) {
+      if (t >= T) continue;
+      const int64_t tb = (int64_t)t * Bp + bp;
+      const int64_t tm = ((tb * Nq + n) * H + h) * dh + 4 * d4;
+      unpack4(a_in + tm, av[t]);
+      unpack4(gsp + tm, gv[t]);
+    }
+    // membrane before reset, as the LIF forward computed it
+    {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int t = 0; t < kLifMaxT; ++t) {
+        if (t >= T) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float cur = use_gain ? __fmul_rn(av[t][q], L.gain) : av[t][q];
+          u[t][q] = __fadd_rn(__fmul_rn(v[q], beta), cur);
+          sb[t][q] = u[t][q] > vth;
+          v[q] = sb[t][q] ? vr : u[t][q];
+        }
+      }
+    }
+    float gstate[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int t = kLifMaxT - 1; t >= 0; --t) {
+      if (t >= T) continue;
+      float gs[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float sg = lif_surrogate(L.surrogate, __fadd_rn(u[t][q], -vth), L.k, L.c_arctan);
+        const float g = __fadd_rn(__fmul_rn(gv[t][q], sg), sb[t][q] ? 0.0f : gstate[q]);
+        const float ga = use_gain ? __fmul_rn(g, L.gain) : g;  // dL/da
+        const float vprev = t > 0 ? (sb[t - 1][q] ? vr : u[t - 1][q]) : 0.0f;
+        bacc = __fadd_rn(bacc, __fmul_rn(g, vprev));
+        gstate[q] = __fmul_rn(g, beta);
+        dot = fmaf(ga, av[t][q], dot);
+        gs[q] = ga * s;
+        col[t][q] += gs[q];
+      }
+      const int64_t b = ((int64_t)t * Bp + bp) * H + h;
+      uint2 hi, lo;
+      split4(make_float4(gs[0], gs[1], gs[2], gs[3]), hi, lo);
+      uint16_t* ph = g_heads + (b * Nq + n) * (2 * dh) + 4 * d4;
+      *reinterpret_cast<uint2*>(ph) = hi;
+      *reinterpret_cast<uint2*>(ph + dh) = lo;
+      uint16_t* pr = g_rows + ((int64_t)n * 2 * B + b) * dh + 4 * d4;
+      *reinterpret_cast<uint2*>(pr) = hi;
+      *reinterpret_cast<uint2*>(pr + B * dh) = lo;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kLifMaxT; ++t) {
+    if (t >= T) continue;
+    const int64_t b = ((int64_t)t * Bp + bp) * H + h;
+    *reinterpret_cast<float4*>(gcol_part + ((int64_t)blockIdx.y * B + b) * dh + 4 * d4) =
+        make_float4(col[t][0], col[t][1], col[t][2], col[t][3]);
+  }
+  gsc_part[(int64_t)blockIdx.y * X + x] = dot;
+  if (gbeta_part) gbeta_part[(int64_t)blockIdx.y * X + x] = bacc;
+}
+
 inline int grid_for(int64_t n4) {
   const int64_t cap = (int64_t)num_sms() * 8;
   int64_t g = (n4 + 255) / 256;
@@ -235,6 +413,85 @@ int spk_xnor_train_grad_finish(const float* ke, const float* rg, const float* u,
         ke, rg, u, dk32, reinterpret_cast<__nv_bfloat16*>(dk), reinterpret_cast<__nv_bfloat16*>(dv), B, (int)Nk,
         (int)dh);
   return check_launch("xnor grad_finish_kernel");
+}
+
+int spk_xnor_train_combine_lif(const float* qm, const float* rv, const float* w, const float* scale,
+                               const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain,
+                               float* a_out, void* spikes, int spike_dtype, int64_t T, int64_t TB, int64_t H,
+                               int64_t Nq, int64_t dh, void* stream) {
+  using namespace spk;
+  int rc = check_dims(TB, H, Nq, dh);
+  if (rc != SPK_OK) return rc;
+  SPK_REQUIRE(T >= 1 && T <= xnort::kLifMaxT && TB % T == 0, SPK_ERR_SHAPE, "T=%lld must be in [1, %d] and divide TB=%lld",
+              (long long)T, xnort::kLifMaxT, (long long)TB);
+  SPK_REQUIRE(qm && rv && w && scale && lif_beta && lif_vth && lif_vreset && a_out && spikes, SPK_ERR_INVALID,
+              "null pointer argument");
+  SPK_REQUIRE(spike_dtype == SPK_F32 || spike_dtype == SPK_F16 || spike_dtype == SPK_BF16, SPK_ERR_INVALID,
+              "spike dtype %d not supported", spike_dtype);
+  SPK_REQUIRE(aligned(qm, 16) && aligned(rv, 16) && aligned(w, 16) && aligned(a_out, 16) && aligned(spikes, 16),
+              SPK_ERR_ALIGN, "qm, rv, w, a_out and spikes must be 16-byte aligned");
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  const int64_t Bp = TB / T, n4 = Bp * H * Nq * (dh / 4);
+  const xnort::LifArgs L{lif_beta, lif_vth, lif_vreset, in_gain, 0, 0.0f, 0.0f};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = xnort::grid_for(n4);
+  if (spike_dtype == SPK_F32)
+    xnort::combine_lif_kernel<float><<<grid, 256, 0, st>>>(qm, rv, w, scale, L, a_out, reinterpret_cast<float*>(spikes),
+                                                           (int)T, Bp, (int)H, (int)Nq, (int)dh);
+  else if (spike_dtype == SPK_F16)
+    xnort::combine_lif_kernel<__half><<<grid, 256, 0, st>>>(qm, rv, w, scale, L, a_out,
+                                                            reinterpret_cast<__half*>(spikes), (int)T, Bp, (int)H,
+                                                            (int)Nq, (int)dh);
+  else
+    xnort::combine_lif_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(qm, rv, w, scale, L, a_out,
+                                                                   reinterpret_cast<__nv_bfloat16*>(spikes), (int)T,
+                                                                   Bp, (int)H, (int)Nq, (int)dh);
+  return check_launch("xnor combine_lif_kernel");
+}
+
+int spk_xnor_train_grad_prep_lif(const void* g_spikes, int gs_dtype, const float* a, const float* scale,
+                                 const float* lif_beta, const float* lif_vth, const float* lif_vreset, float in_gain,
+                                 int surrogate, float surrogate_k, void* g_heads, void* g_rows, float* gcol_part,
+                                 float* gscale_part, float* gbeta_part, int64_t T, int64_t TB, int64_t H, int64_t Nq,
+                                 int64_t dh, void* stream) {
+  using namespace spk;
+  int rc = check_dims(TB, H, Nq, dh);
+  if (rc != SPK_OK) return rc;
+  SPK_REQUIRE(T >= 1 && T <= xnort::kLifMaxT && TB % T == 0, SPK_ERR_SHAPE, "T=%lld must be in [1, %d] and divide TB=%lld",
+              (long long)T, xnort::kLifMaxT, (long long)TB);
+  SPK_REQUIRE(g_spikes && a && scale && lif_beta && lif_vth && lif_vreset && g_heads && g_rows && gcol_part &&
+                  gscale_part,
+              SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(gs_dtype == SPK_F32 || gs_dtype == SPK_F16 || gs_dtype == SPK_BF16, SPK_ERR_INVALID,
+              "gradient dtype %d not supported", gs_dtype);
+  SPK_REQUIRE(surrogate == SPK_SURROGATE_SUPERSPIKE || surrogate == SPK_SURROGATE_ARCTAN, SPK_ERR_INVALID,
+              "unknown surrogate %d", surrogate);
+  SPK_REQUIRE(aligned(g_spikes, 16) && aligned(a, 16) && aligned(g_heads, 8) && aligned(g_rows, 8) &&
+                  aligned(gcol_part, 16),
+              SPK_ERR_ALIGN, "g_spikes, a, gcol_part must be 16-byte and g_heads, g_rows 8-byte aligned");
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  const int64_t Bp = TB / T, X = Bp * H * (dh / 4);
+  SPK_REQUIRE((X + 255) / 256 < (1ll << 31), SPK_ERR_SHAPE, "too many heads");
+  const dim3 grid((unsigned)((X + 255) / 256), (unsigned)spk_xnor_train_prep_chunks(Nq));
+  SPK_REQUIRE(grid.y <= 65535, SPK_ERR_SHAPE, "Nq=%lld too long", (long long)Nq);
+  const xnort::LifArgs L{lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
+                         (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k)};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint16_t* gh = reinterpret_cast<uint16_t*>(g_heads);
+  uint16_t* gr = reinterpret_cast<uint16_t*>(g_rows);
+  if (gs_dtype == SPK_F32)
+    xnort::grad_prep_lif_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(g_spikes), a, scale, L,
+                                                             gh, gr, gcol_part, gscale_part, gbeta_part, (int)T, Bp,
+                                                             (int)H, (int)Nq, (int)dh);
+  else if (gs_dtype == SPK_F16)
+    xnort::grad_prep_lif_kernel<__half><<<grid, 256, 0, st>>>(reinterpret_cast<const __half*>(g_spikes), a, scale,
+                                                              L, gh, gr, gcol_part, gscale_part, gbeta_part, (int)T,
+                                                              Bp, (int)H, (int)Nq, (int)dh);
+  else
+    xnort::grad_prep_lif_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(g_spikes), a, scale, L, gh, gr, gcol_part, gscale_part, gbeta_part,
+        (int)T, Bp, (int)H, (int)Nq, (int)dh);
+  return check_launch("xnor grad_prep_lif_kernel");
 }
 
 }  // extern "C"

@@ -403,3 +403,52 @@ def xnor_train_grad_finish(ke, rg, u, dk32, TB, H, out_dtype):
               _lib.ptr(dv), _lib.DTYPE_CODE[out_dtype], TB, H, Nk, dh, _lib.stream_ptr(ke.device),
               tag="xnor_train_grad_finish", work=dict(bytes=ke.numel() * 20))
     return dk, dv
+
+
+def xnor_train_combine_lif(qm, rv, w, scale, TB, H, T, lif_beta, lif_vth, lif_vr, in_gain=1.0,
+                           spike_dtype=torch.float32):
+    """``xnor_train_combine`` followed by the output LIF over the T-major fold:
+    ``(a [TB, Nq, H*dh] fp32, spikes like a in spike_dtype)``."""
+    _cuda(qm, rv, w)
+    B, Nq, dh = qm.shape
+    dev = qm.device
+    qm, rv, w = qm.contiguous(), rv.contiguous(), w.contiguous()
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, dev)
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    a = torch.empty((TB, Nq, H * dh), dtype=torch.float32, device=dev)
+    s = torch.empty((TB, Nq, H * dh), dtype=spike_dtype, device=dev)
+    _lib.call("spk_xnor_train_combine_lif", _lib.ptr(qm), _lib.ptr(rv), _lib.ptr(w), _lib.ptr(sc), _lib.ptr(b),
+              _lib.ptr(th), _lib.ptr(vr), float(in_gain), _lib.ptr(a), _lib.ptr(s), _lib.DTYPE_CODE[spike_dtype], T, TB,
+              H, Nq, dh, _lib.stream_ptr(dev), tag="xnor_train_combine_lif",
+              work=dict(bytes=a.numel() * (16 + s.element_size())))
+    return a, s
+
+
+def xnor_train_grad_prep_lif(g_spikes, a, scale, H, dh, T, lif_beta, lif_vth, lif_vr, in_gain=1.0,
+                             surrogate="superspike", k=4.0, need_lif_beta=False):
+    """``xnor_train_grad_prep`` after the output LIF's backward: from dL/dspikes
+    and the pre-activation ``a``; returns ``(g_heads, g_rows, gcol [B, dh],
+    sum(dL/da * a), LIF beta gradient [1] or None)``."""
+    _cuda(g_spikes, a)
+    if g_spikes.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        g_spikes = g_spikes.float()
+    g_spikes = g_spikes.contiguous()
+    a = a.contiguous()
+    TB, Nq, D = a.shape
+    B = TB * H
+    dev = a.device
+    C = int(_lib.load().spk_xnor_train_prep_chunks(Nq))
+    X = TB // T * H * dh // 4
+    g_heads = torch.empty((B, Nq, 2 * dh), dtype=torch.bfloat16, device=dev)
+    g_rows = torch.empty((Nq, 2, B, dh), dtype=torch.bfloat16, device=dev)
+    gcol_part = torch.empty((C, B, dh), dtype=torch.float32, device=dev)
+    gsc_part = torch.empty((C, X), dtype=torch.float32, device=dev)
+    gb_part = torch.empty((C, X), dtype=torch.float32, device=dev) if need_lif_beta else None
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, dev)
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_xnor_train_grad_prep_lif", _lib.ptr(g_spikes), _lib.dtype_code(g_spikes), _lib.ptr(a), _lib.ptr(sc),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), _lib.SURROGATE[surrogate], float(k),
+              _lib.ptr(g_heads), _lib.ptr(g_rows), _lib.ptr(gcol_part), _lib.ptr(gsc_part), _lib.ptr(gb_part), T, TB,
+              H, Nq, dh, _lib.stream_ptr(dev), tag="xnor_train_grad_prep_lif",
+              work=dict(bytes=a.numel() * (4 + g_spikes.element_size() + 8)))
+    return g_heads, g_rows, gcol_part.sum(0), gsc_part.sum(), None if gb_part is None else gb_part.sum().reshape(1)

@@ -112,6 +112,41 @@ def test_xnor_score_free_training_core(pkg, Nq, Nk, dtype):
     assert abs(m.scale.grad.item() - rs.grad.item()) <= 1e-5 * gs_bound
 
 
+@pytest.mark.parametrize("spike_dtype", [torch.float32, torch.bfloat16])
+def test_xnor_lif_fused_equals_composition(pkg, spike_dtype):
+    """The attention core with the output LIF fused into its kernels equals the
+    core followed by the lifs LIF module: spikes bit for bit, gradients of Q,
+    K, V and the scale to fp32 rounding."""
+    from spikingtransformer_b200.SSA import SSAMultiHeadAttention, XnorLIF, XnorScoreFree
+    T, Bp, H, Nq, Nk, dh = 4, 3, 2, 24, 40, 48
+    TB = T * Bp
+    m = SSAMultiHeadAttention(d_model=H * dh, n_heads=H, n_steps=T).to(DEV)
+    m.lifs.set_surrogate("arctan", 2.0)
+    g = torch.Generator(device=DEV).manual_seed(17)
+    base = [(torch.rand(TB, n, H, dh, generator=g, device=DEV) < 0.3).float() for n in (Nq, Nk, Nk)]
+    R = m.get_log_pe_bias_cross(Nq, Nk, DEV)
+    gsp = torch.randn(TB, Nq, H * dh, generator=g, device=DEV).to(torch.bfloat16).float()
+    results = []
+    for fused in (False, True):
+        leaves = [t.clone().requires_grad_() for t in base]
+        q, k, v = (t.transpose(1, 2) for t in leaves)
+        m.scale.grad = None
+        if fused:
+            lifs = m.lifs
+            s = XnorLIF.apply(q, k, v, R, m.scale, lifs.effective_beta(), lifs.v_th, lifs.v_reset, lifs.in_gain,
+                              lifs.surrogate, lifs._k_host, T, spike_dtype)
+            assert s.dtype == spike_dtype
+        else:
+            s = m.lifs(XnorScoreFree.apply(q, k, v, R, m.scale))[0]
+        (s.float() * gsp).sum().backward()
+        results.append((s.float(), [t.grad for t in leaves], m.scale.grad.clone()))
+    (s0, g0, sc0), (s1, g1, sc1) = results
+    assert torch.equal(s0, s1)
+    for a, b in zip(g0, g1):
+        assert torch.allclose(a, b, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(sc0, sc1, rtol=1e-4, atol=1e-6)
+
+
 def test_linear_bf16_training_gemm(pkg):
     """The training path's bias-free bf16 GEMM against torch's autocast Linear:
     the same bf16 output, and fp32 input / weight gradients at least as close
