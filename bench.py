@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="images per GPU (forward 256, train 64, decode 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="train: run the one-GPU step eagerly")
     return ap.parse_args()
 
 
@@ -270,24 +271,62 @@ def run_train(args, ws, rank, local):
     if ws > 1:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
                                                         gradient_as_bucket_view=True)
-    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    # one GPU: the forward, backward and optimizer step are captured once into a
+    # CUDA graph (the host would otherwise spend longer enqueueing the step's
+    # ~2,000 launches than the GPU spends running them); each step generates
+    # its batch into the graph's static input buffers and replays the graph.
+    # With DDP (N > 1) the step runs eagerly.
+    use_graph = ws == 1 and not args.no_graph
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=use_graph)
     B = args.batch or 64
     mask = torch.tril(torch.ones(SEQ, SEQ, device=dev)).expand(B, 1, SEQ, SEQ)
 
-    def step(i):
-        src, labels = ops.synth_text_lines(B, 1_000_000 + shard_seed(rank, i), H=IMG[1], W=IMG[2], L=SEQ + 1,
-                                           V=ARCH["tgt_vocab_size"], device=dev)
+    def gen(i):
+        return ops.synth_text_lines(B, 1_000_000 + shard_seed(rank, i), H=IMG[1], W=IMG[2], L=SEQ + 1,
+                                    V=ARCH["tgt_vocab_size"], device=dev)
+
+    def train_step(src, labels):
         tgt_in, tgt_out = labels[:, :-1], labels[:, 1:]
-        opt.zero_grad(set_to_none=True)
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=not use_graph):
             logits, _ = net(src, tgt_in, look_ahead_mask=mask)
         loss, acc, _ = ops.ce_over_t(logits, tgt_out, ignore_index=0, label_smoothing=0.1)
         loss.backward()
         opt.step()
         return loss, acc
 
-    for i in range(args.warmup):
-        step(i)
+    graph_launches = None
+    if use_graph:
+        static_src, static_labels = gen(0)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for i in range(args.warmup):
+                src, labels = gen(i)
+                static_src.copy_(src)
+                static_labels.copy_(labels)
+                opt.zero_grad(set_to_none=True)
+                train_step(static_src, static_labels)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        opt.zero_grad(set_to_none=True)
+        with _lib.LaunchCounter() as counter, torch.cuda.graph(graph):
+            g_loss, g_acc = train_step(static_src, static_labels)
+        graph_launches = counter.total()
+
+        def step(i):
+            src, labels = gen(i)
+            static_src.copy_(src)
+            static_labels.copy_(labels)
+            graph.replay()
+            return g_loss, g_acc
+    else:
+        def step(i):
+            src, labels = gen(i)
+            opt.zero_grad(set_to_none=True)
+            return train_step(src, labels)
+
+        for i in range(args.warmup):
+            step(i)
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
@@ -316,7 +355,8 @@ def run_train(args, ws, rank, local):
                        "loss": "mean over T of CE(ignore_index=0, label_smoothing=0.1), fused with token accuracy",
                        "parallelism": "ddp%d (NCCL all-reduce of gradients)" % ws},
             "loss": last, "token_accuracy": last_acc, "clocks": clk.summary(),
-            "gpu_launches": sum(v["launches"] for v in kernels.values()),
+            "cuda_graph": use_graph, "graph_launches_per_step": graph_launches,
+            "gpu_launches": sum(v["launches"] for v in kernels.values()) + (graph_launches or 0) * args.steps,
             "kernels": {k: {"launches": v["launches"], "ms_per_step": v["ms"] / args.steps}
                         for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])},
         }), flush=True)

@@ -121,12 +121,38 @@ class LaunchRecorder:
         return out
 
 
+class LaunchCounter:
+    """Counts the kernels this library launches while it is active, by tag,
+    without events (usable while a CUDA graph is being captured)."""
+
+    def __init__(self):
+        self.counts = {}
+
+    def __enter__(self):
+        global _counter
+        self._prev = _counter
+        _counter = self
+        return self
+
+    def __exit__(self, *exc):
+        global _counter
+        _counter = self._prev
+        return False
+
+    def total(self):
+        return sum(self.counts.values())
+
+
 _recorder = None
+_counter = None
 
 
 def call(name, *args, tag=None, work=None):
     """Call an int-returning entry point; raise RuntimeError on failure."""
     lib = load()
+    if _counter is not None:
+        k = tag or name
+        _counter.counts[k] = _counter.counts.get(k, 0) + (work or {}).get("launches", 1)
     rec = _recorder
     if rec is not None:
         e0 = torch.cuda.Event(enable_timing=True)

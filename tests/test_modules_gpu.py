@@ -323,6 +323,66 @@ def test_seq2seq_train_steps_bf16_autocast(pkg):
     assert any("out_proj" in n for n in changed) and any("output_layer" in n for n in changed)
 
 
+def test_train_step_cuda_graph_matches_eager(pkg):
+    """A training step (bf16 autocast, fused loss, capturable AdamW) captured in
+    a CUDA graph and replayed gives the losses of the same steps run eagerly
+    from the same start: the training path makes no host synchronisation and
+    keeps no stale cached tensor that a graph would freeze."""
+    from spikingtransformer_b200 import ops
+    B, N = 2, 16
+    data = []
+    for i in range(4):
+        src = synthetic_lines(B, 30 + i).to(DEV)
+        tgt = torch.randint(1, 256, (B, N + 1), device=DEV, generator=torch.Generator(device=DEV).manual_seed(i))
+        data.append((src, tgt))
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(B, 1, N, N)
+
+    def make():
+        m, _ = _bench_models(enc_layers=1, dec_layers=1)
+        m.train()
+        m.set_surrogate("arctan", 2.0)
+        return m, torch.optim.AdamW(m.parameters(), lr=1e-3, fused=True, capturable=True)
+
+    def step(m, opt, src, tgt, cache):
+        with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=cache):
+            logits, _ = m(src, tgt[:, :-1], look_ahead_mask=mask)
+        loss, acc, _ = ops.ce_over_t(logits, tgt[:, 1:], ignore_index=0, label_smoothing=0.1)
+        loss.backward()
+        opt.step()
+        return loss
+
+    m1, o1 = make()
+    eager = []
+    for src, tgt in data:
+        o1.zero_grad(set_to_none=True)
+        eager.append(step(m1, o1, src, tgt, False).item())
+
+    m2, o2 = make()
+    s_src, s_tgt = data[0][0].clone(), data[0][1].clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for src, tgt in data[:2]:
+            s_src.copy_(src)
+            s_tgt.copy_(tgt)
+            o2.zero_grad(set_to_none=True)
+            step(m2, o2, s_src, s_tgt, False)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    o2.zero_grad(set_to_none=True)
+    with torch.cuda.graph(graph):
+        g_loss = step(m2, o2, s_src, s_tgt, False)
+    replayed = []
+    for src, tgt in data[2:]:
+        s_src.copy_(src)
+        s_tgt.copy_(tgt)
+        graph.replay()
+        replayed.append(g_loss.item())
+    assert all(math.isfinite(x) for x in eager + replayed)
+    assert replayed == pytest.approx(eager[2:], rel=1e-4), (eager, replayed)
+    del graph
+
+
 def test_greedy_decode(pkg):
     ours, _ = _bench_models(enc_layers=1, dec_layers=1)
     src = synthetic_lines(1, 4)[0]
