@@ -553,7 +553,26 @@ struct BlockSum {
   __device__ __forceinline__ float sum(float v, int nw) { return sum2(make_float2(v, 0.0f), nw).x; }
 };
 
-template <int EB>
+// spikes of dtype SD (SPK_F32 / SPK_BF16 stored directly; -1: any dtype, chosen at run time)
+template <int SD>
+__device__ __forceinline__ void store_spikes4(void* p, int dt, int64_t i, const float* v) {
+  if constexpr (SD == SPK_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if constexpr (SD == SPK_BF16) {
+    // 0/1 values: the bf16 bit patterns are 0x0000 / 0x3f80
+    uint2 w;
+    w.x = (v[0] != 0.0f ? 0x3f80u : 0u) | (v[1] != 0.0f ? 0x3f800000u : 0u);
+    w.y = (v[2] != 0.0f ? 0x3f80u : 0u) | (v[3] != 0.0f ? 0x3f800000u : 0u);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) = w;
+  } else {
+    store4(p, dt, i, v);
+  }
+}
+
+// Statistics: mean = sum * (1/D) and rstd = rsqrtf(var + eps) (within a few
+// ulp of the IEEE divide and square root; the per-row division and square
+// root dominated the instruction count of this kernel).
+template <int EB, int SD>
 __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const FwdParams p) {
   __shared__ float2 red[2 * kTokMaxWarps];
   BlockSum bs{red, 0};
@@ -561,6 +580,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
   const int c = threadIdx.x * 4;  // this lane's four columns
   const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
   const int T = p.T, D = p.D;
+  const float invD = 1.0f / (float)D;
   const float4 g4 = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
   const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -592,14 +612,14 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
       raw_unpack<EB>(raw[t], p.pre_dtype, x);
 #pragma unroll
       for (int e = 0; e < 4; ++e) x[e] += pp[e];
-      const float mean = bs.sum((x[0] + x[1]) + (x[2] + x[3]), nw) / (float)D;
+      const float mean = bs.sum((x[0] + x[1]) + (x[2] + x[3]), nw) * invD;
       float s2 = 0.0f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float d = x[e] - mean;
         s2 = fmaf(d, d, s2);
       }
-      const float rstd = 1.0f / sqrtf(bs.sum(s2, nw) / (float)D + p.eps);
+      const float rstd = rsqrtf(fmaf(bs.sum(s2, nw), invD, p.eps));
       const int64_t row = (int64_t)t * p.R + tok;
       if (threadIdx.x == 0) p.stats[row] = make_float2(mean, rstd);
 #pragma unroll
@@ -611,7 +631,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
         x[e] = sp ? 1.0f : 0.0f;
         v[e] = sp ? vr : u;
       }
-      store4(p.spikes, p.spike_dtype, so + t * lay.t_stride, x);
+      store_spikes4<SD>(p.spikes, p.spike_dtype, so + t * lay.t_stride, x);
     }
   }
 }
@@ -866,10 +886,15 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
   if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
   if (use_tok((int)D) && aligned16) {
     const int grid = tok_grid(R, (int)D), threads = (int)D / 4;
-    if (pre_dtype == SPK_F32)
-      ln_lif_fwd_tok_kernel<4><<<grid, threads, 0, st>>>(p);
-    else
-      ln_lif_fwd_tok_kernel<2><<<grid, threads, 0, st>>>(p);
+    if (pre_dtype == SPK_F32) {
+      spike_dtype == SPK_F32 ? ln_lif_fwd_tok_kernel<4, SPK_F32><<<grid, threads, 0, st>>>(p)
+      : spike_dtype == SPK_BF16 ? ln_lif_fwd_tok_kernel<4, SPK_BF16><<<grid, threads, 0, st>>>(p)
+                                : ln_lif_fwd_tok_kernel<4, -1><<<grid, threads, 0, st>>>(p);
+    } else {
+      spike_dtype == SPK_F32 ? ln_lif_fwd_tok_kernel<2, SPK_F32><<<grid, threads, 0, st>>>(p)
+      : spike_dtype == SPK_BF16 ? ln_lif_fwd_tok_kernel<2, SPK_BF16><<<grid, threads, 0, st>>>(p)
+                                : ln_lif_fwd_tok_kernel<2, -1><<<grid, threads, 0, st>>>(p);
+    }
   } else {
     // D not a multiple of 128 (so D <= 512): one warp per token, single columns
     const int nw = pick_nw((int)D);
