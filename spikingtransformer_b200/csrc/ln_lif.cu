@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
 // the saved statistics, then the steps are walked backwards; BPTT of step t
 // gives dL/dy of row t, whose LayerNorm backward (one pair of block sums)
 // runs at once.
-template <int EBP, int EBG, bool PF>
+template <int EBP, int EBG, bool PF, int SURR>
 __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_lif_bwd_tok_kernel(const BwdParams p) {
   __shared__ float2 red[2 * kTokMaxWarps];
   BlockSum bs{red, 0};
@@ -653,7 +653,9 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
   const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
-  float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_b[4] = {0.f, 0.f, 0.f, 0.f}, acc_d[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 acc_g2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float2 acc_b2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float2 acc_d2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float acc_lb = 0.0f;
   const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
   RawVec<EBP> np_[kMaxT];
@@ -688,59 +690,89 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
     } else {
       load_tok(tok, rp, rg, st);
     }
-    // membrane before reset at every step
-    float u[kMaxT][4];
+    // membrane before reset at every step (pairs of columns in packed f32x2
+    // arithmetic, each operation rounded like its scalar form)
+    const float2 beta2 = make_float2(lb, lb), gain2 = make_float2(p.gain, p.gain);
+    const float2 gg2[2] = {make_float2(gg[0], gg[1]), make_float2(gg[2], gg[3])};
+    const float2 bb2[2] = {make_float2(bb[0], bb[1]), make_float2(bb[2], bb[3])};
+    const float2 pp2[2] = {make_float2(pp[0], pp[1]), make_float2(pp[2], pp[3])};
+    float2 u[kMaxT][2];
     {
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 v[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int t = 0; t < kMaxT; ++t) {
         if (t >= T) continue;
         float x[4];
         raw_unpack<EBP>(rp[t], p.pre_dtype, x);
+        const float2 m2 = make_float2(-st[t].x, -st[t].x), r2 = make_float2(st[t].y, st[t].y);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float xh = ((x[e] + pp[e]) - st[t].x) * st[t].y;
-          const float y = fmaf(xh, gg[e], bb[e]);
-          const float cur = p.gain != 1.0f ? __fmul_rn(y, p.gain) : y;
-          const float uu = __fadd_rn(__fmul_rn(v[e], lb), cur);
-          u[t][e] = uu;
-          v[e] = uu > vth ? vr : uu;
+        for (int j = 0; j < 2; ++j) {
+          const float2 xh = mul2(add2(add2(make_float2(x[2 * j], x[2 * j + 1]), pp2[j]), m2), r2);
+          const float2 y = fma2(xh, gg2[j], bb2[j]);
+          const float2 cur = p.gain != 1.0f ? mul2(y, gain2) : y;
+          const float2 uu = add2(mul2(v[j], beta2), cur);
+          u[t][j] = uu;
+          v[j].x = uu.x > vth ? vr : uu.x;
+          v[j].y = uu.y > vth ? vr : uu.y;
         }
       }
     }
-    float gstate[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 gstate[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    const float2 nvth2 = make_float2(-vth, -vth);
 #pragma unroll
     for (int t = kMaxT - 1; t >= 0; --t) {
       if (t >= T) continue;
-      float gy[4], x[4], xh[4];
-      raw_unpack<EBG>(rg[t], p.gs_dtype, gy);
+      float gyv[4], x[4];
+      raw_unpack<EBG>(rg[t], p.gs_dtype, gyv);
       raw_unpack<EBP>(rp[t], p.pre_dtype, x);
-      float a = 0.0f, b = 0.0f;
+      const float2 m2 = make_float2(-st[t].x, -st[t].x), r2 = make_float2(st[t].y, st[t].y);
+      float2 gy[2], xh[2];
+      float2 av = make_float2(0.f, 0.f), bv = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int j = 0; j < 2; ++j) {
         // BPTT step t: dL/ds -> dL/dy
-        const float sg = surrogate_grad(p.surrogate, u[t][e] - vth, p.k, p.c_arctan);
-        const bool sp = u[t][e] > vth;
-        const float gv = gy[e] * sg + (sp ? 0.0f : gstate[e]);
-        const float vprev = t > 0 ? (u[t - 1][e] > vth ? vr : u[t - 1][e]) : 0.0f;
-        acc_lb = fmaf(gv, vprev, acc_lb);
-        gstate[e] = gv * lb;
-        gy[e] = p.gain != 1.0f ? gv * p.gain : gv;
+        const float2 d = add2(u[t][j], nvth2);
+        float2 sg;
+        if constexpr (SURR == SPK_SURROGATE_SUPERSPIKE) {
+          const float2 q = fma2(make_float2(p.k, p.k), make_float2(fabsf(d.x), fabsf(d.y)), make_float2(1.f, 1.f));
+          const float2 q2 = mul2(q, q);
+          sg = make_float2(__fdividef(1.0f, q2.x), __fdividef(1.0f, q2.y));
+        } else {
+          const float2 z = mul2(make_float2(p.c_arctan, p.c_arctan), d);
+          const float2 den = fma2(z, z, make_float2(1.f, 1.f));
+          const float hk = 0.5f * p.k;
+          sg = make_float2(__fdividef(hk, den.x), __fdividef(hk, den.y));
+        }
+        const bool sx = u[t][j].x > vth, sy = u[t][j].y > vth;
+        const float2 from = make_float2(sx ? 0.0f : gstate[j].x, sy ? 0.0f : gstate[j].y);
+        const float2 gv = fma2(make_float2(gyv[2 * j], gyv[2 * j + 1]), sg, from);
+        float2 vprev = make_float2(0.f, 0.f);
+        if (t > 0) {
+          vprev.x = u[t - 1][j].x > vth ? vr : u[t - 1][j].x;
+          vprev.y = u[t - 1][j].y > vth ? vr : u[t - 1][j].y;
+        }
+        const float2 lbp = mul2(gv, vprev);
+        acc_lb += lbp.x + lbp.y;
+        gstate[j] = mul2(gv, beta2);
+        gy[j] = p.gain != 1.0f ? mul2(gv, gain2) : gv;
         // LayerNorm backward terms of row t
-        xh[e] = ((x[e] + pp[e]) - st[t].x) * st[t].y;
-        const float gx = gy[e] * gg[e];
-        a += gx;
-        b = fmaf(gx, xh[e], b);
-        acc_g[e] = fmaf(gy[e], xh[e], acc_g[e]);
-        acc_b[e] += gy[e];
+        xh[j] = mul2(add2(add2(make_float2(x[2 * j], x[2 * j + 1]), pp2[j]), m2), r2);
+        const float2 gx = mul2(gy[j], gg2[j]);
+        av = add2(av, gx);
+        bv = fma2(gx, xh[j], bv);
+        acc_g2[j] = fma2(gy[j], xh[j], acc_g2[j]);
+        acc_b2[j] = add2(acc_b2[j], gy[j]);
       }
-      const float2 ab = bs.sum2(make_float2(a, b), nw);
-      const float ma = ab.x * invD, mb = ab.y * invD;
+      const float2 ab = bs.sum2(make_float2(av.x + av.y, bv.x + bv.y), nw);
+      const float2 ma = make_float2(-ab.x * invD, -ab.x * invD), mb = make_float2(-ab.y * invD, -ab.y * invD);
       float dx[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        dx[e] = st[t].y * (gy[e] * gg[e] - ma - xh[e] * mb);
-        acc_d[e] += dx[e];
+      for (int j = 0; j < 2; ++j) {
+        // dx = rstd (g gamma - mean(g gamma) - x^ mean(g gamma x^))
+        const float2 dd = mul2(fma2(xh[j], mb, fma2(gy[j], gg2[j], ma)), r2);
+        dx[2 * j] = dd.x;
+        dx[2 * j + 1] = dd.y;
+        acc_d2[j] = add2(acc_d2[j], dd);
       }
       store4(p.g_pre, p.pre_dtype, ((int64_t)t * p.R + tok) * D + c, dx);
     }
@@ -749,6 +781,9 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
   // is summed over the block.  Rows are 3 D + 1 floats long, so a row start is
   // only 4-byte aligned: scalar stores.
   float* out = p.part + (int64_t)blockIdx.x * (3 * D + 1);
+  const float acc_g[4] = {acc_g2[0].x, acc_g2[0].y, acc_g2[1].x, acc_g2[1].y};
+  const float acc_b[4] = {acc_b2[0].x, acc_b2[0].y, acc_b2[1].x, acc_b2[1].y};
+  const float acc_d[4] = {acc_d2[0].x, acc_d2[0].y, acc_d2[1].x, acc_d2[1].y};
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     out[c + e] = acc_g[e];
@@ -803,6 +838,25 @@ inline int grid_blocks(int64_t R, int nw, int blocks_per_sm = 2) {
 
 // one-token-per-block kernels: D % 128 == 0; persistent grid of up to 64 warps
 // (at most 16 blocks) per SM
+template <int SURR>
+void launch_bwd_tok(bool p32, bool g32, bool pf, int grid, int threads, cudaStream_t st, const BwdParams& p) {
+  if (pf) {
+    if (p32)
+      g32 ? ln_lif_bwd_tok_kernel<4, 4, true, SURR><<<grid, threads, 0, st>>>(p)
+          : ln_lif_bwd_tok_kernel<4, 2, true, SURR><<<grid, threads, 0, st>>>(p);
+    else
+      g32 ? ln_lif_bwd_tok_kernel<2, 4, true, SURR><<<grid, threads, 0, st>>>(p)
+          : ln_lif_bwd_tok_kernel<2, 2, true, SURR><<<grid, threads, 0, st>>>(p);
+  } else {
+    if (p32)
+      g32 ? ln_lif_bwd_tok_kernel<4, 4, false, SURR><<<grid, threads, 0, st>>>(p)
+          : ln_lif_bwd_tok_kernel<4, 2, false, SURR><<<grid, threads, 0, st>>>(p);
+    else
+      g32 ? ln_lif_bwd_tok_kernel<2, 4, false, SURR><<<grid, threads, 0, st>>>(p)
+          : ln_lif_bwd_tok_kernel<2, 2, false, SURR><<<grid, threads, 0, st>>>(p);
+  }
+}
+
 inline bool use_tok(int D) { return D % 128 == 0 && D <= 128 * kTokMaxWarps; }
 // the one-token-per-block kernels move four elements per vector access and
 // read gamma / beta / bias as float4: every pointer 16-byte aligned
@@ -947,21 +1001,10 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
     if (use_tok((int)D) && aligned16) {
       const int threads = (int)D / 4;
       const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;
-      if (D <= 128 * kTokPfWarps) {
-        if (p32)
-          g32 ? ln_lif_bwd_tok_kernel<4, 4, true><<<grid, threads, 0, st>>>(p)
-              : ln_lif_bwd_tok_kernel<4, 2, true><<<grid, threads, 0, st>>>(p);
-        else
-          g32 ? ln_lif_bwd_tok_kernel<2, 4, true><<<grid, threads, 0, st>>>(p)
-              : ln_lif_bwd_tok_kernel<2, 2, true><<<grid, threads, 0, st>>>(p);
-      } else {
-        if (p32)
-          g32 ? ln_lif_bwd_tok_kernel<4, 4, false><<<grid, threads, 0, st>>>(p)
-              : ln_lif_bwd_tok_kernel<4, 2, false><<<grid, threads, 0, st>>>(p);
-        else
-          g32 ? ln_lif_bwd_tok_kernel<2, 4, false><<<grid, threads, 0, st>>>(p)
-              : ln_lif_bwd_tok_kernel<2, 2, false><<<grid, threads, 0, st>>>(p);
-      }
+      if (surrogate == SPK_SURROGATE_ARCTAN)
+        launch_bwd_tok<SPK_SURROGATE_ARCTAN>(p32, g32, D <= 128 * kTokPfWarps, grid, threads, st, p);
+      else
+        launch_bwd_tok<SPK_SURROGATE_SUPERSPIKE>(p32, g32, D <= 128 * kTokPfWarps, grid, threads, st, p);
     } else {
       // D not a multiple of 128 (so D <= 512): one warp per token, single columns
       p.cpt = (int)D / 32;

@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks at the benchmark shapes (CUDA events, device time).
 
-    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|data|shapes] [--iters N]
+    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|data|shapes|lnlif] [--iters N]
 
   lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 spikes (the MLP
         expansion LIF of a 64-image batch); bound: HBM bytes.
@@ -158,9 +158,36 @@ def bench_shapes_once():
     torch.cuda.synchronize()
 
 
+def bench_lnlif(iters, R=16384, T=4):
+    """LayerNorm->LIF training kernels (``ops.ln_lif_fwd`` / ``ops.ln_lif_bwd``)
+    at the encoder shapes of 64 images per GPU: R tokens x T rows, D = 384 and
+    1536, bf16 pre-activation, spikes and gradient, with the folded bias.
+    Algorithmic bytes: forward pre + spikes, backward pre + gradient + g_pre."""
+    res = []
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for D in (384, 1536):
+        copies = 3
+        pres = [torch.randn(T * R, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(copies)]
+        gss = [torch.randn(T * R, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(copies)]
+        gamma, beta = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
+        bias = torch.zeros(D, device="cuda")
+        lif = torch.tensor([0.5, 1.0, 0.0], device="cuda")
+        stats = ops.ln_lif_fwd(pres[0], gamma, beta, 1e-5, lif[0:1], lif[1:2], lif[2:3], T, in_gain=0.5,
+                               spike_dtype=torch.bfloat16, bias=bias)[1]
+        fms = _time(lambda i: ops.ln_lif_fwd(pres[i % copies], gamma, beta, 1e-5, lif[0:1], lif[1:2], lif[2:3], T,
+                                             in_gain=0.5, spike_dtype=torch.bfloat16, bias=bias), iters)
+        bms = _time(lambda i: ops.ln_lif_bwd(gss[i % copies], pres[i % copies], stats, gamma, beta, lif[0:1],
+                                             lif[1:2], lif[2:3], T, 0.5, "arctan", 2.0, bias=bias, need_bias=True),
+                    iters)
+        el = T * R * D
+        res.append({"kernel": "ln_lif_fwd", "rows": T * R, "D": D, "us": fms * 1e3, "GB/s": el * 4 / fms / 1e6})
+        res.append({"kernel": "ln_lif_bwd", "rows": T * R, "D": D, "us": bms * 1e3, "GB/s": el * 6 / bms / 1e6})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "data", "shapes"])
+    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "data", "shapes", "lnlif"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
     a = ap.parse_args()
@@ -185,6 +212,10 @@ def main():
         for variant in (0, 1):
             out["results"].append(bench_ssa(a.iters, variant))
         out["results"].append(bench_ssa(a.iters, 0, N=64, causal=True))
+    if a.only in (None, "lnlif"):
+        for r in bench_lnlif(a.iters):
+            r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
+            out["results"].append(r)
     if a.only in (None, "data"):
         for r in bench_data(a.iters):
             r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
