@@ -553,6 +553,45 @@ struct BlockSum {
   __device__ __forceinline__ float sum(float v, int nw) { return sum2(make_float2(v, 0.0f), nw).x; }
 };
 
+// Mean and sum of squared deviations of a row in one block reduction: each
+// lane starts from its four columns, and partial (mean, M2) pairs are merged
+// with the parallel-variance formula (Chan et al.), in a fixed order, so
+// every thread gets the same result.  Within a warp both partners of a
+// shuffle hold equal counts: mean = (ma + mb) / 2, M2 = M2a + M2b + d^2 n / 2.
+__constant__ float2 c_merge_w[kTokMaxWarps] = {
+    {0.f, 0.f},           {1.f / 2, 64.f},        {1.f / 3, 256.f / 3},   {1.f / 4, 96.f},
+    {1.f / 5, 512.f / 5}, {1.f / 6, 640.f / 6},   {1.f / 7, 768.f / 7},   {1.f / 8, 112.f},
+    {1.f / 9, 1024.f / 9}, {1.f / 10, 115.2f},    {1.f / 11, 1280.f / 11}, {1.f / 12, 1408.f / 12},
+    {1.f / 13, 1536.f / 13}, {1.f / 14, 1664.f / 14}, {1.f / 15, 1792.f / 15}, {1.f / 16, 120.f}};
+
+__device__ __forceinline__ float2 block_mean_m2(BlockSum& bs, float2 mm, int nw) {
+  float n = 4.0f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mm.x, o);
+    const float o2 = __shfl_xor_sync(0xffffffffu, mm.y, o);
+    const float d = om - mm.x;
+    mm.y = (mm.y + o2) + d * d * (0.5f * n);
+    mm.x = 0.5f * (mm.x + om);
+    n *= 2.0f;
+  }
+  if (nw == 1) return mm;
+  float2* r = bs.red + bs.buf * kTokMaxWarps;
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = mm;
+  __syncthreads();
+  // merging warp w (128 values) into the first w warps: weights 1/(w+1) and
+  // 128 w/(w+1), from a table
+  float2 acc = r[0];
+  for (int w = 1; w < nw; ++w) {
+    const float2 b = r[w];
+    const float d = b.x - acc.x;
+    acc.x = fmaf(d, c_merge_w[w].x, acc.x);
+    acc.y = fmaf(d * d, c_merge_w[w].y, acc.y + b.y);
+  }
+  bs.buf ^= 1;
+  return acc;
+}
+
 // spikes of dtype SD (SPK_F32 / SPK_BF16 stored directly; -1: any dtype, chosen at run time)
 template <int SD>
 __device__ __forceinline__ void store_spikes4(void* p, int dt, int64_t i, const float* v) {
@@ -584,7 +623,10 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
   const float4 g4 = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
   const float4 b4 = p.beta_ln ? __ldg(reinterpret_cast<const float4*>(p.beta_ln + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 p4 = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w}, pp[4] = {p4.x, p4.y, p4.z, p4.w};
+  const float2 gg2[2] = {make_float2(g4.x, g4.y), make_float2(g4.z, g4.w)};
+  const float2 bb2[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+  const float2 pp2[2] = {make_float2(p4.x, p4.y), make_float2(p4.z, p4.w)};
+  const float2 beta2 = make_float2(lb, lb), gain2 = make_float2(p.gain, p.gain);
   const SpikeLayout lay(p.R, D, c, p.hd, p.seq);
   // the next token's rows are loaded while this one is processed
   RawVec<EB> nxt[kMaxT];
@@ -604,32 +646,33 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
       for (int t = 0; t < kMaxT; ++t)
         if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + tn) * D + c);
     }
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 v2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t) {
       if (t >= T) continue;
       float x[4];
       raw_unpack<EB>(raw[t], p.pre_dtype, x);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] += pp[e];
-      const float mean = bs.sum((x[0] + x[1]) + (x[2] + x[3]), nw) * invD;
-      float s2 = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float d = x[e] - mean;
-        s2 = fmaf(d, d, s2);
-      }
-      const float rstd = rsqrtf(fmaf(bs.sum(s2, nw), invD, p.eps));
+      const float2 x01 = add2(make_float2(x[0], x[1]), pp2[0]), x23 = add2(make_float2(x[2], x[3]), pp2[1]);
+      // this lane's (mean, M2), then one block merge
+      const float lm = ((x01.x + x01.y) + (x23.x + x23.y)) * 0.25f;
+      const float2 d01 = add2(x01, make_float2(-lm, -lm)), d23 = add2(x23, make_float2(-lm, -lm));
+      const float2 q = fma2(d01, d01, mul2(d23, d23));
+      const float2 mv = block_mean_m2(bs, make_float2(lm, q.x + q.y), nw);
+      const float mean = mv.x;
+      const float rstd = rsqrtf(fmaf(mv.y, invD, p.eps));
       const int64_t row = (int64_t)t * p.R + tok;
       if (threadIdx.x == 0) p.stats[row] = make_float2(mean, rstd);
+      const float2 nm2 = make_float2(-mean, -mean), r2 = make_float2(rstd, rstd);
+      const float2 xs[2] = {x01, x23};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float y = fmaf((x[e] - mean) * rstd, gg[e], bb[e]);
-        const float cur = p.gain != 1.0f ? __fmul_rn(y, p.gain) : y;
-        const float u = __fadd_rn(__fmul_rn(v[e], lb), cur);
-        const bool sp = u > vth;
-        x[e] = sp ? 1.0f : 0.0f;
-        v[e] = sp ? vr : u;
+      for (int j = 0; j < 2; ++j) {
+        const float2 y = fma2(mul2(add2(xs[j], nm2), r2), gg2[j], bb2[j]);
+        const float2 cur = p.gain != 1.0f ? mul2(y, gain2) : y;
+        const float2 u = add2(mul2(v2[j], beta2), cur);
+        const bool sx = u.x > vth, sy = u.y > vth;
+        x[2 * j] = sx ? 1.0f : 0.0f;
+        x[2 * j + 1] = sy ? 1.0f : 0.0f;
+        v2[j] = make_float2(sx ? vr : u.x, sy ? vr : u.y);
       }
       store_spikes4<SD>(p.spikes, p.spike_dtype, so + t * lay.t_stride, x);
     }
