@@ -139,6 +139,8 @@ int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void
  *   reset.  pre_bias ([D] fp32 or NULL) is the preceding Linear's bias, so
  *   that Linear can run without one.
  * pre: [T][R][D] (f32/f16/bf16); spikes: [T][R][D] in spike_dtype;
+ * pre_ld: row stride of pre in elements (0 or D: contiguous; wider: pre is a
+ * column slice of a wider GEMM output, D % 128 == 0 only).
  * With head_dim > 0 the spikes are written head-major instead,
  * [T*B][D/head_dim][seq_len][head_dim] with R = B * seq_len (the layout of
  * SSA.py's per-head Q, K, V, :221-233), for D % 128 == 0 only.
@@ -149,8 +151,8 @@ int spk_lif_bwd_noalloc(const float* g_spikes, const float* g_vfinal, const void
 int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
                    const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
                    const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D,
-                   int64_t head_dim, int64_t seq_len, void* spikes, int spike_dtype, float* stats,
-                   void* stream);
+                   int64_t pre_ld, int64_t head_dim, int64_t seq_len, void* spikes, int spike_dtype,
+                   float* stats, void* stream);
 
 /*
  * Backward of spk_ln_lif_fwd (LIFLayer.backward Lif.py:46-102 composed with
@@ -161,8 +163,9 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
  *   g_lif_beta = sum g_v v_prev
  * (sums over all rows, reduced in a fixed order).  g_spikes: f32/f16/bf16;
  * g_pre has pre's dtype; pre_bias is the forward's; g_gamma / g_beta_ln /
- * g_bias / g_lif_beta may be NULL.  head_dim / seq_len: the forward's;
- * g_spikes is then read head-major.
+ * g_bias / g_lif_beta may be NULL.  pre_ld / head_dim / seq_len: the
+ * forward's; g_pre has pre's row stride, and g_spikes is read head-major when
+ * head_dim > 0.
  * workspace: spk_ln_lif_bwd_workspace_bytes(T, R, D) bytes.
  */
 int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D);
@@ -170,8 +173,8 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
                    const float* pre_bias, const float* stats, const float* ln_gamma,
                    const float* ln_beta, const float* lif_beta, const float* lif_vth,
                    const float* lif_vreset, float in_gain, int surrogate, float surrogate_k, int64_t T,
-                   int64_t R, int64_t D, int64_t head_dim, int64_t seq_len, void* g_pre, float* g_gamma,
-                   float* g_beta_ln, float* g_bias, float* g_lif_beta, void* workspace,
+                   int64_t R, int64_t D, int64_t pre_ld, int64_t head_dim, int64_t seq_len, void* g_pre,
+                   float* g_gamma, float* g_beta_ln, float* g_bias, float* g_lif_beta, void* workspace,
                    int64_t workspace_bytes, void* stream);
 
 /*

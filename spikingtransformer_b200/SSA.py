@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from ._fused import bf16_input, fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train
+from ._fused import bf16_input, fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train, qkv_ln_lif_train
 from .Lif import LIF
 
 
@@ -117,9 +117,17 @@ class _SSACore(nn.Module):
         qb = bf16_input(query)
         kb = qb if key is query else bf16_input(key)
         vb = kb if value is key else (qb if value is query else bf16_input(value))
-        q = lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True, heads=(hd, N), xb=qb)
-        k = lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True, heads=(hd, Nk), xb=kb)
-        v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk), xb=vb)
+        qkv = None
+        if key is query and value is query:
+            # self-attention: one GEMM for Q, K and V
+            qkv = qkv_ln_lif_train(query, (self.q_proj, self.k_proj, self.v_proj), (self.lnq, self.lnk, self.lnv),
+                                   (self.lifq, self.lifk, self.lifv), (hd, N), xb=qb)
+        if qkv is not None:
+            q, k, v = qkv
+        else:
+            q = lin_ln_lif_train(query, self.q_proj, self.lnq, self.lifq, narrow=True, heads=(hd, N), xb=qb)
+            k = lin_ln_lif_train(key, self.k_proj, self.lnk, self.lifk, narrow=True, heads=(hd, Nk), xb=kb)
+            v = lin_ln_lif_train(value, self.v_proj, self.lnv, self.lifv, narrow=True, heads=(hd, Nk), xb=vb)
         # token-major [TB, N, D]; the lifs LIF is per neuron, so it commutes with
         # the reference's transpose back from heads (SSA.py:242-247)
         s = self._combine_lif(q, k, v, attention_mask)

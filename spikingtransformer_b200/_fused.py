@@ -119,6 +119,84 @@ class LNLIFFunction(torch.autograd.Function):
         return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, None, None
 
 
+class QKVLNLIF(torch.autograd.Function):
+    """The Q, K and V LayerNorm->LIF passes of a self-attention over the column
+    slices of one ``[rows, 3D]`` GEMM output (``x [Wq; Wk; Wv]^T``).  Each pass
+    reads its slice in place, and the backward writes the three input
+    gradients into one ``[rows, 3D]`` buffer, so the GEMM before it has a
+    single input gradient (one dgrad GEMM over K = 3D, accumulated in fp32).
+    ``per`` holds, for Q, K and V, ``(eps, k, surrogate, in_gain)``; the
+    tensors are, for Q, K and V, ``(bias, ln weight, ln bias, lif beta, v_th,
+    v_reset)``."""
+
+    @staticmethod
+    def forward(ctx, pre3, T, per, spike_dtype, heads, *tensors):
+        D = pre3.shape[-1] // 3
+        outs, stats = [], []
+        for i in range(3):
+            pb, w, b, lb, vth, vr = tensors[6 * i:6 * i + 6]
+            eps, _, _, gain = per[i]
+            s, st = ops.ln_lif_fwd(pre3[..., i * D:(i + 1) * D], w, b, eps, lb, vth, vr, T, gain,
+                                   spike_dtype=spike_dtype, bias=pb, heads=heads)
+            outs.append(s)
+            stats.append(st)
+        ctx.save_for_backward(pre3, *stats, *tensors)
+        ctx.T, ctx.per, ctx.heads = int(T), per, heads
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *g_spikes):
+        pre3, st0, st1, st2 = ctx.saved_tensors[:4]
+        tensors = ctx.saved_tensors[4:]
+        stats = (st0, st1, st2)
+        need = ctx.needs_input_grad
+        D = pre3.shape[-1] // 3
+        g3 = torch.empty_like(pre3)
+        grads = []
+        for i in range(3):
+            pb, w, b, lb, vth, vr = tensors[6 * i:6 * i + 6]
+            _, k, surrogate, gain = ctx.per[i]
+            n = 5 + 6 * i  # index of this pass's bias among forward's inputs
+            gs = g_spikes[i]
+            if gs is None:
+                shape = (pre3.shape[0] * pre3.shape[1] // ctx.heads[1], D // ctx.heads[0], ctx.heads[1],
+                         ctx.heads[0]) if ctx.heads is not None else pre3[..., :D].shape
+                gs = torch.zeros(shape, dtype=pre3.dtype, device=pre3.device)
+            _, gw, gb, glb, gpb = ops.ln_lif_bwd(gs, pre3[..., i * D:(i + 1) * D], stats[i], w, b, lb, vth, vr,
+                                                 ctx.T, gain, surrogate, k, need_gamma=need[n + 1],
+                                                 need_beta=need[n + 2], need_lif_beta=need[n + 3], bias=pb,
+                                                 need_bias=pb is not None and need[n], heads=ctx.heads,
+                                                 g_pre_out=g3[..., i * D:(i + 1) * D])
+            grads += [gpb.to(pb.dtype) if gpb is not None else None, gw.to(w.dtype) if gw is not None else None,
+                      gb.to(b.dtype) if gb is not None else None,
+                      glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None, None, None]
+        return (g3, None, None, None, None, *grads)
+
+
+def qkv_ln_lif_train(x, projs, lns, lifs, heads, xb=None):
+    """Q, K, V spikes (head-major ``[TB, H, N, dh]``) of a self-attention on the
+    autograd path from one GEMM: under bf16 autocast and with D % 128 == 0,
+    ``x [Wq; Wk; Wv]^T`` in one ``LinearBF16`` and the three LayerNorm->LIF
+    passes in ``QKVLNLIF``; None when that path does not apply (the caller
+    then projects separately)."""
+    D = projs[0].out_features
+    if xb is None:
+        xb = bf16_input(x)
+    if (xb is None or D % 128 or heads[0] % 4 or D % heads[0]
+            or any(p.out_features != D or p.weight.dtype != torch.float32 for p in projs)
+            or not all(_ln_lif_fusable(x, D, ln, lif) for ln, lif in zip(lns, lifs))
+            or len({lif.n_steps for lif in lifs}) != 1):
+        return None
+    w3 = torch.cat([p.weight for p in projs], dim=0)
+    pre3 = LinearBF16.apply(x, w3, xb, w3.detach().to(torch.bfloat16))
+    per = [(ln.eps, lif._k_host, lif.surrogate, lif.in_gain) for ln, lif in zip(lns, lifs)]
+    tensors = []
+    for p, ln, lif in zip(projs, lns, lifs):
+        tensors += [p.bias, ln.weight, ln.bias, lif.effective_beta(), lif.v_th, lif.v_reset]
+    dt = torch.get_autocast_dtype(x.device.type)
+    return QKVLNLIF.apply(pre3, lifs[0].n_steps, per, dt, heads, *tensors)
+
+
 def _ln_lif_fusable(x, D, ln, lif):
     return (x.is_cuda and isinstance(ln, torch.nn.LayerNorm) and ln.elementwise_affine
             and tuple(ln.normalized_shape) == (D,) and x.shape[0] % lif.n_steps == 0

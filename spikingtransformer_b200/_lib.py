@@ -38,10 +38,11 @@ SIGNATURES = {
     "spk_linear_ln_lif_fwd": ([_p, _p, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _p, _i, _p,
                                _p, _p], _i),
     "spk_linear_fwd": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),
-    "spk_ln_lif_fwd": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),
+    "spk_ln_lif_fwd": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p],
+                       _i),
     "spk_ln_lif_bwd_workspace_bytes": ([_i64, _i64, _i64], _i64),
-    "spk_ln_lif_bwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _f, _i, _f, _i64, _i64, _i64, _i64, _i64, _p,
-                        _p, _p, _p, _p, _p, _i64, _p], _i),
+    "spk_ln_lif_bwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _f, _i, _f, _i64, _i64, _i64, _i64, _i64, _i64,
+                        _p, _p, _p, _p, _p, _p, _i64, _p], _i),
     "spk_ssa_fwd": ([_p, _p, _p, _i, _i, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64,
                      _i64, _i64, _p, _i, _p, _p], _i),
     "spk_embed_pe_lif_fwd": ([_p, _p, _f, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),

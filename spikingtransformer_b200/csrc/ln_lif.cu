@@ -56,6 +56,7 @@ struct FwdParams {
   int64_t R;
   int D, cpt;
   int hd, seq;  // head-major spikes [T*B][D/hd][seq][hd] when hd > 0 (R = B * seq)
+  int64_t ld;   // row stride of pre (and g_pre) in elements (D, or wider for a column slice)
 };
 
 struct BwdParams {
@@ -77,6 +78,7 @@ struct BwdParams {
   int64_t R;
   int D, cpt;
   int hd, seq;  // head-major spikes [T*B][D/hd][seq][hd] when hd > 0 (R = B * seq)
+  int64_t ld;   // row stride of pre (and g_pre) in elements (D, or wider for a column slice)
 };
 
 __device__ __forceinline__ float load_elem(const void* p, int dt, int64_t i) {
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
   if ((int64_t)blockIdx.x < p.R) {
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t)
-      if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + blockIdx.x) * D + c);
+      if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + blockIdx.x) * p.ld + c);
   }
   for (int64_t tok = blockIdx.x; tok < p.R; tok += gridDim.x) {
     const int64_t so = lay.tok_off(tok, D) + lay.col_off;
@@ -644,7 +646,7 @@ __global__ void __launch_bounds__(32 * kTokMaxWarps) ln_lif_fwd_tok_kernel(const
     if (tn < p.R) {
 #pragma unroll
       for (int t = 0; t < kMaxT; ++t)
-        if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + tn) * D + c);
+        if (t < T) raw_load<EB>(nxt[t], p.pre, ((int64_t)t * p.R + tn) * p.ld + c);
     }
     float2 v2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -712,7 +714,7 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
       if (t >= T) continue;
       const int64_t row = (int64_t)t * p.R + tk;
       st[t] = p.stats[row];
-      raw_load<EBP>(rp[t], p.pre, row * D + c);
+      raw_load<EBP>(rp[t], p.pre, row * p.ld + c);
       raw_load<EBG>(rg[t], p.g_spikes, so + t * lay.t_stride);
     }
   };
@@ -817,7 +819,7 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
         dx[2 * j + 1] = dd.y;
         acc_d2[j] = add2(acc_d2[j], dd);
       }
-      store4(p.g_pre, p.pre_dtype, ((int64_t)t * p.R + tok) * D + c, dx);
+      store4(p.g_pre, p.pre_dtype, ((int64_t)t * p.R + tok) * p.ld + c, dx);
     }
   }
   // per-block partials: each thread owns its four columns; the LIF beta term
@@ -924,6 +926,16 @@ inline int bwd_grid(int64_t R, int D, bool aligned16) {
 
 using namespace lnlif;
 
+// pre row stride wider than D (a column slice of a wider GEMM output): only the
+// one-token-per-block kernels
+static int check_ld(int64_t ld, int64_t D, bool tok_ok) {
+  if (ld == D) return SPK_OK;
+  SPK_REQUIRE(ld > D && tok_ok, SPK_ERR_SHAPE,
+              "pre row stride %lld needs D %% 128 == 0 (D=%lld), a stride >= D and a multiple of 4, and 16-byte "
+              "aligned pointers", (long long)ld, (long long)D);
+  return SPK_OK;
+}
+
 // head-major spike layout (head_dim > 0): only the one-token-per-block kernels
 static int check_heads(int64_t head_dim, int64_t seq_len, int64_t R, int D, bool tok_ok) {
   if (head_dim <= 0) return SPK_OK;
@@ -960,8 +972,8 @@ int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D) {
 
 int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
                    const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
-                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, int64_t head_dim,
-                   int64_t seq_len, void* spikes, int spike_dtype, float* stats, void* stream) {
+                   const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, int64_t pre_ld,
+                   int64_t head_dim, int64_t seq_len, void* spikes, int spike_dtype, float* stats, void* stream) {
   using namespace spk;
   int rc = check_ln_lif((int)T, R, (int)D);
   if (rc != SPK_OK) return rc;
@@ -974,9 +986,10 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
   if (R == 0) return SPK_OK;
   FwdParams p = {pre, pre_dtype, pre_bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain,
                  spikes, spike_dtype, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0,
-                 (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1)};
+                 (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1), pre_ld > 0 ? pre_ld : D};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const bool aligned16 = tok_aligned({pre, spikes, ln_gamma, ln_beta, pre_bias});
+  const bool aligned16 = tok_aligned({pre, spikes, ln_gamma, ln_beta, pre_bias}) && p.ld % 4 == 0;
+  if ((rc = check_ld(p.ld, D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
   SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
               "D=%lld > %d needs pre, spikes, ln_gamma, ln_beta and pre_bias 16-byte aligned", (long long)D,
               32 * kMaxCpt);
@@ -1004,7 +1017,8 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
 int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype, const float* pre_bias,
                    const float* stats, const float* ln_gamma, const float* ln_beta, const float* lif_beta,
                    const float* lif_vth, const float* lif_vreset, float in_gain, int surrogate, float surrogate_k,
-                   int64_t T, int64_t R, int64_t D, int64_t head_dim, int64_t seq_len, void* g_pre, float* g_gamma,
+                   int64_t T, int64_t R, int64_t D, int64_t pre_ld, int64_t head_dim, int64_t seq_len, void* g_pre,
+                   float* g_gamma,
                    float* g_beta_ln, float* g_bias, float* g_lif_beta, void* workspace, int64_t workspace_bytes,
                    void* stream) {
   using namespace spk;
@@ -1024,7 +1038,9 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
               (long long)workspace_bytes, (long long)need);
   if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const bool aligned16 = tok_aligned({g_spikes, pre, g_pre, ln_gamma, ln_beta, pre_bias});
+  const int64_t ld = pre_ld > 0 ? pre_ld : D;
+  const bool aligned16 = tok_aligned({g_spikes, pre, g_pre, ln_gamma, ln_beta, pre_bias}) && ld % 4 == 0;
+  if ((rc = check_ld(ld, D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
   SPK_REQUIRE(aligned16 || D <= 32 * kMaxCpt, SPK_ERR_ALIGN,
               "D=%lld > %d needs g_spikes, pre, g_pre, ln_gamma, ln_beta and pre_bias 16-byte aligned",
               (long long)D, 32 * kMaxCpt);
@@ -1040,7 +1056,7 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
     BwdParams p = {g_spikes, gs_dtype, pre, pre_dtype, pre_bias, reinterpret_cast<const float2*>(stats), ln_gamma,
                    ln_beta, lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
                    (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k), g_pre, part, (int)T, R, (int)D, 0,
-                   (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1)};
+                   (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1), pre_ld > 0 ? pre_ld : D};
     if (use_tok((int)D) && aligned16) {
       const int threads = (int)D / 4;
       const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;

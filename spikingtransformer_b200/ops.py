@@ -121,16 +121,34 @@ def ln_lif_ok(T, D):
     return 1 <= T <= 4 and D % 32 == 0 and 32 <= D <= 2048 and (D <= 512 or D % 128 == 0)
 
 
+def _row_stride(t):
+    """Row stride (elements) of ``t`` viewed as ``[rows, t.shape[-1]]`` with unit
+    column stride (a column slice of a wider tensor qualifies), else None."""
+    if t.dim() < 2 or t.stride(-1) != 1:
+        return None
+    ld = t.stride(-2)
+    expected = ld
+    for i in range(t.dim() - 2, 0, -1):
+        expected *= t.shape[i]
+        if t.stride(i - 1) != expected:
+            return None
+    return ld
+
+
 def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
                spike_dtype=torch.float32, bias=None, heads=None):
     """``LIF(LayerNorm(pre + bias))`` over the t-major fold; ``pre`` ``[T*R, ..., D]``,
     ``bias`` ``[D]`` or None (the preceding Linear's bias, taken out of its GEMM).
     ``heads=(head_dim, seq_len)``: spikes written head-major, ``[T*R/seq_len,
     D/head_dim, seq_len, head_dim]`` (the per-head layout the attention reads).
-    Returns ``(spikes like pre in spike_dtype, stats fp32 [T*R', 2] (mean, rstd))``."""
+    ``pre`` may be a column slice of a wider tensor (row stride > D, read in
+    place).  Returns ``(spikes like pre in spike_dtype, stats fp32 [T*R', 2]
+    (mean, rstd))``."""
     _cuda(pre)
-    pre = pre.contiguous()
     D = pre.shape[-1]
+    ld = _row_stride(pre)
+    if ld is None or ld < D or (ld != D and (D % 128 or ld % 4)):
+        pre, ld = pre.contiguous(), D
     rows = pre.numel() // D
     if rows % T:
         raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
@@ -146,7 +164,7 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
     _lib.call("spk_ln_lif_fwd", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(pb), _lib.ptr(g), _lib.ptr(bt),
               float(ln_eps),
-              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, hd, sl, _lib.ptr(spikes),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, D, ld, hd, sl, _lib.ptr(spikes),
               _lib.DTYPE_CODE[spike_dtype], _lib.ptr(stats), _lib.stream_ptr(dev), tag="ln_lif_fwd D=%d" % D,
               work=dict(bytes=rows * D * (pre.element_size() + spikes.element_size()) + rows * 8))
     return spikes, stats
@@ -154,20 +172,29 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
 
 def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
                surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True, bias=None,
-               need_bias=False, heads=None):
+               need_bias=False, heads=None, g_pre_out=None):
     """Backward of ``ln_lif_fwd``: ``(g_pre like pre, g_gamma [D] or None, g_beta [D] or None,
     g_lif_beta [1] or None, g_bias [D] or None)``; ``bias`` and ``heads`` are the
-    forward's (with ``heads``, ``g_spikes`` is head-major like the spikes)."""
+    forward's (with ``heads``, ``g_spikes`` is head-major like the spikes).
+    ``g_pre_out``: where to write g_pre, with pre's shape and row stride (e.g.
+    the matching column slice of a wider gradient buffer)."""
     _cuda(g_spikes, pre, stats)
-    pre = pre.contiguous()
+    D = pre.shape[-1]
+    ld = _row_stride(pre)
+    strided_ok = ld is not None and ld >= D and (ld == D or (D % 128 == 0 and ld % 4 == 0))
+    if g_pre_out is not None:
+        if not strided_ok or _row_stride(g_pre_out) != ld or g_pre_out.shape != pre.shape \
+                or g_pre_out.dtype != pre.dtype:
+            raise RuntimeError("g_pre_out must match pre's shape, dtype and row stride")
+    elif not strided_ok or ld != D:
+        pre, ld = pre.contiguous(), D
     g_spikes = g_spikes.contiguous()
     if g_spikes.dtype not in (torch.float32, torch.float16, torch.bfloat16):
         g_spikes = g_spikes.float()
-    D = pre.shape[-1]
     rows = pre.numel() // D
     R = rows // T
     dev = pre.device
-    g_pre = torch.empty_like(pre)
+    g_pre = g_pre_out if g_pre_out is not None else torch.empty(pre.shape, dtype=pre.dtype, device=dev)
     gg = torch.empty(D, dtype=torch.float32, device=dev) if need_gamma else None
     gb = torch.empty(D, dtype=torch.float32, device=dev) if need_beta else None
     glb = torch.empty(1, dtype=torch.float32, device=dev) if need_lif_beta else None
@@ -181,7 +208,7 @@ def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_v
     b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
     _lib.call("spk_ln_lif_bwd", _lib.ptr(g_spikes), _lib.dtype_code(g_spikes), _lib.ptr(pre), _lib.dtype_code(pre),
               _lib.ptr(pb), _lib.ptr(stats), _lib.ptr(g), _lib.ptr(bt), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr),
-              float(in_gain), _lib.SURROGATE[surrogate], float(k), T, R, D, hd, sl, _lib.ptr(g_pre), _lib.ptr(gg),
+              float(in_gain), _lib.SURROGATE[surrogate], float(k), T, R, D, ld, hd, sl, _lib.ptr(g_pre), _lib.ptr(gg),
               _lib.ptr(gb), _lib.ptr(gpb), _lib.ptr(glb), _lib.ptr(ws), wsb, _lib.stream_ptr(dev),
               tag="ln_lif_bwd D=%d" % D,
               work=dict(bytes=rows * D * (g_spikes.element_size() + 2 * pre.element_size()) + rows * 8))

@@ -147,6 +147,39 @@ def test_xnor_lif_fused_equals_composition(pkg, spike_dtype):
     assert torch.allclose(sc0, sc1, rtol=1e-4, atol=1e-6)
 
 
+def test_fused_qkv_training_path_matches_separate(pkg, monkeypatch):
+    """Self-attention under bf16 autocast with Q, K and V from one GEMM and one
+    LayerNorm->LIF Function against the three separate projections: the same
+    spikes (up to a GEMM rounding flip near threshold) and close gradients for
+    every projection, LayerNorm and LIF parameter."""
+    import spikingtransformer_b200.SSA as ssa_mod
+    T, TB, N, D, H = 4, 8, 16, 256, 4
+    g = torch.Generator(device=DEV).manual_seed(23)
+    x = (torch.rand(TB, N, D, generator=g, device=DEV) < 0.3).float()
+    base = ssa_mod.SSAMultiHeadAttention(d_model=D, n_heads=H, n_steps=T).to(DEV)
+    base.lifq.set_surrogate("arctan", 2.0)
+    w = torch.randn(TB, N, D, generator=g, device=DEV)
+    runs = []
+    for fused in (True, False):
+        m = ssa_mod.SSAMultiHeadAttention(d_model=D, n_heads=H, n_steps=T).to(DEV)
+        m.load_state_dict(base.state_dict())
+        if not fused:
+            monkeypatch.setattr(ssa_mod, "qkv_ln_lif_train", lambda *a, **k: None)
+        xi = x.clone().requires_grad_()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = m(xi)
+        (y.float() * w).sum().backward()
+        runs.append((y.float().detach(), xi.grad.clone(), {n: p.grad.clone() for n, p in m.named_parameters()
+                                                           if p.grad is not None}))
+    (y1, gx1, g1), (y2, gx2, g2) = runs
+    assert (y1 != y2).float().mean().item() < 0.01
+    assert set(g1) == set(g2)
+    for n in g1:
+        ref = g2[n].abs().max().item()
+        assert (g1[n] - g2[n]).abs().max().item() <= 0.05 * ref + 1e-6, n
+    assert (gx1 - gx2).abs().max().item() <= 0.05 * gx2.abs().max().item() + 1e-6
+
+
 def test_linear_bf16_training_gemm(pkg):
     """The training path's bias-free bf16 GEMM against torch's autocast Linear:
     the same bf16 output, and fp32 input / weight gradients at least as close
