@@ -254,6 +254,19 @@ def test_linear_plain(ops):
         assert torch.allclose(out.cpu(), ref, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("B,C,H,W,p", [(3, 1, 32, 64, 16), (2, 3, 12, 18, 6), (2, 2, 8, 24, 4)])
+def test_patch_im2col_matches_unfold(ops, B, C, H, W, p):
+    """Patch rows [hi | lo] in bf16 against torch's unfold of the same image
+    (vector kernel for p % 4 == 0 and W % 4 == 0, scalar kernel otherwise)."""
+    g = gen(B * 100 + p)
+    img = torch.rand(B, C, H, W, generator=g)
+    a = ops.patch_im2col(img.to(DEV), p).cpu()
+    ref = F.unfold(img, p, stride=p).transpose(1, 2).reshape(-1, C * p * p)
+    hi = ref.to(torch.bfloat16)
+    lo = (ref - hi.float()).to(torch.bfloat16)
+    assert torch.equal(a, torch.cat([hi, lo], dim=1))
+
+
 def test_patch_embed_split(ops):
     g = gen(3)
     img = torch.rand(3, 1, 32, 64, generator=g)
