@@ -267,16 +267,27 @@ def run_train(args, ws, rank, local):
     round_weights_bf16(model)
     model.set_surrogate("arctan", 2.0)
     model = model.to(dev).train()
+    # The forward, backward and optimizer step are captured once into a CUDA
+    # graph (the host would otherwise spend longer enqueueing the step's ~2,000
+    # launches than the GPU spends running them); each step generates its batch
+    # into the graph's static input buffers and replays the graph.  With N > 1
+    # every parameter's gradient is a view into one flat fp32 buffer, and the
+    # graph ends its backward with one NCCL all-reduce of that buffer (divided
+    # by N): data parallelism without DDP's hooks, which a graph cannot hold.
+    # --no-graph runs the step eagerly (DDP for N > 1).
+    use_graph = not args.no_graph
     net = model
-    if ws > 1:
+    flat = None
+    if ws > 1 and not use_graph:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
                                                         gradient_as_bucket_view=True)
-    # one GPU: the forward, backward and optimizer step are captured once into a
-    # CUDA graph (the host would otherwise spend longer enqueueing the step's
-    # ~2,000 launches than the GPU spends running them); each step generates
-    # its batch into the graph's static input buffers and replays the graph.
-    # With DDP (N > 1) the step runs eagerly.
-    use_graph = ws == 1 and not args.no_graph
+    if ws > 1 and use_graph:
+        params = [p for p in model.parameters() if p.requires_grad]
+        flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+        off = 0
+        for p in params:
+            p.grad = flat[off:off + p.numel()].view_as(p)
+            off += p.numel()
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=use_graph)
     B = args.batch or 64
     mask = torch.tril(torch.ones(SEQ, SEQ, device=dev)).expand(B, 1, SEQ, SEQ)
@@ -285,16 +296,26 @@ def run_train(args, ws, rank, local):
         return ops.synth_text_lines(B, 1_000_000 + shard_seed(rank, i), H=IMG[1], W=IMG[2], L=SEQ + 1,
                                     V=ARCH["tgt_vocab_size"], device=dev)
 
+    def zero_grads():
+        if flat is not None:
+            flat.zero_()  # the gradients stay views into it
+        else:
+            opt.zero_grad(set_to_none=True)
+
     def train_step(src, labels):
         tgt_in, tgt_out = labels[:, :-1], labels[:, 1:]
         with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=not use_graph):
             logits, _ = net(src, tgt_in, look_ahead_mask=mask)
         loss, acc, _ = ops.ce_over_t(logits, tgt_out, ignore_index=0, label_smoothing=0.1)
         loss.backward()
+        if flat is not None:
+            dist.all_reduce(flat)
+            flat.div_(ws)
         opt.step()
         return loss, acc
 
     graph_launches = None
+    graphs = {}  # released before the process group (a graph that holds NCCL calls must go first)
     if use_graph:
         static_src, static_labels = gen(0)
         side = torch.cuda.Stream(dev)
@@ -304,12 +325,15 @@ def run_train(args, ws, rank, local):
                 src, labels = gen(i)
                 static_src.copy_(src)
                 static_labels.copy_(labels)
-                opt.zero_grad(set_to_none=True)
+                zero_grads()
                 train_step(static_src, static_labels)
         torch.cuda.current_stream(dev).wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        opt.zero_grad(set_to_none=True)
-        with _lib.LaunchCounter() as counter, torch.cuda.graph(graph):
+        graphs["train"] = torch.cuda.CUDAGraph()
+        if flat is None:
+            opt.zero_grad(set_to_none=True)
+        with _lib.LaunchCounter() as counter, torch.cuda.graph(graphs["train"]):
+            if flat is not None:
+                flat.zero_()
             g_loss, g_acc = train_step(static_src, static_labels)
         graph_launches = counter.total()
 
@@ -317,12 +341,12 @@ def run_train(args, ws, rank, local):
             src, labels = gen(i)
             static_src.copy_(src)
             static_labels.copy_(labels)
-            graph.replay()
+            graphs["train"].replay()
             return g_loss, g_acc
     else:
         def step(i):
             src, labels = gen(i)
-            opt.zero_grad(set_to_none=True)
+            zero_grads()
             return train_step(src, labels)
 
         for i in range(args.warmup):
@@ -353,13 +377,17 @@ def run_train(args, ws, rank, local):
                        "seq_len": SEQ, "image": list(IMG), "T": 4, "layers": "8 enc + 4 dec",
                        "optimizer": "AdamW lr 1e-4", "surrogate": "arctan alpha 2",
                        "loss": "mean over T of CE(ignore_index=0, label_smoothing=0.1), fused with token accuracy",
-                       "parallelism": "ddp%d (NCCL all-reduce of gradients)" % ws},
+                       "parallelism": ("dp%d (flat fp32 gradient all-reduce over NCCL inside the CUDA graph)" % ws
+                                       if flat is not None else "ddp%d (NCCL all-reduce of gradients)" % ws)},
             "loss": last, "token_accuracy": last_acc, "clocks": clk.summary(),
             "cuda_graph": use_graph, "graph_launches_per_step": graph_launches,
             "gpu_launches": sum(v["launches"] for v in kernels.values()) + (graph_launches or 0) * args.steps,
             "kernels": {k: {"launches": v["launches"], "ms_per_step": v["ms"] / args.steps}
                         for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])},
         }), flush=True)
+    graphs.clear()
+    step = None
+    torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
