@@ -244,6 +244,24 @@ def run_reference(args, ws, rank):
     }), flush=True)
 
 
+def flat_grad_views(params, device):
+    """One zeroed fp32 buffer holding every parameter's gradient as a view (in
+    order), for a data-parallel step that all-reduces a single tensor."""
+    flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=device)
+    off = 0
+    for p in params:
+        p.grad = flat[off:off + p.numel()].view_as(p)
+        off += p.numel()
+    return flat
+
+
+def average_flat_grads(flat, ws):
+    """Sum the flat gradient buffer over the ranks and divide by their number."""
+    import torch.distributed as dist
+    dist.all_reduce(flat)
+    flat.div_(ws)
+
+
 def run_train(args, ws, rank, local):
     """--workload train: forward + backward + AdamW step of the same model, one
     process per GPU, gradients all-reduced by DDP over NCCL (bf16 autocast as
@@ -282,12 +300,7 @@ def run_train(args, ws, rank, local):
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
                                                         gradient_as_bucket_view=True)
     if ws > 1 and use_graph:
-        params = [p for p in model.parameters() if p.requires_grad]
-        flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
-        off = 0
-        for p in params:
-            p.grad = flat[off:off + p.numel()].view_as(p)
-            off += p.numel()
+        flat = flat_grad_views([p for p in model.parameters() if p.requires_grad], dev)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=use_graph)
     B = args.batch or 64
     mask = torch.tril(torch.ones(SEQ, SEQ, device=dev)).expand(B, 1, SEQ, SEQ)
@@ -309,8 +322,7 @@ def run_train(args, ws, rank, local):
         loss, acc, _ = ops.ce_over_t(logits, tgt_out, ignore_index=0, label_smoothing=0.1)
         loss.backward()
         if flat is not None:
-            dist.all_reduce(flat)
-            flat.div_(ws)
+            average_flat_grads(flat, ws)
         opt.step()
         return loss, acc
 

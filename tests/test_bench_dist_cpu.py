@@ -73,3 +73,53 @@ def test_reference_arm_other_ranks_do_no_work(rank, capsys):
     ns = type("A", (), dict(steps=1, warmup=0))()
     bench.run_reference(ns, 2, rank)
     assert capsys.readouterr().out == ""
+
+
+def _dp_worker(rank, ws, port, out):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import bench
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60))
+    try:
+        results = []
+        for mode in ("ddp", "flat"):
+            torch.manual_seed(0)  # same initial weights on every rank
+            model = torch.nn.Sequential(torch.nn.Linear(12, 16), torch.nn.Tanh(), torch.nn.Linear(16, 3))
+            net = torch.nn.parallel.DistributedDataParallel(model) if mode == "ddp" else model
+            opt = torch.optim.AdamW(model.parameters(), lr=1e-2)
+            flat = bench.flat_grad_views(list(model.parameters()), torch.device("cpu")) if mode == "flat" else None
+            for step in range(3):
+                g = torch.Generator().manual_seed(100 * rank + step)  # each rank its own batch
+                x, y = torch.randn(8, 12, generator=g), torch.randn(8, 3, generator=g)
+                if flat is not None:
+                    flat.zero_()
+                else:
+                    opt.zero_grad(set_to_none=True)
+                torch.nn.functional.mse_loss(net(x), y).backward()
+                if flat is not None:
+                    bench.average_flat_grads(flat, ws)
+                opt.step()
+            if flat is not None:
+                # the gradients are still the views the optimizer read
+                assert all(p.grad.data_ptr() >= flat.data_ptr() for p in model.parameters())
+            results.append(torch.cat([p.detach().reshape(-1) for p in model.parameters()]).tolist())
+        out[rank] = results
+    finally:
+        dist.destroy_process_group()
+
+
+def test_flat_gradient_data_parallel_matches_ddp():
+    """The training bench's multi-GPU step (gradients as views into one flat
+    buffer, one all-reduce, divided by the world size) updates the weights as
+    DistributedDataParallel does, and identically on every rank."""
+    ws = 2
+    port = _free_port()
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_dp_worker, args=(ws, port, out), nprocs=ws, join=True, start_method="spawn")
+        res = dict(out)
+    ddp0, flat0 = (torch.tensor(v) for v in res[0])
+    ddp1, flat1 = (torch.tensor(v) for v in res[1])
+    assert torch.equal(flat0, flat1) and torch.equal(ddp0, ddp1)
+    assert torch.allclose(flat0, ddp0, rtol=1e-5, atol=1e-6)
