@@ -315,6 +315,14 @@ int spk_xnor_train_grad_finish(const float* ke, const float* rg, const float* u,
                                void* dv, int out_dtype, int64_t TB, int64_t H, int64_t Nk, int64_t dh, void* stream);
 
 /*
+ * n_major: out[n][b][:] = in[b][n][:] for B x N rows of row_bytes bytes
+ * (a multiple of 16; in and out 16-byte aligned).  Makes the n-major
+ * [Nk][B][dh] operand of the shared log-distance product R V (SSA.py:235-240)
+ * from the head-major V [B][Nk][dh].
+ */
+int spk_xnor_train_n_major(const void* in, void* out, int64_t B, int64_t N, int64_t row_bytes, void* stream);
+
+/*
  * combine followed by the attention's output LIF (SSA.py:242, the LIF
  * module of Lif.py:288-441 over the T-major fold, T <= 4, TB % T == 0):
  * a_out <- the combined pre-activation (as spk_xnor_train_combine's out),

@@ -286,7 +286,8 @@ def _xnor_products(q, k, v, R):
     cv, w = cw[:, :1], cw[:, 1:]
     Mb = (2.0 * kv - cv).to(torch.bfloat16)                        # exact: |M| <= Nk
     qm = _bmm32(qb, Mb)                                            # [B, Nq, dh]
-    rv = torch.mm(Rb, vb.permute(1, 0, 2).reshape(Nk, B * dh), out_dtype=torch.float32)
+    vn = ops.xnor_train_n_major(vb) if (dh * 2) % 16 == 0 else vb.permute(1, 0, 2).reshape(Nk, B * dh)
+    rv = torch.mm(Rb, vn, out_dtype=torch.float32)
     return qb, kb, vb, Mb, Rb, qm, rv, w
 
 

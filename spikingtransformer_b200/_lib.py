@@ -54,6 +54,7 @@ SIGNATURES = {
     "spk_xnor_train_prep_chunks": ([_i64], _i64),
     "spk_xnor_train_grad_prep": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
     "spk_xnor_train_grad_finish": ([_p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _i64, _p], _i),
+    "spk_xnor_train_n_major": ([_p, _p, _i64, _i64, _i64, _p], _i),
     "spk_xnor_train_combine_lif": ([_p, _p, _p, _p, _p, _p, _p, _f, _p, _p, _i, _i64, _i64, _i64, _i64, _i64, _p], _i),
     "spk_xnor_train_grad_prep_lif": ([_p, _i, _p, _p, _p, _p, _p, _f, _i, _f, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                       _i64, _i64, _p], _i),

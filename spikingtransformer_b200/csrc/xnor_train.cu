@@ -328,6 +328,23 @@ __global__ void __launch_bounds__(256) grad_prep_lif_kernel(
   if (gbeta_part) gbeta_part[(int64_t)blockIdx.y * X + x] = bacc;
 }
 
+// n_major: out[n][b][:] = in[b][n][:] for rows of r16 16-byte words (the
+// n-major operand of the shared log-distance product R V).  Threads walk the
+// output in order, so the stores are fully coalesced and every input row is
+// read as whole 32-byte sectors.
+template <typename I>
+__global__ void __launch_bounds__(256) n_major_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, I B,
+                                                      I N, I r16) {
+  const I total = N * B * r16;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+    const I c = i % r16;
+    const I r = i / r16;
+    const I b = r % B;
+    const I n = r / B;
+    out[i] = __ldg(in + (b * N + n) * r16 + c);
+  }
+}
+
 inline int grid_for(int64_t n4) {
   const int64_t cap = (int64_t)num_sms() * 8;
   int64_t g = (n4 + 255) / 256;
@@ -361,6 +378,26 @@ int spk_xnor_train_combine(const float* qm, const float* rv, const float* w, con
   xnort::combine_kernel<<<xnort::grid_for(n4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       qm, rv, w, scale, out, TB, (int)H, (int)Nq, (int)dh);
   return check_launch("xnor combine_kernel");
+}
+
+int spk_xnor_train_n_major(const void* in, void* out, int64_t B, int64_t N, int64_t row_bytes, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(B >= 1 && N >= 1 && row_bytes >= 16 && row_bytes % 16 == 0 && B * N * row_bytes < (1ll << 40),
+              SPK_ERR_SHAPE, "unsupported sizes B=%lld N=%lld row_bytes=%lld (row_bytes a multiple of 16)",
+              (long long)B, (long long)N, (long long)row_bytes);
+  SPK_REQUIRE(in && out, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(aligned(in, 16) && aligned(out, 16), SPK_ERR_ALIGN, "in and out must be 16-byte aligned");
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  const int64_t r16 = row_bytes / 16, total = B * N * r16;
+  auto st = reinterpret_cast<cudaStream_t>(stream);
+  const auto* src = reinterpret_cast<const uint4*>(in);
+  auto* dst = reinterpret_cast<uint4*>(out);
+  if (total < (1ll << 30))  // 32-bit indices: total plus one grid stride stays below 2^31
+    xnort::n_major_kernel<int><<<xnort::grid_for(total), 256, 0, st>>>(src, dst, (int)B, (int)N, (int)r16);
+  else
+    xnort::n_major_kernel<int64_t><<<xnort::grid_for(total), 256, 0, st>>>(src, dst, B, N, r16);
+  return check_launch("xnor n_major_kernel");
 }
 
 int64_t spk_xnor_train_prep_chunks(int64_t Nq) { return (Nq + spk::xnort::kChunk - 1) / spk::xnort::kChunk; }

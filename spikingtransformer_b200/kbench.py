@@ -8,7 +8,9 @@
         Bernoulli(0.15) spikes (bf16), tau=2 neuron; bound: bf16 tensor FLOPs.
   ssa   spiking attention on Q, K, V [T=4, B=32, H=8, N=256, d=48]
         Bernoulli(0.15), plain (QK^T)V*0.125 and XNOR variants, plus the
-        causal N=64 case; FLOPs counted dense (QK^T and PV).
+        causal N=64 case; FLOPs counted dense (QK^T and PV); and the n-major
+        copy of V [2048, 256, 48] bf16 that the training path's R V reads,
+        beside torch's permute copy.
 Inputs are regenerated per configuration; each timed iteration rotates over
 input copies whose total exceeds the 126 MB L2.  Prints one JSON line.
 """
@@ -89,6 +91,21 @@ def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48):
     flops = 4.0 * T * B * H * N * N * d
     return {"kernel": "ssa", "variant": "plain" if variant == 0 else "xnor", "causal": causal,
             "shape": [T, B, H, N, d], "ms": ms, "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops}
+
+
+def bench_n_major(iters, B=2048, N=256, d=48):
+    """The n-major copy of V for the training attention's R V product
+    ([B, N, d] bf16 -> [N, B*d], B = T*images*H at 64 images), against
+    torch's strided permute copy of the same tensor; bound: HBM bytes."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    xs = [(torch.rand(B, N, d, device="cuda", generator=g) < 0.15).to(torch.bfloat16) for _ in range(3)]
+    nbytes = 2 * xs[0].numel() * 2
+    out = []
+    for name, fn in (("xnor_train_n_major", ops.xnor_train_n_major),
+                     ("torch permute copy", lambda x: x.permute(1, 0, 2).reshape(N, B * d))):
+        ms = _time(lambda i: fn(xs[i % 3]), iters)
+        out.append({"kernel": name, "shape": [B, N, d], "ms": ms, "GB/s": nbytes / ms / 1e6, "bytes": nbytes})
+    return out
 
 
 def bench_data(iters):
@@ -212,6 +229,9 @@ def main():
         for variant in (0, 1):
             out["results"].append(bench_ssa(a.iters, variant))
         out["results"].append(bench_ssa(a.iters, 0, N=64, causal=True))
+        for r in bench_n_major(a.iters):
+            r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
+            out["results"].append(r)
     if a.only in (None, "lnlif"):
         for r in bench_lnlif(a.iters):
             r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]

@@ -432,6 +432,22 @@ def xnor_train_grad_finish(ke, rg, u, dk32, TB, H, out_dtype):
     return dk, dv
 
 
+def xnor_train_n_major(x):
+    """``x`` ``[B, N, d]`` -> ``[N, B*d]`` with ``out[n, b*d:(b+1)*d] = x[b, n]``
+    (the n-major operand of ``R @ V``).  Rows of ``d`` elements must span a
+    multiple of 16 bytes."""
+    _cuda(x)
+    B, N, d = x.shape
+    row_bytes = d * x.element_size()
+    if row_bytes % 16:
+        raise ValueError(f"xnor_train_n_major: rows of {row_bytes} bytes are not a multiple of 16")
+    x = x.contiguous()
+    out = torch.empty((N, B * d), dtype=x.dtype, device=x.device)
+    _lib.call("spk_xnor_train_n_major", _lib.ptr(x), _lib.ptr(out), B, N, row_bytes, _lib.stream_ptr(x.device),
+              tag="xnor_train_n_major", work=dict(bytes=2 * x.numel() * x.element_size()))
+    return out
+
+
 def xnor_train_combine_lif(qm, rv, w, scale, TB, H, T, lif_beta, lif_vth, lif_vr, in_gain=1.0,
                            spike_dtype=torch.float32):
     """``xnor_train_combine`` followed by the output LIF over the T-major fold:

@@ -267,6 +267,19 @@ def test_patch_im2col_matches_unfold(ops, B, C, H, W, p):
     assert torch.equal(a, torch.cat([hi, lo], dim=1))
 
 
+@pytest.mark.parametrize("B,N,d,dtype", [(2048, 256, 48, torch.bfloat16), (37, 19, 8, torch.bfloat16),
+                                         (5, 300, 4, torch.float32), (3, 1, 64, torch.uint8)])
+def test_xnor_n_major_matches_permute(ops, B, N, d, dtype):
+    """The n-major copy of V ([B, N, d] -> [N, B*d]) equals torch's permute
+    bit for bit; rows that are not a multiple of 16 bytes are refused."""
+    g = gen(B + N + d)
+    x = (torch.rand(B, N, d, generator=g) * 200).to(dtype)
+    out = ops.xnor_train_n_major(x.to(DEV)).cpu()
+    assert torch.equal(out, x.permute(1, 0, 2).reshape(N, B * d))
+    with pytest.raises(ValueError):
+        ops.xnor_train_n_major(torch.zeros(2, 3, 5, dtype=torch.bfloat16, device=DEV))
+
+
 def test_patch_embed_split(ops):
     g = gen(3)
     img = torch.rand(3, 1, 32, 64, generator=g)
