@@ -16,9 +16,13 @@ reference modules, oracle/) on the host cores on a bounded sample of the same
 workload; under torchrun only rank 0 runs it.
 
 One JSON line on rank 0: the metric, the device-timed value, the end-to-end
-value through host buffers (e2e), the roofline of the dominant kernel, the CPU
-baseline, the SM clocks sampled during the timed region and the number of
-library kernel launches.
+value through host buffers (e2e), the roofline of the dominant kernel, one
+roofline line per kernel family (the fused GEMM and attention launches of the
+forward, the LIF scan alone), the three kernel families alone at their
+benchmark configurations, the CPU baseline, the SM clocks sampled during the
+timed region and the number of library kernel launches.  The timed region
+only counts launches; per-kernel device times come from further steps with an
+event pair around every launch.
 """
 
 import argparse
@@ -58,6 +62,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="train: run the one-GPU step eagerly")
+    ap.add_argument("--surrogate", default="arctan", choices=["arctan", "superspike"],
+                    help="train: LIF surrogate gradient (arctan alpha 2, the training benchmark's; superspike k 4, "
+                         "the reference trainer's)")
+    ap.add_argument("--no-kernel-configs", action="store_true",
+                    help="forward: skip the standalone LIF / Linear-LN-LIF / attention timings")
     return ap.parse_args()
 
 
@@ -186,9 +195,128 @@ def measured_peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def cpu_threads():
+    """Use every host thread for the CPU legs (the cpu_baseline sample and the
+    reference arm run the same way); returns the count."""
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def peak_for(bound, peaks, peak_src, clocks):
+    """Roofline denominator: measured HBM copy bandwidth, or the bf16 dense
+    GEMM peak in the regime the sampled clocks show (burst when the median SM
+    clock under load stayed within 5% of its maximum, else sustained)."""
+    if bound == "hbm":
+        return peaks["hbm_gbs"], "HBM copy (%s)" % peak_src
+    sm = (clocks or {}).get("sm_mhz")
+    mx = (clocks or {}).get("sm_max_mhz") or peaks.get("sm_max_mhz")
+    if sm is not None and mx and sm >= 0.95 * mx:
+        return peaks["bf16_tflops"], ("bf16 dense, burst (%s): median SM clock %.0f of %.0f MHz in the timed region"
+                                      % (peak_src, sm, mx))
+    return (peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
+            "bf16 dense, sustained (%s): median SM clock %s MHz in the timed region" % (peak_src, sm))
+
+
+def roofline_entry(tag, rec, bound, peaks, peak_src, clocks):
+    """achieved / peak of one launch kind from its recorded device time."""
+    per_launch_s = rec["ms"] / rec["launches"] / 1000.0
+    peak, kind = peak_for(bound, peaks, peak_src, clocks)
+    if bound == "tensor":
+        achieved, unit = rec["flops"] / rec["launches"] / per_launch_s / 1e12, "TFLOP/s"
+    else:
+        achieved, unit = rec["bytes"] / rec["launches"] / per_launch_s / 1e9, "GB/s"
+    return {"kernel": tag, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_kind": kind, "ms_per_launch": per_launch_s * 1000.0, "launches_timed": rec["launches"],
+            "algorithmic_bytes": rec["bytes"] / rec["launches"], "algorithmic_flops": rec["flops"] / rec["launches"]}
+
+
+def config_kernels(dev, peaks, peak_src):
+    """The three kernel families alone at their benchmark configurations,
+    timed with CUDA events on the launching stream (each call after 3 warm-up
+    calls, inputs rotated over copies whose total exceeds the 126 MB L2):
+
+    * LIF scan at the MLP-expand shape of 64 images, [4, 64*256*1536] fp32
+      N(0.5, 1), tau = 2 neuron: forward to packed-bit spikes and to bf16
+      spikes, backward from packed-bit spikes;
+    * fused Linear -> LayerNorm -> LIF, A [4*32*256, 384] Bernoulli(0.15) bf16,
+      W [1536, 384] bf16, bf16 spikes;
+    * attention core + LIF on [4, 32, 8, 256, 48] Bernoulli(0.15) spikes,
+      plain ((Q K^T) V * 0.125) and XNOR forms, and the causal form at N = 64.
+
+    Kernels timed alone: the bf16 peak is the burst figure."""
+    from spikingtransformer_b200 import ops
+    burst = {"sm_mhz": 1.0, "sm_max_mhz": 1.0}
+    out = {}
+
+    def timed(fn, reps):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def add(name, bound, ms, nbytes=0.0, flops=0.0, note=None):
+        rec = {"ms": ms, "launches": 1, "bytes": nbytes, "flops": flops}
+        e = roofline_entry(name, rec, bound, peaks, peak_src, burst)
+        if note:
+            e["note"] = note
+        out[name] = e
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    # ---- LIF scan
+    T, M = 4, 64 * 256 * 1536
+    x = torch.randn(T, M, generator=g, device=dev).add_(0.5)
+    ms = timed(lambda i: ops.lif_fwd(x, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype="bits"), 10)
+    add("lif_fwd [4, 25165824] f32 -> packed-bit spikes", "hbm", ms, T * M * 4 + T * M / 8 + 4 * M)
+    ms = timed(lambda i: ops.lif_fwd(x, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype=torch.bfloat16), 10)
+    add("lif_fwd [4, 25165824] f32 -> bf16 spikes", "hbm", ms, T * M * 6 + 4 * M)
+    sb, _ = ops.lif_fwd(x, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype="bits", want_v_final=False)
+    gs = torch.randn(T, M, generator=g, device=dev)
+    ms = timed(lambda i: ops.lif_bwd(gs, None, x, sb, 0.5, 1.0, 0.0, in_gain=0.5, spikes_packed=True), 10)
+    add("lif_bwd [4, 25165824] f32, packed-bit spikes", "hbm", ms, T * M * 12 + T * M / 8,
+        note="bytes: g_spikes, x and grad_x fp32 plus the packed spikes; the reference also writes and re-reads "
+             "a [T, N] fp32 membrane history")
+    del x, gs, sb
+    # ---- fused Linear -> LayerNorm -> LIF
+    R, K, N = 32 * 256, 384, 1536
+    As = [(torch.rand(T * R, K, generator=g, device=dev) < 0.15).to(torch.bfloat16) for _ in range(6)]
+    W = ((torch.rand(N, K, generator=g, device=dev) * 2 - 1) / math.sqrt(K)).to(torch.bfloat16)
+    bias = (torch.rand(N, generator=g, device=dev) * 2 - 1) * 0.01
+    ones, zeros = torch.ones(N, device=dev), torch.zeros(N, device=dev)
+    ms = timed(lambda i: ops.linear_ln_lif(As[i % 6], W, bias, ones, zeros, 1e-5, 0.5, 1.0, 0.0, T, in_gain=0.5), 20)
+    add("linear_ln_lif [32768, 384] x [384, 1536] -> bf16 spikes", "tensor", ms,
+        nbytes=(T * R * K + N * K) * 2 + T * R * N * 2, flops=2.0 * T * R * K * N)
+    del As
+    # ---- attention core + LIF
+    for Ns, causal, nsets in ((256, False, 3), (64, True, 8)):
+        B, H, dh = 32, 8, 48
+        sets = [tuple((torch.rand(T * B, Ns, H * dh, generator=g, device=dev) < 0.15).to(torch.bfloat16)
+                      for _ in range(3)) for _ in range(nsets)]
+        nbytes = 4.0 * T * B * Ns * H * dh * 2  # q, k, v in, spikes out (bf16)
+        dense = 4.0 * T * B * H * Ns * Ns * dh
+        for variant, scale, vname in ((0, 0.125, "plain"), (1, (1.0 / dh) ** 0.5, "xnor")):
+            ms = timed(lambda i: ops.ssa(*sets[i % nsets], T, B, H, variant, scale, 0.5, 0.5, 0.0, in_gain=0.5,
+                                         causal=causal), 20)
+            name = "ssa %s [4, 32, 8, %d, 48]%s" % (vname, Ns, " causal" if causal else "")
+            add(name, "hbm", ms, nbytes=nbytes, flops=dense,
+                note="%.1f dense-equivalent TFLOP/s (QK^T and SV counted dense)" % (dense / (ms / 1000.0) / 1e12))
+        del sets
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_oracle_rate(target_s=12.0, max_batch=64):
     """Images/s of the CPU oracle forward on a bounded sample (all host threads)."""
     from oracle import modules as om
+    cpu_threads()
     torch.manual_seed(0)
     m = om.Seq2Seq(**ARCH).eval()
     round_weights_bf16(m)
@@ -211,7 +339,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     from oracle import modules as om
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_threads()
     torch.manual_seed(0)
     m = om.Seq2Seq(**ARCH).eval()
     round_weights_bf16(m)
@@ -268,7 +396,9 @@ def run_train(args, ws, rank, local):
     the reference trains under fp16 autocast, train_spikeformer.py:545-555;
     loss = mean over T of CrossEntropyLoss(ignore_index=0, label_smoothing=0.1)
     of each step's logits, train_spikeformer.py:269,309-323, fused with the
-    token accuracy; arctan surrogate, alpha = 2).  Each step generates its
+    token accuracy).  The surrogate is the training benchmark's arctan with
+    alpha = 2, which differs from the reference trainer's SuperSpike with
+    k = 4 (Lif.py:280-282); --surrogate superspike selects that one.  Each step generates its
     batch on the device (images and byte targets from a per-rank, per-step
     seed), so no host data path enters the step."""
     import datetime
@@ -283,7 +413,8 @@ def run_train(args, ws, rank, local):
     torch.manual_seed(0)  # same initial weights on every rank
     model = Seq2Seq(**ARCH)
     round_weights_bf16(model)
-    model.set_surrogate("arctan", 2.0)
+    if args.surrogate == "arctan":
+        model.set_surrogate("arctan", 2.0)
     model = model.to(dev).train()
     # The forward, backward and optimizer step are captured once into a CUDA
     # graph (the host would otherwise spend longer enqueueing the step's ~2,000
@@ -387,7 +518,8 @@ def run_train(args, ws, rank, local):
             "data": "synthetic, generated on the device each step",
             "config": {"workload": "ocr_seq2seq_train_step", "global_batch": ws * B, "per_gpu_batch": B,
                        "seq_len": SEQ, "image": list(IMG), "T": 4, "layers": "8 enc + 4 dec",
-                       "optimizer": "AdamW lr 1e-4", "surrogate": "arctan alpha 2",
+                       "optimizer": "AdamW lr 1e-4",
+                       "surrogate": "arctan alpha 2" if args.surrogate == "arctan" else "superspike k 4",
                        "loss": "mean over T of CE(ignore_index=0, label_smoothing=0.1), fused with token accuracy",
                        "parallelism": ("dp%d (flat fp32 gradient all-reduce over NCCL inside the CUDA graph)" % ws
                                        if flat is not None else "ddp%d (NCCL all-reduce of gradients)" % ws)},
@@ -530,7 +662,8 @@ def main():
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+        # the timed region: only launches counted (no events between kernels)
+        with ClockSampler(local) as clk, _lib.LaunchCounter() as counter:
             e0.record()
             for i in range(args.steps):
                 step(i)
@@ -541,6 +674,13 @@ def main():
         torch.cuda.synchronize()
         ms = max_over_ranks(e0.elapsed_time(e1), dev)
         ops.device_error_check()
+        clocks = clk.summary()
+        # per-kernel device times in a separate pass (an event pair around every launch)
+        n_rec = min(args.steps, 5)
+        with _lib.LaunchRecorder() as rec:
+            for i in range(n_rec):
+                step(i)
+        kernels = rec.summary()
 
         # ---- end to end through the public API: pinned host inputs in, logits out
         e2e = None
@@ -573,24 +713,29 @@ def main():
             e2e = {"value": ws * B * args.steps / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h, "ms_per_step": ems / args.steps}
 
-    kernels = rec.summary()
-    launches = sum(v["launches"] for v in kernels.values())
+    launches = counter.total()
     peaks, peak_src = measured_peaks()
-    # dominant kernel = largest total device time in the timed region
+
+    def bound_of(tag):
+        # the attention kernels are memory-bound (score-free regrouping); the
+        # fused GEMMs are contractions
+        return "tensor" if kernels[tag]["flops"] > 0 and not tag.startswith("ssa") else "hbm"
+
+    # dominant kernel = largest total device time per step
     dom_tag, dom = max(kernels.items(), key=lambda kv: kv[1]["ms"])
-    per_launch_ms = dom["ms"] / dom["launches"]
-    if dom["flops"] > 0:
-        achieved = dom["flops"] / dom["launches"] / (per_launch_ms / 1000.0) / 1e12
-        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-        roof = {"bound": "tensor", "unit": "TFLOP/s", "peak_kind": "bf16 dense, sustained (%s)" % peak_src}
-    else:
-        achieved = dom["bytes"] / dom["launches"] / (per_launch_ms / 1000.0) / 1e9
-        peak = peaks.get("hbm_gbs")
-        roof = {"bound": "hbm", "unit": "GB/s", "peak_kind": "HBM copy (%s)" % peak_src}
-    roof.update({"kernel": dom_tag, "achieved": achieved, "peak": peak, "frac": achieved / peak,
-                 "traffic": NCU_TRAFFIC.get(dom_tag) if B == 256 else None,
-                 "traffic_unit": "bytes per launch (ncu dram read + write)",
-                 "algorithmic_bytes": dom["bytes"] / dom["launches"], "ms_per_launch": per_launch_ms})
+    roof = roofline_entry(dom_tag, dom, bound_of(dom_tag), peaks, peak_src, clocks)
+    roof["traffic"] = NCU_TRAFFIC.get(dom_tag) if B == 256 else None
+    roof["traffic_unit"] = "bytes per launch (ncu dram read + write)"
+    # one line per kernel family: the fused GEMMs and the attention launches of the
+    # forward (from the recorded pass), the LIF scan from its standalone timing
+    by_family = {}
+    for fam, pick in (("linear_ln_lif", lambda t: t.startswith("linear_ln_lif")), ("ssa", lambda t: t.startswith("ssa"))):
+        tags = sorted((t for t in kernels if pick(t)), key=lambda t: -kernels[t]["ms"])
+        by_family[fam] = [roofline_entry(t, kernels[t], bound_of(t), peaks, peak_src, clocks) for t in tags]
+    cfg_kernels = None
+    if rank == 0 and not args.no_kernel_configs:
+        cfg_kernels = config_kernels(dev, peaks, peak_src)
+        by_family["lif"] = [v for k, v in cfg_kernels.items() if k.startswith("lif")]
 
     if rank == 0:
         value = ws * B * args.steps / (ms / 1000.0)
@@ -600,7 +745,7 @@ def main():
             cpu = {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                    "sample": "%d images [1,64,1024], one full 8+4-layer forward of the PyTorch eager oracle "
                              "(fp32), %.1f s" % (nb, dt)}
-        breakdown = {k: {"launches": v["launches"], "ms_per_step": v["ms"] / args.steps,
+        breakdown = {k: {"launches": v["launches"] // n_rec, "ms_per_step": v["ms"] / n_rec,
                          "share": v["ms"] / max(1e-9, sum(x["ms"] for x in kernels.values()))}
                      for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])}
         line = {
@@ -611,8 +756,11 @@ def main():
                        "seq_len": SEQ, "image": list(IMG), "T": 4, "d_model": 384, "heads": 8, "ff_dim": 1536,
                        "layers": "8 enc + 4 dec", "vocab": 256, "parallelism": "dp%d (batch-sharded, no collective)" % ws,
                        "l2": "inputs rotate over 4 sets of 67 MB images (> 126 MB L2); activations per step >> L2"},
-            "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
-            "kernels": breakdown,
+            "e2e": e2e, "roofline": roof, "roofline_by_family": by_family, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": launches, "gpu_launches_per_step": launches // args.steps,
+            "kernels": breakdown, "kernels_note": "per-kernel device times from %d further steps with an event pair "
+                                                  "around every launch (not the timed region)" % n_rec,
+            "kernel_configs": cfg_kernels,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:

@@ -66,6 +66,10 @@ extern "C" {
 #define SPK_F16 1
 #define SPK_BF16 2
 #define SPK_U8 3
+#define SPK_FP8 4 /* fp8 e4m3 (spikes only: 1.0 = 0x38, 0.0 = 0x00)          */
+#define SPK_BIT 5 /* packed bits (spikes only): a [T][N] spike tensor is     */
+                  /* T rows of ceil(N/8) bytes, neuron n at bit n%8 of byte  */
+                  /* n/8; bits past N in a row's last byte are 0            */
 
 /* LIF surrogate gradients */
 #define SPK_SURROGATE_SUPERSPIKE 0 /* 1/(1+k|v-th|)^2, Lif.py:280-282        */
@@ -77,13 +81,21 @@ const char* spk_last_error(void);
 /* Reads (synchronising `stream`) and clears the device-side error flags set
  * by bounded waits in the tensor-core kernels; SPK_ERR_TIMEOUT if any was set. */
 int spk_device_error_check(void* stream);
+/* Self-test of the bounded device-side waits (no counterpart in the
+ * reference): one block waits on an mbarrier that nothing arrives at, through
+ * the wait loop the tensor-core kernels use but with a limit of limit_ns
+ * (at most 1 s) instead of 2 s; the wait gives up, sets the device error flag
+ * and the kernel returns, so the next spk_device_error_check reports
+ * SPK_ERR_TIMEOUT (and clears the flag). */
+int spk_test_bounded_wait(int64_t limit_ns, void* stream);
 
 /*
  * LIF forward scan over T steps (Lif.py:118-165):
  *   v_0 = 0;  v = beta*v + in_gain*x[t];  s[t] = (v > v_th);  v = s[t] ? v_reset : v
  *   v_final = v after the last step.
  * x: [T][N] of x_dtype (F32/F16/BF16), spikes: [T][N] of spike_dtype
- * (F32/BF16/U8, values 0 or 1), v_final: [N] fp32 (may be NULL).
+ * (F32/BF16/U8/FP8, values 0 or 1, or BIT: packed, ceil(N/8) bytes per
+ * step), v_final: [N] fp32 (may be NULL).
  * in_gain == 1 reproduces the reference exactly (two roundings per step).
  */
 int spk_lif_fwd(const void* x, int x_dtype, void* spikes, int spike_dtype, float* v_final,
@@ -93,7 +105,8 @@ int spk_lif_fwd(const void* x, int x_dtype, void* spikes, int spike_dtype, float
 /*
  * LIF backward (Lif.py:221-276) with the membrane history held in registers.
  * g_spikes: [T][N] fp32; g_vfinal: [N] fp32 or NULL; x: [T][N] x_dtype;
- * spikes: [T][N] spike_dtype (from spk_lif_fwd).  grad_x: [T][N] x_dtype.
+ * spikes: [T][N] spike_dtype (from spk_lif_fwd, any of its spike dtypes
+ * including packed bits).  grad_x: [T][N] x_dtype.
  * grad_beta: one fp32 (device), the sum over all neurons (Lif.py:95);
  * may be NULL.  `surrogate_k` is k (SuperSpike) or alpha (arctan).
  * workspace: fp32 scratch of spk_lif_bwd_workspace_bytes(T, N) bytes
@@ -120,7 +133,10 @@ int spk_lif_bwd(const float* g_spikes, const float* g_vfinal, const void* x, int
  * need more is rejected with SPK_ERR_SHAPE; T > 64 is rejected as in
  * spk_lif_bwd).  The first call on a device, with that device current, looks
  * up the array's address (cudaGetSymbolAddress); make that first call before
- * any stream capture.  All calls on a device share the array: calls whose
+ * any stream capture.  The address stays cached for the life of the
+ * process: after cudaDeviceReset on a device the module may load elsewhere,
+ * so do not call this entry point on that device again.  All calls on a
+ * device share the array: calls whose
  * kernels overlap on the GPU (unordered streams) race and must be serialised
  * by the caller.  No cudaMalloc, cudaFree or allocating library routine is
  * called.

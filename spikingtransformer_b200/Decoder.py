@@ -5,13 +5,24 @@
 ``Decoder``: ``num_layers`` of them (``:28-43``).
 """
 
-import torch
 import torch.nn as nn
 
-from ._fused import fast_path_ok
-from .Encoder import bf16_exact
+from ._fused import fast_path_ok, spike_counts_bf16
+from .Encoder import stream_copy_bf16, stream_out
 from .SSA import SSAMultiHeadAttention
 from .SpikingMLP import SpikingMLP
+
+
+def _fast_inputs(module, x, enc_output, mask):
+    """(private bf16 copy of x, bf16 encoder output) for the fused path, or
+    (None, None) when either may not be exact in bf16."""
+    if not fast_path_ok(x, enc_output, mask, module=module):
+        return None, None
+    enc = spike_counts_bf16(enc_output)
+    if enc is None:
+        return None, None
+    xb = stream_copy_bf16(x)
+    return (xb, enc.contiguous()) if xb is not None else (None, None)
 
 
 class DecoderLayer(nn.Module):
@@ -32,9 +43,9 @@ class DecoderLayer(nn.Module):
         return x
 
     def forward(self, x, enc_output, mask=None):
-        if fast_path_ok(x, enc_output, mask, module=self) and bf16_exact(x) and bf16_exact(enc_output):
-            enc = enc_output.to(torch.bfloat16).contiguous()
-            return self._fast(x.to(torch.bfloat16).contiguous(), enc, mask).to(x.dtype)
+        xb, enc = _fast_inputs(self, x, enc_output, mask)
+        if xb is not None:
+            return stream_out(self._fast(xb, enc, mask), x)
         x = x + self.self_attns(x, x, x, attention_mask=mask)
         x = x + self.cross_attns(x, enc_output, enc_output)
         return x + self.mlp(x)
@@ -57,9 +68,9 @@ class Decoder(nn.Module):
         return x
 
     def forward(self, x, enc_output, mask=None):
-        if fast_path_ok(x, enc_output, mask, module=self) and bf16_exact(x) and bf16_exact(enc_output):
-            enc = enc_output.to(torch.bfloat16).contiguous()
-            return self._fast(x.to(torch.bfloat16).contiguous(), enc, mask).to(x.dtype)
+        xb, enc = _fast_inputs(self, x, enc_output, mask)
+        if xb is not None:
+            return stream_out(self._fast(xb, enc, mask), x)
         for layer in self.layers:
             x = layer(x, enc_output, mask=mask)
         return x

@@ -5,23 +5,33 @@
 
 Inference keeps the residual stream as bf16 spike counts (exact: the stream
 is a sum of spikes) and the fused kernels add each block's output spikes into
-it in place.  A stream that is not exactly representable in bf16 takes the
-per-module path with an fp32 residual instead.
+a copy of it in place.  The stream takes that path when it is bf16 or was
+produced by this package's spiking modules (known without reading it back to
+the host); any other stream takes the per-module path with an fp32 residual.
 """
 
 import torch
 import torch.nn as nn
 
-from ._fused import fast_path_ok
+from ._fused import fast_path_ok, mark_spike_counts, spike_counts_bf16
 from .SSA import SSAMultiHeadAttention
 from .SpikingMLP import SpikingMLP
 
 
-def bf16_exact(x):
-    """True if every element of ``x`` is exactly representable in bf16."""
-    if x.dtype == torch.bfloat16:
-        return True
-    return bool(torch.equal(x.to(torch.bfloat16).to(x.dtype), x))
+def stream_copy_bf16(x):
+    """A private contiguous bf16 copy of the residual stream ``x`` for the
+    in-place fused path, or None when ``x`` may not be exact in bf16."""
+    xb = spike_counts_bf16(x)
+    if xb is None:
+        return None
+    return xb.clone(memory_format=torch.contiguous_format)
+
+
+def stream_out(out_bf16, like):
+    """The fused path's result in the caller's dtype, marked as spike counts."""
+    if like.dtype == torch.bfloat16:
+        return out_bf16
+    return mark_spike_counts(out_bf16.to(like.dtype), out_bf16)
 
 
 class EncoderLayer(nn.Module):
@@ -38,9 +48,9 @@ class EncoderLayer(nn.Module):
         return x
 
     def forward(self, x, mask=None):
-        if fast_path_ok(x, mask, module=self) and bf16_exact(x):
-            out = self._fast(x.to(torch.bfloat16).contiguous(), mask)
-            return out.to(x.dtype)
+        xb = stream_copy_bf16(x) if fast_path_ok(x, mask, module=self) else None
+        if xb is not None:
+            return stream_out(self._fast(xb, mask), x)
         x = x + self.self_attns(x, x, x, attention_mask=mask)
         return x + self.mlp(x)
 
@@ -58,8 +68,9 @@ class Encoder(nn.Module):
         return x
 
     def forward(self, x, mask=None):
-        if fast_path_ok(x, mask, module=self) and bf16_exact(x):
-            return self._fast(x.to(torch.bfloat16).contiguous(), mask).to(x.dtype)
+        xb = stream_copy_bf16(x) if fast_path_ok(x, mask, module=self) else None
+        if xb is not None:
+            return stream_out(self._fast(xb, mask), x)
         for layer in self.layers:
             x = layer(x, mask=mask)
         return x

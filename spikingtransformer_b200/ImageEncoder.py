@@ -14,7 +14,7 @@ import torch
 from torch import nn
 
 from . import ops
-from ._fused import bf16_weight, fast_path_ok, lif_params, ln_lif
+from ._fused import bf16_weight, fast_path_ok, lif_params, ln_lif, mark_spike_counts
 from .Lif import LIF
 
 
@@ -101,6 +101,8 @@ class CNNBackbone(nn.Module):
         x = self.reduce(x)
         rpe_value = self.rpe(x)
         x = (x + rpe_value).transpose(-1, -2)
+        if not x.requires_grad:
+            mark_spike_counts(x)  # sums of two spike trains
         record["RPE2D"] = rpe_value
         record["output"] = x
         return x, record
@@ -149,7 +151,8 @@ class PatchEmbed(nn.Module):
 
     def forward(self, x):
         if fast_path_ok(x, module=self):
-            s = self._fused(x, t_broadcast=False).float()
+            sb = self._fused(x, t_broadcast=False)
+            s = mark_spike_counts(sb.float(), sb)
             return s, {"output": s}
         if self._tiles(x):
             # conv bias handed to the LayerNorm->LIF kernels

@@ -22,6 +22,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
+from ._fused import mark_spike_counts
 
 
 class LIFLayer(torch.autograd.Function):
@@ -39,11 +40,12 @@ class LIFLayer(torch.autograd.Function):
             raise RuntimeError("LIFLayer expects [T, B, F], got %s" % (tuple(input_current.shape),))
         x = input_current.contiguous()
         spikes, v_final = ops.lif_fwd(x, beta, v_th, v_reset, in_gain, torch.float32)
-        k = float(k_superspike) if not isinstance(k_superspike, torch.Tensor) else float(k_superspike.item())
         ctx.save_for_backward(x, spikes, beta if isinstance(beta, torch.Tensor) else torch.tensor(float(beta)),
                               v_th if isinstance(v_th, torch.Tensor) else torch.tensor(float(v_th)),
                               v_reset if isinstance(v_reset, torch.Tensor) else torch.tensor(float(v_reset)))
-        ctx.k = k
+        # a tensor k (the reference's LIF module passes a host float) is read
+        # back only if the backward runs, never in the forward
+        ctx.k = k_superspike
         ctx.surrogate = surrogate
         ctx.in_gain = float(in_gain)
         ctx.mark_non_differentiable(v_final)
@@ -53,8 +55,9 @@ class LIFLayer(torch.autograd.Function):
     def backward(ctx, grad_output_spikes, grad_v_mem_final):
         x, spikes, beta, v_th, v_reset = ctx.saved_tensors
         need_beta = ctx.needs_input_grad[1]
+        k = float(ctx.k)
         gx, gb = ops.lif_bwd(grad_output_spikes, grad_v_mem_final, x, spikes, beta, v_th, v_reset,
-                             ctx.in_gain, ctx.surrogate, ctx.k, need_beta_grad=need_beta)
+                             ctx.in_gain, ctx.surrogate, k, need_beta_grad=need_beta)
         if gb is not None:
             gb = gb.reshape(beta.shape).to(beta.dtype)
         return gx, gb, None, None, None, None, None
@@ -138,6 +141,8 @@ class LIF(nn.Module):
                                          self.surrogate, self.in_gain)
         spikes = spikes.view(shape)
         v_final = v_final.view(shape[0] // self.n_steps, *shape[1:])
+        if not spikes.requires_grad:
+            mark_spike_counts(spikes)
         return spikes, v_final
 
     def extra_repr(self) -> str:

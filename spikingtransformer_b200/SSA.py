@@ -15,14 +15,14 @@ the LIF kernels of this package, so autograd sees the same graph as the
 reference.
 """
 
-import math
 from typing import Optional
 
 import torch
 import torch.nn as nn
 
 from . import ops
-from ._fused import bf16_input, fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train, qkv_ln_lif_train
+from ._fused import (bf16_input, fast_path_ok, lif_params, lin_ln_lif, lin_ln_lif_train, mark_spike_counts,
+                     qkv_ln_lif_train)
 from .Lif import LIF
 
 
@@ -100,7 +100,7 @@ class _SSACore(nn.Module):
         v = lin_ln_lif(value, self.v_proj, self.lnv, self.lifv, T)[0].view(TB, Nk, D)
         a = self._attend(q, k, v, T, attention_mask)
         out = lin_ln_lif(a, self.out_proj, self.lno, self.lifo, T, spike_dtype=torch.float32)[0]
-        return out.view(TB, N, D)
+        return mark_spike_counts(out.view(TB, N, D))
 
     # ---------------------------------------------------------------- autograd path
 
@@ -424,5 +424,3 @@ class SSAMultiHeadAttention_(_SSACore):
             a = a * mask
         return _token_major((a @ v) * 0.125)
 
-
-_ = math  # kept for parity with the reference module namespace

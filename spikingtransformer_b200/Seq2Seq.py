@@ -23,9 +23,9 @@ import torch.nn as nn
 from torch import Tensor
 
 from . import ops
-from ._fused import bf16_weight, fast_path_ok, lif_params
+from ._fused import bf16_weight, fast_path_ok, lif_params, mark_spike_counts, spike_counts_bf16
 from .Decoder import Decoder
-from .Encoder import Encoder, bf16_exact
+from .Encoder import Encoder
 from .ImageEncoder import CNNBackbone, PatchEmbed
 from .Lif import LIF
 
@@ -137,7 +137,8 @@ class Seq2Seq(nn.Module):
 
     def encode(self, src: Tensor):
         if self._fast_ok(src):
-            return self._encode_fast(src).float(), None
+            enc = self._encode_fast(src)
+            return mark_spike_counts(enc.float(), enc), None
         B = src.shape[0]
         T = self.n_steps
         if isinstance(self.image_encoder, PatchEmbed):
@@ -149,9 +150,9 @@ class Seq2Seq(nn.Module):
 
     def decode(self, tgt: Tensor, enc_output: Tensor, look_ahead_mask: Tensor = None,
                enc_padding_mask: Tensor = None, dec_padding_mask: Tensor = None):
-        if self._fast_ok(tgt, enc_output, look_ahead_mask) and bf16_exact(enc_output):
-            enc = enc_output.to(torch.bfloat16).contiguous()
-            return self._decode_fast(tgt, enc, look_ahead_mask), None
+        enc = spike_counts_bf16(enc_output) if self._fast_ok(tgt, enc_output, look_ahead_mask) else None
+        if enc is not None:
+            return self._decode_fast(tgt, enc.contiguous(), look_ahead_mask), None
         T = self.n_steps
         if look_ahead_mask is not None:
             m = look_ahead_mask

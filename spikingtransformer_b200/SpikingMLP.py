@@ -12,7 +12,7 @@ bf16 and never pass through fp32.
 import torch.nn as nn
 import torch
 
-from ._fused import fast_path_ok, lin_ln_lif, lin_ln_lif_train
+from ._fused import fast_path_ok, lin_ln_lif, lin_ln_lif_train, mark_spike_counts
 from .Lif import LIF
 
 
@@ -41,7 +41,7 @@ class SpikingMLP(nn.Module):
             T = self.lifexpand.n_steps
             h = lin_ln_lif(x, self.expand, self.bn_expand, self.lifexpand, T)[0]
             y = lin_ln_lif(h, self.compress, self.bn_compress, self.lifcompress, T, spike_dtype=torch.float32)[0]
-            return y.view(*x.shape[:-1], y.shape[-1])
+            return mark_spike_counts(y.view(*x.shape[:-1], y.shape[-1]))
         # the hidden spikes feed only the compress GEMM: autocast dtype under autocast
         h = lin_ln_lif_train(x, self.expand, self.bn_expand, self.lifexpand, narrow=True)
         return lin_ln_lif_train(h, self.compress, self.bn_compress, self.lifcompress)

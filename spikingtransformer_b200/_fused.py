@@ -6,6 +6,8 @@ source tensor's storage pointer and version counter, so an optimizer step or
 ``load_state_dict`` invalidates them without a host synchronisation.
 """
 
+import weakref
+
 import torch
 
 from . import ops
@@ -72,6 +74,39 @@ def lin_ln_lif(x, lin, ln, lif, T, t_broadcast=False, residual=None, spike_dtype
     return ops.linear_ln_lif(A.reshape(-1, K), W, lin.bias, ln.weight, ln.bias, ln.eps, p[0:1], p[1:2], p[2:3], T,
                              in_gain=lif.in_gain, t_broadcast=t_broadcast, spike_dtype=spike_dtype,
                              residual=residual, want_spikes=want_spikes, want_ln_out=want_ln_out)
+
+
+_SPIKE_COUNTS = {}
+
+
+def mark_spike_counts(t, bf16=None):
+    """Record that ``t`` holds spike counts (small non-negative integers, exact
+    in bf16), with its bf16 copy if one exists; returns ``t``.  The record
+    lasts while ``t`` lives and is ignored once ``t`` is modified in place."""
+    key = id(t)
+
+    def drop(_ref, key=key):
+        entry = _SPIKE_COUNTS.get(key)
+        if entry is not None and entry[0] is _ref:
+            del _SPIKE_COUNTS[key]
+
+    _SPIKE_COUNTS[key] = (weakref.ref(t, drop), t._version, bf16)
+    return t
+
+
+def spike_counts_bf16(t):
+    """The bf16 form of a residual-stream tensor without a host
+    synchronisation: ``t`` when it is bf16, the recorded copy (or a cast) when
+    ``t`` was produced by this package's spiking modules and has not been
+    modified since; None when exactness cannot be known without reading ``t``
+    back (the caller then takes the per-module path, which works on any
+    values)."""
+    if t.dtype == torch.bfloat16:
+        return t
+    entry = _SPIKE_COUNTS.get(id(t))
+    if entry is None or entry[0]() is not t or entry[1] != t._version:
+        return None
+    return entry[2] if entry[2] is not None else t.to(torch.bfloat16)
 
 
 def fast_path_ok(*tensors, module=None):

@@ -15,8 +15,9 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libspk.so")
 HEADER = os.path.join(os.path.dirname(PKG), "include", "spk.h")
 
-F32, F16, BF16, U8 = 0, 1, 2, 3
-DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.uint8: U8}
+F32, F16, BF16, U8, FP8, BIT = 0, 1, 2, 3, 4, 5
+DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.uint8: U8,
+              torch.float8_e4m3fn: FP8}
 
 SURROGATE = {"superspike": 0, "arctan": 1}
 
@@ -31,6 +32,7 @@ SIGNATURES = {
     "spk_status_string": ([_i], ctypes.c_char_p),
     "spk_last_error": ([], ctypes.c_char_p),
     "spk_device_error_check": ([_p], _i),
+    "spk_test_bounded_wait": ([_i64, _p], _i),
     "spk_lif_fwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _f, _i64, _i64, _p], _i),
     "spk_lif_bwd_workspace_bytes": ([_i64, _i64], _i64),
     "spk_lif_bwd": ([_p, _p, _p, _i, _p, _i, _p, _p, _p, _f, _i, _f, _p, _p, _p, _i64, _i64, _i64, _p], _i),

@@ -117,6 +117,22 @@ int make_tmap_bf16_sw(CUtensorMap* map, const void* base, int rank, const uint64
   return SPK_OK;
 }
 
+// ---- self-test of the bounded wait
+// One thread waits on a freshly initialised mbarrier that nothing arrives at,
+// through the same mbar_wait_for loop the tensor-core pipelines use, with a
+// short limit: the wait gives up, records `code` in this file's device error
+// flag and the kernel returns.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, int code) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait_for(&bar, 0, code, limit_ns);
+  }
+}
+
+SPK_DEFINE_ERROR_READER(capi_read_device_error)
+
 // Per-file device error readers (defined in the kernel files that spin-wait).
 int gemm_read_device_error(cudaStream_t);
 int gemm_il_read_device_error(cudaStream_t);
@@ -124,8 +140,10 @@ int ssa_read_device_error(cudaStream_t);
 int ssa_lin_read_device_error(cudaStream_t);
 int ssa_short_read_device_error(cudaStream_t);
 typedef int (*ErrorReader)(cudaStream_t);
-static ErrorReader g_error_readers[] = {gemm_read_device_error, gemm_il_read_device_error, ssa_read_device_error,
-                                        ssa_lin_read_device_error, ssa_short_read_device_error, nullptr};
+static ErrorReader g_error_readers[] = {gemm_read_device_error,     gemm_il_read_device_error,
+                                        ssa_read_device_error,      ssa_lin_read_device_error,
+                                        ssa_short_read_device_error, capi_read_device_error,
+                                        nullptr};
 
 }  // namespace spk
 
@@ -157,6 +175,16 @@ int spk_device_error_check(void* stream) {
     if (r != SPK_OK) rc = r;
   }
   return rc;
+}
+
+int spk_test_bounded_wait(int64_t limit_ns, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(limit_ns > 0 && limit_ns <= 1000000000ll, SPK_ERR_INVALID, "limit %lld ns outside (0, 1 s]",
+              (long long)limit_ns);
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  bounded_wait_probe_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)limit_ns, 9);
+  return check_launch("bounded_wait_probe_kernel");
 }
 
 }  // extern "C"

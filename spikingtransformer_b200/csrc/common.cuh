@@ -34,6 +34,7 @@ inline int dtype_size(int dt) {
     case SPK_F16: return 2;
     case SPK_BF16: return 2;
     case SPK_U8: return 1;
+    case SPK_FP8: return 1;
     default: return 0;
   }
 }
@@ -81,6 +82,14 @@ template <> struct Elem<SPK_U8> {
   using T = uint8_t;
   __device__ static float load(const T* p) { return (float)(*p); }
   __device__ static T make(float v) { return (uint8_t)(v != 0.0f); }
+};
+// fp8 e4m3 spikes: 1.0 is the byte 0x38 (exponent 7 = bias, mantissa 0), 0.0
+// the byte 0; spike tensors hold nothing else, so any non-zero magnitude
+// byte reads as 1.
+template <> struct Elem<SPK_FP8> {
+  using T = uint8_t;
+  __device__ static float load(const T* p) { return (*p & 0x7f) ? 1.0f : 0.0f; }
+  __device__ static T make(float v) { return v != 0.0f ? (uint8_t)0x38 : (uint8_t)0; }
 };
 
 // ---------------------------------------------------------------- PTX: sync
@@ -135,16 +144,20 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code = 1) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+    if ((i & 255u) == 0 && global_ns() - t0 > limit_ns) {
       atomicExch(&g_spk_device_error, code);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code = 1) {
+  return mbar_wait_for(bar, parity, code, kWaitLimitNs);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

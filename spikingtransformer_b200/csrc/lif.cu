@@ -90,6 +90,76 @@ __global__ void __launch_bounds__(256) lif_fwd_kernel(const void* __restrict__ x
   }
 }
 
+// Packed-bit spikes: thread g owns neurons [8g, 8g + 8) and writes one byte
+// per step, bit i for neuron 8g + i, into rows of ceil(N/8) bytes; a warp's
+// stores cover 32 consecutive bytes.  `vec`: N % 8 == 0 and x aligned for
+// 8-element vector loads; otherwise elements are loaded one by one with a
+// bound on the last group.
+template <int XDT>
+__global__ void __launch_bounds__(256) lif_fwd_bits_kernel(const void* __restrict__ x, uint8_t* __restrict__ spikes,
+                                                           float* __restrict__ v_final, const float* pbeta,
+                                                           const float* pvth, const float* pvr, float gain, int T,
+                                                           int64_t N, bool vec) {
+  using XT = typename Elem<XDT>::T;
+  const float beta = __ldg(pbeta), vth = __ldg(pvth), vr = __ldg(pvr);
+  const bool use_gain = gain != 1.0f;
+  const int64_t NB = (N + 7) / 8;
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < NB; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = g * 8;
+    const int n = N - col < 8 ? (int)(N - col) : 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    for (int t = 0; t < T; ++t) {
+      float xv[8];
+      if (vec) {
+        load_vec<XDT, 8>(x, (int64_t)t * N + col, xv);
+      } else {
+        const XT* row = reinterpret_cast<const XT*>(x) + (int64_t)t * N + col;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = i < n ? Elem<XDT>::load(row + i) : 0.0f;
+      }
+      uint32_t bits = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float cur = use_gain ? __fmul_rn(xv[i], gain) : xv[i];
+        float u = __fadd_rn(__fmul_rn(v[i], beta), cur);
+        bool s = u > vth && i < n;
+        bits |= (s ? 1u : 0u) << i;
+        v[i] = s ? vr : u;
+      }
+      spikes[(int64_t)t * NB + g] = (uint8_t)bits;
+    }
+    if (v_final) {
+      if (vec) {
+        store_vec<SPK_F32, 8>(v_final, col, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < n) v_final[col + i] = v[i];
+      }
+    }
+  }
+}
+
+// Spike bits of neurons [col, col + VEC) at step t (bit i = neuron col + i).
+template <int SDT, int VEC>
+__device__ __forceinline__ uint32_t load_spike_bits(const void* spikes, int t, int64_t N, int64_t col) {
+  if constexpr (SDT == SPK_BIT) {
+    static_assert(VEC == 1 || VEC == 4, "packed bits are read 1 or 4 at a time");
+    const uint8_t* row = reinterpret_cast<const uint8_t*>(spikes) + (int64_t)t * ((N + 7) / 8);
+    const uint32_t byte = __ldg(row + (col >> 3));
+    return (byte >> (col & 7)) & ((1u << VEC) - 1u);
+  } else {
+    float sv[VEC];
+    load_vec<SDT, VEC>(spikes, (int64_t)t * N + col, sv);
+    uint32_t bits = 0;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) bits |= (sv[i] > 0.0f ? 1u : 0u) << i;
+    return bits;
+  }
+}
+
 __device__ __forceinline__ float surrogate(int kind, float u, float k, float c_arctan) {
   if (kind == SPK_SURROGATE_SUPERSPIKE) {
     float a = __fadd_rn(1.0f, __fmul_rn(k, fabsf(u)));
@@ -123,18 +193,15 @@ __global__ void __launch_bounds__(kBwdThreads) lif_bwd_kernel(
 #pragma unroll
     for (int t = 0; t < TMAX; ++t) {
       if (t < T) {
-        float xv[VEC], sv[VEC];
+        float xv[VEC];
         load_vec<XDT, VEC>(x, (int64_t)t * N + col, xv);
-        load_vec<SDT, VEC>(spikes, (int64_t)t * N + col, sv);
-        uint32_t bits = 0;
+        const uint32_t bits = load_spike_bits<SDT, VEC>(spikes, t, N, col);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
           float cur = use_gain ? __fmul_rn(xv[i], gain) : xv[i];
           float u = __fadd_rn(__fmul_rn(v[i], beta), cur);
           vh[t][i] = u;
-          bool s = sv[i] > 0.0f;
-          bits |= (s ? 1u : 0u) << i;
-          v[i] = s ? vr : u;
+          v[i] = ((bits >> i) & 1u) ? vr : u;
         }
         sbits[t] = bits;
       }
@@ -235,6 +302,13 @@ int dispatch_fwd_s(int sdt, bool vec, const void* x, void* s, float* vf, const f
     case SPK_F32: dispatch_fwd_vec<XDT, SPK_F32>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
     case SPK_BF16: dispatch_fwd_vec<XDT, SPK_BF16>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
     case SPK_U8: dispatch_fwd_vec<XDT, SPK_U8>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
+    case SPK_FP8: dispatch_fwd_vec<XDT, SPK_FP8>(vec, x, s, vf, b, th, vr, gain, T, N, st); return SPK_OK;
+    case SPK_BIT: {
+      int grid = grid_for((N + 7) / 8, 256);
+      lif_fwd_bits_kernel<XDT><<<grid, 256, 0, st>>>(x, reinterpret_cast<uint8_t*>(s), vf, b, th, vr, gain, T, N,
+                                                     vec);
+      return SPK_OK;
+    }
     default: return fail(SPK_ERR_INVALID, "spike dtype %d not supported", sdt);
   }
 }
@@ -274,6 +348,10 @@ int dispatch_bwd_s(int sdt, int T, bool vec, int grid, const float* gs, const fl
       return dispatch_bwd_t<XDT, SPK_BF16>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
     case SPK_U8:
       return dispatch_bwd_t<XDT, SPK_U8>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
+    case SPK_FP8:
+      return dispatch_bwd_t<XDT, SPK_FP8>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
+    case SPK_BIT:
+      return dispatch_bwd_t<XDT, SPK_BIT>(T, vec, grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, N, st);
     default: return fail(SPK_ERR_INVALID, "spike dtype %d not supported", sdt);
   }
 }
@@ -302,7 +380,8 @@ int lif_bwd_impl(const float* g_spikes, const float* g_vfinal, const void* x, in
                  int64_t T, int64_t N, cudaStream_t st) {
   // the vector path needs N % 4 == 0 and 16-byte aligned rows for fp32 tensors
   bool vec = T <= 16 && (N % 4 == 0) && aligned(g_spikes, 16) && (!g_vfinal || aligned(g_vfinal, 16)) &&
-             aligned(x, 4 * dtype_size(x_dtype)) && aligned(spikes, 4 * dtype_size(spike_dtype)) &&
+             aligned(x, 4 * dtype_size(x_dtype)) &&
+             (spike_dtype == SPK_BIT || aligned(spikes, 4 * dtype_size(spike_dtype))) &&
              aligned(grad_x, 4 * dtype_size(x_dtype));
   int64_t groups = vec ? N / 4 : N;
   int grid = grid_for(groups, kBwdThreads);
@@ -340,12 +419,13 @@ static int check_lif_args(const void* x, int x_dtype, const void* spikes, int sp
   SPK_REQUIRE(beta && v_th && v_reset, SPK_ERR_INVALID, "null pointer argument");
   SPK_REQUIRE(x_dtype == SPK_F32 || x_dtype == SPK_F16 || x_dtype == SPK_BF16, SPK_ERR_INVALID,
               "x dtype %d not supported", x_dtype);
-  SPK_REQUIRE(spike_dtype == SPK_F32 || spike_dtype == SPK_BF16 || spike_dtype == SPK_U8, SPK_ERR_INVALID,
-              "spike dtype %d not supported", spike_dtype);
+  SPK_REQUIRE(spike_dtype == SPK_F32 || spike_dtype == SPK_BF16 || spike_dtype == SPK_U8 ||
+                  spike_dtype == SPK_FP8 || spike_dtype == SPK_BIT,
+              SPK_ERR_INVALID, "spike dtype %d not supported", spike_dtype);
   SPK_REQUIRE(T >= 1 && T <= 64, SPK_ERR_SHAPE, "T=%lld outside [1, 64]", (long long)T);
   SPK_REQUIRE(N >= 0, SPK_ERR_SHAPE, "N=%lld negative", (long long)N);
-  SPK_REQUIRE(aligned(x, dtype_size(x_dtype)) && aligned(spikes, dtype_size(spike_dtype)), SPK_ERR_ALIGN,
-              "x / spikes not aligned to their element size");
+  SPK_REQUIRE(aligned(x, dtype_size(x_dtype)) && (spike_dtype == SPK_BIT || aligned(spikes, dtype_size(spike_dtype))),
+              SPK_ERR_ALIGN, "x / spikes not aligned to their element size");
   return SPK_OK;
 }
 
@@ -415,7 +495,8 @@ int spk_lif_fwd(const void* x, int x_dtype, void* spikes, int spike_dtype, float
   if (N == 0) return SPK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool vec = (N % 8 == 0) && aligned(x, 8 * dtype_size(x_dtype)) &&
-                   aligned(spikes, 8 * dtype_size(spike_dtype)) && (!v_final || aligned(v_final, 32));
+                   (spike_dtype == SPK_BIT || aligned(spikes, 8 * dtype_size(spike_dtype))) &&
+                   (!v_final || aligned(v_final, 32));
   switch (x_dtype) {
     case SPK_F32: rc = dispatch_fwd_s<SPK_F32>(spike_dtype, vec, x, spikes, v_final, beta, v_th, v_reset, in_gain, (int)T, N, st); break;
     case SPK_F16: rc = dispatch_fwd_s<SPK_F16>(spike_dtype, vec, x, spikes, v_final, beta, v_th, v_reset, in_gain, (int)T, N, st); break;

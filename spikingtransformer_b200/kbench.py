@@ -2,8 +2,9 @@
 
     python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|data|shapes|lnlif] [--iters N]
 
-  lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 spikes (the MLP
-        expansion LIF of a 64-image batch); bound: HBM bytes.
+  lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 and packed-bit
+        spikes (the MLP expansion LIF of a 64-image batch), and the backward
+        from packed bits; bound: HBM bytes.
   gemm  fused Linear(384->1536) -> LayerNorm -> LIF on A [4*32*256, 384]
         Bernoulli(0.15) spikes (bf16), tau=2 neuron; bound: bf16 tensor FLOPs.
   ssa   spiking attention on Q, K, V [T=4, B=32, H=8, N=256, d=48]
@@ -53,13 +54,26 @@ def _time(fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters
 
 
-def bench_lif(iters):
-    T, N = 4, 64 * 256 * 1536
+def bench_lif(iters, N=64 * 256 * 1536):
+    """Forward to bf16 and to packed-bit spikes, and the backward from packed
+    bits, on [4, N] fp32 N(0.5, 1) currents (tau = 2 neuron)."""
+    T = 4
     copies = 2
     xs = [torch.randn(T, N, device="cuda") + 0.5 for _ in range(copies)]
-    ms = _time(lambda i: ops.lif_fwd(xs[i % copies], 0.9, 1.0, 0.0, spike_dtype=torch.bfloat16), iters)
-    nbytes = T * N * (4 + 2) + 4 * N
-    return {"kernel": "lif_fwd", "shape": [T, N], "ms": ms, "GB/s": nbytes / ms / 1e6, "bytes": nbytes}
+    res = []
+    for fmt, sbytes in ((torch.bfloat16, 2 * T * N), ("bits", T * ((N + 7) // 8))):
+        ms = _time(lambda i: ops.lif_fwd(xs[i % copies], 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype=fmt), iters)
+        nbytes = T * N * 4 + sbytes + 4 * N
+        res.append({"kernel": "lif_fwd", "spikes": str(fmt), "shape": [T, N], "ms": ms, "GB/s": nbytes / ms / 1e6,
+                    "bytes": nbytes})
+    sb = [ops.lif_fwd(x, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype="bits", want_v_final=False)[0] for x in xs]
+    gs = torch.randn(T, N, device="cuda")
+    ms = _time(lambda i: ops.lif_bwd(gs, None, xs[i % copies], sb[i % copies], 0.5, 1.0, 0.0, in_gain=0.5,
+                                     spikes_packed=True), iters)
+    nbytes = T * N * 12 + T * ((N + 7) // 8)
+    res.append({"kernel": "lif_bwd", "spikes": "bits", "shape": [T, N], "ms": ms, "GB/s": nbytes / ms / 1e6,
+                "bytes": nbytes})
+    return res
 
 
 def bench_gemm(iters, N=1536, K=384, T=4, R=32 * 256):
@@ -207,6 +221,7 @@ def main():
     ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "data", "shapes", "lnlif"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
+    ap.add_argument("--lif-neurons", type=int, default=64 * 256 * 1536, help="neurons per step for the LIF scan")
     a = ap.parse_args()
     if a.only == "shapes":
         bench_shapes_once()
@@ -217,9 +232,9 @@ def main():
     out = {"peaks": {"hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops_sustained": peaks.get("bf16_tflops_sustained"),
                      "source": src}, "results": []}
     if a.only in (None, "lif"):
-        r = bench_lif(a.iters)
-        r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
-        out["results"].append(r)
+        for r in bench_lif(a.iters, N=a.lif_neurons):
+            r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
+            out["results"].append(r)
     if a.only in (None, "gemm"):
         for n, k in ((1536, 384), (384, 384), (384, 1536)):
             r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)

@@ -29,27 +29,44 @@ def _scalar_f32(v, device):
 def lif_fwd(x, beta, v_th, v_reset, in_gain=1.0, spike_dtype=torch.float32, want_v_final=True):
     """LIF scan over dim 0 of ``x`` ([T, ...]); returns ``(spikes, v_final)``.
 
-    ``x`` may be fp32/fp16/bf16; spikes are ``spike_dtype`` (fp32, bf16 or
-    uint8); ``v_final`` is fp32 shaped like ``x[0]`` (or None).
+    ``x`` may be fp32/fp16/bf16; spikes are ``spike_dtype`` (fp32, bf16,
+    uint8 or float8_e4m3fn, shaped like ``x``) or ``"bits"``: packed bits,
+    uint8 ``[T, ceil(N/8)]`` with neuron n of step t at bit n % 8 of byte
+    ``[t, n // 8]`` (N = ``x[0].numel()``); ``v_final`` is fp32 shaped like
+    ``x[0]`` (or None).
     """
     _cuda(x)
     x = x.contiguous()
     T = x.shape[0]
     N = x[0].numel()
     dev = x.device
-    s = torch.empty(x.shape, dtype=spike_dtype, device=dev)
+    if spike_dtype == "bits":
+        s = torch.empty((T, (N + 7) // 8), dtype=torch.uint8, device=dev)
+        code, out_bytes = _lib.BIT, s.numel()
+    else:
+        s = torch.empty(x.shape, dtype=spike_dtype, device=dev)
+        code, out_bytes = _lib.dtype_code(s), s.numel() * s.element_size()
     vf = torch.empty(x.shape[1:], dtype=torch.float32, device=dev) if want_v_final else None
     b, th, vr = (_scalar_f32(v, dev) for v in (beta, v_th, v_reset))
-    nbytes = T * N * (x.element_size() + s.element_size()) + (4 * N if vf is not None else 0)
-    _lib.call("spk_lif_fwd", _lib.ptr(x), _lib.dtype_code(x), _lib.ptr(s), _lib.dtype_code(s), _lib.ptr(vf),
+    nbytes = T * N * x.element_size() + out_bytes + (4 * N if vf is not None else 0)
+    _lib.call("spk_lif_fwd", _lib.ptr(x), _lib.dtype_code(x), _lib.ptr(s), code, _lib.ptr(vf),
               _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, N, _lib.stream_ptr(dev),
               tag="lif_fwd", work=dict(bytes=nbytes))
     return s, vf
 
 
+def unpack_spike_bits(bits, N):
+    """Packed spike bits ``[T, ceil(N/8)]`` (``lif_fwd(..., spike_dtype="bits")``)
+    -> float 0/1 ``[T, N]`` (a plain tensor op, for checks and inspection)."""
+    shifts = torch.arange(8, device=bits.device, dtype=torch.uint8)
+    b = (bits.unsqueeze(-1) >> shifts) & 1
+    return b.reshape(bits.shape[0], -1)[:, :N].float()
+
+
 def lif_bwd(g_spikes, g_vfinal, x, spikes, beta, v_th, v_reset, in_gain=1.0, surrogate="superspike", k=4.0,
-            need_beta_grad=True):
-    """Backward of ``lif_fwd``; returns ``(grad_x in x.dtype, grad_beta fp32 [1] or None)``."""
+            need_beta_grad=True, spikes_packed=False):
+    """Backward of ``lif_fwd``; returns ``(grad_x in x.dtype, grad_beta fp32 [1] or None)``.
+    ``spikes_packed``: ``spikes`` holds packed bits (``spike_dtype="bits"``)."""
     _cuda(g_spikes, g_vfinal, x, spikes)
     x = x.contiguous()
     spikes = spikes.contiguous()
@@ -67,11 +84,13 @@ def lif_bwd(g_spikes, g_vfinal, x, spikes, beta, v_th, v_reset, in_gain=1.0, sur
         gb = torch.empty(1, dtype=torch.float32, device=dev)
         wsb = int(_lib.load().spk_lif_bwd_workspace_bytes(T, N))
         ws = torch.empty(wsb // 4, dtype=torch.float32, device=dev)
+    s_code = _lib.BIT if spikes_packed else _lib.dtype_code(spikes)
     _lib.call("spk_lif_bwd", _lib.ptr(g_spikes), _lib.ptr(g_vfinal), _lib.ptr(x), _lib.dtype_code(x),
-              _lib.ptr(spikes), _lib.dtype_code(spikes), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain),
+              _lib.ptr(spikes), s_code, _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain),
               _lib.SURROGATE[surrogate], float(k), _lib.ptr(gx), _lib.ptr(gb), _lib.ptr(ws), wsb, T, N,
               _lib.stream_ptr(dev), tag="lif_bwd",
-              work=dict(bytes=T * N * (4 + 2 * x.element_size() + spikes.element_size()), launches=2))
+              work=dict(bytes=T * N * (4 + 2 * x.element_size()) + spikes.numel() * spikes.element_size(),
+                        launches=2))
     return gx, gb
 
 
@@ -258,8 +277,17 @@ def ssa(q, k, v, T, B, H, variant, scale, lif_beta, lif_vth, lif_vr, in_gain=1.0
     _lib.call("spk_ssa_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), int(variant), mask_mode, mptr, *strides,
               _lib.ptr(sc), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, B, H, Nq, Nk, dh,
               _lib.ptr(out), _lib.DTYPE_CODE[out_dtype], _lib.ptr(attn), _lib.stream_ptr(dev),
-              tag="ssa Nq=%d Nk=%d" % (Nq, Nk), work=dict(flops=4.0 * T * B * H * Nq * Nk * dh))
+              tag="ssa Nq=%d Nk=%d" % (Nq, Nk),
+              work=dict(flops=4.0 * T * B * H * Nq * Nk * dh,
+                        bytes=(q.numel() + k.numel() + v.numel()) * 2 + out.numel() * out.element_size()
+                        + (attn.numel() * 4 if attn is not None else 0)
+                        + (_distinct_bytes(m8) if m8 is not None else 0)))
     return out, attn
+
+
+def _distinct_bytes(t):
+    """Bytes of memory behind a (possibly broadcast, stride-0) tensor."""
+    return t.untyped_storage().nbytes()
 
 
 def mask_to_u8(mask, T, B, H, Nq, Nk):

@@ -76,11 +76,15 @@ def stream_forward(fn, host_inputs, host_outputs, device=None):
     d2h.wait_stream(comp)
     ready = [None] * n
     done = [None] * n
+    copied = [None] * n
 
     def copy_in(i):
         with torch.cuda.stream(h2d):
             if i >= 2:
-                h2d.wait_event(done[i - 2])  # the slot's previous batch has been consumed
+                # the slot's previous batch has been consumed, and its result
+                # copied out (the result may alias the slot)
+                h2d.wait_event(done[i - 2])
+                h2d.wait_event(copied[i - 2])
             for dst, src in zip(slots[i % 2], host_inputs[i]):
                 dst.copy_(src, non_blocking=True)
             ev = torch.cuda.Event()
@@ -105,6 +109,8 @@ def stream_forward(fn, host_inputs, host_outputs, device=None):
         with torch.cuda.stream(d2h):
             d2h.wait_event(ev)
             host_outputs[i].copy_(out, non_blocking=True)
+            copied[i] = torch.cuda.Event()
+            copied[i].record(d2h)
         out.record_stream(d2h)  # keep the result's memory until its copy ends
     comp.wait_stream(d2h)
     for s in slots:

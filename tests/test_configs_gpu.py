@@ -1,0 +1,448 @@
+"""Parity at the benchmark configurations' own sizes.
+
+* Fused Linear -> LayerNorm -> LIF at the MLP up-projection shape: A
+  ``[T=4 x 32 images x 256 tokens, 384]`` Bernoulli(0.15) bf16, W
+  ``[1536, 384]`` Kaiming-uniform bf16, bias U(-0.01, 0.01), LayerNorm gamma 1
+  beta 0 eps 1e-5, tau = 2 neuron (beta 0.5, input gain 0.5), v_th 1.
+* The spiking attention block at ``[T=4, B=32, H=8, N=256, d=48]``
+  Bernoulli(0.15) spikes: ``((Q K^T) mask) V * 0.125`` (and the XNOR form the
+  model uses), LIF (tau = 2, v_th 0.5), then out_proj 384 -> 384 bf16,
+  LayerNorm, LIF; and the causal variant at N = 64.
+* The OCR seq2seq (patch 16, D 384, H 8, MLP 1536, 8 encoder + 4 decoder
+  layers, T 4, vocab 256) at 8 images, teacher-forced: every fused kernel of
+  every layer is fed the oracle's input for that kernel, and every layer is
+  fed the oracle's input for that layer.
+* Whole-model gradients of a 1 + 1-layer model (fp32, SuperSpike) against
+  the oracle's autograd, and the reference's training configuration (fp16
+  autocast, GradScaler, CNN backbone, padding-aware decoder mask).
+
+Rules (tests/parity.py): spikes bit-exact except neurons whose oracle
+membrane comes within 1e-4 of threshold; LayerNorm outputs within 1e-3
+relative; spike-count products bit-exact.  A layer whose kernels, each fed
+the oracle's inputs, reproduce the oracle's spikes exactly must reproduce the
+oracle's layer output exactly when composed.
+"""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from oracle import modules as om
+from parity import assert_close_rel, assert_spikes_match, membrane_history
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from spikingtransformer_b200 import ops as o
+    return o
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def kaiming_uniform_bf16(N, K, g):
+    # nn.init.kaiming_uniform_(a=sqrt(5)) on an [N, K] weight: bound 1/sqrt(K)
+    return ((torch.rand(N, K, generator=g) * 2 - 1) / math.sqrt(K)).to(torch.bfloat16)
+
+
+def lif_out_check(ours, pre, T, beta, vth, vr=0.0, gain=1.0, what="spikes"):
+    """Check ``ours`` (spikes in the layout of ``pre``) against the oracle LIF
+    of ``pre`` over the t-major fold; returns the number of spikes that differ
+    (all of them inside the near-threshold band)."""
+    x3 = pre.detach().float().cpu().reshape(T, -1)
+    ref, _ = oracle.lif_forward(x3, beta, vth, vr, in_gain=gain)
+    vh = membrane_history(x3, beta, vth, vr, gain)
+    o = ours.detach().float().cpu().reshape(T, -1)
+    assert_spikes_match(o, ref, vh, vth, what=what)
+    return int((o != ref).sum())
+
+
+# ------------------------------------------------------------------ fused Linear -> LayerNorm -> LIF
+
+
+def test_linear_ln_lif_mlp_expand_full_size(ops):
+    T, R, K, N = 4, 32 * 256, 384, 1536
+    g = gen(2)
+    A = (torch.rand(T * R, K, generator=g) < 0.15).to(torch.bfloat16)
+    W = kaiming_uniform_bf16(N, K, g)
+    bias = (torch.rand(N, generator=g) * 2 - 1) * 0.01
+    gamma, beta_ln = torch.ones(N), torch.zeros(N)
+    pre = torch.addmm(bias, A.float(), W.float().t())
+    y_ref = F.layer_norm(pre, (N,), gamma, beta_ln, 1e-5)
+    del pre
+    args = (A.to(DEV), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV), 1e-5, 0.5, 1.0, 0.0, T)
+    # the general epilogue (fp32 spikes and the LayerNorm output) ...
+    s, y = ops.linear_ln_lif(*args, in_gain=0.5, want_ln_out=True, spike_dtype=torch.float32)
+    assert_close_rel(y, y_ref, what="layernorm out")
+    del y
+    lif_out_check(s, y_ref, T, 0.5, 1.0, gain=0.5, what="spikes (general epilogue)")
+    # ... and the T = 4 epilogue the model runs (bf16 spikes only)
+    s2, _ = ops.linear_ln_lif(*args, in_gain=0.5, spike_dtype=torch.bfloat16)
+    lif_out_check(s2, y_ref, T, 0.5, 1.0, gain=0.5, what="spikes (T=4 epilogue)")
+
+
+# ------------------------------------------------------------------ attention block
+
+
+def attention_oracle(q, k, v, T, H, variant, scale, mask=None, chunk=16):
+    """Exact integer product O (fp32 holds it: every sum is below 2^24) and
+    the reference-rounded attention a [TB, H, Nq, dh] for q [TB, Nq, D], k / v
+    [TB, Nk, D] float 0/1 spikes."""
+    TB, Nq, D = q.shape
+    Nk = k.shape[1]
+    dh = D // H
+    o_int = torch.empty(TB, H, Nq, dh)
+    attn = torch.empty(TB, H, Nq, dh)
+    xm = om.SSAMultiHeadAttention(D, H, n_steps=T)
+    with torch.no_grad():
+        xm.scale.fill_(scale)
+    for c in range(0, TB, chunk):
+        qh = q[c:c + chunk].view(-1, Nq, H, dh).transpose(1, 2)
+        kh = k[c:c + chunk].view(-1, Nk, H, dh).transpose(1, 2)
+        vh = v[c:c + chunk].view(-1, Nk, H, dh).transpose(1, 2)
+        m = None if mask is None else mask[c:c + chunk]
+        with torch.no_grad():
+            if variant == 1:
+                s_int = om.SSAMultiHeadAttention.xnor_scores(qh, kh) + om.log_pe_bias(Nq, Nk)
+                attn[c:c + chunk] = xm.attention(qh, kh, vh, m)
+            else:
+                s_int = qh @ kh.transpose(-2, -1)
+                attn[c:c + chunk] = om.SSAMultiHeadAttention_.attention(None, qh, kh, vh, m)
+            if m is not None:
+                s_int = s_int * m
+            o_int[c:c + chunk] = s_int @ vh
+    return o_int, attn
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("N,causal", [(256, False), (64, True)])
+def test_attention_block_full_size(ops, variant, N, causal):
+    """Q, K, V spikes [4, 32, 8, N, 48] -> attention -> LIF -> out_proj -> LayerNorm -> LIF."""
+    T, B, H, dh = 4, 32, 8, 48
+    D = H * dh
+    g = gen(31 + N + variant)
+    q, k, v = ((torch.rand(T * B, N, D, generator=g) < 0.15).float() for _ in range(3))
+    scale = 0.125 if variant == 0 else (1.0 / dh) ** 0.5
+    mask = torch.tril(torch.ones(N, N)).expand(T * B, 1, N, N) if causal else None
+    o_int, attn_ref = attention_oracle(q, k, v, T, H, variant, scale, mask)
+    s, attn = ops.ssa(q.to(DEV).bfloat16(), k.to(DEV).bfloat16(), v.to(DEV).bfloat16(), T, B, H, variant, scale,
+                      0.5, 0.5, 0.0, in_gain=0.5, causal=causal, out_dtype=torch.bfloat16, want_attn=True)
+    # spike-count products: bit-exact (a = fl(scale * O))
+    assert torch.equal(attn.cpu(), o_int * torch.tensor(scale, dtype=torch.float32))
+    s_heads = s.float().cpu().view(T * B, N, H, dh).transpose(1, 2)
+    if variant == 0:
+        # 0.125 * integer and the tau = 2 LIF are exact on both sides: bit for bit
+        want, _ = oracle.lif_forward(attn_ref.reshape(T, -1), 0.5, 0.5, 0.0, in_gain=0.5)
+        assert torch.equal(s_heads.reshape(T, -1), want)
+    else:
+        # the reference rounds S * scale per element before @ V: near-threshold rule
+        lif_out_check(s_heads, attn_ref, T, 0.5, 0.5, gain=0.5, what="attention spikes")
+    # out_proj 384 -> 384 (bf16) -> LayerNorm -> LIF on the oracle's attention spikes
+    s_ref, _ = oracle.lif_forward(attn_ref.reshape(T, -1), 0.5, 0.5, 0.0, in_gain=0.5)
+    merged = s_ref.view(T * B, H, N, dh).transpose(1, 2).reshape(T * B * N, D)
+    W = kaiming_uniform_bf16(D, D, g)
+    bias = (torch.rand(D, generator=g) * 2 - 1) * 0.01
+    gamma, beta_ln = torch.ones(D), torch.zeros(D)
+    y_ref = F.layer_norm(torch.addmm(bias, merged, W.float().t()), (D,), gamma, beta_ln, 1e-5)
+    so, y = ops.linear_ln_lif(merged.to(DEV).bfloat16(), W.to(DEV), bias.to(DEV), gamma.to(DEV), beta_ln.to(DEV),
+                              1e-5, 0.5, 1.0, 0.0, T, in_gain=0.5, want_ln_out=True, spike_dtype=torch.float32)
+    assert_close_rel(y, y_ref, what="out_proj layernorm")
+    lif_out_check(so, y_ref, T, 0.5, 1.0, gain=0.5, what="out_proj spikes")
+
+
+# ------------------------------------------------------------------ OCR seq2seq, teacher-forced
+
+
+def _bench_models(seed=0, enc_layers=8, dec_layers=4, T=4, D=384, H=8, F_=1536, V=256, patch=16, dropout=0.1,
+                  image_encoder="patch", nb_sps_blocks=4):
+    from spikingtransformer_b200.Seq2Seq import Seq2Seq
+    torch.manual_seed(seed)
+    kw = dict(patch_size=patch, d_model=D, n_heads=H, ff_dim=F_, num_encoder_layers=enc_layers,
+              num_decoder_layers=dec_layers, dropout=dropout, tgt_vocab_size=V, n_steps=T,
+              image_encoder=image_encoder, nb_sps_blocks=nb_sps_blocks)
+    ours = Seq2Seq(**kw)
+    with torch.no_grad():
+        for mod in ours.modules():
+            if isinstance(mod, (torch.nn.Linear, torch.nn.Conv2d, torch.nn.Conv1d)):
+                mod.weight.copy_(mod.weight.to(torch.bfloat16).float())
+    ref = om.Seq2Seq(**kw)
+    ref.load_state_dict(ours.state_dict())
+    return ours.to(DEV), ref
+
+
+def synthetic_lines(B, seed, H=64, W=1024):
+    """Text-line stand-ins: U(0, 0.2) background plus 5-40 black rectangles of
+    side 8-20 px per image, from a seed."""
+    g = torch.Generator().manual_seed(seed)
+    img = torch.rand(B, 1, H, W, generator=g) * 0.2
+    for b in range(B):
+        n = int(torch.randint(5, 41, (1,), generator=g))
+        for _ in range(n):
+            h, w = (int(x) for x in torch.randint(8, 21, (2,), generator=g))
+            y = int(torch.randint(0, H - h + 1, (1,), generator=g))
+            x = int(torch.randint(0, W - w + 1, (1,), generator=g))
+            img[b, 0, y:y + h, x:x + w] = 0.0
+    return img
+
+
+def _beta(lif):
+    return float(lif.effective_beta().detach())
+
+
+class _Tally:
+    def __init__(self):
+        self.flips = {}
+
+    def add(self, name, n):
+        self.flips[name] = self.flips.get(name, 0) + n
+
+
+def _ssa_teacher_forced(ours_sa, ref_sa, x, kv, T, mask_ref, mask_ours, tally, tag):
+    """One attention sub-layer, each kernel fed the oracle's input.  ``x`` /
+    ``kv``: oracle fp32 residual streams (``kv`` None for self-attention).
+    Returns the oracle's ``x + SSA(x, kv, kv)``."""
+    from spikingtransformer_b200._fused import lin_ln_lif
+    src = x if kv is None else kv
+    TB, Nq, D = x.shape
+    Nk = src.shape[1]
+    H, dh = ref_sa.n_heads, ref_sa.d_head
+    xb, sb = x.to(DEV).bfloat16(), src.to(DEV).bfloat16()
+    spikes = {}
+    with torch.no_grad():
+        for name, inp, inp_dev in (("q", x, xb), ("k", src, sb), ("v", src, sb)):
+            proj, ln, lif = getattr(ref_sa, name + "_proj"), getattr(ref_sa, "ln" + name), getattr(ref_sa, "lif" + name)
+            pre = ln(proj(inp))
+            spikes[name] = lif(pre)[0]
+            o = lin_ln_lif(inp_dev, getattr(ours_sa, name + "_proj"), getattr(ours_sa, "ln" + name),
+                           getattr(ours_sa, "lif" + name), T)[0]
+            tally.add(tag + "." + name, lif_out_check(o, pre, T, _beta(lif), float(lif.v_th), what=tag + "." + name))
+        qh = spikes["q"].view(TB, Nq, H, dh).transpose(1, 2)
+        kh = spikes["k"].view(TB, Nk, H, dh).transpose(1, 2)
+        vh = spikes["v"].view(TB, Nk, H, dh).transpose(1, 2)
+        attn = ref_sa.attention(qh, kh, vh, mask_ref)
+        s_ref = ref_sa.lifs(attn)[0]
+        a = ours_sa._attend(spikes["q"].to(DEV).bfloat16(), spikes["k"].to(DEV).bfloat16(),
+                            spikes["v"].to(DEV).bfloat16(), T, mask_ours)
+        a_heads = a.float().cpu().view(TB, Nq, H, dh).transpose(1, 2)
+        tally.add(tag + ".attn", lif_out_check(a_heads, attn, T, _beta(ref_sa.lifs), float(ref_sa.lifs.v_th),
+                                               what=tag + ".attn"))
+        merged = s_ref.transpose(1, 2).reshape(TB, Nq, D)
+        pre_o = ref_sa.lno(ref_sa.out_proj(merged))
+        o_ref = ref_sa.lifo(pre_o)[0]
+        resid = xb.clone()
+        lin_ln_lif(merged.to(DEV).bfloat16(), ours_sa.out_proj, ours_sa.lno, ours_sa.lifo, T,
+                   residual=resid.view(-1, D), want_spikes=False)
+        delta = resid.float().cpu() - x
+        tally.add(tag + ".out_proj", lif_out_check(delta, pre_o, T, _beta(ref_sa.lifo), float(ref_sa.lifo.v_th),
+                                                   what=tag + ".out_proj (residual add)"))
+    return x + o_ref
+
+
+def _mlp_teacher_forced(ours_mlp, ref_mlp, x, T, tally, tag):
+    from spikingtransformer_b200._fused import lin_ln_lif
+    D = x.shape[-1]
+    with torch.no_grad():
+        pre_h = ref_mlp.bn_expand(ref_mlp.expand(x))
+        h = ref_mlp.lifexpand(pre_h)[0]
+        hs = lin_ln_lif(x.to(DEV).bfloat16(), ours_mlp.expand, ours_mlp.bn_expand, ours_mlp.lifexpand, T)[0]
+        tally.add(tag + ".expand", lif_out_check(hs, pre_h, T, _beta(ref_mlp.lifexpand), 1.0, what=tag + ".expand"))
+        pre_c = ref_mlp.bn_compress(ref_mlp.compress(h))
+        c = ref_mlp.lifcompress(pre_c)[0]
+        resid = x.to(DEV).bfloat16().contiguous()
+        lin_ln_lif(h.to(DEV).bfloat16().view(-1, h.shape[-1]), ours_mlp.compress, ours_mlp.bn_compress,
+                   ours_mlp.lifcompress, T, residual=resid.view(-1, D), want_spikes=False)
+        delta = resid.float().cpu() - x
+        tally.add(tag + ".compress", lif_out_check(delta, pre_c, T, _beta(ref_mlp.lifcompress), 1.0,
+                                                   what=tag + ".compress (residual add)"))
+    return x + c
+
+
+def _layer_check(ours_out, ref_out, flips, tag, bound=2e-3):
+    """Composition check of one layer fed the oracle's input: bit-exact when no
+    kernel of the layer flipped a spike; otherwise only the spikes a flip can
+    reach may differ, bounded here as a fraction of the output."""
+    o = ours_out.float().cpu()
+    bad = int((o != ref_out).sum())
+    if flips == 0:
+        assert bad == 0, f"{tag}: {bad} outputs differ although every kernel matched the oracle exactly"
+    else:
+        assert bad <= bound * o.numel(), f"{tag}: {bad} of {o.numel()} outputs differ after {flips} flips"
+    return bad
+
+
+def test_seq2seq_teacher_forced_8_images(pkg_loaded):
+    from spikingtransformer_b200 import ops
+    from spikingtransformer_b200._fused import bf16_weight
+    T, B, N = 4, 8, 64
+    ours, ref = _bench_models()
+    ours.eval()
+    ref.eval()
+    src = synthetic_lines(B, 1)
+    tgt = torch.randint(0, 256, (B, N), generator=gen(2))
+    mask = torch.tril(torch.ones(N, N)).expand(B, 1, N, N)
+    tally = _Tally()
+    layer_bad = {}
+    with torch.no_grad():
+        # image encoder: 16 x 16 patch embedding -> LayerNorm -> LIF, repeated over T
+        pe = ref.image_encoder
+        y = pe.norm(pe.proj(src).flatten(2).transpose(1, 2))
+        y_t = y.unsqueeze(0).expand(T, *y.shape).reshape(T * B, *y.shape[1:])
+        x = pe.lif(y_t)[0]
+        x_ours = ours.image_encoder.encode_images(src.to(DEV))
+        tally.add("patch_embed", lif_out_check(x_ours, y_t, T, _beta(pe.lif), 1.0, what="patch embedding"))
+        # encoder layers
+        for i, (lo, lr) in enumerate(zip(ours.encoder.layers, ref.encoder.layers)):
+            tag = "enc%d" % i
+            before = dict(tally.flips)
+            x1 = _ssa_teacher_forced(lo.self_attns, lr.self_attns, x, None, T, None, None, tally, tag + ".self")
+            x2 = _mlp_teacher_forced(lo.mlp, lr.mlp, x1, T, tally, tag + ".mlp")
+            flips = sum(tally.flips.values()) - sum(before.values())
+            got = lo._fast(x.to(DEV).bfloat16().contiguous())
+            layer_bad[tag] = _layer_check(got, x2, flips, tag)
+            x = x2
+        enc = x
+        enc_dev = enc.to(DEV).bfloat16().contiguous()
+        # decoder input: token embedding + positions -> LIF
+        emb = ref.positional_encoding(ref.tgt_tok_emb(tgt))
+        e_t = emb.unsqueeze(0).expand(T, *emb.shape).reshape(T * B, N, -1)
+        yd = ref.lifPE(e_t)[0]
+        emb_mod = ours.tgt_tok_emb
+        yd_ours, bad_tok = ops.embed_pe_lif(tgt.to(DEV), emb_mod.embedding.weight, math.sqrt(emb_mod.emb_size),
+                                            ours.positional_encoding.pos_embedding, _beta(ours.lifPE), 1.0, 0.0, T)
+        assert int(bad_tok.item()) == 0
+        tally.add("embed", lif_out_check(yd_ours, e_t, T, _beta(ref.lifPE), 1.0, what="token embedding"))
+        mask_ref = mask.unsqueeze(0).repeat(T, 1, 1, 1, 1).reshape(T * B, 1, N, N)
+        H = ref.decoder.layers[0].self_attns.n_heads
+        mask_ours = ops.mask_to_u8(mask.to(DEV), T, B, H, N, N)
+        for i, (lo, lr) in enumerate(zip(ours.decoder.layers, ref.decoder.layers)):
+            tag = "dec%d" % i
+            before = dict(tally.flips)
+            y1 = _ssa_teacher_forced(lo.self_attns, lr.self_attns, yd, None, T, mask_ref, mask_ours, tally,
+                                     tag + ".self")
+            y2 = _ssa_teacher_forced(lo.cross_attns, lr.cross_attns, y1, enc, T, None, None, tally, tag + ".cross")
+            y3 = _mlp_teacher_forced(lo.mlp, lr.mlp, y2, T, tally, tag + ".mlp")
+            flips = sum(tally.flips.values()) - sum(before.values())
+            got = lo._fast(yd.to(DEV).bfloat16().contiguous(), enc_dev, mask_ours)
+            layer_bad[tag] = _layer_check(got, y3, flips, tag)
+            yd = y3
+        # output projection on the oracle's decoder output: fp32 logits
+        D = yd.shape[-1]
+        logits_ref = ref.output_layer(yd)
+        logits = ops.linear(yd.to(DEV).bfloat16().view(-1, D), bf16_weight(ours.output_layer), ours.output_layer.bias)
+        assert_close_rel(logits.view_as(logits_ref), logits_ref, tol=1e-5, what="logits (teacher-forced)")
+        # free-running model: the same forward end to end
+        full, _ = ours(src.to(DEV), tgt.to(DEV), look_ahead_mask=mask.to(DEV))
+        want, _ = ref(src, tgt, look_ahead_mask=mask)
+    print("teacher-forced flips (all near threshold):", {k: v for k, v in tally.flips.items() if v})
+    print("layer outputs differing:", layer_bad)
+    close = torch.isclose(full.cpu(), want, rtol=1e-3, atol=1e-3).float().mean().item()
+    print("free-running logits within 1e-3: %.4f" % close)
+    assert close > 0.9, close
+
+
+@pytest.fixture(scope="module")
+def pkg_loaded():
+    import spikingtransformer_b200 as p
+    p.install_as_triton_layers()
+    return p
+
+
+# ------------------------------------------------------------------ gradients
+
+
+def test_seq2seq_gradients_match_oracle_fp32(pkg_loaded):
+    """Loss and every parameter gradient of a 1 + 1-layer model (fp32,
+    SuperSpike, teacher forcing) against the oracle's autograd.  The forward
+    must match first (a flipped spike changes the graph); then each gradient
+    must agree within 2e-3 of its largest element (the attention backward
+    splits real operands into two bf16 terms, about 2^-16 relative)."""
+    T, B, N, V = 4, 2, 8, 32
+    ours, ref = _bench_models(enc_layers=1, dec_layers=1, D=64, H=2, F_=128, V=V, dropout=0.0)
+    ours.train()
+    ref.train()
+    src = synthetic_lines(B, 7, H=32, W=128)
+    tgt = torch.randint(1, V, (B, N + 1), generator=gen(8))
+    mask = torch.tril(torch.ones(N, N)).expand(B, 1, N, N)
+
+    def loss_of(logits, tout):
+        return sum(F.cross_entropy(logits[t].reshape(-1, V), tout.reshape(-1)) for t in range(T)) / T
+
+    logits, _ = ours(src.to(DEV), tgt[:, :-1].to(DEV), look_ahead_mask=mask.to(DEV))
+    loss = loss_of(logits, tgt[:, 1:].to(DEV))
+    loss.backward()
+    logits_ref, _ = ref(src, tgt[:, :-1], look_ahead_mask=mask)
+    loss_ref = loss_of(logits_ref, tgt[:, 1:])
+    loss_ref.backward()
+    assert_close_rel(logits.detach(), logits_ref.detach(), tol=1e-4, what="logits")
+    assert abs(loss.item() - loss_ref.item()) <= 1e-5 * abs(loss_ref.item())
+    ref_grads = dict(ref.named_parameters())
+    checked = 0
+    for name, p in ours.named_parameters():
+        r = ref_grads[name].grad
+        if r is None:
+            assert p.grad is None or float(p.grad.abs().max()) == 0.0, name
+            continue
+        assert p.grad is not None, name
+        gmax = float(r.abs().max())
+        err = float((p.grad.detach().cpu() - r).abs().max())
+        assert err <= 2e-3 * gmax + 1e-7, (name, err, gmax)
+        checked += 1
+    assert checked > 40
+
+
+def test_reference_training_configuration_fp16_gradscaler_cnn(pkg_loaded):
+    """Six steps as the reference trainer runs them (train_spikeformer.py:
+    540-577): CNN backbone image encoder, fp16 autocast, GradScaler,
+    cross-entropy with label smoothing 0.1 ignoring the padding index, a
+    decoder mask combining the look-ahead and key-padding masks
+    (create_decoder_mask), gradient clipping at 1.0, AdamW.  The first step's
+    loss agrees with the oracle's fp32 loss on the same batch, the losses are
+    finite, and the steps update the weights (GradScaler skips a step whose
+    scaled fp16 gradients overflow and halves its scale, so not every step
+    need apply)."""
+    T, B, V, pad = 4, 2, 40, 0
+    ours, ref = _bench_models(enc_layers=1, dec_layers=1, D=64, H=2, F_=128, V=V, patch=4, dropout=0.0,
+                              image_encoder="cnn", nb_sps_blocks=1)
+    ours.train()
+    ref.train()
+    src = synthetic_lines(B, 9, H=32, W=128)
+    tgt = torch.randint(3, V, (B, 10), generator=gen(10))
+    tgt[0, 7:] = pad  # a shorter line, padded
+    tgt[1, 9:] = pad
+    opt = torch.optim.AdamW(ours.parameters(), lr=1e-4, betas=(0.9, 0.98), eps=1e-9, weight_decay=0.01)
+    scaler = torch.amp.GradScaler("cuda")
+    crit = torch.nn.CrossEntropyLoss(ignore_index=pad, label_smoothing=0.1)
+
+    def step_loss(logits, tout):
+        return sum(crit(logits[t].reshape(-1, V).float(), tout.reshape(-1)) for t in range(T)) / T
+
+    tin, tout = tgt[:, :-1], tgt[:, 1:]
+    with torch.no_grad():
+        mref = ref.create_decoder_mask(tin, pad, "cpu")
+        loss_ref = step_loss(ref(src, tin, look_ahead_mask=mref)[0], tout).item()
+    before = {n: p.detach().clone() for n, p in ours.named_parameters()}
+    s_dev, tin_dev, tout_dev = src.to(DEV), tin.to(DEV), tout.to(DEV)
+    losses = []
+    for _ in range(6):
+        opt.zero_grad(set_to_none=True)
+        mask = ours.create_decoder_mask(tin_dev, pad, DEV)
+        with torch.autocast("cuda", dtype=torch.float16):
+            logits, _ = ours(s_dev, tin_dev, look_ahead_mask=mask)
+            loss = step_loss(logits, tout_dev)
+        scaler.scale(loss).backward()
+        scaler.unscale_(opt)
+        torch.nn.utils.clip_grad_norm_(ours.parameters(), 1.0)
+        scaler.step(opt)
+        scaler.update()
+        losses.append(loss.item())
+    assert all(math.isfinite(x) for x in losses), losses
+    assert abs(losses[0] - loss_ref) <= 0.03 * loss_ref, (losses[0], loss_ref)
+    changed = [n for n, p in ours.named_parameters() if not torch.equal(p.detach(), before[n])]
+    assert any("image_encoder.conv1" in n for n in changed) and any("output_layer" in n for n in changed)

@@ -46,6 +46,33 @@ def test_lif_fwd_cfg1_bit_exact(ops, spike_dtype):
     assert torch.equal(vf.cpu(), vf_ref)
 
 
+@pytest.mark.parametrize("N", [4 * 8 * 128 * 256 // 4, 1001, 8, 3])
+def test_lif_fp8_and_packed_bit_spikes(ops, N):
+    """fp8 (e4m3) and packed-bit spike outputs: the same trains as fp32 spikes,
+    and the backward reads them back bit-exactly (vector path for N % 8 == 0,
+    per-element path for a ragged last byte)."""
+    T = 4
+    g = gen(N)
+    x = torch.randn(T, N, generator=g) + 0.5
+    gs = torch.randn(T, N, generator=g)
+    s_ref, vf_ref = oracle.lif_forward(x, 0.5, 1.0, 0.0, in_gain=0.5)
+    xd = x.to(DEV)
+    s8, vf8 = ops.lif_fwd(xd, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype=torch.float8_e4m3fn)
+    assert s8.dtype == torch.float8_e4m3fn and torch.equal(s8.float().cpu(), s_ref)
+    assert torch.equal(vf8.cpu(), vf_ref)
+    sb, vfb = ops.lif_fwd(xd, 0.5, 1.0, 0.0, in_gain=0.5, spike_dtype="bits")
+    assert sb.shape == (T, (N + 7) // 8) and sb.dtype == torch.uint8
+    assert torch.equal(ops.unpack_spike_bits(sb, N).cpu(), s_ref)
+    assert torch.equal(vfb.cpu(), vf_ref)
+    if N % 8:  # bits past N in the last byte stay 0
+        assert int(sb[:, -1].cpu().max()) < (1 << (N % 8))
+    gx_ref, gb_ref = oracle.lif_backward(gs, None, x, s_ref, 0.5, 1.0, 0.0, in_gain=0.5)
+    for spikes, packed in ((s8, False), (sb, True)):
+        gx, gb = ops.lif_bwd(gs.to(DEV), None, xd, spikes, 0.5, 1.0, 0.0, in_gain=0.5, spikes_packed=packed)
+        assert torch.equal(gx.cpu(), gx_ref)
+        assert torch.allclose(gb.cpu().reshape(()), gb_ref, rtol=1e-4, atol=1e-4)
+
+
 def test_lif_golden(ops, golden_dir):
     for c in torch.load(os.path.join(golden_dir, "lif.pt"), weights_only=False):
         x = c["x_in"].to(DEV)
@@ -397,6 +424,25 @@ def test_embed_pe_lif(ops):
 
 def test_no_device_timeouts(ops):
     ops.device_error_check()
+
+
+def test_bounded_wait_gives_up_and_reports_timeout(ops):
+    """A device-side wait that nothing satisfies ends after its limit (50 ms
+    here instead of the kernels' 2 s): the kernel returns, the context stays
+    usable, and the host sees SPK_ERR_TIMEOUT once, after which the flag is
+    clear."""
+    from spikingtransformer_b200 import _lib
+    lib = _lib.load()
+    ops.device_error_check()
+    st = _lib.stream_ptr(torch.device(DEV))
+    assert lib.spk_test_bounded_wait(50_000_000, st) == 0
+    with pytest.raises(RuntimeError, match="timed out"):
+        ops.device_error_check()
+    ops.device_error_check()  # cleared
+    x = torch.ones(2, 8, device=DEV)
+    s, _ = ops.lif_fwd(x, 0.5, 0.75, 0.0)  # the device still runs work
+    assert s.sum().item() == 8.0
+    assert lib.spk_test_bounded_wait(0, st) == 1  # SPK_ERR_INVALID
 
 
 # ------------------------------------------------------------------ LayerNorm -> LIF (training)

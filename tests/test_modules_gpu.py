@@ -499,6 +499,48 @@ def test_stream_forward_matches_direct_forward(pkg):
         assert torch.equal(shared, want[4])
 
 
+def test_public_stack_forwards_do_not_synchronise(pkg):
+    """Seq2Seq.encode / decode and the Encoder / Decoder / LIF module forwards
+    on the inference path enqueue work without a device-to-host read (the
+    stream's exactness in bf16 is known from where it came from, not read
+    back)."""
+    from spikingtransformer_b200.Lif import LIF
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    B, N = 2, 16
+    src = synthetic_lines(B, 6).to(DEV)
+    tgt = torch.randint(0, 256, (B, N), device=DEV, generator=torch.Generator(device=DEV).manual_seed(6))
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(B, 1, N, N)
+    lif = LIF(n_steps=4).to(DEV)
+    x_in = torch.rand(4 * B, 10, device=DEV)
+    with torch.no_grad():
+        ours(src, tgt, look_ahead_mask=mask)  # warm caches (weights, LIF parameters)
+        torch.cuda.synchronize()
+        torch.cuda.set_sync_debug_mode("error")
+        try:
+            enc, _ = ours.encode(src)
+            logits, _ = ours.decode(tgt, enc, mask)
+            enc2 = ours.encoder(ours.image_encoder.encode_images(src).float())
+            s, _ = lif(x_in)
+        finally:
+            torch.cuda.set_sync_debug_mode(0)
+        want, _ = ours(src, tgt, look_ahead_mask=mask)
+    assert torch.equal(logits, want)
+    assert enc2.dtype == torch.float32 and s.shape == x_in.shape
+
+
+def test_stack_forward_leaves_bf16_input_unchanged(pkg):
+    """A bf16 residual stream handed to Encoder.forward is copied, not
+    updated in place."""
+    ours, _ = _bench_models(enc_layers=1, dec_layers=1)
+    src = synthetic_lines(2, 8).to(DEV)
+    with torch.no_grad():
+        x = ours.image_encoder.encode_images(src)
+        keep = x.clone()
+        y = ours.encoder(x)
+    assert torch.equal(x, keep)
+    assert not torch.equal(y, keep)
+
+
 def test_no_device_timeouts(pkg):
     from spikingtransformer_b200 import ops
     ops.device_error_check()

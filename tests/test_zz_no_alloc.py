@@ -62,9 +62,12 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
     torch.cuda.set_device(dev)
     prm = _params(dev)
     # large (3072-block grid, vector path), then small and odd (scalar path),
-    # then the large one again: bit-exact, the tolerance the LIF tests use
+    # then large and odd (scalar path at the 4096-block cap, every partial of
+    # the static array in use), then the first one again: bit-exact, the
+    # tolerance the LIF tests use
     cases = [(4, 3 << 20, 1, _lib.SURROGATE["superspike"], 4.0, 1.0),
              (3, 1001, 2, _lib.SURROGATE["arctan"], 2.0, 0.5),
+             (4, (3 << 20) + 1, 5, _lib.SURROGATE["superspike"], 4.0, 1.0),
              (4, 3 << 20, 3, _lib.SURROGATE["superspike"], 4.0, 1.0)]
     for T, N, seed, surrogate, k, gain in cases:
         x, spikes, gs, gv = _inputs(T, N, seed)
@@ -73,11 +76,14 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
         gb = torch.full((1,), float("nan"), device=dev)
         torch.cuda.synchronize()
         before = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
+        free_before = torch.cuda.mem_get_info(dev)[0]
         rc = _bwd_noalloc(lib, x, spikes, gs, gv, prm, surrogate, k, gain, gx, gb)
         after = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
         assert rc == 0, lib.spk_last_error().decode()
         assert after == before  # nothing went through torch's allocator
         torch.cuda.synchronize()
+        # nor through the driver: the device's free memory is unchanged
+        assert torch.cuda.mem_get_info(dev)[0] == free_before
         assert torch.equal(gx, want_gx), (T, N)
         assert torch.equal(gb, want_gb), (T, N, gb.item(), want_gb.item())
     assert lib.spk_device_error_check(None) == 0
