@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="train: run the one-GPU step eagerly")
+    ap.add_argument("--bucket-elems", type=int, default=4 << 20,
+                    help="train, N > 1: gradient elements per all-reduce bucket")
     ap.add_argument("--surrogate", default="arctan", choices=["arctan", "superspike"],
                     help="train: LIF surrogate gradient (arctan alpha 2, the training benchmark's; superspike k 4, "
                          "the reference trainer's)")
@@ -244,22 +246,31 @@ def config_kernels(dev, peaks, peak_src):
     * attention core + LIF on [4, 32, 8, 256, 48] Bernoulli(0.15) spikes,
       plain ((Q K^T) V * 0.125) and XNOR forms, and the causal form at N = 64.
 
-    Kernels timed alone: the bf16 peak is the burst figure."""
+    Each measurement replays a CUDA graph of the calls.  Kernels timed alone:
+    the bf16 peak is the burst figure."""
     from spikingtransformer_b200 import ops
     burst = {"sm_mhz": 1.0, "sm_max_mhz": 1.0}
     out = {}
 
     def timed(fn, reps):
+        # the calls are captured once in a CUDA graph and replayed, so the
+        # host's per-call overhead does not leave the GPU idle between them
         for i in range(3):
             fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(reps):
+                fn(i)
+        graph.replay()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(reps):
-            fn(i)
+        graph.replay()
         e1.record()
         torch.cuda.synchronize()
+        del graph
         return e0.elapsed_time(e1) / reps
 
     def add(name, bound, ms, nbytes=0.0, flops=0.0, note=None):
@@ -372,24 +383,6 @@ def run_reference(args, ws, rank):
     }), flush=True)
 
 
-def flat_grad_views(params, device):
-    """One zeroed fp32 buffer holding every parameter's gradient as a view (in
-    order), for a data-parallel step that all-reduces a single tensor."""
-    flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=device)
-    off = 0
-    for p in params:
-        p.grad = flat[off:off + p.numel()].view_as(p)
-        off += p.numel()
-    return flat
-
-
-def average_flat_grads(flat, ws):
-    """Sum the flat gradient buffer over the ranks and divide by their number."""
-    import torch.distributed as dist
-    dist.all_reduce(flat)
-    flat.div_(ws)
-
-
 def run_train(args, ws, rank, local):
     """--workload train: forward + backward + AdamW step of the same model, one
     process per GPU, gradients all-reduced by DDP over NCCL (bf16 autocast as
@@ -420,18 +413,22 @@ def run_train(args, ws, rank, local):
     # graph (the host would otherwise spend longer enqueueing the step's ~2,000
     # launches than the GPU spends running them); each step generates its batch
     # into the graph's static input buffers and replays the graph.  With N > 1
-    # every parameter's gradient is a view into one flat fp32 buffer, and the
-    # graph ends its backward with one NCCL all-reduce of that buffer (divided
-    # by N): data parallelism without DDP's hooks, which a graph cannot hold.
-    # --no-graph runs the step eagerly (DDP for N > 1).
+    # every parameter's gradient is a view into one flat fp32 buffer whose
+    # buckets are cast to bf16 and all-reduced over NCCL on a side stream as
+    # the backward completes them (BucketedGradReducer), so the transfers
+    # overlap the rest of the backward inside the graph.  --no-graph runs the
+    # step eagerly (DDP with its bf16 compression hook for N > 1).
     use_graph = not args.no_graph
     net = model
-    flat = None
+    reducer = None
     if ws > 1 and not use_graph:
+        from torch.distributed.algorithms.ddp_comm_hooks import default_hooks
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
                                                         gradient_as_bucket_view=True)
+        net.register_comm_hook(None, default_hooks.bf16_compress_hook)
     if ws > 1 and use_graph:
-        flat = flat_grad_views([p for p in model.parameters() if p.requires_grad], dev)
+        from spikingtransformer_b200.dp import BucketedGradReducer
+        reducer = BucketedGradReducer(model.parameters(), bucket_elems=args.bucket_elems)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=use_graph)
     B = args.batch or 64
     mask = torch.tril(torch.ones(SEQ, SEQ, device=dev)).expand(B, 1, SEQ, SEQ)
@@ -441,8 +438,8 @@ def run_train(args, ws, rank, local):
                                     V=ARCH["tgt_vocab_size"], device=dev)
 
     def zero_grads():
-        if flat is not None:
-            flat.zero_()  # the gradients stay views into it
+        if reducer is not None:
+            reducer.begin()  # the gradients stay views into its flat buffer
         else:
             opt.zero_grad(set_to_none=True)
 
@@ -452,8 +449,8 @@ def run_train(args, ws, rank, local):
             logits, _ = net(src, tgt_in, look_ahead_mask=mask)
         loss, acc, _ = ops.ce_over_t(logits, tgt_out, ignore_index=0, label_smoothing=0.1)
         loss.backward()
-        if flat is not None:
-            average_flat_grads(flat, ws)
+        if reducer is not None:
+            reducer.finish()
         opt.step()
         return loss, acc
 
@@ -472,11 +469,11 @@ def run_train(args, ws, rank, local):
                 train_step(static_src, static_labels)
         torch.cuda.current_stream(dev).wait_stream(side)
         graphs["train"] = torch.cuda.CUDAGraph()
-        if flat is None:
+        if reducer is None:
             opt.zero_grad(set_to_none=True)
         with _lib.LaunchCounter() as counter, torch.cuda.graph(graphs["train"]):
-            if flat is not None:
-                flat.zero_()
+            if reducer is not None:
+                reducer.begin()
             g_loss, g_acc = train_step(static_src, static_labels)
         graph_launches = counter.total()
 
@@ -521,8 +518,9 @@ def run_train(args, ws, rank, local):
                        "optimizer": "AdamW lr 1e-4",
                        "surrogate": "arctan alpha 2" if args.surrogate == "arctan" else "superspike k 4",
                        "loss": "mean over T of CE(ignore_index=0, label_smoothing=0.1), fused with token accuracy",
-                       "parallelism": ("dp%d (flat fp32 gradient all-reduce over NCCL inside the CUDA graph)" % ws
-                                       if flat is not None else "ddp%d (NCCL all-reduce of gradients)" % ws)},
+                       "parallelism": ("dp%d (bf16 gradient buckets all-reduced over NCCL on a side stream as the "
+                                       "backward completes them, inside the CUDA graph)" % ws if reducer is not None
+                                       else "ddp%d (NCCL all-reduce of bf16-compressed gradient buckets)" % ws)},
             "loss": last, "token_accuracy": last_acc, "clocks": clk.summary(),
             "cuda_graph": use_graph, "graph_launches_per_step": graph_launches,
             "gpu_launches": sum(v["launches"] for v in kernels.values()) + (graph_launches or 0) * args.steps,

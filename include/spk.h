@@ -30,6 +30,10 @@
  *                          SSAMultiHeadAttention_.forward SSA.py:77-87
  *   spk_embed_pe_lif_fwd   TokenEmbedding + PositionalEncoding + lifPE,
  *                          Seq2Seq.py:11-36, :109-114
+ *   spk_linear_affine_lif_fwd  conv (as a GEMM) -> eval BatchNorm -> LIF of
+ *                          CNNBackbone, ImageEncoder.py:8-102
+ *   spk_im2col             the convolutions' patch gather (PixelUnshuffle +
+ *                          Conv2d, Conv1d), ImageEncoder.py:8-102
  *   spk_patch_im2col       patch gather of the 16x16 patch-embedding image
  *                          encoder (no reference counterpart; the OCR
  *                          benchmark's ImageEncoder)
@@ -212,6 +216,40 @@ int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const
                           const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t K, int64_t N,
                           int t_broadcast, void* spikes, int spike_dtype, void* residual, float* ln_out,
                           void* stream);
+
+/*
+ * Fused Linear -> per-feature affine -> LIF: the convolutions of the CNN
+ * image encoder (as GEMMs over spk_im2col patches) with their eval-mode
+ * BatchNorm and LIF (ImageEncoder.py:8-102: conv + bn + lif in
+ * FusedInvertedBottleneck :19-28, ReduceConvBlock :34-44, RPE2D :50-61 and
+ * CNNBackbone :75-100).
+ *   y = (A W^T + bias) * scale + shift  (per feature; no row statistics);
+ *   LIF over T on y; spikes (0/1) as bf16 or fp32; with residual, the spikes
+ *   are also added into it in place (the identity of the bottleneck, the
+ *   x + rpe sum).  For eval-mode BatchNorm, scale = weight / sqrt(var + eps)
+ *   and shift = bias_bn - mean * scale.
+ * A, W, t_broadcast, spikes, residual and the size limits are those of
+ * spk_linear_ln_lif_fwd; scale / shift: [N] fp32 or NULL (1 / 0).
+ */
+int spk_linear_affine_lif_fwd(const void* A, const void* W, const float* bias, const float* scale,
+                              const float* shift, const float* lif_beta, const float* lif_vth,
+                              const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t K, int64_t N,
+                              int t_broadcast, void* spikes, int spike_dtype, void* residual, void* stream);
+
+/*
+ * Patch gather for a convolution with stride (stride_h, stride_w) and zero
+ * padding (pad_h, pad_w): x [N][H][W][C] channels-last (F32 or BF16) ->
+ * out [N*Ho*Wo][Kc] bf16, Ho = (H + 2 pad_h - kh) / stride_h + 1 (Wo alike),
+ * row (n, ho, wo), column (i*kw + j)*C + c for tap (i, j).  BF16 input:
+ * Kc = kh*kw*C.  F32 input: Kc = 2*kh*kw*C, the bf16 rounding of each value
+ * in the first half and of its remainder in the second (against [W | W] the
+ * product is the fp32 convolution to ~2^-17 relative).  Used for the CNN
+ * image encoder's convolutions (ImageEncoder.py:8-102); PixelUnshuffle(p)
+ * followed by a 3x3 / padding-1 convolution is one 3p x 3p / stride-p /
+ * padding-p gather of the image.
+ */
+int spk_im2col(const void* x, int x_dtype, int64_t N, int64_t H, int64_t W, int64_t C, int64_t kh, int64_t kw,
+               int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, void* out, void* stream);
 
 /* out[M][N] (fp32) = A[M][K] W[N][K]^T + bias (bias may be NULL); bf16 A, W. */
 int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, int64_t M, int64_t K, int64_t N,

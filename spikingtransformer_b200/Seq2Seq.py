@@ -102,6 +102,8 @@ class Seq2Seq(nn.Module):
         T = self.n_steps
         if isinstance(self.image_encoder, PatchEmbed):
             x = self.image_encoder.encode_images(src)
+        elif self.image_encoder._fast_ok(src):
+            x = self.image_encoder.encode_images(src, T)
         else:
             B = src.shape[0]
             src_t = src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:])

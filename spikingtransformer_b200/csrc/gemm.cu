@@ -72,6 +72,7 @@ struct Params {
   float* ln_out;            // TCOUPLED: [T][R][N]; TBCAST: [R][N]
   float* out_f32;           // PLAIN: [R][N]
   int vec_out;              // PLAIN: N % 4 == 0 and out, bias 16-byte aligned
+  int norm;                 // TCOUPLED / TBCAST: 1 LayerNorm over the N features, 0 per-feature affine only
 };
 
 struct Smem {
@@ -337,55 +338,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        // ---- LayerNorm statistics
-        float s = 0.0f;
-        for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
-          float v[32];
-          tmem_ld32(trow + c0, v);
-          tmem_wait_ld();
+        // ---- LayerNorm statistics (none for the affine-only epilogue: mean 0, rstd 1)
+        float mean = 0.0f, rstd = 1.0f;
+        if (p.norm) {
+          float s = 0.0f;
+          for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
+            float v[32];
+            tmem_ld32(trow + c0, v);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s += v[i];
-        }
-        const float xsum = s + bsum;
-        const float m_loc = xsum / (float)p.n_cta;
-        float m2 = 0.0f;
-        for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
-          float v[32];
-          tmem_ld32(trow + c0, v);
-          tmem_wait_ld();
+            for (int i = 0; i < 32; ++i) s += v[i];
+          }
+          const float xsum = s + bsum;
+          const float m_loc = xsum / (float)p.n_cta;
+          float m2 = 0.0f;
+          for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
+            float v[32];
+            tmem_ld32(trow + c0, v);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float d = (v[i] + sm.bias[c0 + i]) - m_loc;
-            m2 = fmaf(d, d, m2);
+            for (int i = 0; i < 32; ++i) {
+              const float d = (v[i] + sm.bias[c0 + i]) - m_loc;
+              m2 = fmaf(d, d, m2);
+            }
           }
+          mean = m_loc;
+          float var = m2 / (float)p.n_cta;
+          if (cs > 1) {
+            const int par = iter & 1;
+            float* xb = sm.xbuf + (size_t)par * cs * 128 * 2;
+            const uint32_t my_slot = smem_u32(xb + ((size_t)rank * 128 + row) * 2);
+            for (int r = 0; r < cs; ++r) st_cluster_f32x2(mapa_shared(my_slot, (uint32_t)r), xsum, m2);
+            fence_acq_rel_cluster();
+            __syncwarp();
+            if (lane == 0)
+              for (int r = 0; r < cs; ++r) mbar_arrive_remote(mapa_shared(smem_u32(&sm.xbar[par]), (uint32_t)r));
+            if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 32)) {
+              atomicExch(sm.abort_flag, 1);
+              break;
+            }
+            float tot = 0.0f;
+            for (int r = 0; r < cs; ++r) tot += xb[((size_t)r * 128 + row) * 2];
+            mean = tot / (float)p.N;
+            float M2 = 0.0f;
+            for (int r = 0; r < cs; ++r) {
+              const float sr = xb[((size_t)r * 128 + row) * 2];
+              const float m2r = xb[((size_t)r * 128 + row) * 2 + 1];
+              const float dm = sr / (float)p.n_cta - mean;
+              M2 += m2r + (float)p.n_cta * dm * dm;
+            }
+            var = M2 / (float)p.N;
+          }
+          rstd = 1.0f / sqrtf(var + p.eps);
         }
-        float mean = m_loc, var = m2 / (float)p.n_cta;
-        if (cs > 1) {
-          const int par = iter & 1;
-          float* xb = sm.xbuf + (size_t)par * cs * 128 * 2;
-          const uint32_t my_slot = smem_u32(xb + ((size_t)rank * 128 + row) * 2);
-          for (int r = 0; r < cs; ++r) st_cluster_f32x2(mapa_shared(my_slot, (uint32_t)r), xsum, m2);
-          fence_acq_rel_cluster();
-          __syncwarp();
-          if (lane == 0)
-            for (int r = 0; r < cs; ++r) mbar_arrive_remote(mapa_shared(smem_u32(&sm.xbar[par]), (uint32_t)r));
-          if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 32)) {
-            atomicExch(sm.abort_flag, 1);
-            break;
-          }
-          float tot = 0.0f;
-          for (int r = 0; r < cs; ++r) tot += xb[((size_t)r * 128 + row) * 2];
-          mean = tot / (float)p.N;
-          float M2 = 0.0f;
-          for (int r = 0; r < cs; ++r) {
-            const float sr = xb[((size_t)r * 128 + row) * 2];
-            const float m2r = xb[((size_t)r * 128 + row) * 2 + 1];
-            const float dm = sr / (float)p.n_cta - mean;
-            M2 += m2r + (float)p.n_cta * dm * dm;
-          }
-          var = M2 / (float)p.N;
-        }
-        const float rstd = 1.0f / sqrtf(var + p.eps);
         const int n0 = (int)rank * p.n_cta;
 
         if (MODE == MODE_TCOUPLED) {
@@ -662,6 +667,7 @@ int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const
   p.spk_f32 = spike_dtype == SPK_F32 ? reinterpret_cast<float*>(spikes) : nullptr;
   p.residual = reinterpret_cast<__nv_bfloat16*>(residual);
   p.ln_out = ln_out;
+  p.norm = 1;
   int mode;
   int64_t rows_2d = R;
   if (t_broadcast) {
@@ -690,6 +696,58 @@ int spk_linear_ln_lif_fwd(const void* A, const void* W, const float* bias, const
   rc = launch_gemm(mode, A, W, p, rows_2d, reinterpret_cast<cudaStream_t>(stream));
   if (rc != SPK_OK) return rc;
   return check_launch("gemm_ln_lif_kernel");
+}
+
+int spk_linear_affine_lif_fwd(const void* A, const void* W, const float* bias, const float* scale,
+                              const float* shift, const float* lif_beta, const float* lif_vth,
+                              const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t K, int64_t N,
+                              int t_broadcast, void* spikes, int spike_dtype, void* residual, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(A && W && lif_beta && lif_vth && lif_vreset, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(spike_dtype == SPK_BF16 || spike_dtype == SPK_F32, SPK_ERR_INVALID, "spike dtype must be bf16 or f32");
+  SPK_REQUIRE(spikes || residual, SPK_ERR_INVALID, "neither spikes nor residual output given");
+  SPK_REQUIRE(T >= 1 && T <= 128 && R >= 1 && K >= 8 && K % 8 == 0 && N >= 32, SPK_ERR_SHAPE,
+              "unsupported sizes T=%lld R=%lld K=%lld N=%lld (K must be a multiple of 8)", (long long)T,
+              (long long)R, (long long)K, (long long)N);
+  SPK_REQUIRE(R < (1ll << 31) && K < (1 << 24), SPK_ERR_SHAPE, "R or K too large");
+  SPK_REQUIRE(aligned(A, 16) && aligned(W, 16), SPK_ERR_ALIGN, "A and W must be 16-byte aligned");
+  SPK_REQUIRE((!spikes || aligned(spikes, 16)) && (!residual || aligned(residual, 16)), SPK_ERR_ALIGN,
+              "spike / residual buffers must be 16-byte aligned");
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  Params p = {};
+  if ((rc = pick_split((int)N, &p.cs, &p.n_cta)) != SPK_OK) return rc;
+  p.T = (int)T;
+  p.R = R;
+  p.K = (int)K;
+  p.N = (int)N;
+  p.num_n_tiles = 1;
+  p.wbox = wbox_for(p.n_cta);
+  p.tmem_cols = tmem_cols_for(p.n_cta);
+  p.bias = bias;
+  p.gamma = scale;
+  p.beta_ln = shift;
+  p.norm = 0;
+  p.lif_beta = lif_beta;
+  p.lif_vth = lif_vth;
+  p.lif_vr = lif_vreset;
+  p.gain = in_gain;
+  p.spk_bf16 = spike_dtype == SPK_BF16 ? reinterpret_cast<__nv_bfloat16*>(spikes) : nullptr;
+  p.spk_f32 = spike_dtype == SPK_F32 ? reinterpret_cast<float*>(spikes) : nullptr;
+  p.residual = reinterpret_cast<__nv_bfloat16*>(residual);
+  int mode;
+  if (t_broadcast) {
+    mode = MODE_TBCAST;
+    p.tpt = 128;
+    p.num_m_tiles = (int)((R + 127) / 128);
+  } else {
+    mode = MODE_TCOUPLED;
+    p.tpt = (int)(128 / T);
+    p.num_m_tiles = (int)((R + p.tpt - 1) / p.tpt);
+  }
+  rc = launch_gemm(mode, A, W, p, R, reinterpret_cast<cudaStream_t>(stream));
+  if (rc != SPK_OK) return rc;
+  return check_launch("gemm_ln_lif_kernel<affine>");
 }
 
 int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, int64_t M, int64_t K, int64_t N,

@@ -173,7 +173,7 @@ constexpr int kBwdThreads = 256;
 constexpr int kBwdMaxBlocks = 4096;
 
 template <int XDT, int SDT, int TMAX, int VEC>
-__global__ void __launch_bounds__(kBwdThreads) lif_bwd_kernel(
+__global__ void __launch_bounds__(kBwdThreads, TMAX <= 4 ? 3 : 1) lif_bwd_kernel(
     const float* __restrict__ gs, const float* __restrict__ gvf, const void* __restrict__ x,
     const void* __restrict__ spikes, const float* pbeta, const float* pvth, const float* pvr, float gain,
     int surr, float k, float c_arctan, void* __restrict__ gx, float* __restrict__ partials, int T, int64_t N) {
@@ -187,6 +187,15 @@ __global__ void __launch_bounds__(kBwdThreads) lif_bwd_kernel(
     float vh[TMAX][VEC];
     uint32_t sbits[TMAX];
     float v[VEC];
+    // short scans (T <= 4) load the spike gradients of every step up front,
+    // beside the inputs, so a thread's loads are all in flight at once
+    constexpr bool kPreload = TMAX <= 4;
+    float gpre[kPreload ? TMAX : 1][VEC];
+    if constexpr (kPreload) {
+#pragma unroll
+      for (int t = 0; t < TMAX; ++t)
+        if (t < T) load_vec<SPK_F32, VEC>(gs, (int64_t)t * N + col, gpre[t]);
+    }
 #pragma unroll
     for (int i = 0; i < VEC; ++i) v[i] = 0.0f;
     // pass 1: recompute the pre-reset membrane (Lif.py:222-233)
@@ -220,7 +229,12 @@ __global__ void __launch_bounds__(kBwdThreads) lif_bwd_kernel(
     for (int t = TMAX - 1; t >= 0; --t) {
       if (t < T) {
         float gsv[VEC], out[VEC];
-        load_vec<SPK_F32, VEC>(gs, (int64_t)t * N + col, gsv);
+        if constexpr (kPreload) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) gsv[i] = gpre[kPreload ? t : 0][i];
+        } else {
+          load_vec<SPK_F32, VEC>(gs, (int64_t)t * N + col, gsv);
+        }
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
           const bool s = (sbits[t] >> i) & 1u;
@@ -325,7 +339,10 @@ template <int XDT, int SDT>
 int dispatch_bwd_t(int T, bool vec, int grid, const float* gs, const float* gvf, const void* x, const void* s,
                    const float* b, const float* th, const float* vr, float gain, int surr, float k, float c,
                    void* gx, float* part, int64_t N, cudaStream_t st) {
-  if (T <= 8) {
+  if (T <= 4) {
+    if (vec) launch_bwd<XDT, SDT, 4, 4>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+    else launch_bwd<XDT, SDT, 4, 1>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
+  } else if (T <= 8) {
     if (vec) launch_bwd<XDT, SDT, 8, 4>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
     else launch_bwd<XDT, SDT, 8, 1>(grid, gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx, part, T, N, st);
   } else if (T <= 16) {

@@ -135,6 +135,64 @@ def linear_ln_lif(A, W, bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_
     return spikes, ln_out
 
 
+def linear_affine_lif(A, W, bias, scale, shift, lif_beta, lif_vth, lif_vr, T, in_gain=1.0, t_broadcast=False,
+                      spike_dtype=torch.bfloat16, residual=None, want_spikes=True):
+    """Fused ``LIF((A @ W.T + bias) * scale + shift)`` over the t-major fold
+    (per-feature affine, e.g. an eval-mode BatchNorm; no row statistics).
+
+    ``A``: bf16 ``[T*R, K]`` (or ``[R, K]`` with ``t_broadcast``); ``W``: bf16
+    ``[N, K]``.  Returns the spikes ``[T*R, N]`` (or None when only the
+    ``residual`` (bf16 ``[T*R, N]``) is updated, in place)."""
+    _cuda(A, W, residual)
+    if A.dtype != torch.bfloat16 or W.dtype != torch.bfloat16:
+        raise TypeError("linear_affine_lif expects bf16 A and W")
+    A = A.contiguous()
+    W = W.contiguous()
+    K = A.shape[-1]
+    N = W.shape[0]
+    rows = A.numel() // K
+    R = rows if t_broadcast else rows // T
+    if not t_broadcast and rows % T:
+        raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
+    dev = A.device
+    spikes = torch.empty((T * R, N), dtype=spike_dtype, device=dev) if want_spikes else None
+    if residual is not None and (residual.dtype != torch.bfloat16 or not residual.is_contiguous()):
+        raise TypeError("residual must be a contiguous bf16 tensor")
+    f = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    bias, scale, shift = f(bias), f(scale), f(shift)
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_linear_affine_lif_fwd", _lib.ptr(A), _lib.ptr(W), _lib.ptr(bias), _lib.ptr(scale), _lib.ptr(shift),
+              _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, R, K, N, 1 if t_broadcast else 0,
+              _lib.ptr(spikes), _lib.DTYPE_CODE[spike_dtype], _lib.ptr(residual), _lib.stream_ptr(dev),
+              tag="linear_affine_lif K=%d N=%d rows=%d%s" % (K, N, rows, " +residual" if residual is not None else ""),
+              work=dict(flops=2.0 * rows * K * N,
+                        bytes=(rows * K + N * K) * 2 + T * R * N * (spikes.element_size() if want_spikes else 0)
+                        + (4 * T * R * N if residual is not None else 0)))
+    return spikes
+
+
+def im2col(x, kernel, stride=(1, 1), padding=(0, 0)):
+    """Patches of a channels-last ``x`` ``[N, H, W, C]`` (bf16, or fp32 split
+    into hi | lo bf16 terms) for a ``kernel = (kh, kw)`` convolution: bf16
+    ``[N*Ho*Wo, kh*kw*C]`` (``2*kh*kw*C`` for fp32), column ``(i*kw + j)*C + c``."""
+    _cuda(x)
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    x = x.contiguous()
+    N, H, W, C = x.shape
+    kh, kw = kernel
+    sh, sw = stride
+    ph, pw = padding
+    Ho = (H + 2 * ph - kh) // sh + 1
+    Wo = (W + 2 * pw - kw) // sw + 1
+    K = kh * kw * C * (2 if x.dtype == torch.float32 else 1)
+    out = torch.empty((N * Ho * Wo, K), dtype=torch.bfloat16, device=x.device)
+    _lib.call("spk_im2col", _lib.ptr(x), _lib.dtype_code(x), N, H, W, C, kh, kw, sh, sw, ph, pw, _lib.ptr(out),
+              _lib.stream_ptr(x.device), tag="im2col",
+              work=dict(bytes=x.numel() * x.element_size() + out.numel() * 2))
+    return out
+
+
 def ln_lif_ok(T, D):
     """Shapes the fused LayerNorm -> LIF training kernels take."""
     return 1 <= T <= 4 and D % 32 == 0 and 32 <= D <= 2048 and (D <= 512 or D % 128 == 0)

@@ -79,47 +79,65 @@ def _dp_worker(rank, ws, port, out):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
-    import bench
+    from spikingtransformer_b200.dp import BucketedGradReducer
     dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=60))
     try:
         results = []
-        for mode in ("ddp", "flat"):
+        for mode in ("ddp", "buckets_fp32", "buckets_bf16"):
             torch.manual_seed(0)  # same initial weights on every rank
-            model = torch.nn.Sequential(torch.nn.Linear(12, 16), torch.nn.Tanh(), torch.nn.Linear(16, 3))
-            net = torch.nn.parallel.DistributedDataParallel(model) if mode == "ddp" else model
-            opt = torch.optim.AdamW(model.parameters(), lr=1e-2)
-            flat = bench.flat_grad_views(list(model.parameters()), torch.device("cpu")) if mode == "flat" else None
+            model = torch.nn.Sequential(torch.nn.Linear(12, 16), torch.nn.Tanh(), torch.nn.Linear(16, 16),
+                                        torch.nn.Tanh(), torch.nn.Linear(16, 3))
+            unused = torch.nn.Parameter(torch.zeros(5))  # never receives a gradient
+            params = list(model.parameters()) + [unused]
+            net, reducer = model, None
+            if mode == "ddp":
+                net = torch.nn.parallel.DistributedDataParallel(model)
+            else:
+                # buckets of about 50 elements: several per backward
+                reducer = BucketedGradReducer(params, bucket_elems=50,
+                                              comm_dtype=torch.float32 if mode == "buckets_fp32" else torch.bfloat16)
+                assert len(reducer.buckets) >= 3
+            # plain SGD keeps the update linear in the gradient, so the bf16
+            # rounding of the buckets shows at its own size
+            opt = torch.optim.SGD(model.parameters(), lr=0.1)
             for step in range(3):
                 g = torch.Generator().manual_seed(100 * rank + step)  # each rank its own batch
                 x, y = torch.randn(8, 12, generator=g), torch.randn(8, 3, generator=g)
-                if flat is not None:
-                    flat.zero_()
+                if reducer is not None:
+                    reducer.begin()
                 else:
                     opt.zero_grad(set_to_none=True)
                 torch.nn.functional.mse_loss(net(x), y).backward()
-                if flat is not None:
-                    bench.average_flat_grads(flat, ws)
+                if reducer is not None:
+                    reducer.finish()
                 opt.step()
-            if flat is not None:
+            if reducer is not None:
                 # the gradients are still the views the optimizer read
-                assert all(p.grad.data_ptr() >= flat.data_ptr() for p in model.parameters())
+                assert all(p.grad.data_ptr() >= reducer.flat.data_ptr() for p in model.parameters())
+                assert float(unused.grad.abs().sum()) == 0.0
+                reducer.remove()
             results.append(torch.cat([p.detach().reshape(-1) for p in model.parameters()]).tolist())
         out[rank] = results
     finally:
         dist.destroy_process_group()
 
 
-def test_flat_gradient_data_parallel_matches_ddp():
+def test_bucketed_gradient_reducer_matches_ddp():
     """The training bench's multi-GPU step (gradients as views into one flat
-    buffer, one all-reduce, divided by the world size) updates the weights as
-    DistributedDataParallel does, and identically on every rank."""
+    buffer, buckets all-reduced as the backward completes them, divided by the
+    world size) updates the weights as DistributedDataParallel does: to fp32
+    rounding with fp32 buckets, to bf16 rounding with the bf16 buckets the
+    benchmark sends; and identically on every rank, including a parameter that
+    receives no gradient."""
     ws = 2
     port = _free_port()
     with mp.Manager() as mgr:
         out = mgr.dict()
         mp.start_processes(_dp_worker, args=(ws, port, out), nprocs=ws, join=True, start_method="spawn")
         res = dict(out)
-    ddp0, flat0 = (torch.tensor(v) for v in res[0])
-    ddp1, flat1 = (torch.tensor(v) for v in res[1])
-    assert torch.equal(flat0, flat1) and torch.equal(ddp0, ddp1)
-    assert torch.allclose(flat0, ddp0, rtol=1e-5, atol=1e-6)
+    ddp0, f32_0, bf16_0 = (torch.tensor(v) for v in res[0])
+    ddp1, f32_1, bf16_1 = (torch.tensor(v) for v in res[1])
+    assert torch.equal(f32_0, f32_1) and torch.equal(bf16_0, bf16_1) and torch.equal(ddp0, ddp1)
+    assert torch.allclose(f32_0, ddp0, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(bf16_0, ddp0, rtol=0, atol=1e-3)
+    assert not torch.equal(bf16_0, f32_0)

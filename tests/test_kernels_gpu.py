@@ -318,6 +318,58 @@ def test_patch_embed_split(ops):
     assert torch.allclose(out.cpu(), ref, rtol=2e-5, atol=2e-5)
 
 
+# ------------------------------------------------------------------ convolution patches, affine -> LIF
+
+
+@pytest.mark.parametrize("N,H,W,C,k,s,pd,dtype", [
+    (3, 8, 20, 64, (3, 3), (1, 1), (1, 1), torch.bfloat16),   # bottleneck 3x3 (16-byte chunks)
+    (2, 32, 40, 1, (12, 12), (4, 4), (4, 4), torch.float32),  # PixelUnshuffle(4) + 3x3 on the image, split
+    (4, 8, 9, 64, (8, 1), (1, 1), (0, 0), torch.bfloat16),    # the (channel, height) fold of the reduce block
+    (5, 1, 33, 32, (1, 3), (1, 1), (0, 1), torch.bfloat16),   # Conv1d k=3 of the position encoding
+    (2, 5, 7, 3, (3, 2), (2, 1), (1, 0), torch.bfloat16),     # odd channels: per-element path
+])
+def test_im2col_matches_unfold(ops, N, H, W, C, k, s, pd, dtype):
+    g = gen(N * H + C)
+    x = (torch.rand(N, C, H, W, generator=g) * 3).floor() if dtype == torch.bfloat16 else \
+        torch.rand(N, C, H, W, generator=g)
+    out = ops.im2col(x.permute(0, 2, 3, 1).to(dtype).to(DEV), k, s, pd).cpu()
+    cols = F.unfold(x, k, padding=pd, stride=s)                          # [N, C*kh*kw, L], (c, i, j)
+    L = cols.shape[-1]
+    ref = cols.view(N, C, k[0] * k[1], L).permute(0, 3, 2, 1).reshape(N * L, -1)  # (i, j, c) columns
+    if dtype == torch.float32:
+        hi = ref.to(torch.bfloat16)
+        ref = torch.cat([hi, (ref - hi.float()).to(torch.bfloat16)], dim=1)
+    assert torch.equal(out, ref.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("T,R,K,N,tb,res", [
+    (4, 300, 576, 512, False, False),   # bottleneck 3x3 64 -> 512 (2-CTA cluster, no statistics exchange)
+    (4, 200, 512, 64, False, True),     # bottleneck 1x1 512 -> 64 + identity
+    (4, 150, 288, 128, True, False),    # first convolution, once per image, LIF at every step
+    (3, 77, 96, 32, False, True),
+])
+def test_linear_affine_lif(ops, T, R, K, N, tb, res):
+    g = gen(T * R + K + N)
+    rows = R if tb else T * R
+    A = (torch.rand(rows, K, generator=g) < 0.3).to(torch.bfloat16)
+    W = (torch.randn(N, K, generator=g) / K ** 0.5).to(torch.bfloat16)
+    bias = 0.1 * torch.randn(N, generator=g)
+    scale = 1.0 + 0.3 * torch.randn(N, generator=g)
+    shift = 0.2 * torch.randn(N, generator=g) + 0.5
+    pre = (A.float() @ W.float().t() + bias) * scale + shift
+    y3 = pre.unsqueeze(0).expand(T, *pre.shape).reshape(T, -1) if tb else pre.reshape(T, -1)
+    s_ref, _ = oracle.lif_forward(y3, 0.5, 1.0, 0.0)
+    vh = membrane_history(y3, 0.5, 1.0, 0.0)
+    resid = torch.randint(0, 3, (T * R, N), generator=g).to(torch.bfloat16) if res else None
+    r_dev = resid.to(DEV) if res else None
+    s = ops.linear_affine_lif(A.to(DEV), W.to(DEV), bias.to(DEV), scale.to(DEV), shift.to(DEV), 0.5, 1.0, 0.0, T,
+                              t_broadcast=tb, residual=r_dev, want_spikes=not res)
+    if res:
+        assert s is None
+        s = r_dev.float().cpu() - resid.float()
+    assert_spikes_match(s.float().cpu().reshape(T, -1), s_ref, vh, 1.0, what="affine lif spikes")
+
+
 # ------------------------------------------------------------------ SSA
 
 
@@ -440,8 +492,8 @@ def test_bounded_wait_gives_up_and_reports_timeout(ops):
         ops.device_error_check()
     ops.device_error_check()  # cleared
     x = torch.ones(2, 8, device=DEV)
-    s, _ = ops.lif_fwd(x, 0.5, 0.75, 0.0)  # the device still runs work
-    assert s.sum().item() == 8.0
+    s, _ = ops.lif_fwd(x, 0.5, 0.75, 0.0)  # the device still runs work: v = 1 > 0.75 fires at both steps
+    assert s.sum().item() == 16.0
     assert lib.spk_test_bounded_wait(0, st) == 1  # SPK_ERR_INVALID
 
 

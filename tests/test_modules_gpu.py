@@ -250,6 +250,65 @@ def test_seq2seq_cnn_golden(pkg, golden_dir):
     assert close > 0.95, close
 
 
+def _cnn_pair(D=64, nb_layers=2, T=4, seed=5):
+    """CNNBackbone (ours on the GPU, the oracle's on the CPU) with bf16-rounded
+    convolution weights and non-trivial BatchNorm statistics, in eval mode."""
+    from spikingtransformer_b200.ImageEncoder import CNNBackbone
+    torch.manual_seed(seed)
+    ours = CNNBackbone(d_model=D, nb_layers=nb_layers, patch_size=4, n_steps=T)
+    with torch.no_grad():
+        for m in ours.modules():
+            if isinstance(m, (torch.nn.Conv2d, torch.nn.Conv1d)):
+                m.weight.copy_((m.weight * 3).to(torch.bfloat16).float())
+            if isinstance(m, (torch.nn.BatchNorm2d, torch.nn.BatchNorm1d)):
+                m.running_mean.uniform_(-0.2, 0.2)
+                m.running_var.uniform_(0.5, 1.5)
+                m.weight.uniform_(0.8, 1.2)
+                m.bias.uniform_(0.2, 0.6)
+    ref = om.CNNBackbone(d_model=D, nb_layers=nb_layers, patch_size=4, n_steps=T)
+    ref.load_state_dict(ours.state_dict())
+    return ours.to(DEV).eval(), ref.eval()
+
+
+def test_cnn_backbone_fused_matches_oracle(pkg):
+    """The CNN image encoder in eval mode on this package's kernels (patch
+    gathers, tcgen05 GEMMs with the BatchNorm affine and LIF epilogue), no
+    library convolution: the first convolution's spikes bit-exact outside the
+    near-threshold band, the output tokens within the whole-stack bound, and
+    the once-per-image path equal to the T-fold path."""
+    T, B = 4, 3
+    ours, ref = _cnn_pair()
+    src = synthetic_lines(B, 21, H=32, W=128)
+    x = src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:])
+    with torch.no_grad():
+        y, rec = ours(x.to(DEV))
+        y_ref, rec_ref = ref(x)
+        pre1 = ref.bn1(ref.conv1(ref.space_to_depth(x)))
+        once = ours.encode_images(src.to(DEV), T)
+    assert y.shape == y_ref.shape and y.dtype == torch.float32
+    vh = membrane_history(pre1.reshape(T, -1), 0.5, 1.0, 0.0)
+    assert_spikes_match(rec["conv1"].float().reshape(T, -1), rec_ref["conv1"].reshape(T, -1), vh, 1.0,
+                        what="conv1 spikes")
+    rate = spike_mismatch_rate(y, y_ref)
+    assert rate < 0.01, rate
+    assert torch.equal(once.float(), y)
+
+
+def test_cnn_backbone_runs_no_library_convolution(pkg):
+    ours, _ = _cnn_pair(nb_layers=1)
+    x = synthetic_lines(4, 22, H=32, W=128).to(DEV)
+    with torch.no_grad():
+        ours(x)
+        torch.cuda.synchronize()
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            ours(x)
+            torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("gemm_ln_lif_kernel" in n for n in names), names[:20]
+    library_conv = [n for n in names if ("cudnn" in n.lower() or "conv" in n.lower()) and "spk::" not in n]
+    assert not library_conv, library_conv
+
+
 def _bench_models(seed=0, enc_layers=8, dec_layers=4, T=4):
     """The OCR benchmark architecture (D=384, H=8, F=1536, patch 16, vocab 256),
     bf16-rounded random weights, ours on the GPU and the oracle on the CPU."""
