@@ -221,16 +221,32 @@ def peak_for(bound, peaks, peak_src, clocks):
 
 
 def roofline_entry(tag, rec, bound, peaks, peak_src, clocks):
-    """achieved / peak of one launch kind from its recorded device time."""
+    """achieved / peak of one launch kind from its recorded device time.
+
+    ``bound`` None picks the binding roofline: the one whose minimum time for
+    the launch's algorithmic work is longer (the fused GEMMs at K = N = 384
+    move more bytes per FLOP than the bf16 ridge point and are HBM-bound).
+    Both fractions are reported."""
     per_launch_s = rec["ms"] / rec["launches"] / 1000.0
-    peak, kind = peak_for(bound, peaks, peak_src, clocks)
+    flops = rec["flops"] / rec["launches"]
+    nbytes = rec["bytes"] / rec["launches"]
+    t_peak, t_kind = peak_for("tensor", peaks, peak_src, clocks)
+    h_peak, h_kind = peak_for("hbm", peaks, peak_src, clocks)
+    t_min_tensor = flops / (t_peak * 1e12)
+    t_min_hbm = nbytes / (h_peak * 1e9)
+    if bound is None:
+        bound = "tensor" if t_min_tensor >= t_min_hbm else "hbm"
     if bound == "tensor":
-        achieved, unit = rec["flops"] / rec["launches"] / per_launch_s / 1e12, "TFLOP/s"
+        achieved, unit, peak, kind = flops / per_launch_s / 1e12, "TFLOP/s", t_peak, t_kind
     else:
-        achieved, unit = rec["bytes"] / rec["launches"] / per_launch_s / 1e9, "GB/s"
-    return {"kernel": tag, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-            "peak_kind": kind, "ms_per_launch": per_launch_s * 1000.0, "launches_timed": rec["launches"],
-            "algorithmic_bytes": rec["bytes"] / rec["launches"], "algorithmic_flops": rec["flops"] / rec["launches"]}
+        achieved, unit, peak, kind = nbytes / per_launch_s / 1e9, "GB/s", h_peak, h_kind
+    e = {"kernel": tag, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+         "peak_kind": kind, "ms_per_launch": per_launch_s * 1000.0, "launches_timed": rec["launches"],
+         "algorithmic_bytes": nbytes, "algorithmic_flops": flops}
+    if flops > 0 and nbytes > 0:
+        e["frac_tensor"] = t_min_tensor / per_launch_s
+        e["frac_hbm"] = t_min_hbm / per_launch_s
+    return e
 
 
 def config_kernels(dev, peaks, peak_src):
@@ -302,7 +318,7 @@ def config_kernels(dev, peaks, peak_src):
     bias = (torch.rand(N, generator=g, device=dev) * 2 - 1) * 0.01
     ones, zeros = torch.ones(N, device=dev), torch.zeros(N, device=dev)
     ms = timed(lambda i: ops.linear_ln_lif(As[i % 6], W, bias, ones, zeros, 1e-5, 0.5, 1.0, 0.0, T, in_gain=0.5), 20)
-    add("linear_ln_lif [32768, 384] x [384, 1536] -> bf16 spikes", "tensor", ms,
+    add("linear_ln_lif [32768, 384] x [384, 1536] -> bf16 spikes", None, ms,
         nbytes=(T * R * K + N * K) * 2 + T * R * N * 2, flops=2.0 * T * R * K * N)
     del As
     # ---- attention core + LIF
@@ -520,7 +536,8 @@ def run_train(args, ws, rank, local):
                        "loss": "mean over T of CE(ignore_index=0, label_smoothing=0.1), fused with token accuracy",
                        "parallelism": ("dp%d (bf16 gradient buckets all-reduced over NCCL on a side stream as the "
                                        "backward completes them, inside the CUDA graph)" % ws if reducer is not None
-                                       else "ddp%d (NCCL all-reduce of bf16-compressed gradient buckets)" % ws)},
+                                       else "ddp%d (NCCL all-reduce of bf16-compressed gradient buckets)" % ws
+                                       if ws > 1 else "single GPU")},
             "loss": last, "token_accuracy": last_acc, "clocks": clk.summary(),
             "cuda_graph": use_graph, "graph_launches_per_step": graph_launches,
             "gpu_launches": sum(v["launches"] for v in kernels.values()) + (graph_launches or 0) * args.steps,
@@ -715,9 +732,10 @@ def main():
     peaks, peak_src = measured_peaks()
 
     def bound_of(tag):
-        # the attention kernels are memory-bound (score-free regrouping); the
-        # fused GEMMs are contractions
-        return "tensor" if kernels[tag]["flops"] > 0 and not tag.startswith("ssa") else "hbm"
+        # the attention kernels are memory-bound (score-free regrouping, FLOPs
+        # counted dense-equivalent); for the fused GEMMs the binding roofline
+        # of each shape is picked from its FLOPs and bytes
+        return "hbm" if tag.startswith("ssa") or kernels[tag]["flops"] == 0 else None
 
     # dominant kernel = largest total device time per step
     dom_tag, dom = max(kernels.items(), key=lambda kv: kv[1]["ms"])

@@ -287,6 +287,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     float mem[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) mem[i] = 0.0f;
+    // dense masks read as 16-byte vectors are loaded one unit ahead (the 32
+    // mask bytes of this thread's row and key columns), so their latency
+    // hides behind the previous unit's work
+    const bool mask_pf = p.mask_mode == 2 && p.mask_vec && kc0 + 32 <= p.Nk;
+    auto mask_load = [&](int gg, uint4& m0, uint4& m1) {
+      const int it = (int)blockIdx.x + (gg / p.T) * (int)gridDim.x, tt = gg % p.T;
+      const int bhh = 2 * it + slot;
+      m0 = make_uint4(0u, 0u, 0u, 0u);
+      m1 = m0;
+      if (bhh < BH && qi < p.Nq) {
+        const int b = bhh / p.H, h = bhh % p.H;
+        const uint4* mrow = reinterpret_cast<const uint4*>(p.mask + tt * p.m_st + b * p.m_sb + h * p.m_sh +
+                                                           (int64_t)qi * p.m_sq + kc0);
+        m0 = __ldg(mrow);
+        m1 = __ldg(mrow + 1);
+      }
+    };
+    uint4 pm0 = make_uint4(0u, 0u, 0u, 0u), pm1 = pm0;
+    if (mask_pf && G > 0) mask_load(0, pm0, pm1);
     bool ok = true;
     for (int g = 0; g <= G && ok; ++g) {
       if (g < G) {
@@ -294,6 +313,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = g & 1;
         const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
         const int bh = 2 * item + slot;
+        uint32_t pf_bits = 0u;
+        if (mask_pf) {
+          const uint32_t w[8] = {pm0.x, pm0.y, pm0.z, pm0.w, pm1.x, pm1.y, pm1.z, pm1.w};
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pf_bits |= (((w[i >> 2] >> ((i & 3) * 8)) & 0xffu) != 0u ? 1u : 0u) << i;
+          if (g + 1 < G) mask_load(g + 1, pm0, pm1);
+        }
         if (!mbar_wait(&sm.full[s], (g >> 1) & 1, 161)) { ok = false; break; }
         if (p.mode == 1) {
           if (half == 0)
@@ -315,7 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float c_row = p.mode == 1 ? sm.cq[s * 128 + row] : 0.0f;
         const float* ks = sm.ks + s * 128 + slot * 64;
         uint32_t mbits = 0xffffffffu;  // keep bit per key column of this warp
-        if (p.mask_mode == 2) {
+        if (mask_pf) {
+          mbits = pf_bits;
+        } else if (p.mask_mode == 2) {
           mbits = 0u;
           if (bh < BH && qi < p.Nq) {
             const int b = bh / p.H, h = bh % p.H;

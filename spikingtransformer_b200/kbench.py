@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks at the benchmark shapes (CUDA events, device time).
 
-    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|data|shapes|lnlif] [--iters N]
+    python -m spikingtransformer_b200.kbench [--only lif|gemm|ssa|ssa_model|data|shapes|lnlif] [--iters N]
 
   lif   LIF forward on [T=4, 64*256, 1536] fp32 input -> bf16 and packed-bit
         spikes (the MLP expansion LIF of a 64-image batch), and the backward
@@ -12,6 +12,9 @@
         causal N=64 case; FLOPs counted dense (QK^T and PV); and the n-major
         copy of V [2048, 256, 48] bf16 that the training path's R V reads,
         beside torch's permute copy.
+  ssa_model  the forward's three attention calls at the bench batch (256
+        images): encoder self 256 x 256, decoder cross 64 x 256, decoder
+        self 64 x 64 with the dense look-ahead mask; bound: HBM bytes.
 Inputs are regenerated per configuration; each timed iteration rotates over
 input copies whose total exceeds the 126 MB L2.  Prints one JSON line.
 """
@@ -91,20 +94,27 @@ def bench_gemm(iters, N=1536, K=384, T=4, R=32 * 256):
             "flops": flops}
 
 
-def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48):
+def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48, Nk=None, dense_mask=False):
+    """``dense_mask``: the decoder's call, a [B, 1, N, N] look-ahead mask
+    passed as uint8 and broadcast over T and heads (strides 0)."""
+    Nk = N if Nk is None else Nk
     g = torch.Generator(device="cuda").manual_seed(1)
     copies = 2
-    mk = lambda: (torch.rand(T * B, N, H * d, device="cuda", generator=g) < 0.15).to(torch.bfloat16)  # noqa: E731
-    qkv = [(mk(), mk(), mk()) for _ in range(copies)]
+    mk = lambda n: (torch.rand(T * B, n, H * d, device="cuda", generator=g) < 0.15).to(torch.bfloat16)  # noqa
+    qkv = [(mk(N), mk(Nk), mk(Nk)) for _ in range(copies)]
     scale = 0.125 if variant == 0 else (1.0 / d) ** 0.5
+    mask = ops.mask_to_u8(torch.tril(torch.ones(N, Nk, device="cuda")).expand(B, 1, N, Nk), T, B, H, N, Nk) \
+        if dense_mask else None
 
     def run(i):
         q, k, v = qkv[i % copies]
-        ops.ssa(q, k, v, T, B, H, variant, scale, 0.5, 0.5, 0.0, in_gain=0.5, causal=causal)
+        ops.ssa(q, k, v, T, B, H, variant, scale, 0.5, 0.5, 0.0, in_gain=0.5, causal=causal, mask=mask)
     ms = _time(run, iters)
-    flops = 4.0 * T * B * H * N * N * d
+    flops = 4.0 * T * B * H * N * Nk * d
+    nbytes = 2.0 * T * B * H * d * (2 * N + 2 * Nk)
     return {"kernel": "ssa", "variant": "plain" if variant == 0 else "xnor", "causal": causal,
-            "shape": [T, B, H, N, d], "ms": ms, "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops}
+            "dense_mask": dense_mask, "shape": [T, B, H, N, Nk, d], "ms": ms,
+            "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops, "GB/s": nbytes / ms / 1e6}
 
 
 def bench_n_major(iters, B=2048, N=256, d=48):
@@ -218,7 +228,8 @@ def bench_lnlif(iters, R=16384, T=4):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "data", "shapes", "lnlif"])
+    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "ssa_model", "data", "shapes", "lnlif"])
+    ap.add_argument("--ssa-batch", type=int, default=256, help="images for --only ssa_model")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
     ap.add_argument("--lif-neurons", type=int, default=64 * 256 * 1536, help="neurons per step for the LIF scan")
@@ -239,6 +250,14 @@ def main():
         for n, k in ((1536, 384), (384, 384), (384, 1536)):
             r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)
             r["frac_tensor"] = r["TFLOP/s"] / peaks["bf16_tflops_sustained"]
+            out["results"].append(r)
+    if a.only == "ssa_model":
+        # the three attention calls of the forward at the bench batch: encoder
+        # self (256 x 256), decoder cross (64 x 256), decoder self (64 x 64,
+        # dense look-ahead mask), XNOR form
+        for N, Nk, dm in ((256, 256, False), (64, 256, False), (64, 64, True)):
+            r = bench_ssa(a.iters, 1, N=N, Nk=Nk, B=a.ssa_batch, dense_mask=dm)
+            r["frac_hbm"] = r["GB/s"] / peaks["hbm_gbs"]
             out["results"].append(r)
     if a.only in (None, "ssa"):
         for variant in (0, 1):
