@@ -24,6 +24,9 @@
  *                          SpikingMLP.py:31-36 (expand, compress), plus the
  *                          residual adds Encoder.py:19,22 / Decoder.py:18-25
  *   spk_linear_fwd         Seq2Seq.py:117 output_layer (nn.Linear)
+ *   spk_linear_dgrad,      input and weight gradients of the Linear layers
+ *   spk_linear_wgrad       (autograd of nn.Linear at SSA.py:218-249,
+ *                          SpikingMLP.py:31-36 in train_spikeformer.py:545-561)
  *   spk_ssa_fwd            attention core of SSAMultiHeadAttention.forward,
  *                          SSA.py:230-245 (xnor_attention :145-165, log-PE
  *                          :177-201, mask, scale, @V, lifs) and of
@@ -250,6 +253,24 @@ int spk_linear_affine_lif_fwd(const void* A, const void* W, const float* bias, c
  */
 int spk_im2col(const void* x, int x_dtype, int64_t N, int64_t H, int64_t W, int64_t C, int64_t kh, int64_t kw,
                int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, void* out, void* stream);
+
+/*
+ * Gradients of a bias-free Linear y[M][N] = x[M][K] W[N][K]^T for the
+ * training path (autograd of nn.Linear in SSA.py:218-249 and
+ * SpikingMLP.py:31-36 under the reference's autocast, train_spikeformer.py:545):
+ *   spk_linear_dgrad:  dX[M][K] = G[M][N] W[N][K]        (fp32 out)
+ *   spk_linear_wgrad:  dW[N][K] = G[M][N]^T X[M][K]      (fp32 out)
+ * G, W, X bf16, row-major as torch holds them: the tcgen05 operands read W
+ * (dgrad) and G, X (wgrad) contiguous along their output dimension, so no
+ * transposed copy is made.  The weight gradient splits the sum over the M
+ * rows across CTAs into fp32 partial sums in `workspace`
+ * (spk_linear_wgrad_workspace_bytes(M, N, K) bytes, possibly 0), reduced in a
+ * fixed order.  N and K multiples of 8; pointers 16-byte aligned.
+ */
+int spk_linear_dgrad(const void* G, const void* W, float* dX, int64_t M, int64_t N, int64_t K, void* stream);
+int64_t spk_linear_wgrad_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int spk_linear_wgrad(const void* G, const void* X, float* dW, void* workspace, int64_t workspace_bytes, int64_t M,
+                     int64_t N, int64_t K, void* stream);
 
 /* out[M][N] (fp32) = A[M][K] W[N][K]^T + bias (bias may be NULL); bf16 A, W. */
 int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, int64_t M, int64_t K, int64_t N,

@@ -40,6 +40,9 @@ SIGNATURES = {
     "spk_linear_ln_lif_fwd": ([_p, _p, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _p, _i, _p,
                                _p, _p], _i),
     "spk_linear_fwd": ([_p, _p, _p, _p, _i64, _i64, _i64, _p], _i),
+    "spk_linear_dgrad": ([_p, _p, _p, _i64, _i64, _i64, _p], _i),
+    "spk_linear_wgrad_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "spk_linear_wgrad": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
     "spk_linear_affine_lif_fwd": ([_p, _p, _p, _p, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _p, _i, _p, _p],
                                   _i),
     "spk_im2col": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p], _i),

@@ -73,6 +73,13 @@ struct Params {
   float* out_f32;           // PLAIN: [R][N]
   int vec_out;              // PLAIN: N % 4 == 0 and out, bias 16-byte aligned
   int norm;                 // TCOUPLED / TBCAST: 1 LayerNorm over the N features, 0 per-feature affine only
+  // PLAIN only: operand layouts and split K
+  int a_mn;                 // A stored [K][M] (contiguous along M) instead of [M][K]
+  int b_mn;                 // W stored [K][N] (contiguous along N) instead of [N][K]
+  int k_splits;             // the K blocks are split over this many tiles, each writing partial sums
+  int kb_per_split;         // K blocks (of kBK) per split
+  int64_t split_stride;     // elements between the outputs of consecutive splits
+  int nacc;                 // TMEM accumulators (2: the MMA of tile i+1 runs while the epilogue drains tile i)
 };
 
 struct Smem {
@@ -112,7 +119,7 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   size_t ox = take((size_t)2 * p.cs * 128 * 2 * 4, 16);
   size_t ofull = take(p.stages * 8, 8);
   size_t oempty = take(p.stages * 8, 8);
-  size_t oaf = take(8, 8), oae = take(8, 8), oxb = take(16, 8), odr = take(8, 8);
+  size_t oaf = take(16, 8), oae = take(16, 8), oxb = take(16, 8), odr = take(8, 8);
   size_t otm = take(4, 4), oab = take(4, 4);
   if (s) {
     s->a = base + oa;
@@ -160,16 +167,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cs > 1 ? cluster_ctarank() : 0u;
   const int cid = cs > 1 ? (int)cluster_id_x() : (int)blockIdx.x;
   const int ncl = cs > 1 ? (int)cluster_count_x() : (int)gridDim.x;
-  const int total_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int mn_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int ksplits = (MODE == MODE_PLAIN && p.k_splits > 1) ? p.k_splits : 1;
+  const int total_tiles = mn_tiles * ksplits;
   const int nk = (p.K + kBK - 1) / kBK;
+  // K blocks [kc_lo, kc_hi) of a tile (split K: tile / mn_tiles is the split)
+  auto k_range = [&](int tile, int& kc_lo, int& kc_hi) {
+    if (ksplits > 1) {
+      kc_lo = (tile / mn_tiles) * p.kb_per_split;
+      kc_hi = min(nk, kc_lo + p.kb_per_split);
+    } else {
+      kc_lo = 0;
+      kc_hi = nk;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
-    mbar_init(sm.acc_full, 1);
-    mbar_init(sm.acc_empty, kEpiThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.acc_full[i], 1);
+      mbar_init(&sm.acc_empty[i], kEpiThreads);
+    }
     mbar_init(&sm.xbar[0], 4 * cs);
     mbar_init(&sm.xbar[1], 4 * cs);
     mbar_init(sm.drain, 1);
@@ -212,21 +233,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       int outstanding[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint32_t issued_phase[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int tile = cid; tile < total_tiles && ok; tile += ncl) {
-        const int mt = tile / p.num_n_tiles;
-        const int n0 = (MODE == MODE_PLAIN) ? (tile % p.num_n_tiles) * p.n_cta : (int)rank * p.n_cta;
-        for (int kc = 0; kc < nk; ++kc) {
+        const int tmn = tile % mn_tiles;
+        const int mt = tmn / p.num_n_tiles;
+        const int n0 = (MODE == MODE_PLAIN) ? (tmn % p.num_n_tiles) * p.n_cta : (int)rank * p.n_cta;
+        int kc_lo, kc_hi;
+        k_range(tile, kc_lo, kc_hi);
+        for (int kc = kc_lo; kc < kc_hi; ++kc) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1u, 11)) { ok = false; break; }
           outstanding[stage] = 0;
           if (*((volatile int*)sm.abort_flag)) { ok = false; break; }
           mbar_expect_tx(&sm.full[stage], a_bytes + w_bytes);
           uint8_t* a_dst = sm.a + (size_t)stage * kAStageBytes;
-          if (MODE == MODE_TCOUPLED)
+          if (MODE == MODE_TCOUPLED) {
             tma_load_3d(a_dst, &tmA, &sm.full[stage], kc * kBK, mt * p.tpt, 0);
-          else
+          } else if (MODE == MODE_PLAIN && p.a_mn) {
+            // A [K][M]: two 64 (m) x 64 (k) atoms, 128-byte rows along m
+            tma_load_2d(a_dst, &tmA, &sm.full[stage], mt * 128, kc * kBK);
+            tma_load_2d(a_dst + 8192, &tmA, &sm.full[stage], mt * 128 + 64, kc * kBK);
+          } else {
             tma_load_2d(a_dst, &tmA, &sm.full[stage], kc * kBK, mt * 128);
+          }
           uint8_t* w_dst = sm.w + (size_t)stage * p.n_cta * 128;
-          for (int r = 0; r < p.n_cta; r += p.wbox)
-            tma_load_2d(w_dst + (size_t)r * 128, &tmW, &sm.full[stage], kc * kBK, n0 + r);
+          if (MODE == MODE_PLAIN && p.b_mn) {
+            // W [K][N]: n_cta / 64 atoms of 64 (n) x 64 (k)
+            for (int j = 0; j < p.n_cta; j += 64)
+              tma_load_2d(w_dst + (size_t)j * 128, &tmW, &sm.full[stage], n0 + j, kc * kBK);
+          } else {
+            for (int r = 0; r < p.n_cta; r += p.wbox)
+              tma_load_2d(w_dst + (size_t)r * 128, &tmW, &sm.full[stage], kc * kBK, n0 + r);
+          }
           outstanding[stage] = 1;
           issued_phase[stage] = phase;
           if (++stage == p.stages) { stage = 0; phase ^= 1u; }
@@ -242,13 +277,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     int stage = 0;
-    uint32_t phase = 0, acc_phase = 0;
+    uint32_t phase = 0;
+    int it = 0;
     bool ok = true;
     const int nsub_max = 256;
-    for (int tile = cid; tile < total_tiles && ok; tile += ncl) {
-      if (!mbar_wait(sm.acc_empty, acc_phase ^ 1u, 21)) { ok = false; break; }
+    const int amn = (MODE == MODE_PLAIN) ? p.a_mn : 0, bmn = (MODE == MODE_PLAIN) ? p.b_mn : 0;
+    for (int tile = cid; tile < total_tiles && ok; tile += ncl, ++it) {
+      const int abuf = p.nacc == 2 ? (it & 1) : 0;
+      const uint32_t aph = (uint32_t)(p.nacc == 2 ? (it >> 1) : it) & 1u;
+      if (!mbar_wait(&sm.acc_empty[abuf], aph ^ 1u, 21)) { ok = false; break; }
       tc_fence_after();
-      for (int kc = 0; kc < nk; ++kc) {
+      const uint32_t dacc = tmem + (uint32_t)(abuf * p.n_cta);
+      int kc_lo, kc_hi;
+      k_range(tile, kc_lo, kc_hi);
+      for (int kc = kc_lo; kc < kc_hi; ++kc) {
         if (!mbar_wait(&sm.full[stage], phase, 22)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
@@ -256,11 +298,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t w_addr = smem_u32(sm.w + (size_t)stage * p.n_cta * 128);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t adesc = umma_desc(a_addr + kk * 32, 16, 1024, 2);
+            // K-major operands advance 16 elements (32 bytes) along the 128-byte row per
+            // K step; MN-major ones advance 16 rows (2048 bytes), their 64-wide MN atoms
+            // 8192 bytes apart
+            const uint64_t adesc = amn ? umma_desc(a_addr + kk * 2048, 8192, 1024, 2)
+                                       : umma_desc(a_addr + kk * 32, 16, 1024, 2);
             for (int nb = 0; nb < p.n_cta; nb += nsub_max) {
               const int nsz = min(nsub_max, p.n_cta - nb);
-              const uint64_t bdesc = umma_desc(w_addr + nb * 128 + kk * 32, 16, 1024, 2);
-              umma_bf16(tmem + nb, adesc, bdesc, idesc_bf16_f32(128, nsz, 0, 0), (kc | kk) ? 1u : 0u);
+              const uint64_t bdesc = bmn ? umma_desc(w_addr + (nb / 64) * 8192 + kk * 2048, 8192, 1024, 2)
+                                         : umma_desc(w_addr + nb * 128 + kk * 32, 16, 1024, 2);
+              umma_bf16(dacc + nb, adesc, bdesc, idesc_bf16_f32(128, nsz, amn, bmn),
+                        (kc != kc_lo || kk) ? 1u : 0u);
             }
           }
           umma_commit(&sm.empty[stage]);
@@ -269,9 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++stage == p.stages) { stage = 0; phase ^= 1u; }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(sm.acc_full);
+      if (lane == 0) umma_commit(&sm.acc_full[abuf]);
       __syncwarp();
-      acc_phase ^= 1u;
     }
     if (!ok) {
       atomicExch(sm.abort_flag, 1);
@@ -292,19 +339,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     float bsum = 0.0f;
     if (MODE != MODE_PLAIN)
       for (int c = 0; c < p.n_cta; ++c) bsum += sm.bias[c];
-    uint32_t acc_phase = 0;
     int iter = 0;
     for (int tile = cid; tile < total_tiles; tile += ncl, ++iter) {
-      if (!mbar_wait(sm.acc_full, acc_phase, 31)) { atomicExch(sm.abort_flag, 1); break; }
+      const int abuf = p.nacc == 2 ? (iter & 1) : 0;
+      const uint32_t aph = (uint32_t)(p.nacc == 2 ? (iter >> 1) : iter) & 1u;
+      if (!mbar_wait(&sm.acc_full[abuf], aph, 31)) { atomicExch(sm.abort_flag, 1); break; }
       tc_fence_after();
-      const int mt = tile / p.num_n_tiles;
+      const uint32_t tacc = trow + (uint32_t)(abuf * p.n_cta);  // this thread's lane of the tile's accumulator
+      const int mt = (tile % mn_tiles) / p.num_n_tiles;
 
       if (MODE == MODE_PLAIN) {
-        const int n0 = (tile % p.num_n_tiles) * p.n_cta;
+        const int n0 = ((tile % mn_tiles) % p.num_n_tiles) * p.n_cta;
         const int64_t grow = (int64_t)mt * 128 + row;
+        // split K: split s writes its partial sums s * split_stride further on; the
+        // bias goes into split 0 only
+        const int split = tile / mn_tiles;
+        float* outp = p.out_f32 + (int64_t)split * p.split_stride;
+        const float* biasp = split == 0 ? p.bias : nullptr;
         for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
           float v[32];
-          tmem_ld32(trow + c0, v);
+          tmem_ld32(tacc + c0, v);
           tmem_wait_ld();
           if (p.vec_out) {
             // transpose through the warp's 32 staged rows so that every store
@@ -316,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             const int cb = n0 + c0 + 4 * (lane & 7);
             float4 b4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (p.bias && cb < p.N) b4 = __ldg(reinterpret_cast<const float4*>(p.bias + cb));
+            if (biasp && cb < p.N) b4 = __ldg(reinterpret_cast<const float4*>(biasp + cb));
             const float* ysw = sm.ys + q * 32 * kYsStride + 4 * (lane & 7);
             const int64_t rbase = (int64_t)mt * 128 + q * 32;
 #pragma unroll
@@ -324,16 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int r = 4 * k + (lane >> 3);
               const float4 y = *reinterpret_cast<const float4*>(ysw + r * kYsStride);
               if (rbase + r < p.R && cb < p.N)
-                *reinterpret_cast<float4*>(p.out_f32 + (rbase + r) * p.N + cb) =
+                *reinterpret_cast<float4*>(outp + (rbase + r) * p.N + cb) =
                     make_float4(y.x + b4.x, y.y + b4.y, y.z + b4.z, y.w + b4.w);
             }
             __syncwarp();
           } else if (grow < p.R) {
-            float* dst = p.out_f32 + grow * p.N + n0 + c0;
+            float* dst = outp + grow * p.N + n0 + c0;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const int col = n0 + c0 + i;
-              if (col < p.N) dst[i] = v[i] + (p.bias ? __ldg(p.bias + col) : 0.0f);
+              if (col < p.N) dst[i] = v[i] + (biasp ? __ldg(biasp + col) : 0.0f);
             }
           }
         }
@@ -344,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float s = 0.0f;
           for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
             float v[32];
-            tmem_ld32(trow + c0, v);
+            tmem_ld32(tacc + c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) s += v[i];
@@ -354,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float m2 = 0.0f;
           for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
             float v[32];
-            tmem_ld32(trow + c0, v);
+            tmem_ld32(tacc + c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -400,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int pairs = p.tpt * 16;
           for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
             float v[32];
-            tmem_ld32(trow + c0, v);
+            tmem_ld32(tacc + c0, v);
             tmem_wait_ld();
             float* ys = sm.ys + row * kYsStride;
 #pragma unroll
@@ -443,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t gtok = (int64_t)mt * 128 + row;
           for (int c0 = 0; c0 < p.n_cta; c0 += 32) {
             float v[32];
-            tmem_ld32(trow + c0, v);
+            tmem_ld32(tacc + c0, v);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -488,8 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(sm.acc_empty);
-      acc_phase ^= 1u;
+      mbar_arrive(&sm.acc_empty[abuf]);
     }
   }
 
@@ -507,6 +560,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 SPK_DEFINE_ERROR_READER(gemm_read_device_error)
 
 using namespace gemmk;
+
+static int launch_gemm_maps(int mode, const CUtensorMap& tmA, const CUtensorMap& tmW, Params& p, cudaStream_t st);
+static uint32_t tmem_cols_for(int n);
 
 static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_t T_rows, cudaStream_t st) {
   // ---- tensor maps
@@ -530,6 +586,13 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
     uint32_t box[2] = {kBK, (uint32_t)p.wbox};
     if ((rc = make_tmap_bf16(&tmW, W, 2, dims, strides, box, true)) != SPK_OK) return rc;
   }
+  return launch_gemm_maps(mode, tmA, tmW, p, st);
+}
+
+static int launch_gemm_maps(int mode, const CUtensorMap& tmA, const CUtensorMap& tmW, Params& p, cudaStream_t st) {
+  // two accumulators when both fit in TMEM's 512 columns
+  p.nacc = 2 * p.n_cta <= 512 ? 2 : 1;
+  p.tmem_cols = tmem_cols_for(p.nacc * p.n_cta);
   // ---- stages that fit
   size_t smem = 0;
   for (p.stages = 4; p.stages >= 2; --p.stages) {
@@ -539,7 +602,7 @@ static int launch_gemm(int mode, const void* A, const void* W, Params& p, int64_
   if (smem > (size_t)kMaxSmem) return fail(SPK_ERR_SHAPE, "tile of %d columns does not fit in shared memory", p.n_cta);
 
   const int sms = num_sms();
-  const int total = p.num_m_tiles * p.num_n_tiles;
+  const int total = p.num_m_tiles * p.num_n_tiles * (p.k_splits > 1 ? p.k_splits : 1);
   int clusters = sms / p.cs;
   if (clusters > total) clusters = total;
   if (clusters < 1) clusters = 1;
@@ -622,6 +685,60 @@ static int wbox_for(int n_cta) {
   for (int b = 256; b >= 8; b -= 8)
     if (n_cta % b == 0) return b;
   return 8;
+}
+
+// Sum of the split-K partial outputs, in split order (deterministic).
+__global__ void __launch_bounds__(256) sum_splits_kernel(const float4* __restrict__ part, int splits, int64_t n4,
+                                                         float4* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = part[i];
+    for (int s = 1; s < splits; ++s) {
+      const float4 b = part[(int64_t)s * n4 + i];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    out[i] = a;
+  }
+}
+
+// Output column tile for MN-major B operands: a multiple of 64 up to 256 that
+// wastes the fewest columns (the larger one on a tie).
+static int pick_nt_mn(int64_t N) {
+  int best = 256;
+  int64_t waste = (N + 255) / 256 * 256 - N;
+  for (int w : {192, 128, 64}) {
+    const int64_t ws = (N + w - 1) / w * w - N;
+    if (ws < waste) {
+      waste = ws;
+      best = w;
+    }
+  }
+  return best;
+}
+
+// Split count of the weight-gradient GEMM: enough tiles for about one wave of
+// SMs, at least 4 K blocks per split.
+static int wgrad_splits(int64_t M, int64_t N, int64_t K, int* kb_per_split) {
+  const int64_t nkb = (M + kBK - 1) / kBK;
+  const int nt = pick_nt_mn(K);
+  const int64_t tiles = ((N + 127) / 128) * ((K + nt - 1) / nt);
+  int64_t splits = (num_sms() + tiles - 1) / tiles;
+  const int64_t most = nkb / 4 > 0 ? nkb / 4 : 1;
+  if (splits > most) splits = most;
+  if (splits < 1) splits = 1;
+  const int64_t kbs = (nkb + splits - 1) / splits;
+  *kb_per_split = (int)kbs;
+  return (int)((nkb + kbs - 1) / kbs);
+}
+
+static int make_map_sw128(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                          uint32_t box_outer) {
+  uint64_t dims[2] = {inner, outer};
+  uint64_t strides[1] = {inner * 2};
+  uint32_t box[2] = {box_inner, box_outer};
+  return make_tmap_bf16(m, base, 2, dims, strides, box, true);
 }
 
 }  // namespace spk
@@ -748,6 +865,99 @@ int spk_linear_affine_lif_fwd(const void* A, const void* W, const float* bias, c
   rc = launch_gemm(mode, A, W, p, R, reinterpret_cast<cudaStream_t>(stream));
   if (rc != SPK_OK) return rc;
   return check_launch("gemm_ln_lif_kernel<affine>");
+}
+
+int spk_linear_dgrad(const void* G, const void* W, float* dX, int64_t M, int64_t N, int64_t K, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(G && W && dX, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(M >= 1 && N >= 8 && N % 8 == 0 && K >= 8 && K % 8 == 0 && M < (1ll << 31) && N < (1 << 24) &&
+                  K < (1 << 24),
+              SPK_ERR_SHAPE, "unsupported sizes M=%lld N=%lld K=%lld (N and K multiples of 8)", (long long)M,
+              (long long)N, (long long)K);
+  SPK_REQUIRE(aligned(G, 16) && aligned(W, 16) && aligned(dX, 16), SPK_ERR_ALIGN,
+              "G, W and dX must be 16-byte aligned");
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  Params p = {};
+  p.T = 1;
+  p.R = M;
+  p.K = (int)N;  // reduction
+  p.N = (int)K;  // output columns
+  p.cs = 1;
+  p.n_cta = pick_nt_mn(K);
+  p.num_n_tiles = (int)((K + p.n_cta - 1) / p.n_cta);
+  p.num_m_tiles = (int)((M + 127) / 128);
+  p.wbox = 64;
+  p.tmem_cols = tmem_cols_for(p.n_cta);
+  p.out_f32 = dX;
+  p.vec_out = 1;
+  p.b_mn = 1;
+  p.k_splits = 1;
+  p.tpt = 128;
+  CUtensorMap tmA, tmW;
+  if ((rc = make_map_sw128(&tmA, G, (uint64_t)N, (uint64_t)M, kBK, 128)) != SPK_OK) return rc;  // G [M][N]
+  if ((rc = make_map_sw128(&tmW, W, (uint64_t)K, (uint64_t)N, 64, kBK)) != SPK_OK) return rc;   // W [N][K]
+  rc = launch_gemm_maps(MODE_PLAIN, tmA, tmW, p, reinterpret_cast<cudaStream_t>(stream));
+  if (rc != SPK_OK) return rc;
+  return check_launch("gemm_ln_lif_kernel<plain, dgrad>");
+}
+
+int64_t spk_linear_wgrad_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  int kbs = 0;
+  const int splits = spk::wgrad_splits(M, N, K, &kbs);
+  return splits > 1 ? (int64_t)splits * N * K * (int64_t)sizeof(float) : 0;
+}
+
+int spk_linear_wgrad(const void* G, const void* X, float* dW, void* workspace, int64_t workspace_bytes, int64_t M,
+                     int64_t N, int64_t K, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(G && X && dW, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(M >= 1 && N >= 8 && N % 8 == 0 && K >= 8 && K % 8 == 0 && M < (1ll << 31) && N < (1 << 24) &&
+                  K < (1 << 24),
+              SPK_ERR_SHAPE, "unsupported sizes M=%lld N=%lld K=%lld (N and K multiples of 8)", (long long)M,
+              (long long)N, (long long)K);
+  SPK_REQUIRE(aligned(G, 16) && aligned(X, 16) && aligned(dW, 16), SPK_ERR_ALIGN,
+              "G, X and dW must be 16-byte aligned");
+  const int64_t need = spk_linear_wgrad_workspace_bytes(M, N, K);
+  SPK_REQUIRE(workspace_bytes >= need && (need == 0 || (workspace && aligned(workspace, 16))), SPK_ERR_INVALID,
+              "workspace of %lld bytes; spk_linear_wgrad_workspace_bytes() = %lld", (long long)workspace_bytes,
+              (long long)need);
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Params p = {};
+  p.T = 1;
+  p.R = N;       // output rows
+  p.K = (int)M;  // reduction over the M rows of G and X
+  p.N = (int)K;  // output columns
+  p.cs = 1;
+  p.n_cta = pick_nt_mn(K);
+  p.num_n_tiles = (int)((K + p.n_cta - 1) / p.n_cta);
+  p.num_m_tiles = (int)((N + 127) / 128);
+  p.wbox = 64;
+  p.tmem_cols = tmem_cols_for(p.n_cta);
+  p.a_mn = 1;
+  p.b_mn = 1;
+  p.k_splits = wgrad_splits(M, N, K, &p.kb_per_split);
+  p.split_stride = N * K;
+  p.out_f32 = p.k_splits > 1 ? reinterpret_cast<float*>(workspace) : dW;
+  p.vec_out = 1;
+  p.tpt = 128;
+  CUtensorMap tmA, tmW;
+  if ((rc = make_map_sw128(&tmA, G, (uint64_t)N, (uint64_t)M, 64, kBK)) != SPK_OK) return rc;  // G [M][N]
+  if ((rc = make_map_sw128(&tmW, X, (uint64_t)K, (uint64_t)M, 64, kBK)) != SPK_OK) return rc;  // X [M][K]
+  rc = launch_gemm_maps(MODE_PLAIN, tmA, tmW, p, st);
+  if (rc != SPK_OK) return rc;
+  if ((rc = check_launch("gemm_ln_lif_kernel<plain, wgrad>")) != SPK_OK) return rc;
+  if (p.k_splits > 1) {
+    const int64_t n4 = N * K / 4;
+    int64_t grid = (n4 + 255) / 256;
+    if (grid > (int64_t)num_sms() * 8) grid = num_sms() * 8;
+    sum_splits_kernel<<<(unsigned)grid, 256, 0, st>>>(reinterpret_cast<const float4*>(workspace), p.k_splits, n4,
+                                                      reinterpret_cast<float4*>(dW));
+    return check_launch("sum_splits_kernel");
+  }
+  return SPK_OK;
 }
 
 int spk_linear_fwd(const void* A, const void* W, const float* bias, float* out, int64_t M, int64_t K, int64_t N,

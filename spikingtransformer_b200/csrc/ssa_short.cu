@@ -290,6 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // dense masks read as 16-byte vectors are loaded one unit ahead (the 32
     // mask bytes of this thread's row and key columns), so their latency
     // hides behind the previous unit's work
+    // the log-distance bias of this thread's row and 32 key columns: the same for
+    // every unit, so it stays in registers (XNOR form only)
+    float rbias[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int kj = kc0 + i;
+      const int dist = qi > kj ? qi - kj : kj - qi;
+      rbias[i] = (p.mode == 1 && dist < p.lmax) ? (float)sm.rl[dist] : 0.0f;
+    }
     const bool mask_pf = p.mask_mode == 2 && p.mask_vec && kc0 + 32 <= p.Nk;
     auto mask_load = [&](int gg, uint4& m0, uint4& m1) {
       const int it = (int)blockIdx.x + (gg / p.T) * (int)gridDim.x, tt = gg % p.T;
@@ -370,15 +379,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld_fence32(raw);
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float sc = __uint_as_float(raw[i]);
-          if (p.mode == 1) {
-            const int kj = kc0 + i;
-            const int dist = qi > kj ? qi - kj : kj - qi;
-            const float rb = (dist < p.lmax) ? (float)sm.rl[dist] : 0.0f;
-            sc = fmaf(2.0f, sc, c_row - ks[kj]) + rb;
+        for (int i0 = 0; i0 < 32; i0 += 4) {
+          // four key sums in one 16-byte load (the same address in every lane)
+          const float4 k4 = p.mode == 1 ? *reinterpret_cast<const float4*>(ks + kc0 + i0)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = i0 + u;
+            float sc = __uint_as_float(raw[i]);
+            if (p.mode == 1) sc = fmaf(2.0f, sc, c_row - kv[u]) + rbias[i];
+            v[i] = ((mbits >> i) & 1u) ? sc : 0.0f;
           }
-          v[i] = ((mbits >> i) & 1u) ? sc : 0.0f;
         }
         // 32 keys of row `row` into the slot's 64-key atom (K-major, 128-byte swizzle)
         uint8_t* prow = sm.p + s * 2 * kTile + slot * kTile + row * 128;

@@ -12,6 +12,8 @@
         causal N=64 case; FLOPs counted dense (QK^T and PV); and the n-major
         copy of V [2048, 256, 48] bf16 that the training path's R V reads,
         beside torch's permute copy.
+  train_gemm  the training step's Linear gradient GEMMs (dgrad, wgrad) at 64
+        images, this package's kernels beside torch's.
   ssa_model  the forward's three attention calls at the bench batch (256
         images): encoder self 256 x 256, decoder cross 64 x 256, decoder
         self 64 x 64 with the dense look-ahead mask; bound: HBM bytes.
@@ -115,6 +117,28 @@ def bench_ssa(iters, variant, N=256, causal=False, T=4, B=32, H=8, d=48, Nk=None
     return {"kernel": "ssa", "variant": "plain" if variant == 0 else "xnor", "causal": causal,
             "dense_mask": dense_mask, "shape": [T, B, H, N, Nk, d], "ms": ms,
             "TFLOP/s_dense_equiv": flops / ms / 1e9, "flops_dense": flops, "GB/s": nbytes / ms / 1e6}
+
+
+def bench_train_gemm(iters, M=65536):
+    """The training step's Linear gradient GEMMs at 64 images (M = 4 x 64 x 256
+    rows): this package's tcgen05 kernels beside torch's (cuBLAS), bf16
+    operands, fp32 output; FLOPs 2 M N K."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    out = []
+    for N, K, what in ((1152, 384, "q/k/v stacked"), (384, 384, "out_proj"), (1536, 384, "expand"),
+                       (384, 1536, "compress")):
+        Gs = [torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16) for _ in range(2)]
+        Xs = [(torch.rand(M, K, device="cuda", generator=g) < 0.2).to(torch.bfloat16) for _ in range(2)]
+        W = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        flops = 2.0 * M * N * K
+        for name, fn in (("dgrad ours", lambda i: ops.linear_dgrad(Gs[i % 2], W)),
+                         ("dgrad torch", lambda i: torch.mm(Gs[i % 2], W, out_dtype=torch.float32)),
+                         ("wgrad ours", lambda i: ops.linear_wgrad(Gs[i % 2], Xs[i % 2])),
+                         ("wgrad torch", lambda i: torch.mm(Gs[i % 2].t(), Xs[i % 2], out_dtype=torch.float32))):
+            ms = _time(fn, iters)
+            out.append({"kernel": name, "layer": what, "M": M, "N": N, "K": K, "ms": ms,
+                        "TFLOP/s": flops / ms / 1e9})
+    return out
 
 
 def bench_n_major(iters, B=2048, N=256, d=48):
@@ -228,7 +252,8 @@ def bench_lnlif(iters, R=16384, T=4):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=None, choices=["lif", "gemm", "ssa", "ssa_model", "data", "shapes", "lnlif"])
+    ap.add_argument("--only", default=None,
+                    choices=["lif", "gemm", "ssa", "ssa_model", "train_gemm", "data", "shapes", "lnlif"])
     ap.add_argument("--ssa-batch", type=int, default=256, help="images for --only ssa_model")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
@@ -250,6 +275,9 @@ def main():
         for n, k in ((1536, 384), (384, 384), (384, 1536)):
             r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)
             r["frac_tensor"] = r["TFLOP/s"] / peaks["bf16_tflops_sustained"]
+            out["results"].append(r)
+    if a.only == "train_gemm":
+        for r in bench_train_gemm(a.iters):
             out["results"].append(r)
     if a.only == "ssa_model":
         # the three attention calls of the forward at the bench batch: encoder

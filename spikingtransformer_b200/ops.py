@@ -306,6 +306,45 @@ def linear(A, W, bias=None):
     return out
 
 
+def linear_grads_ok(g, w_or_x):
+    """Shapes the training Linear gradient kernels take: 2-D-able bf16
+    tensors whose feature sizes are multiples of 8, 16-byte aligned."""
+    return (g.is_cuda and g.dtype == torch.bfloat16 and w_or_x.dtype == torch.bfloat16 and g.shape[-1] % 8 == 0
+            and w_or_x.shape[-1] % 8 == 0 and g.data_ptr() % 16 == 0 and w_or_x.data_ptr() % 16 == 0)
+
+
+def linear_dgrad(G, W):
+    """``G @ W`` in fp32 for ``G`` bf16 ``[M, N]`` and the Linear weight ``W`` bf16
+    ``[N, K]``: the input gradient of ``x @ W.T``."""
+    _cuda(G, W)
+    G = G.reshape(-1, G.shape[-1]).contiguous()
+    W = W.contiguous()
+    M, N = G.shape
+    K = W.shape[1]
+    out = torch.empty((M, K), dtype=torch.float32, device=G.device)
+    _lib.call("spk_linear_dgrad", _lib.ptr(G), _lib.ptr(W), _lib.ptr(out), M, N, K, _lib.stream_ptr(G.device),
+              tag="linear_dgrad N=%d K=%d" % (N, K),
+              work=dict(flops=2.0 * M * N * K, bytes=(M * N + N * K) * 2 + M * K * 4))
+    return out
+
+
+def linear_wgrad(G, X):
+    """``G.T @ X`` in fp32 for ``G`` bf16 ``[M, N]`` and ``X`` bf16 ``[M, K]``: the
+    weight gradient of ``x @ W.T``, summed over the M rows."""
+    _cuda(G, X)
+    G = G.reshape(-1, G.shape[-1]).contiguous()
+    X = X.reshape(-1, X.shape[-1]).contiguous()
+    M, N = G.shape
+    K = X.shape[1]
+    out = torch.empty((N, K), dtype=torch.float32, device=G.device)
+    wsb = int(_lib.load().spk_linear_wgrad_workspace_bytes(M, N, K))
+    ws = torch.empty(max(wsb, 16) // 4, dtype=torch.float32, device=G.device)
+    _lib.call("spk_linear_wgrad", _lib.ptr(G), _lib.ptr(X), _lib.ptr(out), _lib.ptr(ws), wsb, M, N, K,
+              _lib.stream_ptr(G.device), tag="linear_wgrad N=%d K=%d" % (N, K),
+              work=dict(flops=2.0 * M * N * K, bytes=(M * N + M * K) * 2 + N * K * 4))
+    return out
+
+
 def ssa(q, k, v, T, B, H, variant, scale, lif_beta, lif_vth, lif_vr, in_gain=1.0, mask=None, causal=False,
         out_dtype=torch.bfloat16, want_attn=False):
     """Spiking attention core + output LIF on head-merged bf16 spikes.

@@ -281,6 +281,33 @@ def test_linear_plain(ops):
         assert torch.allclose(out.cpu(), ref, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("M,N,K", [
+    (65536, 384, 384),     # q/k/v, out_proj at 64 images (T = 4)
+    (4096, 1152, 384),     # the stacked Q/K/V projection
+    (2048, 1536, 384),     # MLP expand
+    (3000, 384, 1536),     # MLP compress, rows not a multiple of 128
+    (77, 32, 40),          # small model: partial tiles in every dimension
+    (129, 96, 200),
+])
+def test_linear_training_gradients(ops, M, N, K):
+    """Input and weight gradients of a bias-free Linear from bf16 operands
+    against the fp64 products of the same bf16 values: within 1e-5 of the
+    largest element (fp32 accumulation)."""
+    g = gen(M + N + K)
+    G = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    X = (torch.rand(M, K, generator=g) < 0.2).to(torch.bfloat16)
+    dx = ops.linear_dgrad(G.to(DEV), W.to(DEV)).cpu()
+    dw = ops.linear_wgrad(G.to(DEV), X.to(DEV)).cpu()
+    dx_ref = G.double() @ W.double()
+    dw_ref = G.double().t() @ X.double()
+    assert dx.dtype == torch.float32 and dx.shape == (M, K) and dw.shape == (N, K)
+    assert (dx.double() - dx_ref).abs().max() <= 1e-5 * dx_ref.abs().max()
+    assert (dw.double() - dw_ref).abs().max() <= 1e-5 * dw_ref.abs().max()
+    # the same call twice gives the same bits (fixed-order split sums)
+    assert torch.equal(ops.linear_wgrad(G.to(DEV), X.to(DEV)).cpu(), dw)
+
+
 @pytest.mark.parametrize("B,C,H,W,p", [(3, 1, 32, 64, 16), (2, 3, 12, 18, 6), (2, 2, 8, 24, 4)])
 def test_patch_im2col_matches_unfold(ops, B, C, H, W, p):
     """Patch rows [hi | lo] in bf16 against torch's unfold of the same image
