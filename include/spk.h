@@ -43,6 +43,9 @@
  *   spk_synth_text_lines   on-device synthetic text-line batch (stands in for
  *                          the rendered lines of wiki_text_images3.py:173-236
  *                          and the DataLoader of train_spikeformer.py)
+ *   spk_attn_masked_train_fwd / _bwd
+ *                          the decoder's masked self-attention core in
+ *                          training, SSA.py:234-242 and its autograd
  *   spk_ce_over_t          the training loss and token accuracy,
  *                          train_spikeformer.py:309-323 (step_loss with
  *                          CrossEntropyLoss(ignore_index, label_smoothing),
@@ -421,6 +424,35 @@ int spk_xnor_train_grad_prep_lif(const void* g_spikes, int gs_dtype, const float
                                  int surrogate, float surrogate_k, void* g_heads, void* g_rows, float* gcol_part,
                                  float* gscale_part, float* gbeta_part, int64_t T, int64_t TB, int64_t H, int64_t Nq,
                                  int64_t dh, void* stream);
+
+/*
+ * Masked spiking attention core for training, short sequences (Nq, Nk <= 64,
+ * dh <= 64): the decoder's masked self-attention (SSA.py:234-242 with
+ * xnor_attention :145-165 and the log-distance bias :177-201; plain form
+ * SSA.py:81-84), which the reference differentiates with torch's autograd
+ * through the dense score matrix.  One CTA per (t*b, head) keeps S in shared
+ * memory.
+ *   fwd:  a = scale * ((S * M) V), token-major a [T*B][Nq][H*dh] fp32
+ *   bwd:  from g = dL/da (same layout, fp32): dq, dk, dv (the layout and
+ *         dtype of q, k, v) and per-unit partial sums of dL/dscale,
+ *         dscale_part [T*B*H] fp32 (summed by the caller).
+ * q, k, v: dtype SPK_F32 / SPK_F16 / SPK_BF16 spikes, element (tb, h, n, d)
+ * at tb*strides[0] + h*strides[1] + n*strides[2] + d for q (strides[3..5]
+ * for k, strides[6..8] for v; `strides` is a host array of 9).  mask: NULL or
+ * uint8 (t, b, h, i, j) at t*mask_stride_t + b*mask_stride_b + h*mask_stride_h
+ * + i*mask_stride_q + j, nonzero = keep.  variant 1 XNOR, 0 plain; scale a
+ * device fp32 scalar.
+ */
+int spk_attn_masked_train_fwd(const void* q, const void* k, const void* v, int dtype, const int64_t* strides,
+                              const uint8_t* mask, int64_t mask_stride_t, int64_t mask_stride_b,
+                              int64_t mask_stride_h, int64_t mask_stride_q, int variant, const float* scale,
+                              int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, float* a,
+                              void* stream);
+int spk_attn_masked_train_bwd(const void* q, const void* k, const void* v, int dtype, const int64_t* strides,
+                              const uint8_t* mask, int64_t mask_stride_t, int64_t mask_stride_b,
+                              int64_t mask_stride_h, int64_t mask_stride_q, int variant, const float* scale,
+                              int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, const float* g,
+                              void* dq, void* dk, void* dv, float* dscale_part, void* stream);
 
 #ifdef __cplusplus
 }

@@ -209,6 +209,8 @@ class SSAMultiHeadAttention(_SSACore):
     def _combine(self, q, k, v, mask):
         """Attention core before the lifs LIF: q [TB, H, Nq, dh], k / v [TB, H,
         Nk, dh] -> token-major [TB, Nq, H*dh]."""
+        if mask is not None and masked_short_ok(q, k, self.lifs.n_steps):
+            return MaskedShortAttention.apply(q, k, v, self.scale, mask, self.lifs.n_steps, 1)
         if mask is not None:
             a = self.xnor_attention(q, k)
             a = a + self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device).unsqueeze(0).unsqueeze(0)
@@ -229,6 +231,54 @@ class SSAMultiHeadAttention(_SSACore):
             m = m - kf.sum(-1).unsqueeze(-2) @ vf
             m = m + R @ vf
             return _token_major(m * self.scale)
+
+
+def masked_short_ok(q, k, T):
+    """The masked short-sequence attention kernels take this call: CUDA, Nq,
+    Nk, dh <= 64, the T-fold divisible by T."""
+    return (q.is_cuda and q.dim() == 4 and q.shape[2] <= 64 and k.shape[2] <= 64 and q.shape[3] <= 64
+            and q.shape[0] % T == 0)
+
+
+def _dense(t, dtype):
+    """``t`` in ``dtype``, contiguous in some dimension order (one copy if not)."""
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if not (t.is_contiguous() or t.transpose(1, 2).is_contiguous()):
+        t = t.contiguous()
+    return t
+
+
+class MaskedShortAttention(torch.autograd.Function):
+    """Masked attention core for sequences of at most 64 positions (the
+    decoder's masked self-attention, ``SSA.py:234-242``; plain form
+    ``SSA.py:81-84``): ``scale * ((S * mask) @ V)`` token-major fp32, with S
+    the XNOR score plus the log-distance bias (``variant`` 1) or ``Q K^T``
+    (0).  Forward and backward each run one kernel
+    (``spk_attn_masked_train_fwd`` / ``_bwd``) with the score matrix in shared
+    memory; gradients of Q, K, V (in their dtype) and of a learnable scale."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, scale, mask, T, variant):
+        dt = q.dtype if q.dtype in (torch.float32, torch.float16, torch.bfloat16) else torch.float32
+        q, k, v = _dense(q, dt), _dense(k, dt), _dense(v, dt)
+        with torch.autocast(q.device.type, enabled=False):
+            a = ops.attn_masked_train_fwd(q, k, v, mask, scale, T, variant)
+        ctx.save_for_backward(q, k, v, scale if isinstance(scale, torch.Tensor) else None)
+        ctx.scale_value, ctx.mask, ctx.T, ctx.variant = scale, mask, T, variant
+        return a
+
+    @staticmethod
+    def backward(ctx, g):
+        q, k, v, scale_t = ctx.saved_tensors
+        scale = scale_t if scale_t is not None else ctx.scale_value
+        with torch.autocast(q.device.type, enabled=False):
+            dq, dk, dv, gscale = ops.attn_masked_train_bwd(q, k, v, ctx.mask, scale, ctx.T, ctx.variant, g)
+        if scale_t is not None and ctx.needs_input_grad[3]:
+            gscale = gscale.reshape(scale_t.shape).to(scale_t.dtype)
+        else:
+            gscale = None
+        return dq, dk, dv, gscale, None, None, None
 
 
 def _token_major(a):
@@ -419,6 +469,8 @@ class SSAMultiHeadAttention_(_SSACore):
         return c
 
     def _combine(self, q, k, v, mask):
+        if masked_short_ok(q, k, self.lifs.n_steps):
+            return MaskedShortAttention.apply(q, k, v, self._scale_tensor(q.device), mask, self.lifs.n_steps, 0)
         a = q @ k.transpose(-2, -1)
         if mask is not None:
             a = a * mask

@@ -58,6 +58,10 @@ SIGNATURES = {
     "spk_synth_text_lines": ([_p, _i64, _i64, _i64, ctypes.c_uint64, _p, _i64, _i64, _p], _i),
     "spk_ce_over_t_workspace_bytes": ([_i64], _i64),
     "spk_ce_over_t": ([_p, _i, _p, _i64, _i64, _i64, _i64, _f, _p, _p, _p, _i64, _p, _p], _i),
+    "spk_attn_masked_train_fwd": ([_p, _p, _p, _i, _p, _p, _i64, _i64, _i64, _i64, _i, _p, _i64, _i64, _i64, _i64,
+                                   _i64, _i64, _p, _p], _i),
+    "spk_attn_masked_train_bwd": ([_p, _p, _p, _i, _p, _p, _i64, _i64, _i64, _i64, _i, _p, _i64, _i64, _i64, _i64,
+                                   _i64, _i64, _p, _p, _p, _p, _p, _p], _i),
     "spk_xnor_train_combine": ([_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),
     "spk_xnor_train_prep_chunks": ([_i64], _i64),
     "spk_xnor_train_grad_prep": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p], _i),

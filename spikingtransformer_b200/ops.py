@@ -387,6 +387,65 @@ def _distinct_bytes(t):
     return t.untyped_storage().nbytes()
 
 
+def _head_strides(*ts):
+    """(t*b, head, position) element strides of [TB, H, N, d] tensors, packed
+    as a ctypes int64 array; the d stride must be 1."""
+    import ctypes
+    vals = []
+    for t in ts:
+        if t.stride(-1) != 1:
+            raise RuntimeError("attention operands need unit stride along the head dimension")
+        vals += [t.stride(0), t.stride(1), t.stride(2)]
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def _masked_short_args(q, k, v, mask, T):
+    TB, H, Nq, dh = q.shape
+    Nk = k.shape[2]
+    B = TB // T
+    m8, ms = None, (0, 0, 0, 0)
+    if mask is not None:
+        m8 = mask_to_u8(mask, T, B, H, Nq, Nk)
+        ms = tuple(m8.stride(i) for i in range(4))
+    return TB, H, Nq, Nk, dh, B, m8, ms
+
+
+def attn_masked_train_fwd(q, k, v, mask, scale, T, variant):
+    """``scale * ((S * M) V)`` token-major fp32 ``[TB, Nq, H*dh]`` for head-major
+    spikes ``q [TB, H, Nq, dh]``, ``k / v [TB, H, Nk, dh]`` (one dtype), Nq, Nk,
+    dh <= 64; ``mask`` None or broadcastable as for ``ssa``; ``variant`` 1 XNOR
+    with the log-distance bias, 0 plain."""
+    _cuda(q, k, v, mask)
+    TB, H, Nq, Nk, dh, B, m8, ms = _masked_short_args(q, k, v, mask, T)
+    a = torch.empty((TB, Nq, H * dh), dtype=torch.float32, device=q.device)
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, q.device)
+    _lib.call("spk_attn_masked_train_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(q),
+              _head_strides(q, k, v), _lib.ptr(m8), *ms, int(variant), _lib.ptr(sc), T, B, H, Nq, Nk, dh,
+              _lib.ptr(a), _lib.stream_ptr(q.device), tag="attn_masked_train_fwd",
+              work=dict(flops=4.0 * TB * H * Nq * Nk * dh))
+    return a
+
+
+def attn_masked_train_bwd(q, k, v, mask, scale, T, variant, g):
+    """Backward of ``attn_masked_train_fwd`` from ``g = dL/da`` (fp32, token-major):
+    ``(dq, dk, dv)`` shaped and typed like q, k, v, and dL/dscale."""
+    _cuda(q, k, v, mask, g)
+    TB, H, Nq, Nk, dh, B, m8, ms = _masked_short_args(q, k, v, mask, T)
+    g = g.float().contiguous()
+    # the gradients are written with the operands' own strides
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if (dq.stride(), dk.stride(), dv.stride()) != (q.stride(), k.stride(), v.stride()):
+        raise RuntimeError("attn_masked_train_bwd needs dense q, k, v (contiguous in some dimension order)")
+    part = torch.empty(TB * H, dtype=torch.float32, device=q.device)
+    sc = _scalar_f32(scale.detach() if isinstance(scale, torch.Tensor) else scale, q.device)
+    _lib.call("spk_attn_masked_train_bwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(q),
+              _head_strides(q, k, v), _lib.ptr(m8), *ms, int(variant), _lib.ptr(sc), T, B, H, Nq, Nk, dh,
+              _lib.ptr(g), _lib.ptr(dq),
+              _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(part), _lib.stream_ptr(q.device), tag="attn_masked_train_bwd",
+              work=dict(flops=10.0 * TB * H * Nq * Nk * dh))
+    return dq, dk, dv, part.sum()
+
+
 def mask_to_u8(mask, T, B, H, Nq, Nk):
     """uint8 view of an attention mask, expanded (stride 0) to [T, B, H, Nq, Nk].
 

@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this folder from the reference implementation.
 
 Runs the reference ``Triton_Layers`` modules of flofiz/SpikingTransformer
-(imported from a local checkout, default ``/root/reference``) on seeded inputs
+(imported from a local checkout given by ``--ref`` or the
+``SPK_REFERENCE`` environment variable) on seeded inputs
 and stores inputs, state dicts, intermediate tensors and outputs as small
 ``.pt`` files.  The reference LIF kernels (``Lif.py:108-276``) are Triton
 kernels behind an autotuner that needs a GPU; here they run under the Triton
@@ -13,7 +14,7 @@ Linear weights are rounded to bf16 before the reference runs (the benchmark
 model uses bf16 weights, and the CUDA kernels consume bf16 weights), so the
 fixtures pin the reference's fp32 arithmetic on bf16-representable weights.
 
-Usage:  python tests/golden/make_golden.py [--ref /root/reference]
+Usage:  python tests/golden/make_golden.py --ref <reference checkout>
 """
 
 import argparse
@@ -244,8 +245,11 @@ def make_seq2seq(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SPK_REFERENCE"),
+                    help="checkout of flofiz/SpikingTransformer (default: $SPK_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or SPK_REFERENCE")
     torch.set_num_threads(1)
     ref = load_reference(args.ref)
     make_lif(ref)

@@ -112,6 +112,82 @@ def test_xnor_score_free_training_core(pkg, Nq, Nk, dtype):
     assert abs(m.scale.grad.item() - rs.grad.item()) <= 1e-5 * gs_bound
 
 
+@pytest.mark.parametrize("variant,Nq,Nk,dtype,maskkind", [
+    (1, 64, 64, torch.float32, "causal+pad"),   # the decoder's masked self-attention
+    (1, 64, 64, torch.bfloat16, "causal"),
+    (1, 17, 40, torch.float32, "dense"),
+    (0, 64, 64, torch.float32, "causal"),       # plain form (SSAMultiHeadAttention_)
+    (0, 33, 20, torch.bfloat16, None),
+])
+def test_masked_short_attention_training_core(pkg, variant, Nq, Nk, dtype, maskkind):
+    """The masked attention core of the training path (one kernel each way,
+    score matrix in shared memory) against the reference formula
+    (``SSA.py:234-242``; plain ``SSA.py:81-84``) differentiated in float64:
+    the forward bit for bit (integer S, P V, one scale multiply), gradients of
+    Q, K, V and the scale within 1e-5 of the largest element (1e-2 in bf16)."""
+    from spikingtransformer_b200.SSA import MaskedShortAttention
+    T, Bp, H, dh = 4, 3, 2, 48
+    TB = T * Bp
+    g = torch.Generator(device=DEV).manual_seed(Nq * 7 + Nk + variant)
+    leaves = [(torch.rand(TB, n, H, dh, generator=g, device=DEV) < 0.3).to(dtype).requires_grad_()
+              for n in (Nq, Nk, Nk)]
+    q, k, v = (t.transpose(1, 2) for t in leaves)
+    mask = None
+    if maskkind is not None:
+        if maskkind.startswith("causal"):
+            m = torch.tril(torch.ones(Nq, Nk, device=DEV)).expand(Bp, 1, Nq, Nk).clone()
+            if maskkind.endswith("pad"):
+                m[0, :, :, 50:] = 0.0  # padded keys of image 0
+        else:
+            m = (torch.rand(Bp, 1, Nq, Nk, generator=g, device=DEV) < 0.7).float()
+        mask = m.unsqueeze(0).repeat(T, 1, 1, 1, 1).reshape(TB, 1, Nq, Nk)  # the reference's T-fold
+    scale = torch.tensor((1.0 / dh) ** 0.5 if variant == 1 else 0.125, device=DEV, requires_grad=variant == 1)
+    out = MaskedShortAttention.apply(q, k, v, scale, mask, T, variant)
+    w = torch.randn(out.shape, generator=g, device=DEV)
+    (out * w).sum().backward()
+    rl = [t.detach().double().requires_grad_() for t in leaves]
+    rq, rk, rv = (t.transpose(1, 2) for t in rl)
+    rs = scale.detach().double().requires_grad_()
+    if variant == 1:
+        iq = torch.arange(Nq, device=DEV).unsqueeze(1)
+        jk = torch.arange(Nk, device=DEV).unsqueeze(0)
+        R = torch.ceil(torch.log2((max(Nq, Nk) - 1) / ((iq - jk).abs().double() + 1))).clamp(min=0)
+        S = dh - (rq.sum(-1, keepdim=True) + rk.sum(-1, keepdim=True).transpose(2, 3) - 2 * rq @ rk.transpose(2, 3))
+        S = S + R
+    else:
+        S = rq @ rk.transpose(2, 3)
+    if mask is not None:
+        S = S * mask.double()
+    ref = ((S @ rv) * rs).transpose(1, 2).reshape(TB, Nq, H * dh)
+    (ref * w.double()).sum().backward()
+    assert out.dtype == torch.float32 and torch.equal(out, ref.float())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    for name, a, b in (("q", leaves[0].grad, rl[0].grad), ("k", leaves[1].grad, rl[1].grad),
+                       ("v", leaves[2].grad, rl[2].grad)):
+        assert a.dtype == dtype
+        assert (a.double() - b).abs().max().item() <= tol * b.abs().max().item(), name
+    if variant == 1:
+        assert abs(scale.grad.item() - rs.grad.item()) <= 1e-5 * abs(rs.grad.item())
+
+
+def test_decoder_masked_attention_trains_on_the_fused_core(pkg):
+    """A decoder layer's masked self-attention under autograd runs the fused
+    core kernels (no eager score matrix)."""
+    from spikingtransformer_b200 import _lib
+    from spikingtransformer_b200.Decoder import DecoderLayer
+    T, B, N, D = 4, 2, 16, 64
+    layer = DecoderLayer(D, 2, 128, n_steps=T).to(DEV)
+    x = (torch.rand(T * B, N, D, device=DEV) < 0.3).float().requires_grad_()
+    enc = (torch.rand(T * B, 24, D, device=DEV) < 0.3).float()
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(T * B, 1, N, N)
+    with _lib.LaunchCounter() as counter:
+        y = layer(x, enc, mask=mask)
+        y.sum().backward()
+    assert counter.counts.get("attn_masked_train_fwd") == 1, counter.counts
+    assert counter.counts.get("attn_masked_train_bwd") == 1, counter.counts
+    assert x.grad is not None and torch.isfinite(x.grad).all()
+
+
 @pytest.mark.parametrize("spike_dtype", [torch.float32, torch.bfloat16])
 def test_xnor_lif_fused_equals_composition(pkg, spike_dtype):
     """The attention core with the output LIF fused into its kernels equals the
