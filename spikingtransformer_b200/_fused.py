@@ -261,7 +261,7 @@ class LinearBF16(torch.autograd.Function):
     runs in either direction and fp32 gradients are summed in fp32.  They are
     torch's (cuBLAS): this package's tcgen05 gradient GEMMs
     (``ops.linear_dgrad`` / ``ops.linear_wgrad``) compute the same products
-    but take 1.1-2.8x cuBLAS's time at the training shapes."""
+    but take 1.1-1.6x cuBLAS's time at the training shapes."""
 
     @staticmethod
     def forward(ctx, x, w, xb, wb):

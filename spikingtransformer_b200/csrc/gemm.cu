@@ -718,13 +718,18 @@ static int pick_nt_mn(int64_t N) {
   return best;
 }
 
-// Split count of the weight-gradient GEMM: enough tiles for about one wave of
-// SMs, at least 4 K blocks per split.
+// Output column tile of the gradient GEMMs: the whole row when it fits one
+// CTA's TMEM (K <= 512, a multiple of 64: the A tile is then read once per row
+// block), else pick_nt_mn.
+static int pick_nt_grad(int64_t K) { return (K <= 512 && K % 64 == 0) ? (int)K : pick_nt_mn(K); }
+
+// Split count of the weight-gradient GEMM: as many splits as fill one wave of
+// SMs without a second partial wave, at least 4 K blocks per split.
 static int wgrad_splits(int64_t M, int64_t N, int64_t K, int* kb_per_split) {
   const int64_t nkb = (M + kBK - 1) / kBK;
-  const int nt = pick_nt_mn(K);
+  const int nt = pick_nt_grad(K);
   const int64_t tiles = ((N + 127) / 128) * ((K + nt - 1) / nt);
-  int64_t splits = (num_sms() + tiles - 1) / tiles;
+  int64_t splits = num_sms() / tiles;
   const int64_t most = nkb / 4 > 0 ? nkb / 4 : 1;
   if (splits > most) splits = most;
   if (splits < 1) splits = 1;
@@ -884,7 +889,7 @@ int spk_linear_dgrad(const void* G, const void* W, float* dX, int64_t M, int64_t
   p.K = (int)N;  // reduction
   p.N = (int)K;  // output columns
   p.cs = 1;
-  p.n_cta = pick_nt_mn(K);
+  p.n_cta = pick_nt_grad(K);
   p.num_n_tiles = (int)((K + p.n_cta - 1) / p.n_cta);
   p.num_m_tiles = (int)((M + 127) / 128);
   p.wbox = 64;
@@ -931,7 +936,7 @@ int spk_linear_wgrad(const void* G, const void* X, float* dW, void* workspace, i
   p.K = (int)M;  // reduction over the M rows of G and X
   p.N = (int)K;  // output columns
   p.cs = 1;
-  p.n_cta = pick_nt_mn(K);
+  p.n_cta = pick_nt_grad(K);
   p.num_n_tiles = (int)((K + p.n_cta - 1) / p.n_cta);
   p.num_m_tiles = (int)((N + 127) / 128);
   p.wbox = 64;

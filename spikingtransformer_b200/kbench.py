@@ -12,6 +12,8 @@
         causal N=64 case; FLOPs counted dense (QK^T and PV); and the n-major
         copy of V [2048, 256, 48] bf16 that the training path's R V reads,
         beside torch's permute copy.
+  cnn   the reference's CNN image encoder (eval) on 64 text lines of 32 x 512,
+        fused path beside the library convolutions.
   train_gemm  the training step's Linear gradient GEMMs (dgrad, wgrad) at 64
         images, this package's kernels beside torch's.
   ssa_model  the forward's three attention calls at the bench batch (256
@@ -141,6 +143,39 @@ def bench_train_gemm(iters, M=65536):
     return out
 
 
+def bench_cnn(iters, B=64, T=4, D=384, layers=4, H=32, W=512):
+    """The reference's CNN image encoder (``CNNBackbone``, patch 4, 32 x 512
+    text lines, eval mode) on B images repeated over T: this package's fused
+    path (patch gathers + GEMMs with the BatchNorm-affine and LIF epilogue,
+    first convolution once per image) beside the reference composition on
+    the same module (library convolutions and BatchNorm, the LIF kernel) on
+    the T-fold."""
+    from .ImageEncoder import CNNBackbone
+    torch.manual_seed(0)
+    m = CNNBackbone(d_model=D, nb_layers=layers, patch_size=4, n_steps=T).cuda().eval()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    srcs = [torch.rand(B, 1, H, W, device="cuda", generator=g) * 0.2 for _ in range(2)]
+    folds = [x.unsqueeze(0).expand(T, *x.shape).reshape(T * B, 1, H, W).contiguous() for x in srcs]
+    out = []
+    with torch.no_grad():
+        ms = _time(lambda i: m.encode_images(srcs[i % 2], T), iters)
+        out.append({"kernel": "cnn_backbone fused", "images": B, "T": T, "layers": layers, "ms": ms,
+                    "images/s": B / ms * 1e3})
+
+        def library(i):
+            x = m.space_to_depth(folds[i % 2])
+            x = m.lif_1(m.bn1(m.conv1(x)))[0]
+            x = m.lif_2(m.bn2(m.conv2(x)))[0]
+            for layer in m.layers:
+                x = layer(x)
+            x = m.reduce(x)
+            return x + m.rpe(x)
+        ms = _time(library, iters)
+        out.append({"kernel": "cnn_backbone library conv + BatchNorm + LIF kernel", "images": B, "T": T,
+                    "layers": layers, "ms": ms, "images/s": B / ms * 1e3})
+    return out
+
+
 def bench_n_major(iters, B=2048, N=256, d=48):
     """The n-major copy of V for the training attention's R V product
     ([B, N, d] bf16 -> [N, B*d], B = T*images*H at 64 images), against
@@ -253,7 +288,7 @@ def bench_lnlif(iters, R=16384, T=4):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None,
-                    choices=["lif", "gemm", "ssa", "ssa_model", "train_gemm", "data", "shapes", "lnlif"])
+                    choices=["lif", "gemm", "ssa", "ssa_model", "train_gemm", "cnn", "data", "shapes", "lnlif"])
     ap.add_argument("--ssa-batch", type=int, default=256, help="images for --only ssa_model")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
@@ -275,6 +310,9 @@ def main():
         for n, k in ((1536, 384), (384, 384), (384, 1536)):
             r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)
             r["frac_tensor"] = r["TFLOP/s"] / peaks["bf16_tflops_sustained"]
+            out["results"].append(r)
+    if a.only == "cnn":
+        for r in bench_cnn(a.iters):
             out["results"].append(r)
     if a.only == "train_gemm":
         for r in bench_train_gemm(a.iters):
