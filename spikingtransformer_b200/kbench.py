@@ -12,6 +12,8 @@
         causal N=64 case; FLOPs counted dense (QK^T and PV); and the n-major
         copy of V [2048, 256, 48] bf16 that the training path's R V reads,
         beside torch's permute copy.
+  attn_train  the decoder's masked self-attention core in training (forward
+        and backward), fused kernels beside the reference composition.
   cnn   the reference's CNN image encoder (eval) on 64 text lines of 32 x 512,
         fused path beside the library convolutions.
   train_gemm  the training step's Linear gradient GEMMs (dgrad, wgrad) at 64
@@ -176,6 +178,45 @@ def bench_cnn(iters, B=64, T=4, D=384, layers=4, H=32, W=512):
     return out
 
 
+def bench_attn_train(iters, B=64, T=4, H=8, N=64, d=48):
+    """The decoder's masked self-attention core in training at 64 images
+    (``[T*B, H, 64, 48]`` head-major bf16 spikes, causal mask, XNOR with the
+    log-distance bias): the fused forward and backward kernels, and the
+    reference composition (score matrix, bias, mask, scale, @ V and their
+    autograd) beside them."""
+    from .SSA import MaskedShortAttention, SSAMultiHeadAttention
+    g = torch.Generator(device="cuda").manual_seed(7)
+    TB = T * B
+    q, k, v = ((torch.rand(TB, H, N, d, device="cuda", generator=g) < 0.3).to(torch.bfloat16) for _ in range(3))
+    mask = torch.tril(torch.ones(N, N, device="cuda")).expand(TB, 1, N, N)
+    scale = torch.tensor((1.0 / d) ** 0.5, device="cuda", requires_grad=True)
+    gout = torch.randn(TB, N, H * d, device="cuda", generator=g)
+    m = SSAMultiHeadAttention(H * d, H, n_steps=T).cuda()
+    out = []
+
+    def fused(i):
+        qq, kk, vv = (t.detach().requires_grad_() for t in (q, k, v))
+        MaskedShortAttention.apply(qq, kk, vv, scale, mask, T, 1).backward(gout)
+
+    def composition(i):
+        qq, kk, vv = (t.detach().float().requires_grad_() for t in (q, k, v))
+        a = m.xnor_attention(qq, kk) + m.get_log_pe_bias_cross(N, N, qq.device)
+        ((a * mask * scale) @ vv).transpose(1, 2).reshape(TB, N, H * d).backward(gout)
+    for name, fn in (("masked attention fwd+bwd, fused kernels", fused),
+                     ("masked attention fwd+bwd, reference composition", composition)):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(iters):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        out.append({"kernel": name, "shape": [TB, H, N, d], "ms": e0.elapsed_time(e1) / iters})
+    return out
+
+
 def bench_n_major(iters, B=2048, N=256, d=48):
     """The n-major copy of V for the training attention's R V product
     ([B, N, d] bf16 -> [N, B*d], B = T*images*H at 64 images), against
@@ -288,7 +329,8 @@ def bench_lnlif(iters, R=16384, T=4):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None,
-                    choices=["lif", "gemm", "ssa", "ssa_model", "train_gemm", "cnn", "data", "shapes", "lnlif"])
+                    choices=["lif", "gemm", "ssa", "ssa_model", "train_gemm", "cnn", "attn_train", "data", "shapes",
+                             "lnlif"])
     ap.add_argument("--ssa-batch", type=int, default=256, help="images for --only ssa_model")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tokens", type=int, default=32 * 256, help="tokens per step for the gemm shapes")
@@ -310,6 +352,9 @@ def main():
         for n, k in ((1536, 384), (384, 384), (384, 1536)):
             r = bench_gemm(a.iters, N=n, K=k, R=a.tokens)
             r["frac_tensor"] = r["TFLOP/s"] / peaks["bf16_tflops_sustained"]
+            out["results"].append(r)
+    if a.only == "attn_train":
+        for r in bench_attn_train(a.iters):
             out["results"].append(r)
     if a.only == "cnn":
         for r in bench_cnn(a.iters):

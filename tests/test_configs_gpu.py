@@ -453,3 +453,80 @@ def test_reference_training_configuration_fp16_gradscaler_cnn(pkg_loaded):
     assert abs(losses[0] - loss_ref) <= 0.03 * loss_ref, (losses[0], loss_ref)
     changed = [n for n, p in ours.named_parameters() if not torch.equal(p.detach(), before[n])]
     assert any("image_encoder.conv1" in n for n in changed) and any("output_layer" in n for n in changed)
+
+
+# ------------------------------------------------------------------ CNN image encoder, teacher-forced
+
+
+def test_cnn_backbone_teacher_forced(pkg_loaded):
+    """The reference's CNN image encoder (``ImageEncoder.py:8-102``: PixelUnshuffle
+    + 3x3 conv, 1x1 conv, four inverted bottlenecks, the (channel, height)
+    reduce, the Conv1d position encoding; eval-mode BatchNorm; D = 384) on 4
+    text lines of 32 x 512 at T = 4, every fused convolution fed the oracle's
+    input for it: spikes bit-exact outside the near-threshold band, the
+    identity and ``x + rpe`` sums exact."""
+    from spikingtransformer_b200 import ops
+    from spikingtransformer_b200.ImageEncoder import CNNBackbone, _conv_affine_lif, _taps_last
+    T, B, D, L = 4, 4, 384, 4
+    torch.manual_seed(11)
+    ours = CNNBackbone(d_model=D, nb_layers=L, patch_size=4, n_steps=T)
+    with torch.no_grad():
+        for m in ours.modules():
+            if isinstance(m, (torch.nn.Conv2d, torch.nn.Conv1d)):
+                m.weight.copy_((m.weight * 3).to(torch.bfloat16).float())
+            if isinstance(m, (torch.nn.BatchNorm2d, torch.nn.BatchNorm1d)):
+                m.running_mean.uniform_(-0.2, 0.2)
+                m.running_var.uniform_(0.5, 1.5)
+                m.weight.uniform_(0.8, 1.2)
+                m.bias.uniform_(0.2, 0.6)
+    ref = om.CNNBackbone(d_model=D, nb_layers=L, patch_size=4, n_steps=T).eval()
+    ref.load_state_dict(ours.state_dict())
+    ours = ours.to(DEV).eval()
+    src = synthetic_lines(B, 12, H=32, W=512)
+    x = src.unsqueeze(0).expand(T, *src.shape).reshape(T * B, *src.shape[1:])
+
+    def cl(t):  # NCHW oracle tensor -> channels-last bf16 on the device
+        return t.permute(0, 2, 3, 1).contiguous().to(DEV).to(torch.bfloat16)
+
+    def check(ours_cl, pre_nchw, lif, what):
+        # channels-last spikes against the oracle LIF of the NCHW pre-activation
+        o = ours_cl.float().cpu().reshape(pre_nchw.shape[0], *pre_nchw.shape[2:], pre_nchw.shape[1])
+        return lif_out_check(o.permute(0, 3, 1, 2).contiguous(), pre_nchw, T, _beta(lif), float(lif.v_th), what=what)
+
+    flips = 0
+    with torch.no_grad():
+        # PixelUnshuffle + conv1 (once per image), then conv2
+        pre1 = ref.bn1(ref.conv1(ref.space_to_depth(x)))
+        s1 = ref.lif_1(pre1)[0]
+        got1 = ours._fast(src.to(DEV), T, t_broadcast=True)[1]["conv1"]  # NCHW view of channels-last spikes
+        flips += lif_out_check(got1, pre1, T, _beta(ref.lif_1), 1.0, what="conv1")
+        pre2 = ref.bn2(ref.conv2(s1))
+        s2 = ref.lif_2(pre2)[0]
+        got2 = _conv_affine_lif(cl(s1).view(-1, s1.shape[1]), ours.conv2, ours.bn2, ours.lif_2, _taps_last, T)
+        flips += check(got2, pre2, ref.lif_2, "conv2")
+        xo = s2
+        for n, (lo, lr) in enumerate(zip(ours.layers, ref.layers)):
+            pre_h = lr.bn1(lr.conv1(xo))
+            h = lr.lif_1(pre_h)[0]
+            a = ops.im2col(cl(xo), (3, 3), (1, 1), (1, 1))
+            got_h = _conv_affine_lif(a, lo.conv1, lo.bn1, lo.lif_1, _taps_last, T)
+            flips += check(got_h, pre_h, lr.lif_1, "bottleneck %d conv1" % n)
+            pre_o = lr.bn2(lr.conv2(h))
+            out = lr.lif_2(pre_o)[0] + xo
+            resid = cl(xo)
+            _conv_affine_lif(cl(h).view(-1, h.shape[1]), lo.conv2, lo.bn2, lo.lif_2, _taps_last, T,
+                             residual=resid.view(-1, xo.shape[1]))
+            delta = resid.float().cpu() - cl(xo).float().cpu()
+            flips += check(delta, pre_o, lr.lif_2, "bottleneck %d conv2 + identity" % n)
+            xo = out
+        b_, c_, h_, w_ = xo.shape
+        pre_r = ref.reduce.bn(ref.reduce.conv(xo.reshape(b_, c_ * h_, w_).unsqueeze(-2))).squeeze(-2)
+        r0 = ref.reduce.lif(pre_r)[0]
+        got_r = ours.reduce._fast(cl(xo), T)  # [TB, W, D]
+        flips += lif_out_check(got_r.transpose(1, 2), pre_r, T, _beta(ref.reduce.lif), 1.0, what="reduce")
+        pre_p = ref.rpe.bn(ref.rpe.conv(r0))
+        r0_cl = r0.transpose(1, 2).contiguous().to(DEV).to(torch.bfloat16)
+        got_sum = ours.rpe._fast_sum(r0_cl, T)
+        delta = got_sum.float().cpu() - r0.transpose(1, 2)
+        flips += lif_out_check(delta.transpose(1, 2), pre_p, T, _beta(ref.rpe.lif), 1.0, what="rpe")
+    print("CNN teacher-forced flips (all near threshold):", flips)
