@@ -839,6 +839,531 @@ __global__ void __launch_bounds__(PF ? 32 * kTokPfWarps : 32 * kTokMaxWarps) ln_
   if (threadIdx.x == 0) out[3 * D] = lbs;
 }
 
+// ---------------------------------------------------------------------------
+// One token per group of G warps, twelve columns per lane: D = 384 G with
+// G = 1, 2 or 4 (the model's D = 384 and 1536).  A lane holds three 4-column
+// vectors of every row, at columns 128 (i G + wg) + 4 lane (wg the warp's
+// index in its group), so one warp access of vector i covers 128 consecutive
+// columns.  The row reductions of a token run once for all T rows together
+// (forward: each row's mean and M2; backward: each row's two LayerNorm sums):
+// by shuffles within a warp and, for G > 1, through double-buffered shared
+// slots behind a named barrier of the group.  The per-row costs (reductions,
+// statistics, addressing) are spread over twelve elements per lane, and a
+// single-warp token needs no barrier.
+
+constexpr int kGrpWarps = 8;  // warps per block
+constexpr int kGrpNV = 3;     // 4-column vectors per lane and row
+constexpr int kGrpFwdStages = 2;  // staged tokens per warp: the rows of kStages - 1 tokens are in flight
+constexpr int kGrpBwdStages = 2;
+constexpr int kGrpBwdWarps = 8;   // warps per block of the backward
+
+inline bool use_grp(int D) { return D == 384 || D == 768 || D == 1536; }
+
+// Mean and M2 of up to kMaxT rows over the 32 lanes of a warp, each lane
+// starting from n0 values; the partners of every shuffle hold equal counts,
+// so mean = (ma + mb) / 2 and M2 = M2a + M2b + d^2 n / 2, and every lane ends
+// with the same result.
+__device__ __forceinline__ void warp_mean_m2(float2 (&mm)[kMaxT], int T, float n0) {
+  float n = n0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      const float om = __shfl_xor_sync(0xffffffffu, mm[t].x, o);
+      const float o2 = __shfl_xor_sync(0xffffffffu, mm[t].y, o);
+      const float d = om - mm[t].x;
+      mm[t].y = (mm[t].y + o2) + d * d * (0.5f * n);
+      mm[t].x = 0.5f * (mm[t].x + om);
+    }
+    n *= 2.0f;
+  }
+}
+
+// sums of up to kMaxT float2 values over the 32 lanes of a warp (the same on every lane)
+__device__ __forceinline__ void warp_sum2(float2 (&v)[kMaxT], int T) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      v[t].x += __shfl_xor_sync(0xffffffffu, v[t].x, o);
+      v[t].y += __shfl_xor_sync(0xffffffffu, v[t].y, o);
+    }
+  }
+}
+
+// the value of row `lane` (lanes < kMaxT) of a per-row register array
+__device__ __forceinline__ float2 row_of_lane(const float2 (&v)[kMaxT], int lane) {
+  float2 r = v[0];
+#pragma unroll
+  for (int t = 1; t < kMaxT; ++t)
+    if (lane == t) r = v[t];
+  return r;
+}
+
+// Exchange of per-warp row values between the G warps of a token group:
+// slot [buf][grp][w][t]; one named barrier (id 1 + grp) per exchange.  A slot
+// is rewritten two exchanges later, after a barrier that every reader of it
+// has passed.
+template <int G, int W>
+struct GroupXch {
+  float2* slots;  // [2][NG][G][kMaxT]
+  int grp, wg, buf;
+  __device__ __forceinline__ float2* put(const float2 (&v)[kMaxT], int lane) {
+    constexpr int NG = W / G;
+    float2* base = slots + ((size_t)buf * NG + grp) * G * kMaxT;
+    if (lane < kMaxT) base[wg * kMaxT + lane] = row_of_lane(v, lane);
+    named_bar_sync(1 + grp, 32 * G);
+    buf ^= 1;
+    return base;
+  }
+  // (mean, M2) of every row merged over the group's warps in warp order; each
+  // warp contributed n_w values per row
+  __device__ __forceinline__ void merge_mean_m2(float2 (&mm)[kMaxT], int T, int lane, float n_w) {
+    if constexpr (G > 1) {
+      const float2* r = put(mm, lane);
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t) {
+        if (t >= T) continue;
+        float2 acc = r[t];
+#pragma unroll
+        for (int w = 1; w < G; ++w) {
+          // merging warp w into the first w warps: weights 1/(w+1) and n_w w/(w+1)
+          const float2 b = r[w * kMaxT + t];
+          const float d = b.x - acc.x;
+          acc.x = fmaf(d, 1.0f / (float)(w + 1), acc.x);
+          acc.y = fmaf(d * d, n_w * (float)w / (float)(w + 1), acc.y + b.y);
+        }
+        mm[t] = acc;
+      }
+    }
+  }
+  __device__ __forceinline__ void sum(float2 (&v)[kMaxT], int T, int lane) {
+    if constexpr (G > 1) {
+      const float2* r = put(v, lane);
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t) {
+        if (t >= T) continue;
+        float2 acc = r[t];
+#pragma unroll
+        for (int w = 1; w < G; ++w) {
+          acc.x += r[w * kMaxT + t].x;
+          acc.y += r[w * kMaxT + t].y;
+        }
+        v[t] = acc;
+      }
+    }
+  }
+};
+
+template <int EB>
+__device__ __forceinline__ void cp_async_vec(RawVec<EB>* dst, const void* src) {
+  if constexpr (EB == 2)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Four consecutive fp32 values loaded afresh at every call (volatile: not
+// hoisted out of the token loop and kept in registers for the whole kernel)
+__device__ __forceinline__ float4 ld_fresh4(const float* q) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(q));
+  return v;
+}
+
+// The LayerNorm parameters of the four columns c..c+3, as pairs: gamma and
+// beta scaled by the LIF input gain (the LIF's input is gain (x^ gamma +
+// beta), formed as x^ (gain gamma) + gain beta by the forward and by the
+// backward's recomputation alike), and the Linear bias.
+template <typename Params>
+__device__ __forceinline__ void ln_params(const Params& p, int c, float2 gain2, float2 (&gq)[2], float2 (&bq)[2],
+                                          float2 (&pq)[2]) {
+  const float4 g4 = p.gamma ? ld_fresh4(p.gamma + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+  const float4 b4 = p.beta_ln ? ld_fresh4(p.beta_ln + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 p4 = p.bias ? ld_fresh4(p.bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  gq[0] = mul2(make_float2(g4.x, g4.y), gain2);
+  gq[1] = mul2(make_float2(g4.z, g4.w), gain2);
+  bq[0] = mul2(make_float2(b4.x, b4.y), gain2);
+  bq[1] = mul2(make_float2(b4.z, b4.w), gain2);
+  pq[0] = make_float2(p4.x, p4.y);
+  pq[1] = make_float2(p4.z, p4.w);
+}
+
+template <int EB, int SD, int G>
+__global__ void __launch_bounds__(32 * kGrpWarps, EB == 2 ? 2 : 1) ln_lif_fwd_grp_kernel(const FwdParams p) {
+  constexpr int NV = kGrpNV, NG = kGrpWarps / G;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ float2 xch[G > 1 ? 2 * NG * G * kMaxT : 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / G, wg = warp - grp * G;
+  constexpr int S = kGrpFwdStages;
+  // this warp's S stages of [kMaxT][NV][32 lanes] pre-activation vectors
+  RawVec<EB>* pre_s = reinterpret_cast<RawVec<EB>*>(smem) + (size_t)warp * S * kMaxT * NV * 32;
+  auto pre_at = [&](int s, int t, int i) { return pre_s + ((s * kMaxT + t) * NV + i) * 32 + lane; };
+  GroupXch<G, kGrpWarps> gx{xch, grp, wg, 0};
+  const int T = p.T;
+  const float invD = 1.0f / (float)p.D;
+  const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+  const SpikeLayout lay(p.R, p.D, 0, p.hd, p.seq);
+  const float2 beta2 = make_float2(lb, lb), gain2 = make_float2(p.gain, p.gain);
+  int cols[NV];
+  int64_t coff[NV];
+  float2 gg[NV][2], bb[NV][2], pb[NV][2];  // gain gamma, gain beta, bias
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = 128 * (i * G + wg) + 4 * lane;
+    cols[i] = c;
+    coff[i] = SpikeLayout(p.R, p.D, c, p.hd, p.seq).col_off;
+    ln_params(p, c, gain2, gg[i], bb[i], pb[i]);
+  }
+  const int64_t step = (int64_t)gridDim.x * NG;
+  int64_t tok = (int64_t)blockIdx.x * NG + grp;
+  // the rows of the next S - 1 tokens are in flight while this one is processed
+  auto issue = [&](int64_t tk, int s) {
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      const int64_t rb = ((int64_t)t * p.R + tk) * p.ld;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        cp_async_vec<EB>(pre_at(s, t, i), reinterpret_cast<const unsigned char*>(p.pre) + (rb + cols[i]) * EB);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < S - 1; ++k) {
+    if (tok + k * step < p.R) issue(tok + k * step, k);
+    cp_async_commit();
+  }
+  int s = 0;
+  for (; tok < p.R; tok += step, s = s + 1 == S ? 0 : s + 1) {
+    const int64_t tn = tok + (S - 1) * step;
+    if (tn < p.R) issue(tn, s == 0 ? S - 1 : s - 1);
+    cp_async_commit();
+    cp_async_wait<S - 1>();  // this token's vectors have landed
+    // each row's (mean, M2): the lane's twelve values, then the warp, then the group
+    float2 mm[kMaxT];
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      mm[t] = make_float2(0.0f, 0.0f);
+      if (t >= T) continue;
+      float2 xs[NV][2];
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float x[4];
+        raw_unpack<EB>(*pre_at(s, t, i), p.pre_dtype, x);
+        xs[i][0] = add2(make_float2(x[0], x[1]), pb[i][0]);
+        xs[i][1] = add2(make_float2(x[2], x[3]), pb[i][1]);
+        sum += (xs[i][0].x + xs[i][0].y) + (xs[i][1].x + xs[i][1].y);
+      }
+      const float lm = sum * (1.0f / (4 * NV));
+      const float2 nl = make_float2(-lm, -lm);
+      float2 q = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float2 d = add2(xs[i][j], nl);
+          q = fma2(d, d, q);
+        }
+      mm[t] = make_float2(lm, q.x + q.y);
+    }
+    warp_mean_m2(mm, T, (float)(4 * NV));
+    gx.merge_mean_m2(mm, T, lane, (float)(32 * 4 * NV));
+    float2 nm[kMaxT], rs[kMaxT];
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      const float rstd = rsqrtf(fmaf(mm[t].y, invD, p.eps));
+      nm[t] = make_float2(-mm[t].x, -mm[t].x);
+      rs[t] = make_float2(rstd, rstd);
+      mm[t].y = rstd;
+    }
+    if (wg == 0 && lane < T) p.stats[(int64_t)lane * p.R + tok] = row_of_lane(mm, lane);
+    // LayerNorm output and the LIF over t
+    const int64_t sb = lay.tok_off(tok, p.D);
+    float2 v[NV][2];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i][0] = v[i][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float x[4];
+        raw_unpack<EB>(*pre_at(s, t, i), p.pre_dtype, x);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float2 xb = add2(make_float2(x[2 * j], x[2 * j + 1]), pb[i][j]);
+          const float2 u = add2(mul2(v[i][j], beta2), fma2(mul2(add2(xb, nm[t]), rs[t]), gg[i][j], bb[i][j]));
+          const bool sx = u.x > vth, sy = u.y > vth;
+          x[2 * j] = sx ? 1.0f : 0.0f;
+          x[2 * j + 1] = sy ? 1.0f : 0.0f;
+          v[i][j] = make_float2(sx ? vr : u.x, sy ? vr : u.y);
+        }
+        store_spikes4<SD>(p.spikes, p.spike_dtype, sb + t * lay.t_stride + coff[i], x);
+      }
+    }
+  }
+}
+
+// Backward staging: per warp, a ring of stages, each [kMaxT][kGrpNV][32 lanes]
+// vectors of the pre-activation, the same of the spike gradient, and the
+// token's kMaxT row statistics.  Each lane copies (cp.async) and later reads
+// only its own vectors, so a lane's wait_group is the only synchronisation
+// the vectors need; the statistics, copied by lanes t < T, are read by every
+// lane after a __syncwarp.
+template <int EBP, int EBG>
+constexpr size_t grp_bwd_stage_bytes() {
+  return (size_t)kMaxT * kGrpNV * 32 * (4 * EBP + 4 * EBG) + kMaxT * sizeof(float2);
+}
+// fp32 pre-activation and gradient: one stage (two would exceed the shared memory)
+template <int EBP, int EBG>
+constexpr int grp_bwd_stages() {
+  return EBP + EBG > 6 ? 1 : kGrpBwdStages;
+}
+template <int EBP, int EBG>
+constexpr int grp_bwd_warps() {
+  return kGrpBwdWarps;
+}
+// per warp: the stages, then the current token's x^ ([kMaxT][kGrpNV][32 lanes] float4)
+constexpr size_t kGrpXhatBytes = (size_t)kMaxT * kGrpNV * 32 * sizeof(float4);
+template <int EBP, int EBG>
+constexpr size_t grp_bwd_warp_bytes() {
+  return grp_bwd_stages<EBP, EBG>() * grp_bwd_stage_bytes<EBP, EBG>() + kGrpXhatBytes;
+}
+template <int EBP, int EBG>
+constexpr size_t grp_bwd_smem_bytes() {
+  return (size_t)grp_bwd_warps<EBP, EBG>() * grp_bwd_warp_bytes<EBP, EBG>();
+}
+
+// Backward, one token per group: the token's rows arrive in shared memory one
+// token ahead (cp.async); the membrane is recomputed in t order from the
+// saved statistics; the steps are walked backwards (BPTT) giving dL/dy of
+// every row, with the rows' two LayerNorm sums accumulated on the way; one
+// reduction of those sums for all T rows; then dL/dx of every row.
+template <int EBP, int EBG, int SURR, int G>
+__global__ void __launch_bounds__(32 * grp_bwd_warps<EBP, EBG>(), 1) ln_lif_bwd_grp_kernel(const BwdParams p) {
+  constexpr int NV = kGrpNV, W = grp_bwd_warps<EBP, EBG>(), NG = W / G;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ float2 xch[G > 1 ? 2 * NG * G * kMaxT : 1];
+  __shared__ float lb_red[W];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / G, wg = warp - grp * G;
+  GroupXch<G, W> gx{xch, grp, wg, 0};
+  const int T = p.T, D = p.D;
+  const float invD = 1.0f / (float)D;
+  const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
+  const SpikeLayout lay(p.R, D, 0, p.hd, p.seq);
+  constexpr int S = grp_bwd_stages<EBP, EBG>();
+  // this warp's stages (pre vectors, gradient vectors, row statistics), then x^
+  RawVec<EBP>* pre_s = reinterpret_cast<RawVec<EBP>*>(smem + (size_t)warp * grp_bwd_warp_bytes<EBP, EBG>());
+  RawVec<EBG>* gs_s = reinterpret_cast<RawVec<EBG>*>(pre_s + S * kMaxT * NV * 32);
+  float2* st_s = reinterpret_cast<float2*>(gs_s + S * kMaxT * NV * 32);
+  float4* xh_s = reinterpret_cast<float4*>(st_s + S * kMaxT);
+  auto xh_at = [&](int t, int i) { return xh_s + (t * NV + i) * 32 + lane; };
+  auto pre_at = [&](int s, int t, int i) { return pre_s + ((s * kMaxT + t) * NV + i) * 32 + lane; };
+  auto gs_at = [&](int s, int t, int i) { return gs_s + ((s * kMaxT + t) * NV + i) * 32 + lane; };
+  const float2 beta2 = make_float2(lb, lb), gain2 = make_float2(p.gain, p.gain), nvth2 = make_float2(-vth, -vth);
+  int cols[NV];
+  int64_t coff[NV];
+  float2 gg[NV][2], bb[NV][2], pb[NV][2];  // gain gamma, gain beta, bias
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = 128 * (i * G + wg) + 4 * lane;
+    cols[i] = c;
+    coff[i] = SpikeLayout(p.R, D, c, p.hd, p.seq).col_off;
+    ln_params(p, c, gain2, gg[i], bb[i], pb[i]);
+  }
+  float2 acc_g[NV][2], acc_b[NV][2], acc_d[NV][2];  // per column: sum of dL/dv x^, of dL/dv, of dL/dx
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) acc_g[i][j] = acc_b[i][j] = acc_d[i][j] = make_float2(0.0f, 0.0f);
+  float2 acc_lb = make_float2(0.0f, 0.0f);
+  const int64_t step = (int64_t)gridDim.x * NG;
+  int64_t tok = (int64_t)blockIdx.x * NG + grp;
+  auto issue = [&](int64_t tk, int s) {
+    const int64_t so = lay.tok_off(tk, D);
+    if (lane < T)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(st_s + s * kMaxT + lane)),
+                   "l"(p.stats + (int64_t)lane * p.R + tk)
+                   : "memory");
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      const int64_t rb = ((int64_t)t * p.R + tk) * p.ld;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        cp_async_vec<EBP>(pre_at(s, t, i), reinterpret_cast<const unsigned char*>(p.pre) + (rb + cols[i]) * EBP);
+        cp_async_vec<EBG>(gs_at(s, t, i),
+                          reinterpret_cast<const unsigned char*>(p.g_spikes) + (so + t * lay.t_stride + coff[i]) * EBG);
+      }
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < S - 1; ++k) {
+    if (tok + k * step < p.R) issue(tok + k * step, k);
+    cp_async_commit();
+  }
+  int s = 0;
+  for (; tok < p.R; tok += step, s = s + 1 == S ? 0 : s + 1) {
+    const int64_t tn = tok + (S - 1) * step;
+    __syncwarp();  // every lane has read the statistics of the stage about to be refilled
+    if (tn < p.R) issue(tn, s == 0 ? S - 1 : s - 1);
+    cp_async_commit();
+    cp_async_wait<S - 1>();  // this token's vectors and statistics have landed
+    __syncwarp();            // the statistics were copied by lanes t < T
+    float2 nm[kMaxT], rs[kMaxT];
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      const float2 st = t < T ? st_s[s * kMaxT + t] : make_float2(0.0f, 1.0f);
+      nm[t] = make_float2(-st.x, -st.x);
+      rs[t] = make_float2(st.y, st.y);
+    }
+    // x^ of every row (kept in shared memory for the two later passes) and
+    // the membrane before reset at every step
+    float2 u[kMaxT][NV][2];
+    {
+      float2 v[NV][2];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) v[i][0] = v[i][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int t = 0; t < kMaxT; ++t) {
+        if (t >= T) continue;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          float x[4];
+          raw_unpack<EBP>(*pre_at(s, t, i), p.pre_dtype, x);
+          float2 xh[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            xh[j] = mul2(add2(add2(make_float2(x[2 * j], x[2 * j + 1]), pb[i][j]), nm[t]), rs[t]);
+            const float2 uu = add2(mul2(v[i][j], beta2), fma2(xh[j], gg[i][j], bb[i][j]));
+            u[t][i][j] = uu;
+            v[i][j] = make_float2(uu.x > vth ? vr : uu.x, uu.y > vth ? vr : uu.y);
+          }
+          *xh_at(t, i) = make_float4(xh[0].x, xh[0].y, xh[1].x, xh[1].y);
+        }
+      }
+    }
+    // BPTT: dL/dv of every row (into u[t], which step t - 1 no longer reads),
+    // and each row's sums of g gamma and g gamma x^ (g = gain dL/dv = dL/dy)
+    float2 sums[kMaxT];
+    {
+      float2 gst[NV][2];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) gst[i][0] = gst[i][1] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int t = kMaxT - 1; t >= 0; --t) {
+        sums[t] = make_float2(0.0f, 0.0f);
+        if (t >= T) continue;
+        float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          float gsv[4];
+          raw_unpack<EBG>(*gs_at(s, t, i), p.gs_dtype, gsv);
+          const float4 x4 = *xh_at(t, i);
+          const float2 xh[2] = {make_float2(x4.x, x4.y), make_float2(x4.z, x4.w)};
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float2 uu = u[t][i][j];
+            const float2 d = add2(uu, nvth2);
+            float2 sg;
+            if constexpr (SURR == SPK_SURROGATE_SUPERSPIKE) {
+              const float2 q = fma2(make_float2(p.k, p.k), make_float2(fabsf(d.x), fabsf(d.y)), make_float2(1.f, 1.f));
+              const float2 q2 = mul2(q, q);
+              sg = make_float2(__fdividef(1.0f, q2.x), __fdividef(1.0f, q2.y));
+            } else {
+              const float2 z = mul2(make_float2(p.c_arctan, p.c_arctan), d);
+              const float2 den = fma2(z, z, make_float2(1.f, 1.f));
+              const float hk = 0.5f * p.k;
+              sg = make_float2(__fdividef(hk, den.x), __fdividef(hk, den.y));
+            }
+            const float2 from = make_float2(uu.x > vth ? 0.0f : gst[i][j].x, uu.y > vth ? 0.0f : gst[i][j].y);
+            const float2 gv = fma2(make_float2(gsv[2 * j], gsv[2 * j + 1]), sg, from);
+            if (t > 0) {
+              const float2 up = u[t - 1][i][j];
+              acc_lb = fma2(gv, make_float2(up.x > vth ? vr : up.x, up.y > vth ? vr : up.y), acc_lb);
+            }
+            gst[i][j] = mul2(gv, beta2);
+            u[t][i][j] = gv;
+            const float2 gxg = mul2(gv, gg[i][j]);  // dL/dy gamma = dL/dv gain gamma
+            sa = add2(sa, gxg);
+            sb = fma2(gxg, xh[j], sb);
+          }
+        }
+        sums[t] = make_float2(sa.x + sa.y, sb.x + sb.y);
+      }
+    }
+    warp_sum2(sums, T);
+    gx.sum(sums, T, lane);
+    // dx = rstd (g gamma - mean(g gamma) - x^ mean(g gamma x^)), and the
+    // per-column sums of dL/dv x^, dL/dv and dx
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) {
+      if (t >= T) continue;
+      const float2 ma = make_float2(-sums[t].x * invD, -sums[t].x * invD);
+      const float2 mb = make_float2(-sums[t].y * invD, -sums[t].y * invD);
+      const int64_t rb = ((int64_t)t * p.R + tok) * p.ld;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const float4 x4 = *xh_at(t, i);
+        const float2 xh[2] = {make_float2(x4.x, x4.y), make_float2(x4.z, x4.w)};
+        float dx[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float2 gv = u[t][i][j];
+          const float2 dd = mul2(fma2(xh[j], mb, fma2(gv, gg[i][j], ma)), rs[t]);
+          dx[2 * j] = dd.x;
+          dx[2 * j + 1] = dd.y;
+          acc_g[i][j] = fma2(gv, xh[j], acc_g[i][j]);
+          acc_b[i][j] = add2(acc_b[i][j], gv);
+          acc_d[i][j] = add2(acc_d[i][j], dd);
+        }
+        store4(p.g_pre, p.pre_dtype, rb + cols[i], dx);
+      }
+    }
+  }
+  // block partials: the token groups' column sums added in group order, the
+  // LIF beta term over the warps in warp order (the staging memory is reused)
+  cp_async_wait<0>();
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem);  // [NG][3 D]
+  // dL/dgamma = sum dL/dy x^ and dL/dbeta = sum dL/dy, with dL/dy = gain dL/dv
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float* r = red + (size_t)grp * 3 * D + cols[i];
+    const float2 g0 = mul2(acc_g[i][0], gain2), g1 = mul2(acc_g[i][1], gain2);
+    const float2 b0 = mul2(acc_b[i][0], gain2), b1 = mul2(acc_b[i][1], gain2);
+    *reinterpret_cast<float4*>(r) = make_float4(g0.x, g0.y, g1.x, g1.y);
+    *reinterpret_cast<float4*>(r + D) = make_float4(b0.x, b0.y, b1.x, b1.y);
+    *reinterpret_cast<float4*>(r + 2 * D) = make_float4(acc_d[i][0].x, acc_d[i][0].y, acc_d[i][1].x, acc_d[i][1].y);
+  }
+  const float lbw = warp_sum(acc_lb.x + acc_lb.y);
+  if (lane == 0) lb_red[warp] = lbw;
+  __syncthreads();
+  float* out = p.part + (int64_t)blockIdx.x * (3 * D + 1);
+  for (int c = threadIdx.x; c < 3 * D; c += blockDim.x) {
+    float a = red[c];
+#pragma unroll
+    for (int g = 1; g < NG; ++g) a += red[(size_t)g * 3 * D + c];
+    out[c] = a;
+  }
+  if (threadIdx.x == 0) {
+    float a = lb_red[0];
+#pragma unroll
+    for (int w = 1; w < W; ++w) a += lb_red[w];
+    out[3 * D] = a;
+  }
+}
+
 // column c of the [rows][W] partials (dgamma, dbeta, dbias, LIF beta): 32 row
 // groups (rows r = g mod 32, in order) per column, combined in group order
 constexpr int kSumGroups = 32;
@@ -918,8 +1443,73 @@ inline int tok_grid(int64_t R, int D) {
   const int64_t g = R < cap ? R : cap;
   return g < 1 ? 1 : (int)g;
 }
-inline int bwd_grid(int64_t R, int D, bool aligned16) {
-  return R == 0 ? 1 : (use_tok(D) && aligned16) ? tok_grid(R, D) : grid_blocks(R, pick_nw(D));
+// token-group kernels: blocks of `warps` warps, warps / G tokens at a time;
+// blocks_per_sm resident blocks (the backward holds one per SM)
+inline int grp_grid(int64_t R, int D, int blocks_per_sm, int warps = kGrpWarps) {
+  const int ng = warps / (D / 384);
+  const int64_t need = (R + ng - 1) / ng, cap = (int64_t)num_sms() * blocks_per_sm;
+  const int64_t g = need < cap ? need : cap;
+  return g < 1 ? 1 : (int)g;
+}
+constexpr int kGrpFwdBlocksPerSm = 2;
+constexpr int kGrpBwdBlocksPerSm = 1;
+
+// grp_warps: warps per block of the token-group backward (8 or kGrpBwdWarps, by input widths)
+inline int bwd_grid(int64_t R, int D, bool aligned16, int grp_warps = 8) {
+  if (R == 0) return 1;
+  if (use_grp(D) && aligned16) return grp_grid(R, D, kGrpBwdBlocksPerSm, grp_warps);
+  return use_tok(D) && aligned16 ? tok_grid(R, D) : grid_blocks(R, pick_nw(D));
+}
+
+template <int EB, int SD, int G>
+int launch_fwd_grp_g(int grid, cudaStream_t st, const FwdParams& p) {
+  constexpr size_t smem = (size_t)kGrpWarps * kGrpFwdStages * kMaxT * kGrpNV * 32 * 4 * EB;
+  static bool attr_set = false;  // per instantiation; idempotent if two threads race
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(ln_lif_fwd_grp_kernel<EB, SD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  ln_lif_fwd_grp_kernel<EB, SD, G><<<grid, 32 * kGrpWarps, smem, st>>>(p);
+  return SPK_OK;
+}
+
+template <int EB, int SD>
+int launch_fwd_grp(int D, int grid, cudaStream_t st, const FwdParams& p) {
+  if (D == 384) return launch_fwd_grp_g<EB, SD, 1>(grid, st, p);
+  if (D == 768) return launch_fwd_grp_g<EB, SD, 2>(grid, st, p);
+  return launch_fwd_grp_g<EB, SD, 4>(grid, st, p);
+}
+
+template <int EBP, int EBG, int SURR, int G>
+int launch_bwd_grp_g(int grid, cudaStream_t st, const BwdParams& p) {
+  constexpr size_t smem = grp_bwd_smem_bytes<EBP, EBG>();
+  static_assert(smem >= (size_t)grp_bwd_warps<EBP, EBG>() * 3 * 384 * sizeof(float),
+                "block partials reuse the staging memory");
+  static_assert(smem <= 227 * 1024, "staging exceeds the shared memory of a block");
+  static bool attr_set = false;  // per instantiation; idempotent if two threads race
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(ln_lif_bwd_grp_kernel<EBP, EBG, SURR, G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  ln_lif_bwd_grp_kernel<EBP, EBG, SURR, G><<<grid, 32 * grp_bwd_warps<EBP, EBG>(), smem, st>>>(p);
+  return SPK_OK;
+}
+
+template <int EBP, int EBG, int SURR>
+int launch_bwd_grp_d(int D, int grid, cudaStream_t st, const BwdParams& p) {
+  if (D == 384) return launch_bwd_grp_g<EBP, EBG, SURR, 1>(grid, st, p);
+  if (D == 768) return launch_bwd_grp_g<EBP, EBG, SURR, 2>(grid, st, p);
+  return launch_bwd_grp_g<EBP, EBG, SURR, 4>(grid, st, p);
+}
+
+template <int SURR>
+int launch_bwd_grp(bool p32, bool g32, int D, int grid, cudaStream_t st, const BwdParams& p) {
+  if (p32) return g32 ? launch_bwd_grp_d<4, 4, SURR>(D, grid, st, p) : launch_bwd_grp_d<4, 2, SURR>(D, grid, st, p);
+  return g32 ? launch_bwd_grp_d<2, 4, SURR>(D, grid, st, p) : launch_bwd_grp_d<2, 2, SURR>(D, grid, st, p);
 }
 
 }  // namespace lnlif
@@ -964,9 +1554,9 @@ extern "C" {
 int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D) {
   (void)T;
   if (D < 32 || D > 4 * 32 * spk::lnlif::kMaxCpt || R < 0) return 0;
-  // the larger of the backward's two possible grids on the current device (one
-  // partial row per block)
-  const int g1 = spk::lnlif::bwd_grid(R, (int)D, true), g2 = spk::lnlif::bwd_grid(R, (int)D, false);
+  // the largest of the backward's possible grids on the current device (one
+  // partial row per block); fewer warps per block give more blocks
+  const int g1 = spk::lnlif::bwd_grid(R, (int)D, true, 8), g2 = spk::lnlif::bwd_grid(R, (int)D, false);
   return (int64_t)(g1 > g2 ? g1 : g2) * (3 * D + 1) * (int64_t)sizeof(float);
 }
 
@@ -994,7 +1584,19 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
               "D=%lld > %d needs pre, spikes, ln_gamma, ln_beta and pre_bias 16-byte aligned", (long long)D,
               32 * kMaxCpt);
   if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
-  if (use_tok((int)D) && aligned16) {
+  if (use_grp((int)D) && aligned16) {
+    const int grid = grp_grid(R, (int)D, pre_dtype == SPK_F32 ? 1 : kGrpFwdBlocksPerSm);
+    if (pre_dtype == SPK_F32) {
+      rc = spike_dtype == SPK_F32    ? launch_fwd_grp<4, SPK_F32>((int)D, grid, st, p)
+           : spike_dtype == SPK_BF16 ? launch_fwd_grp<4, SPK_BF16>((int)D, grid, st, p)
+                                     : launch_fwd_grp<4, -1>((int)D, grid, st, p);
+    } else {
+      rc = spike_dtype == SPK_F32    ? launch_fwd_grp<2, SPK_F32>((int)D, grid, st, p)
+           : spike_dtype == SPK_BF16 ? launch_fwd_grp<2, SPK_BF16>((int)D, grid, st, p)
+                                     : launch_fwd_grp<2, -1>((int)D, grid, st, p);
+    }
+    if (rc != SPK_OK) return rc;
+  } else if (use_tok((int)D) && aligned16) {
     const int grid = tok_grid(R, (int)D), threads = (int)D / 4;
     if (pre_dtype == SPK_F32) {
       spike_dtype == SPK_F32 ? ln_lif_fwd_tok_kernel<4, SPK_F32><<<grid, threads, 0, st>>>(p)
@@ -1045,7 +1647,8 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
               "D=%lld > %d needs g_spikes, pre, g_pre, ln_gamma, ln_beta and pre_bias 16-byte aligned",
               (long long)D, 32 * kMaxCpt);
   if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
-  const int grid = bwd_grid(R, (int)D, aligned16);
+  const int grid = bwd_grid(R, (int)D, aligned16,
+                            pre_dtype == SPK_F32 && gs_dtype == SPK_F32 ? 8 : kGrpBwdWarps);
   SPK_REQUIRE((int64_t)grid * (3 * D + 1) * 4 <= workspace_bytes, SPK_ERR_INVALID, "workspace too small for %d blocks",
               grid);
   float* part = reinterpret_cast<float*>(workspace);
@@ -1057,7 +1660,12 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
                    ln_beta, lif_beta, lif_vth, lif_vreset, in_gain, surrogate, surrogate_k,
                    (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k), g_pre, part, (int)T, R, (int)D, 0,
                    (int)(head_dim > 0 ? head_dim : 0), (int)(seq_len > 0 ? seq_len : 1), pre_ld > 0 ? pre_ld : D};
-    if (use_tok((int)D) && aligned16) {
+    if (use_grp((int)D) && aligned16) {
+      const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;
+      rc = surrogate == SPK_SURROGATE_ARCTAN ? launch_bwd_grp<SPK_SURROGATE_ARCTAN>(p32, g32, (int)D, grid, st, p)
+                                             : launch_bwd_grp<SPK_SURROGATE_SUPERSPIKE>(p32, g32, (int)D, grid, st, p);
+      if (rc != SPK_OK) return rc;
+    } else if (use_tok((int)D) && aligned16) {
       const int threads = (int)D / 4;
       const bool p32 = pre_dtype == SPK_F32, g32 = gs_dtype == SPK_F32;
       if (surrogate == SPK_SURROGATE_ARCTAN)

@@ -301,28 +301,41 @@ def bench_shapes_once():
 
 def bench_lnlif(iters, R=16384, T=4):
     """LayerNorm->LIF training kernels (``ops.ln_lif_fwd`` / ``ops.ln_lif_bwd``)
-    at the encoder shapes of 64 images per GPU: R tokens x T rows, D = 384 and
-    1536, bf16 pre-activation, spikes and gradient, with the folded bias.
-    Algorithmic bytes: forward pre + spikes, backward pre + gradient + g_pre."""
+    at the encoder shapes of 64 images per GPU: R tokens x T rows, bf16
+    pre-activation with the folded bias. Cases: D = 384 and 1536 with bf16
+    spikes and gradient (the MLP hidden layer and the plain row-major form),
+    D = 384 with head-major spikes and gradient [T*B, 8, 256, 48] (Q, K, V),
+    and D = 384 with fp32 spikes and gradient (spikes that join the residual
+    stream). Algorithmic bytes: forward pre + spikes + the row statistics,
+    backward pre + gradient + g_pre + the statistics; every input rotates
+    over three copies, 150 MB or more per set."""
     res = []
     g = torch.Generator(device="cuda").manual_seed(0)
-    for D in (384, 1536):
+    cases = ((384, torch.bfloat16, None), (1536, torch.bfloat16, None), (384, torch.bfloat16, (48, 256)),
+             (384, torch.float32, None))
+    for D, sdt, heads in cases:
         copies = 3
         pres = [torch.randn(T * R, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(copies)]
-        gss = [torch.randn(T * R, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(copies)]
+        gshape = (T * R // heads[1], D // heads[0], heads[1], heads[0]) if heads else (T * R, D)
+        gss = [torch.randn(gshape, device="cuda", generator=g).to(sdt) for _ in range(copies)]
         gamma, beta = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
         bias = torch.zeros(D, device="cuda")
         lif = torch.tensor([0.5, 1.0, 0.0], device="cuda")
         stats = ops.ln_lif_fwd(pres[0], gamma, beta, 1e-5, lif[0:1], lif[1:2], lif[2:3], T, in_gain=0.5,
-                               spike_dtype=torch.bfloat16, bias=bias)[1]
+                               spike_dtype=sdt, bias=bias, heads=heads)[1]
         fms = _time(lambda i: ops.ln_lif_fwd(pres[i % copies], gamma, beta, 1e-5, lif[0:1], lif[1:2], lif[2:3], T,
-                                             in_gain=0.5, spike_dtype=torch.bfloat16, bias=bias), iters)
+                                             in_gain=0.5, spike_dtype=sdt, bias=bias, heads=heads), iters)
         bms = _time(lambda i: ops.ln_lif_bwd(gss[i % copies], pres[i % copies], stats, gamma, beta, lif[0:1],
-                                             lif[1:2], lif[2:3], T, 0.5, "arctan", 2.0, bias=bias, need_bias=True),
-                    iters)
-        el = T * R * D
-        res.append({"kernel": "ln_lif_fwd", "rows": T * R, "D": D, "us": fms * 1e3, "GB/s": el * 4 / fms / 1e6})
-        res.append({"kernel": "ln_lif_bwd", "rows": T * R, "D": D, "us": bms * 1e3, "GB/s": el * 6 / bms / 1e6})
+                                             lif[1:2], lif[2:3], T, 0.5, "arctan", 2.0, bias=bias, need_bias=True,
+                                             heads=heads), iters)
+        el, rows, es = T * R * D, T * R, torch.finfo(sdt).bits // 8
+        fbytes = el * (2 + es) + rows * 8
+        bbytes = el * (2 + es + 2) + rows * 8
+        tag = "D=%d %s%s" % (D, str(sdt).replace("torch.", ""), " head-major" if heads else "")
+        res.append({"kernel": "ln_lif_fwd", "case": tag, "rows": rows, "D": D, "us": fms * 1e3,
+                    "GB/s": fbytes / fms / 1e6})
+        res.append({"kernel": "ln_lif_bwd", "case": tag, "rows": rows, "D": D, "us": bms * 1e3,
+                    "GB/s": bbytes / bms / 1e6})
     return res
 
 

@@ -536,6 +536,10 @@ def test_bounded_wait_gives_up_and_reports_timeout(ops):
     (1, 5, 512, torch.float32, "superspike", 1.0),
     (2, 9, 1536, torch.float32, "superspike", 1.0),
     (4, 30, 256, torch.float16, "arctan", 1.0),
+    (4, 12, 768, torch.bfloat16, "superspike", 1.0),  # two warps per token
+    (1, 7, 768, torch.float32, "arctan", 0.5),
+    (3, 10, 384, torch.bfloat16, "superspike", 1.0),
+    (4, 301, 384, torch.bfloat16, "arctan", 1.0),     # several tokens per warp
 ])
 def test_ln_lif_train_fwd_bwd(ops, T, R, D, pre_dtype, surrogate, gain):
     g = gen(T * 100 + R + D)
@@ -609,6 +613,26 @@ def test_ln_lif_train_head_major_spikes(ops, pre_dtype, gs_dtype):
                        bias=bias, need_bias=True, heads=(dh, N))
     for x, y in zip(a, b):
         assert (x is None and y is None) or torch.equal(x, y)
+
+
+@pytest.mark.parametrize("D", [384, 1536])
+def test_ln_lif_train_bf16_gradient_equals_fp32_path(ops, D):
+    """A bf16 spike gradient gives the same results as the same values in fp32
+    (the kernels widen every input to fp32 before any arithmetic)."""
+    g = gen(D + 5)
+    T, R = 4, 700
+    pre = (torch.randn(T * R, D, generator=g) * 1.4).to(torch.bfloat16).to(DEV)
+    gamma = (1.0 + 0.2 * torch.randn(D, generator=g)).to(DEV)
+    beta_ln = (0.3 * torch.randn(D, generator=g)).to(DEV)
+    bias = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    _, stats = ops.ln_lif_fwd(pre, gamma, beta_ln, 1e-5, 0.8, 1.0, 0.0, T, bias=bias, spike_dtype=torch.bfloat16)
+    gs16 = torch.randn(T * R, D, generator=g).to(torch.bfloat16).to(DEV)
+    a = ops.ln_lif_bwd(gs16, pre, stats, gamma, beta_ln, 0.8, 1.0, 0.0, T, 1.0, "arctan", 2.0, bias=bias,
+                       need_bias=True)
+    b = ops.ln_lif_bwd(gs16.float(), pre, stats, gamma, beta_ln, 0.8, 1.0, 0.0, T, 1.0, "arctan", 2.0, bias=bias,
+                       need_bias=True)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
 
 
 def test_ln_lif_train_unaligned_inputs(ops):
