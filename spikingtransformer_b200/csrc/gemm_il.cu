@@ -36,6 +36,10 @@ namespace gil {
 
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
+// the T = 4 epilogue: 16 warps, four groups of one warp per TMEM lane quadrant
+// (each accumulator drained by two groups, one per half of the CTA's columns)
+constexpr int kEpiWarpsTV = 16;
+constexpr int kThreadsTV = 32 * (2 + kEpiWarpsTV);
 constexpr int kBK = 64;
 constexpr int kAStage = 128 * 128;
 constexpr int kMaxSmem = 232448;
@@ -50,6 +54,8 @@ struct Params {
   int64_t R;
   int K, N, n_cta, cs, num_m_tiles, stages, wbox;
   int res_prefetch;  // the residual rows may be bulk-prefetched (16-byte aligned blocks)
+  int nbox;          // T = 4 epilogue: staging boxes per warp
+  int epi_warps;     // T = 4 epilogue: 8 or 16 epilogue warps
   int epi;           // epilogue variant (kEpiTranspose, kEpiTV, kEpiTB)
   uint32_t tmem_cols;
   const float *bias, *gamma, *beta_ln;
@@ -90,16 +96,18 @@ __host__ __device__ inline size_t smem_layout(const Params& p, uint8_t* base, Sm
   size_t oa = take((size_t)p.stages * kAStage, 1024);
   size_t ow = take((size_t)p.stages * p.n_cta * 128, 1024);
   size_t oon = take(128 * 32, 128), obs = take((size_t)p.n_cta * 32, 128);
-  size_t oxs = p.epi == 1   ? take((size_t)kEpiWarps * 2 * kStgBox, 1024)
+  size_t oxs = p.epi == 1   ? take((size_t)p.epi_warps * p.nbox * kStgBox, 1024)
                : p.epi == 0 ? take(kEpiWarps * 32 * kXS * 4, 16)
                             : take((size_t)kEpiWarps * p.T * 2048, 1024);
   size_t ob = take(p.n_cta * 4, 16), og = take(p.n_cta * 4, 16), obe = take(p.n_cta * 4, 16);
-  size_t ost = take(2 * 2 * 128 * 8, 16);
+  // (mean, M2) of the two column halves: [2 parities][2 halves][128 rows]; the
+  // T = 4 epilogue keeps two slots per parity ([2][2 slots][2][128])
+  size_t ost = take((size_t)(p.epi == 1 ? 2 : 1) * 2 * 2 * 128 * 8, 16);
   size_t oxb = take((size_t)2 * p.cs * 128 * 8, 16);
   size_t omw = take(16 * 8, 8);
   size_t ofu = take(p.stages * 8, 8), oem = take(p.stages * 8, 8);
   size_t oaf = take(16, 8), oae = take(16, 8), oxbar = take(16, 8), odr = take(8, 8);
-  size_t orb = take(kEpiWarps * 2 * 8, 8);
+  size_t orb = take(kEpiWarpsTV * 2 * 8, 8);
   size_t otm = take(4, 4), oab = take(4, 4);
   if (s) {
     s->a = base + oa;
@@ -157,6 +165,7 @@ __device__ __forceinline__ float2 merge_weights(float na, float nb) {
 
 // (mean, M2) of the calling thread's TMEM lane over nch 32-column chunks starting at trow
 // (32x32b loads, double-buffered); sums shifted by the row's first value
+template <bool DB = true>
 __device__ __forceinline__ void lane_row_stats(uint32_t trow, int nch, float inv_cols, float& mean, float& m2) {
   float2 s1a = make_float2(0.0f, 0.0f), s2a = s1a, s1b = s1a, s2b = s1a, nK2 = s1a;
   auto stats_chunk = [&](const uint32_t (&r)[32]) {
@@ -171,6 +180,19 @@ __device__ __forceinline__ void lane_row_stats(uint32_t trow, int nch, float inv
     }
   };
   float K = 0.0f;
+  if constexpr (!DB) {
+    // single-buffered (register-lean) form
+    for (int c = 0; c < nch; ++c) {
+      uint32_t ra[32];
+      tmem_ld32_raw(trow + c * 32, ra);
+      tmem_wait_ld_fence32(ra);
+      if (c == 0) {
+        K = __uint_as_float(ra[0]);
+        nK2 = make_float2(-K, -K);
+      }
+      stats_chunk(ra);
+    }
+  } else {
   uint32_t ra[32], rb[32];
   tmem_ld32_raw(trow, ra);
   for (int c = 0; c < nch; ++c) {
@@ -188,6 +210,7 @@ __device__ __forceinline__ void lane_row_stats(uint32_t trow, int nch, float inv
       stats_chunk(rb);
     }
   }
+  }
   const float S1 = (s1a.x + s1a.y) + (s1b.x + s1b.y);
   const float S2 = (s2a.x + s2a.y) + (s2b.x + s2b.y);
   mean = K + S1 * inv_cols;
@@ -197,14 +220,18 @@ __device__ __forceinline__ void lane_row_stats(uint32_t trow, int nch, float inv
 // epilogue variants
 constexpr int kEpiTranspose = 0;  // rows tok*T + t, lanes transposed through shared memory
 constexpr int kEpiTV = 1;         // T = 4, rows t-major within groups of 8 tokens, transposed TMEM reads
+constexpr int kEpiTV8 = 3;        // the same with 8 epilogue warps (long K: the tensor cores set the pace)
+__host__ __device__ constexpr bool is_tv(int e) { return e == kEpiTV || e == kEpiTV8; }
+__host__ __device__ constexpr int tv_warps(int e) { return e == kEpiTV ? kEpiWarpsTV : kEpiWarps; }
 constexpr int kEpiTB = 2;         // t-broadcast: rows are tokens, one pre-activation for every step
 
 template <int T, bool FAST, bool RES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(EPI == kEpiTV ? kThreadsTV : kThreads, 1)
     gemm_il_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmO, const Params p) {
   constexpr int CPL = 16 / T;  // columns per lane after the transposition
   constexpr int TPQ = 32 / T;  // tokens per TMEM lane quadrant
+  constexpr int NT = EPI == kEpiTV ? kThreadsTV : kThreads;
   pdl_trigger();
   // dynamic shared memory, 1024-byte aligned (128-byte swizzle atoms); pointers derived from
   // it by plain arithmetic so the compiler keeps them in the shared address space
@@ -226,12 +253,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.acc_full[i], 1);
-      mbar_init(&sm.acc_empty[i], EPI != kEpiTranspose ? kEpiWarps / 2 : kEpiWarps);
+      mbar_init(&sm.acc_empty[i], is_tv(EPI) ? tv_warps(EPI) / 2 : EPI == kEpiTB ? kEpiWarps / 2 : kEpiWarps);
       mbar_init(&sm.xbar[i], 1);  // one local arrive (with the expected bytes) per use
     }
     mbar_init(sm.drain, 1);
-    if (EPI == kEpiTV)
-      for (int i = 0; i < kEpiWarps * 2; ++i) mbar_init(&sm.rbar[i], 1);
+    if (is_tv(EPI))
+      for (int i = 0; i < kEpiWarpsTV * 2; ++i) mbar_init(&sm.rbar[i], 1);
     *sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -245,13 +272,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // no-swizzle K-major layout: 8 x 8 core matrices of 128 bytes, (row, k) at
     // (row / 8) * 256 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2
     const int n0 = (int)rank * p.n_cta;
-    for (int i = threadIdx.x; i < 128 * 2; i += kThreads) {
+    for (int i = threadIdx.x; i < 128 * 2; i += NT) {
       const int r = i >> 1, k8 = i & 1;
       uint4 w = make_uint4(0u, 0u, 0u, 0u);
       if (k8 == 0) w.x = 0x3F803F80u;  // 1.0, 1.0
       *reinterpret_cast<uint4*>(sm.ones + (r >> 3) * 256 + k8 * 128 + (r & 7) * 16) = w;
     }
-    for (int i = threadIdx.x; i < p.n_cta * 2; i += kThreads) {
+    for (int i = threadIdx.x; i < p.n_cta * 2; i += NT) {
       const int r = i >> 1, k8 = i & 1;
       uint4 w = make_uint4(0u, 0u, 0u, 0u);
       if (k8 == 0 && p.bias) {
@@ -273,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.mw[r] = r == 0 ? merge_weights((float)(p.n_cta >> 1), (float)(p.n_cta >> 1))
                         : merge_weights((float)(p.n_cta * r), (float)p.n_cta);
     }
-    for (int c = threadIdx.x; c < p.n_cta; c += kThreads) {
+    for (int c = threadIdx.x; c < p.n_cta; c += NT) {
       sm.bias[c] = p.bias ? p.bias[n0 + c] : 0.0f;
       sm.gamma[c] = (p.gamma ? p.gamma[n0 + c] : 1.0f) * g;
       sm.beta[c] = (p.beta_ln ? p.beta_ln[n0 + c] : 0.0f) * g;
@@ -315,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           outstanding &= ~(1u << stage);
           if (*((volatile int*)sm.abort_flag)) { ok = false; break; }
           mbar_expect_tx(&sm.full[stage], bytes);
-          if (EPI == kEpiTV)  // dims {K, 8 tokens, T, R / 8}: rows g*32 + t*8 + k
+          if (is_tv(EPI))  // dims {K, 8 tokens, T, R / 8}: rows g*32 + t*8 + k
             tma_load_4d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, 0, 0, tile * 4);
           else if (EPI == kEpiTB)  // dims {K, R}: rows = tokens
             tma_load_2d(sm.a + (size_t)stage * kAStage, &tmA, &sm.full[stage], kc * kBK, tile * 128);
@@ -375,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       mbar_wait(sm.drain, 0, 123);
     }
-  } else if constexpr (EPI == kEpiTV) {
+  } else if constexpr (is_tv(EPI)) {
     // ---------------------------------------------------------------- epilogue, transposed TMEM reads
     // Tile rows are ordered q*32 + t*8 + k (k = token within the quadrant's group of 8), so two
     // 16x256b loads at lanes q*32 and q*32 + 16 hand thread i all four steps of token i/4 for the
@@ -383,38 +410,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 32-column chunk are staged with stmatrix as a [t][token][32] box in the 64-byte swizzle and
     // written by one TMA store per warp; with a residual, the box is first loaded by TMA, added to
     // with ldmatrix / stmatrix, and stored back.
+    // The epilogue warps form groups of one warp per lane quadrant; group g drains accumulator
+    // g % 2 (every other tile of the CTA's sequence).  With 16 warps (short K, where the
+    // epilogue sets the pace) group g covers the columns [h n_cta / 2, (h + 1) n_cta / 2), h =
+    // g / 2, and a row's statistics are merged over the two halves through shared memory (one
+    // named barrier per accumulator) before the cluster merge: four epilogue warps per scheduler
+    // hide each other's TMEM, shuffle and arithmetic latencies, and TMEM is read single-buffered.
+    // With 8 warps (long K) a group covers all of the CTA's columns and reads TMEM
+    // double-buffered.
     static_assert(T == 4 && FAST, "transposed-read epilogue: T = 4, bf16 spikes or residual");
-    static_assert(EPI == kEpiTV, "");
+    constexpr int EW = tv_warps(EPI);   // epilogue warps
+    constexpr int HALVES = EW / 8;      // groups per accumulator: column halves of the slice
     const int ew = warp - 2;
     const int q = warp & 3;         // TMEM lane quadrant
-    const int grp = ew >> 2;        // tile parity: group g drains accumulator g of every other tile
+    const int grp = ew >> 2;        // 0..3
+    const int buf = grp & 1;        // accumulator (tile parity) drained by this group
+    const int h = grp >> 1;         // column half of the CTA's slice (0 with 8 warps)
     const int tok_l = lane >> 2;    // token within the group of 8
     const int cp = lane & 3;        // column pair within each 8-column group
-    const int nch = p.n_cta / 32;
+    const int half = p.n_cta / HALVES;
+    const int nch = half / 32;      // this warp's 32-column chunks
+    const int c0 = h * half;        // this warp's first column within the CTA's slice
+    const int row = q * 32 + lane;  // this lane's tile row in the statistics pass
     const uint32_t lane_lo = (uint32_t)(q * 32) << 16, lane_hi = (uint32_t)(q * 32 + 16) << 16;
     const float beta = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
     const float2 beta2 = make_float2(beta, beta), nbeta2 = make_float2(-beta, -beta);
     const float bvr = __fmul_rn(beta, vr);
     const float2 bvr2 = make_float2(bvr, bvr);
-    const int n0 = (int)rank * p.n_cta;
-    const float inv_cta = 1.0f / (float)p.n_cta;
+    const int n0 = (int)rank * p.n_cta + c0;  // this warp's first output column
+    const float inv_half = 1.0f / (float)half;
     const float inv_n_all = 1.0f / (float)p.N;
-    // this warp's two staging boxes; lane i addresses row i%8 of matrix i/8 (8-column group) in
-    // the 64-byte swizzle (16-byte unit u of row r at u ^ ((r >> 1) & 3))
-    uint8_t* stg = sm.stg + (size_t)ew * 2 * kStgBox;
+    const float2 w_half = sm.mw[0];
+    // this warp's staging boxes (two with a residual: the next chunk's residual box loads while
+    // this one is added to; else one); lane i addresses row i%8 of matrix i/8 (8-column group)
+    // in the 64-byte swizzle (16-byte unit u of row r at u ^ ((r >> 1) & 3))
+    constexpr int NBOX = (EW == 8 || RES) ? 2 : 1;
+    constexpr uint32_t kBoxMask = NBOX - 1;
+    uint8_t* stg = sm.stg + (size_t)ew * NBOX * kStgBox;
     const int r8 = lane & 7, m8 = lane >> 3;
     const uint32_t mat_off = (uint32_t)(r8 * 64 + ((m8 ^ ((r8 >> 1) & 3)) << 4));
     uint64_t* rbar = sm.rbar + ew * 2;
-    uint32_t sc = 0;      // boxes staged so far by this warp (buffer sc & 1)
+    uint32_t sc = 0;      // boxes staged so far by this warp (buffer sc & kBoxMask)
     uint32_t rpar = 0;    // bit b: parity of the next residual-box completion on buffer b
     uint32_t rout = 0;    // bit b: a residual box is in flight to buffer b (warp-uniform)
     bool rfail = false;   // a residual box did not land in time: stop waiting for them
     if (lane == 0) tma_prefetch_desc(&tmO);
-    // the two groups take alternate tiles of this CTA's sequence (iteration parity = group), so
-    // one group's waits overlap the other's arithmetic; each warp covers all n_cta columns
-    int iter = grp;
-    for (int tile = cid + grp * ncl; tile < p.num_m_tiles; tile += 2 * ncl, iter += 2) {
-      const int buf = grp;
+    int iter = buf;
+    for (int tile = cid + buf * ncl; tile < p.num_m_tiles; tile += 2 * ncl, iter += 2) {
       const int y0 = tile * 32 + q * 8;  // first token of this warp's rows
       if (RES && lane == 0) {
         // the tile's first residual box: its latency hides behind the statistics
@@ -426,22 +468,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (RES) rout |= 1u << (sc & 1u);
       if (!mbar_wait(&sm.acc_full[buf], (uint32_t)(iter >> 1) & 1u, 131)) { atomicExch(sm.abort_flag, 1); break; }
       tc_fence_after();
-      const uint32_t tcol = tmem + (uint32_t)(buf * p.n_cta);
-      // ---- statistics: lane l owns tile row q*32 + l (= step l / 8 of token l % 8) over the CTA's
-      // columns (32x32b loads), sums shifted by the row's first value (the accumulator already
-      // holds the bias)
+      const uint32_t tcol = tmem + (uint32_t)(buf * p.n_cta + c0);
+      // ---- statistics: lane l owns tile row q*32 + l (= step l / 8 of token l % 8) over this
+      // warp's columns (32x32b loads), sums shifted by the row's first value (the accumulator
+      // already holds the bias)
       float mean, m2;
-      lane_row_stats(tcol + lane_lo, nch, inv_cta, mean, m2);
-      // ---- merge across the CTAs of the cluster (the row's columns are split over them)
+      lane_row_stats<EW == 8>(tcol + lane_lo, nch, inv_half, mean, m2);
+      // ---- merge the two column halves (the other group of this accumulator holds the other
+      // half); two slots per accumulator, alternating by tile, so a slot is rewritten only after
+      // a barrier that every reader of it has passed
+      if constexpr (HALVES == 2) {
+        float2* st = sm.stat + (size_t)(buf * 2 + ((iter >> 1) & 1)) * 256;
+        st[h * 128 + row] = make_float2(mean, m2);
+        named_bar_sync(2 + buf, 32 * EW / 2);
+        const float2 o = st[(h ^ 1) * 128 + row];
+        const float2 a = h == 0 ? make_float2(mean, m2) : o;
+        const float2 b = h == 0 ? o : make_float2(mean, m2);
+        mean = a.x;
+        m2 = a.y;
+        chan_merge(mean, m2, b.x, b.y, w_half);
+      }
+      // ---- merge across the CTAs of the cluster (the row's columns are split over them); the
+      // first-half group sends, both groups wait and merge
       if (cs > 1) {
-        const int par = grp;
+        const int par = buf;
         float2* xb = sm.xbuf + (size_t)par * cs * 128;
-        const int row = q * 32 + lane;
-        const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + row);
-        const uint32_t bar = smem_u32(&sm.xbar[par]);
-        for (int r = 0; r < cs; ++r)
-          st_async_f32x2(mapa_shared(slot, (uint32_t)r), mean, m2, mapa_shared(bar, (uint32_t)r));
-        if (ew == grp * 4 && lane == 0) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
+        if (h == 0) {
+          const uint32_t slot = smem_u32(xb + (size_t)rank * 128 + row);
+          const uint32_t bar = smem_u32(&sm.xbar[par]);
+          for (int r = 0; r < cs; ++r)
+            st_async_f32x2(mapa_shared(slot, (uint32_t)r), mean, m2, mapa_shared(bar, (uint32_t)r));
+          if (ew == grp * 4 && lane == 0) mbar_expect_tx(&sm.xbar[par], (uint32_t)(cs * 128 * 8));
+        }
         if (!mbar_wait_cluster(&sm.xbar[par], (uint32_t)((iter >> 1) & 1), 132)) {
           atomicExch(sm.abort_flag, 1);
           break;
@@ -467,13 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // ---- normalise, LIF over t in registers, stage and store one box per 32 columns
       auto lif_chunk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16], int c) {
-        const int b = (int)(sc & 1u);
+        const int b = (int)(sc & kBoxMask);
         uint8_t* box = stg + b * kStgBox;
         const uint32_t box_lane = smem_u32(box) + mat_off;
         uint32_t bits[4][4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int col = c * 32 + 8 * j + 2 * cp;
+          const int col = c0 + c * 32 + 8 * j + 2 * cp;
           const float2 g2 = *reinterpret_cast<const float2*>(sm.gamma + col);
           const float2 e2 = *reinterpret_cast<const float2*>(sm.beta + col);
           float2 u = make_float2(0.0f, 0.0f), sp = u;
@@ -524,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stmatrix_x4(box_lane + t * 512, rv[0], rv[1], rv[2], rv[3]);
           }
         } else {
-          if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+          if (lane == 0) bulk_wait_read<NBOX - 1>();  // the store that last read this box is done with it
           __syncwarp();
 #pragma unroll
           for (int t = 0; t < 4; ++t) stmatrix_x4(box_lane + t * 512, bits[t][0], bits[t][1], bits[t][2], bits[t][3]);
@@ -537,7 +595,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++sc;
       };
-      {
+      if constexpr (EW == 16) {
+        // single-buffered TMEM reads: the other three warps of the scheduler run meanwhile
+        for (int c = 0; c < nch; ++c) {
+          uint32_t a0[16], a1[16];
+          tmem_ld16x256_x4_raw(tcol + lane_lo + c * 32, a0);
+          tmem_ld16x256_x4_raw(tcol + lane_hi + c * 32, a1);
+          tmem_wait_ld_fence2(a0, a1);
+          if (c + 1 == nch) {
+            // last TMEM read of this buffer: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+          }
+          lif_chunk(a0, a1, c);
+        }
+      } else {
+        // double-buffered TMEM reads: chunk c + 1 loads while chunk c is processed
         uint32_t a0[16], a1[16], b0[16], b1[16];
         tmem_ld16x256_x4_raw(tcol + lane_lo, a0);
         tmem_ld16x256_x4_raw(tcol + lane_hi, a1);
@@ -1202,10 +1276,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const Params);
 
 template <int T>
-KernelFn pick_kernel(bool fast, bool res, bool tv) {
+KernelFn pick_kernel(bool fast, bool res, bool tv, bool tv16) {
   if (!fast) return gemm_il_kernel<T, false, true, kEpiTranspose>;
   if constexpr (T == 4) {
-    if (tv) return res ? gemm_il_kernel<4, true, true, kEpiTV> : gemm_il_kernel<4, true, false, kEpiTV>;
+    if (tv && tv16) return res ? gemm_il_kernel<4, true, true, kEpiTV> : gemm_il_kernel<4, true, false, kEpiTV>;
+    if (tv) return res ? gemm_il_kernel<4, true, true, kEpiTV8> : gemm_il_kernel<4, true, false, kEpiTV8>;
   }
   return res ? gemm_il_kernel<T, true, true, kEpiTranspose> : gemm_il_kernel<T, true, false, kEpiTranspose>;
 }
@@ -1274,6 +1349,11 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   const bool tv = !t_broadcast && T == 4 && fast && R % 8 == 0 && N % 8 == 0 && out != nullptr &&
                   !(res && spk_bf16) && aligned(out, 16);
   p.epi = t_broadcast ? kEpiTB : tv ? kEpiTV : kEpiTranspose;
+  // T = 4 epilogue: 16 warps where it sets the pace (K <= 512), else 8 (the deeper operand
+  // pipeline that the smaller staging area leaves room for keeps the tensor cores fed)
+  const bool tv16 = tv && K <= 512;
+  p.epi_warps = tv16 ? kEpiWarpsTV : kEpiWarps;
+  p.nbox = tv16 && residual == nullptr ? 1 : 2;
 
   CUtensorMap tmA, tmW, tmO;
   int rc;
@@ -1324,11 +1404,11 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
     kern = gemm_il_kernel<1, true, false, kEpiTB>;  // T is read from the parameters
   } else {
     switch (T) {
-      case 1: kern = pick_kernel<1>(fast, res, false); break;
-      case 2: kern = pick_kernel<2>(fast, res, false); break;
-      case 4: kern = pick_kernel<4>(fast, res, tv); break;
-      case 8: kern = pick_kernel<8>(fast, res, false); break;
-      default: kern = pick_kernel<16>(fast, res, false); break;
+      case 1: kern = pick_kernel<1>(fast, res, false, false); break;
+      case 2: kern = pick_kernel<2>(fast, res, false, false); break;
+      case 4: kern = pick_kernel<4>(fast, res, tv, tv16); break;
+      case 8: kern = pick_kernel<8>(fast, res, false, false); break;
+      default: kern = pick_kernel<16>(fast, res, false, false); break;
     }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1338,7 +1418,7 @@ int launch_gemm_il(const void* A, const void* W, const float* bias, const float*
   if (clusters < 1) clusters = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(clusters * cs), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(tv16 ? kThreadsTV : kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];

@@ -204,6 +204,7 @@ def test_linear_ln_lif_fast(ops, T, R, K, N, gain, vr, res):
     (104, 128, 64, 1.0, 0.0, False),     # one 32-column chunk per warp
     (72, 192, 512, 0.8, 0.1, True),      # 2-CTA cluster of 256 columns, K not a multiple of 64
     (40, 384, 256, 1.0, 0.0, False),
+    (48, 768, 384, 0.5, 0.0, False),     # K > 512: the 8-warp epilogue without a residual
 ])
 def test_linear_ln_lif_t4_transposed_epilogue(ops, R, K, N, gain, vr, res):
     """T = 4 with a token count divisible by 8 and one bf16 output (the spikes,
