@@ -524,7 +524,9 @@ __global__ void __launch_bounds__(EPI == kEpiTV ? kThreadsTV : kThreads, 1)
         nmr2[t] = make_float2(nmr, nmr);
       }
       // ---- normalise, LIF over t in registers, stage and store one box per 32 columns
-      auto lif_chunk = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16], int c) {
+      // `next` runs once this chunk's TMEM registers are consumed (before the staging and the
+      // store): the single-buffered form issues the next chunk's TMEM loads there
+      auto lif_chunk = [&](uint32_t (&lo)[16], uint32_t (&hi)[16], int c, auto&& next) {
         const int b = (int)(sc & kBoxMask);
         uint8_t* box = stg + b * kStgBox;
         const uint32_t box_lane = smem_u32(box) + mat_off;
@@ -550,6 +552,7 @@ __global__ void __launch_bounds__(EPI == kEpiTV ? kThreadsTV : kThreads, 1)
             bits[t][j] = bf16x2_of_01(sp.x, sp.y);
           }
         }
+        next(lo, hi);
         if constexpr (RES) {
           if (!rfail && !mbar_wait(&rbar[b], (rpar >> b) & 1u, 133)) {
             atomicExch(sm.abort_flag, 1);
@@ -595,20 +598,27 @@ __global__ void __launch_bounds__(EPI == kEpiTV ? kThreadsTV : kThreads, 1)
         }
         ++sc;
       };
+      auto no_next = [](uint32_t (&)[16], uint32_t (&)[16]) {};
       if constexpr (EW == 16) {
-        // single-buffered TMEM reads: the other three warps of the scheduler run meanwhile
+        // single-buffered TMEM reads: chunk c + 1 is loaded into the same registers as soon as
+        // chunk c's LIF has consumed them, so its latency overlaps chunk c's staging and store
+        uint32_t a0[16], a1[16];
+        tmem_ld16x256_x4_raw(tcol + lane_lo, a0);
+        tmem_ld16x256_x4_raw(tcol + lane_hi, a1);
         for (int c = 0; c < nch; ++c) {
-          uint32_t a0[16], a1[16];
-          tmem_ld16x256_x4_raw(tcol + lane_lo + c * 32, a0);
-          tmem_ld16x256_x4_raw(tcol + lane_hi + c * 32, a1);
           tmem_wait_ld_fence2(a0, a1);
           if (c + 1 == nch) {
             // last TMEM read of this buffer: hand it back to the MMA warp
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+            lif_chunk(a0, a1, c, no_next);
+          } else {
+            lif_chunk(a0, a1, c, [&](uint32_t (&lo)[16], uint32_t (&hi)[16]) {
+              tmem_ld16x256_x4_raw(tcol + lane_lo + (c + 1) * 32, lo);
+              tmem_ld16x256_x4_raw(tcol + lane_hi + (c + 1) * 32, hi);
+            });
           }
-          lif_chunk(a0, a1, c);
         }
       } else {
         // double-buffered TMEM reads: chunk c + 1 loads while chunk c is processed
@@ -636,9 +646,9 @@ __global__ void __launch_bounds__(EPI == kEpiTV ? kThreadsTV : kThreads, 1)
             if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
           }
           if ((c & 1) == 0)
-            lif_chunk(a0, a1, c);
+            lif_chunk(a0, a1, c, no_next);
           else
-            lif_chunk(b0, b1, c);
+            lif_chunk(b0, b1, c, no_next);
         }
       }
     }
