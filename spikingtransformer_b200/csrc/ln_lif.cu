@@ -855,7 +855,7 @@ constexpr int kGrpWarps = 8;  // warps per block
 constexpr int kGrpNV = 3;     // 4-column vectors per lane and row
 constexpr int kGrpFwdStages = 2;  // staged tokens per warp: the rows of kStages - 1 tokens are in flight
 constexpr int kGrpBwdStages = 2;
-constexpr int kGrpBwdWarps = 8;   // warps per block of the backward
+constexpr int kGrpBwdNV = 3;      // the backward's 4-column vectors per lane and row (1 or 3)
 
 inline bool use_grp(int D) { return D == 384 || D == 768 || D == 1536; }
 
@@ -1113,34 +1113,39 @@ __global__ void __launch_bounds__(32 * kGrpWarps, EB == 2 ? 2 : 1) ln_lif_fwd_gr
   }
 }
 
-// Backward staging: per warp, a ring of stages, each [kMaxT][kGrpNV][32 lanes]
+// Backward staging: per warp, a ring of stages, each [kMaxT][NV][32 lanes]
 // vectors of the pre-activation, the same of the spike gradient, and the
 // token's kMaxT row statistics.  Each lane copies (cp.async) and later reads
 // only its own vectors, so a lane's wait_group is the only synchronisation
 // the vectors need; the statistics, copied by lanes t < T, are read by every
 // lane after a __syncwarp.
-template <int EBP, int EBG>
+template <int EBP, int EBG, int NV>
 constexpr size_t grp_bwd_stage_bytes() {
-  return (size_t)kMaxT * kGrpNV * 32 * (4 * EBP + 4 * EBG) + kMaxT * sizeof(float2);
+  return (size_t)kMaxT * NV * 32 * (4 * EBP + 4 * EBG) + kMaxT * sizeof(float2);
 }
-// fp32 pre-activation and gradient: one stage (two would exceed the shared memory)
-template <int EBP, int EBG>
+// fp32 pre-activation and gradient with three vectors per lane: one stage (two would exceed
+// the shared memory)
+template <int EBP, int EBG, int NV>
 constexpr int grp_bwd_stages() {
-  return EBP + EBG > 6 ? 1 : kGrpBwdStages;
+  return NV == 3 && EBP + EBG > 6 ? 1 : kGrpBwdStages;
 }
-template <int EBP, int EBG>
+// warps per block: 8 with three vectors per lane (234 registers), 12 with one
+template <int NV>
 constexpr int grp_bwd_warps() {
-  return kGrpBwdWarps;
+  return NV == 3 ? 8 : 12;
 }
-// per warp: the stages, then the current token's x^ ([kMaxT][kGrpNV][32 lanes] float4)
-constexpr size_t kGrpXhatBytes = (size_t)kMaxT * kGrpNV * 32 * sizeof(float4);
-template <int EBP, int EBG>
+// per warp: the stages, then the current token's x^ ([kMaxT][NV][32 lanes] float4)
+template <int NV>
+constexpr size_t grp_xhat_bytes() {
+  return (size_t)kMaxT * NV * 32 * sizeof(float4);
+}
+template <int EBP, int EBG, int NV>
 constexpr size_t grp_bwd_warp_bytes() {
-  return grp_bwd_stages<EBP, EBG>() * grp_bwd_stage_bytes<EBP, EBG>() + kGrpXhatBytes;
+  return grp_bwd_stages<EBP, EBG, NV>() * grp_bwd_stage_bytes<EBP, EBG, NV>() + grp_xhat_bytes<NV>();
 }
-template <int EBP, int EBG>
+template <int EBP, int EBG, int NV>
 constexpr size_t grp_bwd_smem_bytes() {
-  return (size_t)grp_bwd_warps<EBP, EBG>() * grp_bwd_warp_bytes<EBP, EBG>();
+  return (size_t)grp_bwd_warps<NV>() * grp_bwd_warp_bytes<EBP, EBG, NV>();
 }
 
 // Backward, one token per group: the token's rows arrive in shared memory one
@@ -1148,9 +1153,9 @@ constexpr size_t grp_bwd_smem_bytes() {
 // saved statistics; the steps are walked backwards (BPTT) giving dL/dy of
 // every row, with the rows' two LayerNorm sums accumulated on the way; one
 // reduction of those sums for all T rows; then dL/dx of every row.
-template <int EBP, int EBG, int SURR, int G>
-__global__ void __launch_bounds__(32 * grp_bwd_warps<EBP, EBG>(), 1) ln_lif_bwd_grp_kernel(const BwdParams p) {
-  constexpr int NV = kGrpNV, W = grp_bwd_warps<EBP, EBG>(), NG = W / G;
+template <int EBP, int EBG, int SURR, int NV, int G>
+__global__ void __launch_bounds__(32 * grp_bwd_warps<NV>(), 1) ln_lif_bwd_grp_kernel(const BwdParams p) {
+  constexpr int W = grp_bwd_warps<NV>(), NG = W / G;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float2 xch[G > 1 ? 2 * NG * G * kMaxT : 1];
   __shared__ float lb_red[W];
@@ -1161,9 +1166,9 @@ __global__ void __launch_bounds__(32 * grp_bwd_warps<EBP, EBG>(), 1) ln_lif_bwd_
   const float invD = 1.0f / (float)D;
   const float lb = __ldg(p.lif_beta), vth = __ldg(p.lif_vth), vr = __ldg(p.lif_vr);
   const SpikeLayout lay(p.R, D, 0, p.hd, p.seq);
-  constexpr int S = grp_bwd_stages<EBP, EBG>();
+  constexpr int S = grp_bwd_stages<EBP, EBG, NV>();
   // this warp's stages (pre vectors, gradient vectors, row statistics), then x^
-  RawVec<EBP>* pre_s = reinterpret_cast<RawVec<EBP>*>(smem + (size_t)warp * grp_bwd_warp_bytes<EBP, EBG>());
+  RawVec<EBP>* pre_s = reinterpret_cast<RawVec<EBP>*>(smem + (size_t)warp * grp_bwd_warp_bytes<EBP, EBG, NV>());
   RawVec<EBG>* gs_s = reinterpret_cast<RawVec<EBG>*>(pre_s + S * kMaxT * NV * 32);
   float2* st_s = reinterpret_cast<float2*>(gs_s + S * kMaxT * NV * 32);
   float4* xh_s = reinterpret_cast<float4*>(st_s + S * kMaxT);
@@ -1445,8 +1450,8 @@ inline int tok_grid(int64_t R, int D) {
 }
 // token-group kernels: blocks of `warps` warps, warps / G tokens at a time;
 // blocks_per_sm resident blocks (the backward holds one per SM)
-inline int grp_grid(int64_t R, int D, int blocks_per_sm, int warps = kGrpWarps) {
-  const int ng = warps / (D / 384);
+inline int grp_grid(int64_t R, int D, int blocks_per_sm, int warps = kGrpWarps, int nv = kGrpNV) {
+  const int ng = warps / (D / (128 * nv));
   const int64_t need = (R + ng - 1) / ng, cap = (int64_t)num_sms() * blocks_per_sm;
   const int64_t g = need < cap ? need : cap;
   return g < 1 ? 1 : (int)g;
@@ -1454,10 +1459,11 @@ inline int grp_grid(int64_t R, int D, int blocks_per_sm, int warps = kGrpWarps) 
 constexpr int kGrpFwdBlocksPerSm = 2;
 constexpr int kGrpBwdBlocksPerSm = 1;
 
-// grp_warps: warps per block of the token-group backward (8 or kGrpBwdWarps, by input widths)
-inline int bwd_grid(int64_t R, int D, bool aligned16, int grp_warps = 8) {
+// token-group backward: warps per block and vectors per lane
+inline int bwd_grid(int64_t R, int D, bool aligned16) {
   if (R == 0) return 1;
-  if (use_grp(D) && aligned16) return grp_grid(R, D, kGrpBwdBlocksPerSm, grp_warps);
+  if (use_grp(D) && aligned16)
+    return grp_grid(R, D, kGrpBwdBlocksPerSm, grp_bwd_warps<kGrpBwdNV>(), kGrpBwdNV);
   return use_tok(D) && aligned16 ? tok_grid(R, D) : grid_blocks(R, pick_nw(D));
 }
 
@@ -1482,28 +1488,29 @@ int launch_fwd_grp(int D, int grid, cudaStream_t st, const FwdParams& p) {
   return launch_fwd_grp_g<EB, SD, 4>(grid, st, p);
 }
 
-template <int EBP, int EBG, int SURR, int G>
+template <int EBP, int EBG, int SURR, int NV, int G>
 int launch_bwd_grp_g(int grid, cudaStream_t st, const BwdParams& p) {
-  constexpr size_t smem = grp_bwd_smem_bytes<EBP, EBG>();
-  static_assert(smem >= (size_t)grp_bwd_warps<EBP, EBG>() * 3 * 384 * sizeof(float),
+  constexpr size_t smem = grp_bwd_smem_bytes<EBP, EBG, NV>();
+  static_assert(smem >= (size_t)grp_bwd_warps<NV>() * 3 * 128 * NV * sizeof(float),
                 "block partials reuse the staging memory");
   static_assert(smem <= 227 * 1024, "staging exceeds the shared memory of a block");
   static bool attr_set = false;  // per instantiation; idempotent if two threads race
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(ln_lif_bwd_grp_kernel<EBP, EBG, SURR, G>,
+    cudaError_t e = cudaFuncSetAttribute(ln_lif_bwd_grp_kernel<EBP, EBG, SURR, NV, G>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set = true;
   }
-  ln_lif_bwd_grp_kernel<EBP, EBG, SURR, G><<<grid, 32 * grp_bwd_warps<EBP, EBG>(), smem, st>>>(p);
+  ln_lif_bwd_grp_kernel<EBP, EBG, SURR, NV, G><<<grid, 32 * grp_bwd_warps<NV>(), smem, st>>>(p);
   return SPK_OK;
 }
 
 template <int EBP, int EBG, int SURR>
 int launch_bwd_grp_d(int D, int grid, cudaStream_t st, const BwdParams& p) {
-  if (D == 384) return launch_bwd_grp_g<EBP, EBG, SURR, 1>(grid, st, p);
-  if (D == 768) return launch_bwd_grp_g<EBP, EBG, SURR, 2>(grid, st, p);
-  return launch_bwd_grp_g<EBP, EBG, SURR, 4>(grid, st, p);
+  constexpr int NV = kGrpBwdNV, G1 = 3 / NV;  // warps per token at D = 384
+  if (D == 384) return launch_bwd_grp_g<EBP, EBG, SURR, NV, G1>(grid, st, p);
+  if (D == 768) return launch_bwd_grp_g<EBP, EBG, SURR, NV, 2 * G1>(grid, st, p);
+  return launch_bwd_grp_g<EBP, EBG, SURR, NV, 4 * G1>(grid, st, p);
 }
 
 template <int SURR>
@@ -1556,7 +1563,7 @@ int64_t spk_ln_lif_bwd_workspace_bytes(int64_t T, int64_t R, int64_t D) {
   if (D < 32 || D > 4 * 32 * spk::lnlif::kMaxCpt || R < 0) return 0;
   // the largest of the backward's possible grids on the current device (one
   // partial row per block); fewer warps per block give more blocks
-  const int g1 = spk::lnlif::bwd_grid(R, (int)D, true, 8), g2 = spk::lnlif::bwd_grid(R, (int)D, false);
+  const int g1 = spk::lnlif::bwd_grid(R, (int)D, true), g2 = spk::lnlif::bwd_grid(R, (int)D, false);
   return (int64_t)(g1 > g2 ? g1 : g2) * (3 * D + 1) * (int64_t)sizeof(float);
 }
 
@@ -1647,8 +1654,7 @@ int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_
               "D=%lld > %d needs g_spikes, pre, g_pre, ln_gamma, ln_beta and pre_bias 16-byte aligned",
               (long long)D, 32 * kMaxCpt);
   if ((rc = check_heads(head_dim, seq_len, R, (int)D, use_tok((int)D) && aligned16)) != SPK_OK) return rc;
-  const int grid = bwd_grid(R, (int)D, aligned16,
-                            pre_dtype == SPK_F32 && gs_dtype == SPK_F32 ? 8 : kGrpBwdWarps);
+  const int grid = bwd_grid(R, (int)D, aligned16);
   SPK_REQUIRE((int64_t)grid * (3 * D + 1) * 4 <= workspace_bytes, SPK_ERR_INVALID, "workspace too small for %d blocks",
               grid);
   float* part = reinterpret_cast<float*>(workspace);
