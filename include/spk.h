@@ -181,6 +181,23 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
                    float* stats, void* stream);
 
 /*
+ * spk_ln_lif_fwd with the residual connection of a transformer layer fused in
+ * (Encoder.py:19-22, Decoder.py:18-24: x = x + LIF(LN(Linear(...)))):
+ *   out[t*R + r][d] = residual[t*R + r][d] + spike,
+ * fp32 row-major [T*R][D], and, when out_bf16 is not null, the same values in
+ * bf16 (spike counts are small integers, exact in both; the bf16 copy is what
+ * the next layer's GEMMs read).  stats as in spk_ln_lif_fwd.  D must be 384,
+ * 768 or 1536 and every pointer 16-byte aligned; SPK_ERR_UNSUPPORTED
+ * otherwise (the caller then adds the spikes of spk_ln_lif_fwd itself).  The
+ * backward is spk_ln_lif_bwd with g_spikes = dL/dout (dL/dresidual = dL/dout).
+ */
+int spk_ln_lif_fwd_residual(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
+                            const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
+                            const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D,
+                            int64_t pre_ld, const float* residual, float* out, void* out_bf16, float* stats,
+                            void* stream);
+
+/*
  * Backward of spk_ln_lif_fwd (LIFLayer.backward Lif.py:46-102 composed with
  * the LayerNorm backward): recomputes x^ and the membrane from pre and stats,
  * BPTT with the surrogate, then

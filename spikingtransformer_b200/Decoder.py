@@ -46,9 +46,9 @@ class DecoderLayer(nn.Module):
         xb, enc = _fast_inputs(self, x, enc_output, mask)
         if xb is not None:
             return stream_out(self._fast(xb, enc, mask), x)
-        x = x + self.self_attns(x, x, x, attention_mask=mask)
-        x = x + self.cross_attns(x, enc_output, enc_output)
-        return x + self.mlp(x)
+        x = self.self_attns.add_to(x, x, x, attention_mask=mask)
+        x = self.cross_attns.add_to(x, enc_output, enc_output)
+        return self.mlp.add_to(x)
 
 
 class Decoder(nn.Module):

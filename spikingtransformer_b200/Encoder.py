@@ -51,8 +51,8 @@ class EncoderLayer(nn.Module):
         xb = stream_copy_bf16(x) if fast_path_ok(x, mask, module=self) else None
         if xb is not None:
             return stream_out(self._fast(xb, mask), x)
-        x = x + self.self_attns(x, x, x, attention_mask=mask)
-        return x + self.mlp(x)
+        x = self.self_attns.add_to(x, x, x, attention_mask=mask)
+        return self.mlp.add_to(x)
 
 
 class Encoder(nn.Module):

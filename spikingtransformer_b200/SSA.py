@@ -107,7 +107,7 @@ class _SSACore(nn.Module):
     def _scores(self, q, k):
         raise NotImplementedError
 
-    def _reference_forward(self, query, key, value, attention_mask):
+    def _reference_forward(self, query, key, value, attention_mask, residual=None):
         TB, N, D = query.shape
         Nk = key.shape[1]
         # Q, K, V spikes feed only the attention products, so under autocast
@@ -131,11 +131,21 @@ class _SSACore(nn.Module):
         # token-major [TB, N, D]; the lifs LIF is per neuron, so it commutes with
         # the reference's transpose back from heads (SSA.py:242-247)
         s = self._combine_lif(q, k, v, attention_mask)
-        return lin_ln_lif_train(s, self.out_proj, self.lno, self.lifo)
+        return lin_ln_lif_train(s, self.out_proj, self.lno, self.lifo, residual=residual)
 
     def _combine_lif(self, q, k, v, mask):
         """lifs(attention core) -> token-major spikes [TB, N, H*dh]."""
         return self.lifs(self._combine(q, k, v, mask))[0]
+
+    def add_to(self, x, key=None, value=None, attention_mask=None):
+        """``x + self(x, key, value, attention_mask)``, the residual connection of
+        an encoder / decoder layer (``Encoder.py:19``, ``Decoder.py:18-21``); on
+        the autograd path the add is fused into the output LayerNorm->LIF kernel."""
+        key = x if key is None else key
+        value = x if value is None else value
+        if fast_path_ok(x, key, value, attention_mask, module=self):
+            return x + self._fast_public(x, key, value, attention_mask)
+        return self._reference_forward(x, key, value, attention_mask, residual=x)
 
     def forward(self, query: torch.Tensor, key: Optional[torch.Tensor] = None, value: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -45,3 +45,12 @@ class SpikingMLP(nn.Module):
         # the hidden spikes feed only the compress GEMM: autocast dtype under autocast
         h = lin_ln_lif_train(x, self.expand, self.bn_expand, self.lifexpand, narrow=True)
         return lin_ln_lif_train(h, self.compress, self.bn_compress, self.lifcompress)
+
+    def add_to(self, x):
+        """``x + self(x)``, the residual connection of an encoder / decoder layer
+        (``Encoder.py:22``, ``Decoder.py:24``); on the autograd path the add is
+        fused into the compress LayerNorm->LIF kernel."""
+        if fast_path_ok(x, module=self):
+            return x + self(x)
+        h = lin_ln_lif_train(x, self.expand, self.bn_expand, self.lifexpand, narrow=True)
+        return lin_ln_lif_train(h, self.compress, self.bn_compress, self.lifcompress, residual=x)

@@ -79,6 +79,11 @@ def lin_ln_lif(x, lin, ln, lif, T, t_broadcast=False, residual=None, spike_dtype
 _SPIKE_COUNTS = {}
 
 
+# the residual connections of the training path go through LNLIFResidualFunction
+# (False: spikes and a separate add, the composition the fused form is tested against)
+RESIDUAL_FUSION = True
+
+
 def mark_spike_counts(t, bf16=None):
     """Record that ``t`` holds spike counts (small non-negative integers, exact
     in bf16), with its bf16 copy if one exists; returns ``t``.  The record
@@ -152,6 +157,41 @@ class LNLIFFunction(torch.autograd.Function):
         gb = gb.to(b.dtype) if gb is not None else None
         glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
         return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, None, None
+
+
+class LNLIFResidualFunction(torch.autograd.Function):
+    """``residual + lif(ln(pre + bias))`` for training: the residual connection
+    of a transformer layer (``Encoder.py:19-22``, ``Decoder.py:18-24``) fused
+    into the LayerNorm->LIF forward kernel (``ops.ln_lif_fwd_residual``), which
+    under bf16 autocast also writes the bf16 copy the next layer's GEMMs read
+    (recorded with ``mark_spike_counts``).  Backward: ``dL/dresidual =
+    dL/dout``, and ``ops.ln_lif_bwd`` with ``g_spikes = dL/dout``."""
+
+    @staticmethod
+    def forward(ctx, pre, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset, eps, k, surrogate, in_gain, T,
+                residual):
+        want_bf16 = _autocast_bf16(residual)
+        out, stats, outb = ops.ln_lif_fwd_residual(pre, ln_weight, ln_bias, eps, lif_beta, v_th, v_reset, T,
+                                                   residual.detach(), in_gain, bias=bias, want_bf16=want_bf16)
+        ctx.save_for_backward(pre, stats, bias, ln_weight, ln_bias, lif_beta, v_th, v_reset)
+        ctx.k, ctx.surrogate, ctx.in_gain, ctx.T = float(k), surrogate, float(in_gain), int(T)
+        if outb is not None:
+            mark_spike_counts(out, bf16=outb)
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out):
+        pre, stats, pb, w, b, lb, vth, vr = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        g_pre, gw, gb, glb, gpb = ops.ln_lif_bwd(g_out, pre, stats, w, b, lb, vth, vr, ctx.T, ctx.in_gain,
+                                                 ctx.surrogate, ctx.k, need_gamma=need[2], need_beta=need[3],
+                                                 need_lif_beta=need[4], bias=pb,
+                                                 need_bias=pb is not None and need[1])
+        gpb = gpb.to(pb.dtype) if gpb is not None else None
+        gw = gw.to(w.dtype) if gw is not None else None
+        gb = gb.to(b.dtype) if gb is not None else None
+        glb = glb.reshape(lb.shape).to(lb.dtype) if glb is not None else None
+        return g_pre, gpb, gw, gb, glb, None, None, None, None, None, None, None, g_out if need[12] else None
 
 
 class QKVLNLIF(torch.autograd.Function):
@@ -286,12 +326,23 @@ class LinearBF16(torch.autograd.Function):
         return dx, dw, None, None
 
 
+def _autocast_bf16(x):
+    return x.is_cuda and torch.is_autocast_enabled(x.device.type) and \
+        torch.get_autocast_dtype(x.device.type) == torch.bfloat16
+
+
 def bf16_input(x):
     """The bf16 copy of an activation that ``lin_ln_lif_train`` GEMMs read under
-    bf16 autocast (None otherwise); made once and passed to every consumer."""
-    if x.is_cuda and torch.is_autocast_enabled(x.device.type) and \
-            torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
-        return x.detach().to(torch.bfloat16) if x.dtype != torch.bfloat16 else x.detach()
+    bf16 autocast (None otherwise); made once and passed to every consumer.  A
+    residual-stream tensor written by ``LNLIFResidualFunction`` already has
+    one (recorded with ``mark_spike_counts``)."""
+    if _autocast_bf16(x):
+        if x.dtype == torch.bfloat16:
+            return x.detach()
+        entry = _SPIKE_COUNTS.get(id(x))
+        if entry is not None and entry[0]() is x and entry[1] == x._version and entry[2] is not None:
+            return entry[2]
+        return x.detach().to(torch.bfloat16)
     return None
 
 
@@ -303,7 +354,7 @@ def _linear_nobias(x, lin, xb):
     return LinearBF16.apply(x, lin.weight, xb, bf16_weight(lin))
 
 
-def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None, xb=None):
+def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None, xb=None, residual=None):
     """``lif(ln(lin(x)))[0]`` on the autograd path.  With the fused kernels the
     GEMM runs without the bias, which the LayerNorm->LIF kernels add and
     differentiate; under bf16 autocast it is ``LinearBF16`` on ``xb`` (the
@@ -312,8 +363,17 @@ def lin_ln_lif_train(x, lin, ln, lif, narrow=False, heads=None, xb=None):
     for spikes whose consumer is a GEMM that reads that dtype.  ``heads =
     (head_dim, n)`` for ``x`` ``[TB, n, D]``: return the spikes as ``[TB,
     D/head_dim, n, head_dim]``, written in that layout by the kernel where it
-    can."""
+    can.  ``residual``: return ``residual + lif(ln(lin(x)))[0]`` instead (the
+    residual connection of a transformer layer), fused into the LayerNorm->LIF
+    kernel where it applies."""
     D = lin.out_features
+    if residual is not None:
+        if not narrow and heads is None and _ln_lif_fusable(x, D, ln, lif) and RESIDUAL_FUSION:
+            pre = _linear_nobias(x, lin, xb)
+            if ops.ln_lif_residual_ok(pre, residual) and residual.shape[-1] == D:
+                return LNLIFResidualFunction.apply(pre, lin.bias, *_lif_args(ln, lif), residual)
+            return residual + LNLIFFunction.apply(pre, lin.bias, *_lif_args(ln, lif), torch.float32, None)
+        return residual + lin_ln_lif_train(x, lin, ln, lif, narrow=narrow, heads=heads, xb=xb)
     if _ln_lif_fusable(x, D, ln, lif):
         pre = _linear_nobias(x, lin, xb)
         dt = torch.float32

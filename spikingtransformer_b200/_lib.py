@@ -48,6 +48,8 @@ SIGNATURES = {
     "spk_im2col": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p], _i),
     "spk_ln_lif_fwd": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p],
                        _i),
+    "spk_ln_lif_fwd_residual": ([_p, _i, _p, _p, _p, _f, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _p, _p, _p, _p,
+                                 _p], _i),
     "spk_ln_lif_bwd_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "spk_ln_lif_bwd": ([_p, _i, _p, _i, _p, _p, _p, _p, _p, _p, _p, _f, _i, _f, _i64, _i64, _i64, _i64, _i64, _i64,
                         _p, _p, _p, _p, _p, _p, _i64, _p], _i),

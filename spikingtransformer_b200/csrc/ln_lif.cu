@@ -57,6 +57,8 @@ struct FwdParams {
   int D, cpt;
   int hd, seq;  // head-major spikes [T*B][D/hd][seq][hd] when hd > 0 (R = B * seq)
   int64_t ld;   // row stride of pre (and g_pre) in elements (D, or wider for a column slice)
+  const float* residual;  // token-group kernels: spikes = residual + LIF output (fp32, row-major), or null
+  __nv_bfloat16* out_bf16;  // with a residual: also a bf16 copy of the fp32 output, or null
 };
 
 struct BwdParams {
@@ -996,7 +998,9 @@ __device__ __forceinline__ void ln_params(const Params& p, int c, float2 gain2, 
   pq[1] = make_float2(p4.z, p4.w);
 }
 
-template <int EB, int SD, int G>
+// RESID: the output is residual + spikes in fp32 (row-major, the residual stream of a
+// transformer layer, Encoder.py:19-22 / Decoder.py:18-24), with an optional bf16 copy.
+template <int EB, int SD, int G, bool RESID = false>
 __global__ void __launch_bounds__(32 * kGrpWarps, EB == 2 ? 2 : 1) ln_lif_fwd_grp_kernel(const FwdParams p) {
   constexpr int NV = kGrpNV, NG = kGrpWarps / G;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1107,7 +1111,22 @@ __global__ void __launch_bounds__(32 * kGrpWarps, EB == 2 ? 2 : 1) ln_lif_fwd_gr
           x[2 * j + 1] = sy ? 1.0f : 0.0f;
           v[i][j] = make_float2(sx ? vr : u.x, sy ? vr : u.y);
         }
-        store_spikes4<SD>(p.spikes, p.spike_dtype, sb + t * lay.t_stride + coff[i], x);
+        const int64_t oi = sb + t * lay.t_stride + coff[i];
+        if constexpr (RESID) {
+          // spike counts: the sum of a small integer and 0/1 is exact in fp32 and bf16
+          const float4 r = __ldg(reinterpret_cast<const float4*>(p.residual + oi));
+          const float4 o = make_float4(r.x + x[0], r.y + x[1], r.z + x[2], r.w + x[3]);
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.spikes) + oi) = o;
+          if (p.out_bf16) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&lo);
+            w.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(p.out_bf16 + oi) = w;
+          }
+        } else {
+          store_spikes4<SD>(p.spikes, p.spike_dtype, oi, x);
+        }
       }
     }
   }
@@ -1467,25 +1486,25 @@ inline int bwd_grid(int64_t R, int D, bool aligned16) {
   return use_tok(D) && aligned16 ? tok_grid(R, D) : grid_blocks(R, pick_nw(D));
 }
 
-template <int EB, int SD, int G>
+template <int EB, int SD, int G, bool RESID = false>
 int launch_fwd_grp_g(int grid, cudaStream_t st, const FwdParams& p) {
   constexpr size_t smem = (size_t)kGrpWarps * kGrpFwdStages * kMaxT * kGrpNV * 32 * 4 * EB;
   static bool attr_set = false;  // per instantiation; idempotent if two threads race
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(ln_lif_fwd_grp_kernel<EB, SD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(ln_lif_fwd_grp_kernel<EB, SD, G, RESID>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(SPK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set = true;
   }
-  ln_lif_fwd_grp_kernel<EB, SD, G><<<grid, 32 * kGrpWarps, smem, st>>>(p);
+  ln_lif_fwd_grp_kernel<EB, SD, G, RESID><<<grid, 32 * kGrpWarps, smem, st>>>(p);
   return SPK_OK;
 }
 
-template <int EB, int SD>
+template <int EB, int SD, bool RESID = false>
 int launch_fwd_grp(int D, int grid, cudaStream_t st, const FwdParams& p) {
-  if (D == 384) return launch_fwd_grp_g<EB, SD, 1>(grid, st, p);
-  if (D == 768) return launch_fwd_grp_g<EB, SD, 2>(grid, st, p);
-  return launch_fwd_grp_g<EB, SD, 4>(grid, st, p);
+  if (D == 384) return launch_fwd_grp_g<EB, SD, 1, RESID>(grid, st, p);
+  if (D == 768) return launch_fwd_grp_g<EB, SD, 2, RESID>(grid, st, p);
+  return launch_fwd_grp_g<EB, SD, 4, RESID>(grid, st, p);
 }
 
 template <int EBP, int EBG, int SURR, int NV, int G>
@@ -1621,6 +1640,34 @@ int spk_ln_lif_fwd(const void* pre, int pre_dtype, const float* pre_bias, const 
     ln_lif_fwd_kernel<1, 1, kMaxCpt><<<grid_blocks(R, nw, 8), kThreads, 0, st>>>(p);
   }
   return check_launch("ln_lif_fwd_kernel");
+}
+
+int spk_ln_lif_fwd_residual(const void* pre, int pre_dtype, const float* pre_bias, const float* ln_gamma,
+                            const float* ln_beta, float ln_eps, const float* lif_beta, const float* lif_vth,
+                            const float* lif_vreset, float in_gain, int64_t T, int64_t R, int64_t D, int64_t pre_ld,
+                            const float* residual, float* out, void* out_bf16, float* stats, void* stream) {
+  using namespace spk;
+  int rc = check_ln_lif((int)T, R, (int)D);
+  if (rc != SPK_OK) return rc;
+  SPK_REQUIRE((pre && residual && out && stats) || R == 0, SPK_ERR_INVALID, "null pointer argument");
+  SPK_REQUIRE(lif_beta && lif_vth && lif_vreset, SPK_ERR_INVALID, "null LIF parameter");
+  SPK_REQUIRE(pre_dtype == SPK_F32 || pre_dtype == SPK_F16 || pre_dtype == SPK_BF16, SPK_ERR_INVALID,
+              "pre dtype %d not supported", pre_dtype);
+  if ((rc = check_stream_device(stream)) != SPK_OK) return rc;
+  if (R == 0) return SPK_OK;
+  const int64_t ld = pre_ld > 0 ? pre_ld : D;
+  const bool aligned16 = tok_aligned({pre, residual, out, out_bf16, ln_gamma, ln_beta, pre_bias}) && ld % 4 == 0;
+  if (!(use_grp((int)D) && aligned16))
+    return fail(SPK_ERR_UNSUPPORTED, "residual form needs D in {384, 768, 1536} and 16-byte aligned pointers");
+  FwdParams p = {pre, pre_dtype, pre_bias, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vreset, in_gain,
+                 out, SPK_F32, reinterpret_cast<float2*>(stats), (int)T, R, (int)D, 0, 0, 1, ld,
+                 residual, reinterpret_cast<__nv_bfloat16*>(out_bf16)};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = grp_grid(R, (int)D, pre_dtype == SPK_F32 ? 1 : kGrpFwdBlocksPerSm);
+  rc = pre_dtype == SPK_F32 ? launch_fwd_grp<4, SPK_F32, true>((int)D, grid, st, p)
+                            : launch_fwd_grp<2, SPK_F32, true>((int)D, grid, st, p);
+  if (rc != SPK_OK) return rc;
+  return check_launch("ln_lif_fwd_grp_kernel");
 }
 
 int spk_ln_lif_bwd(const void* g_spikes, int gs_dtype, const void* pre, int pre_dtype, const float* pre_bias,

@@ -247,6 +247,47 @@ def ln_lif_fwd(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, in_
     return spikes, stats
 
 
+def ln_lif_residual_ok(pre, residual):
+    """Whether ``ln_lif_fwd_residual`` takes these tensors: D = 384, 768 or
+    1536, fp32 residual ``[rows, D]`` laid out like the output, 16-byte aligned
+    rows."""
+    D = pre.shape[-1]
+    ld = _row_stride(pre)
+    return (D in (384, 768, 1536) and pre.is_cuda and residual.is_cuda and residual.dtype == torch.float32
+            and residual.is_contiguous() and residual.numel() == pre.numel() and ld is not None and ld % 4 == 0
+            and pre.data_ptr() % 16 == 0 and residual.data_ptr() % 16 == 0)
+
+
+def ln_lif_fwd_residual(pre, ln_gamma, ln_beta, ln_eps, lif_beta, lif_vth, lif_vr, T, residual, in_gain=1.0,
+                        bias=None, want_bf16=False):
+    """``residual + LIF(LayerNorm(pre + bias))`` in one kernel: the residual
+    connection of a transformer layer (``Encoder.py:19-22``,
+    ``Decoder.py:18-24``) fused into the LayerNorm->LIF forward.  Returns
+    ``(out fp32 like residual, stats [T*R, 2], out in bf16 or None)``; the
+    backward is ``ln_lif_bwd`` with ``g_spikes = dL/dout``.  Callers check
+    ``ln_lif_residual_ok`` first."""
+    _cuda(pre, residual)
+    D = pre.shape[-1]
+    ld = _row_stride(pre)
+    rows = pre.numel() // D
+    if rows % T:
+        raise RuntimeError("rows %d not divisible by T=%d" % (rows, T))
+    dev = pre.device
+    out = torch.empty(residual.shape, dtype=torch.float32, device=dev)
+    outb = torch.empty(residual.shape, dtype=torch.bfloat16, device=dev) if want_bf16 else None
+    stats = torch.empty((rows, 2), dtype=torch.float32, device=dev)
+    g = None if ln_gamma is None else ln_gamma.detach().float().contiguous()
+    bt = None if ln_beta is None else ln_beta.detach().float().contiguous()
+    pb = None if bias is None else bias.detach().float().contiguous()
+    b, th, vr = (_scalar_f32(v, dev) for v in (lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_ln_lif_fwd_residual", _lib.ptr(pre), _lib.dtype_code(pre), _lib.ptr(pb), _lib.ptr(g),
+              _lib.ptr(bt), float(ln_eps), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, rows // T,
+              D, ld, _lib.ptr(residual), _lib.ptr(out), _lib.ptr(outb), _lib.ptr(stats), _lib.stream_ptr(dev),
+              tag="ln_lif_fwd_residual D=%d" % D,
+              work=dict(bytes=rows * D * (pre.element_size() + 8 + (2 if want_bf16 else 0)) + rows * 8))
+    return out, stats, outb
+
+
 def ln_lif_bwd(g_spikes, pre, stats, ln_gamma, ln_beta, lif_beta, lif_vth, lif_vr, T, in_gain=1.0,
                surrogate="superspike", k=4.0, need_gamma=True, need_beta=True, need_lif_beta=True, bias=None,
                need_bias=False, heads=None, g_pre_out=None):

@@ -636,6 +636,30 @@ def test_ln_lif_train_bf16_gradient_equals_fp32_path(ops, D):
         assert torch.equal(x, y)
 
 
+@pytest.mark.parametrize("D,pre_dtype", [(384, torch.bfloat16), (1536, torch.bfloat16), (384, torch.float32)])
+def test_ln_lif_fwd_residual_equals_spikes_plus_residual(ops, D, pre_dtype):
+    """The residual form writes residual + the spikes of ln_lif_fwd, bit for
+    bit, with the same row statistics, and its bf16 copy equals the output
+    cast to bf16."""
+    g = gen(D + 77)
+    T, R = 4, 900
+    pre = (torch.randn(T * R, D, generator=g) * 1.3).to(pre_dtype).to(DEV)
+    gamma = (1.0 + 0.2 * torch.randn(D, generator=g)).to(DEV)
+    beta_ln = (0.3 * torch.randn(D, generator=g)).to(DEV)
+    bias = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    resid = torch.randint(0, 9, (T * R, D), generator=g).float().to(DEV)
+    s, st = ops.ln_lif_fwd(pre, gamma, beta_ln, 1e-5, 0.8, 1.0, 0.0, T, in_gain=0.5, bias=bias)
+    assert ops.ln_lif_residual_ok(pre, resid)
+    out, st2, outb = ops.ln_lif_fwd_residual(pre, gamma, beta_ln, 1e-5, 0.8, 1.0, 0.0, T, resid, in_gain=0.5,
+                                             bias=bias, want_bf16=True)
+    assert torch.equal(out, resid + s)
+    assert torch.equal(st2, st)
+    assert torch.equal(outb, out.to(torch.bfloat16))
+    out2, _, none = ops.ln_lif_fwd_residual(pre, gamma, beta_ln, 1e-5, 0.8, 1.0, 0.0, T, resid, in_gain=0.5,
+                                            bias=bias)
+    assert none is None and torch.equal(out2, out)
+
+
 def test_ln_lif_train_unaligned_inputs(ops):
     """The vectorised one-token-per-block kernels need 16-byte aligned rows:
     an input offset by one element takes the scalar kernels (D <= 512) with the

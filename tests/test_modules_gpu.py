@@ -256,6 +256,45 @@ def test_fused_qkv_training_path_matches_separate(pkg, monkeypatch):
     assert (gx1 - gx2).abs().max().item() <= 0.05 * gx2.abs().max().item() + 1e-6
 
 
+def test_residual_fusion_matches_composition(pkg, monkeypatch):
+    """An encoder and a decoder layer trained under bf16 autocast with the
+    residual adds fused into the LayerNorm->LIF kernels (and the next GEMM's
+    bf16 copy written by them) against spikes plus separate adds: identical
+    outputs (spike counts are exact either way) and the same gradients up to
+    the order of fp32 gradient sums."""
+    import spikingtransformer_b200._fused as fz
+    from spikingtransformer_b200.Encoder import EncoderLayer
+    from spikingtransformer_b200.Decoder import DecoderLayer
+    T, B, N, M, D, H, F = 4, 3, 16, 8, 384, 8, 1536
+    g = torch.Generator(device=DEV).manual_seed(41)
+    x = (torch.rand(T * B, N, D, generator=g, device=DEV) < 0.2).float()
+    y0 = (torch.rand(T * B, M, D, generator=g, device=DEV) < 0.2).float()
+    w = torch.randn(T * B, M, D, generator=g, device=DEV)
+    torch.manual_seed(3)
+    enc0 = EncoderLayer(d_model=D, n_heads=H, ff_dim=F, n_steps=T).to(DEV)
+    dec0 = DecoderLayer(d_model=D, n_heads=H, ff_dim=F, n_steps=T).to(DEV)
+    runs = []
+    for fused in (True, False):
+        monkeypatch.setattr(fz, "RESIDUAL_FUSION", fused)
+        enc = EncoderLayer(d_model=D, n_heads=H, ff_dim=F, n_steps=T).to(DEV)
+        dec = DecoderLayer(d_model=D, n_heads=H, ff_dim=F, n_steps=T).to(DEV)
+        enc.load_state_dict(enc0.state_dict())
+        dec.load_state_dict(dec0.state_dict())
+        xi, yi = x.clone().requires_grad_(), y0.clone().requires_grad_()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = dec(yi, enc(xi))
+        (out.float() * w).sum().backward()
+        grads = {n: p.grad.clone() for m in (enc, dec) for n, p in m.named_parameters() if p.grad is not None}
+        runs.append((out.detach().float(), xi.grad.clone(), yi.grad.clone(), grads))
+    (o1, gx1, gy1, g1), (o2, gx2, gy2, g2) = runs
+    assert torch.equal(o1, o2)
+    assert set(g1) == set(g2)
+    for n in g1:
+        assert torch.allclose(g1[n], g2[n], rtol=1e-5, atol=1e-6 * (g2[n].abs().max().item() + 1.0)), n
+    for a, b in ((gx1, gx2), (gy1, gy2)):
+        assert torch.allclose(a, b, rtol=1e-5, atol=1e-6 * (b.abs().max().item() + 1.0))
+
+
 def test_linear_bf16_training_gemm(pkg):
     """The training path's bias-free bf16 GEMM against torch's autocast Linear:
     the same bf16 output, and fp32 input / weight gradients at least as close
