@@ -173,10 +173,10 @@ class ClockSampler:
 
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture of
-# the same launch shape; profiles/dram_traffic_b256_shapes.md) of the kernels that can be
-# the dominant one of the 256-image forward
+# the same launch shape) of the kernels that can be the dominant one of the 256-image
+# forward
 NCU_TRAFFIC = {
-    "linear_ln_lif K=384 N=384 rows=262144": 355.2e6,
+    "linear_ln_lif K=384 N=384 rows=262144": 358.5e6,
     "linear_ln_lif K=384 N=384 rows=262144 +residual": 558.5e6,
     "linear_ln_lif K=384 N=1536 rows=262144": 950.6e6,
     "linear_ln_lif K=1536 N=384 rows=262144 +residual": 1212.4e6,
