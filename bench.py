@@ -52,7 +52,7 @@ SEQ = 64
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="forward", choices=["forward", "train", "decode"],
@@ -124,52 +124,81 @@ def max_over_ranks(x, device):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms.
+
+    Start it before the warm-up steps (nvidia-smi takes a few hundred ms to
+    print its first line) and bracket the timed region with begin() and
+    end(): summary() keeps only the samples taken inside that window."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, interval_ms=100):
         self.index = index
-        self.samples = []
+        self.interval_ms = interval_ms
+        self.samples = []  # (host monotonic time, fields)
         self.proc = None
+        self.t0 = None
+        self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.interval_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except (OSError, ValueError):
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 8:
-                self.samples.append(parts)
+    def begin(self):
+        self.t0 = time.monotonic()
 
-    def __exit__(self, *exc):
+    def end(self):
+        self.t1 = time.monotonic()
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.proc = None
+
+    def __enter__(self):
+        return self.start()
+
+    def __exit__(self, *exc):
+        self.stop()
         return False
 
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append((time.monotonic(), parts))
+
+    def window(self):
+        """Samples inside [begin, end]; all of them when no window was marked."""
+        lo = self.t0 if self.t0 is not None else float("-inf")
+        hi = self.t1 if self.t1 is not None else float("inf")
+        return [s for t, s in self.samples if lo <= t <= hi]
+
     def summary(self):
-        if not self.samples:
+        samples = self.window()
+        if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        sm = [float(s[0]) for s in samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in samples if s[1].replace(".", "").isdigit()]
+        pw = [float(s[2]) for s in samples if s[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].lower() == "active"})
+        reasons = sorted({names[i] for s in samples for i in range(4) if s[4 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "power_w_median": statistics.median(pw) if pw else None,
+                "reasons": reasons, "samples": len(samples), "interval_ms": self.interval_ms}
 
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture of
@@ -513,11 +542,15 @@ def run_train(args, ws, rank, local):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+        # nvidia-smi prints its first sample a few hundred ms after it starts
+        time.sleep(0.5)
+        clk.begin()
         e0.record()
         for i in range(args.steps):
             loss, acc = step(args.warmup + i)
         e1.record()
         torch.cuda.synchronize()
+        clk.end()
     if ws > 1:
         dist.barrier()
     ms = max_over_ranks(e0.elapsed_time(e1), dev)
@@ -587,11 +620,14 @@ def run_decode(args, ws, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     steps = max(1, args.steps // 4)
     with ClockSampler(local) as clk, _lib.LaunchRecorder() as rec:
+        time.sleep(0.5)
+        clk.begin()
         e0.record()
         for _ in range(steps):
             ys, _ = batch_decode()
         e1.record()
         torch.cuda.synchronize()
+        clk.end()
     ms = max_over_ranks(e0.elapsed_time(e1), dev) / steps
     kernels = rec.summary()
     # the reference API: one image at a time
@@ -669,21 +705,27 @@ def main():
         return logits
 
     with torch.no_grad():
-        for i in range(args.warmup):
-            step(i)
-        torch.cuda.synchronize()
-        if ws > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        # the timed region: only launches counted (no events between kernels)
-        with ClockSampler(local) as clk, _lib.LaunchCounter() as counter:
-            e0.record()
-            for i in range(args.steps):
+        clk = ClockSampler(local).start()
+        try:
+            for i in range(args.warmup):
                 step(i)
-            e1.record()
             torch.cuda.synchronize()
+            if ws > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            # the timed region: only launches counted (no events between kernels)
+            with _lib.LaunchCounter() as counter:
+                clk.begin()
+                e0.record()
+                for i in range(args.steps):
+                    step(i)
+                e1.record()
+                torch.cuda.synchronize()
+                clk.end()
+        finally:
+            clk.stop()
         if ws > 1:
             dist.barrier()
         torch.cuda.synchronize()
