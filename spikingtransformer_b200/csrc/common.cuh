@@ -417,6 +417,23 @@ __device__ __forceinline__ void tmem_wait_ld_fence2(uint32_t (&a)[16], uint32_t 
                : "memory");
 }
 
+// ---------------------------------------------------------------- spike tiles
+// number of ones in row r of a 128B-swizzled tile of bf16 spikes (first n
+// elements, n % 8 == 0).  A spike is 0x0000 or 0x3F80, so bit 7 of each half
+// word counts it: the masked words add up to 0x80 per one in each half (at
+// most 32 ones per half, no carry into the other half).
+__device__ __forceinline__ int row_count_sw128(const uint8_t* tile, int r, int n) {
+  constexpr uint32_t kBit = 0x00800080u;
+  uint32_t acc = 0u;
+  const int chunks = n >> 3;
+  for (int c = 0; c < chunks; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4));
+    acc += (w.x & kBit) + (w.y & kBit);
+    acc += (w.z & kBit) + (w.w & kBit);
+  }
+  return (int)(((acc & 0xFFFFu) + (acc >> 16)) >> 7);
+}
+
 // ---------------------------------------------------------------- packed fp32x2 arithmetic (sm_100)
 // Each operation rounds like its scalar fp32 counterpart (round to nearest).
 __device__ __forceinline__ float2 add2(float2 a, float2 b) {

@@ -104,21 +104,6 @@ __host__ __device__ inline size_t smem_layout(int lmax, uint8_t* base, Smem* s) 
   return off;
 }
 
-__device__ __forceinline__ float row_sum_sw128(const uint8_t* tile, int r, int n) {
-  float s = 0.0f;
-  const int chunks = (n + 7) >> 3;
-  for (int c = 0; c < chunks; ++c) {
-    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      s += f.x + f.y;
-    }
-  }
-  return s;
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -342,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&sm.kv_full[s], ph, 91)) return false;
       if (XNOR) {
         const int j = grp * 128 + lrow;
-        const float ks = row_sum_sw128(sm.k + s * kKVTile, j, p.dh);
+        const float ks = (float)row_count_sw128(sm.k + s * kKVTile, j, p.dh);
         __nv_bfloat16* slot = reinterpret_cast<__nv_bfloat16*>(sm.aux + j * 128 + ((0 ^ (j & 7)) << 4)) + 1;
         *slot = __float2bfloat16_rn(ks);
       }

@@ -8,16 +8,23 @@
 // pairs ("slots") into every tile: rows 0-63 hold slot 0's queries and keys,
 // rows 64-127 slot 1's.
 //
-//   S = Q K^T   one 128 x 128 tcgen05.mma (fp32 in TMEM; integer counts, exact)
-//   P           the epilogue writes only the two diagonal 64 x 64 blocks
-//               (XNOR transform, bias, mask, bf16 integers); the off-diagonal
-//               blocks are zeroed once and never written, so P V mixes no
-//               values across slots
-//   O = P V     tcgen05.mma with V as an MN-major operand (exact integer sums)
+//   S = Q K^T   one 128 x 128 tcgen05.mma (fp32 in TMEM; integer counts, exact);
+//               row r of slot sl reads its own keys at columns 64 sl .. 64 sl + 63
+//   P           128 rows x 64 keys: each row holds its own slot's keys (XNOR
+//               transform, bias, mask, bf16 integers)
+//   O = P [V0 | V1]  K = 64, N = 128, with V as an MN-major operand whose two
+//               64-column atoms are the two slots' V tiles (exact integer
+//               sums); slot sl's rows keep columns 64 sl .. 64 sl + dh - 1.
+//               Half of the product is discarded, but a one-CTA M = 128 MMA
+//               costs about the same at N = 128 as at N = 48, so four N = 128
+//               instructions replace eight block-diagonal N = 48 ones
 //   a = scale O, LIF over t in registers, bf16 / fp32 spikes
 //
 // CTAs are persistent over items (slot pairs); a CTA walks its items' T steps
-// as a sequence of units.  Q, K, V, S, P and O are double-buffered, and the
+// as a sequence of units.  Q, K and V sit in a ring of three stages, so the
+// loads of the next two units are in flight while a unit is computed (a unit
+// moves about 37 KB, and one SM's share of HBM needs about two units in
+// flight to cover the load latency); S, P and O are double-buffered.  The
 // epilogue is software-pipelined: in iteration g it builds P of unit g, then
 // emits the spikes of unit g-1, whose P V product ran meanwhile.
 //
@@ -36,6 +43,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kTile = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
 constexpr int kHalf = 64 * 128;   // one slot's 64 rows
 constexpr int kMaxLen = 64;
+constexpr int kStages = 3;  // Q/K/V ring
 
 struct Params {
   int T, B, H, Nq, Nk, dh, dsplit;
@@ -57,12 +65,12 @@ struct Params {
 };
 
 struct Smem {
-  uint8_t* q;   // 2 x kTile
-  uint8_t* k;   // 2 x kTile
-  uint8_t* v;   // 2 x kTile
-  uint8_t* p;   // 2 x (2 x kTile): 128 rows x 128 keys bf16 = two 64-key atoms
-  float* ks;    // 2 x 128 key sums
-  float* cq;    // 2 x 128 dh - query sums
+  uint8_t* q;   // kStages x kTile
+  uint8_t* k;   // kStages x kTile
+  uint8_t* v;   // kStages x kTile
+  uint8_t* p;   // 2 x kTile: 128 rows x 64 keys bf16 (one 64-key atom)
+  float* ks;    // kStages x 128 key sums
+  float* cq;    // kStages x 128 dh - query sums
   uint8_t* rl;  // log-distance table [kMaxLen]
   uint64_t *full, *empty, *sums, *s_full, *s_empty, *p_full, *p_empty, *o_full, *o_empty, *drain;
   uint32_t* tmem_base;
@@ -78,11 +86,11 @@ __host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
     off += bytes;
     return o;
   };
-  size_t oq = take(2 * kTile, 1024), ok = take(2 * kTile, 1024), ov = take(2 * kTile, 1024);
-  size_t op = take(4 * kTile, 1024);
-  size_t oks = take(2 * 128 * 4, 16), ocq = take(2 * 128 * 4, 16);
+  size_t oq = take(kStages * kTile, 1024), ok = take(kStages * kTile, 1024), ov = take(kStages * kTile, 1024);
+  size_t op = take(2 * kTile, 1024);
+  size_t oks = take(kStages * 128 * 4, 16), ocq = take(kStages * 128 * 4, 16);
   size_t orl = take(kMaxLen, 16);
-  size_t ob = take(19 * 8, 8);
+  size_t ob = take((3 * kStages + 13) * 8, 8);
   size_t otm = take(4, 4);
   if (s) {
     s->q = base + oq;
@@ -94,34 +102,34 @@ __host__ __device__ inline size_t smem_layout(uint8_t* base, Smem* s) {
     s->rl = base + orl;
     uint64_t* b = reinterpret_cast<uint64_t*>(base + ob);
     s->full = b + 0;
-    s->empty = b + 2;
-    s->sums = b + 4;
-    s->s_full = b + 6;
-    s->s_empty = b + 8;
-    s->p_full = b + 10;
-    s->p_empty = b + 12;
-    s->o_full = b + 14;
-    s->o_empty = b + 16;
-    s->drain = b + 18;
+    s->empty = b + kStages;
+    s->sums = b + 2 * kStages;
+    uint64_t* d = b + 3 * kStages;  // double-buffered S / P / O barriers
+    s->s_full = d + 0;
+    s->s_empty = d + 2;
+    s->p_full = d + 4;
+    s->p_empty = d + 6;
+    s->o_full = d + 8;
+    s->o_empty = d + 10;
+    s->drain = d + 12;
     s->tmem_base = reinterpret_cast<uint32_t*>(base + otm);
   }
   return off;
 }
 
-// sum of the bf16 {0,1} values of row r of a 128B-swizzled tile (first n elems)
-__device__ __forceinline__ float row_sum_sw128(const uint8_t* tile, int r, int n) {
-  float s = 0.0f;
-  const int chunks = (n + 7) >> 3;
-  for (int c = 0; c < chunks; ++c) {
-    const uint4 w = *reinterpret_cast<const uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      s += f.x + f.y;
-    }
-  }
-  return s;
+// bit 7 of each byte of the result is set when that byte of w is nonzero
+// (adding 0x7F to the low seven bits carries into bit 7 exactly when they are
+// not all zero; no carry crosses a byte)
+__device__ __forceinline__ uint32_t byte_nonzero_msb(uint32_t w) {
+  return (((w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | w) & 0x80808080u;
+}
+
+// byte permute: result byte k is byte sel[4k+2:4k] of x, or that byte's sign bit
+// replicated when sel bit 4k+3 is set
+__device__ __forceinline__ uint32_t prmt_u32(uint32_t x, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %1, %2;" : "=r"(d) : "r"(x), "r"(sel));
+  return d;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -151,19 +159,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int G = my_items * p.T;  // units of this CTA
   const int dsteps = (p.dh + 15) >> 4;
 
-  // zero every operand buffer once: the off-diagonal blocks of P stay zero for
-  // the whole kernel, and an unused slot of the last item reads finite data
+  // zero every operand buffer once: an unused slot of the last item then reads
+  // finite data
   {
     uint4 z = make_uint4(0u, 0u, 0u, 0u);
     uint4* b = reinterpret_cast<uint4*>(sm.q);
-    const int n = (10 * kTile) / 16;  // q, k, v (2 each) and p (4) are contiguous
+    const int n = ((3 * kStages + 2) * kTile) / 16;  // q, k, v (kStages each) and p (2) are contiguous
     for (int i = threadIdx.x; i < n; i += kThreads) b[i] = z;
   }
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1 + kEpiWarps);
       mbar_init(&sm.sums[i], kEpiWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1);
       mbar_init(&sm.s_empty[i], kEpiWarps);
       mbar_init(&sm.p_full[i], kEpiWarps);
@@ -204,14 +214,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       bool ok = true;
-      int last_ph[2] = {-1, -1};
+      int last_ph[kStages];
+      for (int i = 0; i < kStages; ++i) last_ph[i] = -1;
       for (int g = 0; g < G; ++g) {
-        const int s = g & 1;
-        if (!mbar_wait(&sm.empty[s], ((g >> 1) & 1) ^ 1u, 141)) { ok = false; break; }
+        const int s = g % kStages;
+        const uint32_t ph = (uint32_t)(g / kStages) & 1u;
+        if (!mbar_wait(&sm.empty[s], ph ^ 1u, 141)) { ok = false; break; }
         const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
         const int nslots = (2 * item + 1 < BH) ? 2 : 1;
         mbar_expect_tx(&sm.full[s], (uint32_t)(3 * nslots * kHalf));
-        last_ph[s] = (g >> 1) & 1;
+        last_ph[s] = (int)ph;
         for (int sl = 0; sl < nslots; ++sl) {
           const int bh = 2 * item + sl, b = bh / p.H, h = bh % p.H, z = t * p.B + b;
           // 4-D maps {dh, H, N, T*B}, box {64, 1, 64, 1}: d >= dh and rows >= N read as zero
@@ -221,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < kStages; ++i)
           if (last_ph[i] >= 0) mbar_wait(&sm.full[i], (uint32_t)last_ph[i], 142);
       }
     }
@@ -229,14 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     bool ok = true;
     const uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
-    const uint32_t idesc_pv = idesc_bf16_f32(128, dsteps * 16, 0, 1);
+    const uint32_t idesc_pv = idesc_bf16_f32(128, 128, 0, 1);
     auto issue_s = [&](int g) -> bool {
-      const int s = g & 1;
-      if (!mbar_wait(&sm.full[s], (g >> 1) & 1, 151)) return false;
+      const int s = g & 1, qs = g % kStages;
+      if (!mbar_wait(&sm.full[qs], (uint32_t)(g / kStages) & 1u, 151)) return false;
       if (!mbar_wait(&sm.s_empty[s], ((g >> 1) & 1) ^ 1u, 152)) return false;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t qa = smem_u32(sm.q + s * kTile), ka = smem_u32(sm.k + s * kTile);
+        const uint32_t qa = smem_u32(sm.q + qs * kTile), ka = smem_u32(sm.k + qs * kTile);
         for (int kk = 0; kk < dsteps; ++kk)
           umma_bf16(tm_s + s * 128, umma_desc(qa + kk * 32, 16, 1024, 2), umma_desc(ka + kk * 32, 16, 1024, 2),
                     idesc_s, kk > 0 ? 1u : 0u);
@@ -248,21 +260,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (G > 0 && !issue_s(0)) ok = false;
     for (int g = 0; g < G && ok; ++g) {
       if (g + 1 < G && !issue_s(g + 1)) { ok = false; break; }
-      const int s = g & 1;
+      const int s = g & 1, qs = g % kStages;
       if (!mbar_wait(&sm.p_full[s], (g >> 1) & 1, 153)) { ok = false; break; }
       if (!mbar_wait(&sm.o_empty[s], ((g >> 1) & 1) ^ 1u, 154)) { ok = false; break; }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t pa = smem_u32(sm.p + s * 2 * kTile), va = smem_u32(sm.v + s * kTile);
+        const uint32_t pa = smem_u32(sm.p + s * kTile), va = smem_u32(sm.v + qs * kTile);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t adesc = umma_desc(pa + (kk >> 2) * kTile + (kk & 3) * 32, 16, 1024, 2);
-          const uint64_t bdesc = umma_desc(va + kk * 2048, kTile, 1024, 2);
-          umma_bf16(tm_o + s * 64, adesc, bdesc, idesc_pv, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {
+          // keys 16 kk .. 16 kk + 15 of each slot; the two slots' V tiles are the
+          // two 64-column atoms of B (kHalf bytes apart)
+          const uint64_t adesc = umma_desc(pa + kk * 32, 16, 1024, 2);
+          const uint64_t bdesc = umma_desc(va + kk * 2048, kHalf, 1024, 2);
+          umma_bf16(tm_o + s * 128, adesc, bdesc, idesc_pv, kk > 0 ? 1u : 0u);
         }
         umma_commit(&sm.o_full[s]);
         umma_commit(&sm.p_empty[s]);
-        umma_commit(&sm.empty[s]);
+        umma_commit(&sm.empty[qs]);
       }
       __syncwarp();
     }
@@ -287,122 +301,160 @@ __global__ void __launch_bounds__(kThreads, 1)
     float mem[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) mem[i] = 0.0f;
+    // the log-distance bias of this thread's row and 32 key columns: the same for
+    // every unit, so it stays in registers, as fp32 pairs (XNOR form only)
+    float2 rb2[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float r[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kj = kc0 + 2 * i + e;
+        const int dist = qi > kj ? qi - kj : kj - qi;
+        r[e] = (p.mode == 1 && dist < p.lmax) ? (float)sm.rl[dist] : 0.0f;
+      }
+      rb2[i] = make_float2(r[0], r[1]);
+    }
+    const bool mask_pf = p.mask_mode == 2 && p.mask_vec && kc0 + 32 <= p.Nk;
+    // where a unit's rows go: step t, item (slot pair) and this thread's (batch,
+    // head); advanced one unit at a time, with one division per item
+    struct UnitPos {
+      int t, item, b, h;
+      bool valid;  // the slot exists and the row is a query
+    };
+    auto set_item = [&](UnitPos& u) {
+      const int bh = 2 * u.item + slot;
+      u.valid = bh < BH && qi < p.Nq;
+      u.b = bh / p.H;
+      u.h = bh - u.b * p.H;
+    };
+    auto advance = [&](UnitPos& u) {
+      if (++u.t == p.T) {
+        u.t = 0;
+        u.item += (int)gridDim.x;
+        set_item(u);
+      }
+    };
+    UnitPos cur;
+    cur.t = 0;
+    cur.item = (int)blockIdx.x;
+    set_item(cur);
+    UnitPos nxt = cur, prv = cur;
+    advance(nxt);
     // dense masks read as 16-byte vectors are loaded one unit ahead (the 32
     // mask bytes of this thread's row and key columns), so their latency
     // hides behind the previous unit's work
-    // the log-distance bias of this thread's row and 32 key columns: the same for
-    // every unit, so it stays in registers (XNOR form only)
-    float rbias[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int kj = kc0 + i;
-      const int dist = qi > kj ? qi - kj : kj - qi;
-      rbias[i] = (p.mode == 1 && dist < p.lmax) ? (float)sm.rl[dist] : 0.0f;
-    }
-    const bool mask_pf = p.mask_mode == 2 && p.mask_vec && kc0 + 32 <= p.Nk;
-    auto mask_load = [&](int gg, uint4& m0, uint4& m1) {
-      const int it = (int)blockIdx.x + (gg / p.T) * (int)gridDim.x, tt = gg % p.T;
-      const int bhh = 2 * it + slot;
+    auto mask_load = [&](const UnitPos& u, uint4& m0, uint4& m1) {
       m0 = make_uint4(0u, 0u, 0u, 0u);
       m1 = m0;
-      if (bhh < BH && qi < p.Nq) {
-        const int b = bhh / p.H, h = bhh % p.H;
-        const uint4* mrow = reinterpret_cast<const uint4*>(p.mask + tt * p.m_st + b * p.m_sb + h * p.m_sh +
+      if (u.valid) {
+        const uint4* mrow = reinterpret_cast<const uint4*>(p.mask + u.t * p.m_st + u.b * p.m_sb + u.h * p.m_sh +
                                                            (int64_t)qi * p.m_sq + kc0);
         m0 = __ldg(mrow);
         m1 = __ldg(mrow + 1);
       }
     };
+    // key sums (-|k_j|, first-half warps) and dh - |q_i| (second half) of unit gg
+    // into its stage; the epilogue is then done with the stage's Q and K.  Run
+    // one unit ahead, so that the all-warp barrier on the sums is met by the
+    // time P needs them.
+    auto sums = [&](int gg) -> bool {
+      const int qs = gg % kStages;
+      if (!mbar_wait(&sm.full[qs], (uint32_t)(gg / kStages) & 1u, 161)) return false;
+      if (p.mode == 1) {
+        if (half == 0)
+          sm.ks[qs * 128 + row] = -(float)row_count_sw128(sm.k + qs * kTile, row, p.dh);
+        else
+          sm.cq[qs * 128 + row] = (float)(p.dh - row_count_sw128(sm.q + qs * kTile, row, p.dh));
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.empty[qs]);
+        if (p.mode == 1) mbar_arrive(&sm.sums[qs]);
+      }
+      return true;
+    };
     uint4 pm0 = make_uint4(0u, 0u, 0u, 0u), pm1 = pm0;
-    if (mask_pf && G > 0) mask_load(0, pm0, pm1);
-    bool ok = true;
+    if (mask_pf && G > 0) mask_load(cur, pm0, pm1);
+    const float2 two2 = make_float2(2.0f, 2.0f), scale2 = make_float2(scale, scale);
+    const float2 gain2 = make_float2(p.gain, p.gain), beta2 = make_float2(beta, beta);
+    bool ok = G == 0 || sums(0);
     for (int g = 0; g <= G && ok; ++g) {
       if (g < G) {
         // ---- build P of unit g
-        const int s = g & 1;
-        const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
-        const int bh = 2 * item + slot;
-        uint32_t pf_bits = 0u;
+        const int s = g & 1, qs = g % kStages;
+        const uint32_t qph = (uint32_t)(g / kStages) & 1u;
+        // keep flags of this thread's 32 key columns: the most significant bit of
+        // byte i of fw[i / 4] is set when key kc0 + i is kept
+        uint32_t fw[8];
         if (mask_pf) {
           const uint32_t w[8] = {pm0.x, pm0.y, pm0.z, pm0.w, pm1.x, pm1.y, pm1.z, pm1.w};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) pf_bits |= (((w[i >> 2] >> ((i & 3) * 8)) & 0xffu) != 0u ? 1u : 0u) << i;
-          if (g + 1 < G) mask_load(g + 1, pm0, pm1);
+          for (int k = 0; k < 8; ++k) fw[k] = byte_nonzero_msb(w[k]);
+          if (g + 1 < G) mask_load(nxt, pm0, pm1);
+        } else {
+          uint32_t mbits = 0xffffffffu;  // keep bit per key column of this warp
+          if (p.mask_mode == 2) {
+            mbits = 0u;
+            if (cur.valid) {
+              const uint8_t* mrow =
+                  p.mask + cur.t * p.m_st + cur.b * p.m_sb + cur.h * p.m_sh + (int64_t)qi * p.m_sq + kc0;
+              for (int i = 0; i < 32 && kc0 + i < p.Nk; ++i) mbits |= (mrow[i] != 0 ? 1u : 0u) << i;
+            }
+          } else if (p.mask_mode == 1) {
+            // key kj = kc0 + i is kept when kj <= qi
+            const int n = qi - kc0 + 1;
+            mbits = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+          }
+          if (p.Nk - kc0 < 32) {
+            const int n = p.Nk - kc0;
+            mbits &= n <= 0 ? 0u : ((1u << n) - 1u);
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            // bit j of the nibble to bit 7 of byte j (the shifted copies do not overlap)
+            const uint32_t x = (mbits >> (4 * k)) & 0xFu;
+            fw[k] = ((x * 0x00204081u) & 0x01010101u) << 7;
+          }
         }
-        if (!mbar_wait(&sm.full[s], (g >> 1) & 1, 161)) { ok = false; break; }
-        if (p.mode == 1) {
-          if (half == 0)
-            sm.ks[s * 128 + row] = row_sum_sw128(sm.k + s * kTile, row, p.dh);
-          else
-            sm.cq[s * 128 + row] = (float)p.dh - row_sum_sw128(sm.q + s * kTile, row, p.dh);
-        }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sm.empty[s]);
-          if (p.mode == 1) mbar_arrive(&sm.sums[s]);
-        }
-        if (p.mode == 1 && !mbar_wait(&sm.sums[s], (g >> 1) & 1, 162)) { ok = false; break; }
+        if (p.mode == 1 && !mbar_wait(&sm.sums[qs], qph, 162)) { ok = false; break; }
         if (!mbar_wait(&sm.s_full[s], (g >> 1) & 1, 163)) { ok = false; break; }
         if (!mbar_wait(&sm.p_empty[s], ((g >> 1) & 1) ^ 1u, 164)) { ok = false; break; }
         tc_fence_after();
         uint32_t raw[32];
         tmem_ld32_raw(tm_s + s * 128 + lane_off + slot * 64 + kc0, raw);
-        const float c_row = p.mode == 1 ? sm.cq[s * 128 + row] : 0.0f;
-        const float* ks = sm.ks + s * 128 + slot * 64;
-        uint32_t mbits = 0xffffffffu;  // keep bit per key column of this warp
-        if (mask_pf) {
-          mbits = pf_bits;
-        } else if (p.mask_mode == 2) {
-          mbits = 0u;
-          if (bh < BH && qi < p.Nq) {
-            const int b = bh / p.H, h = bh % p.H;
-            const uint8_t* mrow = p.mask + t * p.m_st + b * p.m_sb + h * p.m_sh + (int64_t)qi * p.m_sq + kc0;
-            if (p.mask_vec && kc0 + 32 <= p.Nk) {
-              const uint4 m0 = __ldg(reinterpret_cast<const uint4*>(mrow));
-              const uint4 m1 = __ldg(reinterpret_cast<const uint4*>(mrow) + 1);
-              const uint32_t w[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-#pragma unroll
-              for (int i = 0; i < 32; ++i) mbits |= (((w[i >> 2] >> ((i & 3) * 8)) & 0xffu) != 0u ? 1u : 0u) << i;
-            } else {
-              for (int i = 0; i < 32 && kc0 + i < p.Nk; ++i) mbits |= (mrow[i] != 0 ? 1u : 0u) << i;
-            }
-          }
-        } else if (p.mask_mode == 1) {
-          // key kj = kc0 + i is kept when kj <= qi
-          const int n = qi - kc0 + 1;
-          mbits = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
-        }
-        if (p.Nk - kc0 < 32) {
-          const int n = p.Nk - kc0;
-          mbits &= n <= 0 ? 0u : ((1u << n) - 1u);
-        }
+        const float c_row = p.mode == 1 ? sm.cq[qs * 128 + row] : 0.0f;
+        const float2 c2 = make_float2(c_row, c_row);
+        const float* nks = sm.ks + qs * 128 + slot * 64 + kc0;  // -|k_j|
         tmem_wait_ld_fence32(raw);
-        float v[32];
+        // S' = 2 S + (c_i + R_ij - |k_j|) in packed fp32 pairs (all integers, exact), then
+        // bf16 pairs (exact: |S'| < 256) with the masked keys cleared
+        uint32_t pw[16];
 #pragma unroll
-        for (int i0 = 0; i0 < 32; i0 += 4) {
+        for (int i0 = 0; i0 < 16; i0 += 2) {
           // four key sums in one 16-byte load (the same address in every lane)
-          const float4 k4 = p.mode == 1 ? *reinterpret_cast<const float4*>(ks + kc0 + i0)
+          const float4 k4 = p.mode == 1 ? *reinterpret_cast<const float4*>(nks + 2 * i0)
                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 2; ++u) {
             const int i = i0 + u;
-            float sc = __uint_as_float(raw[i]);
-            if (p.mode == 1) sc = fmaf(2.0f, sc, c_row - kv[u]) + rbias[i];
-            v[i] = ((mbits >> i) & 1u) ? sc : 0.0f;
+            float2 sc = make_float2(__uint_as_float(raw[2 * i]), __uint_as_float(raw[2 * i + 1]));
+            if (p.mode == 1) {
+              const float2 nk2 = u == 0 ? make_float2(k4.x, k4.y) : make_float2(k4.z, k4.w);
+              sc = fma2(sc, two2, add2(add2(rb2[i], c2), nk2));
+            }
+            // keep masks of keys 2i, 2i+1 as 0xFFFF halves (sign replication of the flags)
+            const uint32_t keep = prmt_u32(fw[i >> 1], (i & 1) ? 0xBBAAu : 0x9988u);
+            pw[i] = pack_bf16x2(sc.x, sc.y) & keep;
           }
         }
-        // 32 keys of row `row` into the slot's 64-key atom (K-major, 128-byte swizzle)
-        uint8_t* prow = sm.p + s * 2 * kTile + slot * kTile + row * 128;
+        // 32 keys of row `row` into the 64-key atom (K-major, 128-byte swizzle)
+        uint8_t* prow = sm.p + s * kTile + row * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int ch = half * 4 + c;
-          uint4 w;
-          w.x = pack_bf16x2(v[c * 8 + 0], v[c * 8 + 1]);
-          w.y = pack_bf16x2(v[c * 8 + 2], v[c * 8 + 3]);
-          w.z = pack_bf16x2(v[c * 8 + 4], v[c * 8 + 5]);
-          w.w = pack_bf16x2(v[c * 8 + 6], v[c * 8 + 7]);
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = w;
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
         }
         tc_fence_before();
         fence_proxy_async_smem();
@@ -411,60 +463,63 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&sm.s_empty[s]);
           mbar_arrive(&sm.p_full[s]);
         }
+        if (g + 1 < G && !sums(g + 1)) { ok = false; break; }
       }
       if (g >= 1) {
-        // ---- spikes of unit u = g - 1
+        // ---- spikes of unit g - 1
         const int u = g - 1, s = u & 1;
-        const int item = (int)blockIdx.x + (u / p.T) * (int)gridDim.x, t = u % p.T;
-        const int bh = 2 * item + slot;
         if (!mbar_wait(&sm.o_full[s], (u >> 1) & 1, 165)) { ok = false; break; }
         tc_fence_after();
         uint32_t raw[32];
-        tmem_ld32_raw(tm_o + s * 64 + lane_off + dcol0, raw);
+        tmem_ld32_raw(tm_o + s * 128 + lane_off + slot * 64 + dcol0, raw);
         tmem_wait_ld_fence32(raw);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.o_empty[s]);
-        if (t == 0) {
+        if (prv.t == 0) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) mem[i] = 0.0f;
         }
-        if (bh < BH && qi < p.Nq) {
-          const int b = bh / p.H, h = bh % p.H;
-          const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh + dcol0;
-          float* aout = p.attn_out
-                            ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh + dcol0
-                            : nullptr;
+        if (prv.valid) {
+          const int64_t obase = (((int64_t)prv.t * p.B + prv.b) * p.Nq + qi) * D + (int64_t)prv.h * p.dh + dcol0;
+          float* aout = p.attn_out ? p.attn_out + ((((int64_t)prv.t * p.B + prv.b) * p.H + prv.h) * p.Nq + qi) * p.dh +
+                                         dcol0
+                                   : nullptr;
 #pragma unroll
           for (int d0 = 0; d0 < 32; d0 += 8) {
             if (d0 < dcols) {
-              float sp[8];
+              // a = scale O, LIF over t: packed fp32 pairs that round as the scalar
+              // reference (a * gain is exact when the gain is 1)
+              uint32_t bits[4];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float a = __fmul_rn(__uint_as_float(raw[d0 + i]), scale);
-                if (aout) aout[d0 + i] = a;
-                const float cur = p.gain != 1.0f ? __fmul_rn(a, p.gain) : a;
-                const float uu = __fadd_rn(__fmul_rn(mem[d0 + i], beta), cur);
-                const bool fire = uu > vth;
-                sp[i] = fire ? 1.0f : 0.0f;
-                mem[d0 + i] = fire ? vr : uu;
+              for (int j = 0; j < 8; j += 2) {
+                const int dd = d0 + j;
+                const float2 a = mul2(make_float2(__uint_as_float(raw[dd]), __uint_as_float(raw[dd + 1])), scale2);
+                if (aout) *reinterpret_cast<float2*>(aout + dd) = a;
+                const float2 uu = add2(mul2(make_float2(mem[dd], mem[dd + 1]), beta2), mul2(a, gain2));
+                const bool f0 = uu.x > vth, f1 = uu.y > vth;
+                mem[dd] = f0 ? vr : uu.x;
+                mem[dd + 1] = f1 ? vr : uu.y;
+                bits[j >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
               }
-              if (p.out_bf16) {
-                uint4 w;
-                w.x = pack_bf16x2(sp[0], sp[1]);
-                w.y = pack_bf16x2(sp[2], sp[3]);
-                w.z = pack_bf16x2(sp[4], sp[5]);
-                w.w = pack_bf16x2(sp[6], sp[7]);
-                *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = w;
-              }
+              if (p.out_bf16)
+                *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
               if (p.out_f32) {
-                *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = make_float4(sp[0], sp[1], sp[2], sp[3]);
-                *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = make_float4(sp[4], sp[5], sp[6], sp[7]);
+                float4 lo, hi;
+                lo.x = (bits[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bits[0] >> 16) ? 1.0f : 0.0f;
+                lo.z = (bits[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bits[1] >> 16) ? 1.0f : 0.0f;
+                hi.x = (bits[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bits[2] >> 16) ? 1.0f : 0.0f;
+                hi.z = (bits[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bits[3] >> 16) ? 1.0f : 0.0f;
+                *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = lo;
+                *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = hi;
               }
             }
           }
         }
       }
+      prv = cur;
+      cur = nxt;
+      advance(nxt);
     }
     (void)ok;
   }

@@ -453,6 +453,8 @@ def spikes_qkv(seed, TB, Nq, Nk, D, p=0.15):
     (3, 5, 3, 33, 50, 32, "dense"),
     (2, 3, 3, 64, 20, 16, "dense"),
     (2, 2, 4, 12, 12, 8, "causal"),
+    (2, 3, 2, 48, 48, 64, "causal"),  # head width 64: the slots' V tiles fill both atoms of P V
+    (1, 3, 1, 64, 64, 64, "dense"),
 ])
 def test_ssa(ops, variant, T, B, H, Nq, Nk, dh, maskkind):
     D = H * dh
