@@ -434,6 +434,13 @@ __device__ __forceinline__ int row_count_sw128(const uint8_t* tile, int r, int n
   return (int)(((acc & 0xFFFFu) + (acc >> 16)) >> 7);
 }
 
+// 32-byte global store (sm_100): the address must be 32-byte aligned
+__device__ __forceinline__ void st_global_v8(void* ptr, uint4 lo, uint4 hi) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(lo.x), "r"(lo.y),
+               "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- packed fp32x2 arithmetic (sm_100)
 // Each operation rounds like its scalar fp32 counterpart (round to nearest).
 __device__ __forceinline__ float2 add2(float2 a, float2 b) {

@@ -52,6 +52,7 @@ struct Params {
   float* out_f32;
   float* attn_out;
   int lmax, items;
+  int v8;  // bf16 output rows may be written as 32-byte vectors (16-column chunks)
 };
 
 struct Smem {
@@ -422,11 +423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // reference (the integer terms are exact in any order).
       auto out_chunk = [&](int c, const uint32_t (&rc)[16]) {
         const int c0 = c * 16;
+        uint32_t bits[8];  // bf16 spike pairs of the chunk's 16 columns
 #pragma unroll
         for (int d8 = 0; d8 < 16; d8 += 8) {
           const int d0 = c0 + d8;
           if (d0 < dc0 || d0 >= dc0 + dcols) continue;
-          uint32_t bits[4];
 #pragma unroll
           for (int i = 0; i < 8; i += 4) {
             const float4 cs4 = *reinterpret_cast<const float4*>(csp + d0 + i);
@@ -448,16 +449,35 @@ __global__ void __launch_bounds__(kThreads, 1)
               const bool f0 = u.x > vth, f1 = u.y > vth;
               mem[dd] = f0 ? vr : u.x;
               mem[dd + 1] = f1 ? vr : u.y;
-              bits[(i + j) >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
+              bits[(d8 + i + j) >> 1] = (f0 ? 0x3F80u : 0u) | (f1 ? 0x3F800000u : 0u);
             }
           }
-          if (p.out_bf16) *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[0], bits[1], bits[2], bits[3]);
-          if (p.out_f32) {
+        }
+        const bool whole = c0 >= dc0 && c0 + 16 <= dc0 + dcols;
+        if (p.out_bf16 && whole && p.v8) {
+          // the chunk's 32 bytes in one store: whole sectors
+          st_global_v8(p.out_bf16 + obase + c0, make_uint4(bits[0], bits[1], bits[2], bits[3]),
+                       make_uint4(bits[4], bits[5], bits[6], bits[7]));
+        } else if (p.out_bf16) {
+#pragma unroll
+          for (int d8 = 0; d8 < 16; d8 += 8) {
+            const int d0 = c0 + d8;
+            if (d0 < dc0 || d0 >= dc0 + dcols) continue;
+            const int w = d8 >> 1;
+            *reinterpret_cast<uint4*>(p.out_bf16 + obase + d0) = make_uint4(bits[w], bits[w + 1], bits[w + 2], bits[w + 3]);
+          }
+        }
+        if (p.out_f32) {
+#pragma unroll
+          for (int d8 = 0; d8 < 16; d8 += 8) {
+            const int d0 = c0 + d8;
+            if (d0 < dc0 || d0 >= dc0 + dcols) continue;
+            const uint32_t* bw = bits + (d8 >> 1);
             float4 lo, hi;
-            lo.x = (bits[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bits[0] >> 16) ? 1.0f : 0.0f;
-            lo.z = (bits[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bits[1] >> 16) ? 1.0f : 0.0f;
-            hi.x = (bits[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bits[2] >> 16) ? 1.0f : 0.0f;
-            hi.z = (bits[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bits[3] >> 16) ? 1.0f : 0.0f;
+            lo.x = (bw[0] & 0xFFFFu) ? 1.0f : 0.0f; lo.y = (bw[0] >> 16) ? 1.0f : 0.0f;
+            lo.z = (bw[1] & 0xFFFFu) ? 1.0f : 0.0f; lo.w = (bw[1] >> 16) ? 1.0f : 0.0f;
+            hi.x = (bw[2] & 0xFFFFu) ? 1.0f : 0.0f; hi.y = (bw[2] >> 16) ? 1.0f : 0.0f;
+            hi.z = (bw[3] & 0xFFFFu) ? 1.0f : 0.0f; hi.w = (bw[3] >> 16) ? 1.0f : 0.0f;
             *reinterpret_cast<float4*>(p.out_f32 + obase + d0) = lo;
             *reinterpret_cast<float4*>(p.out_f32 + obase + d0 + 4) = hi;
           }
@@ -533,6 +553,7 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   p.lif_vr = lif_vr;
   p.gain = gain;
   p.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  p.v8 = dh % 16 == 0 && aligned(out_bf16, 32);
   p.out_f32 = out_f32;
   p.attn_out = attn_out;
   p.QB = (Nq + 127) / 128;
