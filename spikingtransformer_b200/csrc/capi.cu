@@ -139,11 +139,12 @@ int gemm_il_read_device_error(cudaStream_t);
 int ssa_read_device_error(cudaStream_t);
 int ssa_lin_read_device_error(cudaStream_t);
 int ssa_short_read_device_error(cudaStream_t);
+int lif_read_device_error(cudaStream_t);
 typedef int (*ErrorReader)(cudaStream_t);
 static ErrorReader g_error_readers[] = {gemm_read_device_error,     gemm_il_read_device_error,
                                         ssa_read_device_error,      ssa_lin_read_device_error,
-                                        ssa_short_read_device_error, capi_read_device_error,
-                                        nullptr};
+                                        ssa_short_read_device_error, lif_read_device_error,
+                                        capi_read_device_error,      nullptr};
 
 }  // namespace spk
 

@@ -268,6 +268,188 @@ __global__ void __launch_bounds__(kBwdThreads, TMAX <= 4 ? 3 : 1) lif_bwd_kernel
   }
 }
 
+// ---- backward, staged through shared memory (fp32 x, T <= 4) --------------
+// Persistent blocks walk tiles of kSTile neurons.  One thread issues bulk
+// copies (cp.async.bulk, contiguous rows, no tensor map) of a tile's x,
+// spike-gradient, spike and g_vfinal rows into a ring of shared-memory stages,
+// up to kSStages tiles ahead, so the loads of the next tiles are in flight
+// while a tile is computed and no registers are spent holding them.  The
+// arithmetic is the register kernel's, operation for operation, so the
+// results are the same bit for bit.
+constexpr int kSTile = 4 * kBwdThreads;  // neurons per tile (4 per thread)
+constexpr int kSRow = kSTile * 4;        // bytes of one fp32 row of a tile
+
+template <int SDT>
+__host__ __device__ constexpr int staged_spike_row(int n) {
+  return SDT == SPK_BIT ? n / 8 : SDT == SPK_BF16 ? 2 * n : n;
+}
+template <int SDT>
+__host__ __device__ constexpr int staged_stages() {
+  return SDT == SPK_BIT ? 3 : 2;
+}
+// stage: x [4][kSTile] f32 | g_s [4][kSTile] f32 | g_vfinal [kSTile] f32 | spikes [4][row]
+template <int SDT>
+__host__ __device__ constexpr int staged_stage_bytes() {
+  return (9 * kSRow + 4 * staged_spike_row<SDT>(kSTile) + 127) / 128 * 128;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int SDT>
+__global__ void __launch_bounds__(kBwdThreads, 2) lif_bwd_staged_kernel(
+    const float* __restrict__ gs, const float* __restrict__ gvf, const float* __restrict__ x,
+    const void* __restrict__ spikes, const float* pbeta, const float* pvth, const float* pvr, float gain,
+    int surr, float k, float c_arctan, float* __restrict__ gx, float* __restrict__ partials, int T, int64_t N) {
+  constexpr int S = staged_stages<SDT>();
+  constexpr int SB = staged_spike_row<SDT>(kSTile);
+  constexpr int kStage = staged_stage_bytes<SDT>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[S];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  const int64_t tiles = (N + kSTile - 1) / kSTile;
+  const int my = (int)((tiles - (int64_t)blockIdx.x + gridDim.x - 1) / gridDim.x);
+  const int64_t srow = SDT == SPK_BIT ? N / 8 : (int64_t)staged_spike_row<SDT>(1) * N;  // spike bytes per step
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const float beta = __ldg(pbeta), vth = __ldg(pvth), vr = __ldg(pvr);
+  const bool use_gain = gain != 1.0f;
+  // tile j of this block's sequence into stage j % S
+  auto issue = [&](int j) {
+    const int s = j % S;
+    const int64_t base = ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) * kSTile;
+    const int64_t left = N - base;
+    const int n = left < kSTile ? (int)left : kSTile;
+    const uint32_t rb = (uint32_t)n * 4u, sb = (uint32_t)staged_spike_row<SDT>(n);
+    const int64_t sbase = SDT == SPK_BIT ? base / 8 : base * staged_spike_row<SDT>(1);  // spike bytes before the tile
+    uint8_t* st = smem + (size_t)s * kStage;
+    mbar_expect_tx(&full[s], (uint32_t)T * (2u * rb + sb) + (gvf ? rb : 0u));
+    for (int t = 0; t < T; ++t) {
+      bulk_load(st + t * kSRow, x + (int64_t)t * N + base, rb, &full[s]);
+      bulk_load(st + (4 + t) * kSRow, gs + (int64_t)t * N + base, rb, &full[s]);
+      bulk_load(st + 9 * kSRow + t * SB, reinterpret_cast<const uint8_t*>(spikes) + t * srow + sbase, sb, &full[s]);
+    }
+    if (gvf) bulk_load(st + 8 * kSRow, gvf + base, rb, &full[s]);
+  };
+  if (tid == 0)
+    for (int j = 0; j < S && j < my; ++j) issue(j);
+  float thread_acc = 0.0f;
+  int j = 0;
+  for (; j < my; ++j) {
+    const int s = j % S;
+    if (!mbar_wait(&full[s], (uint32_t)(j / S) & 1u, 181)) abort_flag = 1;
+    const int64_t base = ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) * kSTile;
+    const int64_t left = N - base;
+    const int n = left < kSTile ? (int)left : kSTile;
+    const uint8_t* st = smem + (size_t)s * kStage;
+    if (!abort_flag && tid * 4 < n) {
+      const int col = tid * 4;
+      float vh[4][4], gsv[4][4], v[4];
+      uint32_t sbits[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (t < T) {
+          const float4 g4 = *reinterpret_cast<const float4*>(st + (4 + t) * kSRow + col * 4);
+          gsv[t][0] = g4.x; gsv[t][1] = g4.y; gsv[t][2] = g4.z; gsv[t][3] = g4.w;
+          if constexpr (SDT == SPK_BIT) {
+            const uint32_t byte = st[9 * kSRow + t * SB + (col >> 3)];
+            sbits[t] = (byte >> (col & 7)) & 0xFu;
+          } else {
+            float sv[4];
+            load_vec<SDT, 4>(st + 9 * kSRow + t * SB, col, sv);
+            uint32_t bits = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) bits |= (sv[i] > 0.0f ? 1u : 0u) << i;
+            sbits[t] = bits;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = 0.0f;
+      // pass 1: the pre-reset membrane (Lif.py:222-233)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (t < T) {
+          const float4 x4 = *reinterpret_cast<const float4*>(st + t * kSRow + col * 4);
+          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float cur = use_gain ? __fmul_rn(xv[i], gain) : xv[i];
+            float u = __fadd_rn(__fmul_rn(v[i], beta), cur);
+            vh[t][i] = u;
+            v[i] = ((sbits[t] >> i) & 1u) ? vr : u;
+          }
+        }
+      }
+      // pass 2: reverse sweep (Lif.py:236-273)
+      float gstate[4], acc[4];
+      if (gvf) {
+        const float4 v4 = *reinterpret_cast<const float4*>(st + 8 * kSRow + col * 4);
+        gstate[0] = v4.x; gstate[1] = v4.y; gstate[2] = v4.z; gstate[3] = v4.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gstate[i] = 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = 0.0f;
+#pragma unroll
+      for (int t = 3; t >= 0; --t) {
+        if (t < T) {
+          float out[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const bool sp = (sbits[t] >> i) & 1u;
+            const float sg = surrogate(surr, __fadd_rn(vh[t][i], -vth), k, c_arctan);
+            const float from_state = sp ? 0.0f : gstate[i];
+            const float gv = __fadd_rn(__fmul_rn(gsv[t][i], sg), from_state);
+            out[i] = use_gain ? __fmul_rn(gv, gain) : gv;
+            float vprev = 0.0f;
+            if (t > 0) vprev = ((sbits[t - 1] >> i) & 1u) ? vr : vh[t - 1][i];
+            acc[i] = __fadd_rn(acc[i], __fmul_rn(gv, vprev));
+            gstate[i] = __fmul_rn(gv, beta);
+          }
+          *reinterpret_cast<float4*>(gx + (int64_t)t * N + base + col) = make_float4(out[0], out[1], out[2], out[3]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) thread_acc += acc[i];
+    }
+    __syncthreads();  // every thread is done with stage s (and has seen abort_flag)
+    if (abort_flag) break;
+    if (tid == 0 && j + S < my) {
+      fence_proxy_async_smem();  // the reads above come before the copies that overwrite them
+      issue(j + S);
+    }
+  }
+  if (abort_flag && tid == 0) {
+    // tiles j .. j + S - 1 may still have copies in flight: let them land
+    // before the block exits (each wait bounded)
+    for (int jj = j; jj < my && jj < j + S; ++jj) mbar_wait(&full[jj % S], (uint32_t)(jj / S) & 1u, 182);
+  }
+  // deterministic block reduction of the grad_beta partial
+  __shared__ float red[kBwdThreads / 32];
+  float s = thread_acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float r = threadIdx.x < kBwdThreads / 32 ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (threadIdx.x == 0 && partials) partials[blockIdx.x] = r;
+  }
+}
+
 __global__ void __launch_bounds__(1024) sum_partials_kernel(const float* __restrict__ partials, int n,
                                                             float* __restrict__ out) {
   __shared__ float red[32];
@@ -335,6 +517,24 @@ void launch_bwd(int grid, const float* gs, const float* gvf, const void* x, cons
                                                                     gx, part, T, N);
 }
 
+// The staged backward for fp32 x and T <= 4; returns the grid it launched
+// (the number of grad_beta partials), or 0 when it does not take the call.
+template <int SDT>
+int launch_bwd_staged(const float* gs, const float* gvf, const float* x, const void* s, const float* b,
+                      const float* th, const float* vr, float gain, int surr, float k, float c, float* gx,
+                      float* part, int T, int64_t N, cudaStream_t st) {
+  const int64_t tiles = (N + kSTile - 1) / kSTile;
+  int64_t grid = 2 * (int64_t)num_sms();
+  if (grid > tiles) grid = tiles;
+  const int smem = staged_stages<SDT>() * staged_stage_bytes<SDT>();
+  if (cudaFuncSetAttribute(lif_bwd_staged_kernel<SDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return 0;
+  lif_bwd_staged_kernel<SDT><<<(int)grid, kBwdThreads, smem, st>>>(gs, gvf, x, s, b, th, vr, gain, surr, k, c, gx,
+                                                                    part, T, N);
+  return (int)grid;
+}
+
 template <int XDT, int SDT>
 int dispatch_bwd_t(int T, bool vec, int grid, const float* gs, const float* gvf, const void* x, const void* s,
                    const float* b, const float* th, const float* vr, float gain, int surr, float k, float c,
@@ -377,6 +577,8 @@ int dispatch_bwd_s(int sdt, int T, bool vec, int grid, const float* gs, const fl
 
 using namespace lifk;
 
+SPK_DEFINE_ERROR_READER(lif_read_device_error)
+
 // Shared implementation of the backward entry points: `partials` holds at
 // least bwd_grid(T, N) floats.
 int lif_bwd_impl(const float* g_spikes, const float* g_vfinal, const void* x, int x_dtype, const void* spikes,
@@ -405,6 +607,32 @@ int lif_bwd_impl(const float* g_spikes, const float* g_vfinal, const void* x, in
   if (grid > kBwdMaxBlocks) grid = kBwdMaxBlocks;
   const float c = (float)(3.14159265358979323846 / 2.0 * (double)surrogate_k);
   int rc;
+  // fp32 currents, T <= 4, whole 128-neuron blocks and 16-byte aligned rows:
+  // the kernel that stages its inputs through shared memory with bulk copies
+  const bool staged = x_dtype == SPK_F32 && T <= 4 && N > 0 && N % 128 == 0 &&
+                      (spike_dtype == SPK_BIT || spike_dtype == SPK_BF16 || spike_dtype == SPK_U8 ||
+                       spike_dtype == SPK_FP8) &&
+                      aligned(g_spikes, 16) && (!g_vfinal || aligned(g_vfinal, 16)) && aligned(x, 16) &&
+                      aligned(spikes, 16) && aligned(grad_x, 16);
+  if (staged) {
+    const float* xf = static_cast<const float*>(x);
+    float* gxf = static_cast<float*>(grad_x);
+    int sg = 0;
+    switch (spike_dtype) {
+      case SPK_BIT: sg = launch_bwd_staged<SPK_BIT>(g_spikes, g_vfinal, xf, spikes, beta, v_th, v_reset, in_gain, surrogate_kind, surrogate_k, c, gxf, partials, (int)T, N, st); break;
+      case SPK_BF16: sg = launch_bwd_staged<SPK_BF16>(g_spikes, g_vfinal, xf, spikes, beta, v_th, v_reset, in_gain, surrogate_kind, surrogate_k, c, gxf, partials, (int)T, N, st); break;
+      case SPK_U8: sg = launch_bwd_staged<SPK_U8>(g_spikes, g_vfinal, xf, spikes, beta, v_th, v_reset, in_gain, surrogate_kind, surrogate_k, c, gxf, partials, (int)T, N, st); break;
+      default: sg = launch_bwd_staged<SPK_FP8>(g_spikes, g_vfinal, xf, spikes, beta, v_th, v_reset, in_gain, surrogate_kind, surrogate_k, c, gxf, partials, (int)T, N, st); break;
+    }
+    if (sg > 0) {
+      if ((rc = check_launch("lif_bwd_staged_kernel")) != SPK_OK) return rc;
+      if (grad_beta) {
+        sum_partials_kernel<<<1, 1024, 0, st>>>(partials, sg, grad_beta);
+        if ((rc = check_launch("sum_partials_kernel")) != SPK_OK) return rc;
+      }
+      return SPK_OK;
+    }
+  }
   switch (x_dtype) {
     case SPK_F32:
       rc = dispatch_bwd_s<SPK_F32>(spike_dtype, (int)T, vec, grid, g_spikes, g_vfinal, x, spikes, beta, v_th,

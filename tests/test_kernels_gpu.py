@@ -107,6 +107,34 @@ def test_lif_shapes_and_surrogates(ops, T, N, surrogate):
     assert torch.allclose(gb.cpu().reshape(()), gb_ref, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("T,N", [(1, 128), (3, 5 * 1024 + 384), (4, 600 * 1024)])
+@pytest.mark.parametrize("surrogate", ["superspike", "arctan"])
+def test_lif_bwd_staged_inputs(ops, T, N, surrogate):
+    """The backward that stages its inputs through shared memory with bulk
+    copies (fp32 currents, T <= 4, N a multiple of 128): every spike format it
+    reads, with and without g_vfinal, a partial last tile of 1024 neurons and
+    more tiles than blocks."""
+    g = gen(7 * N + T)
+    x = torch.randn(T, N, generator=g) + 0.4
+    gs = torch.randn(T, N, generator=g)
+    gvf = torch.randn(N, generator=g)
+    s_ref, _ = oracle.lif_forward(x, 0.7, 1.0, 0.0, in_gain=0.5)
+    xd = x.to(DEV)
+    for sd in (torch.bfloat16, torch.uint8, torch.float8_e4m3fn, "bits"):
+        s, _ = ops.lif_fwd(xd, 0.7, 1.0, 0.0, in_gain=0.5, spike_dtype=sd)
+        for gv in (None, gvf):
+            gx_ref, gb_ref = oracle.lif_backward(gs, gv, x, s_ref, 0.7, 1.0, 0.0, k=2.0, in_gain=0.5,
+                                                 surrogate=surrogate)
+            gx, gb = ops.lif_bwd(gs.to(DEV), None if gv is None else gv.to(DEV), xd, s, 0.7, 1.0, 0.0,
+                                 in_gain=0.5, surrogate=surrogate, k=2.0, spikes_packed=sd == "bits")
+            what = "%s spikes, g_vfinal %s" % (sd, gv is not None)
+            if surrogate == "superspike":
+                assert torch.equal(gx.cpu(), gx_ref), what
+            else:
+                assert torch.allclose(gx.cpu(), gx_ref, rtol=1e-6, atol=1e-7), what
+            assert torch.allclose(gb.cpu().reshape(()), gb_ref, rtol=1e-4, atol=1e-4), what
+
+
 def test_lif_empty(ops):
     x = torch.empty(4, 0, device=DEV)
     s, vf = ops.lif_fwd(x, 0.9, 1.0, 0.0)
