@@ -15,7 +15,7 @@ from spikingtransformer_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def _inputs(T, N, seed, x_dtype=torch.float32):
+def _inputs(T, N, seed, x_dtype=torch.float32, spike_dtype=torch.float32):
     g = torch.Generator().manual_seed(seed)
     x = (torch.randn(T, N, generator=g) * 0.8 + 0.6).to(x_dtype)
     v = torch.zeros(N)
@@ -27,7 +27,7 @@ def _inputs(T, N, seed, x_dtype=torch.float32):
     gs = torch.randn(T, N, generator=g)
     gv = torch.randn(N, generator=g)
     dev = torch.device("cuda", 0)
-    return x.to(dev), spikes.to(dev), gs.to(dev), gv.to(dev)
+    return x.to(dev), spikes.to(spike_dtype).to(dev), gs.to(dev), gv.to(dev)
 
 
 def _params(dev):
@@ -65,12 +65,16 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
     # then large and odd (scalar path at the 4096-block cap, every partial of
     # the static array in use), then the first one again: bit-exact, the
     # tolerance the LIF tests use
-    cases = [(4, 3 << 20, 1, _lib.SURROGATE["superspike"], 4.0, 1.0),
-             (3, 1001, 2, _lib.SURROGATE["arctan"], 2.0, 0.5),
-             (4, (3 << 20) + 1, 5, _lib.SURROGATE["superspike"], 4.0, 1.0),
-             (4, 3 << 20, 3, _lib.SURROGATE["superspike"], 4.0, 1.0)]
-    for T, N, seed, surrogate, k, gain in cases:
-        x, spikes, gs, gv = _inputs(T, N, seed)
+    # the last case has bf16 spikes, which the shared-memory-staged backward
+    # (persistent blocks, one partial each) takes
+    f32, bf16 = torch.float32, torch.bfloat16
+    cases = [(4, 3 << 20, 1, _lib.SURROGATE["superspike"], 4.0, 1.0, f32),
+             (3, 1001, 2, _lib.SURROGATE["arctan"], 2.0, 0.5, f32),
+             (4, (3 << 20) + 1, 5, _lib.SURROGATE["superspike"], 4.0, 1.0, f32),
+             (4, 3 << 20, 3, _lib.SURROGATE["superspike"], 4.0, 1.0, f32),
+             (4, 3 << 20, 6, _lib.SURROGATE["arctan"], 2.0, 0.5, bf16)]
+    for T, N, seed, surrogate, k, gain, sdt in cases:
+        x, spikes, gs, gv = _inputs(T, N, seed, spike_dtype=sdt)
         want_gx, want_gb = _bwd_workspace(lib, x, spikes, gs, gv, prm, surrogate, k, gain)
         gx = torch.full_like(x, float("nan"))
         gb = torch.full((1,), float("nan"), device=dev)
