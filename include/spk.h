@@ -31,6 +31,9 @@
  *                          SSA.py:230-245 (xnor_attention :145-165, log-PE
  *                          :177-201, mask, scale, @V, lifs) and of
  *                          SSAMultiHeadAttention_.forward SSA.py:77-87
+ *   spk_ssa_fwd_heads      the same without a mask, on head-split operands
+ *                          (the layout of SSA.py:226-228 after split_heads);
+ *                          the training forward of the unmasked core
  *   spk_embed_pe_lif_fwd   TokenEmbedding + PositionalEncoding + lifPE,
  *                          Seq2Seq.py:11-36, :109-114
  *   spk_linear_affine_lif_fwd  conv (as a GEMM) -> eval BatchNorm -> LIF of
@@ -317,6 +320,20 @@ int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int ma
                 const float* scale, const float* lif_beta, const float* lif_vth, const float* lif_vreset,
                 float in_gain, int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, void* out,
                 int out_dtype, float* attn_out, void* stream);
+
+/*
+ * The unmasked core of spk_ssa_fwd (score-free kernel, Nq, Nk <= 256) on
+ * head-split operands: q [T*B][H][Nq][dh], k, v [T*B][H][Nk][dh] bf16 spikes
+ * (0/1), given as views with element strides strides[9] = {q: t*b, head,
+ * position; k: the same; v: the same} (unit stride along dh; every stride a
+ * positive multiple of 8 elements).  out, scale and the LIF parameters as
+ * in spk_ssa_fwd (out token-major [T][B][Nq][H*dh]); attn_out (the LIF input
+ * a = scale * O, or NULL) is token-major too: [T][B][Nq][H*dh] fp32.
+ */
+int spk_ssa_fwd_heads(const void* q, const void* k, const void* v, const int64_t* strides, int variant,
+                      const float* scale, const float* lif_beta, const float* lif_vth, const float* lif_vreset,
+                      float in_gain, int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, void* out,
+                      int out_dtype, float* attn_out, void* stream);
 
 /*
  * tokens: [B][N] int64; emb: [V][D] fp32; pe: [>=N][D] fp32 (row n for

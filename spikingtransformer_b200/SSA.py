@@ -201,6 +201,15 @@ class SSAMultiHeadAttention(_SSACore):
         L = max(seq_len_q, seq_len_k)
         return torch.ceil(torch.log2((L - 1) / (dist + 1))).clamp(min=0)
 
+    def _log_pe_bias(self, seq_len_q, seq_len_k, device):
+        """``get_log_pe_bias_cross`` for this package's own kernels, built once
+        per (Lq, Lk, device) and shared: they only read it."""
+        key = (seq_len_q, seq_len_k, device)
+        R = _LOG_PE_CACHE.get(key)
+        if R is None:
+            R = _LOG_PE_CACHE[key] = self.get_log_pe_bias_cross(seq_len_q, seq_len_k, device)
+        return R
+
     def _combine_lif(self, q, k, v, mask):
         lifs = self.lifs
         TB, H, Nq, dh = q.shape
@@ -211,7 +220,7 @@ class SSAMultiHeadAttention(_SSACore):
             dt = torch.float32
             if torch.is_autocast_enabled(q.device.type):
                 dt = torch.get_autocast_dtype(q.device.type)
-            R = self.get_log_pe_bias_cross(Nq, k.shape[2], q.device)
+            R = self._log_pe_bias(Nq, k.shape[2], q.device)
             return XnorLIF.apply(q, k, v, R, self.scale, lifs.effective_beta(), lifs.v_th, lifs.v_reset,
                                  lifs.in_gain, lifs.surrogate, lifs._k_host, lifs.n_steps, dt)
         return super()._combine_lif(q, k, v, mask)
@@ -229,7 +238,7 @@ class SSAMultiHeadAttention(_SSACore):
         #   S V = 2 Q (K^T V) + (dh - |q|) (1^T V) - 1 (s^T V) + R V,  s_j = |k_j|,
         # so neither S nor its gradient is formed.
         dh = q.shape[-1]
-        R = self.get_log_pe_bias_cross(q.shape[2], k.shape[2], q.device)
+        R = self._log_pe_bias(q.shape[2], k.shape[2], q.device)
         if q.is_cuda and k.shape[2] <= 256 and dh <= 256:
             return XnorScoreFree.apply(q, k, v, R, self.scale)
         # fp32 matmuls keep every integer term exact (sums below 2^24), whatever
@@ -324,9 +333,38 @@ def _ones_bf16(r, c, device):
     return t
 
 
+# log-distance bias matrices of the attention kernels, by (Lq, Lk, device)
+_LOG_PE_CACHE = {}
+
+
 def _bmm32(a, b):
     """bf16 x bf16 -> fp32 batched product on the tensor cores."""
     return torch.bmm(a, b, out_dtype=torch.float32)
+
+
+def _score_free_kernel_ok(q, k, v):
+    """The score-free forward kernel takes these head-split operands: Nq, Nk <=
+    256, a head width of 8..64 in steps of 8, unit stride along it and the
+    other strides multiples of 8 elements, 16-byte aligned bf16 data."""
+    if not (q.is_cuda and q.dim() == 4 and q.shape[2] <= 256 and k.shape[2] <= 256):
+        return False
+    dh = q.shape[3]
+    if not (8 <= dh <= 64 and dh % 8 == 0):
+        return False
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.stride(3) != 1 or t.data_ptr() % 16:
+            return False
+        if any(st <= 0 or st % 8 for st in t.stride()[:3]):
+            return False
+    return True
+
+
+def _xnor_m(kb, vb):
+    """``M = 2 K^T V - 1 (1^T V)^T`` in bf16 (exact: ``|M| <= Nk``), the small
+    operand of the regrouped core's products."""
+    kv = _bmm32(kb.transpose(1, 2), vb)
+    cv = vb.sum(1, keepdim=True, dtype=torch.float32)
+    return (2.0 * kv - cv).to(torch.bfloat16)
 
 
 def _xnor_products(q, k, v, R):
@@ -438,9 +476,19 @@ class XnorLIF(torch.autograd.Function):
     def forward(ctx, q, k, v, R, scale, lif_beta, v_th, v_reset, in_gain, surrogate, k_sg, T, spike_dtype):
         with torch.autocast("cuda", enabled=False):
             TB, H = q.shape[:2]
-            qb, kb, vb, Mb, Rb, qm, rv, w = _xnor_products(q, k, v, R)
-            a, spikes = ops.xnor_train_combine_lif(qm, rv, w, scale, TB, H, T, lif_beta, v_th, v_reset, in_gain,
-                                                   spike_dtype)
+            if spike_dtype in (torch.bfloat16, torch.float32) and _score_free_kernel_ok(q, k, v):
+                # the forward kernel of the unmasked core (score-free, exact, the
+                # LIF in its epilogue) reads the head-split operands in place and
+                # writes the spikes and the LIF input a; the backward's small
+                # product M is formed there
+                spikes, a = ops.ssa_heads(q, k, v, T, 1, scale, lif_beta, v_th, v_reset, in_gain,
+                                          out_dtype=spike_dtype, want_attn=True)
+                qb, kb, vb = (_flat_bf16(t) for t in (q, k, v))
+                Mb, Rb = None, R.to(torch.bfloat16)
+            else:
+                qb, kb, vb, Mb, Rb, qm, rv, w = _xnor_products(q, k, v, R)
+                a, spikes = ops.xnor_train_combine_lif(qm, rv, w, scale, TB, H, T, lif_beta, v_th, v_reset,
+                                                       in_gain, spike_dtype)
         ctx.save_for_backward(qb, kb, vb, Mb, Rb, a, scale, lif_beta, v_th, v_reset)
         ctx.meta = ((q.dtype, q.shape), (k.dtype, k.shape), (v.dtype, v.shape))
         ctx.lif = (float(in_gain), surrogate, float(k_sg), int(T))
@@ -453,6 +501,8 @@ class XnorLIF(torch.autograd.Function):
         gain, surrogate, k_sg, T = ctx.lif
         need_lb = ctx.needs_input_grad[5]
         with torch.autocast("cuda", enabled=False):
+            if Mb is None:
+                Mb = _xnor_m(kb, vb)
             g_heads, g_rows, gcol, gdot, glb = ops.xnor_train_grad_prep_lif(
                 g, a, scale, H, dh, T, lb, vth, vr, gain, surrogate, k_sg, need_lif_beta=need_lb)
             gscale = (gdot / scale.float()).reshape(scale.shape).to(scale.dtype)

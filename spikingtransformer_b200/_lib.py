@@ -55,6 +55,8 @@ SIGNATURES = {
                         _p, _p, _p, _p, _p, _p, _i64, _p], _i),
     "spk_ssa_fwd": ([_p, _p, _p, _i, _i, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64,
                      _i64, _i64, _p, _i, _p, _p], _i),
+    "spk_ssa_fwd_heads": ([_p, _p, _p, _p, _i, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i,
+                           _p, _p], _i),
     "spk_embed_pe_lif_fwd": ([_p, _p, _f, _p, _p, _p, _p, _f, _i64, _i64, _i64, _i64, _i64, _p, _i, _p, _p], _i),
     "spk_patch_im2col": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _p], _i),
     "spk_synth_text_lines": ([_p, _i64, _i64, _i64, ctypes.c_uint64, _p, _i64, _i64, _p], _i),

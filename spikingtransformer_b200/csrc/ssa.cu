@@ -447,7 +447,7 @@ using namespace ssak;
 int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, int T, int B, int H,
                    int Nq, int Nk, int dh, int variant, const float* scale, const float* lif_beta,
                    const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
-                   float* attn_out, cudaStream_t st);
+                   float* attn_out, bool attn_token_major, cudaStream_t st);
 
 // two (batch, head) pairs per tile for Nq, Nk <= 64 (ssa_short.cu)
 int launch_ssa_short(const void* q, const void* k, const void* v, int T, int B, int H, int Nq, int Nk, int dh,
@@ -472,9 +472,54 @@ static int make_qkv_map(CUtensorMap* m, const void* ptr, int dh, int H, int N, i
   return make_tmap_bf16(m, ptr, 4, dims, strides, box, true);
 }
 
+// q / k / v as [T*B][H][N][dh] views with element strides (t*b, head,
+// position) and unit stride along dh
+static int make_heads_map(CUtensorMap* m, const void* ptr, int dh, int H, int N, int TB, const int64_t* st) {
+  uint64_t dims[4] = {(uint64_t)dh, (uint64_t)H, (uint64_t)N, (uint64_t)TB};
+  uint64_t strides[3] = {(uint64_t)st[1] * 2, (uint64_t)st[2] * 2, (uint64_t)st[0] * 2};
+  uint32_t box[4] = {64, 1, 128, 1};
+  return make_tmap_bf16(m, ptr, 4, dims, strides, box, true);
+}
+
 }  // namespace spk
 
 extern "C" {
+
+int spk_ssa_fwd_heads(const void* q, const void* k, const void* v, const int64_t* strides, int variant,
+                      const float* scale, const float* lif_beta, const float* lif_vth, const float* lif_vreset,
+                      float in_gain, int64_t T, int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t dh, void* out,
+                      int out_dtype, float* attn_out, void* stream) {
+  using namespace spk;
+  SPK_REQUIRE(q && k && v && strides && out && scale && lif_beta && lif_vth && lif_vreset, SPK_ERR_INVALID,
+              "null pointer argument");
+  SPK_REQUIRE(variant == 0 || variant == 1, SPK_ERR_INVALID, "variant must be 0 (plain) or 1 (xnor)");
+  SPK_REQUIRE(out_dtype == SPK_BF16 || out_dtype == SPK_F32, SPK_ERR_INVALID, "out dtype must be bf16 or f32");
+  SPK_REQUIRE(dh >= 8 && dh <= 64 && dh % 8 == 0, SPK_ERR_SHAPE, "head dim %lld unsupported (8..64, multiple of 8)",
+              (long long)dh);
+  SPK_REQUIRE(T >= 1 && B >= 1 && H >= 1 && Nq >= 1 && Nk >= 1 && Nq <= 256 && Nk <= 256, SPK_ERR_SHAPE,
+              "unsupported sizes T=%lld B=%lld H=%lld Nq=%lld Nk=%lld (Nq, Nk <= 256)", (long long)T, (long long)B,
+              (long long)H, (long long)Nq, (long long)Nk);
+  SPK_REQUIRE(T * B < (1ll << 31) && B * H < (1ll << 31), SPK_ERR_SHAPE, "grid too large");
+  for (int i = 0; i < 9; ++i)
+    SPK_REQUIRE(strides[i] > 0 && (strides[i] * 2) % 16 == 0, SPK_ERR_ALIGN,
+                "operand strides must be positive multiples of 8 elements (stride %d = %lld)", i,
+                (long long)strides[i]);
+  SPK_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16), SPK_ERR_ALIGN,
+              "q, k, v and out must be 16-byte aligned");
+  int rc = check_stream_device(stream);
+  if (rc != SPK_OK) return rc;
+  CUtensorMap tq, tk, tv;
+  const int TB = (int)(T * B);
+  if ((rc = make_heads_map(&tq, q, (int)dh, (int)H, (int)Nq, TB, strides)) != SPK_OK) return rc;
+  if ((rc = make_heads_map(&tk, k, (int)dh, (int)H, (int)Nk, TB, strides + 3)) != SPK_OK) return rc;
+  if ((rc = make_heads_map(&tv, v, (int)dh, (int)H, (int)Nk, TB, strides + 6)) != SPK_OK) return rc;
+  rc = launch_ssa_lin(tq, tk, tv, (int)T, (int)B, (int)H, (int)Nq, (int)Nk, (int)dh, variant, scale, lif_beta,
+                      lif_vth, lif_vreset, in_gain, out_dtype == SPK_BF16 ? out : nullptr,
+                      out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out, true,
+                      reinterpret_cast<cudaStream_t>(stream));
+  if (rc != SPK_OK) return rc;
+  return check_launch("ssa_lin_kernel");
+}
 
 int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int mask_mode, const uint8_t* mask,
                 int64_t mask_stride_t, int64_t mask_stride_b, int64_t mask_stride_h, int64_t mask_stride_q,
@@ -504,7 +549,7 @@ int spk_ssa_fwd(const void* q, const void* k, const void* v, int variant, int ma
   if (mask_mode == 0 && !force_dense()) {
     rc = launch_ssa_lin(tq, tk, tv, (int)T, (int)B, (int)H, (int)Nq, (int)Nk, (int)dh, variant, scale, lif_beta,
                         lif_vth, lif_vreset, in_gain, out_dtype == SPK_BF16 ? out : nullptr,
-                        out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out,
+                        out_dtype == SPK_F32 ? reinterpret_cast<float*>(out) : nullptr, attn_out, false,
                         reinterpret_cast<cudaStream_t>(stream));
     if (rc == SPK_OK) return check_launch("ssa_lin_kernel");
     if (rc != SPK_ERR_UNSUPPORTED) return rc;

@@ -51,6 +51,7 @@ struct Params {
   __nv_bfloat16* out_bf16;
   float* out_f32;
   float* attn_out;
+  int attn_tok;  // attn_out token-major [T][B][Nq][H*dh] (else [T][B][H][Nq][dh])
   int lmax, items;
   int v8;  // bf16 output rows may be written as 32-byte vectors (16-column chunks)
 };
@@ -405,7 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t ta = tm_d2 + qb * NO + lane_off;
       const int64_t obase = (((int64_t)t * p.B + b) * p.Nq + qi) * D + (int64_t)h * p.dh;
-      float* aout = p.attn_out ? p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh : nullptr;
+      float* aout = !p.attn_out ? nullptr
+                    : p.attn_tok ? p.attn_out + obase
+                                 : p.attn_out + ((((int64_t)t * p.B + b) * p.H + h) * p.Nq + qi) * p.dh;
       const float* csp = sm.cs + par * 64;
       const float* kvp = sm.kv + par * 64;
       const bool row_ok = qi < p.Nq;
@@ -537,7 +540,7 @@ SPK_DEFINE_ERROR_READER(ssa_lin_read_device_error)
 int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, int T, int B, int H,
                    int Nq, int Nk, int dh, int variant, const float* scale, const float* lif_beta,
                    const float* lif_vth, const float* lif_vr, float gain, void* out_bf16, float* out_f32,
-                   float* attn_out, cudaStream_t st) {
+                   float* attn_out, bool attn_token_major, cudaStream_t st) {
   using namespace ssal;
   if (Nq > 256 || Nk > 256 || dh > 64 || dh % 8 != 0) return SPK_ERR_UNSUPPORTED;
   Params p = {};
@@ -556,6 +559,7 @@ int launch_ssa_lin(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   p.v8 = dh % 16 == 0 && aligned(out_bf16, 32);
   p.out_f32 = out_f32;
   p.attn_out = attn_out;
+  p.attn_tok = attn_token_major ? 1 : 0;
   p.QB = (Nq + 127) / 128;
   p.dsplit = ((dh / 8 + 1) / 2) * 8;
   p.lmax = Nq > Nk ? Nq : Nk;

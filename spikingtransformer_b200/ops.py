@@ -423,6 +423,31 @@ def ssa(q, k, v, T, B, H, variant, scale, lif_beta, lif_vth, lif_vr, in_gain=1.0
     return out, attn
 
 
+def ssa_heads(q, k, v, T, variant, scale, lif_beta, lif_vth, lif_vr, in_gain=1.0, out_dtype=torch.bfloat16,
+              want_attn=False):
+    """Unmasked attention core + output LIF on head-split bf16 spikes (any
+    strides with a unit stride along the head dimension): ``q`` ``[T*B, H, Nq,
+    dh]``, ``k``/``v`` ``[T*B, H, Nk, dh]``, Nq, Nk <= 256.  Returns ``(spikes
+    [T*B, Nq, H*dh], a fp32 [T*B, Nq, H*dh] or None)``: ``a`` is the LIF input
+    ``scale * O``, token-major like the spikes."""
+    _cuda(q, k, v)
+    q, k, v = (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16) for t in (q, k, v))
+    TB, H, Nq, dh = q.shape
+    Nk = k.shape[2]
+    dev = q.device
+    out = torch.empty((TB, Nq, H * dh), dtype=out_dtype, device=dev)
+    attn = torch.empty((TB, Nq, H * dh), dtype=torch.float32, device=dev) if want_attn else None
+    sc, b, th, vr = (_scalar_f32(x, dev) for x in (scale, lif_beta, lif_vth, lif_vr))
+    _lib.call("spk_ssa_fwd_heads", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _head_strides(q, k, v), int(variant),
+              _lib.ptr(sc), _lib.ptr(b), _lib.ptr(th), _lib.ptr(vr), float(in_gain), T, TB // T, H, Nq, Nk, dh,
+              _lib.ptr(out), _lib.DTYPE_CODE[out_dtype], _lib.ptr(attn), _lib.stream_ptr(dev),
+              tag="ssa Nq=%d Nk=%d" % (Nq, Nk),
+              work=dict(flops=4.0 * TB * H * Nq * Nk * dh,
+                        bytes=(q.numel() + k.numel() + v.numel()) * 2 + out.numel() * out.element_size()
+                        + (attn.numel() * 4 if attn is not None else 0)))
+    return out, attn
+
+
 def _distinct_bytes(t):
     """Bytes of memory behind a (possibly broadcast, stride-0) tensor."""
     return t.untyped_storage().nbytes()

@@ -514,6 +514,23 @@ def test_ssa(ops, variant, T, B, H, Nq, Nk, dh, maskkind):
 # ------------------------------------------------------------------ embedding
 
 
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("T,B,H,Nq,Nk,dh", [(4, 2, 8, 256, 256, 48), (4, 3, 2, 64, 256, 48), (2, 2, 3, 40, 70, 64)])
+def test_ssa_heads_equals_token_major(ops, variant, T, B, H, Nq, Nk, dh):
+    """The head-split entry point (operands as strided [T*B, H, N, dh] views,
+    the layout of the training forward) gives the token-major entry point's
+    spikes and LIF input bit for bit."""
+    D = H * dh
+    q, k, v = spikes_qkv(Nq * 13 + Nk + dh + variant, T * B, Nq, Nk, D, p=0.15)
+    q, k, v = (t.to(DEV).bfloat16() for t in (q, k, v))
+    scale = 0.125 if variant == 0 else (1.0 / dh) ** 0.5
+    s_ref, a_ref = ops.ssa(q, k, v, T, B, H, variant, scale, 0.9, 0.5, 0.0, in_gain=0.5, want_attn=True)
+    heads = [t.view(T * B, t.shape[1], H, dh).transpose(1, 2) for t in (q, k, v)]  # strided views
+    s, a = ops.ssa_heads(*heads, T, variant, scale, 0.9, 0.5, 0.0, in_gain=0.5, want_attn=True)
+    assert torch.equal(s, s_ref)
+    assert torch.equal(a, a_ref.transpose(1, 2).reshape(T * B, Nq, D))
+
+
 def test_embed_pe_lif(ops):
     g = gen(4)
     V, D, B, N, T = 50, 32, 3, 7, 4

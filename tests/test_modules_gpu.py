@@ -188,18 +188,20 @@ def test_decoder_masked_attention_trains_on_the_fused_core(pkg):
     assert x.grad is not None and torch.isfinite(x.grad).all()
 
 
+@pytest.mark.parametrize("in_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("spike_dtype", [torch.float32, torch.bfloat16])
-def test_xnor_lif_fused_equals_composition(pkg, spike_dtype):
+def test_xnor_lif_fused_equals_composition(pkg, spike_dtype, in_dtype):
     """The attention core with the output LIF fused into its kernels equals the
     core followed by the lifs LIF module: spikes bit for bit, gradients of Q,
-    K, V and the scale to fp32 rounding."""
+    K, V and the scale to fp32 rounding.  With bf16 operands the forward runs
+    the score-free inference kernel on the head-split views in place."""
     from spikingtransformer_b200.SSA import SSAMultiHeadAttention, XnorLIF, XnorScoreFree
     T, Bp, H, Nq, Nk, dh = 4, 3, 2, 24, 40, 48
     TB = T * Bp
     m = SSAMultiHeadAttention(d_model=H * dh, n_heads=H, n_steps=T).to(DEV)
     m.lifs.set_surrogate("arctan", 2.0)
     g = torch.Generator(device=DEV).manual_seed(17)
-    base = [(torch.rand(TB, n, H, dh, generator=g, device=DEV) < 0.3).float() for n in (Nq, Nk, Nk)]
+    base = [(torch.rand(TB, n, H, dh, generator=g, device=DEV) < 0.3).to(in_dtype) for n in (Nq, Nk, Nk)]
     R = m.get_log_pe_bias_cross(Nq, Nk, DEV)
     gsp = torch.randn(TB, Nq, H * dh, generator=g, device=DEV).to(torch.bfloat16).float()
     results = []
@@ -219,7 +221,7 @@ def test_xnor_lif_fused_equals_composition(pkg, spike_dtype):
     (s0, g0, sc0), (s1, g1, sc1) = results
     assert torch.equal(s0, s1)
     for a, b in zip(g0, g1):
-        assert torch.allclose(a, b, rtol=1e-5, atol=1e-6)
+        assert torch.allclose(a.float(), b.float(), rtol=1e-5, atol=1e-6)
     assert torch.allclose(sc0, sc1, rtol=1e-4, atol=1e-6)
 
 
