@@ -720,3 +720,30 @@ def test_stack_forward_leaves_bf16_input_unchanged(pkg):
 def test_no_device_timeouts(pkg):
     from spikingtransformer_b200 import ops
     ops.device_error_check()
+
+
+def test_forward_cuda_graph_matches_eager(pkg):
+    """The inference forward captured once in a CUDA graph (as the forward
+    benchmark times it) and replayed on new inputs copied into its buffers
+    gives the eager forward's logits bit for bit."""
+    ours, _ = _bench_models(enc_layers=2, dec_layers=1)
+    B, N = 4, 64
+    sets = []
+    for i in range(3):
+        src = synthetic_lines(B, 40 + i).to(DEV)
+        tgt = torch.randint(0, 256, (B, N), device=DEV, generator=torch.Generator(device=DEV).manual_seed(40 + i))
+        sets.append((src, tgt))
+    mask = torch.tril(torch.ones(N, N, device=DEV)).expand(B, 1, N, N).contiguous()
+    with torch.no_grad():
+        static = [t.clone() for t in sets[0]]
+        ours(static[0], static[1], look_ahead_mask=mask)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = ours(static[0], static[1], look_ahead_mask=mask)[0]
+        for i in (1, 2, 0):
+            for a, b in zip(static, sets[i]):
+                a.copy_(b)
+            graph.replay()
+            want = ours(sets[i][0], sets[i][1], look_ahead_mask=mask)[0]
+            assert torch.equal(out, want), i
