@@ -390,9 +390,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && n_units > 0) ok = build_mb(0);
       if (ok && n_units > 1) ok = key_sums(1);
     }
+    // unit position (step t, batch b, head h), advanced one unit at a time
+    // with one division per item
+    int t = 0, item = (int)blockIdx.x, b = item / p.H, h = item - b * p.H;
     for (int g = 0; g < n_units && ok; ++g) {
-      const int item = (int)blockIdx.x + (g / p.T) * (int)gridDim.x, t = g % p.T;
-      const int b = item / p.H, h = item % p.H;
+      if (g > 0 && ++t == p.T) {
+        t = 0;
+        item += (int)gridDim.x;
+        b = item / p.H;
+        h = item - b * p.H;
+      }
       const int par = g & 1;
       if (t == 0) {
 #pragma unroll
