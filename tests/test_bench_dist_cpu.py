@@ -141,3 +141,25 @@ def test_bucketed_gradient_reducer_matches_ddp():
     assert torch.allclose(f32_0, ddp0, rtol=1e-5, atol=1e-6)
     assert torch.allclose(bf16_0, ddp0, rtol=0, atol=1e-3)
     assert not torch.equal(bf16_0, f32_0)
+
+
+def test_clock_sampler_keeps_only_the_timed_window():
+    """bench.ClockSampler: samples taken before begin() or after end() (the
+    warm-up, the sampler's start-up) are left out of the summary; the median
+    SM clock, the maximum and the throttle reasons come from the window only."""
+    sys.path.insert(0, ROOT)
+    import bench
+    clk = bench.ClockSampler(0)
+    row = lambda mhz, cap: [str(mhz), "1965", "500.0", "0x0", "Not Active", "Not Active", "Not Active", cap]  # noqa
+    clk.samples = [(0.0, row(1965, "Not Active")),     # before the window
+                   (1.0, row(1600, "Active")),
+                   (1.1, row(1650, "Active")),
+                   (1.2, row(1700, "Not Active")),
+                   (5.0, row(900, "Not Active"))]       # after it
+    clk.t0, clk.t1 = 0.5, 2.0
+    s = clk.summary()
+    assert s["samples"] == 3
+    assert s["sm_mhz"] == 1650.0 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
+    clk.t0, clk.t1 = 3.0, 4.0  # a window with no sample in it
+    assert clk.summary()["reasons"] == ["unavailable"]
