@@ -19,6 +19,23 @@ def test_exports_every_declared_symbol():
     assert set(declared) <= set(_lib.SIGNATURES), set(declared) - set(_lib.SIGNATURES)
 
 
+def test_binding_argument_counts_match_the_header():
+    """Every prototype in include/spk.h takes as many arguments as the ctypes
+    binding passes (a drifted binding would push arguments into the wrong
+    slots without any error from ctypes)."""
+    import re
+    text = re.sub(r"/\*.*?\*/", "", open(_lib.HEADER).read(), flags=re.S)
+    protos = re.findall(r"\b(spk_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S)
+    assert len(protos) >= 10
+    wrong = {}
+    for name, args in protos:
+        args = args.strip()
+        n = 0 if args in ("", "void") else args.count(",") + 1
+        if name in _lib.SIGNATURES and len(_lib.SIGNATURES[name][0]) != n:
+            wrong[name] = (n, len(_lib.SIGNATURES[name][0]))
+    assert not wrong, wrong
+
+
 def test_version_and_status_strings():
     lib = _lib.load()
     assert lib.spk_version() >= 1
