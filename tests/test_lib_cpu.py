@@ -51,6 +51,9 @@ def test_null_arguments_rejected_without_device():
     rc = lib.spk_ssa_fwd(None, None, None, 1, 0, None, 0, 0, 0, 0, None, None, None, None, 1.0,
                          1, 1, 1, 1, 1, 48, None, 2, None, None)
     assert rc == 1
+    rc = lib.spk_ssa_fwd_heads(None, None, None, None, 1, None, None, None, None, 1.0, 1, 1, 1, 1, 1, 48, None, 2,
+                               None, None)
+    assert rc == 1
 
 
 def test_shape_limits_rejected_without_device():
@@ -64,6 +67,10 @@ def test_shape_limits_rejected_without_device():
     rc = lib.spk_linear_ln_lif_fwd(buf, buf, None, None, None, 1e-5, buf, buf, buf, 1.0, 4, 8, 12, 64, 0, buf,
                                    2, None, None, None)
     assert rc == 2  # K % 8 != 0
+    strides = (ctypes.c_int64 * 9)(*([8] * 9))
+    rc = lib.spk_ssa_fwd_heads(buf, buf, buf, strides, 1, buf, buf, buf, buf, 1.0, 1, 1, 1, 300, 8, 48, buf, 2,
+                               None, None)
+    assert rc == 2  # Nq > 256
 
 
 def test_workspace_query():
